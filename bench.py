@@ -1,0 +1,296 @@
+"""Decode benchmark: batch-1 greedy decode of the Qwen2.5-3B-shaped Q4_K_M
+synthetic model through the C ABI.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+One process per GPU (torchrun for N > 1). Every rank decodes its own
+conversation with replicated weights — independent conversations, no
+collective on the data path — so `value` is the sum over ranks (weak scaling).
+A step is one decode token: the forward of one token plus the greedy pick.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s bs=1, 3B-shape Q4_K_M; weight-stream HBM GB/s vs ~8 TB/s peak"
+WORKLOAD = "qwen2.5-3B-shape Q4_K_M (Q6_K tied output, half of attn_v/ffn_down), synthetic N(0,0.02), " \
+           "512-token seeded prompt, greedy decode bs=1"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def model_path(config: str, seed: int) -> str:
+    d = os.environ.get("CXM_MODEL_DIR", tempfile.gettempdir())
+    return os.path.join(d, f"cxm_{config}_s{seed}.gguf")
+
+
+def ensure_model(config: str, seed: int) -> str:
+    import cosxamix_b200 as cx
+    p = model_path(config, seed)
+    if not os.path.exists(p):
+        t = time.time()
+        cx.synth_write(p, cx.synth_spec(config, seed=seed))
+        print(f"[bench] wrote {p} in {time.time() - t:.1f}s", file=sys.stderr)
+    return p
+
+
+def seeded_prompt(seed: int, n: int, vocab: int):
+    # uniform token ids from the reference's xorshift64* (src/daiss.rs:317-337)
+    st = seed if seed else 0x9E3779B97F4A7C15
+    out = []
+    for _ in range(n):
+        x = st
+        x ^= x >> 12
+        x ^= (x << 25) & 0xFFFFFFFFFFFFFFFF
+        x ^= x >> 27
+        st = x
+        out.append(((x * 0x2545F4914F6CDD1D) & 0xFFFFFFFFFFFFFFFF) % vocab)
+    return out
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (clocks + throttle reasons)."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, device: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", str(device)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) == 9 and parts[1].isdigit():
+                    rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        smax = max(int(r[2]) for r in rows)
+        loaded = [int(r[1]) for r in rows if float(r[3] or 0) > 200] or [int(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax, "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(path: str, prompt_len: int, budget_s: float, threads: int = 0) -> dict:
+    """The oracle (C restatement of the reference's engine_own decode) on the
+    host cores: decode tokens at context `prompt_len` for about `budget_s`."""
+    from oracle import oracle as O
+    if threads:
+        O.set_threads(threads)
+    m = O.Model(path)
+    c = m.cache()
+    c.fill(prompt_len, seed=1)
+    tok = 17
+    t0 = time.perf_counter()
+    logits = m.forward(c, [tok])
+    first = time.perf_counter() - t0
+    n = max(2, min(200, int(budget_s / max(first, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        tok = int(O.lib().orc_argmax(O.ptr(logits), logits.size))
+        logits = m.forward(c, [tok])
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tok/s", "cores": O.threads(), "kind": "port",
+            "sample": f"{n} greedy decode tokens at context {prompt_len}..{prompt_len + n} "
+                      f"(KV prefix filled with seeded values instead of a CPU prefill), C restatement of the "
+                      f"reference's engine_own path (reference Rust not buildable here)"}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    """`--impl reference`: the reference's CPU implementation of the path
+    (its C restatement, oracle/), timed on this box's host cores."""
+    if rank != 0:
+        return
+    path = ensure_model(args.config, args.seed)
+    from oracle import oracle as O
+    m = O.Model(path)
+    c = m.cache()
+    c.fill(args.prompt, seed=1)
+    tok = 17
+    logits = None
+    for _ in range(args.warmup):
+        logits = m.forward(c, [tok])
+        tok = int(O.lib().orc_argmax(O.ptr(logits), logits.size))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        logits = m.forward(c, [tok])
+        tok = int(O.lib().orc_argmax(O.ptr(logits), logits.size))
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1000 / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "prompt": args.prompt, "decode_steps": args.steps},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": O.threads(), "kind": "port",
+                         "sample": f"{args.steps} greedy decode tokens per step-set at context {args.prompt} (KV "
+                                   f"prefix seeded instead of a CPU prefill); C restatement of the reference's "
+                                   f"engine_own decode, all host threads (reference Rust not buildable here)"},
+        "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="qwen3b")
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--seed", type=int, default=42)
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import cosxamix_b200 as cx
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    if rank == 0:
+        path = ensure_model(args.config, args.seed)
+    if world > 1:
+        dist.barrier()
+    path = model_path(args.config, args.seed)
+
+    m = cx.Modelo(path, device=local)
+    cfg = m.cfg
+    e2e_steps = max(8, min(args.steps, 64))
+    need = args.prompt + args.warmup + args.steps + e2e_steps + 8
+    cache = m.cache(min(need, cfg.ctx))
+    prompt = seeded_prompt(args.seed + rank, args.prompt, cfg.vocab)
+    m.forward(prompt, cache)                           # prefill (untimed)
+    m.bench_decode(cache, args.warmup)                 # warm-up steps (untimed)
+
+    # timed: K decode steps, inputs resident, device events on the model stream
+    clocks = Clocks(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = m.bench_decode(cache, args.steps)
+    torch.cuda.synchronize()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clk = clocks.stop()
+    value = world * args.steps / (ms / 1000.0)
+
+    # end to end through the public API: host token in, host token out
+    pinned = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    sampler = cx.Muestreador.voraz()
+    tok = m.elegir(sampler)
+    import ctypes
+    lib = cx.lib()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        pinned[0] = tok
+        rc = lib.cxm_forward(m.h, cache.h, pinned.data_ptr(), 1, None)
+        if rc:
+            raise ValueError(cx._err())
+        tok = m.elegir(sampler)
+    dt = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([dt], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    e2e = world * e2e_steps / dt
+
+    # dominant kernel: the gate/up matvec, cycled over the 36 layers (HBM)
+    mv_ms, mv_bytes = m.bench_matvec(3 * cfg.n_layer)
+    peak, peak_kind = peaks()
+    achieved = mv_bytes / (mv_ms / 1000.0) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "matvec_gateup_qwen3b.md")) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    traffic = int(line.split(":")[1].strip())
+    except OSError:
+        pass
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(path, args.prompt, args.cpu_budget)
+    wbytes = m.weight_bytes
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "prompt": args.prompt, "decode_steps": args.steps,
+                   "parallelism": f"dp{world} (independent conversations, replicated weights)",
+                   "l2": "inputs larger than L2: 1.92 GB of weights streamed per step vs 126 MB L2"},
+        "weight_stream": {"bytes_per_token": wbytes, "gbs_per_gpu": round(value / world * wbytes / 1e9, 1),
+                          "frac": round(value / world * wbytes / 1e9 / peak, 4), "peak_gbs": peak,
+                          "peak_kind": peak_kind},
+        "roofline": {"kernel": "k_matvec gate/up (Q4_K, 2x11008x2048)", "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": mv_bytes, "launch_ms": round(mv_ms, 5),
+                     "peak_kind": peak_kind},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 12,
+                "api": "cxm_forward([token]) + cxm_sample per step, pinned host token"},
+        "gpu_launches": args.steps * m.step_launches,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

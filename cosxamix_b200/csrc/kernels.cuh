@@ -1,0 +1,339 @@
+// Device code of the decode step: k-quant matvec (all five super-block
+// layouts), fused activation quantization, RoPE + KV append, split-K
+// flash-decode attention, embedding lookup and the greedy argmax.
+//
+// Weights live in HBM as "planes" (see DMat): the GGUF super-block bytes are
+// split once at load into 16-byte-aligned per-row arrays so every weight load
+// is a coalesced 128-bit load, without changing a single bit of the values.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace cxm {
+
+// ── repacked weight matrix ──
+// Plane A per super-block: Q4_K 144 B (whole block), Q5_K 176 B (whole block),
+// Q6_K 192 B (ql|qh), Q3_K 96 B (hmask|qs), Q2_K 64 B (qs).
+// Plane S: Q6_K 16 B int8 scales, Q3_K 12 B packed 6-bit scales, Q2_K 16 B.
+// Plane D: Q6_K 2 B (d), Q3_K 2 B (d), Q2_K 4 B (d, dmin).
+struct DMat {
+    int type, rows, K, nblk;
+    const uint8_t *a, *s, *d;
+    uint32_t a_row, s_row, d_row;  // bytes per row of each plane
+};
+
+__host__ __device__ inline int plane_a_bytes(int t) {
+    return t == 12 ? 144 : t == 13 ? 176 : t == 14 ? 192 : t == 11 ? 96 : t == 10 ? 64 : 0;
+}
+__host__ __device__ inline int plane_s_bytes(int t) { return t == 14 ? 16 : t == 11 ? 12 : t == 10 ? 16 : 0; }
+__host__ __device__ inline int plane_d_bytes(int t) { return t == 14 ? 2 : t == 11 ? 2 : t == 10 ? 4 : 0; }
+
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+    return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFF)));
+}
+
+// Exact IEEE ops, never contracted into FMA: the per-sub-block terms keep the
+// reference's rounding (the sums over sub-blocks are reordered by the warp
+// reduction, which is the only difference left).
+__device__ __forceinline__ float fm(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fs(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fa(float a, float b) { return __fadd_rn(a, b); }
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w0, uint32_t w1, uint32_t w2, int i) {
+    uint32_t w = i < 4 ? w0 : (i < 8 ? w1 : w2);
+    return (w >> (8 * (i & 3))) & 0xFF;
+}
+
+// 6-bit scale/min of sub-block j from the 12 packed bytes (words w0..w2 hold
+// bytes 0..11). src/quant.rs:108-117.
+__device__ __forceinline__ void scale_min_k4(int j, uint32_t w0, uint32_t w1, uint32_t w2, int &sc, int &mn) {
+    if (j < 4) {
+        sc = byte_of(w0, w1, w2, j) & 63;
+        mn = byte_of(w0, w1, w2, j + 4) & 63;
+    } else {
+        sc = (byte_of(w0, w1, w2, j + 4) & 0xF) | ((byte_of(w0, w1, w2, j - 4) >> 6) << 4);
+        mn = (byte_of(w0, w1, w2, j + 4) >> 4) | ((byte_of(w0, w1, w2, j) >> 6) << 4);
+    }
+}
+
+struct XQ {  // the quantized activation, in shared memory
+    const int8_t *q;
+    const float *e, *s;
+};
+
+__device__ __forceinline__ int dot8(const uint32_t *w, const int4 *x2) {
+    // 32 bytes of unsigned weight values (8 words) against 32 i8 activations
+    int4 a = x2[0], b = x2[1];
+    int s = 0;
+    s = __dp4a((int)w[0], a.x, s);
+    s = __dp4a((int)w[1], a.y, s);
+    s = __dp4a((int)w[2], a.z, s);
+    s = __dp4a((int)w[3], a.w, s);
+    s = __dp4a((int)w[4], b.x, s);
+    s = __dp4a((int)w[5], b.y, s);
+    s = __dp4a((int)w[6], b.z, s);
+    s = __dp4a((int)w[7], b.w, s);
+    return s;
+}
+__device__ __forceinline__ int dot4w(const uint32_t *w, int4 a) {
+    int s = 0;
+    s = __dp4a((int)w[0], a.x, s);
+    s = __dp4a((int)w[1], a.y, s);
+    s = __dp4a((int)w[2], a.z, s);
+    s = __dp4a((int)w[3], a.w, s);
+    return s;
+}
+
+__device__ __forceinline__ void ld32(const uint8_t *p, uint32_t w[8]) {
+    uint4 a = __ldg((const uint4 *)p), b = __ldg((const uint4 *)(p + 16));
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+    w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+
+// Each lane works on a "quarter": 64 values of one super-block. `qt` in
+// [0, 4*nblk): block b = qt/4, quarter q = qt%4. Returns the float sum of the
+// quarter's sub-block terms (2 terms for sub-blocks of 32, 4 for 16), and the
+// integer sums in `isum` when requested (parity checks).
+
+// Q4_K: src/kernels/scalar.rs:132-170
+__device__ __forceinline__ float quarter_q4k(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+    const int b = qt >> 2, q = qt & 3;
+    const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 144;
+    uint4 hdr = __ldg((const uint4 *)blk);
+    uint32_t w[8];
+    ld32(blk + 16 + 32 * q, w);
+    float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
+    int sc0, m0, sc1, m1;
+    scale_min_k4(2 * q, hdr.y, hdr.z, hdr.w, sc0, m0);
+    scale_min_k4(2 * q + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
+    uint32_t lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        lo[i] = w[i] & 0x0F0F0F0Fu;
+        hi[i] = (w[i] >> 4) & 0x0F0F0F0Fu;
+    }
+    const int4 *xp = (const int4 *)(x.q + b * 256 + q * 64);
+    int s0 = dot8(lo, xp), s1 = dot8(hi, xp + 2);
+    const int j0 = b * 8 + 2 * q;
+    if (isum) { isum[0] = s0; isum[1] = s1; }
+    float t0 = fm(x.e[j0], fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), x.s[j0])));
+    float t1 = fm(x.e[j0 + 1], fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), x.s[j0 + 1])));
+    return fa(t0, t1);
+}
+
+// Q5_K: src/kernels/scalar.rs:179-217
+__device__ __forceinline__ float quarter_q5k(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+    const int b = qt >> 2, q = qt & 3;
+    const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 176;
+    uint4 hdr = __ldg((const uint4 *)blk);
+    uint32_t qh[8], w[8];
+    ld32(blk + 16, qh);
+    ld32(blk + 48 + 32 * q, w);
+    float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
+    int sc0, m0, sc1, m1;
+    const int j0 = 2 * q, j1 = 2 * q + 1;
+    scale_min_k4(j0, hdr.y, hdr.z, hdr.w, sc0, m0);
+    scale_min_k4(j1, hdr.y, hdr.z, hdr.w, sc1, m1);
+    uint32_t lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        lo[i] = (w[i] & 0x0F0F0F0Fu) | (((qh[i] >> j0) & 0x01010101u) << 4);
+        hi[i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> j1) & 0x01010101u) << 4);
+    }
+    const int4 *xp = (const int4 *)(x.q + b * 256 + q * 64);
+    int s0 = dot8(lo, xp), s1 = dot8(hi, xp + 2);
+    const int k0 = b * 8 + j0;
+    if (isum) { isum[0] = s0; isum[1] = s1; }
+    float t0 = fm(x.e[k0], fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), x.s[k0])));
+    float t1 = fm(x.e[k0 + 1], fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), x.s[k0 + 1])));
+    return fa(t0, t1);
+}
+
+// Q6_K: src/kernels/scalar.rs:294-324. Quarter q = half h (q>>1) and ql
+// column par (q&1): groups gi = par (low nibbles) and gi = par+2 (high).
+__device__ __forceinline__ float quarter_q6k(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+    const int b = qt >> 2, q = qt & 3, h = q >> 1, par = q & 1;
+    const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 192;
+    uint32_t ql[8], qh[8];
+    ld32(blk + 64 * h + 32 * par, ql);
+    ld32(blk + 128 + 32 * h, qh);
+    uint4 scv = __ldg((const uint4 *)(W.s + (size_t)row * W.s_row + (size_t)b * 16));
+    float d = h2f(__ldg((const unsigned short *)(W.d + (size_t)row * W.d_row + (size_t)b * 2)));
+    uint32_t vlo[8], vhi[8];
+    const int slo = 2 * par, shi = 2 * (par + 2);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        vlo[i] = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> slo) & 0x03030303u) << 4);
+        vhi[i] = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> shi) & 0x03030303u) << 4);
+    }
+    const int glo = 4 * h + par, ghi = glo + 2;
+    const int4 *xlo = (const int4 *)(x.q + b * 256 + 32 * glo);
+    const int4 *xhi = (const int4 *)(x.q + b * 256 + 32 * ghi);
+    int s[4];
+    s[0] = dot4w(vlo, xlo[0]);
+    s[1] = dot4w(vlo + 4, xlo[1]);
+    s[2] = dot4w(vhi, xhi[0]);
+    s[3] = dot4w(vhi + 4, xhi[1]);
+    if (isum) { isum[0] = s[0]; isum[1] = s[1]; isum[2] = s[2]; isum[3] = s[3]; }
+    const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+    float total = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int g = k < 2 ? glo : ghi, md = k & 1;
+        const int si = 2 * g + md;
+        const int sc = (int)(int8_t)((scw[si >> 2] >> (8 * (si & 3))) & 0xFF);
+        const int sub = b * 16 + si;
+        float esc = fm(d, (float)sc);
+        float t = fm(fm(x.e[sub], esc), fs((float)s[k], fm(32.0f, x.s[sub])));
+        total = k == 0 ? t : fa(total, t);
+    }
+    return total;
+}
+
+// Q3_K: src/kernels/scalar.rs:236-275. Quarter q = groups 2q and 2q+1.
+__device__ __forceinline__ float quarter_q3k(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+    const int b = qt >> 2, q = qt & 3;
+    const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 96;
+    uint32_t hm[8], qs[8];
+    ld32(blk, hm);
+    ld32(blk + 32 + 32 * (q >> 1), qs);
+    const uint32_t *sp = (const uint32_t *)(W.s + (size_t)row * W.s_row + (size_t)b * 12);
+    uint32_t a0 = __ldg(sp), a1 = __ldg(sp + 1), tt = __ldg(sp + 2);
+    float d = h2f(__ldg((const unsigned short *)(W.d + (size_t)row * W.d_row + (size_t)b * 2)));
+    // scales of sub-blocks 4q..4q+3 (src/quant.rs:87-106)
+    uint32_t aa = (q & 1) ? a1 : a0;
+    uint32_t wq = ((aa >> ((q >> 1) * 4)) & 0x0F0F0F0Fu) | (((tt >> (2 * q)) & 0x03030303u) << 4);
+    int s[4];
+#pragma unroll
+    for (int gg = 0; gg < 2; gg++) {
+        const int g = 2 * q + gg, sh = 2 * (g & 3);
+        uint32_t v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = ((qs[i] >> sh) & 0x03030303u) | (((hm[i] >> g) & 0x01010101u) << 2);
+        const int4 *xp = (const int4 *)(x.q + b * 256 + 32 * g);
+        s[2 * gg] = dot4w(v, xp[0]);
+        s[2 * gg + 1] = dot4w(v + 4, xp[1]);
+    }
+    if (isum) { isum[0] = s[0]; isum[1] = s[1]; isum[2] = s[2]; isum[3] = s[3]; }
+    float total = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int sc = (int)((wq >> (8 * k)) & 0xFF);
+        const int sub = b * 16 + 4 * q + k;
+        float esc = fm(d, fs((float)sc, 32.0f));
+        float t = fm(fm(x.e[sub], esc), fs((float)s[k], fm(4.0f, x.s[sub])));
+        total = k == 0 ? t : fa(total, t);
+    }
+    return total;
+}
+
+// Q2_K: src/kernels/q2k.rs:41-69. Quarter q = groups 2q and 2q+1.
+__device__ __forceinline__ float quarter_q2k(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+    const int b = qt >> 2, q = qt & 3;
+    const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 64;
+    uint32_t qs[8];
+    ld32(blk + 32 * (q >> 1), qs);
+    uint32_t scw = __ldg((const uint32_t *)(W.s + (size_t)row * W.s_row + (size_t)b * 16 + 4 * q));
+    uint32_t dd = __ldg((const uint32_t *)(W.d + (size_t)row * W.d_row + (size_t)b * 4));
+    float d = h2f(dd), dm = h2f(dd >> 16);
+    int s[4];
+#pragma unroll
+    for (int gg = 0; gg < 2; gg++) {
+        const int g = 2 * q + gg, sh = 2 * (g & 3);
+        uint32_t v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = (qs[i] >> sh) & 0x03030303u;
+        const int4 *xp = (const int4 *)(x.q + b * 256 + 32 * g);
+        s[2 * gg] = dot4w(v, xp[0]);
+        s[2 * gg + 1] = dot4w(v + 4, xp[1]);
+    }
+    if (isum) { isum[0] = s[0]; isum[1] = s[1]; isum[2] = s[2]; isum[3] = s[3]; }
+    float total = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int sc = (int)((scw >> (8 * k)) & 0xFF);
+        const int sub = b * 16 + 4 * q + k;
+        float ev = fm(d, (float)(sc & 0xF)), mv = fm(dm, (float)(sc >> 4));
+        float t = fm(x.e[sub], fs(fm(ev, (float)s[k]), fm(mv, x.s[sub])));
+        total = k == 0 ? t : fa(total, t);
+    }
+    return total;
+}
+
+template <int T>
+__device__ __forceinline__ float quarter(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+    if (T == 12) return quarter_q4k(W, row, qt, x, isum);
+    if (T == 13) return quarter_q5k(W, row, qt, x, isum);
+    if (T == 14) return quarter_q6k(W, row, qt, x, isum);
+    if (T == 11) return quarter_q3k(W, row, qt, x, isum);
+    return quarter_q2k(W, row, qt, x, isum);
+}
+
+// ── dequantize one value from the planes (src/quant.rs:582-679) ──
+__device__ inline float dequant_value(const DMat &W, int row, int idx) {
+    const int b = idx >> 8, r = idx & 255;
+    const uint8_t *A = W.a + (size_t)row * W.a_row + (size_t)b * plane_a_bytes(W.type);
+    switch (W.type) {
+    case 12: case 13: {
+        const uint8_t *blk = A;
+        float d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));
+        uint32_t w0 = blk[4] | (blk[5] << 8) | (blk[6] << 16) | ((uint32_t)blk[7] << 24);
+        uint32_t w1 = blk[8] | (blk[9] << 8) | (blk[10] << 16) | ((uint32_t)blk[11] << 24);
+        uint32_t w2 = blk[12] | (blk[13] << 8) | (blk[14] << 16) | ((uint32_t)blk[15] << 24);
+        const int p = r >> 6, half = (r >> 5) & 1, l = r & 31;
+        int sc, mn;
+        scale_min_k4(2 * p + half, w0, w1, w2, sc, mn);
+        float dl = fm(d, (float)sc), ml = fm(dmin, (float)mn);
+        if (W.type == 12) {
+            uint8_t v = blk[16 + 32 * p + l];
+            int qv = half ? (v >> 4) : (v & 0xF);
+            return fs(fm(dl, (float)qv), ml);
+        }
+        uint8_t v = blk[48 + 32 * p + l];
+        int qv = half ? (v >> 4) : (v & 0xF);
+        float extra = (blk[16 + l] >> (2 * p + half)) & 1 ? 16.0f : 0.0f;
+        return fs(fm(dl, fa((float)qv, extra)), ml);
+    }
+    case 14: {
+        const int h = r >> 7, rr = r & 127, gi = rr >> 5, l = rr & 31;
+        uint8_t qlb = A[64 * h + 32 * (gi & 1) + l];
+        int nib = gi < 2 ? (qlb & 0xF) : (qlb >> 4);
+        int qv = (nib | (((A[128 + 32 * h + l] >> (2 * gi)) & 3) << 4)) - 32;
+        const uint8_t *S = W.s + (size_t)row * W.s_row + (size_t)b * 16;
+        const uint8_t *Dp = W.d + (size_t)row * W.d_row + (size_t)b * 2;
+        float d = h2f(Dp[0] | (Dp[1] << 8));
+        int sc = (int)(int8_t)S[8 * h + (rr >> 4)];
+        return fm(fm(d, (float)sc), (float)qv);
+    }
+    case 11: {
+        const int h = r >> 7, rr = r & 127, r4 = rr >> 5, l = rr & 31, g = 4 * h + r4;
+        const uint8_t *S = W.s + (size_t)row * W.s_row + (size_t)b * 12;
+        const uint8_t *Dp = W.d + (size_t)row * W.d_row + (size_t)b * 2;
+        uint32_t a0 = S[0] | (S[1] << 8) | (S[2] << 16) | ((uint32_t)S[3] << 24);
+        uint32_t a1 = S[4] | (S[5] << 8) | (S[6] << 16) | ((uint32_t)S[7] << 24);
+        uint32_t tt = S[8] | (S[9] << 8) | (S[10] << 16) | ((uint32_t)S[11] << 24);
+        const int is = 2 * g + (l >> 4), wi = is >> 2;
+        uint32_t aa = (wi & 1) ? a1 : a0;
+        uint32_t wq = ((aa >> ((wi >> 1) * 4)) & 0x0F0F0F0Fu) | (((tt >> (2 * wi)) & 0x03030303u) << 4);
+        int sc = (int)((wq >> (8 * (is & 3))) & 0xFF);
+        float d = h2f(Dp[0] | (Dp[1] << 8));
+        float dl = fm(d, fs((float)sc, 32.0f));
+        int hi = (A[l] >> g) & 1 ? 0 : 4;
+        int qv = ((A[32 + 32 * h + l] >> (2 * r4)) & 3) - hi;
+        return fm(dl, (float)qv);
+    }
+    default: {  // 10
+        const int h = r >> 7, rr = r & 127, r4 = rr >> 5, l = rr & 31, g = 4 * h + r4;
+        const uint8_t *S = W.s + (size_t)row * W.s_row + (size_t)b * 16;
+        const uint8_t *Dp = W.d + (size_t)row * W.d_row + (size_t)b * 4;
+        float d = h2f(Dp[0] | (Dp[1] << 8)), dm = h2f(Dp[2] | (Dp[3] << 8));
+        int sc = S[2 * g + (l >> 4)];
+        float dl = fm(d, (float)(sc & 0xF)), ml = fm(dm, (float)(sc >> 4));
+        int qv = (A[32 * h + l] >> (2 * r4)) & 3;
+        return fs(fm(dl, (float)qv), ml);
+    }
+    }
+}
+
+}  // namespace cxm

@@ -1,0 +1,1038 @@
+// Host orchestration of the decode path: model upload (k-quant planes in
+// HBM), KV caches, the per-token step captured as a CUDA graph, and the C ABI
+// of include/cxm.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/cxm.h"
+#include "cxm_internal.h"
+#include "step_kernels.cuh"
+
+using namespace cxm;
+
+#define CU(call)                                                                             \
+    do {                                                                                     \
+        cudaError_t e_ = (call);                                                             \
+        if (e_ != cudaSuccess) {                                                             \
+            set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+            return -1;                                                                       \
+        }                                                                                    \
+    } while (0)
+
+namespace {
+
+struct Layer {
+    DMat q, k, v, o, gate, up, down;
+    float *attn_norm, *ffn_norm, *bq, *bk, *bv;
+};
+
+}  // namespace
+
+struct cxm_model {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    cxm_config cfg{};
+    std::vector<Layer> layers;
+    DMat embd{}, out{};
+    float *embd_f32 = nullptr;
+    float *out_norm = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    std::vector<void *> allocs;
+    float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr, *part = nullptr;
+    int *counter = nullptr, *err = nullptr;
+    unsigned long long *argmax_key = nullptr;
+    int P = 64, S_max = 1;
+    int sms = 148, mv_blocks = 148;
+    uint64_t weight_bytes = 0;
+    bool logits_valid = false;
+
+    ~cxm_model() {
+        if (device >= 0) cudaSetDevice(device);
+        for (void *p : allocs) cudaFree(p);
+        if (stream) cudaStreamDestroy(stream);
+    }
+    template <class T>
+    int alloc(T **p, size_t n) {
+        void *v = nullptr;
+        cudaError_t e = cudaMalloc(&v, std::max<size_t>(n * sizeof(T), 256));
+        if (e != cudaSuccess) {
+            set_error("cudaMalloc of %zu bytes failed: %s", n * sizeof(T), cudaGetErrorString(e));
+            return -1;
+        }
+        allocs.push_back(v);
+        *p = (T *)v;
+        return 0;
+    }
+};
+
+struct cxm_cache {
+    cxm_model *m = nullptr;
+    uint32_t max_tokens = 0, len = 0;
+    float *k = nullptr, *v = nullptr;  // [n_layer][max_tokens][kvd]
+    uint32_t *toks = nullptr;          // [max_tokens + 1]
+    int *d_len = nullptr;
+    cudaGraphExec_t graph[3] = {nullptr, nullptr, nullptr};
+    ~cxm_cache() {
+        if (m) cudaSetDevice(m->device);
+        for (auto &g : graph)
+            if (g) cudaGraphExecDestroy(g);
+        cudaFree(k);
+        cudaFree(v);
+        cudaFree(toks);
+        cudaFree(d_len);
+    }
+};
+
+struct cxm_sampler {
+    uint64_t state;
+    float temperature, top_p;
+};
+
+namespace {
+
+enum StepMode { STEP_PREFILL = 0, STEP_GREEDY = 1, STEP_LOGITS = 2 };
+
+size_t kv_dim(const cxm_model *m) { return (size_t)m->cfg.n_head_kv * m->cfg.head_dim; }
+
+// Split the GGUF super-blocks of a matrix into the 16-byte-aligned planes of
+// DMat and upload them (src/quant.rs layouts; the bytes are not changed).
+int upload_matrix(cxm_model *m, const Gguf &g, const TensorInfo &t, DMat *out) {
+    if (t.dims.size() != 2) {
+        set_error("%s: expected a matrix", t.name.c_str());
+        return -1;
+    }
+    if (!is_kquant(t.type)) {
+        set_error("%s: type %d has no device kernel (k-quants Q2_K..Q6_K only)", t.name.c_str(), t.type);
+        return -1;
+    }
+    const int K = (int)t.dims[0], rows = (int)t.dims[1];
+    if (K % 256) {
+        set_error("%s: rows of %d values are not a multiple of 256", t.name.c_str(), K);
+        return -1;
+    }
+    const int nblk = K / 256, bb = bytes_per_block(t.type);
+    const int pa = plane_a_bytes(t.type), ps = plane_s_bytes(t.type), pd = plane_d_bytes(t.type);
+    DMat d{};
+    d.type = t.type;
+    d.rows = rows;
+    d.K = K;
+    d.nblk = nblk;
+    d.a_row = (uint32_t)(nblk * pa);
+    d.s_row = (uint32_t)(nblk * ps);
+    d.d_row = (uint32_t)(nblk * pd);
+    std::vector<uint8_t> A((size_t)rows * d.a_row), S((size_t)rows * d.s_row), D((size_t)rows * d.d_row);
+    const uint8_t *src = g.data(t);
+    for (int r = 0; r < rows; r++) {
+        for (int b = 0; b < nblk; b++) {
+            const uint8_t *blk = src + ((size_t)r * nblk + b) * bb;
+            uint8_t *a = A.data() + (size_t)r * d.a_row + (size_t)b * pa;
+            uint8_t *s = S.data() + (size_t)r * d.s_row + (size_t)b * ps;
+            uint8_t *dd = D.data() + (size_t)r * d.d_row + (size_t)b * pd;
+            switch (t.type) {
+            case Q4K: case Q5K: memcpy(a, blk, (size_t)bb); break;
+            case Q6K: memcpy(a, blk, 192); memcpy(s, blk + 192, 16); memcpy(dd, blk + 208, 2); break;
+            case Q3K: memcpy(a, blk, 96); memcpy(s, blk + 96, 12); memcpy(dd, blk + 108, 2); break;
+            case Q2K: memcpy(a, blk + 16, 64); memcpy(s, blk, 16); memcpy(dd, blk + 80, 4); break;
+            }
+        }
+    }
+    uint8_t *da = nullptr, *ds = nullptr, *dd = nullptr;
+    if (m->alloc(&da, A.size())) return -1;
+    CU(cudaMemcpy(da, A.data(), A.size(), cudaMemcpyHostToDevice));
+    if (ps) {
+        if (m->alloc(&ds, S.size())) return -1;
+        CU(cudaMemcpy(ds, S.data(), S.size(), cudaMemcpyHostToDevice));
+    }
+    if (pd) {
+        if (m->alloc(&dd, D.size())) return -1;
+        CU(cudaMemcpy(dd, D.data(), D.size(), cudaMemcpyHostToDevice));
+    }
+    d.a = da;
+    d.s = ds;
+    d.d = dd;
+    *out = d;
+    m->weight_bytes += (uint64_t)t.nbytes;
+    return 0;
+}
+
+int upload_vector(cxm_model *m, const Gguf &g, const TensorInfo &t, size_t n, float **out) {
+    if (t.elements() != n) {
+        set_error("%s: %llu values, expected %zu", t.name.c_str(), (unsigned long long)t.elements(), n);
+        return -1;
+    }
+    std::vector<float> h(n);
+    const uint8_t *src = g.data(t);
+    if (t.type == F32) {
+        memcpy(h.data(), src, n * 4);
+    } else if (t.type == F16) {
+        for (size_t i = 0; i < n; i++) h[i] = f16_to_f32((uint16_t)(src[2 * i] | (src[2 * i + 1] << 8)));
+    } else {
+        set_error("%s: vectors must be F32 or F16", t.name.c_str());
+        return -1;
+    }
+    if (m->alloc(out, n)) return -1;
+    CU(cudaMemcpy(*out, h.data(), n * 4, cudaMemcpyHostToDevice));
+    m->weight_bytes += (uint64_t)t.nbytes;
+    return 0;
+}
+
+int sub_of(int type) { return (type == Q4K || type == Q5K) ? 32 : 16; }
+
+void set_need(MatvecParams &p, const DMat &a) {
+    if (sub_of(a.type) == 16) p.need16 = 1; else p.need32 = 1;
+}
+
+size_t matvec_smem(const MatvecParams &p) {
+    size_t b = 0;
+    if (p.need16) b += (size_t)p.K + (size_t)p.K / 16 * 8;
+    if (p.need32) b += (size_t)p.K + (size_t)p.K / 32 * 8;
+    return (b + 15) & ~(size_t)15;
+}
+
+int launch_matvec(cxm_model *m, MatvecParams &p) {
+    p.total_units = 0;
+    for (int i = 0; i < p.nseg; i++) p.total_units += p.seg[i].units;
+    p.err = m->err;
+    int blocks = std::min((p.total_units + kWarps - 1) / kWarps, m->mv_blocks);
+    k_matvec<<<blocks, kThreads, matvec_smem(p), m->stream>>>(p);
+    CU(cudaGetLastError());
+    return 0;
+}
+
+Seg make_seg(const DMat &A, int pairing, int epi, float *out) {
+    Seg s{};
+    s.A = A;
+    s.B = A;
+    s.pairing = pairing;
+    s.epi = epi;
+    s.units = pairing == PAIR_TWO ? A.rows : A.rows / 2;
+    s.out = out;
+    return s;
+}
+
+int launch_attention(cxm_model *m, cxm_cache *c, int layer) {
+    const cxm_config &cfg = m->cfg;
+    AttnParams a{};
+    a.q = m->q;
+    a.k = c->k + (size_t)layer * c->max_tokens * kv_dim(m);
+    a.v = c->v + (size_t)layer * c->max_tokens * kv_dim(m);
+    a.out = m->att;
+    a.part = m->part;
+    a.counter = m->counter;
+    a.d_len = c->d_len;
+    a.H = cfg.n_head;
+    a.KV = cfg.n_head_kv;
+    a.P = m->P;
+    a.S_max = m->S_max;
+    a.max_pos = (int)c->max_tokens;
+    a.scale = 1.0f / sqrtf((float)cfg.head_dim);
+    a.err = m->err;
+    const int G = cfg.n_head / cfg.n_head_kv, hd = cfg.head_dim;
+    const int tpd = kAttnThreads / hd;
+    size_t smem = (size_t)(G * hd + G * m->P + 2 * G + 8 + (tpd > 1 ? tpd * kGMax * hd : 0)) * 4;
+    dim3 grid(cfg.n_head_kv, m->S_max);
+    switch (hd) {
+    case 32: k_attention<32><<<grid, kAttnThreads, smem, m->stream>>>(a); break;
+    case 64: k_attention<64><<<grid, kAttnThreads, smem, m->stream>>>(a); break;
+    case 128: k_attention<128><<<grid, kAttnThreads, smem, m->stream>>>(a); break;
+    default: set_error("head_dim %d unsupported (32, 64, 128)", hd); return -1;
+    }
+    CU(cudaGetLastError());
+    return 0;
+}
+
+// One token of src/forward.rs:375-505 on the device, for the token at
+// toks[*d_len]; ends by advancing *d_len (and, in STEP_GREEDY, writing the
+// argmax token at toks[*d_len + 1]).
+int enqueue_step(cxm_model *m, cxm_cache *c, int mode) {
+    const cxm_config &cfg = m->cfg;
+    const int D = cfg.dim, hd = cfg.head_dim, F = cfg.ffn;
+    const size_t kvd = kv_dim(m);
+    const bool logits = mode != STEP_PREFILL;
+    EmbedParams e{};
+    e.E = m->embd;
+    e.e32 = m->embd_f32;
+    e.toks = c->toks;
+    e.d_len = c->d_len;
+    e.dim = D;
+    e.vocab = cfg.vocab;
+    e.max_pos = (int)c->max_tokens;
+    e.x = m->x;
+    e.argmax_key = logits ? m->argmax_key : nullptr;
+    e.err = m->err;
+    k_embed<<<(D + 255) / 256, 256, 0, m->stream>>>(e);
+    CU(cudaGetLastError());
+
+    for (int l = 0; l < cfg.n_layer; l++) {
+        const Layer &L = m->layers[l];
+        float *kl = c->k + (size_t)l * c->max_tokens * kvd, *vl = c->v + (size_t)l * c->max_tokens * kvd;
+        {  // RMSNorm + quantize, q/k/v with bias, RoPE, KV append
+            MatvecParams p{};
+            p.nseg = 3;
+            p.seg[0] = make_seg(L.q, PAIR_ROPE, EPI_ROPE, m->q);
+            p.seg[0].half = hd / 2;
+            p.seg[0].bias = L.bq;
+            p.seg[1] = make_seg(L.k, PAIR_ROPE, EPI_ROPE, kl);
+            p.seg[1].half = hd / 2;
+            p.seg[1].bias = L.bk;
+            p.seg[1].at_pos = 1;
+            p.seg[1].pos_stride = (int)kvd;
+            p.seg[2] = make_seg(L.v, PAIR_ADJ, EPI_STORE, vl);
+            p.seg[2].bias = L.bv;
+            p.seg[2].at_pos = 1;
+            p.seg[2].pos_stride = (int)kvd;
+            p.K = D;
+            p.prologue = PRO_NORM;
+            p.in = m->x;
+            p.norm_w = L.attn_norm;
+            p.eps = cfg.eps;
+            p.d_len = c->d_len;
+            p.max_pos = (int)c->max_tokens;
+            p.rope_cos = m->rope_cos;
+            p.rope_sin = m->rope_sin;
+            set_need(p, L.q);
+            set_need(p, L.k);
+            set_need(p, L.v);
+            if (launch_matvec(m, p)) return -1;
+        }
+        if (launch_attention(m, c, l)) return -1;
+        {  // o_proj + residual
+            MatvecParams p{};
+            p.nseg = 1;
+            p.seg[0] = make_seg(L.o, PAIR_ADJ, EPI_RESID, m->x);
+            p.K = D;
+            p.prologue = PRO_QUANT;
+            p.in = m->att;
+            p.d_len = c->d_len;
+            set_need(p, L.o);
+            if (launch_matvec(m, p)) return -1;
+        }
+        {  // RMSNorm + quantize, gate/up, SiLU·up
+            MatvecParams p{};
+            p.nseg = 1;
+            p.seg[0] = make_seg(L.gate, PAIR_TWO, EPI_SWIGLU, m->h);
+            p.seg[0].B = L.up;
+            p.K = D;
+            p.prologue = PRO_NORM;
+            p.in = m->x;
+            p.norm_w = L.ffn_norm;
+            p.eps = cfg.eps;
+            p.d_len = c->d_len;
+            set_need(p, L.gate);
+            set_need(p, L.up);
+            if (launch_matvec(m, p)) return -1;
+        }
+        {  // down + residual
+            MatvecParams p{};
+            p.nseg = 1;
+            p.seg[0] = make_seg(L.down, PAIR_ADJ, EPI_RESID, m->x);
+            p.K = F;
+            p.prologue = PRO_QUANT;
+            p.in = m->h;
+            p.d_len = c->d_len;
+            set_need(p, L.down);
+            if (launch_matvec(m, p)) return -1;
+        }
+    }
+    if (logits) {  // final RMSNorm, output projection, argmax
+        MatvecParams p{};
+        p.nseg = 1;
+        p.seg[0] = make_seg(m->out, PAIR_ADJ, EPI_LOGITS, m->logits);
+        p.K = D;
+        p.prologue = PRO_NORM;
+        p.in = m->x;
+        p.norm_w = m->out_norm;
+        p.eps = cfg.eps;
+        p.d_len = c->d_len;
+        p.argmax_key = m->argmax_key;
+        set_need(p, m->out);
+        if (launch_matvec(m, p)) return -1;
+    }
+    k_commit<<<1, 32, 0, m->stream>>>(c->d_len, c->toks, m->argmax_key, mode == STEP_GREEDY ? 1 : 0,
+                                      (int)c->max_tokens + 1);
+    CU(cudaGetLastError());
+    return 0;
+}
+
+int get_graph(cxm_model *m, cxm_cache *c, int mode, cudaGraphExec_t *out) {
+    if (c->graph[mode]) {
+        *out = c->graph[mode];
+        return 0;
+    }
+    cudaGraph_t g = nullptr;
+    CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(m, c, mode);
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return -1;
+    }
+    if (e != cudaSuccess) {
+        set_error("graph capture failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    e = cudaGraphInstantiate(&c->graph[mode], g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+        set_error("graph instantiate failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    *out = c->graph[mode];
+    return 0;
+}
+
+int run_steps(cxm_model *m, cxm_cache *c, int mode, uint32_t n) {
+    if (n == 0) return 0;
+    cudaGraphExec_t g;
+    if (get_graph(m, c, mode, &g)) return -1;
+    for (uint32_t i = 0; i < n; i++) CU(cudaGraphLaunch(g, m->stream));
+    return 0;
+}
+
+int check_err(cxm_model *m) {
+    CU(cudaStreamSynchronize(m->stream));
+    int e = 0;
+    CU(cudaMemcpy(&e, m->err, 4, cudaMemcpyDeviceToHost));
+    if (e) {
+        CU(cudaMemset(m->err, 0, 4));
+        set_error("device reported %s", (e & ERR_TOKEN) ? "a token beyond the vocabulary" : "a position beyond the cache");
+        return -1;
+    }
+    return 0;
+}
+
+}  // namespace
+
+// ─────────────────────────────── C ABI ───────────────────────────────
+
+extern "C" const char *cxm_last_error(void) { return last_error(); }
+
+extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
+    if (!path || !out) {
+        set_error("null argument");
+        return -1;
+    }
+    *out = nullptr;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        set_error("no CUDA device: this library has no CPU path");
+        return -1;
+    }
+    if (device < 0 || device >= ndev) {
+        set_error("device %d out of range (%d devices)", device, ndev);
+        return -1;
+    }
+    CU(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CU(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) {
+        set_error("device %d is sm_%d%d; this build targets sm_100a", device, prop.major, prop.minor);
+        return -1;
+    }
+    Gguf g;
+    if (!g.open(path)) return -1;
+    std::unique_ptr<cxm_model> m(new cxm_model);
+    m->device = device;
+    m->sms = prop.multiProcessorCount;
+    cxm_config &cfg = m->cfg;
+    uint64_t v;
+    const char *ik[] = {"qwen2.block_count", "qwen2.embedding_length", "qwen2.attention.head_count",
+                        "qwen2.attention.head_count_kv", "qwen2.context_length"};
+    int32_t *iv[] = {&cfg.n_layer, &cfg.dim, &cfg.n_head, &cfg.n_head_kv, &cfg.ctx};
+    for (int i = 0; i < 5; i++) {
+        if (!g.meta_int(ik[i], &v)) {
+            set_error("missing metadata %s", ik[i]);
+            return -1;
+        }
+        *iv[i] = (int32_t)v;
+    }
+    double dv;
+    cfg.eps = g.meta_float("qwen2.attention.layer_norm_rms_epsilon", &dv) ? (float)dv : 1e-6f;
+    cfg.rope_base = g.meta_float("qwen2.rope.freq_base", &dv) ? (float)dv : 10000.0f;
+    if (g.meta_int("tokenizer.ggml.eos_token_id", &v)) {
+        cfg.has_eos = 1;
+        cfg.eos = (uint32_t)v;
+    }
+    if (cfg.n_head <= 0 || cfg.dim % cfg.n_head || cfg.n_head_kv <= 0 || cfg.n_head % cfg.n_head_kv) {
+        set_error("inconsistent head counts");
+        return -1;
+    }
+    cfg.head_dim = cfg.dim / cfg.n_head;
+    const TensorInfo *embd = g.tensor("token_embd.weight");
+    const TensorInfo *outw = g.tensor("output.weight");
+    const TensorInfo *onorm = g.tensor("output_norm.weight");
+    if (!embd || !onorm) {
+        set_error("missing tensor %s", embd ? "output_norm.weight" : "token_embd.weight");
+        return -1;
+    }
+    cfg.vocab = (int32_t)embd->dims[1];
+    cfg.tied = outw == nullptr;
+    CU(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    if (embd->type == F32) {
+        if (upload_vector(m.get(), g, *embd, (size_t)cfg.vocab * cfg.dim, &m->embd_f32)) return -1;
+        m->embd.type = 0;
+    } else if (upload_matrix(m.get(), g, *embd, &m->embd)) {
+        return -1;
+    }
+    if (outw) {
+        if (upload_matrix(m.get(), g, *outw, &m->out)) return -1;
+    } else {
+        if (embd->type == F32) {
+            set_error("a tied F32 embedding table has no device output kernel");
+            return -1;
+        }
+        m->out = m->embd;
+    }
+    if (upload_vector(m.get(), g, *onorm, (size_t)cfg.dim, &m->out_norm)) return -1;
+    const size_t hd = (size_t)cfg.head_dim, kvd = (size_t)cfg.n_head_kv * hd;
+    for (int i = 0; i < cfg.n_layer; i++) {
+        Layer L{};
+        auto T = [&](const char *nm) -> const TensorInfo * {
+            std::string n = "blk." + std::to_string(i) + "." + nm;
+            const TensorInfo *t = g.tensor(n);
+            if (!t) set_error("missing tensor %s", n.c_str());
+            return t;
+        };
+        const TensorInfo *t;
+        if (!(t = T("attn_norm.weight")) || upload_vector(m.get(), g, *t, cfg.dim, &L.attn_norm)) return -1;
+        if (!(t = T("attn_q.weight")) || upload_matrix(m.get(), g, *t, &L.q)) return -1;
+        if (!(t = T("attn_q.bias")) || upload_vector(m.get(), g, *t, cfg.dim, &L.bq)) return -1;
+        if (!(t = T("attn_k.weight")) || upload_matrix(m.get(), g, *t, &L.k)) return -1;
+        if (!(t = T("attn_k.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bk)) return -1;
+        if (!(t = T("attn_v.weight")) || upload_matrix(m.get(), g, *t, &L.v)) return -1;
+        if (!(t = T("attn_v.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bv)) return -1;
+        if (!(t = T("attn_output.weight")) || upload_matrix(m.get(), g, *t, &L.o)) return -1;
+        if (!(t = T("ffn_norm.weight")) || upload_vector(m.get(), g, *t, cfg.dim, &L.ffn_norm)) return -1;
+        if (!(t = T("ffn_gate.weight")) || upload_matrix(m.get(), g, *t, &L.gate)) return -1;
+        if (!(t = T("ffn_up.weight")) || upload_matrix(m.get(), g, *t, &L.up)) return -1;
+        if (!(t = T("ffn_down.weight")) || upload_matrix(m.get(), g, *t, &L.down)) return -1;
+        if (L.q.rows != cfg.dim || L.k.rows != (int)kvd || L.v.rows != (int)kvd || L.o.rows != cfg.dim ||
+            L.gate.rows != L.up.rows || L.down.K != L.gate.rows || L.down.rows != cfg.dim) {
+            set_error("layer %d: matrix shapes do not match the config", i);
+            return -1;
+        }
+        m->layers.push_back(L);
+    }
+    cfg.ffn = m->layers.empty() ? 0 : m->layers[0].gate.rows;
+    // RoPE tables exactly as src/ops.rs:1108-1129 (f32 frequency, f64 angle)
+    {
+        const int half = cfg.head_dim / 2;
+        std::vector<float> c((size_t)cfg.ctx * half), s((size_t)cfg.ctx * half);
+        for (int j = 0; j < half; j++) {
+            volatile float expo = 2.0f * (float)j / (float)cfg.head_dim;
+            float freq = 1.0f / powf(cfg.rope_base, expo);
+            for (int p = 0; p < cfg.ctx; p++) {
+                double ang = (double)p * (double)freq;
+                c[(size_t)p * half + j] = (float)cos(ang);
+                s[(size_t)p * half + j] = (float)sin(ang);
+            }
+        }
+        if (m->alloc(&m->rope_cos, c.size()) || m->alloc(&m->rope_sin, s.size())) return -1;
+        CU(cudaMemcpy(m->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+        CU(cudaMemcpy(m->rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+    }
+    // activations and scratch
+    const int G = cfg.n_head / cfg.n_head_kv;
+    m->P = std::max(32, std::min(256, ((cfg.ctx * cfg.n_head_kv + 2 * m->sms - 1) / (2 * m->sms) + 31) / 32 * 32));
+    m->S_max = (cfg.ctx + m->P - 1) / m->P;
+    (void)G;
+    if (m->alloc(&m->x, cfg.dim) || m->alloc(&m->q, cfg.dim) || m->alloc(&m->att, cfg.dim) ||
+        m->alloc(&m->h, std::max(cfg.ffn, 1)) || m->alloc(&m->logits, cfg.vocab) ||
+        m->alloc(&m->part, (size_t)cfg.n_head * m->S_max * (hd + 2)) || m->alloc(&m->counter, cfg.n_head_kv) ||
+        m->alloc(&m->err, 1) || m->alloc(&m->argmax_key, 1))
+        return -1;
+    CU(cudaMemset(m->counter, 0, sizeof(int) * cfg.n_head_kv));
+    CU(cudaMemset(m->err, 0, sizeof(int)));
+    CU(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    int occ = 0;
+    CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_matvec, kThreads, 40 * 1024));
+    m->mv_blocks = m->sms * std::max(occ, 1);
+    CU(cudaDeviceSynchronize());
+    *out = m.release();
+    return 0;
+}
+
+extern "C" int cxm_model_config(const cxm_model *m, cxm_config *out) {
+    if (!m || !out) {
+        set_error("null argument");
+        return -1;
+    }
+    *out = m->cfg;
+    return 0;
+}
+
+extern "C" uint64_t cxm_model_weight_bytes(const cxm_model *m) { return m ? m->weight_bytes : 0; }
+
+extern "C" void cxm_model_close(cxm_model *m) { delete m; }
+
+extern "C" int cxm_cache_new(cxm_model *m, uint32_t max_tokens, cxm_cache **out) {
+    if (!m || !out) {
+        set_error("null argument");
+        return -1;
+    }
+    *out = nullptr;
+    if (max_tokens == 0 || max_tokens > (uint32_t)m->cfg.ctx) {
+        set_error("max_tokens %u must be in 1..=%d (the context)", max_tokens, m->cfg.ctx);
+        return -1;
+    }
+    CU(cudaSetDevice(m->device));
+    std::unique_ptr<cxm_cache> c(new cxm_cache);
+    c->m = m;
+    c->max_tokens = max_tokens;
+    size_t n = (size_t)m->cfg.n_layer * max_tokens * kv_dim(m);
+    CU(cudaMalloc(&c->k, n * 4));
+    CU(cudaMalloc(&c->v, n * 4));
+    CU(cudaMalloc(&c->toks, ((size_t)max_tokens + 2) * 4));
+    CU(cudaMalloc(&c->d_len, 4));
+    CU(cudaMemset(c->d_len, 0, 4));
+    CU(cudaMemset(c->toks, 0, ((size_t)max_tokens + 2) * 4));
+    *out = c.release();
+    return 0;
+}
+
+extern "C" void cxm_cache_free(cxm_cache *c) { delete c; }
+extern "C" uint32_t cxm_cache_len(const cxm_cache *c) { return c ? c->len : 0; }
+
+static int set_len(cxm_cache *c, uint32_t n) {
+    cudaSetDevice(c->m->device);
+    int v = (int)n;
+    CU(cudaMemcpyAsync(c->d_len, &v, 4, cudaMemcpyHostToDevice, c->m->stream));
+    CU(cudaStreamSynchronize(c->m->stream));
+    c->len = n;
+    return 0;
+}
+
+extern "C" int cxm_cache_truncate(cxm_cache *c, uint32_t n) {
+    if (!c) {
+        set_error("null cache");
+        return -1;
+    }
+    if (n >= c->len) return 0;  // Cache::truncar keeps everything when n >= len
+    return set_len(c, n);
+}
+
+extern "C" int cxm_cache_clear(cxm_cache *c) {
+    if (!c) {
+        set_error("null cache");
+        return -1;
+    }
+    return set_len(c, 0);
+}
+
+extern "C" int cxm_cache_copy_prefix(const cxm_cache *src, uint32_t n, cxm_cache *dst) {
+    if (!src || !dst || src->m != dst->m) {
+        set_error("caches must exist and belong to the same model");
+        return -1;
+    }
+    cxm_model *m = src->m;
+    n = std::min(n, src->len);
+    if (n > dst->max_tokens) {
+        set_error("prefix of %u tokens does not fit a cache of %u", n, dst->max_tokens);
+        return -1;
+    }
+    CU(cudaSetDevice(m->device));
+    const size_t kvd = kv_dim(m);
+    if (n) {
+        CU(cudaMemcpy2DAsync(dst->k, dst->max_tokens * kvd * 4, src->k, src->max_tokens * kvd * 4, n * kvd * 4,
+                             m->cfg.n_layer, cudaMemcpyDeviceToDevice, m->stream));
+        CU(cudaMemcpy2DAsync(dst->v, dst->max_tokens * kvd * 4, src->v, src->max_tokens * kvd * 4, n * kvd * 4,
+                             m->cfg.n_layer, cudaMemcpyDeviceToDevice, m->stream));
+        CU(cudaMemcpyAsync(dst->toks, src->toks, (size_t)(n + 1 <= src->max_tokens + 1 ? n + 1 : n) * 4,
+                           cudaMemcpyDeviceToDevice, m->stream));
+    }
+    return set_len(dst, n);
+}
+
+extern "C" int cxm_cache_read(const cxm_cache *c, uint32_t layer, int is_v, float *host_out) {
+    if (!c || !host_out || layer >= (uint32_t)c->m->cfg.n_layer) {
+        set_error("bad cache read");
+        return -1;
+    }
+    cxm_model *m = c->m;
+    CU(cudaSetDevice(m->device));
+    const size_t kvd = kv_dim(m);
+    const float *base = (is_v ? c->v : c->k) + (size_t)layer * c->max_tokens * kvd;
+    CU(cudaStreamSynchronize(m->stream));
+    CU(cudaMemcpy(host_out, base, (size_t)c->len * kvd * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+extern "C" int cxm_forward(cxm_model *m, cxm_cache *c, const uint32_t *tokens, uint32_t n, float *logits_out) {
+    if (!m || !c || c->m != m || (!tokens && n)) {
+        set_error("bad arguments");
+        return -1;
+    }
+    if (n == 0) {
+        set_error("no tokens to process");  // src/forward.rs:376-378
+        return -1;
+    }
+    if ((uint64_t)c->len + n > (uint64_t)m->cfg.ctx) {
+        set_error("%llu tokens exceed the context of %d", (unsigned long long)c->len + n, m->cfg.ctx);
+        return -1;
+    }
+    if ((uint64_t)c->len + n > c->max_tokens) {
+        set_error("%llu tokens exceed the cache of %u", (unsigned long long)c->len + n, c->max_tokens);
+        return -1;
+    }
+    for (uint32_t i = 0; i < n; i++)
+        if (tokens[i] >= (uint32_t)m->cfg.vocab) {
+            set_error("token %u does not fit a vocabulary of %d", tokens[i], m->cfg.vocab);
+            return -1;
+        }
+    CU(cudaSetDevice(m->device));
+    CU(cudaMemcpyAsync(c->toks + c->len, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, m->stream));
+    if (run_steps(m, c, STEP_PREFILL, n - 1) || run_steps(m, c, STEP_LOGITS, 1)) return -1;
+    if (logits_out)
+        CU(cudaMemcpyAsync(logits_out, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    if (check_err(m)) return -1;
+    c->len += n;
+    m->logits_valid = true;
+    return 0;
+}
+
+extern "C" int cxm_sampler_new(uint64_t seed, float temperature, float top_p, cxm_sampler **out) {
+    if (!out) {
+        set_error("null argument");
+        return -1;
+    }
+    cxm_sampler *s = new cxm_sampler;
+    s->state = seed == 0 ? 0x9E3779B97F4A7C15ull : seed;
+    s->temperature = temperature;
+    s->top_p = top_p < 0.0f ? 0.0f : (top_p > 1.0f ? 1.0f : top_p);
+    *out = s;
+    return 0;
+}
+extern "C" void cxm_sampler_free(cxm_sampler *s) { delete s; }
+extern "C" uint64_t cxm_sampler_state(const cxm_sampler *s) { return s ? s->state : 0; }
+
+extern "C" int cxm_sample(cxm_model *m, cxm_sampler *s, uint32_t *token_out) {
+    if (!m || !s || !token_out) {
+        set_error("null argument");
+        return -1;
+    }
+    if (!m->logits_valid) {
+        set_error("no logits: call cxm_forward first");
+        return -1;
+    }
+    if (s->temperature > 0.0f) {
+        set_error("temperature sampling is not available yet");
+        return -1;
+    }
+    CU(cudaSetDevice(m->device));
+    unsigned long long key = 0;
+    CU(cudaStreamSynchronize(m->stream));
+    CU(cudaMemcpy(&key, m->argmax_key, 8, cudaMemcpyDeviceToHost));
+    *token_out = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
+    return 0;
+}
+
+extern "C" int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, uint32_t n_prompt, uint32_t max_new,
+                            cxm_sampler *s, uint32_t *out, uint32_t *n_out) {
+    if (!m || !c || !s || !n_out || (max_new && !out) || c->m != m) {
+        set_error("bad arguments");
+        return -1;
+    }
+    *n_out = 0;
+    if (n_prompt == 0 || !prompt) {
+        set_error("no tokens to process");
+        return -1;
+    }
+    if (s->temperature > 0.0f) {
+        set_error("temperature sampling is not available yet");
+        return -1;
+    }
+    const uint64_t after = (uint64_t)c->len + n_prompt;
+    const uint64_t limit = std::min<uint64_t>((uint64_t)m->cfg.ctx, c->max_tokens);
+    if (after > limit) {
+        set_error("%llu tokens exceed the context of %llu", (unsigned long long)after, (unsigned long long)limit);
+        return -1;
+    }
+    for (uint32_t i = 0; i < n_prompt; i++)
+        if (prompt[i] >= (uint32_t)m->cfg.vocab) {
+            set_error("token %u does not fit a vocabulary of %d", prompt[i], m->cfg.vocab);
+            return -1;
+        }
+    CU(cudaSetDevice(m->device));
+    const uint32_t len0 = c->len;
+    CU(cudaMemcpyAsync(c->toks + len0, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, m->stream));
+    if (run_steps(m, c, STEP_PREFILL, n_prompt - 1)) return -1;
+    if (max_new == 0) {
+        // the prompt is still forwarded (logits of the last token)
+        if (run_steps(m, c, STEP_LOGITS, 1) || check_err(m)) return -1;
+        c->len = (uint32_t)after;
+        m->logits_valid = true;
+        return 0;
+    }
+    // src/forward.rs:544-557: pick, push, stop at the context, forward.
+    // Generated tokens: min(max_new, limit - after + 1); each one except a
+    // context-limited last one is forwarded.
+    const uint64_t gen = std::min<uint64_t>(max_new, limit - after + 1);
+    const uint64_t fwd = std::min<uint64_t>(max_new, limit - after);
+    // step i (0..gen) forwards toks[after-1+i] and writes token i at toks[after+i]
+    if (run_steps(m, c, STEP_GREEDY, (uint32_t)gen)) return -1;
+    if (fwd == gen && run_steps(m, c, STEP_PREFILL, 1)) return -1;
+    if (check_err(m)) return -1;
+    std::vector<uint32_t> toks(gen);
+    CU(cudaMemcpy(toks.data(), c->toks + after, gen * 4, cudaMemcpyDeviceToHost));
+    uint64_t n = gen, forwarded = fwd;
+    if (m->cfg.has_eos) {
+        for (uint64_t i = 0; i < gen; i++)
+            if (toks[i] == m->cfg.eos) {
+                n = i;
+                forwarded = i;
+                break;
+            }
+    }
+    for (uint64_t i = 0; i < n; i++) out[i] = toks[i];
+    *n_out = (uint32_t)n;
+    uint32_t final_len = (uint32_t)(after + forwarded);
+    if (set_len(c, final_len)) return -1;
+    m->logits_valid = false;
+    return 0;
+}
+
+// ── kernel-level entry points ──
+
+namespace {
+struct DevBuf {
+    void *p = nullptr;
+    ~DevBuf() { cudaFree(p); }
+};
+int dev_matrix_from_host(int type, const uint8_t *w, uint32_t rows, uint32_t k, DevBuf bufs[3], DMat *out) {
+    if (!is_kquant(type) || k % 256 || rows == 0) {
+        set_error("type %d, k %u: not a k-quant matrix", type, k);
+        return -1;
+    }
+    const int nblk = (int)(k / 256), bb = bytes_per_block(type);
+    const int pa = plane_a_bytes(type), ps = plane_s_bytes(type), pd = plane_d_bytes(type);
+    DMat d{};
+    d.type = type;
+    d.rows = (int)rows;
+    d.K = (int)k;
+    d.nblk = nblk;
+    d.a_row = (uint32_t)(nblk * pa);
+    d.s_row = (uint32_t)(nblk * ps);
+    d.d_row = (uint32_t)(nblk * pd);
+    std::vector<uint8_t> A((size_t)rows * d.a_row), S((size_t)rows * d.s_row + 16), D((size_t)rows * d.d_row + 16);
+    for (uint32_t r = 0; r < rows; r++)
+        for (int b = 0; b < nblk; b++) {
+            const uint8_t *blk = w + ((size_t)r * nblk + b) * bb;
+            uint8_t *a = A.data() + (size_t)r * d.a_row + (size_t)b * pa;
+            uint8_t *s = S.data() + (size_t)r * d.s_row + (size_t)b * ps;
+            uint8_t *dd = D.data() + (size_t)r * d.d_row + (size_t)b * pd;
+            switch (type) {
+            case Q4K: case Q5K: memcpy(a, blk, (size_t)bb); break;
+            case Q6K: memcpy(a, blk, 192); memcpy(s, blk + 192, 16); memcpy(dd, blk + 208, 2); break;
+            case Q3K: memcpy(a, blk, 96); memcpy(s, blk + 96, 12); memcpy(dd, blk + 108, 2); break;
+            case Q2K: memcpy(a, blk + 16, 64); memcpy(s, blk, 16); memcpy(dd, blk + 80, 4); break;
+            }
+        }
+    CU(cudaMalloc(&bufs[0].p, A.size()));
+    CU(cudaMalloc(&bufs[1].p, S.size()));
+    CU(cudaMalloc(&bufs[2].p, D.size()));
+    CU(cudaMemcpy(bufs[0].p, A.data(), A.size(), cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(bufs[1].p, S.data(), S.size(), cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(bufs[2].p, D.data(), D.size(), cudaMemcpyHostToDevice));
+    d.a = (const uint8_t *)bufs[0].p;
+    d.s = (const uint8_t *)bufs[1].p;
+    d.d = (const uint8_t *)bufs[2].p;
+    *out = d;
+    return 0;
+}
+
+int need_device() {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        set_error("no CUDA device: this library has no CPU path");
+        return -1;
+    }
+    return 0;
+}
+}  // namespace
+
+extern "C" int cxm_debug_subblock_sums(int type, const uint8_t *row, const int8_t *xq, uint32_t nblk, int32_t *out) {
+    if (need_device()) return -1;
+    if (!row || !xq || !out || nblk == 0) {
+        set_error("bad arguments");
+        return -1;
+    }
+    DevBuf b[3], dx, dout;
+    DMat W;
+    if (dev_matrix_from_host(type, row, 1, nblk * 256, b, &W)) return -1;
+    const size_t K = (size_t)nblk * 256, nsub = K / (size_t)sub_of(type);
+    CU(cudaMalloc(&dx.p, K));
+    CU(cudaMalloc(&dout.p, nsub * 4));
+    CU(cudaMemcpy(dx.p, xq, K, cudaMemcpyHostToDevice));
+    size_t smem = ((K + 15) & ~(size_t)15) + K / 16 * 8;
+    if (smem > 48 * 1024) CU(cudaFuncSetAttribute(k_subblock_sums, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_subblock_sums<<<1, 256, smem>>>(W, (const int8_t *)dx.p, (int32_t *)dout.p);
+    CU(cudaGetLastError());
+    CU(cudaDeviceSynchronize());
+    CU(cudaMemcpy(out, dout.p, nsub * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint32_t k, const float *x, float *y) {
+    if (need_device()) return -1;
+    if (!w || !x || !y || rows % 2) {
+        set_error("bad arguments (rows must be even)");
+        return -1;
+    }
+    DevBuf b[3], dx, dy, dlen;
+    DMat W;
+    if (dev_matrix_from_host(type, w, rows, k, b, &W)) return -1;
+    CU(cudaMalloc(&dx.p, (size_t)k * 4));
+    CU(cudaMalloc(&dy.p, (size_t)rows * 4));
+    CU(cudaMemcpy(dx.p, x, (size_t)k * 4, cudaMemcpyHostToDevice));
+    MatvecParams p{};
+    p.nseg = 1;
+    p.seg[0] = make_seg(W, PAIR_ADJ, EPI_STORE, (float *)dy.p);
+    p.total_units = p.seg[0].units;
+    p.K = (int)k;
+    p.prologue = PRO_QUANT;
+    p.in = (const float *)dx.p;
+    set_need(p, W);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    CU(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    int blocks = std::min((p.total_units + kWarps - 1) / kWarps, sms * 4);
+    k_matvec<<<blocks, kThreads, matvec_smem(p)>>>(p);
+    CU(cudaGetLastError());
+    CU(cudaDeviceSynchronize());
+    CU(cudaMemcpy(y, dy.p, (size_t)rows * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+extern "C" int cxm_debug_attention(const float *q, const float *k, const float *v, uint32_t total, uint32_t heads,
+                                   uint32_t heads_kv, uint32_t hd, float *out) {
+    if (need_device()) return -1;
+    if (!q || !k || !v || !out || total == 0 || heads_kv == 0 || heads % heads_kv || (hd != 32 && hd != 64 && hd != 128)) {
+        set_error("bad attention arguments");
+        return -1;
+    }
+    const size_t kvd = (size_t)heads_kv * hd;
+    const int P = 64, S = (int)((total + P - 1) / P);
+    DevBuf dq, dk, dv, dout, dpart, dcnt, dlen, derr;
+    CU(cudaMalloc(&dq.p, (size_t)heads * hd * 4));
+    CU(cudaMalloc(&dk.p, total * kvd * 4));
+    CU(cudaMalloc(&dv.p, total * kvd * 4));
+    CU(cudaMalloc(&dout.p, (size_t)heads * hd * 4));
+    CU(cudaMalloc(&dpart.p, (size_t)heads * S * (hd + 2) * 4));
+    CU(cudaMalloc(&dcnt.p, heads_kv * 4));
+    CU(cudaMalloc(&dlen.p, 4));
+    CU(cudaMalloc(&derr.p, 4));
+    CU(cudaMemcpy(dq.p, q, (size_t)heads * hd * 4, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(dk.p, k, total * kvd * 4, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(dv.p, v, total * kvd * 4, cudaMemcpyHostToDevice));
+    CU(cudaMemset(dcnt.p, 0, heads_kv * 4));
+    CU(cudaMemset(derr.p, 0, 4));
+    int len = (int)total - 1;
+    CU(cudaMemcpy(dlen.p, &len, 4, cudaMemcpyHostToDevice));
+    AttnParams a{};
+    a.q = (const float *)dq.p;
+    a.k = (const float *)dk.p;
+    a.v = (const float *)dv.p;
+    a.out = (float *)dout.p;
+    a.part = (float *)dpart.p;
+    a.counter = (int *)dcnt.p;
+    a.d_len = (const int *)dlen.p;
+    a.H = (int)heads;
+    a.KV = (int)heads_kv;
+    a.P = P;
+    a.S_max = S;
+    a.max_pos = (int)total;
+    a.scale = 1.0f / sqrtf((float)hd);
+    a.err = (int *)derr.p;
+    const int G = (int)(heads / heads_kv), tpd = kAttnThreads / (int)hd;
+    size_t smem = (size_t)(G * (int)hd + G * P + 2 * G + 8 + (tpd > 1 ? tpd * kGMax * (int)hd : 0)) * 4;
+    dim3 grid(heads_kv, S);
+    if (hd == 32) k_attention<32><<<grid, kAttnThreads, smem>>>(a);
+    else if (hd == 64) k_attention<64><<<grid, kAttnThreads, smem>>>(a);
+    else k_attention<128><<<grid, kAttnThreads, smem>>>(a);
+    CU(cudaGetLastError());
+    CU(cudaDeviceSynchronize());
+    CU(cudaMemcpy(out, dout.p, (size_t)heads * hd * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+// ── measurement hooks ──
+
+extern "C" int cxm_step_launches(const cxm_model *m) { return m ? 3 + 5 * m->cfg.n_layer : 0; }
+
+extern "C" int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, float *ms_total) {
+    if (!m || !c || !ms_total || c->m != m) {
+        set_error("bad arguments");
+        return -1;
+    }
+    if (c->len == 0 || (uint64_t)c->len + steps + 1 > std::min<uint64_t>(c->max_tokens, (uint64_t)m->cfg.ctx)) {
+        set_error("cache needs a token to start from and room for %u more", steps);
+        return -1;
+    }
+    CU(cudaSetDevice(m->device));
+    // the step reads the token at toks[len]; start from the last cached one
+    if (set_len(c, c->len - 1)) return -1;
+    cudaGraphExec_t g;
+    if (get_graph(m, c, STEP_GREEDY, &g)) return -1;
+    cudaEvent_t e0, e1;
+    CU(cudaEventCreate(&e0));
+    CU(cudaEventCreate(&e1));
+    CU(cudaEventRecord(e0, m->stream));
+    for (uint32_t i = 0; i < steps; i++) CU(cudaGraphLaunch(g, m->stream));
+    CU(cudaEventRecord(e1, m->stream));
+    CU(cudaEventSynchronize(e1));
+    CU(cudaEventElapsedTime(ms_total, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (check_err(m)) return -1;
+    return set_len(c, c->len + steps);
+}
+
+extern "C" int cxm_bench_matvec(cxm_model *m, uint32_t reps, float *ms_per_launch, uint64_t *bytes_per_launch) {
+    if (!m || !ms_per_launch || !bytes_per_launch || reps == 0 || m->layers.empty()) {
+        set_error("bad arguments");
+        return -1;
+    }
+    CU(cudaSetDevice(m->device));
+    const cxm_config &cfg = m->cfg;
+    auto launch = [&](int l) -> int {
+        const Layer &L = m->layers[(size_t)l % m->layers.size()];
+        MatvecParams p{};
+        p.nseg = 1;
+        p.seg[0] = make_seg(L.gate, PAIR_TWO, EPI_SWIGLU, m->h);
+        p.seg[0].B = L.up;
+        p.K = cfg.dim;
+        p.prologue = PRO_NORM;
+        p.in = m->x;
+        p.norm_w = L.ffn_norm;
+        p.eps = cfg.eps;
+        set_need(p, L.gate);
+        set_need(p, L.up);
+        return launch_matvec(m, p);
+    };
+    for (int i = 0; i < 3; i++)
+        if (launch(i)) return -1;
+    cudaEvent_t e0, e1;
+    CU(cudaEventCreate(&e0));
+    CU(cudaEventCreate(&e1));
+    CU(cudaEventRecord(e0, m->stream));
+    for (uint32_t i = 0; i < reps; i++)
+        if (launch((int)i)) return -1;
+    CU(cudaEventRecord(e1, m->stream));
+    CU(cudaEventSynchronize(e1));
+    float ms = 0;
+    CU(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *ms_per_launch = ms / (float)reps;
+    const Layer &L = m->layers[0];
+    *bytes_per_launch = (uint64_t)L.gate.rows * (uint64_t)(L.gate.K / 256) * (uint64_t)bytes_per_block(L.gate.type) +
+                        (uint64_t)L.up.rows * (uint64_t)(L.up.K / 256) * (uint64_t)bytes_per_block(L.up.type);
+    return check_err(m);
+}

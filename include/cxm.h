@@ -1,0 +1,161 @@
+/*
+ * cxm.h — C ABI of the B200-native Cosxamix decode path.
+ *
+ * The library (cosxamix_b200/libcxm.so) replaces, behind plain pointers and
+ * sizes, the body of the reference's per-token forward and sampler. Citations
+ * name the reference interface each entry point replaces (paths inside the
+ * Cosxamix project).
+ *
+ * Conventions
+ *   - Every `int` result is 0 on success and negative on error; the message is
+ *     in cxm_last_error() (thread-local). This mirrors Result<_, String> ->
+ *     ErrorMotor::Interno (src/engine.rs:108-122, src/engine_own.rs:183).
+ *   - A model handle owns one CUDA stream and its scratch buffers. It is not
+ *     re-entrant: callers serialize, exactly as MotorPropio does with its
+ *     Mutex (src/engine_own.rs:62, :185).
+ *   - There is no CPU fallback: without a usable sm_100a device the open
+ *     calls fail.
+ */
+#ifndef CXM_H
+#define CXM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct cxm_model cxm_model;
+typedef struct cxm_cache cxm_cache;
+typedef struct cxm_sampler cxm_sampler;
+
+/* Mirrors forward::Config (src/forward.rs:36-55) plus the FFN width. */
+typedef struct {
+    int32_t n_layer, dim, n_head, n_head_kv, head_dim, vocab, ctx, ffn;
+    float eps, rope_base;
+    int32_t tied;      /* output projection shares token_embd (src/forward.rs:219-227) */
+    int32_t has_eos;   /* tokenizer.ggml.eos_token_id present (src/forward.rs:514-518) */
+    uint32_t eos;
+} cxm_config;
+
+/* ── model ─────────────────────────────────────────────────────────────── */
+
+/* Modelo::abrir (src/forward.rs:187-266): parse the GGUF, upload every tensor
+ * to HBM once (k-quant blocks repacked into 16-byte-aligned planes) and build
+ * the RoPE tables (src/ops.rs:1108-1129). */
+int  cxm_model_open(const char *gguf_path, int device, cxm_model **out);
+int  cxm_model_config(const cxm_model *m, cxm_config *out);
+/* bytes of weights resident on the device (the per-token weight stream) */
+uint64_t cxm_model_weight_bytes(const cxm_model *m);
+void cxm_model_close(cxm_model *m);
+
+/* ── KV cache (src/forward.rs:62-137) ─────────────────────────────────── */
+
+/* Cache::nuevo: f32 K and V per layer, [max_tokens x n_head_kv*head_dim],
+ * the reference's own layout (src/forward.rs:62-66). */
+int      cxm_cache_new(cxm_model *m, uint32_t max_tokens, cxm_cache **out);
+void     cxm_cache_free(cxm_cache *c);
+uint32_t cxm_cache_len(const cxm_cache *c);                          /* Cache::largo   :77 */
+int      cxm_cache_truncate(cxm_cache *c, uint32_t n);               /* Cache::truncar :98-108 */
+int      cxm_cache_clear(cxm_cache *c);                              /* Cache::limpiar :81-87 */
+/* Cache::prefijo (:115-127): dst becomes a copy of the first n tokens of src
+ * (device-to-device; dst must belong to the same model). */
+int      cxm_cache_copy_prefix(const cxm_cache *src, uint32_t n, cxm_cache *dst);
+/* Copy layer `layer`'s K (is_v = 0) or V (is_v = 1) rows [0, len) to host:
+ * len * n_head_kv * head_dim floats. Test/inspection access. */
+int      cxm_cache_read(const cxm_cache *c, uint32_t layer, int is_v, float *host_out);
+
+/* ── forward and generation ────────────────────────────────────────────── */
+
+/* Modelo::forward (src/forward.rs:375-505): extend `c` with `n` tokens and
+ * return the logits of the LAST one (vocab floats) into host memory
+ * (`logits_out` may be NULL). */
+int cxm_forward(cxm_model *m, cxm_cache *c, const uint32_t *tokens, uint32_t n, float *logits_out);
+
+/* Muestreador::nuevo (src/sampler.rs:40-48): temperature <= 0 is greedy. */
+int  cxm_sampler_new(uint64_t seed, float temperature, float top_p, cxm_sampler **out);
+void cxm_sampler_free(cxm_sampler *s);
+uint64_t cxm_sampler_state(const cxm_sampler *s);
+
+/* Muestreador::elegir (src/sampler.rs:61-126) on the logits of the model's
+ * last forward, computed on the device. */
+int cxm_sample(cxm_model *m, cxm_sampler *s, uint32_t *token_out);
+
+/* Modelo::generar (src/forward.rs:533-559): forward the prompt, then
+ * sample -> forward one token, up to max_new tokens, stopping at the model's
+ * eos and before the context overflows. The per-token step runs as one
+ * replayed CUDA graph; position and token live in device memory. */
+int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, uint32_t n_prompt, uint32_t max_new,
+                 cxm_sampler *s, uint32_t *out, uint32_t *n_out);
+
+const char *cxm_last_error(void);
+
+/* ── kernel-level entry points (parity checks) ─────────────────────────── */
+
+/* The reference's per-row fused-kernel ABI (src/kernels/c.rs:18-30,
+ * src/kernels/q2k.rs:153: float f(blocks, xq, xe, xs, n_superblocks)) lifted
+ * to the device: the integer sub-block sums of one GGUF row against an i8
+ * activation, one int32 per sub-block (16 or 32 values). Host pointers. */
+int cxm_debug_subblock_sums(int ggml_type, const uint8_t *row, const int8_t *xq, uint32_t n_superblocks,
+                            int32_t *out);
+
+/* ops::matmul_auto with one activation row (src/ops.rs:1056-1093):
+ * y[rows] = W[rows x k] · x[k], W raw GGUF k-quant bytes. Host pointers. */
+int cxm_debug_matvec(int ggml_type, const uint8_t *w, uint32_t rows, uint32_t k, const float *x, float *y);
+
+/* ops::atencion for one new token (src/ops.rs:1258-1325) on the device's
+ * split-K flash-decode kernel: q[heads*hd], k/v[total x heads_kv*hd]. Host
+ * pointers; allocates its device buffers per call. */
+int cxm_debug_attention(const float *q, const float *k, const float *v, uint32_t total, uint32_t heads,
+                        uint32_t heads_kv, uint32_t head_dim, float *out);
+
+/* ── measurement hooks (no counterpart in the reference: timing only) ──── */
+
+/* Replay the greedy decode step `steps` times for the token at the cache's
+ * current end, timing on the device (CUDA events on the model's stream).
+ * Inputs stay resident; the cache grows by `steps`. */
+int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, float *ms_total);
+
+/* Average device time of one launch of the gate/up matvec (the largest
+ * kernel of a layer), cycling over the layers so every launch streams its
+ * own weights from HBM. `bytes_per_launch` = GGUF bytes of gate + up. */
+int cxm_bench_matvec(cxm_model *m, uint32_t reps, float *ms_per_launch, uint64_t *bytes_per_launch);
+
+/* Number of kernel launches in one greedy decode step. */
+int cxm_step_launches(const cxm_model *m);
+
+/* ── synthetic models (src/daiss.rs:422-586 + src/quant_kquants.rs) ────── */
+
+/* Tensor-type recipes for the synthetic GGUF writer. */
+enum {
+    CXM_MIX_UNIFORM = 0,  /* every 2-D tensor in `type` */
+    CXM_MIX_Q4_K_M = 1    /* Q6_K for the output projection (or tied token_embd) and
+                             for attn_v / ffn_down of even layers; Q4_K elsewhere */
+};
+
+typedef struct {
+    int32_t vocab, dim, n_layer, n_head, n_head_kv, ffn, ctx;
+    float eps, rope_base;
+    int32_t tied;       /* omit output.weight */
+    int32_t mix;        /* CXM_MIX_* */
+    int32_t type;       /* GGML type for CXM_MIX_UNIFORM */
+    uint64_t seed;
+    float sigma;        /* N(0, sigma) for every matrix */
+    int32_t threads;    /* 0 = all host threads */
+} cxm_synth_spec;
+
+/* Write a seeded random-init qwen2-keyed GGUF: row r of tensor `name` draws
+ * from Azar(semilla_de(seed, name, r)) (src/daiss.rs:364-379), Box-Muller
+ * pairs, then the k-quant writer of its type. Norms are 1, biases 0. */
+int cxm_synth_write(const cxm_synth_spec *spec, const char *path);
+
+/* Quantize n floats (multiple of 256) to `ggml_type` with the library's
+ * k-quant writers (Q2_K/Q3_K/Q4_K/Q5_K after src/quant_kquants.rs, Q6_K our
+ * own); returns the number of bytes written, or <0. */
+int64_t cxm_quantize(int ggml_type, const float *x, uint64_t n, uint8_t *out, uint64_t out_cap);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1464,3 +1464,19 @@ int orc_generate(orc_model *m, orc_cache *c, const uint32_t *prompt, int n_promp
     *n_out = n;
     return rc;
 }
+
+/* Test infrastructure for the timed CPU baseline: fill positions [len, n) of
+ * every layer with seeded values in [-1, 1) so a decode step sees a context
+ * of n positions without paying for an n-token CPU prefill. The values only
+ * shape the attention's cost, never a parity check. */
+void orc_cache_fill(orc_cache *c, int n, uint64_t seed) {
+    if (n <= c->len) return;
+    cache_reserve(c, n);
+    uint64_t st = orc_azar_seed(seed);
+    for (int l = 0; l < c->n_layer; l++)
+        for (size_t i = (size_t)c->len * c->kv_dim; i < (size_t)n * c->kv_dim; i++) {
+            c->k[l][i] = (float)(orc_azar_next(&st) >> 40) / 8388608.0f - 1.0f;
+            c->v[l][i] = (float)(orc_azar_next(&st) >> 40) / 8388608.0f - 1.0f;
+        }
+    c->len = n;
+}

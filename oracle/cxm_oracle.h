@@ -118,6 +118,8 @@ int orc_forward(orc_model *m, orc_cache *c, const uint32_t *tokens, int n, float
 int orc_generate(orc_model *m, orc_cache *c, const uint32_t *prompt, int n_prompt, int max_new,
                  orc_sampler *s, uint32_t *out, int *n_out);
 
+void orc_cache_fill(orc_cache *c, int n, uint64_t seed);
+
 void orc_set_threads(int n);
 int  orc_get_threads(void);
 

@@ -80,6 +80,7 @@ def _declare(L: C.CDLL) -> None:
         "orc_cache_layer": (P, [P, C.c_int, C.c_int]),
         "orc_forward": (C.c_int, [P, P, P, C.c_int, P]),
         "orc_generate": (C.c_int, [P, P, P, C.c_int, C.c_int, P, P, P]),
+        "orc_cache_fill": (None, [P, C.c_int, C.c_uint64]),
         "orc_set_threads": (None, [C.c_int]),
         "orc_get_threads": (C.c_int, []),
     }
@@ -261,6 +262,9 @@ class Cache:
 
     def prefix(self, n: int) -> "Cache":
         return Cache(self.model, lib().orc_cache_prefix(self.h, n))
+
+    def fill(self, n: int, seed: int = 1) -> None:
+        lib().orc_cache_fill(self.h, n, seed)
 
     def layer(self, l: int, v: bool) -> np.ndarray:
         cfg = self.model.config
