@@ -70,6 +70,7 @@ def lib() -> C.CDLL:
             "cxm_debug_subblock_sums": (C.c_int, [C.c_int, P, P, C.c_uint32, P]),
             "cxm_debug_matvec": (C.c_int, [C.c_int, P, C.c_uint32, C.c_uint32, P, P]),
             "cxm_debug_attention": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P]),
+            "cxm_debug_expf": (C.c_int, [P, P, C.c_uint64]),
             "cxm_bench_decode": (C.c_int, [P, P, C.c_uint32, C.POINTER(C.c_float)]),
             "cxm_bench_matvec": (C.c_int, [P, C.c_uint32, C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
             "cxm_step_launches": (C.c_int, [P]),
@@ -292,6 +293,14 @@ def matvec(ggml_type: int, w: np.ndarray, rows: int, k: int, x: np.ndarray) -> n
     x = np.ascontiguousarray(x, np.float32)
     y = np.zeros(rows, np.float32)
     _check(lib().cxm_debug_matvec(ggml_type, _ptr(w), rows, k, _ptr(x), _ptr(y)))
+    return y
+
+
+def expf(x: np.ndarray) -> np.ndarray:
+    """The device exp of the decode path (matches the host libm expf)."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.zeros_like(x)
+    _check(lib().cxm_debug_expf(_ptr(x), _ptr(y), x.size))
     return y
 
 

@@ -1,0 +1,122 @@
+// Single-precision exp that returns, bit for bit, what the host's C library
+// (glibc 2.27+, x86-64 FMA build) returns for expf().
+//
+// Why: the reference computes every exponential of the decode path (softmax
+// in attention, SiLU, the sampler) with Rust's f32::exp, which calls the C
+// library's expf. glibc's expf is not correctly rounded (it differs from the
+// correctly rounded result in ~0.008% of inputs), and the decode path is so
+// sensitive to a 1-ulp change (it flips i8 activation roundings) that parity
+// needs the very same rounding. So this restates the published method glibc
+// uses — the table-driven exp2 reduction of Szabolcs Nagy's "optimized-routines"
+// expf (Arm, 2017): x·N/ln2 = k + r with N = 32, exp(x) = 2^(k/N)·2^(r/N),
+// 2^(k/N) from a 32-entry table, 2^(r/N) from a cubic — evaluated in double
+// with the fused multiply-adds an FMA build of that method performs.
+//
+// Verified exhaustively against the host libm on every finite float input
+// (tests/test_expf.py, tests/test_gpu_expf.py).
+#pragma once
+
+#include <stdint.h>
+#include <string.h>
+
+#ifdef __CUDACC__
+#define CXM_HD __host__ __device__ __forceinline__
+#else
+#define CXM_HD inline
+#endif
+
+namespace cxm {
+
+// bits(2^(i/32)) - (i << 47): 2^(i/32) rounded to the nearest double, with the
+// exponent contribution of i removed so that adding (k << 47) rebuilds 2^(k/32).
+#define CXM_EXP2_TABLE                                                                                  \
+    {0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,      \
+     0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,      \
+     0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,      \
+     0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,      \
+     0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,      \
+     0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,      \
+     0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,      \
+     0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull}
+
+#ifdef __CUDACC__
+__device__ __constant__ uint64_t kExp2TabDev[32] = CXM_EXP2_TABLE;
+#endif
+static const uint64_t kExp2TabHost[32] = CXM_EXP2_TABLE;
+
+CXM_HD uint32_t f2u(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    return u;
+}
+CXM_HD double u2d(uint64_t u) {
+    double d;
+    memcpy(&d, &u, 8);
+    return d;
+}
+CXM_HD uint64_t d2u(double d) {
+    uint64_t u;
+    memcpy(&u, &d, 8);
+    return u;
+}
+
+CXM_HD double fma_d(double a, double b, double c) {
+#ifdef __CUDA_ARCH__
+    return __fma_rn(a, b, c);
+#else
+    return __builtin_fma(a, b, c);
+#endif
+}
+CXM_HD double mul_d(double a, double b) {
+#ifdef __CUDA_ARCH__
+    return __dmul_rn(a, b);
+#else
+    volatile double r = a * b;
+    return r;
+#endif
+}
+CXM_HD double add_d(double a, double b) {
+#ifdef __CUDA_ARCH__
+    return __dadd_rn(a, b);
+#else
+    volatile double r = a + b;
+    return r;
+#endif
+}
+
+CXM_HD float expf_glibc(float x) {
+    const double kInvLn2N = 0x1.71547652b82fep+0 * 32;  // N/ln2
+    const double kShift = 0x1.8p+52;                     // round-to-int by addition
+    // cubic for 2^(r/N), r in [-1/2, 1/2], coefficients of the published method
+    const double c0 = 0x1.c6af84b912394p-5 / (32.0 * 32.0 * 32.0);
+    const double c1 = 0x1.ebfce50fac4f3p-3 / (32.0 * 32.0);
+    const double c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+    const uint32_t ux = f2u(x);
+    const uint32_t abstop = (ux >> 20) & 0x7ff;
+    if (abstop >= 0x42b) {  // |x| >= 88, or inf/nan
+        if (ux == 0xff800000u) return 0.0f;
+        if (abstop >= 0x7f8) return x + x;
+        if (x > 0x1.62e42ep6f) return __builtin_inff();
+        if (x < -0x1.9fe368p6f) return 0.0f;
+    }
+    // the FMA build folds the product x·N/ln2 into both of its uses
+    double kd = fma_d(kInvLn2N, (double)x, kShift);
+    const uint64_t ki = d2u(kd);
+    kd = add_d(kd, -kShift);
+    const double r = fma_d(kInvLn2N, (double)x, -kd);
+#ifdef __CUDA_ARCH__
+    uint64_t t = kExp2TabDev[ki % 32];
+#else
+    uint64_t t = kExp2TabHost[ki % 32];
+#endif
+    t += ki << 47;
+    const double s = u2d(t);
+    const double zc = fma_d(c0, r, c1);
+    const double r2 = mul_d(r, r);
+    double y = fma_d(c2, r, 1.0);
+    y = fma_d(zc, r2, y);
+    y = mul_d(y, s);
+    return (float)y;
+}
+
+}  // namespace cxm

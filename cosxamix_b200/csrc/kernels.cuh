@@ -97,7 +97,7 @@ __device__ __forceinline__ void ld32(const uint8_t *p, uint32_t w[8]) {
 // integer sums in `isum` when requested (parity checks).
 
 // Q4_K: src/kernels/scalar.rs:132-170
-__device__ __forceinline__ float quarter_q4k(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+__device__ __forceinline__ void quarter_q4k(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
     const int b = qt >> 2, q = qt & 3;
     const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 144;
     uint4 hdr = __ldg((const uint4 *)blk);
@@ -117,13 +117,12 @@ __device__ __forceinline__ float quarter_q4k(const DMat &W, int row, int qt, con
     int s0 = dot8(lo, xp), s1 = dot8(hi, xp + 2);
     const int j0 = b * 8 + 2 * q;
     if (isum) { isum[0] = s0; isum[1] = s1; }
-    float t0 = fm(x.e[j0], fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), x.s[j0])));
-    float t1 = fm(x.e[j0 + 1], fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), x.s[j0 + 1])));
-    return fa(t0, t1);
+    t[0] = fm(x.e[j0], fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), x.s[j0])));
+    t[1] = fm(x.e[j0 + 1], fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), x.s[j0 + 1])));
 }
 
 // Q5_K: src/kernels/scalar.rs:179-217
-__device__ __forceinline__ float quarter_q5k(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+__device__ __forceinline__ void quarter_q5k(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
     const int b = qt >> 2, q = qt & 3;
     const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 176;
     uint4 hdr = __ldg((const uint4 *)blk);
@@ -145,14 +144,13 @@ __device__ __forceinline__ float quarter_q5k(const DMat &W, int row, int qt, con
     int s0 = dot8(lo, xp), s1 = dot8(hi, xp + 2);
     const int k0 = b * 8 + j0;
     if (isum) { isum[0] = s0; isum[1] = s1; }
-    float t0 = fm(x.e[k0], fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), x.s[k0])));
-    float t1 = fm(x.e[k0 + 1], fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), x.s[k0 + 1])));
-    return fa(t0, t1);
+    t[0] = fm(x.e[k0], fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), x.s[k0])));
+    t[1] = fm(x.e[k0 + 1], fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), x.s[k0 + 1])));
 }
 
 // Q6_K: src/kernels/scalar.rs:294-324. Quarter q = half h (q>>1) and ql
 // column par (q&1): groups gi = par (low nibbles) and gi = par+2 (high).
-__device__ __forceinline__ float quarter_q6k(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+__device__ __forceinline__ void quarter_q6k(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
     const int b = qt >> 2, q = qt & 3, h = q >> 1, par = q & 1;
     const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 192;
     uint32_t ql[8], qh[8];
@@ -177,7 +175,6 @@ __device__ __forceinline__ float quarter_q6k(const DMat &W, int row, int qt, con
     s[3] = dot4w(vhi + 4, xhi[1]);
     if (isum) { isum[0] = s[0]; isum[1] = s[1]; isum[2] = s[2]; isum[3] = s[3]; }
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
-    float total = 0.0f;
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         const int g = k < 2 ? glo : ghi, md = k & 1;
@@ -185,14 +182,12 @@ __device__ __forceinline__ float quarter_q6k(const DMat &W, int row, int qt, con
         const int sc = (int)(int8_t)((scw[si >> 2] >> (8 * (si & 3))) & 0xFF);
         const int sub = b * 16 + si;
         float esc = fm(d, (float)sc);
-        float t = fm(fm(x.e[sub], esc), fs((float)s[k], fm(32.0f, x.s[sub])));
-        total = k == 0 ? t : fa(total, t);
+        t[k] = fm(fm(x.e[sub], esc), fs((float)s[k], fm(32.0f, x.s[sub])));
     }
-    return total;
 }
 
 // Q3_K: src/kernels/scalar.rs:236-275. Quarter q = groups 2q and 2q+1.
-__device__ __forceinline__ float quarter_q3k(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+__device__ __forceinline__ void quarter_q3k(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
     const int b = qt >> 2, q = qt & 3;
     const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 96;
     uint32_t hm[8], qs[8];
@@ -216,20 +211,17 @@ __device__ __forceinline__ float quarter_q3k(const DMat &W, int row, int qt, con
         s[2 * gg + 1] = dot4w(v + 4, xp[1]);
     }
     if (isum) { isum[0] = s[0]; isum[1] = s[1]; isum[2] = s[2]; isum[3] = s[3]; }
-    float total = 0.0f;
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         const int sc = (int)((wq >> (8 * k)) & 0xFF);
         const int sub = b * 16 + 4 * q + k;
         float esc = fm(d, fs((float)sc, 32.0f));
-        float t = fm(fm(x.e[sub], esc), fs((float)s[k], fm(4.0f, x.s[sub])));
-        total = k == 0 ? t : fa(total, t);
+        t[k] = fm(fm(x.e[sub], esc), fs((float)s[k], fm(4.0f, x.s[sub])));
     }
-    return total;
 }
 
 // Q2_K: src/kernels/q2k.rs:41-69. Quarter q = groups 2q and 2q+1.
-__device__ __forceinline__ float quarter_q2k(const DMat &W, int row, int qt, const XQ &x, int *isum) {
+__device__ __forceinline__ void quarter_q2k(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
     const int b = qt >> 2, q = qt & 3;
     const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 64;
     uint32_t qs[8];
@@ -249,25 +241,37 @@ __device__ __forceinline__ float quarter_q2k(const DMat &W, int row, int qt, con
         s[2 * gg + 1] = dot4w(v + 4, xp[1]);
     }
     if (isum) { isum[0] = s[0]; isum[1] = s[1]; isum[2] = s[2]; isum[3] = s[3]; }
-    float total = 0.0f;
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         const int sc = (int)((scw >> (8 * k)) & 0xFF);
         const int sub = b * 16 + 4 * q + k;
         float ev = fm(d, (float)(sc & 0xF)), mv = fm(dm, (float)(sc >> 4));
-        float t = fm(x.e[sub], fs(fm(ev, (float)s[k]), fm(mv, x.s[sub])));
-        total = k == 0 ? t : fa(total, t);
+        t[k] = fm(x.e[sub], fs(fm(ev, (float)s[k]), fm(mv, x.s[sub])));
     }
-    return total;
 }
 
+// Terms of one quarter, in the order of their sub-blocks; `term_sub` gives
+// the sub-block (within the super-block) of term k. The row total is the
+// sequential f32 sum of all terms in sub-block order (src/kernels/scalar.rs:
+// `total += ...` per sub-block), which the matvec kernel reproduces exactly.
 template <int T>
-__device__ __forceinline__ float quarter(const DMat &W, int row, int qt, const XQ &x, int *isum) {
-    if (T == 12) return quarter_q4k(W, row, qt, x, isum);
-    if (T == 13) return quarter_q5k(W, row, qt, x, isum);
-    if (T == 14) return quarter_q6k(W, row, qt, x, isum);
-    if (T == 11) return quarter_q3k(W, row, qt, x, isum);
-    return quarter_q2k(W, row, qt, x, isum);
+__device__ __forceinline__ void quarter(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
+    if (T == 12) quarter_q4k(W, row, qt, x, t, isum);
+    else if (T == 13) quarter_q5k(W, row, qt, x, t, isum);
+    else if (T == 14) quarter_q6k(W, row, qt, x, t, isum);
+    else if (T == 11) quarter_q3k(W, row, qt, x, t, isum);
+    else quarter_q2k(W, row, qt, x, t, isum);
+}
+
+__host__ __device__ __forceinline__ int terms_per_quarter(int type) { return (type == 12 || type == 13) ? 2 : 4; }
+__host__ __device__ __forceinline__ int subs_per_block(int type) { return (type == 12 || type == 13) ? 8 : 16; }
+__device__ __forceinline__ int term_sub(int type, int q, int k) {
+    if (type == 12 || type == 13) return 2 * q + k;
+    if (type == 14) {
+        const int g = 4 * (q >> 1) + (q & 1) + (k >= 2 ? 2 : 0);
+        return 2 * g + (k & 1);
+    }
+    return 4 * q + k;
 }
 
 // ── dequantize one value from the planes (src/quant.rs:582-679) ──

@@ -44,10 +44,9 @@ struct cxm_model {
     float *embd_f32 = nullptr;
     float *out_norm = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     std::vector<void *> allocs;
-    float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr, *part = nullptr;
-    int *counter = nullptr, *err = nullptr;
+    float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    int *err = nullptr;
     unsigned long long *argmax_key = nullptr;
-    int P = 64, S_max = 1;
     int sms = 148, mv_blocks = 148;
     uint64_t weight_bytes = 0;
     bool logits_valid = false;
@@ -189,7 +188,7 @@ void set_need(MatvecParams &p, const DMat &a) {
 }
 
 size_t matvec_smem(const MatvecParams &p) {
-    size_t b = 0;
+    size_t b = (size_t)kWarps * kTileFloats * sizeof(float);
     if (p.need16) b += (size_t)p.K + (size_t)p.K / 16 * 8;
     if (p.need32) b += (size_t)p.K + (size_t)p.K / 32 * 8;
     return (b + 15) & ~(size_t)15;
@@ -216,6 +215,14 @@ Seg make_seg(const DMat &A, int pairing, int epi, float *out) {
     return s;
 }
 
+size_t attention_smem(int hd, uint32_t max_pos) { return ((size_t)hd + max_pos + 4) * sizeof(float); }
+
+int set_kernel_smem_limits() {
+    CU(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    CU(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    return 0;
+}
+
 int launch_attention(cxm_model *m, cxm_cache *c, int layer) {
     const cxm_config &cfg = m->cfg;
     AttnParams a{};
@@ -223,26 +230,15 @@ int launch_attention(cxm_model *m, cxm_cache *c, int layer) {
     a.k = c->k + (size_t)layer * c->max_tokens * kv_dim(m);
     a.v = c->v + (size_t)layer * c->max_tokens * kv_dim(m);
     a.out = m->att;
-    a.part = m->part;
-    a.counter = m->counter;
     a.d_len = c->d_len;
     a.H = cfg.n_head;
     a.KV = cfg.n_head_kv;
-    a.P = m->P;
-    a.S_max = m->S_max;
+    a.hd = cfg.head_dim;
     a.max_pos = (int)c->max_tokens;
-    a.scale = 1.0f / sqrtf((float)cfg.head_dim);
+    a.scale = 1.0f / sqrtf((float)cfg.head_dim);  // src/ops.rs:1287
     a.err = m->err;
-    const int G = cfg.n_head / cfg.n_head_kv, hd = cfg.head_dim;
-    const int tpd = kAttnThreads / hd;
-    size_t smem = (size_t)(G * hd + G * m->P + 2 * G + 8 + (tpd > 1 ? tpd * kGMax * hd : 0)) * 4;
-    dim3 grid(cfg.n_head_kv, m->S_max);
-    switch (hd) {
-    case 32: k_attention<32><<<grid, kAttnThreads, smem, m->stream>>>(a); break;
-    case 64: k_attention<64><<<grid, kAttnThreads, smem, m->stream>>>(a); break;
-    case 128: k_attention<128><<<grid, kAttnThreads, smem, m->stream>>>(a); break;
-    default: set_error("head_dim %d unsupported (32, 64, 128)", hd); return -1;
-    }
+    const size_t smem = attention_smem(cfg.head_dim, c->max_tokens);
+    k_attention<<<cfg.n_head, kAttnThreads, smem, m->stream>>>(a);
     CU(cudaGetLastError());
     return 0;
 }
@@ -537,21 +533,20 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
         CU(cudaMemcpy(m->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
         CU(cudaMemcpy(m->rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
     }
-    // activations and scratch
-    const int G = cfg.n_head / cfg.n_head_kv;
-    m->P = std::max(32, std::min(256, ((cfg.ctx * cfg.n_head_kv + 2 * m->sms - 1) / (2 * m->sms) + 31) / 32 * 32));
-    m->S_max = (cfg.ctx + m->P - 1) / m->P;
-    (void)G;
+    // activations
     if (m->alloc(&m->x, cfg.dim) || m->alloc(&m->q, cfg.dim) || m->alloc(&m->att, cfg.dim) ||
-        m->alloc(&m->h, std::max(cfg.ffn, 1)) || m->alloc(&m->logits, cfg.vocab) ||
-        m->alloc(&m->part, (size_t)cfg.n_head * m->S_max * (hd + 2)) || m->alloc(&m->counter, cfg.n_head_kv) ||
-        m->alloc(&m->err, 1) || m->alloc(&m->argmax_key, 1))
+        m->alloc(&m->h, std::max(cfg.ffn, 1)) || m->alloc(&m->logits, cfg.vocab) || m->alloc(&m->err, 1) ||
+        m->alloc(&m->argmax_key, 1))
         return -1;
-    CU(cudaMemset(m->counter, 0, sizeof(int) * cfg.n_head_kv));
     CU(cudaMemset(m->err, 0, sizeof(int)));
-    CU(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+    if (set_kernel_smem_limits()) return -1;
+    if (attention_smem(cfg.head_dim, (uint32_t)cfg.ctx) > 200 * 1024) {
+        set_error("context %d is beyond the attention kernel's shared-memory score buffer", cfg.ctx);
+        return -1;
+    }
     int occ = 0;
-    CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_matvec, kThreads, 40 * 1024));
+    CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_matvec, kThreads,
+                                                     kWarps * kTileFloats * sizeof(float) + 24 * 1024));
     m->mv_blocks = m->sms * std::max(occ, 1);
     CU(cudaDeviceSynchronize());
     *out = m.release();
@@ -901,8 +896,8 @@ extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint3
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    CU(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
-    int blocks = std::min((p.total_units + kWarps - 1) / kWarps, sms * 4);
+    if (set_kernel_smem_limits()) return -1;
+    int blocks = std::min((p.total_units + kWarps - 1) / kWarps, sms * 2);
     k_matvec<<<blocks, kThreads, matvec_smem(p)>>>(p);
     CU(cudaGetLastError());
     CU(cudaDeviceSynchronize());
@@ -913,25 +908,22 @@ extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint3
 extern "C" int cxm_debug_attention(const float *q, const float *k, const float *v, uint32_t total, uint32_t heads,
                                    uint32_t heads_kv, uint32_t hd, float *out) {
     if (need_device()) return -1;
-    if (!q || !k || !v || !out || total == 0 || heads_kv == 0 || heads % heads_kv || (hd != 32 && hd != 64 && hd != 128)) {
+    if (!q || !k || !v || !out || total == 0 || heads_kv == 0 || heads % heads_kv || hd % 4 || hd == 0 ||
+        attention_smem((int)hd, total) > 200 * 1024) {
         set_error("bad attention arguments");
         return -1;
     }
     const size_t kvd = (size_t)heads_kv * hd;
-    const int P = 64, S = (int)((total + P - 1) / P);
-    DevBuf dq, dk, dv, dout, dpart, dcnt, dlen, derr;
+    DevBuf dq, dk, dv, dout, dlen, derr;
     CU(cudaMalloc(&dq.p, (size_t)heads * hd * 4));
     CU(cudaMalloc(&dk.p, total * kvd * 4));
     CU(cudaMalloc(&dv.p, total * kvd * 4));
     CU(cudaMalloc(&dout.p, (size_t)heads * hd * 4));
-    CU(cudaMalloc(&dpart.p, (size_t)heads * S * (hd + 2) * 4));
-    CU(cudaMalloc(&dcnt.p, heads_kv * 4));
     CU(cudaMalloc(&dlen.p, 4));
     CU(cudaMalloc(&derr.p, 4));
     CU(cudaMemcpy(dq.p, q, (size_t)heads * hd * 4, cudaMemcpyHostToDevice));
     CU(cudaMemcpy(dk.p, k, total * kvd * 4, cudaMemcpyHostToDevice));
     CU(cudaMemcpy(dv.p, v, total * kvd * 4, cudaMemcpyHostToDevice));
-    CU(cudaMemset(dcnt.p, 0, heads_kv * 4));
     CU(cudaMemset(derr.p, 0, 4));
     int len = (int)total - 1;
     CU(cudaMemcpy(dlen.p, &len, 4, cudaMemcpyHostToDevice));
@@ -940,25 +932,35 @@ extern "C" int cxm_debug_attention(const float *q, const float *k, const float *
     a.k = (const float *)dk.p;
     a.v = (const float *)dv.p;
     a.out = (float *)dout.p;
-    a.part = (float *)dpart.p;
-    a.counter = (int *)dcnt.p;
     a.d_len = (const int *)dlen.p;
     a.H = (int)heads;
     a.KV = (int)heads_kv;
-    a.P = P;
-    a.S_max = S;
+    a.hd = (int)hd;
     a.max_pos = (int)total;
     a.scale = 1.0f / sqrtf((float)hd);
     a.err = (int *)derr.p;
-    const int G = (int)(heads / heads_kv), tpd = kAttnThreads / (int)hd;
-    size_t smem = (size_t)(G * (int)hd + G * P + 2 * G + 8 + (tpd > 1 ? tpd * kGMax * (int)hd : 0)) * 4;
-    dim3 grid(heads_kv, S);
-    if (hd == 32) k_attention<32><<<grid, kAttnThreads, smem>>>(a);
-    else if (hd == 64) k_attention<64><<<grid, kAttnThreads, smem>>>(a);
-    else k_attention<128><<<grid, kAttnThreads, smem>>>(a);
+    if (set_kernel_smem_limits()) return -1;
+    k_attention<<<heads, kAttnThreads, attention_smem((int)hd, total)>>>(a);
     CU(cudaGetLastError());
     CU(cudaDeviceSynchronize());
     CU(cudaMemcpy(out, dout.p, (size_t)heads * hd * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+extern "C" int cxm_debug_expf(const float *x, float *y, uint64_t n) {
+    if (need_device()) return -1;
+    if (!x || !y || n == 0) {
+        set_error("bad arguments");
+        return -1;
+    }
+    DevBuf dx, dy;
+    CU(cudaMalloc(&dx.p, n * 4));
+    CU(cudaMalloc(&dy.p, n * 4));
+    CU(cudaMemcpy(dx.p, x, n * 4, cudaMemcpyHostToDevice));
+    k_expf<<<1024, 256>>>((const float *)dx.p, (float *)dy.p, (int)n);
+    CU(cudaGetLastError());
+    CU(cudaDeviceSynchronize());
+    CU(cudaMemcpy(y, dy.p, n * 4, cudaMemcpyDeviceToHost));
     return 0;
 }
 

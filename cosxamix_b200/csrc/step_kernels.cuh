@@ -1,14 +1,26 @@
 // The kernels of one decode step. Launched by model.cu, each step captured
 // once into a CUDA graph and replayed; the position and the token are read
 // from device memory so the same graph serves every step of a conversation.
+//
+// Numerics: every float operation reproduces the reference's scalar
+// specification in value AND order — per-sub-block terms summed sequentially
+// per row, attention dot products, softmax sum and the probability-weighted
+// value sum accumulated sequentially, and exp computed as the host libm
+// computes it. On the random-init models of the benchmark a single 1-ulp
+// difference flips an i8 activation rounding and moves the logits by more than
+// the 1e-3 parity bar, so nothing less than identical rounding passes it.
 #pragma once
 
+#include "expf_glibc.h"
 #include "kernels.cuh"
 
 namespace cxm {
 
 constexpr int kThreads = 256;  // matvec CTA: 8 warps
 constexpr int kWarps = kThreads / 32;
+constexpr int kBatch = 8;          // row pairs per warp batch (16 sequential chains)
+constexpr int kTileStride = 132;   // floats per row of a warp's term tile (128 terms + pad)
+constexpr int kTileFloats = 2 * kBatch * kTileStride;
 
 // error flags written by kernels (never a trap); read by the host after sync
 enum : int { ERR_TOKEN = 1, ERR_POSITION = 2 };
@@ -51,11 +63,6 @@ struct MatvecParams {
     int *err;
 };
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
 __device__ __forceinline__ int warp_sum_i(int v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -84,16 +91,16 @@ __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe
         double acc = 0.0;
         for (int i = tid; i < K; i += blockDim.x) {
             double v = (double)p.in[i];
-            acc += v * v;
+            acc = __dadd_rn(acc, __dmul_rn(v, v));
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        for (int o = 16; o > 0; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
         if (lane == 0) red[warp] = acc;
         __syncthreads();
         if (tid == 0) {
             double s = 0.0;
-            for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += red[w];
-            red[0] = 1.0 / sqrt(s / (double)K + (double)p.eps);
+            for (int w = 0; w < (int)(blockDim.x >> 5); w++) s = __dadd_rn(s, red[w]);
+            red[0] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s, (double)K), (double)p.eps)));
         }
         __syncthreads();
         scale = red[0];
@@ -102,7 +109,7 @@ __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe
     for (int c = warp; c < nchunk; c += (blockDim.x >> 5)) {
         const int i = c * 32 + lane;
         float v = p.in[i];
-        if (p.prologue == PRO_NORM) v = __fmul_rn((float)((double)v * scale), p.norm_w[i]);
+        if (p.prologue == PRO_NORM) v = __fmul_rn(__double2float_rn(__dmul_rn((double)v, scale)), p.norm_w[i]);
         const float av = fabsf(v);
         if (p.need32) {
             float amax = av;
@@ -136,41 +143,71 @@ __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe
     __syncthreads();
 }
 
+__device__ __forceinline__ void quarter_any(const DMat &W, int row, int qt, const XQ &x, float *t) {
+    switch (W.type) {
+    case 12: quarter<12>(W, row, qt, x, t, nullptr); break;
+    case 13: quarter<13>(W, row, qt, x, t, nullptr); break;
+    case 14: quarter<14>(W, row, qt, x, t, nullptr); break;
+    case 11: quarter<11>(W, row, qt, x, t, nullptr); break;
+    default: quarter<10>(W, row, qt, x, t, nullptr); break;
+    }
+}
+
+// Terms of quarter qt of rows r0 (of A) and r1 (of B), stored in the tile at
+// their sub-block positions relative to the iteration's first block.
 template <int T>
-__device__ __forceinline__ void pair_dot(const DMat &A, int r0, const DMat &B, int r1, int lane, const XQ &x,
-                                         float &y0, float &y1) {
-    const int nq = A.nblk * 4;
-    float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll 2
-    for (int qt = lane; qt < nq; qt += 32) {
-        float t0 = quarter<T>(A, r0, qt, x, nullptr);
-        float t1 = quarter<T>(B, r1, qt, x, nullptr);
-        a0 += t0;
-        a1 += t1;
+__device__ __forceinline__ void pair_terms(const DMat &A, int r0, const DMat &B, int r1, int qt, int it, const XQ &x,
+                                           float *row0, float *row1) {
+    float t0[4], t1[4];
+    quarter<T>(A, r0, qt, x, t0, nullptr);
+    quarter<T>(B, r1, qt, x, t1, nullptr);
+    const int q = qt & 3, bl = (qt >> 2) - it * 8;
+    constexpr int tpq = (T == 12 || T == 13) ? 2 : 4, spb = (T == 12 || T == 13) ? 8 : 16;
+#pragma unroll
+    for (int k = 0; k < tpq; k++) {
+        const int pos = bl * spb + term_sub(T, q, k);
+        row0[pos] = t0[k];
+        row1[pos] = t1[k];
     }
-    y0 = a0;
-    y1 = a1;
 }
 
-__device__ __forceinline__ float row_dot_any(const DMat &W, int r, int lane, const XQ &x) {
-    const int nq = W.nblk * 4;
-    float a = 0.0f;
-    for (int qt = lane; qt < nq; qt += 32) {
-        switch (W.type) {
-        case 12: a += quarter<12>(W, r, qt, x, nullptr); break;
-        case 13: a += quarter<13>(W, r, qt, x, nullptr); break;
-        case 14: a += quarter<14>(W, r, qt, x, nullptr); break;
-        case 11: a += quarter<11>(W, r, qt, x, nullptr); break;
-        default: a += quarter<10>(W, r, qt, x, nullptr); break;
-        }
+struct Unit {
+    int seg, r0, r1;
+};
+
+__device__ __forceinline__ Unit decode_unit(const MatvecParams &p, int u) {
+    int s = 0;
+    while (s < p.nseg - 1 && u >= p.seg[s].units) {
+        u -= p.seg[s].units;
+        s++;
     }
-    return a;
+    const Seg &g = p.seg[s];
+    Unit r;
+    r.seg = s;
+    if (g.pairing == PAIR_ADJ) {
+        r.r0 = 2 * u;
+        r.r1 = 2 * u + 1;
+    } else if (g.pairing == PAIR_ROPE) {
+        const int h = u / g.half, i = u - h * g.half;
+        r.r0 = h * 2 * g.half + i;
+        r.r1 = r.r0 + g.half;
+    } else {
+        r.r0 = u;
+        r.r1 = u;
+    }
+    return r;
 }
 
+// k-quant matvec, several matrices per launch (q|k|v, gate|up), activation
+// quantization fused in front and the consumer fused behind. A warp takes
+// batches of up to 8 row pairs; per 32-quarter iteration its lanes produce the
+// sub-block terms of every row into a shared-memory tile, then 16 lanes — one
+// per row — add their row's terms in sub-block order onto a running f32 total.
 __global__ void __launch_bounds__(kThreads) k_matvec(const __grid_constant__ MatvecParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int K = p.K;
-    int8_t *xq16 = (int8_t *)smem;
+    float *tiles = (float *)smem;
+    int8_t *xq16 = (int8_t *)(tiles + kWarps * kTileFloats);
     int8_t *xq32 = xq16 + (p.need16 ? K : 0);
     float *xe16 = (float *)(xq32 + (p.need32 ? K : 0));
     float *xs16 = xe16 + (p.need16 ? K / 16 : 0);
@@ -184,90 +221,121 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const __grid_constant__ Mat
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gwarp = blockIdx.x * kWarps + warp, nwarps = gridDim.x * kWarps;
     const int pos = p.d_len ? *p.d_len : 0;
+    const int nq = (K / 256) * 4;
+    float *tile = tiles + warp * kTileFloats;
+    const XQ x16{xq16, xe16, xs16}, x32{xq32, xe32, xs32};
     unsigned long long best = 0ull;
 
-    for (int u = gwarp; u < p.total_units; u += nwarps) {
-        int s = 0, uu = u;
-        while (s < p.nseg - 1 && uu >= p.seg[s].units) {
-            uu -= p.seg[s].units;
-            s++;
+    for (int k0 = 0;; k0 += kBatch) {
+        const int first = gwarp + k0 * nwarps;
+        if (first >= p.total_units) break;
+        const int nb = min(kBatch, (p.total_units - first + nwarps - 1) / nwarps);
+        // lane L < 2*nb owns the chain of row slot L (unit L/2, row L%2)
+        int my_type = 0;
+        if (lane < 2 * nb) {
+            const Unit mu = decode_unit(p, first + (lane >> 1) * nwarps);
+            const Seg &mg = p.seg[mu.seg];
+            my_type = (lane & 1) && mg.pairing == PAIR_TWO ? mg.B.type : mg.A.type;
         }
-        const Seg &g = p.seg[s];
-        int r0, r1;
-        if (g.pairing == PAIR_ADJ) {
-            r0 = 2 * uu;
-            r1 = 2 * uu + 1;
-        } else if (g.pairing == PAIR_ROPE) {
-            const int h = uu / g.half, i = uu - h * g.half;
-            r0 = h * 2 * g.half + i;
-            r1 = r0 + g.half;
-        } else {
-            r0 = uu;
-            r1 = uu;
-        }
-        const DMat &A = g.A;
-        const DMat &B = (g.pairing == PAIR_TWO) ? g.B : g.A;
-        const int sub = (A.type == 12 || A.type == 13) ? 32 : 16;
-        const XQ x = sub == 32 ? XQ{xq32, xe32, xs32} : XQ{xq16, xe16, xs16};
-        float y0, y1;
-        if (A.type == B.type) {
-            switch (A.type) {
-            case 12: pair_dot<12>(A, r0, B, r1, lane, x, y0, y1); break;
-            case 13: pair_dot<13>(A, r0, B, r1, lane, x, y0, y1); break;
-            case 14: pair_dot<14>(A, r0, B, r1, lane, x, y0, y1); break;
-            case 11: pair_dot<11>(A, r0, B, r1, lane, x, y0, y1); break;
-            default: pair_dot<10>(A, r0, B, r1, lane, x, y0, y1); break;
-            }
-        } else {
-            const int subB = (B.type == 12 || B.type == 13) ? 32 : 16;
-            const XQ xb = subB == 32 ? XQ{xq32, xe32, xs32} : XQ{xq16, xe16, xs16};
-            y0 = row_dot_any(A, r0, lane, x);
-            y1 = row_dot_any(B, r1, lane, xb);
-        }
-        y0 = warp_sum(y0);
-        y1 = warp_sum(y1);
-        if (lane == 0 && !(g.at_pos && (pos < 0 || pos >= p.max_pos))) {
-            float *out = g.out + (g.at_pos ? (size_t)pos * g.pos_stride : 0);
-            switch (g.epi) {
-            case EPI_STORE:
-                if (g.bias) {
-                    y0 = fa(y0, g.bias[r0]);
-                    y1 = fa(y1, g.bias[r1]);
+        float total = 0.0f;
+        for (int it = 0; it * 32 < nq; it++) {
+            const int qt = it * 32 + lane;
+            for (int j = 0; j < nb; j++) {
+                const Unit un = decode_unit(p, first + j * nwarps);
+                const Seg &g = p.seg[un.seg];
+                const DMat &A = g.A;
+                const DMat &B = (g.pairing == PAIR_TWO) ? g.B : g.A;
+                float *row0 = tile + (2 * j) * kTileStride, *row1 = row0 + kTileStride;
+                if (qt < nq) {
+                    const XQ &xa = (A.type == 12 || A.type == 13) ? x32 : x16;
+                    if (A.type == B.type) {
+                        switch (A.type) {
+                        case 12: pair_terms<12>(A, un.r0, B, un.r1, qt, it, xa, row0, row1); break;
+                        case 13: pair_terms<13>(A, un.r0, B, un.r1, qt, it, xa, row0, row1); break;
+                        case 14: pair_terms<14>(A, un.r0, B, un.r1, qt, it, xa, row0, row1); break;
+                        case 11: pair_terms<11>(A, un.r0, B, un.r1, qt, it, xa, row0, row1); break;
+                        default: pair_terms<10>(A, un.r0, B, un.r1, qt, it, xa, row0, row1); break;
+                        }
+                    } else {
+                        const XQ &xb = (B.type == 12 || B.type == 13) ? x32 : x16;
+                        float t0[4], t1[4];
+                        quarter_any(A, un.r0, qt, xa, t0);
+                        quarter_any(B, un.r1, qt, xb, t1);
+                        const int q = qt & 3, bl = (qt >> 2) - it * 8;
+                        for (int k = 0; k < terms_per_quarter(A.type); k++)
+                            row0[bl * subs_per_block(A.type) + term_sub(A.type, q, k)] = t0[k];
+                        for (int k = 0; k < terms_per_quarter(B.type); k++)
+                            row1[bl * subs_per_block(B.type) + term_sub(B.type, q, k)] = t1[k];
+                    }
                 }
-                out[r0] = y0;
-                out[r1] = y1;
-                break;
-            case EPI_ROPE: {
-                // src/ops.rs:1150-1193, split-half pair (i, i + hd/2) at pos
-                const int i = r0 % (2 * g.half);
-                const float c = p.rope_cos[(size_t)pos * g.half + i], sn = p.rope_sin[(size_t)pos * g.half + i];
-                const float a = fa(y0, g.bias[r0]), b = fa(y1, g.bias[r1]);
-                out[r0] = fs(fm(a, c), fm(b, sn));
-                out[r1] = fa(fm(a, sn), fm(b, c));
-                break;
             }
-            case EPI_RESID:
-                out[r0] = fa(out[r0], y0);
-                out[r1] = fa(out[r1], y1);
-                break;
-            case EPI_SWIGLU: {
-                const float act = __fdiv_rn(y0, fa(1.0f, expf(-y0)));
-                out[r0] = fm(act, y1);
-                break;
+            __syncwarp();
+            if (lane < 2 * nb) {
+                const int blocks = min(8, (nq - it * 32) >> 2);
+                const int nterms = blocks * subs_per_block(my_type);
+                const float4 *src = (const float4 *)(tile + lane * kTileStride);
+                for (int c = 0; c < (nterms >> 2); c++) {
+                    const float4 v = src[c];
+                    total = fa(fa(fa(fa(total, v.x), v.y), v.z), v.w);
+                }
             }
-            case EPI_LOGITS: {
-                out[r0] = y0;
-                out[r1] = y1;
-                unsigned long long k0 = (y0 == y0) ? argmax_key(y0, (uint32_t)r0) : 0ull;
-                unsigned long long k1 = (y1 == y1) ? argmax_key(y1, (uint32_t)r1) : 0ull;
-                unsigned long long k = k0 > k1 ? k0 : k1;
-                best = k > best ? k : best;
-                break;
-            }
+            __syncwarp();
+        }
+        const float other = __shfl_down_sync(0xffffffffu, total, 1);
+        if (lane < 2 * nb && !(lane & 1)) {
+            const Unit un = decode_unit(p, first + (lane >> 1) * nwarps);
+            const Seg &g = p.seg[un.seg];
+            const int r0 = un.r0, r1 = un.r1;
+            float y0 = total, y1 = other;
+            if (!(g.at_pos && (pos < 0 || pos >= p.max_pos))) {
+                float *out = g.out + (g.at_pos ? (size_t)pos * g.pos_stride : 0);
+                switch (g.epi) {
+                case EPI_STORE:
+                    if (g.bias) {
+                        y0 = fa(y0, g.bias[r0]);
+                        y1 = fa(y1, g.bias[r1]);
+                    }
+                    out[r0] = y0;
+                    out[r1] = y1;
+                    break;
+                case EPI_ROPE: {
+                    // src/ops.rs:1150-1193, split-half pair (i, i + hd/2) at pos
+                    const int i = r0 % (2 * g.half);
+                    const float c = p.rope_cos[(size_t)pos * g.half + i], sn = p.rope_sin[(size_t)pos * g.half + i];
+                    const float a = fa(y0, g.bias[r0]), b = fa(y1, g.bias[r1]);
+                    out[r0] = fs(fm(a, c), fm(b, sn));
+                    out[r1] = fa(fm(a, sn), fm(b, c));
+                    break;
+                }
+                case EPI_RESID:
+                    out[r0] = fa(out[r0], y0);
+                    out[r1] = fa(out[r1], y1);
+                    break;
+                case EPI_SWIGLU: {
+                    // src/kernels/scalar.rs:63-67 then `*a *= u`
+                    const float act = __fdiv_rn(y0, fa(1.0f, expf_glibc(-y0)));
+                    out[r0] = fm(act, y1);
+                    break;
+                }
+                case EPI_LOGITS: {
+                    out[r0] = y0;
+                    out[r1] = y1;
+                    unsigned long long ka = (y0 == y0) ? argmax_key(y0, (uint32_t)r0) : 0ull;
+                    unsigned long long kb = (y1 == y1) ? argmax_key(y1, (uint32_t)r1) : 0ull;
+                    unsigned long long kk = ka > kb ? ka : kb;
+                    best = kk > best ? kk : best;
+                    break;
+                }
+                }
             }
         }
     }
     if (p.argmax_key) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+            best = v > best ? v : best;
+        }
         if (lane == 0) best_s[warp] = best;
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -278,145 +346,101 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const __grid_constant__ Mat
     }
 }
 
-// ── split-K flash-decode attention (src/ops.rs:1258-1325 for one new token)
-// grid (n_head_kv, S_max): CTA (g, s) handles positions [s*P, min((s+1)*P, n))
-// for the G = H/KV query heads of kv head g, writes (m, l, o) partials, and
-// the last CTA of each kv head to arrive merges them. n = *d_len + 1.
+// ── attention for one new token (src/ops.rs:1258-1325), one CTA per query
+// head, in the reference's order: each score is the sequential dot over the
+// head dimension times 1/sqrt(hd); softmax subtracts the max, exponentiates,
+// adds the exponentials position by position and multiplies by 1/total
+// (src/ops.rs:1206-1230); the output adds p·v position by position per dim.
 struct AttnParams {
-    const float *q;   // [H*hd], rotated
+    const float *q;      // [H*hd], rotated
     const float *k, *v;  // layer base, [max_tokens][KV*hd]
-    float *out;       // [H*hd]
-    float *part;      // [H][S_max][hd + 2]
-    int *counter;     // [KV], zero between launches
+    float *out;          // [H*hd]
     const int *d_len;
-    int H, KV, P, S_max, max_pos;
+    int H, KV, hd, max_pos;
     float scale;
     int *err;
 };
 
-constexpr int kAttnThreads = 128;
-constexpr int kGMax = 8;
+constexpr int kAttnThreads = 512;
 
-template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constant__ AttnParams p) {
     extern __shared__ __align__(16) float sm[];
-    const int G = p.H / p.KV, kvh = blockIdx.x, s = blockIdx.y;
+    const int h = blockIdx.x, G = p.H / p.KV, g = h / G, hd = p.hd, tid = threadIdx.x;
     const int n = *p.d_len + 1;
-    if (n > p.max_pos) {
-        if (threadIdx.x == 0 && s == 0 && kvh == 0) atomicOr(p.err, ERR_POSITION);
+    if (n > p.max_pos || n <= 0) {
+        if (tid == 0 && h == 0) atomicOr(p.err, ERR_POSITION);
         return;
     }
-    const int nsplit = (n + p.P - 1) / p.P;
-    if (s >= nsplit) return;
-    const int start = s * p.P, cnt = min(p.P, n - start);
-    const int kvd = p.KV * HD;
-    float *qs = sm;                  // [G][HD]
-    float *sc = qs + G * HD;         // [G][P]
-    float *red = sc + G * p.P;       // [G][2] (m, l)
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int i = tid; i < G * HD; i += kAttnThreads) qs[i] = p.q[(size_t)kvh * G * HD + i];
+    const int kvd = p.KV * hd;
+    float *qs = sm;              // [hd]
+    float *sc = sm + hd;         // [n]
+    __shared__ float red[kAttnThreads / 32];
+    __shared__ float bcast;
+    for (int i = tid; i < hd; i += kAttnThreads) qs[i] = p.q[(size_t)h * hd + i];
     __syncthreads();
-
-    // scores: C lanes per position, 4 dims each
-    constexpr int C = HD / 4, PPW = 32 / C;
-    const int pl = lane / C, c = lane % C;
-    const float *kb = p.k + (size_t)kvh * HD;
-    for (int p0 = warp * PPW; p0 < cnt; p0 += (kAttnThreads / 32) * PPW) {
-        const int pp = p0 + pl;
-        const bool valid = pp < cnt;
-        float4 kv4 = valid ? __ldg((const float4 *)(kb + (size_t)(start + pp) * kvd) + c) : make_float4(0, 0, 0, 0);
-        for (int g = 0; g < G; g++) {
-            float4 q4 = ((const float4 *)(qs + g * HD))[c];
-            float part = q4.x * kv4.x + q4.y * kv4.y + q4.z * kv4.z + q4.w * kv4.w;
-#pragma unroll
-            for (int o = C / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-            if (c == 0 && valid) sc[g * p.P + pp] = fm(part, p.scale);
+    const float4 *q4 = (const float4 *)qs;
+    for (int pp = tid; pp < n; pp += kAttnThreads) {
+        const float4 *kr = (const float4 *)(p.k + (size_t)pp * kvd + (size_t)g * hd);
+        float acc = 0.0f;
+        for (int c = 0; c < hd / 4; c++) {
+            const float4 kv = __ldg(kr + c), qv = q4[c];
+            acc = fa(acc, fm(qv.x, kv.x));
+            acc = fa(acc, fm(qv.y, kv.y));
+            acc = fa(acc, fm(qv.z, kv.z));
+            acc = fa(acc, fm(qv.w, kv.w));
         }
+        sc[pp] = fm(acc, p.scale);
     }
     __syncthreads();
-    // softmax numerators per head (src/ops.rs:1206-1230: subtract the max, exp)
-    for (int g = warp; g < G; g += kAttnThreads / 32) {
-        float m = -INFINITY;
-        for (int i = lane; i < cnt; i += 32) m = fmaxf(m, sc[g * p.P + i]);
+    float m = -INFINITY;
+    for (int i = tid; i < n; i += kAttnThreads) m = fmaxf(m, sc[i]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.0f;
-        for (int i = lane; i < cnt; i += 32) {
-            float e = expf(sc[g * p.P + i] - m);
-            sc[g * p.P + i] = e;
-            l += e;
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            red[2 * g] = m;
-            red[2 * g + 1] = l;
-        }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float mm = -INFINITY;
+        for (int w = 0; w < kAttnThreads / 32; w++) mm = fmaxf(mm, red[w]);
+        bcast = mm;
     }
     __syncthreads();
-    // o = Σ e·v ; TPD threads share one dim over interleaved positions
-    constexpr int TPD = kAttnThreads / HD;
-    const int d = tid % HD, pg = tid / HD;
-    const float *vb = p.v + (size_t)kvh * HD + d;
-    float acc[kGMax];
-    float *accs = sc + G * p.P + 2 * G + 8;  // [TPD][G][HD] reduction scratch (TPD > 1)
-    for (int g0 = 0; g0 < G; g0 += kGMax) {
-        const int gn = min(kGMax, G - g0);
-#pragma unroll
-        for (int j = 0; j < kGMax; j++) acc[j] = 0.0f;
-        for (int i = pg; i < cnt; i += TPD) {
-            const float vv = __ldg(vb + (size_t)(start + i) * kvd);
-#pragma unroll
-            for (int j = 0; j < kGMax; j++)
-                if (j < gn) acc[j] += sc[(g0 + j) * p.P + i] * vv;
-        }
-        if (TPD > 1) {
-#pragma unroll
-            for (int j = 0; j < kGMax; j++)
-                if (j < gn) accs[(pg * kGMax + j) * HD + d] = acc[j];
-            __syncthreads();
-            if (pg == 0) {
-                for (int t = 1; t < TPD; t++)
-#pragma unroll
-                    for (int j = 0; j < kGMax; j++)
-                        if (j < gn) acc[j] += accs[(t * kGMax + j) * HD + d];
+    const float mx = bcast;
+    if (!isfinite(mx)) {
+        const float u = __fdiv_rn(1.0f, (float)n);
+        for (int i = tid; i < n; i += kAttnThreads) sc[i] = u;
+    } else {
+        for (int i = tid; i < n; i += kAttnThreads) sc[i] = expf_glibc(fs(sc[i], mx));
+        __syncthreads();
+        if (tid == 0) {
+            float total = 0.0f;
+            int i = 0;
+            for (; i + 4 <= n; i += 4) {
+                const float4 v = *(const float4 *)(sc + i);
+                total = fa(fa(fa(fa(total, v.x), v.y), v.z), v.w);
             }
-            __syncthreads();
+            for (; i < n; i++) total = fa(total, sc[i]);
+            bcast = __fdiv_rn(1.0f, total);
         }
-        if (pg == 0) {
-            for (int j = 0; j < gn; j++) {
-                const int h = kvh * G + g0 + j;
-                float *pp = p.part + ((size_t)h * p.S_max + s) * (HD + 2);
-                pp[d] = acc[j];
-                if (d == 0) {
-                    pp[HD] = red[2 * (g0 + j)];
-                    pp[HD + 1] = red[2 * (g0 + j) + 1];
-                }
-            }
-        }
+        __syncthreads();
+        const float inv = bcast;
+        for (int i = tid; i < n; i += kAttnThreads) sc[i] = fm(sc[i], inv);
     }
-    // last CTA of this kv head merges the splits
-    __threadfence();
     __syncthreads();
-    __shared__ int last;
-    if (tid == 0) last = (atomicAdd(p.counter + kvh, 1) == nsplit - 1);
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    for (int i = tid; i < G * HD; i += kAttnThreads) {
-        const int g = i / HD, dd = i % HD, h = kvh * G + g;
-        const float *base = p.part + (size_t)h * p.S_max * (HD + 2);
-        float M = -INFINITY;
-        for (int t = 0; t < nsplit; t++) M = fmaxf(M, __ldcg(base + (size_t)t * (HD + 2) + HD));
-        float L = 0.0f, o = 0.0f;
-        for (int t = 0; t < nsplit; t++) {
-            const float *pp = base + (size_t)t * (HD + 2);
-            const float w = expf(__ldcg(pp + HD) - M);
-            L += __ldcg(pp + HD + 1) * w;
-            o += __ldcg(pp + dd) * w;
+    for (int d = tid; d < hd; d += kAttnThreads) {
+        const float *vb = p.v + (size_t)g * hd + d;
+        float acc = 0.0f;
+        int pp = 0;
+        for (; pp + 4 <= n; pp += 4) {
+            const float v0 = __ldg(vb + (size_t)pp * kvd), v1 = __ldg(vb + (size_t)(pp + 1) * kvd);
+            const float v2 = __ldg(vb + (size_t)(pp + 2) * kvd), v3 = __ldg(vb + (size_t)(pp + 3) * kvd);
+            acc = fa(acc, fm(sc[pp], v0));
+            acc = fa(acc, fm(sc[pp + 1], v1));
+            acc = fa(acc, fm(sc[pp + 2], v2));
+            acc = fa(acc, fm(sc[pp + 3], v3));
         }
-        p.out[(size_t)h * HD + dd] = o / L;
+        for (; pp < n; pp++) acc = fa(acc, fm(sc[pp], __ldg(vb + (size_t)pp * kvd)));
+        p.out[(size_t)h * hd + d] = acc;
     }
-    if (tid == 0) p.counter[kvh] = 0;
 }
 
 // ── embedding row (src/forward.rs:389-405): x = dequant(token_embd[tok]) ──
@@ -456,50 +480,38 @@ __global__ void k_commit(int *d_len, uint32_t *toks, const unsigned long long *a
     *d_len = len + 1;
 }
 
-// ── kernel-level parity: integer sub-block sums of rows against an xq ──
+// ── kernel-level parity: integer sub-block sums of one row against an xq ──
 __global__ void k_subblock_sums(DMat W, const int8_t *xq_g, int32_t *out) {
     extern __shared__ __align__(16) unsigned char smem[];
     int8_t *xq = (int8_t *)smem;
     for (int i = threadIdx.x; i < W.K; i += blockDim.x) xq[i] = xq_g[i];
-    __syncthreads();
-    const int sub = (W.type == 12 || W.type == 13) ? 32 : 16;
-    const int per_quarter = 64 / sub;
-    XQ x{xq, nullptr, nullptr};
-    // one thread per quarter; the float part is not needed
-    float *dummy_e = (float *)(smem + ((W.K + 15) & ~15));
-    float *dummy_s = dummy_e + W.K / 16;
+    float *zero_e = (float *)(smem + ((W.K + 15) & ~15));
+    float *zero_s = zero_e + W.K / 16;
     for (int i = threadIdx.x; i < W.K / 16; i += blockDim.x) {
-        dummy_e[i] = 0.0f;
-        dummy_s[i] = 0.0f;
+        zero_e[i] = 0.0f;
+        zero_s[i] = 0.0f;
     }
     __syncthreads();
-    x.e = dummy_e;
-    x.s = dummy_s;
+    const XQ x{xq, zero_e, zero_s};
     for (int qt = threadIdx.x; qt < W.nblk * 4; qt += blockDim.x) {
         int is[4];
+        float t[4];
         switch (W.type) {
-        case 12: quarter<12>(W, 0, qt, x, is); break;
-        case 13: quarter<13>(W, 0, qt, x, is); break;
-        case 14: quarter<14>(W, 0, qt, x, is); break;
-        case 11: quarter<11>(W, 0, qt, x, is); break;
-        default: quarter<10>(W, 0, qt, x, is); break;
+        case 12: quarter<12>(W, 0, qt, x, t, is); break;
+        case 13: quarter<13>(W, 0, qt, x, t, is); break;
+        case 14: quarter<14>(W, 0, qt, x, t, is); break;
+        case 11: quarter<11>(W, 0, qt, x, t, is); break;
+        default: quarter<10>(W, 0, qt, x, t, is); break;
         }
         const int b = qt >> 2, q = qt & 3;
-        if (sub == 32) {
-            out[b * 8 + 2 * q] = is[0];
-            out[b * 8 + 2 * q + 1] = is[1];
-        } else if (W.type == 14) {
-            // quarter q of Q6_K covers groups 4h+par and 4h+par+2
-            const int h = q >> 1, par = q & 1, glo = 4 * h + par, ghi = glo + 2;
-            out[b * 16 + 2 * glo] = is[0];
-            out[b * 16 + 2 * glo + 1] = is[1];
-            out[b * 16 + 2 * ghi] = is[2];
-            out[b * 16 + 2 * ghi + 1] = is[3];
-        } else {
-            for (int k = 0; k < 4; k++) out[b * 16 + 4 * q + k] = is[k];
-        }
-        (void)per_quarter;
+        for (int k = 0; k < terms_per_quarter(W.type); k++)
+            out[b * subs_per_block(W.type) + term_sub(W.type, q, k)] = is[k];
     }
+}
+
+// ── expf parity probe: the device exp against the host libm ──
+__global__ void k_expf(const float *x, float *y, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) y[i] = expf_glibc(x[i]);
 }
 
 }  // namespace cxm

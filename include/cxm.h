@@ -110,6 +110,11 @@ int cxm_debug_matvec(int ggml_type, const uint8_t *w, uint32_t rows, uint32_t k,
 int cxm_debug_attention(const float *q, const float *k, const float *v, uint32_t total, uint32_t heads,
                         uint32_t heads_kv, uint32_t head_dim, float *out);
 
+/* f32::exp as every exponential of the path computes it on the device
+ * (softmax, SiLU): the same rounding as the host C library's expf, which the
+ * reference's f32::exp calls (src/ops.rs:1221, src/kernels/scalar.rs:65). */
+int cxm_debug_expf(const float *x, float *y, uint64_t n);
+
 /* ── measurement hooks (no counterpart in the reference: timing only) ──── */
 
 /* Replay the greedy decode step `steps` times for the token at the cache's

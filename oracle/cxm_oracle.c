@@ -1480,3 +1480,9 @@ void orc_cache_fill(orc_cache *c, int n, uint64_t seed) {
         }
     c->len = n;
 }
+
+/* the host C library's expf over an array (the function the reference's
+ * f32::exp calls); used to check the device exp */
+void orc_expf(const float *x, float *y, size_t n) {
+    for (size_t i = 0; i < n; i++) y[i] = expf(x[i]);
+}

@@ -119,6 +119,7 @@ int orc_generate(orc_model *m, orc_cache *c, const uint32_t *prompt, int n_promp
                  orc_sampler *s, uint32_t *out, int *n_out);
 
 void orc_cache_fill(orc_cache *c, int n, uint64_t seed);
+void orc_expf(const float *x, float *y, size_t n);
 
 void orc_set_threads(int n);
 int  orc_get_threads(void);

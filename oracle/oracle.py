@@ -81,6 +81,7 @@ def _declare(L: C.CDLL) -> None:
         "orc_forward": (C.c_int, [P, P, P, C.c_int, P]),
         "orc_generate": (C.c_int, [P, P, P, C.c_int, C.c_int, P, P, P]),
         "orc_cache_fill": (None, [P, C.c_int, C.c_uint64]),
+        "orc_expf": (None, [P, P, C.c_size_t]),
         "orc_set_threads": (None, [C.c_int]),
         "orc_get_threads": (C.c_int, []),
     }

@@ -62,14 +62,32 @@ def test_subblock_sums_bit_exact_on_golden_rows():
 
 @pytest.mark.parametrize("t", TYPES)
 @pytest.mark.parametrize("k", [256, 2048, 11008])
-def test_matvec_matches_oracle(t, k):
+def test_matvec_matches_oracle_bit_exact(t, k):
+    # the device sums each row's sub-block terms in the reference's order, so
+    # the f32 result is the oracle's to the last bit (the reference's own bar
+    # for a fused kernel is 1e-4 relative, src/kernels/mod.rs:887-893)
     rows = 70
     w = cx.quantize(t, normals(rows * k, 0.02, k + t))
     x = normals(k, 1.0, 7 * k + t)
     got = cx.matvec(t, w, rows, k, x)
     want = O.matmul(x, w, t, k, rows)[0]
-    scale = np.maximum(np.abs(want), 1.0)
-    assert (np.abs(got - want) / scale).max() < 1e-4
+    assert (np.abs(got - want) / np.maximum(np.abs(want), 1.0)).max() < 1e-4
+    np.testing.assert_array_equal(got, want)
+
+
+def test_expf_matches_host_libm():
+    rng = np.random.default_rng(11)
+    x = np.concatenate([
+        rng.uniform(-110, 95, 4_000_000).astype(np.float32),
+        rng.uniform(-1, 1, 2_000_000).astype(np.float32),
+        np.frombuffer(rng.integers(0, 2**32, 2_000_000, dtype=np.uint64).astype(np.uint32).tobytes(), np.float32),
+        np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 88.0, 88.72283, -103.97, -104.0, 1e-30, -1e-30], np.float32),
+    ])
+    got = cx.expf(x)
+    want = np.zeros_like(x)
+    O.lib().orc_expf(O.ptr(x), O.ptr(want), x.size)
+    same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+    assert same.all(), x[~same][:5]
 
 
 def test_matvec_matches_reference_kernels_golden():
@@ -102,6 +120,7 @@ def test_attention_matches_oracle(heads, kvh, hd, total):
     got = cx.attention(q, k, v, total, heads, kvh, hd)
     want = O.attention(q, k, v, 1, total, heads, kvh, hd)
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-5)
+    np.testing.assert_array_equal(got, want)
 
 
 # ── model level (tiny config) ──
@@ -118,16 +137,18 @@ def test_tiny_logits_match_oracle(tiny_path):
     got = m.forward(prompt, c)
     want = om.forward(oc, prompt)
     assert rel_range(got, want) <= 1e-3
+    np.testing.assert_array_equal(got, want)
     assert len(c) == len(oc) == 32
     # decode steps keep agreeing
     for t in (17, 4000, 8191):
         got = m.forward([t], c)
         want = om.forward(oc, [t])
         assert rel_range(got, want) <= 1e-3
+        np.testing.assert_array_equal(got, want)
     # and the KV cache contents agree
     for layer in (0, 5):
-        np.testing.assert_allclose(c.capa(layer), oc.layer(layer, False), rtol=1e-3, atol=1e-4)
-        np.testing.assert_allclose(c.capa(layer, True), oc.layer(layer, True), rtol=1e-3, atol=1e-4)
+        np.testing.assert_array_equal(c.capa(layer), oc.layer(layer, False))
+        np.testing.assert_array_equal(c.capa(layer, True), oc.layer(layer, True))
 
 
 def test_tiny_greedy_64_tokens_identical(tiny_path):
@@ -178,3 +199,30 @@ def test_errors_are_reported_not_faulted(tiny_path):
     assert len(c) == 0
     m.forward([1, 2, 3], c)
     assert len(c) == 3
+
+
+# ── model level (Qwen2.5-3B shape) ──
+
+@pytest.fixture(scope="module")
+def qwen3b_path():
+    import bench
+    return bench.ensure_model("qwen3b", 42)
+
+
+def test_qwen3b_prompt_logits_and_64_greedy_tokens(qwen3b_path):
+    """The north-star bar on the benchmark's own model: logits of a seeded
+    prompt within 1e-3 of the range (here: bit-identical) and the first 64
+    greedy tokens identical to the oracle's."""
+    m = cx.Modelo(qwen3b_path)
+    om = O.Model(qwen3b_path)
+    prompt = prompt_of(42, 16, m.cfg.vocab)
+    c, oc = m.cache(256), om.cache()
+    got = m.forward(prompt, c)
+    want = om.forward(oc, prompt)
+    assert rel_range(got, want) <= 1e-3
+    np.testing.assert_array_equal(got, want)
+    c2, oc2 = m.cache(256), om.cache()
+    toks = m.generar(prompt, 64, cx.Muestreador.voraz(), c2)
+    otoks = om.generate(oc2, prompt, 64, O.Sampler(0, 0.0, 1.0))
+    assert toks == otoks
+    assert len(c2) == len(oc2) == 16 + 64
