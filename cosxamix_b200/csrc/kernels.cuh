@@ -1,10 +1,11 @@
-// Device code of the decode step: k-quant matvec (all five super-block
-// layouts), fused activation quantization, RoPE + KV append, split-K
-// flash-decode attention, embedding lookup and the greedy argmax.
+// Device code shared by the decode kernels: the weight planes, the k-quant
+// super-block arithmetic of the five layouts, and the dequantization of a
+// single value (embedding rows).
 //
 // Weights live in HBM as "planes" (see DMat): the GGUF super-block bytes are
 // split once at load into 16-byte-aligned per-row arrays so every weight load
-// is a coalesced 128-bit load, without changing a single bit of the values.
+// is an aligned 128-bit load or bulk copy, without changing a single bit of
+// the values.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -17,10 +18,11 @@ namespace cxm {
 // Q6_K 192 B (ql|qh), Q3_K 96 B (hmask|qs), Q2_K 64 B (qs).
 // Plane S: Q6_K 16 B int8 scales, Q3_K 12 B packed 6-bit scales, Q2_K 16 B.
 // Plane D: Q6_K 2 B (d), Q3_K 2 B (d), Q2_K 4 B (d, dmin).
+// Row pitches are multiples of 16 bytes (S and D rows padded).
 struct DMat {
     int type, rows, K, nblk;
     const uint8_t *a, *s, *d;
-    uint32_t a_row, s_row, d_row;  // bytes per row of each plane
+    uint32_t a_row, s_row, d_row;  // bytes per row of each plane (pitch)
 };
 
 __host__ __device__ inline int plane_a_bytes(int t) {
@@ -28,14 +30,14 @@ __host__ __device__ inline int plane_a_bytes(int t) {
 }
 __host__ __device__ inline int plane_s_bytes(int t) { return t == 14 ? 16 : t == 11 ? 12 : t == 10 ? 16 : 0; }
 __host__ __device__ inline int plane_d_bytes(int t) { return t == 14 ? 2 : t == 11 ? 2 : t == 10 ? 4 : 0; }
+__host__ __device__ inline uint32_t pitch16(uint32_t b) { return (b + 15u) & ~15u; }
 
 __device__ __forceinline__ float h2f(uint32_t bits16) {
     return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFF)));
 }
 
-// Exact IEEE ops, never contracted into FMA: the per-sub-block terms keep the
-// reference's rounding (the sums over sub-blocks are reordered by the warp
-// reduction, which is the only difference left).
+// Exact IEEE single-precision operations, never contracted into FMA, so every
+// term keeps the reference's rounding.
 __device__ __forceinline__ float fm(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fs(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float fa(float a, float b) { return __fadd_rn(a, b); }
@@ -62,20 +64,6 @@ struct XQ {  // the quantized activation, in shared memory
     const float *e, *s;
 };
 
-__device__ __forceinline__ int dot8(const uint32_t *w, const int4 *x2) {
-    // 32 bytes of unsigned weight values (8 words) against 32 i8 activations
-    int4 a = x2[0], b = x2[1];
-    int s = 0;
-    s = __dp4a((int)w[0], a.x, s);
-    s = __dp4a((int)w[1], a.y, s);
-    s = __dp4a((int)w[2], a.z, s);
-    s = __dp4a((int)w[3], a.w, s);
-    s = __dp4a((int)w[4], b.x, s);
-    s = __dp4a((int)w[5], b.y, s);
-    s = __dp4a((int)w[6], b.z, s);
-    s = __dp4a((int)w[7], b.w, s);
-    return s;
-}
 __device__ __forceinline__ int dot4w(const uint32_t *w, int4 a) {
     int s = 0;
     s = __dp4a((int)w[0], a.x, s);
@@ -85,25 +73,43 @@ __device__ __forceinline__ int dot4w(const uint32_t *w, int4 a) {
     return s;
 }
 
+// loads from global memory (read-only path) or from shared memory (plain)
+template <bool G>
+__device__ __forceinline__ uint4 ld16(const uint8_t *p) {
+    if (G) return __ldg((const uint4 *)p);
+    return *(const uint4 *)p;
+}
+template <bool G>
+__device__ __forceinline__ uint32_t ld4(const uint8_t *p) {
+    if (G) return __ldg((const uint32_t *)p);
+    return *(const uint32_t *)p;
+}
+template <bool G>
+__device__ __forceinline__ uint32_t ld2(const uint8_t *p) {
+    if (G) return __ldg((const unsigned short *)p);
+    return *(const unsigned short *)p;
+}
+template <bool G>
 __device__ __forceinline__ void ld32(const uint8_t *p, uint32_t w[8]) {
-    uint4 a = __ldg((const uint4 *)p), b = __ldg((const uint4 *)(p + 16));
+    uint4 a = ld16<G>(p), b = ld16<G>(p + 16);
     w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
     w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
 }
 
-// Each lane works on a "quarter": 64 values of one super-block. `qt` in
-// [0, 4*nblk): block b = qt/4, quarter q = qt%4. Returns the float sum of the
-// quarter's sub-block terms (2 terms for sub-blocks of 32, 4 for 16), and the
-// integer sums in `isum` when requested (parity checks).
+// ── one "quarter" (64 values) of a super-block ──
+// A lane works on quarter q (0..3) of super-block b (the block's index along
+// the row, which addresses the activation). `pa`, `ps`, `pd` point at this
+// block's bytes in planes A, S and D. Writes the quarter's sub-block terms
+// t[0..tpq) in the order of term_sub(); `isum` (optional) gets the integer
+// sub-block sums.
 
 // Q4_K: src/kernels/scalar.rs:132-170
-__device__ __forceinline__ void quarter_q4k(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
-    const int b = qt >> 2, q = qt & 3;
-    const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 144;
-    uint4 hdr = __ldg((const uint4 *)blk);
+template <bool G>
+__device__ __forceinline__ void q_q4k(const uint8_t *pa, int b, int q, const XQ &x, float *t, int *isum) {
+    const uint4 hdr = ld16<G>(pa);
     uint32_t w[8];
-    ld32(blk + 16 + 32 * q, w);
-    float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
+    ld32<G>(pa + 16 + 32 * q, w);
+    const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
     int sc0, m0, sc1, m1;
     scale_min_k4(2 * q, hdr.y, hdr.z, hdr.w, sc0, m0);
     scale_min_k4(2 * q + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
@@ -114,7 +120,8 @@ __device__ __forceinline__ void quarter_q4k(const DMat &W, int row, int qt, cons
         hi[i] = (w[i] >> 4) & 0x0F0F0F0Fu;
     }
     const int4 *xp = (const int4 *)(x.q + b * 256 + q * 64);
-    int s0 = dot8(lo, xp), s1 = dot8(hi, xp + 2);
+    const int s0 = dot4w(lo, xp[0]) + dot4w(lo + 4, xp[1]);
+    const int s1 = dot4w(hi, xp[2]) + dot4w(hi + 4, xp[3]);
     const int j0 = b * 8 + 2 * q;
     if (isum) { isum[0] = s0; isum[1] = s1; }
     t[0] = fm(x.e[j0], fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), x.s[j0])));
@@ -122,14 +129,13 @@ __device__ __forceinline__ void quarter_q4k(const DMat &W, int row, int qt, cons
 }
 
 // Q5_K: src/kernels/scalar.rs:179-217
-__device__ __forceinline__ void quarter_q5k(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
-    const int b = qt >> 2, q = qt & 3;
-    const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 176;
-    uint4 hdr = __ldg((const uint4 *)blk);
+template <bool G>
+__device__ __forceinline__ void q_q5k(const uint8_t *pa, int b, int q, const XQ &x, float *t, int *isum) {
+    const uint4 hdr = ld16<G>(pa);
     uint32_t qh[8], w[8];
-    ld32(blk + 16, qh);
-    ld32(blk + 48 + 32 * q, w);
-    float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
+    ld32<G>(pa + 16, qh);
+    ld32<G>(pa + 48 + 32 * q, w);
+    const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
     int sc0, m0, sc1, m1;
     const int j0 = 2 * q, j1 = 2 * q + 1;
     scale_min_k4(j0, hdr.y, hdr.z, hdr.w, sc0, m0);
@@ -141,7 +147,8 @@ __device__ __forceinline__ void quarter_q5k(const DMat &W, int row, int qt, cons
         hi[i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> j1) & 0x01010101u) << 4);
     }
     const int4 *xp = (const int4 *)(x.q + b * 256 + q * 64);
-    int s0 = dot8(lo, xp), s1 = dot8(hi, xp + 2);
+    const int s0 = dot4w(lo, xp[0]) + dot4w(lo + 4, xp[1]);
+    const int s1 = dot4w(hi, xp[2]) + dot4w(hi + 4, xp[3]);
     const int k0 = b * 8 + j0;
     if (isum) { isum[0] = s0; isum[1] = s1; }
     t[0] = fm(x.e[k0], fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), x.s[k0])));
@@ -150,14 +157,15 @@ __device__ __forceinline__ void quarter_q5k(const DMat &W, int row, int qt, cons
 
 // Q6_K: src/kernels/scalar.rs:294-324. Quarter q = half h (q>>1) and ql
 // column par (q&1): groups gi = par (low nibbles) and gi = par+2 (high).
-__device__ __forceinline__ void quarter_q6k(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
-    const int b = qt >> 2, q = qt & 3, h = q >> 1, par = q & 1;
-    const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 192;
+template <bool G>
+__device__ __forceinline__ void q_q6k(const uint8_t *pa, const uint8_t *ps, const uint8_t *pd, int b, int q,
+                                      const XQ &x, float *t, int *isum) {
+    const int h = q >> 1, par = q & 1;
     uint32_t ql[8], qh[8];
-    ld32(blk + 64 * h + 32 * par, ql);
-    ld32(blk + 128 + 32 * h, qh);
-    uint4 scv = __ldg((const uint4 *)(W.s + (size_t)row * W.s_row + (size_t)b * 16));
-    float d = h2f(__ldg((const unsigned short *)(W.d + (size_t)row * W.d_row + (size_t)b * 2)));
+    ld32<G>(pa + 64 * h + 32 * par, ql);
+    ld32<G>(pa + 128 + 32 * h, qh);
+    const uint4 scv = ld16<G>(ps);
+    const float d = h2f(ld2<G>(pd));
     uint32_t vlo[8], vhi[8];
     const int slo = 2 * par, shi = 2 * (par + 2);
 #pragma unroll
@@ -181,24 +189,23 @@ __device__ __forceinline__ void quarter_q6k(const DMat &W, int row, int qt, cons
         const int si = 2 * g + md;
         const int sc = (int)(int8_t)((scw[si >> 2] >> (8 * (si & 3))) & 0xFF);
         const int sub = b * 16 + si;
-        float esc = fm(d, (float)sc);
+        const float esc = fm(d, (float)sc);
         t[k] = fm(fm(x.e[sub], esc), fs((float)s[k], fm(32.0f, x.s[sub])));
     }
 }
 
 // Q3_K: src/kernels/scalar.rs:236-275. Quarter q = groups 2q and 2q+1.
-__device__ __forceinline__ void quarter_q3k(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
-    const int b = qt >> 2, q = qt & 3;
-    const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 96;
+template <bool G>
+__device__ __forceinline__ void q_q3k(const uint8_t *pa, const uint8_t *ps, const uint8_t *pd, int b, int q,
+                                      const XQ &x, float *t, int *isum) {
     uint32_t hm[8], qs[8];
-    ld32(blk, hm);
-    ld32(blk + 32 + 32 * (q >> 1), qs);
-    const uint32_t *sp = (const uint32_t *)(W.s + (size_t)row * W.s_row + (size_t)b * 12);
-    uint32_t a0 = __ldg(sp), a1 = __ldg(sp + 1), tt = __ldg(sp + 2);
-    float d = h2f(__ldg((const unsigned short *)(W.d + (size_t)row * W.d_row + (size_t)b * 2)));
+    ld32<G>(pa, hm);
+    ld32<G>(pa + 32 + 32 * (q >> 1), qs);
+    const uint32_t a0 = ld4<G>(ps), a1 = ld4<G>(ps + 4), tt = ld4<G>(ps + 8);
+    const float d = h2f(ld2<G>(pd));
     // scales of sub-blocks 4q..4q+3 (src/quant.rs:87-106)
-    uint32_t aa = (q & 1) ? a1 : a0;
-    uint32_t wq = ((aa >> ((q >> 1) * 4)) & 0x0F0F0F0Fu) | (((tt >> (2 * q)) & 0x03030303u) << 4);
+    const uint32_t aa = (q & 1) ? a1 : a0;
+    const uint32_t wq = ((aa >> ((q >> 1) * 4)) & 0x0F0F0F0Fu) | (((tt >> (2 * q)) & 0x03030303u) << 4);
     int s[4];
 #pragma unroll
     for (int gg = 0; gg < 2; gg++) {
@@ -215,20 +222,20 @@ __device__ __forceinline__ void quarter_q3k(const DMat &W, int row, int qt, cons
     for (int k = 0; k < 4; k++) {
         const int sc = (int)((wq >> (8 * k)) & 0xFF);
         const int sub = b * 16 + 4 * q + k;
-        float esc = fm(d, fs((float)sc, 32.0f));
+        const float esc = fm(d, fs((float)sc, 32.0f));
         t[k] = fm(fm(x.e[sub], esc), fs((float)s[k], fm(4.0f, x.s[sub])));
     }
 }
 
 // Q2_K: src/kernels/q2k.rs:41-69. Quarter q = groups 2q and 2q+1.
-__device__ __forceinline__ void quarter_q2k(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
-    const int b = qt >> 2, q = qt & 3;
-    const uint8_t *blk = W.a + (size_t)row * W.a_row + (size_t)b * 64;
+template <bool G>
+__device__ __forceinline__ void q_q2k(const uint8_t *pa, const uint8_t *ps, const uint8_t *pd, int b, int q,
+                                      const XQ &x, float *t, int *isum) {
     uint32_t qs[8];
-    ld32(blk + 32 * (q >> 1), qs);
-    uint32_t scw = __ldg((const uint32_t *)(W.s + (size_t)row * W.s_row + (size_t)b * 16 + 4 * q));
-    uint32_t dd = __ldg((const uint32_t *)(W.d + (size_t)row * W.d_row + (size_t)b * 4));
-    float d = h2f(dd), dm = h2f(dd >> 16);
+    ld32<G>(pa + 32 * (q >> 1), qs);
+    const uint32_t scw = ld4<G>(ps + 4 * q);
+    const uint32_t dd = ld4<G>(pd);
+    const float d = h2f(dd), dm = h2f(dd >> 16);
     int s[4];
 #pragma unroll
     for (int gg = 0; gg < 2; gg++) {
@@ -245,22 +252,32 @@ __device__ __forceinline__ void quarter_q2k(const DMat &W, int row, int qt, cons
     for (int k = 0; k < 4; k++) {
         const int sc = (int)((scw >> (8 * k)) & 0xFF);
         const int sub = b * 16 + 4 * q + k;
-        float ev = fm(d, (float)(sc & 0xF)), mv = fm(dm, (float)(sc >> 4));
+        const float ev = fm(d, (float)(sc & 0xF)), mv = fm(dm, (float)(sc >> 4));
         t[k] = fm(x.e[sub], fs(fm(ev, (float)s[k]), fm(mv, x.s[sub])));
     }
 }
 
-// Terms of one quarter, in the order of their sub-blocks; `term_sub` gives
-// the sub-block (within the super-block) of term k. The row total is the
-// sequential f32 sum of all terms in sub-block order (src/kernels/scalar.rs:
-// `total += ...` per sub-block), which the matvec kernel reproduces exactly.
+// One quarter of format T. The row total of the reference is the sequential
+// f32 sum of all terms in sub-block order (src/kernels/scalar.rs, `total +=`
+// per sub-block); callers reproduce it exactly.
+template <int T, bool G>
+__device__ __forceinline__ void quarter_at(const uint8_t *pa, const uint8_t *ps, const uint8_t *pd, int b, int q,
+                                           const XQ &x, float *t, int *isum) {
+    if (T == 12) q_q4k<G>(pa, b, q, x, t, isum);
+    else if (T == 13) q_q5k<G>(pa, b, q, x, t, isum);
+    else if (T == 14) q_q6k<G>(pa, ps, pd, b, q, x, t, isum);
+    else if (T == 11) q_q3k<G>(pa, ps, pd, b, q, x, t, isum);
+    else q_q2k<G>(pa, ps, pd, b, q, x, t, isum);
+}
+
+// quarter qt (block qt/4, quarter qt%4) of row `row` of a matrix in HBM
 template <int T>
 __device__ __forceinline__ void quarter(const DMat &W, int row, int qt, const XQ &x, float *t, int *isum) {
-    if (T == 12) quarter_q4k(W, row, qt, x, t, isum);
-    else if (T == 13) quarter_q5k(W, row, qt, x, t, isum);
-    else if (T == 14) quarter_q6k(W, row, qt, x, t, isum);
-    else if (T == 11) quarter_q3k(W, row, qt, x, t, isum);
-    else quarter_q2k(W, row, qt, x, t, isum);
+    const int b = qt >> 2;
+    const uint8_t *pa = W.a + (size_t)row * W.a_row + (size_t)b * plane_a_bytes(T);
+    const uint8_t *ps = W.s + (size_t)row * W.s_row + (size_t)b * plane_s_bytes(T);
+    const uint8_t *pd = W.d + (size_t)row * W.d_row + (size_t)b * plane_d_bytes(T);
+    quarter_at<T, true>(pa, ps, pd, b, qt & 3, x, t, isum);
 }
 
 __host__ __device__ __forceinline__ int terms_per_quarter(int type) { return (type == 12 || type == 13) ? 2 : 4; }

@@ -45,9 +45,10 @@ struct cxm_model {
     float *out_norm = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     std::vector<void *> allocs;
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    float *scores = nullptr;  // attention scratch [n_head][ctx]
     int *err = nullptr;
     unsigned long long *argmax_key = nullptr;
-    int sms = 148, mv_blocks = 148;
+    int sms = 148;
     uint64_t weight_bytes = 0;
     bool logits_valid = false;
 
@@ -123,8 +124,8 @@ int upload_matrix(cxm_model *m, const Gguf &g, const TensorInfo &t, DMat *out) {
     d.K = K;
     d.nblk = nblk;
     d.a_row = (uint32_t)(nblk * pa);
-    d.s_row = (uint32_t)(nblk * ps);
-    d.d_row = (uint32_t)(nblk * pd);
+    d.s_row = pitch16((uint32_t)(nblk * ps));
+    d.d_row = pitch16((uint32_t)(nblk * pd));
     std::vector<uint8_t> A((size_t)rows * d.a_row), S((size_t)rows * d.s_row), D((size_t)rows * d.d_row);
     const uint8_t *src = g.data(t);
     for (int r = 0; r < rows; r++) {
@@ -187,22 +188,36 @@ void set_need(MatvecParams &p, const DMat &a) {
     if (sub_of(a.type) == 16) p.need16 = 1; else p.need32 = 1;
 }
 
-size_t matvec_smem(const MatvecParams &p) {
-    size_t b = (size_t)kWarps * kTileFloats * sizeof(float);
-    if (p.need16) b += (size_t)p.K + (size_t)p.K / 16 * 8;
-    if (p.need32) b += (size_t)p.K + (size_t)p.K / 32 * 8;
-    return (b + 15) & ~(size_t)15;
-}
+size_t matvec_smem(const MatvecParams &p) { return matvec_smem_bytes(p.K, p.need16, p.need32); }
 
-int launch_matvec(cxm_model *m, MatvecParams &p) {
-    p.total_units = 0;
-    for (int i = 0; i < p.nseg; i++) p.total_units += p.seg[i].units;
-    p.err = m->err;
-    int blocks = std::min((p.total_units + kWarps - 1) / kWarps, m->mv_blocks);
-    k_matvec<<<blocks, kThreads, matvec_smem(p), m->stream>>>(p);
-    CU(cudaGetLastError());
+// Launch with programmatic dependent launch: the kernel may start while the
+// previous one in the stream finishes (each kernel calls griddep_wait()
+// before it touches data the previous one produced).
+template <typename... Args>
+int launch_pdl(void (*kernel)(Args...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CU(cudaLaunchKernelEx(&cfg, kernel, args...));
     return 0;
 }
+
+int launch_matvec_on(cudaStream_t st, int sms, int *err, MatvecParams &p) {
+    p.total_units = 0;
+    for (int i = 0; i < p.nseg; i++) p.total_units += p.seg[i].units;
+    p.err = err;
+    const int blocks = std::max(1, std::min(p.total_units, sms));
+    return launch_pdl(k_matvec, dim3(blocks), dim3(kMvThreads), matvec_smem(p), st, p);
+}
+
+int launch_matvec(cxm_model *m, MatvecParams &p) { return launch_matvec_on(m->stream, m->sms, m->err, p); }
 
 Seg make_seg(const DMat &A, int pairing, int epi, float *out) {
     Seg s{};
@@ -215,12 +230,23 @@ Seg make_seg(const DMat &A, int pairing, int epi, float *out) {
     return s;
 }
 
-size_t attention_smem(int hd, uint32_t max_pos) { return ((size_t)hd + max_pos + 4) * sizeof(float); }
+size_t scores_smem(int hd) { return ((size_t)kScoreThreads * kKRow + (size_t)hd) * sizeof(float); }
+size_t out_smem(uint32_t max_pos) {
+    return ((size_t)((max_pos + 3) & ~3u) + 2 * kVChunk * kOutDims) * sizeof(float);
+}
 
 int set_kernel_smem_limits() {
-    CU(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    CU(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    CU(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    CU(cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    CU(cudaFuncSetAttribute(k_attn_out, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     return 0;
+}
+
+// src/ops.rs:1258-1325 for the token at *d_len, over positions 0..=*d_len
+int launch_attention_on(cudaStream_t st, AttnParams &a) {
+    const dim3 gs(a.H, (a.max_pos + kScoreThreads - 1) / kScoreThreads), go(a.H, (a.hd + kOutDims - 1) / kOutDims);
+    if (launch_pdl(k_attn_scores, gs, dim3(kScoreThreads), scores_smem(a.hd), st, a)) return -1;
+    return launch_pdl(k_attn_out, go, dim3(kOutThreads), out_smem((uint32_t)a.max_pos), st, a);
 }
 
 int launch_attention(cxm_model *m, cxm_cache *c, int layer) {
@@ -230,17 +256,16 @@ int launch_attention(cxm_model *m, cxm_cache *c, int layer) {
     a.k = c->k + (size_t)layer * c->max_tokens * kv_dim(m);
     a.v = c->v + (size_t)layer * c->max_tokens * kv_dim(m);
     a.out = m->att;
+    a.scores = m->scores;
     a.d_len = c->d_len;
     a.H = cfg.n_head;
     a.KV = cfg.n_head_kv;
     a.hd = cfg.head_dim;
     a.max_pos = (int)c->max_tokens;
+    a.score_stride = cfg.ctx;
     a.scale = 1.0f / sqrtf((float)cfg.head_dim);  // src/ops.rs:1287
     a.err = m->err;
-    const size_t smem = attention_smem(cfg.head_dim, c->max_tokens);
-    k_attention<<<cfg.n_head, kAttnThreads, smem, m->stream>>>(a);
-    CU(cudaGetLastError());
-    return 0;
+    return launch_attention_on(m->stream, a);
 }
 
 // One token of src/forward.rs:375-505 on the device, for the token at
@@ -262,8 +287,7 @@ int enqueue_step(cxm_model *m, cxm_cache *c, int mode) {
     e.x = m->x;
     e.argmax_key = logits ? m->argmax_key : nullptr;
     e.err = m->err;
-    k_embed<<<(D + 255) / 256, 256, 0, m->stream>>>(e);
-    CU(cudaGetLastError());
+    if (launch_pdl(k_embed, dim3((D + 255) / 256), dim3(256), 0, m->stream, e)) return -1;
 
     for (int l = 0; l < cfg.n_layer; l++) {
         const Layer &L = m->layers[l];
@@ -350,10 +374,8 @@ int enqueue_step(cxm_model *m, cxm_cache *c, int mode) {
         set_need(p, m->out);
         if (launch_matvec(m, p)) return -1;
     }
-    k_commit<<<1, 32, 0, m->stream>>>(c->d_len, c->toks, m->argmax_key, mode == STEP_GREEDY ? 1 : 0,
-                                      (int)c->max_tokens + 1);
-    CU(cudaGetLastError());
-    return 0;
+    return launch_pdl(k_commit, dim3(1), dim3(32), 0, m->stream, c->d_len, c->toks,
+                      (const unsigned long long *)m->argmax_key, mode == STEP_GREEDY ? 1 : 0, (int)c->max_tokens + 1);
 }
 
 int get_graph(cxm_model *m, cxm_cache *c, int mode, cudaGraphExec_t *out) {
@@ -536,18 +558,15 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
     // activations
     if (m->alloc(&m->x, cfg.dim) || m->alloc(&m->q, cfg.dim) || m->alloc(&m->att, cfg.dim) ||
         m->alloc(&m->h, std::max(cfg.ffn, 1)) || m->alloc(&m->logits, cfg.vocab) || m->alloc(&m->err, 1) ||
-        m->alloc(&m->argmax_key, 1))
+        m->alloc(&m->argmax_key, 1) || m->alloc(&m->scores, (size_t)cfg.n_head * cfg.ctx))
         return -1;
     CU(cudaMemset(m->err, 0, sizeof(int)));
     if (set_kernel_smem_limits()) return -1;
-    if (attention_smem(cfg.head_dim, (uint32_t)cfg.ctx) > 200 * 1024) {
-        set_error("context %d is beyond the attention kernel's shared-memory score buffer", cfg.ctx);
+    if (out_smem((uint32_t)cfg.ctx) > 200 * 1024 || cfg.head_dim % 16 || cfg.head_dim > kKRow - 4) {
+        set_error("context %d / head_dim %d are beyond the attention kernels' shared-memory layout", cfg.ctx,
+                  cfg.head_dim);
         return -1;
     }
-    int occ = 0;
-    CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_matvec, kThreads,
-                                                     kWarps * kTileFloats * sizeof(float) + 24 * 1024));
-    m->mv_blocks = m->sms * std::max(occ, 1);
     CU(cudaDeviceSynchronize());
     *out = m.release();
     return 0;
@@ -812,8 +831,8 @@ int dev_matrix_from_host(int type, const uint8_t *w, uint32_t rows, uint32_t k, 
     d.K = (int)k;
     d.nblk = nblk;
     d.a_row = (uint32_t)(nblk * pa);
-    d.s_row = (uint32_t)(nblk * ps);
-    d.d_row = (uint32_t)(nblk * pd);
+    d.s_row = pitch16((uint32_t)(nblk * ps));
+    d.d_row = pitch16((uint32_t)(nblk * pd));
     std::vector<uint8_t> A((size_t)rows * d.a_row), S((size_t)rows * d.s_row + 16), D((size_t)rows * d.d_row + 16);
     for (uint32_t r = 0; r < rows; r++)
         for (int b = 0; b < nblk; b++) {
@@ -897,10 +916,17 @@ extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint3
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (set_kernel_smem_limits()) return -1;
-    int blocks = std::min((p.total_units + kWarps - 1) / kWarps, sms * 2);
-    k_matvec<<<blocks, kThreads, matvec_smem(p)>>>(p);
-    CU(cudaGetLastError());
+    DevBuf derr;
+    CU(cudaMalloc(&derr.p, 4));
+    CU(cudaMemset(derr.p, 0, 4));
+    if (launch_matvec_on(0, sms, (int *)derr.p, p)) return -1;
     CU(cudaDeviceSynchronize());
+    int e = 0;
+    CU(cudaMemcpy(&e, derr.p, 4, cudaMemcpyDeviceToHost));
+    if (e) {
+        set_error("matvec kernel reported error flags %d", e);
+        return -1;
+    }
     CU(cudaMemcpy(y, dy.p, (size_t)rows * 4, cudaMemcpyDeviceToHost));
     return 0;
 }
@@ -908,13 +934,14 @@ extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint3
 extern "C" int cxm_debug_attention(const float *q, const float *k, const float *v, uint32_t total, uint32_t heads,
                                    uint32_t heads_kv, uint32_t hd, float *out) {
     if (need_device()) return -1;
-    if (!q || !k || !v || !out || total == 0 || heads_kv == 0 || heads % heads_kv || hd % 4 || hd == 0 ||
-        attention_smem((int)hd, total) > 200 * 1024) {
+    if (!q || !k || !v || !out || total == 0 || heads_kv == 0 || heads % heads_kv || hd % 16 || hd == 0 ||
+        hd > (uint32_t)(kKRow - 4) || out_smem(total) > 200 * 1024) {
         set_error("bad attention arguments");
         return -1;
     }
     const size_t kvd = (size_t)heads_kv * hd;
-    DevBuf dq, dk, dv, dout, dlen, derr;
+    DevBuf dq, dk, dv, dout, dlen, derr, dsc;
+    CU(cudaMalloc(&dsc.p, (size_t)heads * total * 4));
     CU(cudaMalloc(&dq.p, (size_t)heads * hd * 4));
     CU(cudaMalloc(&dk.p, total * kvd * 4));
     CU(cudaMalloc(&dv.p, total * kvd * 4));
@@ -937,12 +964,19 @@ extern "C" int cxm_debug_attention(const float *q, const float *k, const float *
     a.KV = (int)heads_kv;
     a.hd = (int)hd;
     a.max_pos = (int)total;
+    a.score_stride = (int)total;
+    a.scores = (float *)dsc.p;
     a.scale = 1.0f / sqrtf((float)hd);
     a.err = (int *)derr.p;
     if (set_kernel_smem_limits()) return -1;
-    k_attention<<<heads, kAttnThreads, attention_smem((int)hd, total)>>>(a);
-    CU(cudaGetLastError());
+    if (launch_attention_on(0, a)) return -1;
     CU(cudaDeviceSynchronize());
+    int e = 0;
+    CU(cudaMemcpy(&e, derr.p, 4, cudaMemcpyDeviceToHost));
+    if (e) {
+        set_error("attention kernels reported error flags %d", e);
+        return -1;
+    }
     CU(cudaMemcpy(out, dout.p, (size_t)heads * hd * 4, cudaMemcpyDeviceToHost));
     return 0;
 }

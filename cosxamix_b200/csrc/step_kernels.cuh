@@ -13,17 +13,12 @@
 
 #include "expf_glibc.h"
 #include "kernels.cuh"
+#include "pipeline.cuh"
 
 namespace cxm {
 
-constexpr int kThreads = 256;  // matvec CTA: 8 warps
-constexpr int kWarps = kThreads / 32;
-constexpr int kBatch = 8;          // row pairs per warp batch (16 sequential chains)
-constexpr int kTileStride = 132;   // floats per row of a warp's term tile (128 terms + pad)
-constexpr int kTileFloats = 2 * kBatch * kTileStride;
-
 // error flags written by kernels (never a trap); read by the host after sync
-enum : int { ERR_TOKEN = 1, ERR_POSITION = 2 };
+enum : int { ERR_TOKEN = 1, ERR_POSITION = 2, ERR_TIMEOUT = 4 };
 
 enum Pairing : int {
     PAIR_ADJ = 0,   // unit u = rows (2u, 2u+1) of A
@@ -63,6 +58,32 @@ struct MatvecParams {
     int *err;
 };
 
+// ── matvec geometry ──
+constexpr int kCW = 8;                          // consumer warps
+constexpr int kMvThreads = (kCW + 1) * 32;      // + one producer warp
+constexpr int kStages = 3;                      // smem ring depth
+constexpr int kSlots = 32;                      // row slots per stage (16 row pairs)
+constexpr int kChunk = 8;                       // super-blocks per stage (2048 values)
+constexpr int kSlotA = kChunk * 192, kSlotS = kChunk * 16, kSlotD = kChunk * 4;
+constexpr int kStageA = kSlots * kSlotA, kStageS = kSlots * kSlotS, kStageD = kSlots * kSlotD;
+constexpr int kStageBytes = kStageA + kStageS + kStageD;  // 54 KB
+constexpr int kTermStride = 132;                // floats per slot of a warp's term tile
+constexpr int kSlotsPerWarp = kSlots / kCW;     // 4
+constexpr int kTermFloats = kSlotsPerWarp * kTermStride;
+
+__host__ __device__ inline size_t matvec_act_bytes(int K, int need16, int need32) {
+    size_t b = 0;
+    if (need16) b += (size_t)K + (size_t)K / 16 * 8;
+    if (need32) b += (size_t)K + (size_t)K / 32 * 8;
+    return (b + 15) & ~(size_t)15;
+}
+__host__ __device__ inline size_t matvec_smem_bytes(int K, int need16, int need32) {
+    return (size_t)kStages * kStageBytes + (size_t)kCW * kTermFloats * 4 + kSlots * 4 +
+           matvec_act_bytes(K, need16, need32) + 128;
+}
+
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kCW * 32) : "memory"); }
+
 __device__ __forceinline__ int warp_sum_i(int v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -79,34 +100,33 @@ __device__ __forceinline__ uint32_t argmax_index(unsigned long long key) {
     return 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
 }
 
-// Activation quantization into shared memory, redundantly per CTA:
-// optional RMSNorm (src/kernels/scalar.rs:36-54, f64 sum of squares), then
-// i8 per sub-block of 16 and/or 32 (src/ops.rs:178-198).
+// Activation quantization into shared memory, redundantly per CTA, by the
+// consumer warps: optional RMSNorm (src/kernels/scalar.rs:36-54, f64 sum of
+// squares), then i8 per sub-block of 16 and/or 32 (src/ops.rs:178-198).
 __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe16, float *xs16, int8_t *xq32,
-                                  float *xe32, float *xs32, double *red) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+                                  float *xe32, float *xs32, double *red, double *scale_s) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = kCW * 32;
     const int K = p.K;
     double scale = 0.0;
     if (p.prologue == PRO_NORM) {
         double acc = 0.0;
-        for (int i = tid; i < K; i += blockDim.x) {
-            double v = (double)p.in[i];
+        for (int i = tid; i < K; i += nt) {
+            const double v = (double)p.in[i];
             acc = __dadd_rn(acc, __dmul_rn(v, v));
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
         if (lane == 0) red[warp] = acc;
-        __syncthreads();
+        consumers_sync();
         if (tid == 0) {
             double s = 0.0;
-            for (int w = 0; w < (int)(blockDim.x >> 5); w++) s = __dadd_rn(s, red[w]);
-            red[0] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s, (double)K), (double)p.eps)));
+            for (int w = 0; w < kCW; w++) s = __dadd_rn(s, red[w]);
+            *scale_s = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s, (double)K), (double)p.eps)));
         }
-        __syncthreads();
-        scale = red[0];
+        consumers_sync();
+        scale = *scale_s;
     }
-    const int nchunk = K >> 5;
-    for (int c = warp; c < nchunk; c += (blockDim.x >> 5)) {
+    for (int c = warp; c < (K >> 5); c += kCW) {
         const int i = c * 32 + lane;
         float v = p.in[i];
         if (p.prologue == PRO_NORM) v = __fmul_rn(__double2float_rn(__dmul_rn((double)v, scale)), p.norm_w[i]);
@@ -115,10 +135,10 @@ __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe
             float amax = av;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-            int qv = (int)roundf(__fmul_rn(v, inv));
+            const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+            const int qv = (int)roundf(__fmul_rn(v, inv));
             xq32[i] = (int8_t)qv;
-            int s = warp_sum_i((int)(int8_t)qv);
+            const int s = warp_sum_i((int)(int8_t)qv);
             if (lane == 0) {
                 xe32[c] = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f;
                 xs32[c] = (float)s;
@@ -128,8 +148,8 @@ __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe
             float amax = av;
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-            int qv = (int)roundf(__fmul_rn(v, inv));
+            const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+            const int qv = (int)roundf(__fmul_rn(v, inv));
             xq16[i] = (int8_t)qv;
             int s = (int)(int8_t)qv;
 #pragma unroll
@@ -140,140 +160,270 @@ __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe
             }
         }
     }
-    __syncthreads();
+    consumers_sync();
 }
 
-__device__ __forceinline__ void quarter_any(const DMat &W, int row, int qt, const XQ &x, float *t) {
-    switch (W.type) {
-    case 12: quarter<12>(W, row, qt, x, t, nullptr); break;
-    case 13: quarter<13>(W, row, qt, x, t, nullptr); break;
-    case 14: quarter<14>(W, row, qt, x, t, nullptr); break;
-    case 11: quarter<11>(W, row, qt, x, t, nullptr); break;
-    default: quarter<10>(W, row, qt, x, t, nullptr); break;
-    }
-}
-
-// Terms of quarter qt of rows r0 (of A) and r1 (of B), stored in the tile at
-// their sub-block positions relative to the iteration's first block.
-template <int T>
-__device__ __forceinline__ void pair_terms(const DMat &A, int r0, const DMat &B, int r1, int qt, int it, const XQ &x,
-                                           float *row0, float *row1) {
-    float t0[4], t1[4];
-    quarter<T>(A, r0, qt, x, t0, nullptr);
-    quarter<T>(B, r1, qt, x, t1, nullptr);
-    const int q = qt & 3, bl = (qt >> 2) - it * 8;
-    constexpr int tpq = (T == 12 || T == 13) ? 2 : 4, spb = (T == 12 || T == 13) ? 8 : 16;
-#pragma unroll
-    for (int k = 0; k < tpq; k++) {
-        const int pos = bl * spb + term_sub(T, q, k);
-        row0[pos] = t0[k];
-        row1[pos] = t1[k];
-    }
-}
-
-struct Unit {
-    int seg, r0, r1;
+// ── work decomposition ──
+// A CTA owns a contiguous, balanced range of units. It walks them in groups of
+// at most 16 units (rows of one segment), and each group in k-chunks of 8
+// super-blocks: one chunk of a group is one pipeline stage. Unit j of a group
+// occupies slots 2j (its first row) and 2j+1 (its second row), so both rows of
+// a unit land in the same consumer warp.
+struct Grp {
+    int seg, local, n;
 };
 
-__device__ __forceinline__ Unit decode_unit(const MatvecParams &p, int u) {
-    int s = 0;
+__device__ __forceinline__ bool grp_next(const MatvecParams &p, int &gu, int ue, Grp &g) {
+    if (gu >= ue) return false;
+    int s = 0, u = gu;
     while (s < p.nseg - 1 && u >= p.seg[s].units) {
         u -= p.seg[s].units;
         s++;
     }
-    const Seg &g = p.seg[s];
-    Unit r;
-    r.seg = s;
-    if (g.pairing == PAIR_ADJ) {
-        r.r0 = 2 * u;
-        r.r1 = 2 * u + 1;
-    } else if (g.pairing == PAIR_ROPE) {
-        const int h = u / g.half, i = u - h * g.half;
-        r.r0 = h * 2 * g.half + i;
-        r.r1 = r.r0 + g.half;
-    } else {
-        r.r0 = u;
-        r.r1 = u;
+    const Seg &sg = p.seg[s];
+    int n = min(16, min(ue - gu, sg.units - u));
+    if (sg.pairing == PAIR_ROPE) n = min(n, sg.half - u % sg.half);
+    g.seg = s;
+    g.local = u;
+    g.n = n;
+    gu += n;
+    return true;
+}
+
+// matrix and row of a slot; false when the slot is empty
+__device__ __forceinline__ bool slot_row(const MatvecParams &p, const Grp &g, int slot, const DMat *&M, int &row) {
+    const Seg &s = p.seg[g.seg];
+    if (slot >= 2 * g.n) return false;
+    if (s.pairing == PAIR_ADJ) {
+        M = &s.A;
+        row = 2 * g.local + slot;
+        return true;
     }
-    return r;
+    const int j = slot >> 1, hi = slot & 1;
+    if (s.pairing == PAIR_ROPE) {
+        const int h = g.local / s.half, i = g.local % s.half;
+        M = &s.A;
+        row = h * 2 * s.half + i + j + (hi ? s.half : 0);
+    } else {
+        M = hi ? &s.B : &s.A;
+        row = g.local + j;
+    }
+    return true;
+}
+
+template <int T>
+__device__ __forceinline__ void chunk_terms(const uint8_t *sa, const uint8_t *ss, const uint8_t *sd, int b0, int lane,
+                                            const XQ &x, float *tile_row) {
+    float t[4];
+    const int bl = lane >> 2, q = lane & 3;
+    quarter_at<T, false>(sa + bl * plane_a_bytes(T), ss + bl * plane_s_bytes(T), sd + bl * plane_d_bytes(T), b0 + bl,
+                         q, x, t, nullptr);
+    constexpr int tpq = (T == 12 || T == 13) ? 2 : 4, spb = (T == 12 || T == 13) ? 8 : 16;
+#pragma unroll
+    for (int k = 0; k < tpq; k++) tile_row[bl * spb + term_sub(T, q, k)] = t[k];
+}
+
+__device__ void unit_epilogue(const MatvecParams &p, const Seg &g, int r0, int r1, float y0, float y1, int pos,
+                              unsigned long long &best) {
+    if (g.at_pos && (pos < 0 || pos >= p.max_pos)) return;
+    float *out = g.out + (g.at_pos ? (size_t)pos * g.pos_stride : 0);
+    switch (g.epi) {
+    case EPI_STORE:
+        if (g.bias) {
+            y0 = fa(y0, g.bias[r0]);
+            y1 = fa(y1, g.bias[r1]);
+        }
+        out[r0] = y0;
+        out[r1] = y1;
+        break;
+    case EPI_ROPE: {
+        // src/ops.rs:1150-1193, split-half pair (i, i + hd/2) at pos
+        const int i = r0 % (2 * g.half);
+        const float c = p.rope_cos[(size_t)pos * g.half + i], sn = p.rope_sin[(size_t)pos * g.half + i];
+        const float a = fa(y0, g.bias[r0]), b = fa(y1, g.bias[r1]);
+        out[r0] = fs(fm(a, c), fm(b, sn));
+        out[r1] = fa(fm(a, sn), fm(b, c));
+        break;
+    }
+    case EPI_RESID:
+        out[r0] = fa(out[r0], y0);
+        out[r1] = fa(out[r1], y1);
+        break;
+    case EPI_SWIGLU: {
+        // src/kernels/scalar.rs:63-67 then `*a *= u` (src/forward.rs:485-487)
+        const float act = __fdiv_rn(y0, fa(1.0f, expf_glibc(-y0)));
+        out[r0] = fm(act, y1);
+        break;
+    }
+    case EPI_LOGITS: {
+        out[r0] = y0;
+        out[r1] = y1;
+        const unsigned long long ka = (y0 == y0) ? argmax_key(y0, (uint32_t)r0) : 0ull;
+        const unsigned long long kb = (y1 == y1) ? argmax_key(y1, (uint32_t)r1) : 0ull;
+        const unsigned long long kk = ka > kb ? ka : kb;
+        best = kk > best ? kk : best;
+        break;
+    }
+    }
 }
 
 // k-quant matvec, several matrices per launch (q|k|v, gate|up), activation
-// quantization fused in front and the consumer fused behind. A warp takes
-// batches of up to 8 row pairs; per 32-quarter iteration its lanes produce the
-// sub-block terms of every row into a shared-memory tile, then 16 lanes — one
-// per row — add their row's terms in sub-block order onto a running f32 total.
-__global__ void __launch_bounds__(kThreads) k_matvec(const __grid_constant__ MatvecParams p) {
-    extern __shared__ __align__(16) unsigned char smem[];
+// quantization fused in front and the consumer fused behind. Persistent: one
+// CTA per SM. A producer warp streams each stage's weight planes with bulk
+// copies (the TMA unit) into a 3-deep shared-memory ring; 8 consumer warps
+// turn a stage into sub-block terms (a lane per quarter super-block) and one
+// lane per row adds them, in sub-block order, onto the row's running total.
+__global__ void __launch_bounds__(kMvThreads, 1) k_matvec(const __grid_constant__ MatvecParams p) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+    unsigned char *stages = smem;
+    float *tiles = (float *)(smem + (size_t)kStages * kStageBytes);
+    float *ybuf = tiles + kCW * kTermFloats;
+    int8_t *xq16 = (int8_t *)(ybuf + kSlots);
     const int K = p.K;
-    float *tiles = (float *)smem;
-    int8_t *xq16 = (int8_t *)(tiles + kWarps * kTileFloats);
     int8_t *xq32 = xq16 + (p.need16 ? K : 0);
     float *xe16 = (float *)(xq32 + (p.need32 ? K : 0));
     float *xs16 = xe16 + (p.need16 ? K / 16 : 0);
     float *xe32 = xs16 + (p.need16 ? K / 16 : 0);
     float *xs32 = xe32 + (p.need32 ? K / 32 : 0);
-    __shared__ double red[kWarps];
-    __shared__ unsigned long long best_s[kWarps];
+    __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
+    __shared__ volatile int abort_flag;
+    __shared__ double red[kCW];
+    __shared__ double scale_s;
+    __shared__ unsigned long long best_s[kCW];
 
-    prologue_quantize(p, xq16, xe16, xs16, xq32, xe32, xs32, red);
-
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gwarp = blockIdx.x * kWarps + warp, nwarps = gridDim.x * kWarps;
-    const int pos = p.d_len ? *p.d_len : 0;
-    const int nq = (K / 256) * 4;
-    float *tile = tiles + warp * kTileFloats;
-    const XQ x16{xq16, xe16, xs16}, x32{xq32, xe32, xs32};
-    unsigned long long best = 0ull;
-
-    for (int k0 = 0;; k0 += kBatch) {
-        const int first = gwarp + k0 * nwarps;
-        if (first >= p.total_units) break;
-        const int nb = min(kBatch, (p.total_units - first + nwarps - 1) / nwarps);
-        // lane L < 2*nb owns the chain of row slot L (unit L/2, row L%2)
-        int my_type = 0;
-        if (lane < 2 * nb) {
-            const Unit mu = decode_unit(p, first + (lane >> 1) * nwarps);
-            const Seg &mg = p.seg[mu.seg];
-            my_type = (lane & 1) && mg.pairing == PAIR_TWO ? mg.B.type : mg.A.type;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kCW);
         }
+        abort_flag = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    griddep_launch_dependents();
+
+    const int U = p.total_units, G = gridDim.x;
+    const int ub = (int)(((long long)blockIdx.x * U) / G), ue = (int)(((long long)(blockIdx.x + 1) * U) / G);
+    const int nblk = K / 256, nkc = (nblk + kChunk - 1) / kChunk;
+
+    if (warp == kCW) {
+        // ── producer: weights never depend on the previous kernel, so they
+        // start streaming before the dependency wait ──
+        uint32_t it = 0;
+        int gu = ub;
+        Grp g;
+        bool ok = true;
+        while (ok && grp_next(p, gu, ue, g)) {
+            for (int kc = 0; kc < nkc && ok; kc++, it++) {
+                const int s = it % kStages;
+                const uint32_t ph = (it / kStages) & 1;
+                int got = 1;
+                if (lane == 0) got = mbar_wait_bounded(&empty[s], ph ^ 1, &abort_flag) ? 1 : 0;
+                got = __shfl_sync(0xffffffffu, got, 0);  // warp-uniform, and orders the copies after the wait
+                if (!got) {
+                    ok = false;
+                    break;
+                }
+                const int b0 = kc * kChunk, nb = min(kChunk, nblk - b0);
+                // bytes of this stage, each lane one slot
+                const DMat *M = nullptr;
+                int row = 0;
+                const bool valid = slot_row(p, g, lane, M, row);
+                uint32_t ba = 0, bs = 0, bd = 0;
+                if (valid) {
+                    ba = (uint32_t)(nb * plane_a_bytes(M->type));
+                    bs = plane_s_bytes(M->type) ? pitch16((uint32_t)(nb * plane_s_bytes(M->type))) : 0;
+                    bd = plane_d_bytes(M->type) ? pitch16((uint32_t)(nb * plane_d_bytes(M->type))) : 0;
+                }
+                uint32_t bytes = ba + bs + bd;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes);
+                __syncwarp();
+                if (valid) {
+                    unsigned char *st = stages + (size_t)s * kStageBytes;
+                    bulk_g2s(st + lane * kSlotA, M->a + (size_t)row * M->a_row + (size_t)b0 * plane_a_bytes(M->type),
+                             ba, &full[s]);
+                    if (bs)
+                        bulk_g2s(st + kStageA + lane * kSlotS,
+                                 M->s + (size_t)row * M->s_row + (size_t)b0 * plane_s_bytes(M->type), bs, &full[s]);
+                    if (bd)
+                        bulk_g2s(st + kStageA + kStageS + lane * kSlotD,
+                                 M->d + (size_t)row * M->d_row + (size_t)b0 * plane_d_bytes(M->type), bd, &full[s]);
+                }
+            }
+        }
+        if (!ok) {
+            if (lane == 0) {
+                abort_flag = 1;
+                atomicOr(p.err, ERR_TIMEOUT);
+            }
+        }
+        // drain: the last stages issued must have landed before the CTA exits
+        if (lane == 0) {
+            const uint32_t last = it;
+            for (uint32_t j = last > (uint32_t)kStages ? last - kStages : 0; j < last; j++)
+                mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1, &abort_flag, 1u << 20);
+        }
+        return;
+    }
+
+    // ── consumers ──
+    griddep_wait();  // activations, caches and the residual come from earlier kernels
+    prologue_quantize(p, xq16, xe16, xs16, xq32, xe32, xs32, red, &scale_s);
+    const XQ x16{xq16, xe16, xs16}, x32{xq32, xe32, xs32};
+    const int pos = p.d_len ? *p.d_len : 0;
+    float *tile = tiles + warp * kTermFloats;
+    const int slot0 = warp * kSlotsPerWarp;  // this warp's slots: row pairs 2*warp and 2*warp+1
+    unsigned long long best = 0ull;
+    uint32_t it = 0;
+    int gu = ub;
+    Grp g;
+    bool ok = true;
+    while (ok && grp_next(p, gu, ue, g)) {
+        // lane r < nvalid owns the running total of slot slot0 + r
+        const DMat *Ms[kSlotsPerWarp];
+        int rows[kSlotsPerWarp];
+        int nvalid = 0;
+        for (int r = 0; r < kSlotsPerWarp; r++)
+            if (slot_row(p, g, slot0 + r, Ms[r], rows[r])) nvalid = r + 1;
         float total = 0.0f;
-        for (int it = 0; it * 32 < nq; it++) {
-            const int qt = it * 32 + lane;
-            for (int j = 0; j < nb; j++) {
-                const Unit un = decode_unit(p, first + j * nwarps);
-                const Seg &g = p.seg[un.seg];
-                const DMat &A = g.A;
-                const DMat &B = (g.pairing == PAIR_TWO) ? g.B : g.A;
-                float *row0 = tile + (2 * j) * kTileStride, *row1 = row0 + kTileStride;
-                if (qt < nq) {
-                    const XQ &xa = (A.type == 12 || A.type == 13) ? x32 : x16;
-                    if (A.type == B.type) {
-                        switch (A.type) {
-                        case 12: pair_terms<12>(A, un.r0, B, un.r1, qt, it, xa, row0, row1); break;
-                        case 13: pair_terms<13>(A, un.r0, B, un.r1, qt, it, xa, row0, row1); break;
-                        case 14: pair_terms<14>(A, un.r0, B, un.r1, qt, it, xa, row0, row1); break;
-                        case 11: pair_terms<11>(A, un.r0, B, un.r1, qt, it, xa, row0, row1); break;
-                        default: pair_terms<10>(A, un.r0, B, un.r1, qt, it, xa, row0, row1); break;
-                        }
-                    } else {
-                        const XQ &xb = (B.type == 12 || B.type == 13) ? x32 : x16;
-                        float t0[4], t1[4];
-                        quarter_any(A, un.r0, qt, xa, t0);
-                        quarter_any(B, un.r1, qt, xb, t1);
-                        const int q = qt & 3, bl = (qt >> 2) - it * 8;
-                        for (int k = 0; k < terms_per_quarter(A.type); k++)
-                            row0[bl * subs_per_block(A.type) + term_sub(A.type, q, k)] = t0[k];
-                        for (int k = 0; k < terms_per_quarter(B.type); k++)
-                            row1[bl * subs_per_block(B.type) + term_sub(B.type, q, k)] = t1[k];
+        int my_type = 0;
+        for (int r = 0; r < nvalid; r++)
+            if (lane == r) my_type = Ms[r]->type;
+        for (int kc = 0; kc < nkc; kc++, it++) {
+            const int s = it % kStages;
+            const uint32_t ph = (it / kStages) & 1;
+            const bool got = mbar_wait_bounded(&full[s], ph, &abort_flag);
+            if (!__all_sync(0xffffffffu, got)) {
+                ok = false;
+                break;
+            }
+            const int b0 = kc * kChunk, nb = min(kChunk, nblk - b0);
+            const unsigned char *st = stages + (size_t)s * kStageBytes;
+            for (int r = 0; r < nvalid; r++) {  // warp-uniform loop over the slots
+                const int slot = slot0 + r, T = Ms[r]->type;
+                if (lane < nb * 4) {
+                    const uint8_t *sa = st + slot * kSlotA, *ss = st + kStageA + slot * kSlotS,
+                                  *sd = st + kStageA + kStageS + slot * kSlotD;
+                    const XQ &x = (T == 12 || T == 13) ? x32 : x16;
+                    float *tr = tile + r * kTermStride;
+                    switch (T) {
+                    case 12: chunk_terms<12>(sa, ss, sd, b0, lane, x, tr); break;
+                    case 13: chunk_terms<13>(sa, ss, sd, b0, lane, x, tr); break;
+                    case 14: chunk_terms<14>(sa, ss, sd, b0, lane, x, tr); break;
+                    case 11: chunk_terms<11>(sa, ss, sd, b0, lane, x, tr); break;
+                    default: chunk_terms<10>(sa, ss, sd, b0, lane, x, tr); break;
                     }
                 }
             }
             __syncwarp();
-            if (lane < 2 * nb) {
-                const int blocks = min(8, (nq - it * 32) >> 2);
-                const int nterms = blocks * subs_per_block(my_type);
-                const float4 *src = (const float4 *)(tile + lane * kTileStride);
+            if (lane == 0) mbar_arrive(&empty[s]);  // the stage's weights are consumed
+            if (lane < nvalid) {
+                const int nterms = nb * subs_per_block(my_type);
+                const float4 *src = (const float4 *)(tile + lane * kTermStride);
                 for (int c = 0; c < (nterms >> 2); c++) {
                     const float4 v = src[c];
                     total = fa(fa(fa(fa(total, v.x), v.y), v.z), v.w);
@@ -281,166 +431,175 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const __grid_constant__ Mat
             }
             __syncwarp();
         }
+        if (!ok) break;
+        // lanes 0,1 hold row pair 2*warp; lanes 2,3 row pair 2*warp+1
         const float other = __shfl_down_sync(0xffffffffu, total, 1);
-        if (lane < 2 * nb && !(lane & 1)) {
-            const Unit un = decode_unit(p, first + (lane >> 1) * nwarps);
-            const Seg &g = p.seg[un.seg];
-            const int r0 = un.r0, r1 = un.r1;
-            float y0 = total, y1 = other;
-            if (!(g.at_pos && (pos < 0 || pos >= p.max_pos))) {
-                float *out = g.out + (g.at_pos ? (size_t)pos * g.pos_stride : 0);
-                switch (g.epi) {
-                case EPI_STORE:
-                    if (g.bias) {
-                        y0 = fa(y0, g.bias[r0]);
-                        y1 = fa(y1, g.bias[r1]);
-                    }
-                    out[r0] = y0;
-                    out[r1] = y1;
-                    break;
-                case EPI_ROPE: {
-                    // src/ops.rs:1150-1193, split-half pair (i, i + hd/2) at pos
-                    const int i = r0 % (2 * g.half);
-                    const float c = p.rope_cos[(size_t)pos * g.half + i], sn = p.rope_sin[(size_t)pos * g.half + i];
-                    const float a = fa(y0, g.bias[r0]), b = fa(y1, g.bias[r1]);
-                    out[r0] = fs(fm(a, c), fm(b, sn));
-                    out[r1] = fa(fm(a, sn), fm(b, c));
-                    break;
-                }
-                case EPI_RESID:
-                    out[r0] = fa(out[r0], y0);
-                    out[r1] = fa(out[r1], y1);
-                    break;
-                case EPI_SWIGLU: {
-                    // src/kernels/scalar.rs:63-67 then `*a *= u`
-                    const float act = __fdiv_rn(y0, fa(1.0f, expf_glibc(-y0)));
-                    out[r0] = fm(act, y1);
-                    break;
-                }
-                case EPI_LOGITS: {
-                    out[r0] = y0;
-                    out[r1] = y1;
-                    unsigned long long ka = (y0 == y0) ? argmax_key(y0, (uint32_t)r0) : 0ull;
-                    unsigned long long kb = (y1 == y1) ? argmax_key(y1, (uint32_t)r1) : 0ull;
-                    unsigned long long kk = ka > kb ? ka : kb;
-                    best = kk > best ? kk : best;
-                    break;
-                }
-                }
-            }
+        if (!(lane & 1) && lane + 1 < nvalid) {
+            const Seg &sg = p.seg[g.seg];
+            unit_epilogue(p, sg, rows[lane], rows[lane + 1], total, other, pos, best);
         }
+    }
+    if (!ok && lane == 0) {
+        abort_flag = 1;
+        atomicOr(p.err, ERR_TIMEOUT);
     }
     if (p.argmax_key) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+            const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
             best = v > best ? v : best;
         }
         if (lane == 0) best_s[warp] = best;
-        __syncthreads();
-        if (threadIdx.x == 0) {
+        consumers_sync();
+        if (tid == 0) {
             unsigned long long b = 0;
-            for (int w = 0; w < kWarps; w++) b = best_s[w] > b ? best_s[w] : b;
+            for (int w = 0; w < kCW; w++) b = best_s[w] > b ? best_s[w] : b;
             if (b) atomicMax(p.argmax_key, b);
         }
     }
 }
 
-// ── attention for one new token (src/ops.rs:1258-1325), one CTA per query
-// head, in the reference's order: each score is the sequential dot over the
-// head dimension times 1/sqrt(hd); softmax subtracts the max, exponentiates,
-// adds the exponentials position by position and multiplies by 1/total
-// (src/ops.rs:1206-1230); the output adds p·v position by position per dim.
+// ── attention for one new token (src/ops.rs:1258-1325) in the reference's
+// order, in two kernels over many SMs:
+//   scores: score[h][p] = (sequential dot of q_h and k_p over the head dim)·scale
+//   output: softmax over the head's scores (subtract the max, libm exp, sum the
+//           exponentials position by position, multiply by 1/total;
+//           src/ops.rs:1206-1230), then out[d] = Σ_p prob_p·v_p[d] added
+//           position by position.
 struct AttnParams {
     const float *q;      // [H*hd], rotated
     const float *k, *v;  // layer base, [max_tokens][KV*hd]
     float *out;          // [H*hd]
+    float *scores;       // scratch [H][max_pos]
     const int *d_len;
-    int H, KV, hd, max_pos;
+    int H, KV, hd, max_pos, score_stride;
     float scale;
     int *err;
 };
 
-constexpr int kAttnThreads = 512;
+constexpr int kScoreThreads = 128;   // positions per score CTA
+constexpr int kKRow = 132;           // smem row stride (floats) of staged K rows
+constexpr int kOutThreads = 128;
+constexpr int kOutDims = 16;         // head dims per output CTA
+constexpr int kVChunk = 64;          // positions per staged V chunk
 
-__global__ void __launch_bounds__(kAttnThreads) k_attention(const __grid_constant__ AttnParams p) {
-    extern __shared__ __align__(16) float sm[];
-    const int h = blockIdx.x, G = p.H / p.KV, g = h / G, hd = p.hd, tid = threadIdx.x;
+__global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_constant__ AttnParams p) {
+    extern __shared__ __align__(16) float ks[];  // [kScoreThreads][kKRow] then q [hd]
+    griddep_launch_dependents();
+    griddep_wait();
+    const int h = blockIdx.x, split = blockIdx.y, tid = threadIdx.x;
     const int n = *p.d_len + 1;
     if (n > p.max_pos || n <= 0) {
-        if (tid == 0 && h == 0) atomicOr(p.err, ERR_POSITION);
+        if (tid == 0 && h == 0 && split == 0) atomicOr(p.err, ERR_POSITION);
         return;
     }
-    const int kvd = p.KV * hd;
-    float *qs = sm;              // [hd]
-    float *sc = sm + hd;         // [n]
-    __shared__ float red[kAttnThreads / 32];
-    __shared__ float bcast;
-    for (int i = tid; i < hd; i += kAttnThreads) qs[i] = p.q[(size_t)h * hd + i];
+    const int p0 = split * kScoreThreads;
+    if (p0 >= n) return;
+    const int cnt = min(kScoreThreads, n - p0);
+    const int hd = p.hd, G = p.H / p.KV, g = h / G, kvd = p.KV * hd, c4 = hd / 4;
+    float *qs = ks + kScoreThreads * kKRow;
+    for (int i = tid; i < hd; i += kScoreThreads) qs[i] = p.q[(size_t)h * hd + i];
+    // stage the K rows of these positions (coalesced 16-byte loads)
+    for (int i = tid; i < cnt * c4; i += kScoreThreads) {
+        const int r = i / c4, c = i - r * c4;
+        const float4 v = __ldg((const float4 *)(p.k + (size_t)(p0 + r) * kvd + (size_t)g * hd) + c);
+        *(float4 *)(ks + r * kKRow + 4 * c) = v;
+    }
     __syncthreads();
-    const float4 *q4 = (const float4 *)qs;
-    for (int pp = tid; pp < n; pp += kAttnThreads) {
-        const float4 *kr = (const float4 *)(p.k + (size_t)pp * kvd + (size_t)g * hd);
+    if (tid < cnt) {
+        const float4 *kr = (const float4 *)(ks + tid * kKRow);
+        const float4 *q4 = (const float4 *)qs;
         float acc = 0.0f;
-        for (int c = 0; c < hd / 4; c++) {
-            const float4 kv = __ldg(kr + c), qv = q4[c];
+        for (int c = 0; c < c4; c++) {
+            const float4 kv = kr[c], qv = q4[c];
             acc = fa(acc, fm(qv.x, kv.x));
             acc = fa(acc, fm(qv.y, kv.y));
             acc = fa(acc, fm(qv.z, kv.z));
             acc = fa(acc, fm(qv.w, kv.w));
         }
-        sc[pp] = fm(acc, p.scale);
+        p.scores[(size_t)h * p.score_stride + p0 + tid] = fm(acc, p.scale);
     }
-    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant__ AttnParams p) {
+    extern __shared__ __align__(16) float so[];  // probs [max_pos] then V chunks [2][kVChunk][kOutDims]
+    __shared__ float red[kOutThreads / 32];
+    __shared__ float bcast;
+    griddep_launch_dependents();
+    griddep_wait();
+    const int h = blockIdx.x, dslice = blockIdx.y, tid = threadIdx.x;
+    const int n = *p.d_len + 1;
+    if (n > p.max_pos || n <= 0) return;  // k_attn_scores reported it
+    const int hd = p.hd, G = p.H / p.KV, g = h / G, kvd = p.KV * hd;
+    const int d0 = dslice * kOutDims;
+    if (d0 >= hd) return;
+    float *pr = so;
+    float *vs = so + ((p.max_pos + 3) & ~3);
+    const float *sc = p.scores + (size_t)h * p.score_stride;
     float m = -INFINITY;
-    for (int i = tid; i < n; i += kAttnThreads) m = fmaxf(m, sc[i]);
+    for (int i = tid; i < n; i += kOutThreads) {
+        const float v = sc[i];
+        pr[i] = v;
+        m = fmaxf(m, v);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((tid & 31) == 0) red[tid >> 5] = m;
     __syncthreads();
     if (tid == 0) {
         float mm = -INFINITY;
-        for (int w = 0; w < kAttnThreads / 32; w++) mm = fmaxf(mm, red[w]);
+        for (int w = 0; w < kOutThreads / 32; w++) mm = fmaxf(mm, red[w]);
         bcast = mm;
     }
     __syncthreads();
     const float mx = bcast;
+    __syncthreads();
     if (!isfinite(mx)) {
         const float u = __fdiv_rn(1.0f, (float)n);
-        for (int i = tid; i < n; i += kAttnThreads) sc[i] = u;
+        for (int i = tid; i < n; i += kOutThreads) pr[i] = u;
     } else {
-        for (int i = tid; i < n; i += kAttnThreads) sc[i] = expf_glibc(fs(sc[i], mx));
+        for (int i = tid; i < n; i += kOutThreads) pr[i] = expf_glibc(fs(pr[i], mx));
         __syncthreads();
         if (tid == 0) {
             float total = 0.0f;
             int i = 0;
             for (; i + 4 <= n; i += 4) {
-                const float4 v = *(const float4 *)(sc + i);
+                const float4 v = *(const float4 *)(pr + i);
                 total = fa(fa(fa(fa(total, v.x), v.y), v.z), v.w);
             }
-            for (; i < n; i++) total = fa(total, sc[i]);
+            for (; i < n; i++) total = fa(total, pr[i]);
             bcast = __fdiv_rn(1.0f, total);
         }
         __syncthreads();
         const float inv = bcast;
-        for (int i = tid; i < n; i += kAttnThreads) sc[i] = fm(sc[i], inv);
+        for (int i = tid; i < n; i += kOutThreads) pr[i] = fm(pr[i], inv);
     }
     __syncthreads();
-    for (int d = tid; d < hd; d += kAttnThreads) {
-        const float *vb = p.v + (size_t)g * hd + d;
-        float acc = 0.0f;
-        int pp = 0;
-        for (; pp + 4 <= n; pp += 4) {
-            const float v0 = __ldg(vb + (size_t)pp * kvd), v1 = __ldg(vb + (size_t)(pp + 1) * kvd);
-            const float v2 = __ldg(vb + (size_t)(pp + 2) * kvd), v3 = __ldg(vb + (size_t)(pp + 3) * kvd);
-            acc = fa(acc, fm(sc[pp], v0));
-            acc = fa(acc, fm(sc[pp + 1], v1));
-            acc = fa(acc, fm(sc[pp + 2], v2));
-            acc = fa(acc, fm(sc[pp + 3], v3));
+    // V: chunks of kVChunk positions x kOutDims dims, double-buffered; the
+    // first kOutDims threads run one sequential chain per dim
+    const float *vb = p.v + (size_t)g * hd + d0;
+    const int nchunks = (n + kVChunk - 1) / kVChunk;
+    auto stage = [&](int c, int buf) {
+        const int base = c * kVChunk, cnt = min(kVChunk, n - base);
+        float *dst = vs + buf * kVChunk * kOutDims;
+        for (int i = tid; i < cnt * (kOutDims / 4); i += kOutThreads) {
+            const int r = i / (kOutDims / 4), q = i - r * (kOutDims / 4);
+            *(float4 *)(dst + r * kOutDims + 4 * q) = __ldg((const float4 *)(vb + (size_t)(base + r) * kvd) + q);
         }
-        for (; pp < n; pp++) acc = fa(acc, fm(sc[pp], __ldg(vb + (size_t)pp * kvd)));
-        p.out[(size_t)h * hd + d] = acc;
+    };
+    stage(0, 0);
+    __syncthreads();
+    float acc = 0.0f;
+    for (int c = 0; c < nchunks; c++) {
+        if (c + 1 < nchunks) stage(c + 1, (c + 1) & 1);
+        if (tid < kOutDims && d0 + tid < hd) {
+            const float *src = vs + (c & 1) * kVChunk * kOutDims + tid;
+            const int base = c * kVChunk, cnt = min(kVChunk, n - base);
+            for (int r = 0; r < cnt; r++) acc = fa(acc, fm(pr[base + r], src[r * kOutDims]));
+        }
+        __syncthreads();
     }
+    if (tid < kOutDims && d0 + tid < hd) p.out[(size_t)h * hd + d0 + tid] = acc;
 }
 
 // ── embedding row (src/forward.rs:389-405): x = dequant(token_embd[tok]) ──
@@ -456,6 +615,8 @@ struct EmbedParams {
 };
 
 __global__ void k_embed(const __grid_constant__ EmbedParams p) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int pos = *p.d_len;
     if (pos >= p.max_pos) {
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(p.err, ERR_POSITION);
@@ -474,6 +635,7 @@ __global__ void k_embed(const __grid_constant__ EmbedParams p) {
 // ── end of step: append the chosen token, advance the position ──
 __global__ void k_commit(int *d_len, uint32_t *toks, const unsigned long long *argmax_key, int write_token,
                          int max_pos) {
+    griddep_wait();
     if (threadIdx.x || blockIdx.x) return;
     const int len = *d_len;
     if (write_token && argmax_key && len + 1 < max_pos) toks[len + 1] = argmax_index(*argmax_key);
