@@ -236,7 +236,18 @@ size_t out_smem(uint32_t max_pos) {
 }
 
 int set_kernel_smem_limits() {
-    CU(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    int dev = 0, optin = 0;
+    CU(cudaGetDevice(&dev));
+    CU(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    cudaFuncAttributes fa_{};
+    CU(cudaFuncGetAttributes(&fa_, k_matvec));
+    const int mv_max = optin - (int)fa_.sharedSizeBytes;
+    if ((size_t)mv_max < matvec_smem_bytes(14336, 1, 1)) {
+        set_error("device allows %d bytes of shared memory per block; the matvec needs %zu", mv_max,
+                  matvec_smem_bytes(14336, 1, 1));
+        return -1;
+    }
+    CU(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, mv_max));
     CU(cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     CU(cudaFuncSetAttribute(k_attn_out, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     return 0;
