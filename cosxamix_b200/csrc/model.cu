@@ -232,7 +232,7 @@ Seg make_seg(const DMat &A, int pairing, int epi, float *out) {
 
 size_t scores_smem(int hd) { return ((size_t)kScoreThreads * kKRow + (size_t)hd) * sizeof(float); }
 size_t out_smem(uint32_t max_pos) {
-    return ((size_t)((max_pos + 3) & ~3u) + 2 * kVChunk * kOutDims) * sizeof(float);
+    return ((size_t)((max_pos + 3) & ~3u) + kVRing * kVChunk * kOutDims) * sizeof(float);
 }
 
 int set_kernel_smem_limits() {
@@ -273,7 +273,7 @@ int launch_attention(cxm_model *m, cxm_cache *c, int layer) {
     a.KV = cfg.n_head_kv;
     a.hd = cfg.head_dim;
     a.max_pos = (int)c->max_tokens;
-    a.score_stride = cfg.ctx;
+    a.score_stride = (cfg.ctx + 3) & ~3;
     a.scale = 1.0f / sqrtf((float)cfg.head_dim);  // src/ops.rs:1287
     a.err = m->err;
     return launch_attention_on(m->stream, a);
@@ -569,7 +569,7 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
     // activations
     if (m->alloc(&m->x, cfg.dim) || m->alloc(&m->q, cfg.dim) || m->alloc(&m->att, cfg.dim) ||
         m->alloc(&m->h, std::max(cfg.ffn, 1)) || m->alloc(&m->logits, cfg.vocab) || m->alloc(&m->err, 1) ||
-        m->alloc(&m->argmax_key, 1) || m->alloc(&m->scores, (size_t)cfg.n_head * cfg.ctx))
+        m->alloc(&m->argmax_key, 1) || m->alloc(&m->scores, (size_t)cfg.n_head * ((cfg.ctx + 3) & ~3)))
         return -1;
     CU(cudaMemset(m->err, 0, sizeof(int)));
     if (set_kernel_smem_limits()) return -1;
@@ -952,7 +952,7 @@ extern "C" int cxm_debug_attention(const float *q, const float *k, const float *
     }
     const size_t kvd = (size_t)heads_kv * hd;
     DevBuf dq, dk, dv, dout, dlen, derr, dsc;
-    CU(cudaMalloc(&dsc.p, (size_t)heads * total * 4));
+    CU(cudaMalloc(&dsc.p, (size_t)heads * ((total + 3) & ~3u) * 4));
     CU(cudaMalloc(&dq.p, (size_t)heads * hd * 4));
     CU(cudaMalloc(&dk.p, total * kvd * 4));
     CU(cudaMalloc(&dv.p, total * kvd * 4));
@@ -975,7 +975,7 @@ extern "C" int cxm_debug_attention(const float *q, const float *k, const float *
     a.KV = (int)heads_kv;
     a.hd = (int)hd;
     a.max_pos = (int)total;
-    a.score_stride = (int)total;
+    a.score_stride = (int)((total + 3) & ~3u);
     a.scores = (float *)dsc.p;
     a.scale = 1.0f / sqrtf((float)hd);
     a.err = (int *)derr.p;

@@ -109,10 +109,22 @@ __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe
     const int K = p.K;
     double scale = 0.0;
     if (p.prologue == PRO_NORM) {
+        // sum of squares: 16-byte loads, 4 in flight per thread
+        const float4 *in4 = (const float4 *)p.in;
+        const int K4 = K >> 2;
         double acc = 0.0;
-        for (int i = tid; i < K; i += nt) {
-            const double v = (double)p.in[i];
-            acc = __dadd_rn(acc, __dmul_rn(v, v));
+        for (int i0 = tid; i0 < K4; i0 += 4 * nt) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) v[u] = (i0 + u * nt < K4) ? in4[i0 + u * nt] : make_float4(0, 0, 0, 0);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const double a = v[u].x, b = v[u].y, c = v[u].z, d = v[u].w;
+                acc = __dadd_rn(acc, __dmul_rn(a, a));
+                acc = __dadd_rn(acc, __dmul_rn(b, b));
+                acc = __dadd_rn(acc, __dmul_rn(c, c));
+                acc = __dadd_rn(acc, __dmul_rn(d, d));
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
@@ -126,37 +138,51 @@ __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe
         consumers_sync();
         scale = *scale_s;
     }
-    for (int c = warp; c < (K >> 5); c += kCW) {
-        const int i = c * 32 + lane;
-        float v = p.in[i];
-        if (p.prologue == PRO_NORM) v = __fmul_rn(__double2float_rn(__dmul_rn((double)v, scale)), p.norm_w[i]);
-        const float av = fabsf(v);
-        if (p.need32) {
-            float amax = av;
+    // quantize: a warp per 32-value chunk, 8 chunks' loads in flight per lane
+    const int nchunk = K >> 5;
+    for (int c0 = warp; c0 < nchunk; c0 += 8 * kCW) {
+        float vals[8], ws[8];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-            const int qv = (int)roundf(__fmul_rn(v, inv));
-            xq32[i] = (int8_t)qv;
-            const int s = warp_sum_i((int)(int8_t)qv);
-            if (lane == 0) {
-                xe32[c] = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f;
-                xs32[c] = (float)s;
-            }
+        for (int u = 0; u < 8; u++) {
+            const int c = c0 + u * kCW;
+            vals[u] = c < nchunk ? p.in[c * 32 + lane] : 0.0f;
+            ws[u] = (c < nchunk && p.prologue == PRO_NORM) ? p.norm_w[c * 32 + lane] : 0.0f;
         }
-        if (p.need16) {
-            float amax = av;
 #pragma unroll
-            for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-            const int qv = (int)roundf(__fmul_rn(v, inv));
-            xq16[i] = (int8_t)qv;
-            int s = (int)(int8_t)qv;
+        for (int u = 0; u < 8; u++) {
+            const int c = c0 + u * kCW;
+            if (c >= nchunk) break;
+            const int i = c * 32 + lane;
+            float v = vals[u];
+            if (p.prologue == PRO_NORM) v = __fmul_rn(__double2float_rn(__dmul_rn((double)v, scale)), ws[u]);
+            const float av = fabsf(v);
+            if (p.need32) {
+                float amax = av;
 #pragma unroll
-            for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            if ((lane & 15) == 0) {
-                xe16[2 * c + (lane >> 4)] = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f;
-                xs16[2 * c + (lane >> 4)] = (float)s;
+                for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+                const int qv = (int)roundf(__fmul_rn(v, inv));
+                xq32[i] = (int8_t)qv;
+                const int s = warp_sum_i((int)(int8_t)qv);
+                if (lane == 0) {
+                    xe32[c] = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f;
+                    xs32[c] = (float)s;
+                }
+            }
+            if (p.need16) {
+                float amax = av;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+                const int qv = (int)roundf(__fmul_rn(v, inv));
+                xq16[i] = (int8_t)qv;
+                int s = (int)(int8_t)qv;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                if ((lane & 15) == 0) {
+                    xe16[2 * c + (lane >> 4)] = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f;
+                    xs16[2 * c + (lane >> 4)] = (float)s;
+                }
             }
         }
     }
@@ -482,6 +508,7 @@ constexpr int kKRow = 132;           // smem row stride (floats) of staged K row
 constexpr int kOutThreads = 128;
 constexpr int kOutDims = 16;         // head dims per output CTA
 constexpr int kVChunk = 64;          // positions per staged V chunk
+constexpr int kVRing = 8;            // V chunks in flight
 
 __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_constant__ AttnParams p) {
     extern __shared__ __align__(16) float ks[];  // [kScoreThreads][kKRow] then q [hd]
@@ -498,13 +525,14 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
     const int cnt = min(kScoreThreads, n - p0);
     const int hd = p.hd, G = p.H / p.KV, g = h / G, kvd = p.KV * hd, c4 = hd / 4;
     float *qs = ks + kScoreThreads * kKRow;
-    for (int i = tid; i < hd; i += kScoreThreads) qs[i] = p.q[(size_t)h * hd + i];
-    // stage the K rows of these positions (coalesced 16-byte loads)
+    // stage q and the K rows of these positions: all 16-byte copies in flight
+    for (int i = tid; i < c4; i += kScoreThreads) cp_async16(qs + 4 * i, p.q + (size_t)h * hd + 4 * i);
     for (int i = tid; i < cnt * c4; i += kScoreThreads) {
         const int r = i / c4, c = i - r * c4;
-        const float4 v = __ldg((const float4 *)(p.k + (size_t)(p0 + r) * kvd + (size_t)g * hd) + c);
-        *(float4 *)(ks + r * kKRow + 4 * c) = v;
+        cp_async16(ks + r * kKRow + 4 * c, p.k + (size_t)(p0 + r) * kvd + (size_t)g * hd + 4 * c);
     }
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
     if (tid < cnt) {
         const float4 *kr = (const float4 *)(ks + tid * kKRow);
@@ -522,7 +550,8 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
 }
 
 __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant__ AttnParams p) {
-    extern __shared__ __align__(16) float so[];  // probs [max_pos] then V chunks [2][kVChunk][kOutDims]
+    // smem: probs [max_pos rounded to 4] then a ring of kVRing V chunks [kVChunk][kOutDims]
+    extern __shared__ __align__(16) float so[];
     __shared__ float red[kOutThreads / 32];
     __shared__ float bcast;
     griddep_launch_dependents();
@@ -536,12 +565,29 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
     float *pr = so;
     float *vs = so + ((p.max_pos + 3) & ~3);
     const float *sc = p.scores + (size_t)h * p.score_stride;
-    float m = -INFINITY;
-    for (int i = tid; i < n; i += kOutThreads) {
-        const float v = sc[i];
-        pr[i] = v;
-        m = fmaxf(m, v);
+    const float *vb = p.v + (size_t)g * hd + d0;
+    const int nchunks = (n + kVChunk - 1) / kVChunk;
+    auto stage = [&](int c) {
+        if (c >= nchunks) return;
+        const int base = c * kVChunk, cnt = min(kVChunk, n - base);
+        float *dst = vs + (c % kVRing) * kVChunk * kOutDims;
+        for (int i = tid; i < cnt * (kOutDims / 4); i += kOutThreads) {
+            const int r = i / (kOutDims / 4), q = i - r * (kOutDims / 4);
+            cp_async16(dst + r * kOutDims + 4 * q, vb + (size_t)(base + r) * kvd + 4 * q);
+        }
+    };
+    // the scores and the first V chunks all in flight at once; the softmax
+    // runs while V streams in
+    for (int i = tid; i < (n + 3) / 4; i += kOutThreads) cp_async16(pr + 4 * i, sc + 4 * i);
+    cp_async_commit();
+    for (int c = 0; c < kVRing - 1; c++) {
+        stage(c);
+        cp_async_commit();
     }
+    cp_async_wait<kVRing - 1>();
+    __syncthreads();
+    float m = -INFINITY;
+    for (int i = tid; i < n; i += kOutThreads) m = fmaxf(m, pr[i]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((tid & 31) == 0) red[tid >> 5] = m;
@@ -575,25 +621,15 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
         for (int i = tid; i < n; i += kOutThreads) pr[i] = fm(pr[i], inv);
     }
     __syncthreads();
-    // V: chunks of kVChunk positions x kOutDims dims, double-buffered; the
-    // first kOutDims threads run one sequential chain per dim
-    const float *vb = p.v + (size_t)g * hd + d0;
-    const int nchunks = (n + kVChunk - 1) / kVChunk;
-    auto stage = [&](int c, int buf) {
-        const int base = c * kVChunk, cnt = min(kVChunk, n - base);
-        float *dst = vs + buf * kVChunk * kOutDims;
-        for (int i = tid; i < cnt * (kOutDims / 4); i += kOutThreads) {
-            const int r = i / (kOutDims / 4), q = i - r * (kOutDims / 4);
-            *(float4 *)(dst + r * kOutDims + 4 * q) = __ldg((const float4 *)(vb + (size_t)(base + r) * kvd) + q);
-        }
-    };
-    stage(0, 0);
-    __syncthreads();
+    // out[d] = Σ_p prob_p·v_p[d], one sequential chain per dim
     float acc = 0.0f;
     for (int c = 0; c < nchunks; c++) {
-        if (c + 1 < nchunks) stage(c + 1, (c + 1) & 1);
+        stage(c + kVRing - 1);
+        cp_async_commit();
+        cp_async_wait<kVRing - 1>();
+        __syncthreads();
         if (tid < kOutDims && d0 + tid < hd) {
-            const float *src = vs + (c & 1) * kVChunk * kOutDims + tid;
+            const float *src = vs + (c % kVRing) * kVChunk * kOutDims + tid;
             const int base = c * kVChunk, cnt = min(kVChunk, n - base);
             for (int r = 0; r < cnt; r++) acc = fa(acc, fm(pr[base + r], src[r * kOutDims]));
         }
