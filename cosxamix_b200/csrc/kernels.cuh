@@ -291,6 +291,143 @@ __device__ __forceinline__ int term_sub(int type, int q, int k) {
     return 4 * q + k;
 }
 
+// ── a whole super-block from shared memory ──
+// The streaming matvec gives each lane one super-block of one row: it forms
+// all of the block's sub-block terms t[0..nsub) in sub-block order. `xq` is
+// the activation with each 256-value block padded to kXqStride bytes (bank
+// spread); `xe`/`xs` hold 8 (sub-blocks of 32) or 16 (of 16) floats per block.
+constexpr int kXqStride = 272;
+
+struct XB {  // one block of the quantized activation
+    const int8_t *q;      // 256 values
+    const float *e, *s;   // its scales and sums, nsub each
+};
+
+__device__ __forceinline__ int dot16(uint4 w, int4 a) {
+    int s = __dp4a((int)w.x, a.x, 0);
+    s = __dp4a((int)w.y, a.y, s);
+    s = __dp4a((int)w.z, a.z, s);
+    return __dp4a((int)w.w, a.w, s);
+}
+__device__ __forceinline__ uint4 and4(uint4 v, uint32_t m) { return make_uint4(v.x & m, v.y & m, v.z & m, v.w & m); }
+__device__ __forceinline__ uint4 shr4(uint4 v, int n) { return make_uint4(v.x >> n, v.y >> n, v.z >> n, v.w >> n); }
+__device__ __forceinline__ uint4 or4(uint4 a, uint4 b) { return make_uint4(a.x | b.x, a.y | b.y, a.z | b.z, a.w | b.w); }
+__device__ __forceinline__ uint4 shl4(uint4 v, int n) { return make_uint4(v.x << n, v.y << n, v.z << n, v.w << n); }
+
+// Q4_K / Q5_K: 8 terms (src/kernels/scalar.rs:132-217)
+template <bool Q5>
+__device__ __forceinline__ void block_k4(const uint8_t *pa, const XB &x, float *t) {
+    const uint4 hdr = *(const uint4 *)pa;
+    const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
+    const int4 *xp = (const int4 *)x.q;
+    const uint8_t *qs = pa + (Q5 ? 48 : 16);
+    uint4 qh0 = make_uint4(0, 0, 0, 0), qh1 = qh0;
+    if (Q5) {
+        qh0 = *(const uint4 *)(pa + 16);
+        qh1 = *(const uint4 *)(pa + 32);
+    }
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+        const uint4 wa = *(const uint4 *)(qs + 32 * p), wb = *(const uint4 *)(qs + 32 * p + 16);
+        uint4 la = and4(wa, 0x0F0F0F0Fu), lb = and4(wb, 0x0F0F0F0Fu);
+        uint4 ha = and4(shr4(wa, 4), 0x0F0F0F0Fu), hb = and4(shr4(wb, 4), 0x0F0F0F0Fu);
+        if (Q5) {
+            la = or4(la, shl4(and4(shr4(qh0, 2 * p), 0x01010101u), 4));
+            lb = or4(lb, shl4(and4(shr4(qh1, 2 * p), 0x01010101u), 4));
+            ha = or4(ha, shl4(and4(shr4(qh0, 2 * p + 1), 0x01010101u), 4));
+            hb = or4(hb, shl4(and4(shr4(qh1, 2 * p + 1), 0x01010101u), 4));
+        }
+        const int s0 = dot16(la, xp[4 * p]) + dot16(lb, xp[4 * p + 1]);
+        const int s1 = dot16(ha, xp[4 * p + 2]) + dot16(hb, xp[4 * p + 3]);
+        int sc0, m0, sc1, m1;
+        scale_min_k4(2 * p, hdr.y, hdr.z, hdr.w, sc0, m0);
+        scale_min_k4(2 * p + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
+        const int j0 = 2 * p;
+        t[j0] = fm(x.e[j0], fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), x.s[j0])));
+        t[j0 + 1] = fm(x.e[j0 + 1], fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), x.s[j0 + 1])));
+    }
+}
+
+// Q6_K: 16 terms (src/kernels/scalar.rs:294-324)
+__device__ __forceinline__ void block_q6k(const uint8_t *pa, const uint8_t *ps, const uint8_t *pd, const XB &x,
+                                          float *t) {
+    const float d = h2f(*(const unsigned short *)pd);
+    const uint4 scv = *(const uint4 *)ps;
+    const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+    const int4 *xp = (const int4 *)x.q;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+#pragma unroll
+        for (int md = 0; md < 2; md++) {
+            // 16 positions: ql columns 0 (groups gi 0, 2) and 1 (gi 1, 3), qh bits
+            const uint4 q0 = *(const uint4 *)(pa + 64 * h + 16 * md), q1 = *(const uint4 *)(pa + 64 * h + 32 + 16 * md);
+            const uint4 qh = *(const uint4 *)(pa + 128 + 32 * h + 16 * md);
+#pragma unroll
+            for (int gi = 0; gi < 4; gi++) {
+                const uint4 ql = (gi & 1) ? q1 : q0;
+                const uint4 nib = (gi < 2) ? and4(ql, 0x0F0F0F0Fu) : and4(shr4(ql, 4), 0x0F0F0F0Fu);
+                const uint4 v = or4(nib, shl4(and4(shr4(qh, 2 * gi), 0x03030303u), 4));
+                const int g = 4 * h + gi, si = 2 * g + md;
+                const int s = dot16(v, xp[si]);
+                const int sc = (int)(int8_t)((scw[si >> 2] >> (8 * (si & 3))) & 0xFF);
+                t[si] = fm(fm(x.e[si], fm(d, (float)sc)), fs((float)s, fm(32.0f, x.s[si])));
+            }
+        }
+    }
+}
+
+// Q3_K: 16 terms (src/kernels/scalar.rs:236-275)
+__device__ __forceinline__ void block_q3k(const uint8_t *pa, const uint8_t *ps, const uint8_t *pd, const XB &x,
+                                          float *t) {
+    const float d = h2f(*(const unsigned short *)pd);
+    const uint32_t a0 = *(const uint32_t *)ps, a1 = *(const uint32_t *)(ps + 4), tt = *(const uint32_t *)(ps + 8);
+    const int4 *xp = (const int4 *)x.q;
+#pragma unroll
+    for (int md = 0; md < 2; md++) {
+        const uint4 hm = *(const uint4 *)(pa + 16 * md);
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint4 qs = *(const uint4 *)(pa + 32 + 32 * h + 16 * md);
+#pragma unroll
+            for (int r4 = 0; r4 < 4; r4++) {
+                const int g = 4 * h + r4, si = 2 * g + md, wi = si >> 2;
+                const uint4 v = or4(and4(shr4(qs, 2 * r4), 0x03030303u), shl4(and4(shr4(hm, g), 0x01010101u), 2));
+                const int s = dot16(v, xp[si]);
+                const uint32_t aa = (wi & 1) ? a1 : a0;
+                const uint32_t wq = ((aa >> ((wi >> 1) * 4)) & 0x0F0F0F0Fu) | (((tt >> (2 * wi)) & 0x03030303u) << 4);
+                const int sc = (int)((wq >> (8 * (si & 3))) & 0xFF);
+                t[si] = fm(fm(x.e[si], fm(d, fs((float)sc, 32.0f))), fs((float)s, fm(4.0f, x.s[si])));
+            }
+        }
+    }
+}
+
+// Q2_K: 16 terms (src/kernels/q2k.rs:41-69)
+__device__ __forceinline__ void block_q2k(const uint8_t *pa, const uint8_t *ps, const uint8_t *pd, const XB &x,
+                                          float *t) {
+    const uint32_t dd = *(const uint32_t *)pd;
+    const float d = h2f(dd), dm = h2f(dd >> 16);
+    const uint4 scv = *(const uint4 *)ps;
+    const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+    const int4 *xp = (const int4 *)x.q;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+#pragma unroll
+        for (int md = 0; md < 2; md++) {
+            const uint4 qs = *(const uint4 *)(pa + 32 * h + 16 * md);
+#pragma unroll
+            for (int r4 = 0; r4 < 4; r4++) {
+                const int g = 4 * h + r4, si = 2 * g + md;
+                const uint4 v = and4(shr4(qs, 2 * r4), 0x03030303u);
+                const int s = dot16(v, xp[si]);
+                const int sc = (int)((scw[si >> 2] >> (8 * (si & 3))) & 0xFF);
+                const float ev = fm(d, (float)(sc & 0xF)), mv = fm(dm, (float)(sc >> 4));
+                t[si] = fm(x.e[si], fs(fm(ev, (float)s), fm(mv, x.s[si])));
+            }
+        }
+    }
+}
+
 // ── dequantize one value from the planes (src/quant.rs:582-679) ──
 __device__ inline float dequant_value(const DMat &W, int row, int idx) {
     const int b = idx >> 8, r = idx & 255;

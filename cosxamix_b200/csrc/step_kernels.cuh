@@ -64,22 +64,20 @@ constexpr int kMvThreads = (kCW + 1) * 32;      // + one producer warp
 constexpr int kStages = 3;                      // smem ring depth
 constexpr int kSlots = 32;                      // row slots per stage (16 row pairs)
 constexpr int kChunk = 8;                       // super-blocks per stage (2048 values)
-constexpr int kSlotA = kChunk * 192, kSlotS = kChunk * 16, kSlotD = kChunk * 4;
+// slot strides padded so the 8 lanes of a shared-memory phase hit distinct banks
+constexpr int kSlotA = kChunk * 192 + 32, kSlotS = kChunk * 16 + 32, kSlotD = kChunk * 4;
 constexpr int kStageA = kSlots * kSlotA, kStageS = kSlots * kSlotS, kStageD = kSlots * kSlotD;
-constexpr int kStageBytes = kStageA + kStageS + kStageD;  // 54 KB
-constexpr int kTermStride = 132;                // floats per slot of a warp's term tile
+constexpr int kStageBytes = kStageA + kStageS + kStageD;  // 55 KB
 constexpr int kSlotsPerWarp = kSlots / kCW;     // 4
-constexpr int kTermFloats = kSlotsPerWarp * kTermStride;
 
 __host__ __device__ inline size_t matvec_act_bytes(int K, int need16, int need32) {
     size_t b = 0;
-    if (need16) b += (size_t)K + (size_t)K / 16 * 8;
-    if (need32) b += (size_t)K + (size_t)K / 32 * 8;
+    if (need16) b += (size_t)(K / 256) * kXqStride + (size_t)K / 16 * 8;
+    if (need32) b += (size_t)(K / 256) * kXqStride + (size_t)K / 32 * 8;
     return (b + 15) & ~(size_t)15;
 }
 __host__ __device__ inline size_t matvec_smem_bytes(int K, int need16, int need32) {
-    return (size_t)kStages * kStageBytes + (size_t)kCW * kTermFloats * 4 + kSlots * 4 +
-           matvec_act_bytes(K, need16, need32) + 128;
+    return (size_t)kStages * kStageBytes + matvec_act_bytes(K, need16, need32) + 128;
 }
 
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kCW * 32) : "memory"); }
@@ -162,7 +160,7 @@ __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe
                 for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
                 const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
                 const int qv = (int)roundf(__fmul_rn(v, inv));
-                xq32[i] = (int8_t)qv;
+                xq32[(i >> 8) * kXqStride + (i & 255)] = (int8_t)qv;
                 const int s = warp_sum_i((int)(int8_t)qv);
                 if (lane == 0) {
                     xe32[c] = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f;
@@ -175,7 +173,7 @@ __device__ void prologue_quantize(const MatvecParams &p, int8_t *xq16, float *xe
                 for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
                 const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
                 const int qv = (int)roundf(__fmul_rn(v, inv));
-                xq16[i] = (int8_t)qv;
+                xq16[(i >> 8) * kXqStride + (i & 255)] = (int8_t)qv;
                 int s = (int)(int8_t)qv;
 #pragma unroll
                 for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -296,19 +294,19 @@ __device__ void unit_epilogue(const MatvecParams &p, const Seg &g, int r0, int r
 // k-quant matvec, several matrices per launch (q|k|v, gate|up), activation
 // quantization fused in front and the consumer fused behind. Persistent: one
 // CTA per SM. A producer warp streams each stage's weight planes with bulk
-// copies (the TMA unit) into a 3-deep shared-memory ring; 8 consumer warps
-// turn a stage into sub-block terms (a lane per quarter super-block) and one
-// lane per row adds them, in sub-block order, onto the row's running total.
+// copies (the TMA unit) into a 3-deep shared-memory ring; in the 8 consumer
+// warps a lane takes one super-block of one row (lane = 4*block + slot) and
+// forms all its sub-block terms, then the terms of each row are added in
+// sub-block order onto the row's running total, handed from block to block
+// by warp shuffles.
 __global__ void __launch_bounds__(kMvThreads, 1) k_matvec(const __grid_constant__ MatvecParams p) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
     unsigned char *stages = smem;
-    float *tiles = (float *)(smem + (size_t)kStages * kStageBytes);
-    float *ybuf = tiles + kCW * kTermFloats;
-    int8_t *xq16 = (int8_t *)(ybuf + kSlots);
-    const int K = p.K;
-    int8_t *xq32 = xq16 + (p.need16 ? K : 0);
-    float *xe16 = (float *)(xq32 + (p.need32 ? K : 0));
+    const int K = p.K, nblk = K / 256, nkc = (nblk + kChunk - 1) / kChunk;
+    int8_t *xq16 = (int8_t *)(smem + (size_t)kStages * kStageBytes);
+    int8_t *xq32 = xq16 + (p.need16 ? nblk * kXqStride : 0);
+    float *xe16 = (float *)(xq32 + (p.need32 ? nblk * kXqStride : 0));
     float *xs16 = xe16 + (p.need16 ? K / 16 : 0);
     float *xe32 = xs16 + (p.need16 ? K / 16 : 0);
     float *xs32 = xe32 + (p.need32 ? K / 32 : 0);
@@ -332,7 +330,6 @@ __global__ void __launch_bounds__(kMvThreads, 1) k_matvec(const __grid_constant_
 
     const int U = p.total_units, G = gridDim.x;
     const int ub = (int)(((long long)blockIdx.x * U) / G), ue = (int)(((long long)(blockIdx.x + 1) * U) / G);
-    const int nblk = K / 256, nkc = (nblk + kChunk - 1) / kChunk;
 
     if (warp == kCW) {
         // ── producer: weights never depend on the previous kernel, so they
@@ -353,7 +350,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) k_matvec(const __grid_constant_
                     break;
                 }
                 const int b0 = kc * kChunk, nb = min(kChunk, nblk - b0);
-                // bytes of this stage, each lane one slot
+                // each lane streams one slot's row chunk
                 const DMat *M = nullptr;
                 int row = 0;
                 const bool valid = slot_row(p, g, lane, M, row);
@@ -381,11 +378,9 @@ __global__ void __launch_bounds__(kMvThreads, 1) k_matvec(const __grid_constant_
                 }
             }
         }
-        if (!ok) {
-            if (lane == 0) {
-                abort_flag = 1;
-                atomicOr(p.err, ERR_TIMEOUT);
-            }
+        if (!ok && lane == 0) {
+            abort_flag = 1;
+            atomicOr(p.err, ERR_TIMEOUT);
         }
         // drain: the last stages issued must have landed before the CTA exits
         if (lane == 0) {
@@ -399,26 +394,23 @@ __global__ void __launch_bounds__(kMvThreads, 1) k_matvec(const __grid_constant_
     // ── consumers ──
     griddep_wait();  // activations, caches and the residual come from earlier kernels
     prologue_quantize(p, xq16, xe16, xs16, xq32, xe32, xs32, red, &scale_s);
-    const XQ x16{xq16, xe16, xs16}, x32{xq32, xe32, xs32};
     const int pos = p.d_len ? *p.d_len : 0;
-    float *tile = tiles + warp * kTermFloats;
-    const int slot0 = warp * kSlotsPerWarp;  // this warp's slots: row pairs 2*warp and 2*warp+1
+    const int bl = lane >> 2, sl = lane & 3, slot = warp * kSlotsPerWarp + sl;
     unsigned long long best = 0ull;
     uint32_t it = 0;
     int gu = ub;
     Grp g;
     bool ok = true;
     while (ok && grp_next(p, gu, ue, g)) {
-        // lane r < nvalid owns the running total of slot slot0 + r
-        const DMat *Ms[kSlotsPerWarp];
-        int rows[kSlotsPerWarp];
-        int nvalid = 0;
-        for (int r = 0; r < kSlotsPerWarp; r++)
-            if (slot_row(p, g, slot0 + r, Ms[r], rows[r])) nvalid = r + 1;
-        float total = 0.0f;
-        int my_type = 0;
-        for (int r = 0; r < nvalid; r++)
-            if (lane == r) my_type = Ms[r]->type;
+        const DMat *M = nullptr;
+        int row = 0;
+        const bool valid = slot_row(p, g, slot, M, row);
+        const int T = valid ? M->type : 0;
+        const bool s32 = (T == 12 || T == 13);
+        const int nsub = s32 ? 8 : 16;
+        const int8_t *xq = s32 ? xq32 : xq16;
+        const float *xe = s32 ? xe32 : xe16, *xs = s32 ? xs32 : xs16;
+        float acc = 0.0f;
         for (int kc = 0; kc < nkc; kc++, it++) {
             const int s = it % kStages;
             const uint32_t ph = (it / kStages) & 1;
@@ -428,41 +420,45 @@ __global__ void __launch_bounds__(kMvThreads, 1) k_matvec(const __grid_constant_
                 break;
             }
             const int b0 = kc * kChunk, nb = min(kChunk, nblk - b0);
-            const unsigned char *st = stages + (size_t)s * kStageBytes;
-            for (int r = 0; r < nvalid; r++) {  // warp-uniform loop over the slots
-                const int slot = slot0 + r, T = Ms[r]->type;
-                if (lane < nb * 4) {
-                    const uint8_t *sa = st + slot * kSlotA, *ss = st + kStageA + slot * kSlotS,
-                                  *sd = st + kStageA + kStageS + slot * kSlotD;
-                    const XQ &x = (T == 12 || T == 13) ? x32 : x16;
-                    float *tr = tile + r * kTermStride;
-                    switch (T) {
-                    case 12: chunk_terms<12>(sa, ss, sd, b0, lane, x, tr); break;
-                    case 13: chunk_terms<13>(sa, ss, sd, b0, lane, x, tr); break;
-                    case 14: chunk_terms<14>(sa, ss, sd, b0, lane, x, tr); break;
-                    case 11: chunk_terms<11>(sa, ss, sd, b0, lane, x, tr); break;
-                    default: chunk_terms<10>(sa, ss, sd, b0, lane, x, tr); break;
-                    }
+            float t[16];
+            if (valid && bl < nb) {
+                const unsigned char *st = stages + (size_t)s * kStageBytes;
+                const uint8_t *pa = st + slot * kSlotA + bl * plane_a_bytes(T);
+                const uint8_t *ps = st + kStageA + slot * kSlotS + bl * plane_s_bytes(T);
+                const uint8_t *pd = st + kStageA + kStageS + slot * kSlotD + bl * plane_d_bytes(T);
+                const int b = b0 + bl;
+                const XB xb{xq + b * kXqStride, xe + b * nsub, xs + b * nsub};
+                switch (T) {
+                case 12: block_k4<false>(pa, xb, t); break;
+                case 13: block_k4<true>(pa, xb, t); break;
+                case 14: block_q6k(pa, ps, pd, xb, t); break;
+                case 11: block_q3k(pa, ps, pd, xb, t); break;
+                default: block_q2k(pa, ps, pd, xb, t); break;
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);  // the stage's weights are consumed
-            if (lane < nvalid) {
-                const int nterms = nb * subs_per_block(my_type);
-                const float4 *src = (const float4 *)(tile + lane * kTermStride);
-                for (int c = 0; c < (nterms >> 2); c++) {
-                    const float4 v = src[c];
-                    total = fa(fa(fa(fa(total, v.x), v.y), v.z), v.w);
+            // the row's running total visits the blocks in order
+            float run = acc;
+            for (int j = 0; j < nb; j++) {
+                float v = run;
+                if (valid && bl == j) {
+#pragma unroll
+                    for (int k = 0; k < 16; k++)
+                        if (k < nsub) v = fa(v, t[k]);
                 }
+                run = __shfl_sync(0xffffffffu, v, j * 4 + sl);
             }
-            __syncwarp();
+            acc = run;
         }
         if (!ok) break;
-        // lanes 0,1 hold row pair 2*warp; lanes 2,3 row pair 2*warp+1
-        const float other = __shfl_down_sync(0xffffffffu, total, 1);
-        if (!(lane & 1) && lane + 1 < nvalid) {
-            const Seg &sg = p.seg[g.seg];
-            unit_epilogue(p, sg, rows[lane], rows[lane + 1], total, other, pos, best);
+        // slots sl = 0,1 hold row pair 2*warp; sl = 2,3 row pair 2*warp+1
+        const float other = __shfl_down_sync(0xffffffffu, acc, 1);
+        if (bl == 0 && !(sl & 1)) {
+            const DMat *M1 = nullptr;
+            int row1 = 0;
+            if (valid && slot_row(p, g, slot + 1, M1, row1))
+                unit_epilogue(p, p.seg[g.seg], row, row1, acc, other, pos, best);
         }
     }
     if (!ok && lane == 0) {
