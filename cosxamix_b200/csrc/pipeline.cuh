@@ -24,14 +24,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// One bounded try: the thread is suspended until the phase completes or the
+// hint (in ns) runs out, instead of spinning on the barrier word the bulk
+// copies are completing.
+constexpr uint32_t kSuspendHintNs = 20000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendHintNs)
         : "memory");
     return ok != 0;
 }
@@ -46,13 +51,14 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
-// Bounded wait on a phase of `bar`. Gives up after ~`limit` polls or as soon
-// as another role of the CTA raised `abort`.
+// Bounded wait on a phase of `bar`: at most `limit` tries of up to
+// kSuspendHintNs each (2^16 x 20 us ~ 1.3 s), or until another role of the
+// CTA raised `abort`.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                                  uint32_t limit = (1u << 22)) {
+                                                  uint32_t limit = (1u << 16)) {
     for (uint32_t i = 0; i < limit; i++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 255u && *abort) return false;
+        if (*abort) return false;
     }
     return false;
 }

@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) k_matvec(const __grid_constant_
         if (lane == 0) {
             const uint32_t last = it;
             for (uint32_t j = last > (uint32_t)kStages ? last - kStages : 0; j < last; j++)
-                mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1, &abort_flag, 1u << 20);
+                mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1, &abort_flag, 1u << 14);
         }
         return;
     }
