@@ -1011,7 +1011,9 @@ extern "C" int cxm_debug_expf(const float *x, float *y, uint64_t n) {
 
 // ── measurement hooks ──
 
-extern "C" int cxm_step_launches(const cxm_model *m) { return m ? 3 + 5 * m->cfg.n_layer : 0; }
+// embed, per layer (q|k|v, attention scores, attention output, o, gate|up,
+// down), output projection, commit
+extern "C" int cxm_step_launches(const cxm_model *m) { return m ? 3 + 6 * m->cfg.n_layer : 0; }
 
 extern "C" int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, float *ms_total) {
     if (!m || !c || !ms_total || c->m != m) {
@@ -1065,18 +1067,42 @@ extern "C" int cxm_bench_matvec(cxm_model *m, uint32_t reps, float *ms_per_launc
     };
     for (int i = 0; i < 3; i++)
         if (launch(i)) return -1;
-    cudaEvent_t e0, e1;
-    CU(cudaEventCreate(&e0));
-    CU(cudaEventCreate(&e1));
-    CU(cudaEventRecord(e0, m->stream));
-    for (uint32_t i = 0; i < reps; i++)
-        if (launch((int)i)) return -1;
-    CU(cudaEventRecord(e1, m->stream));
-    CU(cudaEventSynchronize(e1));
+    // the launches are captured into one graph, as the decode step runs, so
+    // host launch overhead is not part of the device time
+    cudaGraph_t graph = nullptr;
+    CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int bad = 0;
+    for (uint32_t i = 0; i < reps && !bad; i++) bad = launch((int)i);
+    const cudaError_t ce = cudaStreamEndCapture(m->stream, &graph);
+    if (bad || ce != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        if (!bad) set_error("graph capture failed: %s", cudaGetErrorString(ce));
+        return -1;
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) {
+        set_error("graph instantiate failed: %s", cudaGetErrorString(ie));
+        return -1;
+    }
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
     float ms = 0;
-    CU(cudaEventElapsedTime(&ms, e0, e1));
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
+    cudaError_t re = cudaGraphLaunch(exec, m->stream);  // warm-up replay
+    if (re == cudaSuccess) re = cudaEventCreate(&e0);
+    if (re == cudaSuccess) re = cudaEventCreate(&e1);
+    if (re == cudaSuccess) re = cudaEventRecord(e0, m->stream);
+    if (re == cudaSuccess) re = cudaGraphLaunch(exec, m->stream);
+    if (re == cudaSuccess) re = cudaEventRecord(e1, m->stream);
+    if (re == cudaSuccess) re = cudaEventSynchronize(e1);
+    if (re == cudaSuccess) re = cudaEventElapsedTime(&ms, e0, e1);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    cudaGraphExecDestroy(exec);
+    if (re != cudaSuccess) {
+        set_error("matvec timing failed: %s", cudaGetErrorString(re));
+        return -1;
+    }
     *ms_per_launch = ms / (float)reps;
     const Layer &L = m->layers[0];
     *bytes_per_launch = (uint64_t)L.gate.rows * (uint64_t)(L.gate.K / 256) * (uint64_t)bytes_per_block(L.gate.type) +
