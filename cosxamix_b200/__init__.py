@@ -71,6 +71,7 @@ def lib() -> C.CDLL:
             "cxm_debug_matvec": (C.c_int, [C.c_int, P, C.c_uint32, C.c_uint32, P, P]),
             "cxm_debug_attention": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P]),
             "cxm_debug_expf": (C.c_int, [P, P, C.c_uint64]),
+            "cxm_attention_noalloc": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P, P]),
             "cxm_bench_decode": (C.c_int, [P, P, C.c_uint32, C.POINTER(C.c_float)]),
             "cxm_bench_matvec": (C.c_int, [P, C.c_uint32, C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
             "cxm_step_launches": (C.c_int, [P]),
@@ -309,3 +310,12 @@ def attention(q, k, v, total: int, heads: int, heads_kv: int, head_dim: int) -> 
     out = np.zeros(heads * head_dim, np.float32)
     _check(lib().cxm_debug_attention(_ptr(q), _ptr(k), _ptr(v), total, heads, heads_kv, head_dim, _ptr(out)))
     return out
+
+
+def attention_noalloc(q_dev: int, k_dev: int, v_dev: int, total: int, heads: int, heads_kv: int, head_dim: int,
+                      out_dev: int, stream: int = 0) -> None:
+    """Attention on caller-owned device buffers (addresses as ints), without
+    any device allocation inside the library; see cxm_attention_noalloc in
+    include/cxm.h for its scratch limit and its sharing rule."""
+    _check(lib().cxm_attention_noalloc(q_dev, k_dev, v_dev, total, heads, heads_kv, head_dim, out_dev,
+                                       stream or None))

@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1108,4 +1109,99 @@ extern "C" int cxm_bench_matvec(cxm_model *m, uint32_t reps, float *ms_per_launc
     *bytes_per_launch = (uint64_t)L.gate.rows * (uint64_t)(L.gate.K / 256) * (uint64_t)bytes_per_block(L.gate.type) +
                         (uint64_t)L.up.rows * (uint64_t)(L.up.K / 256) * (uint64_t)bytes_per_block(L.up.type);
     return check_err(m);
+}
+
+// ── attention without allocation ─────────────────────────────────────────
+// cxm_attention_noalloc is cxm_debug_attention's kernels on caller-owned
+// device buffers, for callers that cannot allocate device memory: a serving
+// process that has already given the whole device to weights and KV caches
+// (a cudaMalloc there fails), and latency-sensitive callers that cannot take
+// the device-wide synchronisation cudaMalloc/cudaFree may imply. It calls no
+// cudaMalloc, cudaFree or allocating library routine. Its scratch (the score
+// rows, the position word and the error word) is the one file-scope device
+// array below, shared by every call on a device: calls whose GPU work
+// overlaps (two host threads, or two streams) race on it.
+constexpr uint32_t kNoAllocScoreCap = 1u << 16;            // score floats: 256 KiB
+constexpr uint32_t kNoAllocFloats = kNoAllocScoreCap + 64;  // + a 256-byte tail: position, error
+static __device__ __align__(256) float g_attn_scratch[kNoAllocFloats];
+
+__global__ void k_noalloc_words(int *len, int *err, int value) {
+    *len = value;
+    *err = 0;
+}
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float *g_noalloc_base[kNoAllocMaxDevices];
+
+// Address of the scratch array on the current device, looked up once per
+// device with that device current; the same first call sets the attention
+// kernels' shared-memory limits on that device.
+int noalloc_scratch(float **out) {
+    int dev = 0;
+    CU(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices) {
+        set_error("device ordinal %d out of range", dev);
+        return -1;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_base[dev]) {
+        if (set_kernel_smem_limits()) return -1;
+        float *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress((void **)&p, g_attn_scratch);
+        if (e != cudaSuccess || !p) {
+            set_error("cudaGetSymbolAddress of the attention scratch failed: %s", cudaGetErrorString(e));
+            return -1;
+        }
+        g_noalloc_base[dev] = p;
+    }
+    *out = g_noalloc_base[dev];
+    return 0;
+}
+}  // namespace
+
+extern "C" int cxm_attention_noalloc(const float *q, const float *k, const float *v, uint32_t total,
+                                     uint32_t heads, uint32_t heads_kv, uint32_t hd, float *out, void *stream) {
+    if (need_device()) return -1;
+    if (!q || !k || !v || !out || total == 0 || heads_kv == 0 || heads % heads_kv || hd % 16 || hd == 0 ||
+        hd > (uint32_t)(kKRow - 4) || out_smem(total) > 200 * 1024) {
+        set_error("bad attention arguments");
+        return -1;
+    }
+    const uint64_t stride = ((uint64_t)total + 3) & ~(uint64_t)3;
+    if ((uint64_t)heads * stride > kNoAllocScoreCap) {
+        set_error("attention scratch holds %u scores (heads x positions rounded up to 4); this call needs %llu",
+                  kNoAllocScoreCap, (unsigned long long)((uint64_t)heads * stride));
+        return -1;
+    }
+    float *base = nullptr;
+    if (noalloc_scratch(&base)) return -1;
+    int *len = (int *)(base + kNoAllocScoreCap), *err = len + 1;
+    const cudaStream_t st = (cudaStream_t)stream;
+    k_noalloc_words<<<1, 1, 0, st>>>(len, err, (int)total - 1);
+    CU(cudaGetLastError());
+    AttnParams a{};
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.out = out;
+    a.d_len = len;
+    a.H = (int)heads;
+    a.KV = (int)heads_kv;
+    a.hd = (int)hd;
+    a.max_pos = (int)total;
+    a.score_stride = (int)stride;
+    a.scores = base;
+    a.scale = 1.0f / sqrtf((float)hd);
+    a.err = err;
+    if (launch_attention_on(st, a)) return -1;
+    int e = 0;
+    CU(cudaMemcpyAsync(&e, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CU(cudaStreamSynchronize(st));
+    if (e) {
+        set_error("attention kernels reported error flags %d", e);
+        return -1;
+    }
+    return 0;
 }

@@ -110,6 +110,26 @@ int cxm_debug_matvec(int ggml_type, const uint8_t *w, uint32_t rows, uint32_t k,
 int cxm_debug_attention(const float *q, const float *k, const float *v, uint32_t total, uint32_t heads,
                         uint32_t heads_kv, uint32_t head_dim, float *out);
 
+/* No counterpart in the reference (its attention, src/ops.rs:1258-1325, runs
+ * on host memory): cxm_debug_attention's kernels on caller-owned DEVICE
+ * buffers, allocating nothing — no cudaMalloc, cudaFree or allocating library
+ * routine. For callers that cannot allocate device memory: a serving process
+ * that has already given the whole device to weights and KV caches, where a
+ * cudaMalloc fails, and latency-sensitive callers that cannot take the
+ * device-wide synchronisation cudaMalloc/cudaFree may imply.
+ *   Limit: heads * round_up(total, 4) <= 65536 scores (a static 256 KiB device
+ *   array); a larger call fails with an error and launches nothing.
+ *   The scratch array is shared by every call on a device: calls whose GPU
+ *   work overlaps (two host threads, or two streams) race on it.
+ *   The first call on each device looks up the array's address and sets the
+ *   kernels' shared-memory limits (with that device current); make that first
+ *   call before any stream capture.
+ *   Work is enqueued on `stream` (a cudaStream_t; NULL = the default stream),
+ *   which is synchronised before the call returns so the kernels' error word
+ *   can be reported. */
+int cxm_attention_noalloc(const float *q, const float *k, const float *v, uint32_t total, uint32_t heads,
+                          uint32_t heads_kv, uint32_t head_dim, float *out, void *stream);
+
 /* f32::exp as every exponential of the path computes it on the device
  * (softmax, SiLU): the same rounding as the host C library's expf, which the
  * reference's f32::exp calls (src/ops.rs:1221, src/kernels/scalar.rs:65). */
