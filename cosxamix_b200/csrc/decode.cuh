@@ -1,0 +1,943 @@
+// The decode step as ONE persistent kernel (one CTA per SM, co-resident by a
+// cooperative launch), running a program of phases:
+//
+//   per layer: q|k|v matvec (norm + quantize in front; bias, RoPE, KV append
+//   behind) · attention scores · softmax + attention output · o matvec
+//   (+ residual) · gate|up matvec (norm in front, SwiGLU behind) · down
+//   matvec (+ residual); then the final norm + output projection + argmax, and
+//   the commit of the position/token.
+//
+// Dependent phases are separated by a grid barrier (bounded spin). Weights
+// never depend on activations, so one producer warp per CTA streams the weight
+// tiles of every matvec phase of the whole step, in the order the consumers
+// will need them, with 1-D bulk copies (the TMA unit; no multicast) into
+// per-warp shared-memory rings — across phase boundaries and while the
+// consumers sit in barriers or attention — and keeps an L2 prefetch running
+// further ahead. HBM streaming therefore never waits for the dependency chain
+// except when the rings and the prefetch window are full.
+//
+// Weights are stored as "quad tiles": a quad is 4 rows (two output pairs: the
+// rows an epilogue combines sit in one quad), and a tile is one quad x up to 8
+// super-blocks, stored lane-interleaved (lane = 4*block + row) in 16-byte
+// chunks so a warp's 32 lanes read consecutive 16-byte words. A warp owns a
+// quad at a time: lane (block, row) forms that super-block's sub-block terms,
+// and each row's running total visits the blocks in order (the reference's
+// sequential sum, src/ops.rs:435-522 with src/kernels/scalar.rs:132-324).
+#pragma once
+
+#include "expf_glibc.h"
+#include "kernels.cuh"
+#include "pipeline.cuh"
+#include "step_kernels.cuh"
+
+namespace cxm {
+
+// ── quad-tiled k-quant matrix ──
+// Quad q starts at base + q*quad_stride; its tile t (super-blocks 8t..8t+nb,
+// nb = min(8, nblk - 8t)) starts 32*t*bpb bytes further. Inside a tile of
+// L = 4*nb lanes (lane = 4*block + row):
+//   plane A  [chunk c][lane] 16-byte units, c < a_chunks(type)
+//   plane S  [lane] s_bytes(type)        (Q6_K 16, Q3_K 12, Q2_K 16)
+//   plane D  [lane] d_bytes(type)        (Q6_K 2, Q3_K 2, Q2_K 4)
+// so a tile holds exactly L GGUF blocks (L*bpb bytes). quad_stride rounds
+// 4*nblk*bpb up to 16 bytes so every tile starts 16-byte aligned.
+struct QMat {
+    const uint8_t *base;
+    int type, rows, K, nblk, nquad, bpb;
+    uint32_t quad_stride;
+};
+
+__host__ __device__ inline int a_chunks(int t) { return plane_a_bytes(t) / 16; }
+__host__ __device__ inline int tile_nb(int nblk, int t) { return nblk - 8 * t < 8 ? nblk - 8 * t : 8; }
+__host__ __device__ inline uint32_t tile_copy_bytes(int nb, int bpb) { return (uint32_t)((4 * nb * bpb + 15) & ~15); }
+__host__ __device__ inline size_t tile_offset(const QMat &M, int q, int t) {
+    return (size_t)q * M.quad_stride + (size_t)t * 32 * (size_t)M.bpb;
+}
+
+// GGUF byte k of super-block b of tiled row r (row order as stored).
+__device__ inline uint8_t qm_block_byte(const QMat &M, int r, int b, int k) {
+    const int q = r >> 2, sl = r & 3, t = b >> 3, bl = b & 7, nb = tile_nb(M.nblk, t), L = 4 * nb;
+    const int lane = 4 * bl + sl;
+    const uint8_t *tile = M.base + tile_offset(M, q, t);
+    const int pa = plane_a_bytes(M.type), ps = plane_s_bytes(M.type), pd = plane_d_bytes(M.type);
+    int lo_a = 0, lo_s = pa, lo_d = pa + ps;  // GGUF offsets of the parts
+    if (M.type == 10) {                        // Q2_K: scales, qs, d|dmin
+        lo_s = 0;
+        lo_a = 16;
+        lo_d = 80;
+    }
+    if (k >= lo_a && k < lo_a + pa) {
+        const int o = k - lo_a;
+        return tile[((o >> 4) * L + lane) * 16 + (o & 15)];
+    }
+    if (ps && k >= lo_s && k < lo_s + ps) return tile[a_chunks(M.type) * L * 16 + lane * ps + (k - lo_s)];
+    return tile[a_chunks(M.type) * L * 16 + L * ps + lane * pd + (k - lo_d)];
+}
+
+// one value of a tiled row, exactly as src/quant.rs:582-679 dequantizes it
+__device__ inline float qm_dequant(const QMat &M, int r, int idx) {
+    const int b = idx >> 8, i = idx & 255;
+    auto B = [&](int k) -> uint32_t { return qm_block_byte(M, r, b, k); };
+    auto H = [&](int k) -> float { return h2f(B(k) | (B(k + 1) << 8)); };
+    switch (M.type) {
+    case 12: case 13: {
+        const float d = H(0), dmin = H(2);
+        const uint32_t w0 = B(4) | B(5) << 8 | B(6) << 16 | B(7) << 24;
+        const uint32_t w1 = B(8) | B(9) << 8 | B(10) << 16 | B(11) << 24;
+        const uint32_t w2 = B(12) | B(13) << 8 | B(14) << 16 | B(15) << 24;
+        const int p = i >> 6, half = (i >> 5) & 1, l = i & 31;
+        int sc, mn;
+        scale_min_k4(2 * p + half, w0, w1, w2, sc, mn);
+        const float dl = fm(d, (float)sc), ml = fm(dmin, (float)mn);
+        if (M.type == 12) {
+            const uint32_t v = B(16 + 32 * p + l);
+            return fs(fm(dl, (float)(half ? (v >> 4) : (v & 0xF))), ml);
+        }
+        const uint32_t v = B(48 + 32 * p + l);
+        const int qv = half ? (int)(v >> 4) : (int)(v & 0xF);
+        const float extra = (B(16 + l) >> (2 * p + half)) & 1 ? 16.0f : 0.0f;
+        return fs(fm(dl, fa((float)qv, extra)), ml);
+    }
+    case 14: {
+        const int h = i >> 7, rr = i & 127, gi = rr >> 5, l = rr & 31;
+        const uint32_t qlb = B(64 * h + 32 * (gi & 1) + l);
+        const int nib = gi < 2 ? (int)(qlb & 0xF) : (int)(qlb >> 4);
+        const int qv = (nib | (int)(((B(128 + 32 * h + l) >> (2 * gi)) & 3) << 4)) - 32;
+        const int sc = (int)(int8_t)B(192 + 8 * h + (rr >> 4));
+        return fm(fm(H(208), (float)sc), (float)qv);
+    }
+    case 11: {
+        const int h = i >> 7, rr = i & 127, r4 = rr >> 5, l = rr & 31, g = 4 * h + r4;
+        const uint32_t a0 = B(96) | B(97) << 8 | B(98) << 16 | B(99) << 24;
+        const uint32_t a1 = B(100) | B(101) << 8 | B(102) << 16 | B(103) << 24;
+        const uint32_t tt = B(104) | B(105) << 8 | B(106) << 16 | B(107) << 24;
+        const int is = 2 * g + (l >> 4), wi = is >> 2;
+        const uint32_t aa = (wi & 1) ? a1 : a0;
+        const uint32_t wq = ((aa >> ((wi >> 1) * 4)) & 0x0F0F0F0Fu) | (((tt >> (2 * wi)) & 0x03030303u) << 4);
+        const int sc = (int)((wq >> (8 * (is & 3))) & 0xFF);
+        const float dl = fm(H(108), fs((float)sc, 32.0f));
+        const int hi = (B(l) >> g) & 1 ? 0 : 4;
+        const int qv = (int)((B(32 + 32 * h + l) >> (2 * r4)) & 3) - hi;
+        return fm(dl, (float)qv);
+    }
+    default: {  // Q2_K
+        const int h = i >> 7, rr = i & 127, r4 = rr >> 5, l = rr & 31, g = 4 * h + r4;
+        const int sc = (int)B(2 * g + (l >> 4));
+        const float dl = fm(H(80), (float)(sc & 0xF)), ml = fm(H(82), (float)(sc >> 4));
+        const int qv = (int)((B(16 + 32 * h + l) >> (2 * r4)) & 3);
+        return fs(fm(dl, (float)qv), ml);
+    }
+    }
+}
+
+// ── the program ──
+enum PhaseKind : int { PH_MATVEC = 0, PH_SCORES = 1, PH_ATTN = 2, PH_COMMIT = 3 };
+
+struct MvSeg {
+    QMat M;
+    int units;                // output units (row pairs); padded quads hold more
+    int pairing, epi, half;   // Pairing, Epilogue; half = head_dim/2 for PAIR_ROPE
+    int at_pos, pos_stride;   // out += pos*pos_stride (K/V cache rows)
+    const float *bias;
+    float *out;
+};
+
+struct MvPhase {
+    MvSeg seg[3];
+    int nseg, nquad, K, ntile;
+    int prologue, need16, need32;
+    const float *in, *norm_w;
+    float eps;
+    QMat E;          // PRO_EMBED: token_embd (tiled); or e32 when it is F32
+    const float *e32;
+    float *x_out;    // PRO_EMBED: CTA 0 stores the embedding row (the residual)
+};
+
+struct AtPhase {
+    const float *q, *k, *v;  // k/v: this layer's cache, [max_pos][KV*hd]
+    float *out, *scores;
+    int H, KV, hd, score_stride, P;  // P: positions per score item
+    float scale;
+};
+
+struct __align__(16) Phase {
+    int kind, barrier;  // barrier: a grid barrier comes first
+    MvPhase mv;
+    AtPhase at;
+};
+static_assert(sizeof(Phase) % 16 == 0, "phase descriptors are staged in 16-byte copies");
+
+struct DecodeArgs {
+    const Phase *prog;
+    int nphase;
+    unsigned *bar;            // grid-barrier counter, zeroed before each launch
+    int *err;
+    int *d_len;               // position of the token; NULL: position 0, no token checks
+    uint32_t *toks;
+    int vocab, max_pos;
+    unsigned long long *argmax_key;
+    const float *rope_cos, *rope_sin;
+    int write_token, commit;  // commit: toks[len+1] = argmax (write_token), len += 1
+    int ring_slots;           // tiles in flight per consumer warp (2..kMaxSlots)
+    uint32_t slot_bytes, region_bytes;
+    int prefetch_tiles;       // L2 prefetch lead of the producer, in tiles
+};
+
+constexpr int kDW = 8;                       // consumer warps
+constexpr int kDecodeThreads = (kDW + 1) * 32;
+constexpr int kMaxSlots = 4;
+constexpr int kTermMax = 16;
+
+__device__ __forceinline__ void dsync() { asm volatile("bar.sync 1, %0;" ::"n"(kDW * 32) : "memory"); }
+
+// named barrier of the consumer warps that also ORs a predicate over them, so
+// a decision taken after it is the same in every consumer thread
+__device__ __forceinline__ bool dsync_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kDW * 32)
+        : "memory");
+    return r != 0;
+}
+
+__host__ __device__ inline size_t act_bytes(int K, int need16, int need32) {
+    size_t b = 0;
+    if (need16) b += (size_t)(K / 256) * kXqStride + (size_t)K / 16 * 8;
+    if (need32) b += (size_t)(K / 256) * kXqStride + (size_t)K / 32 * 8;
+    return (b + 15) & ~(size_t)15;
+}
+
+struct Act {
+    int8_t *q16, *q32;
+    float *e16, *s16, *e32, *s32;
+};
+
+__device__ inline Act carve_act(unsigned char *region, int K, int need16, int need32) {
+    Act a{};
+    unsigned char *p = region;
+    const int nblk = K / 256;
+    if (need16) { a.q16 = (int8_t *)p; p += nblk * kXqStride; }
+    if (need32) { a.q32 = (int8_t *)p; p += nblk * kXqStride; }
+    if (need16) { a.e16 = (float *)p; p += K / 16 * 4; a.s16 = (float *)p; p += K / 16 * 4; }
+    if (need32) { a.e32 = (float *)p; p += K / 32 * 4; a.s32 = (float *)p; p += K / 32 * 4; }
+    return a;
+}
+
+// Activation quantization by the consumer warps, redundantly in every CTA,
+// from the activation `xin` (and the RMSNorm weights `wn`, NULL without the
+// norm) already staged in shared memory: optional RMSNorm
+// (src/kernels/scalar.rs:36-54, f64 sum of squares), then i8 per sub-block of
+// 16 and/or 32 (src/ops.rs:178-198).
+__device__ void quantize_act(const float *xin, const float *wn, int K, float eps, bool need16, bool need32,
+                             const Act &a, double *red, double *scale_s) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = kDW * 32;
+    const bool norm = wn != nullptr;
+    double scale = 0.0;
+    if (norm) {
+        double acc = 0.0;
+        for (int i = tid; i < (K >> 2); i += nt) {
+            const float4 v = ((const float4 *)xin)[i];
+            const double x0 = v.x, x1 = v.y, x2 = v.z, x3 = v.w;
+            acc = __dadd_rn(acc, __dmul_rn(x0, x0));
+            acc = __dadd_rn(acc, __dmul_rn(x1, x1));
+            acc = __dadd_rn(acc, __dmul_rn(x2, x2));
+            acc = __dadd_rn(acc, __dmul_rn(x3, x3));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        if (lane == 0) red[warp] = acc;
+        dsync();
+        if (tid == 0) {
+            double s = 0.0;
+            for (int w = 0; w < kDW; w++) s = __dadd_rn(s, red[w]);
+            *scale_s = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s, (double)K), (double)eps)));
+        }
+        dsync();
+        scale = *scale_s;
+    }
+    // a thread per 16 values: the sub-block of 16, or one half of a sub-block
+    // of 32 (its partner is the neighbouring lane); amax and the i8 sum are
+    // exact in any order
+    const int n16 = K >> 4;
+    for (int base = 0; base < n16; base += nt) {  // trip count uniform across the warp
+        const int c = base + tid;
+        const bool valid = c < n16;
+        float v[16];
+        float amax = 0.0f;
+        if (valid) {
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float4 x = ((const float4 *)xin)[4 * c + u];
+                v[4 * u] = x.x;
+                v[4 * u + 1] = x.y;
+                v[4 * u + 2] = x.z;
+                v[4 * u + 3] = x.w;
+            }
+            if (norm) {
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const float4 w = ((const float4 *)wn)[4 * c + u];
+                    v[4 * u] = __fmul_rn(__double2float_rn(__dmul_rn((double)v[4 * u], scale)), w.x);
+                    v[4 * u + 1] = __fmul_rn(__double2float_rn(__dmul_rn((double)v[4 * u + 1], scale)), w.y);
+                    v[4 * u + 2] = __fmul_rn(__double2float_rn(__dmul_rn((double)v[4 * u + 2], scale)), w.z);
+                    v[4 * u + 3] = __fmul_rn(__double2float_rn(__dmul_rn((double)v[4 * u + 3], scale)), w.w);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 16; u++) amax = fmaxf(amax, fabsf(v[u]));
+        } else {
+#pragma unroll
+            for (int u = 0; u < 16; u++) v[u] = 0.0f;
+        }
+        const int off = ((16 * c) >> 8) * kXqStride + ((16 * c) & 255);
+        if (need16 && valid) {
+            const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+            int sm = 0;
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                const int qv = (int)roundf(__fmul_rn(v[u], inv));
+                sm += qv;
+                w[u >> 2] |= ((uint32_t)qv & 0xFFu) << (8 * (u & 3));
+            }
+            *(uint4 *)(a.q16 + off) = make_uint4(w[0], w[1], w[2], w[3]);
+            a.e16[c] = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f;
+            a.s16[c] = (float)sm;
+        }
+        if (need32) {
+            const float am = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            const float inv = am > 0.0f ? __fdiv_rn(127.0f, am) : 0.0f;
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+            int sm = 0;
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                const int qv = (int)roundf(__fmul_rn(v[u], inv));
+                sm += qv;
+                w[u >> 2] |= ((uint32_t)qv & 0xFFu) << (8 * (u & 3));
+            }
+            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+            if (valid) {
+                *(uint4 *)(a.q32 + off) = make_uint4(w[0], w[1], w[2], w[3]);
+                if (!(c & 1)) {
+                    a.e32[c >> 1] = am > 0.0f ? __fdiv_rn(am, 127.0f) : 0.0f;
+                    a.s32[c >> 1] = (float)sm;
+                }
+            }
+        }
+    }
+    dsync();
+}
+
+// stage n floats (n % 4 == 0) from global memory into shared memory
+__device__ __forceinline__ void stage_floats(float *dst, const float *src, int n) {
+    for (int i = threadIdx.x; i < (n >> 2); i += kDW * 32) cp_async16(dst + 4 * i, src + 4 * i);
+}
+
+// rows (r0, r1) of output unit u of a segment: the pair an epilogue combines
+__device__ __forceinline__ void unit_rows(const MvSeg &g, int u, int &r0, int &r1) {
+    if (g.pairing == PAIR_ADJ) {
+        r0 = 2 * u;
+        r1 = 2 * u + 1;
+    } else if (g.pairing == PAIR_ROPE) {
+        const int h = u / g.half, i = u % g.half;
+        r0 = h * 2 * g.half + i;
+        r1 = r0 + g.half;
+    } else {
+        r0 = r1 = u;  // gate row u, up row u
+    }
+}
+
+// the epilogue's inputs (bias, RoPE rotation, residual), loaded when a
+// quad starts so their latency hides under the quad's tiles
+struct EpiIn {
+    float a, b, c, d;
+};
+
+__device__ __forceinline__ EpiIn epi_load(const DecodeArgs &A, const MvSeg &g, int r0, int r1, int pos) {
+    EpiIn e{0.0f, 0.0f, 0.0f, 0.0f};
+    if (g.at_pos && (pos < 0 || pos >= A.max_pos)) return e;
+    switch (g.epi) {
+    case EPI_STORE:
+        if (g.bias) {
+            e.a = __ldg(g.bias + r0);
+            e.b = __ldg(g.bias + r1);
+        }
+        break;
+    case EPI_ROPE: {
+        const int i = r0 % (2 * g.half);
+        if (g.bias) {
+            e.a = __ldg(g.bias + r0);
+            e.b = __ldg(g.bias + r1);
+        }
+        e.c = __ldg(A.rope_cos + (size_t)pos * g.half + i);
+        e.d = __ldg(A.rope_sin + (size_t)pos * g.half + i);
+        break;
+    }
+    case EPI_RESID:  // this unit's rows are written by this lane only
+        e.a = __ldcg(g.out + r0);
+        e.b = __ldcg(g.out + r1);
+        break;
+    default:
+        break;
+    }
+    return e;
+}
+
+__device__ void unit_epilogue(const DecodeArgs &A, const MvSeg &g, int r0, int r1, float y0, float y1, int pos,
+                              const EpiIn &e, unsigned long long &best) {
+    if (g.at_pos && (pos < 0 || pos >= A.max_pos)) return;
+    float *out = g.out + (g.at_pos ? (size_t)pos * g.pos_stride : 0);
+    switch (g.epi) {
+    case EPI_STORE:
+        if (g.bias) {
+            y0 = fa(y0, e.a);
+            y1 = fa(y1, e.b);
+        }
+        out[r0] = y0;
+        out[r1] = y1;
+        break;
+    case EPI_ROPE: {
+        // src/ops.rs:1150-1193, split-half pair (i, i + hd/2) at pos
+        const float a = g.bias ? fa(y0, e.a) : y0, b = g.bias ? fa(y1, e.b) : y1;
+        out[r0] = fs(fm(a, e.c), fm(b, e.d));
+        out[r1] = fa(fm(a, e.d), fm(b, e.c));
+        break;
+    }
+    case EPI_RESID:  // src/forward.rs:467-469, :489-491
+        out[r0] = fa(e.a, y0);
+        out[r1] = fa(e.b, y1);
+        break;
+    case EPI_SWIGLU: {
+        // src/kernels/scalar.rs:63-67 then `*a *= u` (src/forward.rs:485-487)
+        const float act = __fdiv_rn(y0, fa(1.0f, expf_glibc(-y0)));
+        out[r0] = fm(act, y1);
+        break;
+    }
+    case EPI_LOGITS: {
+        out[r0] = y0;
+        out[r1] = y1;
+        const unsigned long long ka = (y0 == y0) ? argmax_key(y0, (uint32_t)r0) : 0ull;
+        const unsigned long long kb = (y1 == y1) ? argmax_key(y1, (uint32_t)r1) : 0ull;
+        const unsigned long long kk = ka > kb ? ka : kb;
+        best = kk > best ? kk : best;
+        break;
+    }
+    }
+}
+
+// quad range of this CTA in a matvec phase: contiguous and balanced
+__device__ __forceinline__ void cta_quads(int nquad, int &qb, int &qe) {
+    qb = (int)(((long long)blockIdx.x * nquad) / gridDim.x);
+    qe = (int)(((long long)(blockIdx.x + 1) * nquad) / gridDim.x);
+}
+
+// ── the producer's walk over the step's weight tiles ──
+// Both the bulk-copy cursor and the L2-prefetch cursor run this same walk:
+// matvec phases in program order; in each, this CTA's quads in rounds of kDW
+// (quad qb + 8k + w belongs to consumer warp w), each round tile-major, so a
+// warp receives its quads' tiles in the order it consumes them.
+struct Sched {
+    int ph, nseg, ntile, nblk, qb, qe, k, t, w;
+    int segq[3], bpb[3];
+    uint32_t qstride[3];
+    const uint8_t *base[3];
+};
+
+struct Item {
+    const uint8_t *src;
+    uint32_t bytes;
+    int warp;
+};
+
+__device__ inline void sched_init(Sched &s) {
+    s.ph = -1;
+    s.k = s.t = s.w = 0;
+    s.qb = s.qe = 0;
+    s.ntile = 0;
+}
+
+__device__ inline bool sched_next(const DecodeArgs &A, Sched &s, Item &it) {
+    for (;;) {
+        if (s.ph >= A.nphase) return false;
+        if (s.ph >= 0) {
+            while (s.qb + kDW * s.k < s.qe) {
+                while (s.t < s.ntile) {
+                    while (s.w < kDW) {
+                        const int w = s.w++;
+                        int q = s.qb + kDW * s.k + w;
+                        if (q >= s.qe) continue;
+                        int j = 0;
+                        while (j < s.nseg - 1 && q >= s.segq[j]) q -= s.segq[j++];
+                        const int nb = tile_nb(s.nblk, s.t);
+                        it.src = s.base[j] + (size_t)q * s.qstride[j] + (size_t)s.t * 32 * s.bpb[j];
+                        it.bytes = tile_copy_bytes(nb, s.bpb[j]);
+                        it.warp = w;
+                        return true;
+                    }
+                    s.w = 0;
+                    s.t++;
+                }
+                s.t = 0;
+                s.k++;
+            }
+        }
+        // next matvec phase
+        for (s.ph++; s.ph < A.nphase; s.ph++)
+            if (__ldg(&A.prog[s.ph].kind) == PH_MATVEC) break;
+        if (s.ph >= A.nphase) return false;
+        const MvPhase &P = A.prog[s.ph].mv;
+        s.nseg = __ldg(&P.nseg);
+        s.ntile = __ldg(&P.ntile);
+        for (int j = 0; j < 3; j++) {
+            if (j < s.nseg) {
+                s.segq[j] = __ldg(&P.seg[j].M.nquad);
+                s.bpb[j] = __ldg(&P.seg[j].M.bpb);
+                s.qstride[j] = __ldg(&P.seg[j].M.quad_stride);
+                s.base[j] = (const uint8_t *)__ldg((const unsigned long long *)&P.seg[j].M.base);
+            }
+        }
+        s.nblk = __ldg(&P.seg[0].M.nblk);
+        cta_quads(__ldg(&P.nquad), s.qb, s.qe);
+        s.k = s.t = s.w = 0;
+    }
+}
+
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// ── grid barrier among the consumer warps of all CTAs (bounded) ──
+// each poll is an L2 round trip (~0.5 us): 2^21 polls bound a wait near 1 s
+constexpr uint32_t kBarrierSpins = 1u << 21;
+
+__device__ bool grid_sync(const DecodeArgs &A, unsigned target, volatile int *abort_flag, int *ok_s) {
+    dsync();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        __threadfence();
+        atomicAdd(A.bar, 1u);
+        for (uint32_t i = 0;; i++) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(A.bar) : "memory");
+            if ((int)(v - target) >= 0) break;
+            if (i >= kBarrierSpins) {
+                atomicOr(A.err, ERR_TIMEOUT);
+                ok = 0;
+                break;
+            }
+            if ((i & 255) == 255) {
+                if (*(volatile int *)A.err & ERR_TIMEOUT) {  // another CTA gave up
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        if (!ok) *abort_flag = 1;
+        *ok_s = ok;
+    }
+    dsync();
+    return *ok_s != 0;
+}
+
+// ── attention phases (src/ops.rs:1258-1325), reference order ──
+constexpr int kAttnVChunk = 64, kAttnVRing = 8, kAttnDims = 16;
+
+__host__ __device__ inline size_t scores_region(int P, int G, int hd) {
+    return ((size_t)P * (hd + 4) + (size_t)G * hd) * sizeof(float);
+}
+__host__ __device__ inline size_t attn_region(int max_pos) {
+    return ((size_t)((max_pos + 3) & ~3) + (size_t)kAttnVRing * kAttnVChunk * kAttnDims) * sizeof(float);
+}
+
+// score[h][p] = (sequential dot of q_h and k_p over the head dim) · scale; an
+// item is one kv head and P positions, shared by the G query heads on it
+__device__ void phase_scores(const AtPhase &at, int n, float *region) {
+    const int tid = threadIdx.x, hd = at.hd, G = at.H / at.KV, P = at.P, kvd = at.KV * hd, c4 = hd / 4;
+    const int nchunk = (n + P - 1) / P, items = at.KV * nchunk;
+    float *ks = region, *qs = region + (size_t)P * (hd + 4);
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int g = item / nchunk, p0 = (item % nchunk) * P, cnt = min(P, n - p0);
+        for (int i = tid; i < G * c4; i += kDW * 32) {
+            const int hq = i / c4, c = i - hq * c4;
+            cp_async16(qs + hq * hd + 4 * c, at.q + (size_t)(g * G + hq) * hd + 4 * c);
+        }
+        for (int i = tid; i < cnt * c4; i += kDW * 32) {
+            const int r = i / c4, c = i - r * c4;
+            cp_async16(ks + r * (hd + 4) + 4 * c, at.k + (size_t)(p0 + r) * kvd + (size_t)g * hd + 4 * c);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        dsync();
+        if (tid < G * P) {
+            const int hq = tid / P, pp = tid - hq * P;
+            if (pp < cnt) {
+                const float4 *kr = (const float4 *)(ks + pp * (hd + 4));
+                const float4 *q4 = (const float4 *)(qs + hq * hd);
+                float acc = 0.0f;
+                for (int c = 0; c < c4; c++) {
+                    const float4 kv = kr[c], qv = q4[c];
+                    acc = fa(acc, fm(qv.x, kv.x));
+                    acc = fa(acc, fm(qv.y, kv.y));
+                    acc = fa(acc, fm(qv.z, kv.z));
+                    acc = fa(acc, fm(qv.w, kv.w));
+                }
+                at.scores[(size_t)(g * G + hq) * at.score_stride + p0 + pp] = fm(acc, at.scale);
+            }
+        }
+        dsync();
+    }
+}
+
+// softmax over a head's scores (subtract the max, exp, sum position by
+// position, multiply by 1/total; src/ops.rs:1206-1230), then
+// out[d] = Σ_p prob_p·v_p[d] added position by position; an item is one head
+// and kAttnDims dims
+__device__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region, float *fred, float *fbc) {
+    const int tid = threadIdx.x, nt = kDW * 32, hd = at.hd, G = at.H / at.KV, kvd = at.KV * hd;
+    const int nslice = hd / kAttnDims, items = at.H * nslice;
+    float *pr = region;
+    float *vs = region + ((max_pos + 3) & ~3);
+    const int nchunks = (n + kAttnVChunk - 1) / kAttnVChunk;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int h = item / nslice, d0 = (item % nslice) * kAttnDims, g = h / G;
+        const float *sc = at.scores + (size_t)h * at.score_stride;
+        const float *vb = at.v + (size_t)g * hd + d0;
+        auto stage = [&](int c) {
+            if (c >= nchunks) return;
+            const int base = c * kAttnVChunk, cnt = min(kAttnVChunk, n - base);
+            float *dst = vs + (c % kAttnVRing) * kAttnVChunk * kAttnDims;
+            for (int i = tid; i < cnt * (kAttnDims / 4); i += nt) {
+                const int r = i / (kAttnDims / 4), q = i - r * (kAttnDims / 4);
+                cp_async16(dst + r * kAttnDims + 4 * q, vb + (size_t)(base + r) * kvd + 4 * q);
+            }
+        };
+        for (int i = tid; i < (n + 3) / 4; i += nt) cp_async16(pr + 4 * i, sc + 4 * i);
+        cp_async_commit();
+        for (int c = 0; c < kAttnVRing - 1; c++) {
+            stage(c);
+            cp_async_commit();
+        }
+        cp_async_wait<kAttnVRing - 1>();
+        dsync();
+        float m = -INFINITY;
+        for (int i = tid; i < n; i += nt) m = fmaxf(m, pr[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((tid & 31) == 0) fred[tid >> 5] = m;
+        dsync();
+        if (tid == 0) {
+            float mm = -INFINITY;
+            for (int w = 0; w < kDW; w++) mm = fmaxf(mm, fred[w]);
+            *fbc = mm;
+        }
+        dsync();
+        const float mx = *fbc;
+        dsync();
+        if (!isfinite(mx)) {
+            const float u = __fdiv_rn(1.0f, (float)n);
+            for (int i = tid; i < n; i += nt) pr[i] = u;
+        } else {
+            for (int i = tid; i < n; i += nt) pr[i] = expf_glibc(fs(pr[i], mx));
+            dsync();
+            if (tid == 0) {
+                float total = 0.0f;
+                int i = 0;
+                for (; i + 4 <= n; i += 4) {
+                    const float4 v = *(const float4 *)(pr + i);
+                    total = fa(fa(fa(fa(total, v.x), v.y), v.z), v.w);
+                }
+                for (; i < n; i++) total = fa(total, pr[i]);
+                *fbc = __fdiv_rn(1.0f, total);
+            }
+            dsync();
+            const float inv = *fbc;
+            for (int i = tid; i < n; i += nt) pr[i] = fm(pr[i], inv);
+        }
+        dsync();
+        float acc = 0.0f;
+        for (int c = 0; c < nchunks; c++) {
+            stage(c + kAttnVRing - 1);
+            cp_async_commit();
+            cp_async_wait<kAttnVRing - 1>();
+            dsync();
+            if (tid < kAttnDims) {
+                const float *src = vs + (c % kAttnVRing) * kAttnVChunk * kAttnDims + tid;
+                const int base = c * kAttnVChunk, cnt = min(kAttnVChunk, n - base);
+                for (int r = 0; r < cnt; r++) acc = fa(acc, fm(pr[base + r], src[r * kAttnDims]));
+            }
+            dsync();
+        }
+        if (tid < kAttnDims) at.out[(size_t)h * hd + d0 + tid] = acc;
+        cp_async_wait<0>();
+        dsync();
+    }
+}
+
+// ── the kernel ──
+__global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_constant__ DecodeArgs A) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+    const int ns = A.ring_slots;
+    unsigned char *ring = smem;
+    unsigned char *region = ring + (size_t)kDW * ns * A.slot_bytes;
+    Phase *phbuf = (Phase *)(region + A.region_bytes);  // two staged phase descriptors
+    __shared__ __align__(8) uint64_t full[kDW][kMaxSlots], empty[kDW][kMaxSlots];
+    __shared__ volatile int abort_flag;
+    __shared__ int sync_ok;
+    __shared__ double red[kDW];
+    __shared__ double scale_s;
+    __shared__ unsigned long long best_s[kDW];
+    __shared__ float fred[kDW];
+    __shared__ float fbc;
+
+    __shared__ int pos_s, tok_s, bad_s;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        for (int w = 0; w < kDW; w++)
+            for (int s = 0; s < kMaxSlots; s++) {
+                mbar_init(&full[w][s], 1);
+                mbar_init(&empty[w][s], 1);
+            }
+        abort_flag = 0;
+        mbar_fence_init();
+        // The step's position and token, read once here: thread 0 of every CTA
+        // reads them before its first grid barrier, so before the commit of
+        // CTA 0 (after the last barrier) rewrites them.
+        int p = 0, bad = 0;
+        uint32_t t = 0;
+        if (A.d_len) {
+            p = *(volatile int *)A.d_len;
+            const bool pos_ok = p >= 0 && p < A.max_pos;
+            t = pos_ok ? A.toks[p] : 0u;
+            if (!pos_ok) bad = ERR_POSITION;
+            else if (t >= (uint32_t)A.vocab) bad = ERR_TOKEN;
+        }
+        pos_s = p;
+        tok_s = (int)t;
+        bad_s = bad;
+    }
+    __syncthreads();
+
+    // an invalid position or token stops every CTA before any work
+    const int pos = pos_s;
+    const uint32_t tok = (uint32_t)tok_s;
+    if (bad_s) {
+        if (blockIdx.x == 0 && tid == 0) atomicOr(A.err, bad_s);
+        return;
+    }
+
+    if (warp == kDW) {
+        // ── producer: lane 0 walks the step's tiles ──
+        if (lane != 0) return;
+        uint32_t cnt[kDW];
+        for (int w = 0; w < kDW; w++) cnt[w] = 0;
+        Sched fetch, pre;
+        sched_init(fetch);
+        sched_init(pre);
+        long long issued = 0, pre_issued = 0;
+        bool pre_live = A.prefetch_tiles > 0;
+        bool ok = true;
+        Item it, pit;
+        while (sched_next(A, fetch, it)) {
+            while (pre_live && pre_issued < issued + A.prefetch_tiles) {
+                if (!sched_next(A, pre, pit)) {
+                    pre_live = false;
+                    break;
+                }
+                bulk_prefetch_l2(pit.src, pit.bytes);
+                pre_issued++;
+            }
+            const int w = it.warp;
+            const uint32_t c = cnt[w]++;
+            const int s = (int)(c % (uint32_t)ns);
+            if (!mbar_wait_bounded(&empty[w][s], ((c / ns) & 1) ^ 1, &abort_flag)) {
+                ok = false;
+                cnt[w]--;
+                break;
+            }
+            mbar_arrive_expect_tx(&full[w][s], it.bytes);
+            bulk_g2s(ring + ((size_t)w * ns + s) * A.slot_bytes, it.src, it.bytes, &full[w][s]);
+            issued++;
+        }
+        if (!ok) {
+            abort_flag = 1;
+            atomicOr(A.err, ERR_TIMEOUT);
+        }
+        // the copies issued last must land before the CTA may exit
+        for (int w = 0; w < kDW; w++) {
+            const uint32_t last = cnt[w];
+            for (uint32_t j = last > (uint32_t)ns ? last - ns : 0; j < last; j++)
+                mbar_wait_bounded(&full[w][j % ns], (j / ns) & 1, &abort_flag, 1u << 14);
+        }
+        return;
+    }
+
+    // ── consumers ──
+    const int bl = lane >> 2, sl = lane & 3;
+    uint32_t wcnt = 0;  // tiles this warp has consumed
+    unsigned nbar = 0;
+    // A warp that gives up (a wait ran out, or another role raised abort_flag)
+    // skips its remaining work but keeps the phase's control flow, so every
+    // named barrier is still reached by all consumer warps; the phase loop
+    // stops on a barrier-wide OR of the flag.
+    // stage descriptor 0
+    {
+        const int nw = (int)(sizeof(Phase) / 16);
+        for (int i = tid; i < nw; i += kDW * 32) cp_async16((unsigned char *)&phbuf[0] + 16 * i, (const unsigned char *)&A.prog[0] + 16 * i);
+        cp_async_commit();
+        cp_async_wait<0>();
+        dsync();
+    }
+    bool stop = false;
+    for (int pi = 0; pi < A.nphase && !stop; pi++) {
+        const Phase &ph = phbuf[pi & 1];
+        if (pi + 1 < A.nphase) {  // next descriptor streams in during this phase
+            const int nw = (int)(sizeof(Phase) / 16);
+            for (int i = tid; i < nw; i += kDW * 32)
+                cp_async16((unsigned char *)&phbuf[(pi + 1) & 1] + 16 * i, (const unsigned char *)&A.prog[pi + 1] + 16 * i);
+            cp_async_commit();
+        }
+        if (ph.barrier) {
+            nbar++;
+            if (!grid_sync(A, nbar * gridDim.x, &abort_flag, &sync_ok)) break;  // uniform
+        }
+        const int n = pos + 1;
+        if (ph.kind == PH_MATVEC) {
+            const MvPhase &P = ph.mv;
+            const Act act = carve_act(region, P.K, P.need16, P.need32);
+            // the activation and the norm weights: one round of copies
+            float *xin = (float *)(region + act_bytes(P.K, P.need16, P.need32));
+            float *wn = P.prologue == PRO_QUANT ? nullptr : xin + P.K;
+            if (wn) stage_floats(wn, P.norm_w, P.K);
+            if (P.prologue != PRO_EMBED) stage_floats(xin, P.in, P.K);
+            cp_async_commit();
+            if (P.prologue == PRO_EMBED) {
+                for (int i = tid; i < P.K; i += kDW * 32) {
+                    const float v = P.e32 ? __ldg(P.e32 + (size_t)tok * P.K + i) : qm_dequant(P.E, (int)tok, i);
+                    xin[i] = v;
+                    if (blockIdx.x == 0) P.x_out[i] = v;
+                }
+                if (blockIdx.x == 0 && tid == 0 && A.argmax_key) *A.argmax_key = 0ull;
+            }
+            cp_async_wait<0>();
+            dsync();
+            quantize_act(xin, wn, P.K, P.eps, P.need16, P.need32, act, red, &scale_s);
+            unsigned long long best = 0ull;
+            int qb, qe;
+            cta_quads(P.nquad, qb, qe);
+            for (int q0 = qb + warp; q0 < qe; q0 += kDW) {
+                int j = 0, lq = q0;  // phase-global quad index -> segment, local quad
+                while (j < P.nseg - 1 && lq >= P.seg[j].M.nquad) lq -= P.seg[j++].M.nquad;
+                const MvSeg &sg = P.seg[j];
+                const int T = sg.M.type, nblk = sg.M.nblk;
+                const bool s32 = (T == 12 || T == 13);
+                const int nsub = s32 ? 8 : 16;
+                const int8_t *xq = s32 ? act.q32 : act.q16;
+                const float *xe = s32 ? act.e32 : act.e16, *xs = s32 ? act.s32 : act.s16;
+                const int u = 2 * lq + (lane >> 1);
+                const bool epi_lane = (lane == 0 || lane == 2) && u < sg.units;
+                int r0 = 0, r1 = 0;
+                EpiIn ein{0.0f, 0.0f, 0.0f, 0.0f};
+                if (epi_lane) {
+                    unit_rows(sg, u, r0, r1);
+                    ein = epi_load(A, sg, r0, r1, pos);
+                }
+                float acc = 0.0f;
+                bool live = true;
+                for (int t = 0; t < P.ntile; t++) {
+                    const uint32_t c = wcnt++;
+                    const int s = (int)(c % (uint32_t)ns);
+                    bool got = false;
+                    if (live) got = mbar_wait_bounded(&full[warp][s], (c / ns) & 1, &abort_flag);
+                    if (!__all_sync(0xffffffffu, got)) {
+                        if (lane == 0) abort_flag = 1;
+                        live = false;
+                        continue;
+                    }
+                    const int nb = tile_nb(nblk, t), L = 4 * nb;
+                    const unsigned char *tile = ring + ((size_t)warp * ns + s) * A.slot_bytes;
+                    float tv[kTermMax];
+                    if (bl < nb) {
+                        const int cs = L * 16;
+                        const uint8_t *pa = tile + lane * 16;
+                        const uint8_t *pss = tile + a_chunks(T) * cs + lane * plane_s_bytes(T);
+                        const uint8_t *pd = tile + a_chunks(T) * cs + L * plane_s_bytes(T) + lane * plane_d_bytes(T);
+                        const int b = 8 * t + bl;
+                        const XB xb{xq + b * kXqStride, xe + b * nsub, xs + b * nsub};
+                        switch (T) {
+                        case 12: block_k4<false>(pa, cs, xb, tv); break;
+                        case 13: block_k4<true>(pa, cs, xb, tv); break;
+                        case 14: block_q6k(pa, cs, pss, pd, xb, tv); break;
+                        case 11: block_q3k(pa, cs, pss, pd, xb, tv); break;
+                        default: block_q2k(pa, cs, pss, pd, xb, tv); break;
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[warp][s]);  // the tile is consumed
+                    // each row's running total visits the tile's blocks in order
+                    float run = acc;
+                    if (s32) {
+                        for (int jb = 0; jb < nb; jb++) {
+                            float v = run;
+                            if (bl == jb) {
+#pragma unroll
+                                for (int k = 0; k < 8; k++) v = fa(v, tv[k]);
+                            }
+                            run = __shfl_sync(0xffffffffu, v, jb * 4 + sl);
+                        }
+                    } else {
+                        for (int jb = 0; jb < nb; jb++) {
+                            float v = run;
+                            if (bl == jb) {
+#pragma unroll
+                                for (int k = 0; k < 16; k++) v = fa(v, tv[k]);
+                            }
+                            run = __shfl_sync(0xffffffffu, v, jb * 4 + sl);
+                        }
+                    }
+                    acc = run;
+                }
+                if (!live) continue;
+                // lanes 0..3 hold rows 0..3 of the quad: units (rows 0,1) and (rows 2,3)
+                const float other = __shfl_down_sync(0xffffffffu, acc, 1);
+                if (epi_lane) unit_epilogue(A, sg, r0, r1, acc, other, pos, ein, best);
+            }
+            if (A.argmax_key && P.seg[0].epi == EPI_LOGITS) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+                    best = v > best ? v : best;
+                }
+                if (lane == 0) best_s[warp] = best;
+                dsync();
+                if (tid == 0) {
+                    unsigned long long bb = 0;
+                    for (int w = 0; w < kDW; w++) bb = best_s[w] > bb ? best_s[w] : bb;
+                    if (bb) atomicMax(A.argmax_key, bb);
+                }
+            }
+        } else if (ph.kind == PH_SCORES) {
+            phase_scores(ph.at, n, (float *)region);
+        } else if (ph.kind == PH_ATTN) {
+            phase_attn(ph.at, n, A.max_pos, (float *)region, fred, &fbc);
+        } else if (ph.kind == PH_COMMIT) {
+            if (blockIdx.x == 0 && tid == 0 && A.d_len) {
+                if (A.write_token && A.argmax_key && pos + 1 < A.max_pos + 1)
+                    A.toks[pos + 1] = argmax_index(__ldcg(A.argmax_key));
+                if (A.commit) *(volatile int *)A.d_len = pos + 1;
+            }
+        }
+        cp_async_wait<0>();  // the next descriptor
+        stop = dsync_or(abort_flag != 0);
+    }
+    if (stop && tid == 0) atomicOr(A.err, ERR_TIMEOUT);
+}
+
+}  // namespace cxm

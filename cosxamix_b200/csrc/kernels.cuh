@@ -293,9 +293,12 @@ __device__ __forceinline__ int term_sub(int type, int q, int k) {
 
 // ── a whole super-block from shared memory ──
 // The streaming matvec gives each lane one super-block of one row: it forms
-// all of the block's sub-block terms t[0..nsub) in sub-block order. `xq` is
-// the activation with each 256-value block padded to kXqStride bytes (bank
-// spread); `xe`/`xs` hold 8 (sub-blocks of 32) or 16 (of 16) floats per block.
+// all of the block's sub-block terms t[0..nsub) in sub-block order. The
+// block's plane-A bytes are 16-byte chunks `cs` bytes apart (16 when they are
+// contiguous; the lane count x 16 in a quad tile, where the lanes' chunks are
+// interleaved). `xq` is the activation with each 256-value block padded to
+// kXqStride bytes (bank spread); `xe`/`xs` hold 8 (sub-blocks of 32) or 16
+// (of 16) floats per block.
 constexpr int kXqStride = 272;
 
 struct XB {  // one block of the quantized activation
@@ -316,19 +319,19 @@ __device__ __forceinline__ uint4 shl4(uint4 v, int n) { return make_uint4(v.x <<
 
 // Q4_K / Q5_K: 8 terms (src/kernels/scalar.rs:132-217)
 template <bool Q5>
-__device__ __forceinline__ void block_k4(const uint8_t *pa, const XB &x, float *t) {
+__device__ __forceinline__ void block_k4(const uint8_t *pa, int cs, const XB &x, float *t) {
     const uint4 hdr = *(const uint4 *)pa;
     const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
     const int4 *xp = (const int4 *)x.q;
-    const uint8_t *qs = pa + (Q5 ? 48 : 16);
+    const int c0 = Q5 ? 3 : 1;  // first qs chunk
     uint4 qh0 = make_uint4(0, 0, 0, 0), qh1 = qh0;
     if (Q5) {
-        qh0 = *(const uint4 *)(pa + 16);
-        qh1 = *(const uint4 *)(pa + 32);
+        qh0 = *(const uint4 *)(pa + cs);
+        qh1 = *(const uint4 *)(pa + 2 * cs);
     }
 #pragma unroll
     for (int p = 0; p < 4; p++) {
-        const uint4 wa = *(const uint4 *)(qs + 32 * p), wb = *(const uint4 *)(qs + 32 * p + 16);
+        const uint4 wa = *(const uint4 *)(pa + (c0 + 2 * p) * cs), wb = *(const uint4 *)(pa + (c0 + 2 * p + 1) * cs);
         uint4 la = and4(wa, 0x0F0F0F0Fu), lb = and4(wb, 0x0F0F0F0Fu);
         uint4 ha = and4(shr4(wa, 4), 0x0F0F0F0Fu), hb = and4(shr4(wb, 4), 0x0F0F0F0Fu);
         if (Q5) {
@@ -349,8 +352,8 @@ __device__ __forceinline__ void block_k4(const uint8_t *pa, const XB &x, float *
 }
 
 // Q6_K: 16 terms (src/kernels/scalar.rs:294-324)
-__device__ __forceinline__ void block_q6k(const uint8_t *pa, const uint8_t *ps, const uint8_t *pd, const XB &x,
-                                          float *t) {
+__device__ __forceinline__ void block_q6k(const uint8_t *pa, int cs, const uint8_t *ps, const uint8_t *pd,
+                                          const XB &x, float *t) {
     const float d = h2f(*(const unsigned short *)pd);
     const uint4 scv = *(const uint4 *)ps;
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
@@ -360,8 +363,8 @@ __device__ __forceinline__ void block_q6k(const uint8_t *pa, const uint8_t *ps, 
 #pragma unroll
         for (int md = 0; md < 2; md++) {
             // 16 positions: ql columns 0 (groups gi 0, 2) and 1 (gi 1, 3), qh bits
-            const uint4 q0 = *(const uint4 *)(pa + 64 * h + 16 * md), q1 = *(const uint4 *)(pa + 64 * h + 32 + 16 * md);
-            const uint4 qh = *(const uint4 *)(pa + 128 + 32 * h + 16 * md);
+            const uint4 q0 = *(const uint4 *)(pa + (4 * h + md) * cs), q1 = *(const uint4 *)(pa + (4 * h + 2 + md) * cs);
+            const uint4 qh = *(const uint4 *)(pa + (8 + 2 * h + md) * cs);
 #pragma unroll
             for (int gi = 0; gi < 4; gi++) {
                 const uint4 ql = (gi & 1) ? q1 : q0;
@@ -377,17 +380,17 @@ __device__ __forceinline__ void block_q6k(const uint8_t *pa, const uint8_t *ps, 
 }
 
 // Q3_K: 16 terms (src/kernels/scalar.rs:236-275)
-__device__ __forceinline__ void block_q3k(const uint8_t *pa, const uint8_t *ps, const uint8_t *pd, const XB &x,
-                                          float *t) {
+__device__ __forceinline__ void block_q3k(const uint8_t *pa, int cs, const uint8_t *ps, const uint8_t *pd,
+                                          const XB &x, float *t) {
     const float d = h2f(*(const unsigned short *)pd);
     const uint32_t a0 = *(const uint32_t *)ps, a1 = *(const uint32_t *)(ps + 4), tt = *(const uint32_t *)(ps + 8);
     const int4 *xp = (const int4 *)x.q;
 #pragma unroll
     for (int md = 0; md < 2; md++) {
-        const uint4 hm = *(const uint4 *)(pa + 16 * md);
+        const uint4 hm = *(const uint4 *)(pa + md * cs);
 #pragma unroll
         for (int h = 0; h < 2; h++) {
-            const uint4 qs = *(const uint4 *)(pa + 32 + 32 * h + 16 * md);
+            const uint4 qs = *(const uint4 *)(pa + (2 + 2 * h + md) * cs);
 #pragma unroll
             for (int r4 = 0; r4 < 4; r4++) {
                 const int g = 4 * h + r4, si = 2 * g + md, wi = si >> 2;
@@ -403,8 +406,8 @@ __device__ __forceinline__ void block_q3k(const uint8_t *pa, const uint8_t *ps, 
 }
 
 // Q2_K: 16 terms (src/kernels/q2k.rs:41-69)
-__device__ __forceinline__ void block_q2k(const uint8_t *pa, const uint8_t *ps, const uint8_t *pd, const XB &x,
-                                          float *t) {
+__device__ __forceinline__ void block_q2k(const uint8_t *pa, int cs, const uint8_t *ps, const uint8_t *pd,
+                                          const XB &x, float *t) {
     const uint32_t dd = *(const uint32_t *)pd;
     const float d = h2f(dd), dm = h2f(dd >> 16);
     const uint4 scv = *(const uint4 *)ps;
@@ -414,7 +417,7 @@ __device__ __forceinline__ void block_q2k(const uint8_t *pa, const uint8_t *ps, 
     for (int h = 0; h < 2; h++) {
 #pragma unroll
         for (int md = 0; md < 2; md++) {
-            const uint4 qs = *(const uint4 *)(pa + 32 * h + 16 * md);
+            const uint4 qs = *(const uint4 *)(pa + (2 * h + md) * cs);
 #pragma unroll
             for (int r4 = 0; r4 < 4; r4++) {
                 const int g = 4 * h + r4, si = 2 * g + md;

@@ -1,6 +1,7 @@
-// Host orchestration of the decode path: model upload (k-quant planes in
-// HBM), KV caches, the per-token step captured as a CUDA graph, and the C ABI
-// of include/cxm.h.
+// Host orchestration of the decode path: model upload (k-quant quad tiles in
+// HBM), KV caches, the per-token step (one persistent kernel running a
+// program of phases, captured as a CUDA graph), and the C ABI of
+// include/cxm.h.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -10,11 +11,12 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/cxm.h"
 #include "cxm_internal.h"
-#include "step_kernels.cuh"
+#include "decode.cuh"
 
 using namespace cxm;
 
@@ -30,7 +32,7 @@ using namespace cxm;
 namespace {
 
 struct Layer {
-    DMat q, k, v, o, gate, up, down;
+    QMat q, k, v, o, gu, down;  // gu: gate and up interleaved (PAIR_TWO quads)
     float *attn_norm, *ffn_norm, *bq, *bk, *bv;
 };
 
@@ -41,15 +43,17 @@ struct cxm_model {
     cudaStream_t stream = nullptr;
     cxm_config cfg{};
     std::vector<Layer> layers;
-    DMat embd{}, out{};
+    QMat embd{}, out{};
     float *embd_f32 = nullptr;
     float *out_norm = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     std::vector<void *> allocs;
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
     float *scores = nullptr;  // attention scratch [n_head][ctx]
     int *err = nullptr;
+    unsigned *bar = nullptr;  // grid-barrier counter of the decode kernel
     unsigned long long *argmax_key = nullptr;
     int sms = 148;
+    uint32_t slot_bytes = 0;  // largest quad tile of the model
     uint64_t weight_bytes = 0;
     bool logits_valid = false;
 
@@ -72,17 +76,26 @@ struct cxm_model {
     }
 };
 
+// a decode program on the device and the launch geometry it needs
+struct Program {
+    Phase *d = nullptr;
+    int n = 0;
+    size_t region = 0;
+};
+
 struct cxm_cache {
     cxm_model *m = nullptr;
     uint32_t max_tokens = 0, len = 0;
     float *k = nullptr, *v = nullptr;  // [n_layer][max_tokens][kvd]
-    uint32_t *toks = nullptr;          // [max_tokens + 1]
+    uint32_t *toks = nullptr;          // [max_tokens + 2]
     int *d_len = nullptr;
+    Program prog[3];
     cudaGraphExec_t graph[3] = {nullptr, nullptr, nullptr};
     ~cxm_cache() {
         if (m) cudaSetDevice(m->device);
         for (auto &g : graph)
             if (g) cudaGraphExecDestroy(g);
+        for (auto &p : prog) cudaFree(p.d);
         cudaFree(k);
         cudaFree(v);
         cudaFree(toks);
@@ -101,9 +114,92 @@ enum StepMode { STEP_PREFILL = 0, STEP_GREEDY = 1, STEP_LOGITS = 2 };
 
 size_t kv_dim(const cxm_model *m) { return (size_t)m->cfg.n_head_kv * m->cfg.head_dim; }
 
-// Split the GGUF super-blocks of a matrix into the 16-byte-aligned planes of
-// DMat and upload them (src/quant.rs layouts; the bytes are not changed).
-int upload_matrix(cxm_model *m, const Gguf &g, const TensorInfo &t, DMat *out) {
+int sub_of(int type) { return (type == Q4K || type == Q5K) ? 32 : 16; }
+
+// ── quad tiles (the layout QMat describes) ──
+// Tiled row i is row `row` of the GGUF matrix at `m` (its bytes), or a zero
+// row when m is null. The bytes of each block are only moved, never changed.
+struct RowSrc {
+    const uint8_t *m;
+    int row;
+};
+
+QMat tiled_desc(int type, int K, int nrows) {
+    QMat M{};
+    M.type = type;
+    M.K = K;
+    M.nblk = K / 256;
+    M.bpb = bytes_per_block(type);
+    M.nquad = (nrows + 3) / 4;
+    M.rows = 4 * M.nquad;
+    M.quad_stride = (uint32_t)(((size_t)4 * M.nblk * M.bpb + 15) & ~(size_t)15);
+    return M;
+}
+
+void build_tiles(const QMat &M, const std::vector<RowSrc> &rows, std::vector<uint8_t> &buf) {
+    buf.assign((size_t)M.nquad * M.quad_stride, 0);
+    const int T = M.type, pa = plane_a_bytes(T), ps = plane_s_bytes(T), pd = plane_d_bytes(T), ach = pa / 16;
+    int lo_a = 0, lo_s = pa, lo_d = pa + ps;
+    if (T == Q2K) {
+        lo_s = 0;
+        lo_a = 16;
+        lo_d = 80;
+    }
+    const int ntile = (M.nblk + 7) / 8;
+    auto work = [&](int q0, int q1) {
+        for (int q = q0; q < q1; q++)
+            for (int t = 0; t < ntile; t++) {
+                const int nb = tile_nb(M.nblk, t), L = 4 * nb;
+                uint8_t *tile = buf.data() + tile_offset(M, q, t);
+                for (int bl = 0; bl < nb; bl++)
+                    for (int sl = 0; sl < 4; sl++) {
+                        const size_t ri = (size_t)4 * q + sl;
+                        if (ri >= rows.size() || !rows[ri].m) continue;
+                        const uint8_t *blk = rows[ri].m + ((size_t)rows[ri].row * M.nblk + 8 * t + bl) * M.bpb;
+                        const int lane = 4 * bl + sl;
+                        for (int c = 0; c < ach; c++) memcpy(tile + ((size_t)c * L + lane) * 16, blk + lo_a + 16 * c, 16);
+                        if (ps) memcpy(tile + (size_t)ach * L * 16 + (size_t)lane * ps, blk + lo_s, ps);
+                        if (pd) memcpy(tile + (size_t)ach * L * 16 + (size_t)L * ps + (size_t)lane * pd, blk + lo_d, pd);
+                    }
+            }
+    };
+    const int nth = std::max(1, std::min<int>(16, (int)std::thread::hardware_concurrency()));
+    if (M.nquad < 256 || nth == 1) {
+        work(0, M.nquad);
+        return;
+    }
+    std::vector<std::thread> th;
+    for (int i = 0; i < nth; i++)
+        th.emplace_back(work, (int)((long long)M.nquad * i / nth), (int)((long long)M.nquad * (i + 1) / nth));
+    for (auto &x : th) x.join();
+}
+
+// row orders: PAIR_ADJ (rows in order), PAIR_ROPE (rows i and i + half of a
+// head side by side), PAIR_TWO (row u of A, then row u of B)
+std::vector<RowSrc> rows_adj(const uint8_t *a, int n) {
+    std::vector<RowSrc> r(n);
+    for (int i = 0; i < n; i++) r[i] = {a, i};
+    return r;
+}
+std::vector<RowSrc> rows_rope(const uint8_t *a, int n, int half) {
+    std::vector<RowSrc> r(n);
+    for (int u = 0; u < n / 2; u++) {
+        const int h = u / half, i = u % half, r0 = h * 2 * half + i;
+        r[2 * u] = {a, r0};
+        r[2 * u + 1] = {a, r0 + half};
+    }
+    return r;
+}
+std::vector<RowSrc> rows_two(const uint8_t *a, const uint8_t *b, int n) {
+    std::vector<RowSrc> r(2 * (size_t)n);
+    for (int u = 0; u < n; u++) {
+        r[2 * u] = {a, u};
+        r[2 * u + 1] = {b, u};
+    }
+    return r;
+}
+
+int check_matrix(const TensorInfo &t) {
     if (t.dims.size() != 2) {
         set_error("%s: expected a matrix", t.name.c_str());
         return -1;
@@ -112,53 +208,55 @@ int upload_matrix(cxm_model *m, const Gguf &g, const TensorInfo &t, DMat *out) {
         set_error("%s: type %d has no device kernel (k-quants Q2_K..Q6_K only)", t.name.c_str(), t.type);
         return -1;
     }
-    const int K = (int)t.dims[0], rows = (int)t.dims[1];
-    if (K % 256) {
-        set_error("%s: rows of %d values are not a multiple of 256", t.name.c_str(), K);
+    if (t.dims[0] % 256) {
+        set_error("%s: rows of %llu values are not a multiple of 256", t.name.c_str(),
+                  (unsigned long long)t.dims[0]);
         return -1;
     }
-    const int nblk = K / 256, bb = bytes_per_block(t.type);
-    const int pa = plane_a_bytes(t.type), ps = plane_s_bytes(t.type), pd = plane_d_bytes(t.type);
-    DMat d{};
-    d.type = t.type;
-    d.rows = rows;
-    d.K = K;
-    d.nblk = nblk;
-    d.a_row = (uint32_t)(nblk * pa);
-    d.s_row = pitch16((uint32_t)(nblk * ps));
-    d.d_row = pitch16((uint32_t)(nblk * pd));
-    std::vector<uint8_t> A((size_t)rows * d.a_row), S((size_t)rows * d.s_row), D((size_t)rows * d.d_row);
-    const uint8_t *src = g.data(t);
-    for (int r = 0; r < rows; r++) {
-        for (int b = 0; b < nblk; b++) {
-            const uint8_t *blk = src + ((size_t)r * nblk + b) * bb;
-            uint8_t *a = A.data() + (size_t)r * d.a_row + (size_t)b * pa;
-            uint8_t *s = S.data() + (size_t)r * d.s_row + (size_t)b * ps;
-            uint8_t *dd = D.data() + (size_t)r * d.d_row + (size_t)b * pd;
-            switch (t.type) {
-            case Q4K: case Q5K: memcpy(a, blk, (size_t)bb); break;
-            case Q6K: memcpy(a, blk, 192); memcpy(s, blk + 192, 16); memcpy(dd, blk + 208, 2); break;
-            case Q3K: memcpy(a, blk, 96); memcpy(s, blk + 96, 12); memcpy(dd, blk + 108, 2); break;
-            case Q2K: memcpy(a, blk + 16, 64); memcpy(s, blk, 16); memcpy(dd, blk + 80, 4); break;
-            }
-        }
+    return 0;
+}
+
+int upload_tiles(cxm_model *m, QMat &M, const std::vector<RowSrc> &rows) {
+    std::vector<uint8_t> buf;
+    build_tiles(M, rows, buf);
+    uint8_t *d = nullptr;
+    if (m->alloc(&d, buf.size())) return -1;
+    CU(cudaMemcpy(d, buf.data(), buf.size(), cudaMemcpyHostToDevice));
+    M.base = d;
+    m->slot_bytes = std::max<uint32_t>(m->slot_bytes, (uint32_t)(32 * M.bpb));
+    return 0;
+}
+
+// one GGUF matrix, rows in order (pairing ADJ) or RoPE order
+int upload_matrix(cxm_model *m, const Gguf &g, const TensorInfo &t, int pairing, int half, QMat *out) {
+    if (check_matrix(t)) return -1;
+    const int K = (int)t.dims[0], rows = (int)t.dims[1];
+    if (rows % 2 || (pairing == PAIR_ROPE && (half % 2 || rows % (2 * half)))) {
+        set_error("%s: %d rows do not pair", t.name.c_str(), rows);
+        return -1;
     }
-    uint8_t *da = nullptr, *ds = nullptr, *dd = nullptr;
-    if (m->alloc(&da, A.size())) return -1;
-    CU(cudaMemcpy(da, A.data(), A.size(), cudaMemcpyHostToDevice));
-    if (ps) {
-        if (m->alloc(&ds, S.size())) return -1;
-        CU(cudaMemcpy(ds, S.data(), S.size(), cudaMemcpyHostToDevice));
-    }
-    if (pd) {
-        if (m->alloc(&dd, D.size())) return -1;
-        CU(cudaMemcpy(dd, D.data(), D.size(), cudaMemcpyHostToDevice));
-    }
-    d.a = da;
-    d.s = ds;
-    d.d = dd;
-    *out = d;
+    QMat M = tiled_desc(t.type, K, rows);
+    const auto order = pairing == PAIR_ROPE ? rows_rope(g.data(t), rows, half) : rows_adj(g.data(t), rows);
+    if (upload_tiles(m, M, order)) return -1;
+    M.rows = rows;
+    *out = M;
     m->weight_bytes += (uint64_t)t.nbytes;
+    return 0;
+}
+
+// gate and up as one matrix of PAIR_TWO quads
+int upload_pair(cxm_model *m, const Gguf &g, const TensorInfo &a, const TensorInfo &b, QMat *out) {
+    if (check_matrix(a) || check_matrix(b)) return -1;
+    if (a.type != b.type || a.dims[0] != b.dims[0] || a.dims[1] != b.dims[1] || a.dims[1] % 2) {
+        set_error("%s and %s must have the same type and shape", a.name.c_str(), b.name.c_str());
+        return -1;
+    }
+    const int K = (int)a.dims[0], n = (int)a.dims[1];
+    QMat M = tiled_desc(a.type, K, 2 * n);
+    if (upload_tiles(m, M, rows_two(g.data(a), g.data(b), n))) return -1;
+    M.rows = 2 * n;
+    *out = M;
+    m->weight_bytes += (uint64_t)a.nbytes + (uint64_t)b.nbytes;
     return 0;
 }
 
@@ -183,14 +281,6 @@ int upload_vector(cxm_model *m, const Gguf &g, const TensorInfo &t, size_t n, fl
     return 0;
 }
 
-int sub_of(int type) { return (type == Q4K || type == Q5K) ? 32 : 16; }
-
-void set_need(MatvecParams &p, const DMat &a) {
-    if (sub_of(a.type) == 16) p.need16 = 1; else p.need32 = 1;
-}
-
-size_t matvec_smem(const MatvecParams &p) { return matvec_smem_bytes(p.K, p.need16, p.need32); }
-
 // Launch with programmatic dependent launch: the kernel may start while the
 // previous one in the stream finishes (each kernel calls griddep_wait()
 // before it touches data the previous one produced).
@@ -210,45 +300,21 @@ int launch_pdl(void (*kernel)(Args...), dim3 grid, dim3 block, size_t smem, cuda
     return 0;
 }
 
-int launch_matvec_on(cudaStream_t st, int sms, int *err, MatvecParams &p) {
-    p.total_units = 0;
-    for (int i = 0; i < p.nseg; i++) p.total_units += p.seg[i].units;
-    p.err = err;
-    const int blocks = std::max(1, std::min(p.total_units, sms));
-    return launch_pdl(k_matvec, dim3(blocks), dim3(kMvThreads), matvec_smem(p), st, p);
-}
-
-int launch_matvec(cxm_model *m, MatvecParams &p) { return launch_matvec_on(m->stream, m->sms, m->err, p); }
-
-Seg make_seg(const DMat &A, int pairing, int epi, float *out) {
-    Seg s{};
-    s.A = A;
-    s.B = A;
-    s.pairing = pairing;
-    s.epi = epi;
-    s.units = pairing == PAIR_TWO ? A.rows : A.rows / 2;
-    s.out = out;
-    return s;
-}
-
 size_t scores_smem(int hd) { return ((size_t)kScoreThreads * kKRow + (size_t)hd) * sizeof(float); }
 size_t out_smem(uint32_t max_pos) {
     return ((size_t)((max_pos + 3) & ~3u) + kVRing * kVChunk * kOutDims) * sizeof(float);
 }
+
+int g_decode_smem_max = 0;  // dynamic shared memory the decode kernel may use
 
 int set_kernel_smem_limits() {
     int dev = 0, optin = 0;
     CU(cudaGetDevice(&dev));
     CU(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
     cudaFuncAttributes fa_{};
-    CU(cudaFuncGetAttributes(&fa_, k_matvec));
-    const int mv_max = optin - (int)fa_.sharedSizeBytes;
-    if ((size_t)mv_max < matvec_smem_bytes(14336, 1, 1)) {
-        set_error("device allows %d bytes of shared memory per block; the matvec needs %zu", mv_max,
-                  matvec_smem_bytes(14336, 1, 1));
-        return -1;
-    }
-    CU(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, mv_max));
+    CU(cudaFuncGetAttributes(&fa_, k_decode));
+    g_decode_smem_max = optin - (int)fa_.sharedSizeBytes;
+    CU(cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, g_decode_smem_max));
     CU(cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     CU(cudaFuncSetAttribute(k_attn_out, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     return 0;
@@ -261,133 +327,197 @@ int launch_attention_on(cudaStream_t st, AttnParams &a) {
     return launch_pdl(k_attn_out, go, dim3(kOutThreads), out_smem((uint32_t)a.max_pos), st, a);
 }
 
-int launch_attention(cxm_model *m, cxm_cache *c, int layer) {
-    const cxm_config &cfg = m->cfg;
-    AttnParams a{};
-    a.q = m->q;
-    a.k = c->k + (size_t)layer * c->max_tokens * kv_dim(m);
-    a.v = c->v + (size_t)layer * c->max_tokens * kv_dim(m);
-    a.out = m->att;
-    a.scores = m->scores;
-    a.d_len = c->d_len;
-    a.H = cfg.n_head;
-    a.KV = cfg.n_head_kv;
-    a.hd = cfg.head_dim;
-    a.max_pos = (int)c->max_tokens;
-    a.score_stride = (cfg.ctx + 3) & ~3;
-    a.scale = 1.0f / sqrtf((float)cfg.head_dim);  // src/ops.rs:1287
-    a.err = m->err;
-    return launch_attention_on(m->stream, a);
+// ── decode programs ──
+MvSeg mv_seg(const QMat &M, int units, int pairing, int epi, float *out) {
+    MvSeg s{};
+    s.M = M;
+    s.units = units;
+    s.pairing = pairing;
+    s.epi = epi;
+    s.out = out;
+    return s;
 }
 
-// One token of src/forward.rs:375-505 on the device, for the token at
-// toks[*d_len]; ends by advancing *d_len (and, in STEP_GREEDY, writing the
-// argmax token at toks[*d_len + 1]).
-int enqueue_step(cxm_model *m, cxm_cache *c, int mode) {
-    const cxm_config &cfg = m->cfg;
-    const int D = cfg.dim, hd = cfg.head_dim, F = cfg.ffn;
-    const size_t kvd = kv_dim(m);
-    const bool logits = mode != STEP_PREFILL;
-    EmbedParams e{};
-    e.E = m->embd;
-    e.e32 = m->embd_f32;
-    e.toks = c->toks;
-    e.d_len = c->d_len;
-    e.dim = D;
-    e.vocab = cfg.vocab;
-    e.max_pos = (int)c->max_tokens;
-    e.x = m->x;
-    e.argmax_key = logits ? m->argmax_key : nullptr;
-    e.err = m->err;
-    if (launch_pdl(k_embed, dim3((D + 255) / 256), dim3(256), 0, m->stream, e)) return -1;
+Phase mv_phase(const std::vector<MvSeg> &segs, int K, int prologue, const float *in, const float *norm_w, float eps,
+               int barrier) {
+    Phase ph{};
+    ph.kind = PH_MATVEC;
+    ph.barrier = barrier;
+    MvPhase &P = ph.mv;
+    P.nseg = (int)segs.size();
+    for (int i = 0; i < P.nseg; i++) {
+        P.seg[i] = segs[i];
+        P.nquad += segs[i].M.nquad;
+        if (sub_of(segs[i].M.type) == 16) P.need16 = 1; else P.need32 = 1;
+    }
+    P.K = K;
+    P.ntile = (K / 256 + 7) / 8;
+    P.prologue = prologue;
+    P.in = in;
+    P.norm_w = norm_w;
+    P.eps = eps;
+    return ph;
+}
 
+size_t phase_region(const Phase &ph, int max_pos) {
+    if (ph.kind == PH_MATVEC)  // quantized activation + staged activation (+ norm weights)
+        return act_bytes(ph.mv.K, ph.mv.need16, ph.mv.need32) +
+               (size_t)ph.mv.K * sizeof(float) * (ph.mv.prologue == PRO_QUANT ? 1 : 2);
+    if (ph.kind == PH_SCORES) return scores_region(ph.at.P, ph.at.H / ph.at.KV, ph.at.hd);
+    if (ph.kind == PH_ATTN) return attn_region(max_pos);
+    return 0;
+}
+
+// positions per score item: the G query heads of a kv head share its K rows
+int score_positions(int G) { return std::max(1, std::min(64, 256 / std::max(1, G))); }
+
+// The step for the token at *d_len of cache c (src/forward.rs:375-505):
+// embedding (fused into layer 0's first prologue), then per layer q|k|v,
+// scores, softmax+output, o, gate|up, down; the output projection unless the
+// step only prefills; the commit.
+std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode) {
+    const cxm_config &cfg = m->cfg;
+    const int D = cfg.dim, hd = cfg.head_dim, F = cfg.ffn, H = cfg.n_head, KV = cfg.n_head_kv;
+    const size_t kvd = kv_dim(m);
+    std::vector<Phase> prog;
     for (int l = 0; l < cfg.n_layer; l++) {
         const Layer &L = m->layers[l];
         float *kl = c->k + (size_t)l * c->max_tokens * kvd, *vl = c->v + (size_t)l * c->max_tokens * kvd;
         {  // RMSNorm + quantize, q/k/v with bias, RoPE, KV append
-            MatvecParams p{};
-            p.nseg = 3;
-            p.seg[0] = make_seg(L.q, PAIR_ROPE, EPI_ROPE, m->q);
-            p.seg[0].half = hd / 2;
-            p.seg[0].bias = L.bq;
-            p.seg[1] = make_seg(L.k, PAIR_ROPE, EPI_ROPE, kl);
-            p.seg[1].half = hd / 2;
-            p.seg[1].bias = L.bk;
-            p.seg[1].at_pos = 1;
-            p.seg[1].pos_stride = (int)kvd;
-            p.seg[2] = make_seg(L.v, PAIR_ADJ, EPI_STORE, vl);
-            p.seg[2].bias = L.bv;
-            p.seg[2].at_pos = 1;
-            p.seg[2].pos_stride = (int)kvd;
-            p.K = D;
-            p.prologue = PRO_NORM;
-            p.in = m->x;
-            p.norm_w = L.attn_norm;
-            p.eps = cfg.eps;
-            p.d_len = c->d_len;
-            p.max_pos = (int)c->max_tokens;
-            p.rope_cos = m->rope_cos;
-            p.rope_sin = m->rope_sin;
-            set_need(p, L.q);
-            set_need(p, L.k);
-            set_need(p, L.v);
-            if (launch_matvec(m, p)) return -1;
+            MvSeg sq = mv_seg(L.q, D / 2, PAIR_ROPE, EPI_ROPE, m->q);
+            sq.half = hd / 2;
+            sq.bias = L.bq;
+            MvSeg sk = mv_seg(L.k, (int)kvd / 2, PAIR_ROPE, EPI_ROPE, kl);
+            sk.half = hd / 2;
+            sk.bias = L.bk;
+            sk.at_pos = 1;
+            sk.pos_stride = (int)kvd;
+            MvSeg sv = mv_seg(L.v, (int)kvd / 2, PAIR_ADJ, EPI_STORE, vl);
+            sv.bias = L.bv;
+            sv.at_pos = 1;
+            sv.pos_stride = (int)kvd;
+            Phase ph = mv_phase({sq, sk, sv}, D, l == 0 ? PRO_EMBED : PRO_NORM, m->x, L.attn_norm, cfg.eps, l > 0);
+            if (l == 0) {
+                ph.mv.E = m->embd;
+                ph.mv.e32 = m->embd_f32;
+                ph.mv.x_out = m->x;
+            }
+            prog.push_back(ph);
         }
-        if (launch_attention(m, c, l)) return -1;
-        {  // o_proj + residual
-            MatvecParams p{};
-            p.nseg = 1;
-            p.seg[0] = make_seg(L.o, PAIR_ADJ, EPI_RESID, m->x);
-            p.K = D;
-            p.prologue = PRO_QUANT;
-            p.in = m->att;
-            p.d_len = c->d_len;
-            set_need(p, L.o);
-            if (launch_matvec(m, p)) return -1;
+        AtPhase at{};
+        at.q = m->q;
+        at.k = kl;
+        at.v = vl;
+        at.out = m->att;
+        at.scores = m->scores;
+        at.H = H;
+        at.KV = KV;
+        at.hd = hd;
+        at.score_stride = (cfg.ctx + 3) & ~3;
+        at.P = score_positions(H / KV);
+        at.scale = 1.0f / sqrtf((float)hd);  // src/ops.rs:1287
+        {
+            Phase ph{};
+            ph.kind = PH_SCORES;
+            ph.barrier = 1;
+            ph.at = at;
+            prog.push_back(ph);
+            ph.kind = PH_ATTN;
+            prog.push_back(ph);
         }
-        {  // RMSNorm + quantize, gate/up, SiLU·up
-            MatvecParams p{};
-            p.nseg = 1;
-            p.seg[0] = make_seg(L.gate, PAIR_TWO, EPI_SWIGLU, m->h);
-            p.seg[0].B = L.up;
-            p.K = D;
-            p.prologue = PRO_NORM;
-            p.in = m->x;
-            p.norm_w = L.ffn_norm;
-            p.eps = cfg.eps;
-            p.d_len = c->d_len;
-            set_need(p, L.gate);
-            set_need(p, L.up);
-            if (launch_matvec(m, p)) return -1;
-        }
-        {  // down + residual
-            MatvecParams p{};
-            p.nseg = 1;
-            p.seg[0] = make_seg(L.down, PAIR_ADJ, EPI_RESID, m->x);
-            p.K = F;
-            p.prologue = PRO_QUANT;
-            p.in = m->h;
-            p.d_len = c->d_len;
-            set_need(p, L.down);
-            if (launch_matvec(m, p)) return -1;
-        }
+        // o_proj + residual; RMSNorm + gate/up + SwiGLU; down + residual
+        prog.push_back(mv_phase({mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->x)}, D, PRO_QUANT, m->att, nullptr, 0.0f, 1));
+        prog.push_back(mv_phase({mv_seg(L.gu, F, PAIR_TWO, EPI_SWIGLU, m->h)}, D, PRO_NORM, m->x, L.ffn_norm, cfg.eps, 1));
+        prog.push_back(mv_phase({mv_seg(L.down, D / 2, PAIR_ADJ, EPI_RESID, m->x)}, F, PRO_QUANT, m->h, nullptr, 0.0f, 1));
     }
-    if (logits) {  // final RMSNorm, output projection, argmax
-        MatvecParams p{};
-        p.nseg = 1;
-        p.seg[0] = make_seg(m->out, PAIR_ADJ, EPI_LOGITS, m->logits);
-        p.K = D;
-        p.prologue = PRO_NORM;
-        p.in = m->x;
-        p.norm_w = m->out_norm;
-        p.eps = cfg.eps;
-        p.d_len = c->d_len;
-        p.argmax_key = m->argmax_key;
-        set_need(p, m->out);
-        if (launch_matvec(m, p)) return -1;
+    if (mode != STEP_PREFILL)  // final RMSNorm, output projection, argmax
+        prog.push_back(mv_phase({mv_seg(m->out, cfg.vocab / 2, PAIR_ADJ, EPI_LOGITS, m->logits)}, D, PRO_NORM, m->x,
+                                m->out_norm, cfg.eps, 1));
+    Phase cm{};
+    cm.kind = PH_COMMIT;
+    cm.barrier = 1;
+    prog.push_back(cm);
+    return prog;
+}
+
+int upload_program(const std::vector<Phase> &ph, int max_pos, Program *out) {
+    Program p;
+    p.n = (int)ph.size();
+    for (const Phase &x : ph) p.region = std::max(p.region, phase_region(x, max_pos));
+    p.region = (p.region + 127) & ~(size_t)127;
+    CU(cudaMalloc(&p.d, ph.size() * sizeof(Phase)));
+    CU(cudaMemcpy(p.d, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+    *out = p;
+    return 0;
+}
+
+// Shared memory of a decode launch: per-warp tile rings (as many slots as
+// fit, at most kMaxSlots), the activation/attention region, two staged
+// phase descriptors.
+int decode_geometry(uint32_t slot_bytes, const Program &p, DecodeArgs &a, size_t *smem) {
+    const size_t fixed = p.region + 2 * sizeof(Phase) + 128;
+    const uint32_t slot = (std::max<uint32_t>(slot_bytes, 16) + 127) & ~127u;
+    const long long room = (long long)g_decode_smem_max - (long long)fixed;
+    const int ns = (int)std::min<long long>(kMaxSlots, room > 0 ? room / ((long long)kDW * slot) : 0);
+    if (ns < 2) {
+        set_error("the decode kernel needs %zu bytes of shared memory; the device allows %d", fixed + 2 * kDW * slot,
+                  g_decode_smem_max);
+        return -1;
     }
-    return launch_pdl(k_commit, dim3(1), dim3(32), 0, m->stream, c->d_len, c->toks,
-                      (const unsigned long long *)m->argmax_key, mode == STEP_GREEDY ? 1 : 0, (int)c->max_tokens + 1);
+    a.ring_slots = ns;
+    a.slot_bytes = slot;
+    a.region_bytes = (uint32_t)p.region;
+    // The ring alone keeps HBM busy; an L2 prefetch window deepens the memory
+    // queues that every latency-bound access of the step (activations,
+    // barriers) then waits behind.
+    a.prefetch_tiles = 0;
+    *smem = (size_t)kDW * ns * slot + fixed;
+    return 0;
+}
+
+// one decode launch: zero the barrier counter, then the cooperative kernel
+// (every CTA resident at once: the grid barriers need it)
+int launch_decode(int sms, cudaStream_t st, const DecodeArgs &a, size_t smem) {
+    CU(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), st));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms);
+    cfg.blockDim = dim3(kDecodeThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CU(cudaLaunchKernelEx(&cfg, k_decode, a));
+    return 0;
+}
+
+DecodeArgs base_args(cxm_model *m) {
+    DecodeArgs a{};
+    a.bar = m->bar;
+    a.err = m->err;
+    a.vocab = m->cfg.vocab;
+    a.argmax_key = m->argmax_key;
+    a.rope_cos = m->rope_cos;
+    a.rope_sin = m->rope_sin;
+    return a;
+}
+
+int enqueue_step(cxm_model *m, cxm_cache *c, int mode) {
+    Program &p = c->prog[mode];
+    if (!p.d && upload_program(step_program(m, c, mode), (int)c->max_tokens, &p)) return -1;
+    DecodeArgs a = base_args(m);
+    a.prog = p.d;
+    a.nphase = p.n;
+    a.d_len = c->d_len;
+    a.toks = c->toks;
+    a.max_pos = (int)c->max_tokens;
+    a.write_token = mode == STEP_GREEDY;
+    a.commit = 1;
+    size_t smem = 0;
+    if (decode_geometry(m->slot_bytes, p, a, &smem)) return -1;
+    return launch_decode(m->sms, m->stream, a, smem);
 }
 
 int get_graph(cxm_model *m, cxm_cache *c, int mode, cudaGraphExec_t *out) {
@@ -395,6 +525,7 @@ int get_graph(cxm_model *m, cxm_cache *c, int mode, cudaGraphExec_t *out) {
         *out = c->graph[mode];
         return 0;
     }
+    if (!c->prog[mode].d && upload_program(step_program(m, c, mode), (int)c->max_tokens, &c->prog[mode])) return -1;
     cudaGraph_t g = nullptr;
     CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int rc = enqueue_step(m, c, mode);
@@ -431,7 +562,9 @@ int check_err(cxm_model *m) {
     CU(cudaMemcpy(&e, m->err, 4, cudaMemcpyDeviceToHost));
     if (e) {
         CU(cudaMemset(m->err, 0, 4));
-        set_error("device reported %s", (e & ERR_TOKEN) ? "a token beyond the vocabulary" : "a position beyond the cache");
+        set_error("device reported %s", (e & ERR_TOKEN)      ? "a token beyond the vocabulary"
+                                        : (e & ERR_POSITION) ? "a position beyond the cache"
+                                                             : "a wait that timed out");
         return -1;
     }
     return 0;
@@ -507,11 +640,11 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
     if (embd->type == F32) {
         if (upload_vector(m.get(), g, *embd, (size_t)cfg.vocab * cfg.dim, &m->embd_f32)) return -1;
         m->embd.type = 0;
-    } else if (upload_matrix(m.get(), g, *embd, &m->embd)) {
+    } else if (upload_matrix(m.get(), g, *embd, PAIR_ADJ, 0, &m->embd)) {
         return -1;
     }
     if (outw) {
-        if (upload_matrix(m.get(), g, *outw, &m->out)) return -1;
+        if (upload_matrix(m.get(), g, *outw, PAIR_ADJ, 0, &m->out)) return -1;
     } else {
         if (embd->type == F32) {
             set_error("a tied F32 embedding table has no device output kernel");
@@ -529,27 +662,29 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
             if (!t) set_error("missing tensor %s", n.c_str());
             return t;
         };
-        const TensorInfo *t;
+        const TensorInfo *t, *t2;
+        const int half = (int)hd / 2;
         if (!(t = T("attn_norm.weight")) || upload_vector(m.get(), g, *t, cfg.dim, &L.attn_norm)) return -1;
-        if (!(t = T("attn_q.weight")) || upload_matrix(m.get(), g, *t, &L.q)) return -1;
+        if (!(t = T("attn_q.weight")) || upload_matrix(m.get(), g, *t, PAIR_ROPE, half, &L.q)) return -1;
         if (!(t = T("attn_q.bias")) || upload_vector(m.get(), g, *t, cfg.dim, &L.bq)) return -1;
-        if (!(t = T("attn_k.weight")) || upload_matrix(m.get(), g, *t, &L.k)) return -1;
+        if (!(t = T("attn_k.weight")) || upload_matrix(m.get(), g, *t, PAIR_ROPE, half, &L.k)) return -1;
         if (!(t = T("attn_k.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bk)) return -1;
-        if (!(t = T("attn_v.weight")) || upload_matrix(m.get(), g, *t, &L.v)) return -1;
+        if (!(t = T("attn_v.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, &L.v)) return -1;
         if (!(t = T("attn_v.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bv)) return -1;
-        if (!(t = T("attn_output.weight")) || upload_matrix(m.get(), g, *t, &L.o)) return -1;
+        if (!(t = T("attn_output.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, &L.o)) return -1;
         if (!(t = T("ffn_norm.weight")) || upload_vector(m.get(), g, *t, cfg.dim, &L.ffn_norm)) return -1;
-        if (!(t = T("ffn_gate.weight")) || upload_matrix(m.get(), g, *t, &L.gate)) return -1;
-        if (!(t = T("ffn_up.weight")) || upload_matrix(m.get(), g, *t, &L.up)) return -1;
-        if (!(t = T("ffn_down.weight")) || upload_matrix(m.get(), g, *t, &L.down)) return -1;
+        if (!(t = T("ffn_gate.weight")) || !(t2 = T("ffn_up.weight")) || upload_pair(m.get(), g, *t, *t2, &L.gu))
+            return -1;
+        if (!(t = T("ffn_down.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, &L.down)) return -1;
         if (L.q.rows != cfg.dim || L.k.rows != (int)kvd || L.v.rows != (int)kvd || L.o.rows != cfg.dim ||
-            L.gate.rows != L.up.rows || L.down.K != L.gate.rows || L.down.rows != cfg.dim) {
+            L.q.K != cfg.dim || L.k.K != cfg.dim || L.v.K != cfg.dim || L.o.K != cfg.dim || L.gu.K != cfg.dim ||
+            L.down.K != L.gu.rows / 2 || L.down.rows != cfg.dim) {
             set_error("layer %d: matrix shapes do not match the config", i);
             return -1;
         }
         m->layers.push_back(L);
     }
-    cfg.ffn = m->layers.empty() ? 0 : m->layers[0].gate.rows;
+    cfg.ffn = m->layers.empty() ? 0 : m->layers[0].gu.rows / 2;
     // RoPE tables exactly as src/ops.rs:1108-1129 (f32 frequency, f64 angle)
     {
         const int half = cfg.head_dim / 2;
@@ -570,13 +705,21 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
     // activations
     if (m->alloc(&m->x, cfg.dim) || m->alloc(&m->q, cfg.dim) || m->alloc(&m->att, cfg.dim) ||
         m->alloc(&m->h, std::max(cfg.ffn, 1)) || m->alloc(&m->logits, cfg.vocab) || m->alloc(&m->err, 1) ||
-        m->alloc(&m->argmax_key, 1) || m->alloc(&m->scores, (size_t)cfg.n_head * ((cfg.ctx + 3) & ~3)))
+        m->alloc(&m->bar, 1) || m->alloc(&m->argmax_key, 1) ||
+        m->alloc(&m->scores, (size_t)cfg.n_head * ((cfg.ctx + 3) & ~3)))
         return -1;
     CU(cudaMemset(m->err, 0, sizeof(int)));
     if (set_kernel_smem_limits()) return -1;
-    if (out_smem((uint32_t)cfg.ctx) > 200 * 1024 || cfg.head_dim % 16 || cfg.head_dim > kKRow - 4) {
-        set_error("context %d / head_dim %d are beyond the attention kernels' shared-memory layout", cfg.ctx,
-                  cfg.head_dim);
+    if (out_smem((uint32_t)cfg.ctx) > 200 * 1024 || cfg.head_dim % 16 || cfg.head_dim > kKRow - 4 ||
+        cfg.vocab % 2 || cfg.dim % 4) {
+        set_error("context %d / head_dim %d / vocab %d are beyond the decode kernels' layouts", cfg.ctx,
+                  cfg.head_dim, cfg.vocab);
+        return -1;
+    }
+    int per_sm = 0;
+    CU(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode, kDecodeThreads, (size_t)g_decode_smem_max));
+    if (per_sm < 1) {
+        set_error("the decode kernel does not fit an SM");
         return -1;
     }
     CU(cudaDeviceSynchronize());
@@ -906,37 +1049,50 @@ extern "C" int cxm_debug_subblock_sums(int type, const uint8_t *row, const int8_
 
 extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint32_t k, const float *x, float *y) {
     if (need_device()) return -1;
-    if (!w || !x || !y || rows % 2) {
-        set_error("bad arguments (rows must be even)");
+    if (!w || !x || !y || rows % 2 || rows == 0 || !is_kquant(type) || k == 0 || k % 256) {
+        set_error("bad arguments (k-quant type, k a multiple of 256, rows even)");
         return -1;
     }
-    DevBuf b[3], dx, dy, dlen;
-    DMat W;
-    if (dev_matrix_from_host(type, w, rows, k, b, &W)) return -1;
+    // the decode kernel on a one-phase program: quantize x, W·x, store
+    QMat M = tiled_desc(type, (int)k, (int)rows);
+    std::vector<uint8_t> tiles;
+    build_tiles(M, rows_adj(w, (int)rows), tiles);
+    DevBuf dw, dx, dy, derr, dbar, dprog;
+    CU(cudaMalloc(&dw.p, tiles.size()));
+    CU(cudaMemcpy(dw.p, tiles.data(), tiles.size(), cudaMemcpyHostToDevice));
+    M.base = (const uint8_t *)dw.p;
+    M.rows = (int)rows;
     CU(cudaMalloc(&dx.p, (size_t)k * 4));
     CU(cudaMalloc(&dy.p, (size_t)rows * 4));
-    CU(cudaMemcpy(dx.p, x, (size_t)k * 4, cudaMemcpyHostToDevice));
-    MatvecParams p{};
-    p.nseg = 1;
-    p.seg[0] = make_seg(W, PAIR_ADJ, EPI_STORE, (float *)dy.p);
-    p.total_units = p.seg[0].units;
-    p.K = (int)k;
-    p.prologue = PRO_QUANT;
-    p.in = (const float *)dx.p;
-    set_need(p, W);
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (set_kernel_smem_limits()) return -1;
-    DevBuf derr;
     CU(cudaMalloc(&derr.p, 4));
+    CU(cudaMalloc(&dbar.p, 4));
+    CU(cudaMemcpy(dx.p, x, (size_t)k * 4, cudaMemcpyHostToDevice));
     CU(cudaMemset(derr.p, 0, 4));
-    if (launch_matvec_on(0, sms, (int *)derr.p, p)) return -1;
+    Phase ph = mv_phase({mv_seg(M, (int)rows / 2, PAIR_ADJ, EPI_STORE, (float *)dy.p)}, (int)k, PRO_QUANT,
+                        (const float *)dx.p, nullptr, 0.0f, 0);
+    Program prog;
+    prog.n = 1;
+    prog.region = (phase_region(ph, 0) + 127) & ~(size_t)127;
+    CU(cudaMalloc(&dprog.p, sizeof(Phase)));
+    CU(cudaMemcpy(dprog.p, &ph, sizeof(Phase), cudaMemcpyHostToDevice));
+    prog.d = (Phase *)dprog.p;
+    int dev = 0, sms = 148;
+    CU(cudaGetDevice(&dev));
+    CU(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    if (set_kernel_smem_limits()) return -1;
+    DecodeArgs a{};
+    a.prog = prog.d;
+    a.nphase = 1;
+    a.bar = (unsigned *)dbar.p;
+    a.err = (int *)derr.p;
+    size_t smem = 0;
+    if (decode_geometry((uint32_t)(32 * M.bpb), prog, a, &smem)) return -1;
+    if (launch_decode(sms, 0, a, smem)) return -1;
     CU(cudaDeviceSynchronize());
     int e = 0;
     CU(cudaMemcpy(&e, derr.p, 4, cudaMemcpyDeviceToHost));
     if (e) {
-        set_error("matvec kernel reported error flags %d", e);
+        set_error("decode kernel reported error flags %d", e);
         return -1;
     }
     CU(cudaMemcpy(y, dy.p, (size_t)rows * 4, cudaMemcpyDeviceToHost));
@@ -1012,9 +1168,8 @@ extern "C" int cxm_debug_expf(const float *x, float *y, uint64_t n) {
 
 // ── measurement hooks ──
 
-// embed, per layer (q|k|v, attention scores, attention output, o, gate|up,
-// down), output projection, commit
-extern "C" int cxm_step_launches(const cxm_model *m) { return m ? 3 + 6 * m->cfg.n_layer : 0; }
+// the whole step is one launch of the decode kernel
+extern "C" int cxm_step_launches(const cxm_model *m) { return m ? 1 : 0; }
 
 extern "C" int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, float *ms_total) {
     if (!m || !c || !ms_total || c->m != m) {
@@ -1051,63 +1206,46 @@ extern "C" int cxm_bench_matvec(cxm_model *m, uint32_t reps, float *ms_per_launc
     }
     CU(cudaSetDevice(m->device));
     const cxm_config &cfg = m->cfg;
-    auto launch = [&](int l) -> int {
-        const Layer &L = m->layers[(size_t)l % m->layers.size()];
-        MatvecParams p{};
-        p.nseg = 1;
-        p.seg[0] = make_seg(L.gate, PAIR_TWO, EPI_SWIGLU, m->h);
-        p.seg[0].B = L.up;
-        p.K = cfg.dim;
-        p.prologue = PRO_NORM;
-        p.in = m->x;
-        p.norm_w = L.ffn_norm;
-        p.eps = cfg.eps;
-        set_need(p, L.gate);
-        set_need(p, L.up);
-        return launch_matvec(m, p);
-    };
-    for (int i = 0; i < 3; i++)
-        if (launch(i)) return -1;
-    // the launches are captured into one graph, as the decode step runs, so
-    // host launch overhead is not part of the device time
-    cudaGraph_t graph = nullptr;
-    CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-    int bad = 0;
-    for (uint32_t i = 0; i < reps && !bad; i++) bad = launch((int)i);
-    const cudaError_t ce = cudaStreamEndCapture(m->stream, &graph);
-    if (bad || ce != cudaSuccess) {
-        if (graph) cudaGraphDestroy(graph);
-        if (!bad) set_error("graph capture failed: %s", cudaGetErrorString(ce));
-        return -1;
+    // `reps` gate|up phases of the decode kernel in one launch, cycling over
+    // the layers so every phase streams its own weights from HBM, each
+    // behind a grid barrier as in the step
+    std::vector<Phase> ph;
+    for (uint32_t i = 0; i < reps; i++) {
+        const Layer &L = m->layers[i % m->layers.size()];
+        ph.push_back(mv_phase({mv_seg(L.gu, cfg.ffn, PAIR_TWO, EPI_SWIGLU, m->h)}, cfg.dim, PRO_NORM, m->x, L.ffn_norm,
+                              cfg.eps, i > 0));
     }
-    cudaGraphExec_t exec = nullptr;
-    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    if (ie != cudaSuccess) {
-        set_error("graph instantiate failed: %s", cudaGetErrorString(ie));
-        return -1;
-    }
+    Program prog;
+    if (upload_program(ph, 0, &prog)) return -1;
+    struct Free {
+        Phase *p;
+        ~Free() { cudaFree(p); }
+    } f{prog.d};
+    DecodeArgs a = base_args(m);
+    a.prog = prog.d;
+    a.nphase = prog.n;
+    size_t smem = 0;
+    if (decode_geometry(m->slot_bytes, prog, a, &smem)) return -1;
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     float ms = 0;
-    cudaError_t re = cudaGraphLaunch(exec, m->stream);  // warm-up replay
-    if (re == cudaSuccess) re = cudaEventCreate(&e0);
+    if (launch_decode(m->sms, m->stream, a, smem)) return -1;  // warm-up
+    cudaError_t re = cudaEventCreate(&e0);
     if (re == cudaSuccess) re = cudaEventCreate(&e1);
     if (re == cudaSuccess) re = cudaEventRecord(e0, m->stream);
-    if (re == cudaSuccess) re = cudaGraphLaunch(exec, m->stream);
-    if (re == cudaSuccess) re = cudaEventRecord(e1, m->stream);
-    if (re == cudaSuccess) re = cudaEventSynchronize(e1);
-    if (re == cudaSuccess) re = cudaEventElapsedTime(&ms, e0, e1);
+    int rc = re == cudaSuccess ? launch_decode(m->sms, m->stream, a, smem) : 0;
+    if (re == cudaSuccess && !rc) re = cudaEventRecord(e1, m->stream);
+    if (re == cudaSuccess && !rc) re = cudaEventSynchronize(e1);
+    if (re == cudaSuccess && !rc) re = cudaEventElapsedTime(&ms, e0, e1);
     if (e0) cudaEventDestroy(e0);
     if (e1) cudaEventDestroy(e1);
-    cudaGraphExecDestroy(exec);
+    if (rc) return -1;
     if (re != cudaSuccess) {
         set_error("matvec timing failed: %s", cudaGetErrorString(re));
         return -1;
     }
     *ms_per_launch = ms / (float)reps;
     const Layer &L = m->layers[0];
-    *bytes_per_launch = (uint64_t)L.gate.rows * (uint64_t)(L.gate.K / 256) * (uint64_t)bytes_per_block(L.gate.type) +
-                        (uint64_t)L.up.rows * (uint64_t)(L.up.K / 256) * (uint64_t)bytes_per_block(L.up.type);
+    *bytes_per_launch = (uint64_t)L.gu.rows * (uint64_t)L.gu.nblk * (uint64_t)L.gu.bpb;
     return check_err(m);
 }
 

@@ -42,8 +42,9 @@ typedef struct {
 /* ── model ─────────────────────────────────────────────────────────────── */
 
 /* Modelo::abrir (src/forward.rs:187-266): parse the GGUF, upload every tensor
- * to HBM once (k-quant blocks repacked into 16-byte-aligned planes) and build
- * the RoPE tables (src/ops.rs:1108-1129). */
+ * to HBM once (k-quant blocks regrouped, bytes unchanged, into the decode
+ * kernel's tiles of 4 rows x 8 super-blocks) and build the RoPE tables
+ * (src/ops.rs:1108-1129). */
 int  cxm_model_open(const char *gguf_path, int device, cxm_model **out);
 int  cxm_model_config(const cxm_model *m, cxm_config *out);
 /* bytes of weights resident on the device (the per-token weight stream) */
@@ -84,8 +85,9 @@ int cxm_sample(cxm_model *m, cxm_sampler *s, uint32_t *token_out);
 
 /* Modelo::generar (src/forward.rs:533-559): forward the prompt, then
  * sample -> forward one token, up to max_new tokens, stopping at the model's
- * eos and before the context overflows. The per-token step runs as one
- * replayed CUDA graph; position and token live in device memory. */
+ * eos and before the context overflows. The per-token step is one launch of
+ * a persistent kernel, replayed as a CUDA graph; position and token live in
+ * device memory. */
 int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, uint32_t n_prompt, uint32_t max_new,
                  cxm_sampler *s, uint32_t *out, uint32_t *n_out);
 
@@ -142,12 +144,13 @@ int cxm_debug_expf(const float *x, float *y, uint64_t n);
  * Inputs stay resident; the cache grows by `steps`. */
 int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, float *ms_total);
 
-/* Average device time of one launch of the gate/up matvec (the largest
- * kernel of a layer), cycling over the layers so every launch streams its
- * own weights from HBM. `bytes_per_launch` = GGUF bytes of gate + up. */
+/* Average device time of one gate|up matvec phase (the largest of a layer)
+ * of the decode kernel: `reps` such phases, cycling over the layers so every
+ * phase streams its own weights from HBM, run in one launch behind grid
+ * barriers as in the step. `bytes_per_launch` = GGUF bytes of gate + up. */
 int cxm_bench_matvec(cxm_model *m, uint32_t reps, float *ms_per_launch, uint64_t *bytes_per_launch);
 
-/* Number of kernel launches in one greedy decode step. */
+/* Number of kernel launches (of this library's kernels) in one decode step. */
 int cxm_step_launches(const cxm_model *m);
 
 /* ── synthetic models (src/daiss.rs:422-586 + src/quant_kquants.rs) ────── */
