@@ -8,21 +8,25 @@
 //   the commit of the position/token.
 //
 // Dependent phases are separated by a grid barrier (bounded spin). Weights
-// never depend on activations, so one producer warp per CTA streams the weight
-// tiles of every matvec phase of the whole step, in the order the consumers
-// will need them, with 1-D bulk copies (the TMA unit; no multicast) into
-// per-warp shared-memory rings — across phase boundaries and while the
-// consumers sit in barriers or attention — and keeps an L2 prefetch running
-// further ahead. HBM streaming therefore never waits for the dependency chain
-// except when the rings and the prefetch window are full.
+// never depend on activations, so every warp streams its own weight tiles of
+// the whole step, in the order it will need them, with coalesced cp.async
+// copies into a private shared-memory ring that runs ahead across phase
+// boundaries — while the warps sit in barriers, prologues or attention. (Many
+// small 1-D bulk copies from one thread per SM top out near 4.3 TB/s on B200;
+// warp-wide 16-byte copies stream at over 7.) A prologue's inputs (the
+// activation and the norm weights) come in as two 1-D bulk copies.
 //
-// Weights are stored as "quad tiles": a quad is 4 rows (two output pairs: the
-// rows an epilogue combines sit in one quad), and a tile is one quad x up to 8
-// super-blocks, stored lane-interleaved (lane = 4*block + row) in 16-byte
-// chunks so a warp's 32 lanes read consecutive 16-byte words. A warp owns a
-// quad at a time: lane (block, row) forms that super-block's sub-block terms,
-// and each row's running total visits the blocks in order (the reference's
-// sequential sum, src/ops.rs:435-522 with src/kernels/scalar.rs:132-324).
+// Weights are stored as tiles of R rows x LPR super-blocks (R*LPR = 32: one
+// warp's lanes, lane = R*block + row), lane-interleaved in 16-byte chunks so
+// the 32 lanes read consecutive 16-byte words. LPR ("lanes per row") is
+// chosen per matrix: 1 for the tall matrices (a lane owns a row and adds its
+// terms as it forms them), up to 32 for the short ones, whose rows would
+// otherwise leave most warps idle. A warp owns a group of R rows at a time:
+// lane (block, row) forms that super-block's sub-block terms, and each row's
+// running total visits the blocks in order, handed from lane to lane (the
+// reference's sequential sum, src/ops.rs:435-522 with
+// src/kernels/scalar.rs:132-324). The rows an epilogue combines (a RoPE pair,
+// gate and up) are adjacent rows of a group.
 #pragma once
 
 #include "expf_glibc.h"
@@ -32,33 +36,37 @@
 
 namespace cxm {
 
-// ── quad-tiled k-quant matrix ──
-// Quad q starts at base + q*quad_stride; its tile t (super-blocks 8t..8t+nb,
-// nb = min(8, nblk - 8t)) starts 32*t*bpb bytes further. Inside a tile of
-// L = 4*nb lanes (lane = 4*block + row):
+// ── tiled k-quant matrix ──
+// Group g (rows g*R .. g*R+R-1) starts at base + g*group_stride; its tile t
+// (super-blocks t*LPR .. t*LPR+nb, nb = min(LPR, nblk - t*LPR)) starts
+// 32*t*bpb bytes further. Inside a tile of L = R*nb lanes (lane = R*block +
+// row):
 //   plane A  [chunk c][lane] 16-byte units, c < a_chunks(type)
 //   plane S  [lane] s_bytes(type)        (Q6_K 16, Q3_K 12, Q2_K 16)
 //   plane D  [lane] d_bytes(type)        (Q6_K 2, Q3_K 2, Q2_K 4)
-// so a tile holds exactly L GGUF blocks (L*bpb bytes). quad_stride rounds
-// 4*nblk*bpb up to 16 bytes so every tile starts 16-byte aligned.
+// so a tile holds exactly L GGUF blocks (L*bpb bytes). group_stride rounds
+// R*nblk*bpb up to 16 bytes so every tile starts 16-byte aligned.
 struct QMat {
     const uint8_t *base;
-    int type, rows, K, nblk, nquad, bpb;
-    uint32_t quad_stride;
+    int type, rows, K, nblk, ngroup, bpb;
+    int lpr, rpt;  // lanes (super-blocks) per row in a tile; rows per tile = 32 / lpr
+    uint32_t group_stride;
 };
 
 __host__ __device__ inline int a_chunks(int t) { return plane_a_bytes(t) / 16; }
-__host__ __device__ inline int tile_nb(int nblk, int t) { return nblk - 8 * t < 8 ? nblk - 8 * t : 8; }
-__host__ __device__ inline uint32_t tile_copy_bytes(int nb, int bpb) { return (uint32_t)((4 * nb * bpb + 15) & ~15); }
-__host__ __device__ inline size_t tile_offset(const QMat &M, int q, int t) {
-    return (size_t)q * M.quad_stride + (size_t)t * 32 * (size_t)M.bpb;
+__host__ __device__ inline int tile_nb(int nblk, int lpr, int t) { return nblk - lpr * t < lpr ? nblk - lpr * t : lpr; }
+__host__ __device__ inline uint32_t tile_copy_bytes(int rpt, int nb, int bpb) {
+    return (uint32_t)((rpt * nb * bpb + 15) & ~15);
+}
+__host__ __device__ inline size_t tile_offset(const QMat &M, int g, int t) {
+    return (size_t)g * M.group_stride + (size_t)t * 32 * (size_t)M.bpb;
 }
 
 // GGUF byte k of super-block b of tiled row r (row order as stored).
 __device__ inline uint8_t qm_block_byte(const QMat &M, int r, int b, int k) {
-    const int q = r >> 2, sl = r & 3, t = b >> 3, bl = b & 7, nb = tile_nb(M.nblk, t), L = 4 * nb;
-    const int lane = 4 * bl + sl;
-    const uint8_t *tile = M.base + tile_offset(M, q, t);
+    const int g = r / M.rpt, sl = r % M.rpt, t = b / M.lpr, bl = b % M.lpr, nb = tile_nb(M.nblk, M.lpr, t);
+    const int L = M.rpt * nb, lane = M.rpt * bl + sl;
+    const uint8_t *tile = M.base + tile_offset(M, g, t);
     const int pa = plane_a_bytes(M.type), ps = plane_s_bytes(M.type), pd = plane_d_bytes(M.type);
     int lo_a = 0, lo_s = pa, lo_d = pa + ps;  // GGUF offsets of the parts
     if (M.type == 10) {                        // Q2_K: scales, qs, d|dmin
@@ -135,7 +143,7 @@ enum PhaseKind : int { PH_MATVEC = 0, PH_SCORES = 1, PH_ATTN = 2, PH_COMMIT = 3 
 
 struct MvSeg {
     QMat M;
-    int units;                // output units (row pairs); padded quads hold more
+    int units;                // output units (row pairs); padded groups hold more
     int pairing, epi, half;   // Pairing, Epilogue; half = head_dim/2 for PAIR_ROPE
     int at_pos, pos_stride;   // out += pos*pos_stride (K/V cache rows)
     const float *bias;
@@ -144,7 +152,7 @@ struct MvSeg {
 
 struct MvPhase {
     MvSeg seg[3];
-    int nseg, nquad, K, ntile;
+    int nseg, ngroup, K, ntile;  // segments share K and the tile shape (lpr)
     int prologue, need16, need32;
     const float *in, *norm_w;
     float eps;
@@ -178,14 +186,13 @@ struct DecodeArgs {
     unsigned long long *argmax_key;
     const float *rope_cos, *rope_sin;
     int write_token, commit;  // commit: toks[len+1] = argmax (write_token), len += 1
-    int ring_slots;           // tiles in flight per consumer warp (2..kMaxSlots)
+    int ring_slots;           // tile slots per warp ring (2..kMaxSlots)
     uint32_t slot_bytes, region_bytes;
-    int prefetch_tiles;       // L2 prefetch lead of the producer, in tiles
 };
 
-constexpr int kDW = 8;                       // consumer warps
-constexpr int kDecodeThreads = (kDW + 1) * 32;
-constexpr int kMaxSlots = 4;
+constexpr int kDW = 8;                       // warps
+constexpr int kDecodeThreads = kDW * 32;
+constexpr int kMaxSlots = 4;                 // tiles per warp ring
 constexpr int kTermMax = 16;
 
 __device__ __forceinline__ void dsync() { asm volatile("bar.sync 1, %0;" ::"n"(kDW * 32) : "memory"); }
@@ -430,85 +437,109 @@ __device__ void unit_epilogue(const DecodeArgs &A, const MvSeg &g, int r0, int r
     }
 }
 
-// quad range of this CTA in a matvec phase: contiguous and balanced
-__device__ __forceinline__ void cta_quads(int nquad, int &qb, int &qe) {
-    qb = (int)(((long long)blockIdx.x * nquad) / gridDim.x);
-    qe = (int)(((long long)(blockIdx.x + 1) * nquad) / gridDim.x);
+// group range of this CTA in a matvec phase: contiguous and balanced
+__device__ __forceinline__ void cta_groups(int ngroup, int &qb, int &qe) {
+    qb = (int)(((long long)blockIdx.x * ngroup) / gridDim.x);
+    qe = (int)(((long long)(blockIdx.x + 1) * ngroup) / gridDim.x);
 }
 
-// ── the producer's walk over the step's weight tiles ──
-// Both the bulk-copy cursor and the L2-prefetch cursor run this same walk:
-// matvec phases in program order; in each, this CTA's quads in rounds of kDW
-// (quad qb + 8k + w belongs to consumer warp w), each round tile-major, so a
-// warp receives its quads' tiles in the order it consumes them.
-struct Sched {
-    int ph, nseg, ntile, nblk, qb, qe, k, t, w;
-    int segq[3], bpb[3];
-    uint32_t qstride[3];
-    const uint8_t *base[3];
+// ── a warp's walk over its weight tiles ──
+// Every consumer warp streams its own tiles: matvec phases in program order;
+// in each, its row groups qb + warp + 8k of the CTA's range [qb, qe), tile by
+// tile. It copies them with 16-byte cp.async (a warp moves 512 contiguous
+// bytes per instruction) into a private ring, running ring_slots - 1 tiles
+// ahead of its compute, into the next phases too: the weights never depend
+// on the activations, so the copies overlap barriers, prologues and
+// attention.
+struct Feed {
+    int ph, q, qe, t;  // next tile: phase, phase-global group, tile
+    int ntile, nblk, lpr, rpt;
+    int n0, n1;        // groups of segments 0 and 1 (segment 2 takes the rest)
+    int p0, p1, p2;    // bytes per super-block
+    uint32_t g0, g1, g2;  // group strides
+    const uint8_t *b0, *b1, *b2;
 };
 
-struct Item {
-    const uint8_t *src;
-    uint32_t bytes;
-    int warp;
-};
-
-__device__ inline void sched_init(Sched &s) {
-    s.ph = -1;
-    s.k = s.t = s.w = 0;
-    s.qb = s.qe = 0;
-    s.ntile = 0;
-}
-
-__device__ inline bool sched_next(const DecodeArgs &A, Sched &s, Item &it) {
-    for (;;) {
-        if (s.ph >= A.nphase) return false;
-        if (s.ph >= 0) {
-            while (s.qb + kDW * s.k < s.qe) {
-                while (s.t < s.ntile) {
-                    while (s.w < kDW) {
-                        const int w = s.w++;
-                        int q = s.qb + kDW * s.k + w;
-                        if (q >= s.qe) continue;
-                        int j = 0;
-                        while (j < s.nseg - 1 && q >= s.segq[j]) q -= s.segq[j++];
-                        const int nb = tile_nb(s.nblk, s.t);
-                        it.src = s.base[j] + (size_t)q * s.qstride[j] + (size_t)s.t * 32 * s.bpb[j];
-                        it.bytes = tile_copy_bytes(nb, s.bpb[j]);
-                        it.warp = w;
-                        return true;
-                    }
-                    s.w = 0;
-                    s.t++;
-                }
-                s.t = 0;
-                s.k++;
-            }
+// position the walk at the first group of this warp in phase >= f.ph
+__device__ inline void feed_phase(const DecodeArgs &A, Feed &f, int warp) {
+    for (; f.ph < A.nphase; f.ph++) {
+        if (__ldg(&A.prog[f.ph].kind) != PH_MATVEC) continue;
+        const MvPhase &P = A.prog[f.ph].mv;
+        int qb, qe;
+        cta_groups(__ldg(&P.ngroup), qb, qe);
+        if (qb + warp >= qe) continue;
+        const int nseg = __ldg(&P.nseg);
+        f.ntile = __ldg(&P.ntile);
+        f.n0 = __ldg(&P.seg[0].M.ngroup);
+        f.p0 = __ldg(&P.seg[0].M.bpb);
+        f.g0 = __ldg(&P.seg[0].M.group_stride);
+        f.b0 = (const uint8_t *)__ldg((const unsigned long long *)&P.seg[0].M.base);
+        f.n1 = nseg > 1 ? __ldg(&P.seg[1].M.ngroup) : 0x7fffffff;
+        if (nseg > 1) {
+            f.p1 = __ldg(&P.seg[1].M.bpb);
+            f.g1 = __ldg(&P.seg[1].M.group_stride);
+            f.b1 = (const uint8_t *)__ldg((const unsigned long long *)&P.seg[1].M.base);
         }
-        // next matvec phase
-        for (s.ph++; s.ph < A.nphase; s.ph++)
-            if (__ldg(&A.prog[s.ph].kind) == PH_MATVEC) break;
-        if (s.ph >= A.nphase) return false;
-        const MvPhase &P = A.prog[s.ph].mv;
-        s.nseg = __ldg(&P.nseg);
-        s.ntile = __ldg(&P.ntile);
-        for (int j = 0; j < 3; j++) {
-            if (j < s.nseg) {
-                s.segq[j] = __ldg(&P.seg[j].M.nquad);
-                s.bpb[j] = __ldg(&P.seg[j].M.bpb);
-                s.qstride[j] = __ldg(&P.seg[j].M.quad_stride);
-                s.base[j] = (const uint8_t *)__ldg((const unsigned long long *)&P.seg[j].M.base);
-            }
+        if (nseg > 2) {
+            f.p2 = __ldg(&P.seg[2].M.bpb);
+            f.g2 = __ldg(&P.seg[2].M.group_stride);
+            f.b2 = (const uint8_t *)__ldg((const unsigned long long *)&P.seg[2].M.base);
         }
-        s.nblk = __ldg(&P.seg[0].M.nblk);
-        cta_quads(__ldg(&P.nquad), s.qb, s.qe);
-        s.k = s.t = s.w = 0;
+        if (nseg == 1) f.n0 = 0x7fffffff;
+        f.nblk = __ldg(&P.seg[0].M.nblk);
+        f.lpr = __ldg(&P.seg[0].M.lpr);
+        f.rpt = __ldg(&P.seg[0].M.rpt);
+        f.q = qb + warp;
+        f.qe = qe;
+        f.t = 0;
+        return;
     }
 }
 
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+__device__ __forceinline__ bool feed_next(const DecodeArgs &A, Feed &f, int warp, const uint8_t *&src, uint32_t &bytes) {
+    if (f.ph >= A.nphase) return false;
+    int lq = f.q;
+    const uint8_t *b;
+    uint32_t gs;
+    int bpb;
+    if (lq < f.n0) {
+        b = f.b0; gs = f.g0; bpb = f.p0;
+    } else if ((lq -= f.n0) < f.n1) {
+        b = f.b1; gs = f.g1; bpb = f.p1;
+    } else {
+        lq -= f.n1;
+        b = f.b2; gs = f.g2; bpb = f.p2;
+    }
+    const int nb = tile_nb(f.nblk, f.lpr, f.t);
+    src = b + (size_t)lq * gs + (size_t)f.t * 32 * bpb;
+    bytes = tile_copy_bytes(f.rpt, nb, bpb);
+    if (++f.t == f.ntile) {
+        f.t = 0;
+        f.q += kDW;
+        if (f.q >= f.qe) {
+            f.ph++;
+            feed_phase(A, f, warp);
+        }
+    }
+    return true;
+}
+
+// one tile into a ring slot: the warp's lanes copy 16-byte chunks, one group
+__device__ __forceinline__ void issue_tile(unsigned char *slot, const uint8_t *src, uint32_t bytes, int lane) {
+    const uint32_t o0 = (uint32_t)lane * 16;
+#pragma unroll 4
+    for (uint32_t o = o0; o < bytes; o += 512) cp_async16(slot + o, src + o);
+    cp_async_commit();
+}
+
+// wait until at most n of this thread's newest cp.async groups are pending
+__device__ __forceinline__ void cp_async_wait_n(int n) {
+    switch (n) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    default: cp_async_wait<3>(); break;
+    }
 }
 
 // ── grid barrier among the consumer warps of all CTAs (bounded) ──
@@ -679,15 +710,98 @@ __device__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region,
     }
 }
 
+// ── a warp's tile ring ──
+struct Ring {
+    unsigned char *base;
+    uint32_t slot_bytes;
+    int ns;
+    uint32_t issued, consumed;
+    int islot, cslot;  // slots of the next copy and of the next compute
+    Feed feed;
+};
+
+// refill the slot freed last (keeping ns - 1 tiles in flight), then wait for
+// the next tile in this warp's sequence and return its slot
+__device__ __forceinline__ const unsigned char *ring_next(const DecodeArgs &A, Ring &R, int warp, int lane) {
+    const uint8_t *src;
+    uint32_t bytes;
+    if (R.issued < R.consumed + (uint32_t)R.ns && feed_next(A, R.feed, warp, src, bytes)) {
+        issue_tile(R.base + (size_t)R.islot * R.slot_bytes, src, bytes, lane);
+        R.issued++;
+        if (++R.islot == R.ns) R.islot = 0;
+    }
+    cp_async_wait_n((int)(R.issued - R.consumed - 1));
+    __syncwarp();
+    const unsigned char *tile = R.base + (size_t)R.cslot * R.slot_bytes;
+    R.consumed++;
+    if (++R.cslot == R.ns) R.cslot = 0;
+    return tile;
+}
+
+// the sub-block terms of this lane's super-block in a tile of L lanes
+template <int T>
+__device__ __forceinline__ void tile_terms(const unsigned char *tile, int lane, int L, const XB &xb, float *tv) {
+    const int cs = L * 16;
+    const uint8_t *pa = tile + lane * 16;
+    const uint8_t *pss = tile + a_chunks(T) * cs + lane * plane_s_bytes(T);
+    const uint8_t *pd = tile + a_chunks(T) * cs + L * plane_s_bytes(T) + lane * plane_d_bytes(T);
+    if (T == 12) block_k4<false>(pa, cs, xb, tv);
+    else if (T == 13) block_k4<true>(pa, cs, xb, tv);
+    else if (T == 14) block_q6k(pa, cs, pss, pd, xb, tv);
+    else if (T == 11) block_q3k(pa, cs, pss, pd, xb, tv);
+    else block_q2k(pa, cs, pss, pd, xb, tv);
+}
+
+// One row group (rpt = 32/lpr rows x nblk super-blocks) of type T: returns,
+// in lanes 0..rpt-1, the rows' totals, each added term by term in sub-block
+// order (the lane of block j holds its terms until the row's running total
+// reaches it).
+struct Lanes {  // a lane's place in this phase's tiles: lane = rpt*bl + sl
+    int lpr, rpt, bl, sl, ntile;
+};
+
+template <int T>
+__device__ __forceinline__ float group_dot(const DecodeArgs &A, Ring &R, int warp, int lane, int nblk, const Lanes &g,
+                                           const Act &act) {
+    constexpr bool S32 = (T == 12 || T == 13);
+    constexpr int NSUB = S32 ? 8 : 16;
+    const int lpr = g.lpr, rpt = g.rpt, bl = g.bl, sl = g.sl;
+    const int8_t *xq = S32 ? act.q32 : act.q16;
+    const float *xe = S32 ? act.e32 : act.e16, *xs = S32 ? act.s32 : act.s16;
+    float acc = 0.0f;
+    for (int t = 0; t < g.ntile; t++) {
+        const unsigned char *tile = ring_next(A, R, warp, lane);
+        const int nb = nblk - lpr * t < lpr ? nblk - lpr * t : lpr;
+        float tv[NSUB];
+        if (bl < nb) {
+            const int b = lpr * t + bl;
+            const XB xb{xq + b * kXqStride, xe + b * NSUB, xs + b * NSUB};
+            tile_terms<T>(tile, lane, rpt * nb, xb, tv);
+        }
+        __syncwarp();  // the slot may be refilled from here on
+        // each row's running total visits the tile's blocks in order
+        float run = acc;
+        for (int jb = 0; jb < nb; jb++) {
+            float v = run;
+            if (bl == jb) {
+#pragma unroll
+                for (int k = 0; k < NSUB; k++) v = fa(v, tv[k]);
+            }
+            run = __shfl_sync(0xffffffffu, v, jb * rpt + sl);
+        }
+        acc = run;
+    }
+    return acc;
+}
+
 // ── the kernel ──
 __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_constant__ DecodeArgs A) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
     const int ns = A.ring_slots;
-    unsigned char *ring = smem;
-    unsigned char *region = ring + (size_t)kDW * ns * A.slot_bytes;
+    unsigned char *region = smem + (size_t)kDW * ns * A.slot_bytes;
     Phase *phbuf = (Phase *)(region + A.region_bytes);  // two staged phase descriptors
-    __shared__ __align__(8) uint64_t full[kDW][kMaxSlots], empty[kDW][kMaxSlots];
+    __shared__ __align__(8) uint64_t act_bar;           // bulk copies of a prologue's inputs
     __shared__ volatile int abort_flag;
     __shared__ int sync_ok;
     __shared__ double red[kDW];
@@ -695,16 +809,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
     __shared__ unsigned long long best_s[kDW];
     __shared__ float fred[kDW];
     __shared__ float fbc;
-
     __shared__ int pos_s, tok_s, bad_s;
+    // deferred epilogues: (segment, unit, y0, y1) per output unit, per warp
+    __shared__ int2 epi_su[kDW][32];
+    __shared__ float2 epi_y[kDW][32];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int kDescWords = (int)(sizeof(Phase) / 16);
     if (tid == 0) {
-        for (int w = 0; w < kDW; w++)
-            for (int s = 0; s < kMaxSlots; s++) {
-                mbar_init(&full[w][s], 1);
-                mbar_init(&empty[w][s], 1);
-            }
+        mbar_init(&act_bar, 1);
         abort_flag = 0;
         mbar_fence_init();
         // The step's position and token, read once here: thread 0 of every CTA
@@ -723,6 +836,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         tok_s = (int)t;
         bad_s = bad;
     }
+    if (tid < kDescWords) ((uint4 *)&phbuf[0])[tid] = __ldg((const uint4 *)&A.prog[0] + tid);
     __syncthreads();
 
     // an invalid position or token stops every CTA before any work
@@ -733,77 +847,31 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         return;
     }
 
-    if (warp == kDW) {
-        // ── producer: lane 0 walks the step's tiles ──
-        if (lane != 0) return;
-        uint32_t cnt[kDW];
-        for (int w = 0; w < kDW; w++) cnt[w] = 0;
-        Sched fetch, pre;
-        sched_init(fetch);
-        sched_init(pre);
-        long long issued = 0, pre_issued = 0;
-        bool pre_live = A.prefetch_tiles > 0;
-        bool ok = true;
-        Item it, pit;
-        while (sched_next(A, fetch, it)) {
-            while (pre_live && pre_issued < issued + A.prefetch_tiles) {
-                if (!sched_next(A, pre, pit)) {
-                    pre_live = false;
-                    break;
-                }
-                bulk_prefetch_l2(pit.src, pit.bytes);
-                pre_issued++;
-            }
-            const int w = it.warp;
-            const uint32_t c = cnt[w]++;
-            const int s = (int)(c % (uint32_t)ns);
-            if (!mbar_wait_bounded(&empty[w][s], ((c / ns) & 1) ^ 1, &abort_flag)) {
-                ok = false;
-                cnt[w]--;
-                break;
-            }
-            mbar_arrive_expect_tx(&full[w][s], it.bytes);
-            bulk_g2s(ring + ((size_t)w * ns + s) * A.slot_bytes, it.src, it.bytes, &full[w][s]);
-            issued++;
-        }
-        if (!ok) {
-            abort_flag = 1;
-            atomicOr(A.err, ERR_TIMEOUT);
-        }
-        // the copies issued last must land before the CTA may exit
-        for (int w = 0; w < kDW; w++) {
-            const uint32_t last = cnt[w];
-            for (uint32_t j = last > (uint32_t)ns ? last - ns : 0; j < last; j++)
-                mbar_wait_bounded(&full[w][j % ns], (j / ns) & 1, &abort_flag, 1u << 14);
-        }
-        return;
-    }
-
-    // ── consumers ──
-    const int bl = lane >> 2, sl = lane & 3;
-    uint32_t wcnt = 0;  // tiles this warp has consumed
-    unsigned nbar = 0;
-    // A warp that gives up (a wait ran out, or another role raised abort_flag)
-    // skips its remaining work but keeps the phase's control flow, so every
-    // named barrier is still reached by all consumer warps; the phase loop
-    // stops on a barrier-wide OR of the flag.
-    // stage descriptor 0
+    // this warp's tile ring, primed ns - 1 tiles ahead
+    Ring R;
+    R.base = smem + (size_t)warp * ns * A.slot_bytes;
+    R.slot_bytes = A.slot_bytes;
+    R.ns = ns;
+    R.issued = R.consumed = 0;
+    R.islot = R.cslot = 0;
+    R.feed.ph = 0;
+    feed_phase(A, R.feed, warp);
     {
-        const int nw = (int)(sizeof(Phase) / 16);
-        for (int i = tid; i < nw; i += kDW * 32) cp_async16((unsigned char *)&phbuf[0] + 16 * i, (const unsigned char *)&A.prog[0] + 16 * i);
-        cp_async_commit();
-        cp_async_wait<0>();
-        dsync();
+        const uint8_t *src;
+        uint32_t bytes;
+        while (R.issued < (uint32_t)ns - 1 && feed_next(A, R.feed, warp, src, bytes)) {
+            issue_tile(R.base + (size_t)R.islot * R.slot_bytes, src, bytes, lane);
+            R.issued++;
+            if (++R.islot == ns) R.islot = 0;
+        }
     }
+    uint32_t act_phase = 0;
+    unsigned nbar = 0;
     bool stop = false;
     for (int pi = 0; pi < A.nphase && !stop; pi++) {
         const Phase &ph = phbuf[pi & 1];
-        if (pi + 1 < A.nphase) {  // next descriptor streams in during this phase
-            const int nw = (int)(sizeof(Phase) / 16);
-            for (int i = tid; i < nw; i += kDW * 32)
-                cp_async16((unsigned char *)&phbuf[(pi + 1) & 1] + 16 * i, (const unsigned char *)&A.prog[pi + 1] + 16 * i);
-            cp_async_commit();
-        }
+        uint4 nextd = make_uint4(0, 0, 0, 0);  // the next descriptor, stored at the end of this phase
+        if (pi + 1 < A.nphase && tid < kDescWords) nextd = __ldg((const uint4 *)&A.prog[pi + 1] + tid);
         if (ph.barrier) {
             nbar++;
             if (!grid_sync(A, nbar * gridDim.x, &abort_flag, &sync_ok)) break;  // uniform
@@ -812,12 +880,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         if (ph.kind == PH_MATVEC) {
             const MvPhase &P = ph.mv;
             const Act act = carve_act(region, P.K, P.need16, P.need32);
-            // the activation and the norm weights: one round of copies
+            // the activation and the norm weights: bulk copies into the region
             float *xin = (float *)(region + act_bytes(P.K, P.need16, P.need32));
             float *wn = P.prologue == PRO_QUANT ? nullptr : xin + P.K;
-            if (wn) stage_floats(wn, P.norm_w, P.K);
-            if (P.prologue != PRO_EMBED) stage_floats(xin, P.in, P.K);
-            cp_async_commit();
+            const uint32_t kb = (uint32_t)P.K * 4u;
+            if (tid == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_expect_tx(&act_bar, (P.prologue != PRO_EMBED ? kb : 0u) + (wn ? kb : 0u));
+                if (P.prologue != PRO_EMBED) bulk_g2s(xin, P.in, kb, &act_bar);
+                if (wn) bulk_g2s(wn, P.norm_w, kb, &act_bar);
+            }
             if (P.prologue == PRO_EMBED) {
                 for (int i = tid; i < P.K; i += kDW * 32) {
                     const float v = P.e32 ? __ldg(P.e32 + (size_t)tok * P.K + i) : qm_dequant(P.E, (int)tok, i);
@@ -826,89 +898,66 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
                 }
                 if (blockIdx.x == 0 && tid == 0 && A.argmax_key) *A.argmax_key = 0ull;
             }
-            cp_async_wait<0>();
+            const bool landed = mbar_wait_bounded(&act_bar, act_phase, &abort_flag);
+            act_phase ^= 1u;
+            if (!landed) abort_flag = 1;
             dsync();
             quantize_act(xin, wn, P.K, P.eps, P.need16, P.need32, act, red, &scale_s);
             unsigned long long best = 0ull;
             int qb, qe;
-            cta_quads(P.nquad, qb, qe);
+            cta_groups(P.ngroup, qb, qe);
+            Lanes g;
+            g.lpr = P.seg[0].M.lpr;
+            g.rpt = P.seg[0].M.rpt;
+            const int lg = 31 - __clz(g.rpt);
+            g.bl = lane >> lg;
+            g.sl = lane & (g.rpt - 1);
+            g.ntile = P.ntile;
+            const int upg = g.rpt >> 1;  // output units per group
+            int nepi = 0;
+            // The epilogues run 32 units at a time, one per lane, so their
+            // latency (exp, division, loads) is paid once per 32 units.
+            auto flush = [&]() {
+                __syncwarp();
+                const int2 su = lane < nepi ? epi_su[warp][lane] : make_int2(0, -1);
+                if (su.y >= 0) {
+                    const float2 y = epi_y[warp][lane];
+                    const MvSeg &sg = P.seg[su.x];
+                    int r0, r1;
+                    unit_rows(sg, su.y, r0, r1);
+                    const EpiIn ein = epi_load(A, sg, r0, r1, pos);
+                    unit_epilogue(A, sg, r0, r1, y.x, y.y, pos, ein, best);
+                }
+                __syncwarp();
+                nepi = 0;
+            };
             for (int q0 = qb + warp; q0 < qe; q0 += kDW) {
-                int j = 0, lq = q0;  // phase-global quad index -> segment, local quad
-                while (j < P.nseg - 1 && lq >= P.seg[j].M.nquad) lq -= P.seg[j++].M.nquad;
-                const MvSeg &sg = P.seg[j];
-                const int T = sg.M.type, nblk = sg.M.nblk;
-                const bool s32 = (T == 12 || T == 13);
-                const int nsub = s32 ? 8 : 16;
-                const int8_t *xq = s32 ? act.q32 : act.q16;
-                const float *xe = s32 ? act.e32 : act.e16, *xs = s32 ? act.s32 : act.s16;
-                const int u = 2 * lq + (lane >> 1);
-                const bool epi_lane = (lane == 0 || lane == 2) && u < sg.units;
-                int r0 = 0, r1 = 0;
-                EpiIn ein{0.0f, 0.0f, 0.0f, 0.0f};
-                if (epi_lane) {
-                    unit_rows(sg, u, r0, r1);
-                    ein = epi_load(A, sg, r0, r1, pos);
+                int j = 0, lq = q0;  // phase-global group index -> segment, local group
+                while (j < P.nseg - 1 && lq >= P.seg[j].M.ngroup) lq -= P.seg[j++].M.ngroup;
+                const int T = P.seg[j].M.type, nblk = P.seg[j].M.nblk;
+                float acc;
+                switch (T) {
+                case 12: acc = group_dot<12>(A, R, warp, lane, nblk, g, act); break;
+                case 13: acc = group_dot<13>(A, R, warp, lane, nblk, g, act); break;
+                case 14: acc = group_dot<14>(A, R, warp, lane, nblk, g, act); break;
+                case 11: acc = group_dot<11>(A, R, warp, lane, nblk, g, act); break;
+                default: acc = group_dot<10>(A, R, warp, lane, nblk, g, act); break;
                 }
-                float acc = 0.0f;
-                bool live = true;
-                for (int t = 0; t < P.ntile; t++) {
-                    const uint32_t c = wcnt++;
-                    const int s = (int)(c % (uint32_t)ns);
-                    bool got = false;
-                    if (live) got = mbar_wait_bounded(&full[warp][s], (c / ns) & 1, &abort_flag);
-                    if (!__all_sync(0xffffffffu, got)) {
-                        if (lane == 0) abort_flag = 1;
-                        live = false;
-                        continue;
-                    }
-                    const int nb = tile_nb(nblk, t), L = 4 * nb;
-                    const unsigned char *tile = ring + ((size_t)warp * ns + s) * A.slot_bytes;
-                    float tv[kTermMax];
-                    if (bl < nb) {
-                        const int cs = L * 16;
-                        const uint8_t *pa = tile + lane * 16;
-                        const uint8_t *pss = tile + a_chunks(T) * cs + lane * plane_s_bytes(T);
-                        const uint8_t *pd = tile + a_chunks(T) * cs + L * plane_s_bytes(T) + lane * plane_d_bytes(T);
-                        const int b = 8 * t + bl;
-                        const XB xb{xq + b * kXqStride, xe + b * nsub, xs + b * nsub};
-                        switch (T) {
-                        case 12: block_k4<false>(pa, cs, xb, tv); break;
-                        case 13: block_k4<true>(pa, cs, xb, tv); break;
-                        case 14: block_q6k(pa, cs, pss, pd, xb, tv); break;
-                        case 11: block_q3k(pa, cs, pss, pd, xb, tv); break;
-                        default: block_q2k(pa, cs, pss, pd, xb, tv); break;
-                        }
-                    }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[warp][s]);  // the tile is consumed
-                    // each row's running total visits the tile's blocks in order
-                    float run = acc;
-                    if (s32) {
-                        for (int jb = 0; jb < nb; jb++) {
-                            float v = run;
-                            if (bl == jb) {
-#pragma unroll
-                                for (int k = 0; k < 8; k++) v = fa(v, tv[k]);
-                            }
-                            run = __shfl_sync(0xffffffffu, v, jb * 4 + sl);
-                        }
-                    } else {
-                        for (int jb = 0; jb < nb; jb++) {
-                            float v = run;
-                            if (bl == jb) {
-#pragma unroll
-                                for (int k = 0; k < 16; k++) v = fa(v, tv[k]);
-                            }
-                            run = __shfl_sync(0xffffffffu, v, jb * 4 + sl);
-                        }
-                    }
-                    acc = run;
-                }
-                if (!live) continue;
-                // lanes 0..3 hold rows 0..3 of the quad: units (rows 0,1) and (rows 2,3)
+                // lanes 0..rpt-1 hold the group's row totals; an even one owns
+                // the unit of rows (sl, sl+1)
                 const float other = __shfl_down_sync(0xffffffffu, acc, 1);
-                if (epi_lane) unit_epilogue(A, sg, r0, r1, acc, other, pos, ein, best);
+                if (nepi + upg > 32) flush();
+                const int u = (lq * g.rpt + g.sl) >> 1;
+                if (lane < g.rpt && !(g.sl & 1) && u < P.seg[j].units) {
+                    epi_su[warp][nepi + (g.sl >> 1)] = make_int2(j, u);
+                    epi_y[warp][nepi + (g.sl >> 1)] = make_float2(acc, other);
+                }
+                // units past the segment's end (zero rows of a padded group)
+                // are left in place with their unit index and skipped below
+                if (lane < g.rpt && !(g.sl & 1) && u >= P.seg[j].units) epi_su[warp][nepi + (g.sl >> 1)] = make_int2(j, -1);
+                nepi += upg;
             }
+            if (nepi) flush();
             if (A.argmax_key && P.seg[0].epi == EPI_LOGITS) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
@@ -934,9 +983,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
                 if (A.commit) *(volatile int *)A.d_len = pos + 1;
             }
         }
-        cp_async_wait<0>();  // the next descriptor
-        stop = dsync_or(abort_flag != 0);
+        stop = dsync_or(abort_flag != 0);  // every reader of this phase's descriptor is done
+        if (pi + 1 < A.nphase && tid < kDescWords) ((uint4 *)&phbuf[(pi + 1) & 1])[tid] = nextd;
+        dsync();
     }
+    cp_async_wait<0>();  // tiles still in flight land before the CTA exits
     if (stop && tid == 0) atomicOr(A.err, ERR_TIMEOUT);
 }
 

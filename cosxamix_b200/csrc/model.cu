@@ -116,7 +116,7 @@ size_t kv_dim(const cxm_model *m) { return (size_t)m->cfg.n_head_kv * m->cfg.hea
 
 int sub_of(int type) { return (type == Q4K || type == Q5K) ? 32 : 16; }
 
-// ── quad tiles (the layout QMat describes) ──
+// ── tiles (the layout QMat describes) ──
 // Tiled row i is row `row` of the GGUF matrix at `m` (its bytes), or a zero
 // row when m is null. The bytes of each block are only moved, never changed.
 struct RowSrc {
@@ -124,20 +124,41 @@ struct RowSrc {
     int row;
 };
 
-QMat tiled_desc(int type, int K, int nrows) {
+QMat tiled_desc(int type, int K, int nrows, int lpr) {
     QMat M{};
     M.type = type;
     M.K = K;
     M.nblk = K / 256;
     M.bpb = bytes_per_block(type);
-    M.nquad = (nrows + 3) / 4;
-    M.rows = 4 * M.nquad;
-    M.quad_stride = (uint32_t)(((size_t)4 * M.nblk * M.bpb + 15) & ~(size_t)15);
+    M.lpr = lpr;
+    M.rpt = 32 / lpr;
+    M.ngroup = (nrows + M.rpt - 1) / M.rpt;
+    M.rows = M.rpt * M.ngroup;
+    M.group_stride = (uint32_t)(((size_t)M.rpt * M.nblk * M.bpb + 15) & ~(size_t)15);
     return M;
 }
 
+// Lanes per row of a matrix's tiles. A warp works through whole row groups
+// (32/lpr rows), so the phase's groups should split evenly over the SMs'
+// warps: take the fewest lanes per row (a lane then owns more of a row, and
+// the row's chain of additions crosses fewer lanes) for which the busiest
+// warp has at most ~12% more groups than the average one; never more lanes
+// than the row has super-blocks, and at most 16 so a tile holds both rows of
+// an output pair.
+int choose_lpr(int phase_rows, int nblk, int sms) {
+    const long long warps = (long long)kDW * sms;
+    int lpr = 1;
+    while (lpr < 16 && lpr < nblk) {
+        const long long groups = ((long long)phase_rows * lpr + 31) / 32;
+        const long long per_cta = (groups + sms - 1) / sms, busiest = (per_cta + kDW - 1) / kDW;
+        if (groups >= warps && busiest * warps <= groups * 9 / 8) break;
+        lpr *= 2;
+    }
+    return lpr;
+}
+
 void build_tiles(const QMat &M, const std::vector<RowSrc> &rows, std::vector<uint8_t> &buf) {
-    buf.assign((size_t)M.nquad * M.quad_stride, 0);
+    buf.assign((size_t)M.ngroup * M.group_stride, 0);
     const int T = M.type, pa = plane_a_bytes(T), ps = plane_s_bytes(T), pd = plane_d_bytes(T), ach = pa / 16;
     int lo_a = 0, lo_s = pa, lo_d = pa + ps;
     if (T == Q2K) {
@@ -145,18 +166,19 @@ void build_tiles(const QMat &M, const std::vector<RowSrc> &rows, std::vector<uin
         lo_a = 16;
         lo_d = 80;
     }
-    const int ntile = (M.nblk + 7) / 8;
+    const int ntile = (M.nblk + M.lpr - 1) / M.lpr;
     auto work = [&](int q0, int q1) {
         for (int q = q0; q < q1; q++)
             for (int t = 0; t < ntile; t++) {
-                const int nb = tile_nb(M.nblk, t), L = 4 * nb;
+                const int nb = tile_nb(M.nblk, M.lpr, t), L = M.rpt * nb;
                 uint8_t *tile = buf.data() + tile_offset(M, q, t);
                 for (int bl = 0; bl < nb; bl++)
-                    for (int sl = 0; sl < 4; sl++) {
-                        const size_t ri = (size_t)4 * q + sl;
+                    for (int sl = 0; sl < M.rpt; sl++) {
+                        const size_t ri = (size_t)M.rpt * q + sl;
                         if (ri >= rows.size() || !rows[ri].m) continue;
-                        const uint8_t *blk = rows[ri].m + ((size_t)rows[ri].row * M.nblk + 8 * t + bl) * M.bpb;
-                        const int lane = 4 * bl + sl;
+                        const uint8_t *blk =
+                            rows[ri].m + ((size_t)rows[ri].row * M.nblk + (size_t)M.lpr * t + bl) * M.bpb;
+                        const int lane = M.rpt * bl + sl;
                         for (int c = 0; c < ach; c++) memcpy(tile + ((size_t)c * L + lane) * 16, blk + lo_a + 16 * c, 16);
                         if (ps) memcpy(tile + (size_t)ach * L * 16 + (size_t)lane * ps, blk + lo_s, ps);
                         if (pd) memcpy(tile + (size_t)ach * L * 16 + (size_t)L * ps + (size_t)lane * pd, blk + lo_d, pd);
@@ -164,13 +186,13 @@ void build_tiles(const QMat &M, const std::vector<RowSrc> &rows, std::vector<uin
             }
     };
     const int nth = std::max(1, std::min<int>(16, (int)std::thread::hardware_concurrency()));
-    if (M.nquad < 256 || nth == 1) {
-        work(0, M.nquad);
+    if (M.ngroup < 256 || nth == 1) {
+        work(0, M.ngroup);
         return;
     }
     std::vector<std::thread> th;
     for (int i = 0; i < nth; i++)
-        th.emplace_back(work, (int)((long long)M.nquad * i / nth), (int)((long long)M.nquad * (i + 1) / nth));
+        th.emplace_back(work, (int)((long long)M.ngroup * i / nth), (int)((long long)M.ngroup * (i + 1) / nth));
     for (auto &x : th) x.join();
 }
 
@@ -227,15 +249,16 @@ int upload_tiles(cxm_model *m, QMat &M, const std::vector<RowSrc> &rows) {
     return 0;
 }
 
-// one GGUF matrix, rows in order (pairing ADJ) or RoPE order
-int upload_matrix(cxm_model *m, const Gguf &g, const TensorInfo &t, int pairing, int half, QMat *out) {
+// one GGUF matrix, rows in order (pairing ADJ) or RoPE order, in tiles of
+// `lpr` lanes per row
+int upload_matrix(cxm_model *m, const Gguf &g, const TensorInfo &t, int pairing, int half, int lpr, QMat *out) {
     if (check_matrix(t)) return -1;
     const int K = (int)t.dims[0], rows = (int)t.dims[1];
     if (rows % 2 || (pairing == PAIR_ROPE && (half % 2 || rows % (2 * half)))) {
         set_error("%s: %d rows do not pair", t.name.c_str(), rows);
         return -1;
     }
-    QMat M = tiled_desc(t.type, K, rows);
+    QMat M = tiled_desc(t.type, K, rows, lpr);
     const auto order = pairing == PAIR_ROPE ? rows_rope(g.data(t), rows, half) : rows_adj(g.data(t), rows);
     if (upload_tiles(m, M, order)) return -1;
     M.rows = rows;
@@ -245,14 +268,14 @@ int upload_matrix(cxm_model *m, const Gguf &g, const TensorInfo &t, int pairing,
 }
 
 // gate and up as one matrix of PAIR_TWO quads
-int upload_pair(cxm_model *m, const Gguf &g, const TensorInfo &a, const TensorInfo &b, QMat *out) {
+int upload_pair(cxm_model *m, const Gguf &g, const TensorInfo &a, const TensorInfo &b, int lpr, QMat *out) {
     if (check_matrix(a) || check_matrix(b)) return -1;
     if (a.type != b.type || a.dims[0] != b.dims[0] || a.dims[1] != b.dims[1] || a.dims[1] % 2) {
         set_error("%s and %s must have the same type and shape", a.name.c_str(), b.name.c_str());
         return -1;
     }
     const int K = (int)a.dims[0], n = (int)a.dims[1];
-    QMat M = tiled_desc(a.type, K, 2 * n);
+    QMat M = tiled_desc(a.type, K, 2 * n, lpr);
     if (upload_tiles(m, M, rows_two(g.data(a), g.data(b), n))) return -1;
     M.rows = 2 * n;
     *out = M;
@@ -347,11 +370,11 @@ Phase mv_phase(const std::vector<MvSeg> &segs, int K, int prologue, const float 
     P.nseg = (int)segs.size();
     for (int i = 0; i < P.nseg; i++) {
         P.seg[i] = segs[i];
-        P.nquad += segs[i].M.nquad;
+        P.ngroup += segs[i].M.ngroup;
         if (sub_of(segs[i].M.type) == 16) P.need16 = 1; else P.need32 = 1;
     }
     P.K = K;
-    P.ntile = (K / 256 + 7) / 8;
+    P.ntile = (K / 256 + segs[0].M.lpr - 1) / segs[0].M.lpr;
     P.prologue = prologue;
     P.in = in;
     P.norm_w = norm_w;
@@ -467,10 +490,6 @@ int decode_geometry(uint32_t slot_bytes, const Program &p, DecodeArgs &a, size_t
     a.ring_slots = ns;
     a.slot_bytes = slot;
     a.region_bytes = (uint32_t)p.region;
-    // The ring alone keeps HBM busy; an L2 prefetch window deepens the memory
-    // queues that every latency-bound access of the step (activations,
-    // barriers) then waits behind.
-    a.prefetch_tiles = 0;
     *smem = (size_t)kDW * ns * slot + fixed;
     return 0;
 }
@@ -640,11 +659,15 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
     if (embd->type == F32) {
         if (upload_vector(m.get(), g, *embd, (size_t)cfg.vocab * cfg.dim, &m->embd_f32)) return -1;
         m->embd.type = 0;
-    } else if (upload_matrix(m.get(), g, *embd, PAIR_ADJ, 0, &m->embd)) {
+    } else if (upload_matrix(m.get(), g, *embd, PAIR_ADJ, 0,
+                             choose_lpr(cfg.vocab, (int)(embd->dims[0] / 256), m->sms), &m->embd)) {
         return -1;
     }
     if (outw) {
-        if (upload_matrix(m.get(), g, *outw, PAIR_ADJ, 0, &m->out)) return -1;
+        if (check_matrix(*outw) ||
+            upload_matrix(m.get(), g, *outw, PAIR_ADJ, 0, choose_lpr(cfg.vocab, (int)(outw->dims[0] / 256), m->sms),
+                          &m->out))
+            return -1;
     } else {
         if (embd->type == F32) {
             set_error("a tied F32 embedding table has no device output kernel");
@@ -663,19 +686,24 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
             return t;
         };
         const TensorInfo *t, *t2;
-        const int half = (int)hd / 2;
+        const int half = (int)hd / 2, nbd = cfg.dim / 256;
+        // tile shapes by phase: q|k|v share one; o, gate|up and down their own
+        const int lpr_qkv = choose_lpr(cfg.dim + 2 * (int)kvd, nbd, m->sms), lpr_o = choose_lpr(cfg.dim, nbd, m->sms);
+        const TensorInfo *tg = T("ffn_gate.weight"), *td = T("ffn_down.weight");
+        if (!tg || !td || check_matrix(*tg) || check_matrix(*td)) return -1;
+        const int lpr_gu = choose_lpr(2 * (int)tg->dims[1], nbd, m->sms);
+        const int lpr_down = choose_lpr(cfg.dim, (int)(td->dims[0] / 256), m->sms);
         if (!(t = T("attn_norm.weight")) || upload_vector(m.get(), g, *t, cfg.dim, &L.attn_norm)) return -1;
-        if (!(t = T("attn_q.weight")) || upload_matrix(m.get(), g, *t, PAIR_ROPE, half, &L.q)) return -1;
+        if (!(t = T("attn_q.weight")) || upload_matrix(m.get(), g, *t, PAIR_ROPE, half, lpr_qkv, &L.q)) return -1;
         if (!(t = T("attn_q.bias")) || upload_vector(m.get(), g, *t, cfg.dim, &L.bq)) return -1;
-        if (!(t = T("attn_k.weight")) || upload_matrix(m.get(), g, *t, PAIR_ROPE, half, &L.k)) return -1;
+        if (!(t = T("attn_k.weight")) || upload_matrix(m.get(), g, *t, PAIR_ROPE, half, lpr_qkv, &L.k)) return -1;
         if (!(t = T("attn_k.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bk)) return -1;
-        if (!(t = T("attn_v.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, &L.v)) return -1;
+        if (!(t = T("attn_v.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, lpr_qkv, &L.v)) return -1;
         if (!(t = T("attn_v.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bv)) return -1;
-        if (!(t = T("attn_output.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, &L.o)) return -1;
+        if (!(t = T("attn_output.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, lpr_o, &L.o)) return -1;
         if (!(t = T("ffn_norm.weight")) || upload_vector(m.get(), g, *t, cfg.dim, &L.ffn_norm)) return -1;
-        if (!(t = T("ffn_gate.weight")) || !(t2 = T("ffn_up.weight")) || upload_pair(m.get(), g, *t, *t2, &L.gu))
-            return -1;
-        if (!(t = T("ffn_down.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, &L.down)) return -1;
+        if (!(t2 = T("ffn_up.weight")) || upload_pair(m.get(), g, *tg, *t2, lpr_gu, &L.gu)) return -1;
+        if (upload_matrix(m.get(), g, *td, PAIR_ADJ, 0, lpr_down, &L.down)) return -1;
         if (L.q.rows != cfg.dim || L.k.rows != (int)kvd || L.v.rows != (int)kvd || L.o.rows != cfg.dim ||
             L.q.K != cfg.dim || L.k.K != cfg.dim || L.v.K != cfg.dim || L.o.K != cfg.dim || L.gu.K != cfg.dim ||
             L.down.K != L.gu.rows / 2 || L.down.rows != cfg.dim) {
@@ -1054,7 +1082,10 @@ extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint3
         return -1;
     }
     // the decode kernel on a one-phase program: quantize x, W·x, store
-    QMat M = tiled_desc(type, (int)k, (int)rows);
+    int dev0 = 0, sms0 = 148;
+    CU(cudaGetDevice(&dev0));
+    CU(cudaDeviceGetAttribute(&sms0, cudaDevAttrMultiProcessorCount, dev0));
+    QMat M = tiled_desc(type, (int)k, (int)rows, choose_lpr((int)rows, (int)(k / 256), sms0));
     std::vector<uint8_t> tiles;
     build_tiles(M, rows_adj(w, (int)rows), tiles);
     DevBuf dw, dx, dy, derr, dbar, dprog;
@@ -1245,7 +1276,7 @@ extern "C" int cxm_bench_matvec(cxm_model *m, uint32_t reps, float *ms_per_launc
     }
     *ms_per_launch = ms / (float)reps;
     const Layer &L = m->layers[0];
-    *bytes_per_launch = (uint64_t)L.gu.rows * (uint64_t)L.gu.nblk * (uint64_t)L.gu.bpb;
+    *bytes_per_launch = (uint64_t)L.gu.rows * (uint64_t)L.gu.nblk * (uint64_t)L.gu.bpb;  // 2 x ffn rows
     return check_err(m);
 }
 

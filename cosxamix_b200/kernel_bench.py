@@ -1,11 +1,15 @@
 """Kernel micro-benchmarks on a synthetic model (device-timed, CUDA events).
 
     python -m cosxamix_b200.kernel_bench [--config qwen3b] [--reps 108]
+                                         [--layers N] [--vocab V]
 
-Times the gate/up k-quant matvec of the model, cycling over its layers so
-every launch streams its own weights from HBM (36 layers x 25 MB > L2), and
-prints the per-launch time and the algorithmic weight bytes per second. Used
-for the ncu captures summarised under profiles/.
+Times the gate|up matvec phase of the decode kernel: `reps` such phases in
+one launch, behind grid barriers as in the step, cycling over the model's
+layers so every phase streams its own weights (36 layers x 25 MB > L2).
+Prints the per-phase time and the algorithmic weight bytes per second.
+`--layers` / `--vocab` shrink the synthetic model (same matrix shapes) so an
+ncu capture holds little device memory; keep layers x 25 MB above the 126 MB
+L2 for DRAM figures to mean something.
 """
 from __future__ import annotations
 
@@ -13,6 +17,8 @@ import argparse
 import json
 import os
 import sys
+import tempfile
+import time
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
@@ -23,15 +29,31 @@ def main() -> None:
     ap.add_argument("--config", default="qwen3b")
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--reps", type=int, default=108)
+    ap.add_argument("--layers", type=int, default=0)
+    ap.add_argument("--vocab", type=int, default=0)
     args = ap.parse_args()
     import bench
     import cosxamix_b200 as cx
 
-    path = bench.ensure_model(args.config, args.seed)
+    if args.layers or args.vocab:
+        over = {}
+        if args.layers:
+            over["n_layer"] = args.layers
+        if args.vocab:
+            over["vocab"] = args.vocab
+        d = os.environ.get("CXM_MODEL_DIR", tempfile.gettempdir())
+        path = os.path.join(d, f"cxm_{args.config}_s{args.seed}_l{args.layers}_v{args.vocab}.gguf")
+        if not os.path.exists(path):
+            t = time.time()
+            cx.synth_write(path, cx.synth_spec(args.config, seed=args.seed, **over))
+            print(f"[kernel_bench] wrote {path} in {time.time() - t:.1f}s", file=sys.stderr)
+    else:
+        path = bench.ensure_model(args.config, args.seed)
     m = cx.Modelo(path)
     ms, nbytes = m.bench_matvec(args.reps)
-    print(json.dumps({"kernel": "k_matvec gate/up", "config": args.config, "launch_us": round(ms * 1000, 3),
-                      "bytes_per_launch": nbytes, "gbs": round(nbytes / (ms / 1000) / 1e9, 1)}))
+    print(json.dumps({"kernel": "k_decode gate|up phase", "config": args.config, "layers": args.layers or None,
+                      "phase_us": round(ms * 1000, 3), "bytes_per_phase": nbytes,
+                      "gbs": round(nbytes / (ms / 1000) / 1e9, 1)}))
 
 
 if __name__ == "__main__":

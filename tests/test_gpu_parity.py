@@ -75,6 +75,19 @@ def test_matvec_matches_oracle_bit_exact(t, k):
     np.testing.assert_array_equal(got, want)
 
 
+@pytest.mark.parametrize("t", TYPES)
+@pytest.mark.parametrize("rows", [6002, 12010, 20006])
+def test_matvec_tile_shapes_bit_exact(t, rows):
+    # taller matrices get tiles with fewer lanes per row (4, 2 and 1 at these
+    # heights on 148 SMs); row counts that leave the last tile part-filled
+    k = 2048
+    w = cx.quantize(t, normals(rows * k, 0.02, rows + t))
+    x = normals(k, 1.0, 3 * rows + t)
+    got = cx.matvec(t, w, rows, k, x)
+    want = O.matmul(x, w, t, k, rows)[0]
+    np.testing.assert_array_equal(got, want)
+
+
 def test_expf_matches_host_libm():
     rng = np.random.default_rng(11)
     x = np.concatenate([
