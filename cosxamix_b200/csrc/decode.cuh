@@ -550,8 +550,9 @@ __device__ bool grid_sync(const DecodeArgs &A, unsigned target, volatile int *ab
     dsync();
     if (threadIdx.x == 0) {
         int ok = 1;
-        __threadfence();
-        atomicAdd(A.bar, 1u);
+        // release this CTA's writes (made visible to thread 0 by the named
+        // barrier) and arrive, without waiting for the atomic's reply
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(A.bar) : "memory");
         for (uint32_t i = 0;; i++) {
             unsigned v;
             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(A.bar) : "memory");
@@ -872,24 +873,31 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         const Phase &ph = phbuf[pi & 1];
         uint4 nextd = make_uint4(0, 0, 0, 0);  // the next descriptor, stored at the end of this phase
         if (pi + 1 < A.nphase && tid < kDescWords) nextd = __ldg((const uint4 *)&A.prog[pi + 1] + tid);
+        // A matvec's norm weights depend on nothing: their copy starts before
+        // the barrier (the region is free: every warp left the last phase).
+        const bool mv = ph.kind == PH_MATVEC;
+        const bool has_norm = mv && ph.mv.prologue != PRO_QUANT;
+        const uint32_t kbytes = mv ? (uint32_t)ph.mv.K * 4u : 0u;
+        float *xin = mv ? (float *)(region + act_bytes(ph.mv.K, ph.mv.need16, ph.mv.need32)) : nullptr;
+        float *wn = has_norm ? xin + ph.mv.K : nullptr;
+        if (mv && tid == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive_expect_tx(&act_bar, (ph.mv.prologue != PRO_EMBED ? kbytes : 0u) + (has_norm ? kbytes : 0u));
+            if (has_norm) bulk_g2s(wn, ph.mv.norm_w, kbytes, &act_bar);
+        }
         if (ph.barrier) {
             nbar++;
-            if (!grid_sync(A, nbar * gridDim.x, &abort_flag, &sync_ok)) break;  // uniform
+            if (!grid_sync(A, nbar * gridDim.x, &abort_flag, &sync_ok)) {  // uniform
+                if (mv) mbar_wait_bounded(&act_bar, act_phase, &abort_flag, 1u << 14);  // no copy left in flight
+                break;
+            }
         }
         const int n = pos + 1;
         if (ph.kind == PH_MATVEC) {
             const MvPhase &P = ph.mv;
             const Act act = carve_act(region, P.K, P.need16, P.need32);
-            // the activation and the norm weights: bulk copies into the region
-            float *xin = (float *)(region + act_bytes(P.K, P.need16, P.need32));
-            float *wn = P.prologue == PRO_QUANT ? nullptr : xin + P.K;
-            const uint32_t kb = (uint32_t)P.K * 4u;
-            if (tid == 0) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive_expect_tx(&act_bar, (P.prologue != PRO_EMBED ? kb : 0u) + (wn ? kb : 0u));
-                if (P.prologue != PRO_EMBED) bulk_g2s(xin, P.in, kb, &act_bar);
-                if (wn) bulk_g2s(wn, P.norm_w, kb, &act_bar);
-            }
+            // the activation (written by other CTAs before the barrier)
+            if (tid == 0 && P.prologue != PRO_EMBED) bulk_g2s(xin, P.in, kbytes, &act_bar);
             if (P.prologue == PRO_EMBED) {
                 for (int i = tid; i < P.K; i += kDW * 32) {
                     const float v = P.e32 ? __ldg(P.e32 + (size_t)tok * P.K + i) : qm_dequant(P.E, (int)tok, i);
