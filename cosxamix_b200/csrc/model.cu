@@ -17,6 +17,7 @@
 #include "../../include/cxm.h"
 #include "cxm_internal.h"
 #include "decode.cuh"
+#include "sampler.cuh"
 
 using namespace cxm;
 
@@ -52,6 +53,13 @@ struct cxm_model {
     int *err = nullptr;
     unsigned *bar = nullptr;  // grid-barrier counter of the decode kernel
     unsigned long long *argmax_key = nullptr;
+    // sampler (src/sampler.rs): xorshift64* state, (1/T, top_p), picked
+    // token, scratch of the device Muestreador::elegir
+    unsigned long long *rng = nullptr;
+    float *samp_params = nullptr;
+    uint32_t *samp_tok = nullptr;
+    float *samp_probs = nullptr, *samp_prefix = nullptr;
+    uint32_t *samp_k0 = nullptr, *samp_v0 = nullptr, *samp_k1 = nullptr, *samp_v1 = nullptr;
     int sms = 148;
     uint32_t slot_bytes = 0;  // largest quad tile of the model
     uint64_t weight_bytes = 0;
@@ -89,8 +97,8 @@ struct cxm_cache {
     float *k = nullptr, *v = nullptr;  // [n_layer][max_tokens][kvd]
     uint32_t *toks = nullptr;          // [max_tokens + 2]
     int *d_len = nullptr;
-    Program prog[3];
-    cudaGraphExec_t graph[3] = {nullptr, nullptr, nullptr};
+    Program prog[4];
+    cudaGraphExec_t graph[4] = {nullptr, nullptr, nullptr, nullptr};
     ~cxm_cache() {
         if (m) cudaSetDevice(m->device);
         for (auto &g : graph)
@@ -110,7 +118,8 @@ struct cxm_sampler {
 
 namespace {
 
-enum StepMode { STEP_PREFILL = 0, STEP_GREEDY = 1, STEP_LOGITS = 2 };
+// STEP_SAMPLE: the STEP_LOGITS step, then the sampler writes the next token
+enum StepMode { STEP_PREFILL = 0, STEP_GREEDY = 1, STEP_LOGITS = 2, STEP_SAMPLE = 3 };
 
 size_t kv_dim(const cxm_model *m) { return (size_t)m->cfg.n_head_kv * m->cfg.head_dim; }
 
@@ -340,6 +349,7 @@ int set_kernel_smem_limits() {
     CU(cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, g_decode_smem_max));
     CU(cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     CU(cudaFuncSetAttribute(k_attn_out, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    CU(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kScanChunk * (int)sizeof(float)));
     return 0;
 }
 
@@ -523,7 +533,11 @@ DecodeArgs base_args(cxm_model *m) {
     return a;
 }
 
+int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out);
+
 int enqueue_step(cxm_model *m, cxm_cache *c, int mode) {
+    if (mode == STEP_SAMPLE)
+        return enqueue_step(m, c, STEP_LOGITS) || launch_sample(m, c->d_len, c->toks, nullptr) ? -1 : 0;
     Program &p = c->prog[mode];
     if (!p.d && upload_program(step_program(m, c, mode), (int)c->max_tokens, &p)) return -1;
     DecodeArgs a = base_args(m);
@@ -544,7 +558,8 @@ int get_graph(cxm_model *m, cxm_cache *c, int mode, cudaGraphExec_t *out) {
         *out = c->graph[mode];
         return 0;
     }
-    if (!c->prog[mode].d && upload_program(step_program(m, c, mode), (int)c->max_tokens, &c->prog[mode])) return -1;
+    const int pm = mode == STEP_SAMPLE ? STEP_LOGITS : mode;
+    if (!c->prog[pm].d && upload_program(step_program(m, c, pm), (int)c->max_tokens, &c->prog[pm])) return -1;
     cudaGraph_t g = nullptr;
     CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int rc = enqueue_step(m, c, mode);
@@ -572,6 +587,35 @@ int run_steps(cxm_model *m, cxm_cache *c, int mode, uint32_t n) {
     cudaGraphExec_t g;
     if (get_graph(m, c, mode, &g)) return -1;
     for (uint32_t i = 0; i < n; i++) CU(cudaGraphLaunch(g, m->stream));
+    return 0;
+}
+
+// the device Muestreador::elegir on the model's logits, with (1/T, top_p) and
+// the RNG state from device memory; the token goes to toks[*d_len] or *out
+int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out) {
+    SampleArgs a{};
+    a.logits = m->logits;
+    a.n = m->cfg.vocab;
+    a.params = m->samp_params;
+    a.rng = m->rng;
+    a.d_len = d_len;
+    a.toks = toks;
+    a.out = out;
+    a.probs = m->samp_probs;
+    a.prefix = m->samp_prefix;
+    a.key0 = m->samp_k0;
+    a.val0 = m->samp_v0;
+    a.key1 = m->samp_k1;
+    a.val1 = m->samp_v1;
+    k_sample<<<1, kSampThreads, 2 * kScanChunk * sizeof(float), m->stream>>>(a);
+    CU(cudaGetLastError());
+    return 0;
+}
+
+int set_sampler(cxm_model *m, const cxm_sampler *s) {
+    const float prm[2] = {1.0f / s->temperature, s->top_p};  // src/sampler.rs:77
+    CU(cudaMemcpyAsync(m->samp_params, prm, sizeof(prm), cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(m->rng, &s->state, sizeof(uint64_t), cudaMemcpyHostToDevice, m->stream));
     return 0;
 }
 
@@ -733,7 +777,10 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
     // activations
     if (m->alloc(&m->x, cfg.dim) || m->alloc(&m->q, cfg.dim) || m->alloc(&m->att, cfg.dim) ||
         m->alloc(&m->h, std::max(cfg.ffn, 1)) || m->alloc(&m->logits, cfg.vocab) || m->alloc(&m->err, 1) ||
-        m->alloc(&m->bar, 1) || m->alloc(&m->argmax_key, 1) ||
+        m->alloc(&m->bar, 1) || m->alloc(&m->argmax_key, 1) || m->alloc(&m->rng, 1) ||
+        m->alloc(&m->samp_params, 2) || m->alloc(&m->samp_tok, 1) || m->alloc(&m->samp_probs, cfg.vocab) ||
+        m->alloc(&m->samp_prefix, cfg.vocab) || m->alloc(&m->samp_k0, cfg.vocab) ||
+        m->alloc(&m->samp_v0, cfg.vocab) || m->alloc(&m->samp_k1, cfg.vocab) || m->alloc(&m->samp_v1, cfg.vocab) ||
         m->alloc(&m->scores, (size_t)cfg.n_head * ((cfg.ctx + 3) & ~3)))
         return -1;
     CU(cudaMemset(m->err, 0, sizeof(int)));
@@ -917,12 +964,19 @@ extern "C" int cxm_sample(cxm_model *m, cxm_sampler *s, uint32_t *token_out) {
         set_error("no logits: call cxm_forward first");
         return -1;
     }
-    if (s->temperature > 0.0f) {
-        set_error("temperature sampling is not available yet");
-        return -1;
-    }
     CU(cudaSetDevice(m->device));
-    unsigned long long key = 0;
+    if (s->temperature > 0.0f) {  // the device Muestreador::elegir
+        if (set_sampler(m, s) || launch_sample(m, nullptr, nullptr, m->samp_tok)) return -1;
+        uint32_t tok = 0;
+        uint64_t st = 0;
+        CU(cudaMemcpyAsync(&tok, m->samp_tok, 4, cudaMemcpyDeviceToHost, m->stream));
+        CU(cudaMemcpyAsync(&st, m->rng, 8, cudaMemcpyDeviceToHost, m->stream));
+        CU(cudaStreamSynchronize(m->stream));
+        *token_out = tok;
+        s->state = st;
+        return 0;
+    }
+    unsigned long long key = 0;  // greedy: the first maximum (src/sampler.rs:129-137)
     CU(cudaStreamSynchronize(m->stream));
     CU(cudaMemcpy(&key, m->argmax_key, 8, cudaMemcpyDeviceToHost));
     *token_out = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
@@ -940,10 +994,7 @@ extern "C" int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, 
         set_error("no tokens to process");
         return -1;
     }
-    if (s->temperature > 0.0f) {
-        set_error("temperature sampling is not available yet");
-        return -1;
-    }
+    const bool sampled = s->temperature > 0.0f;
     const uint64_t after = (uint64_t)c->len + n_prompt;
     const uint64_t limit = std::min<uint64_t>((uint64_t)m->cfg.ctx, c->max_tokens);
     if (after > limit) {
@@ -972,7 +1023,9 @@ extern "C" int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, 
     const uint64_t gen = std::min<uint64_t>(max_new, limit - after + 1);
     const uint64_t fwd = std::min<uint64_t>(max_new, limit - after);
     // step i (0..gen) forwards toks[after-1+i] and writes token i at toks[after+i]
-    if (run_steps(m, c, STEP_GREEDY, (uint32_t)gen)) return -1;
+    const uint64_t state0 = s->state;
+    if (sampled && set_sampler(m, s)) return -1;
+    if (run_steps(m, c, sampled ? STEP_SAMPLE : STEP_GREEDY, (uint32_t)gen)) return -1;
     if (fwd == gen && run_steps(m, c, STEP_PREFILL, 1)) return -1;
     if (check_err(m)) return -1;
     std::vector<uint32_t> toks(gen);
@@ -988,6 +1041,18 @@ extern "C" int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, 
     }
     for (uint64_t i = 0; i < n; i++) out[i] = toks[i];
     *n_out = (uint32_t)n;
+    if (sampled) {  // one draw per pick, the eos pick included (src/forward.rs:544-548)
+        const uint64_t draws = n < gen ? n + 1 : gen;
+        uint64_t st = state0;
+        for (uint64_t i = 0; i < draws; i++) {
+            uint64_t x = st;
+            x ^= x >> 12;
+            x ^= x << 25;
+            x ^= x >> 27;
+            st = x;
+        }
+        s->state = st;
+    }
     uint32_t final_len = (uint32_t)(after + forwarded);
     if (set_len(c, final_len)) return -1;
     m->logits_valid = false;

@@ -80,7 +80,10 @@ void cxm_sampler_free(cxm_sampler *s);
 uint64_t cxm_sampler_state(const cxm_sampler *s);
 
 /* Muestreador::elegir (src/sampler.rs:61-126) on the logits of the model's
- * last forward, computed on the device. */
+ * last forward, computed on the device: greedy (first maximum) or, with
+ * temperature > 0, the reference's top-p draw with its sums in its order and
+ * equal probabilities ordered by index (the reference's unstable sort leaves
+ * their order unspecified). Advances the sampler's state like the reference. */
 int cxm_sample(cxm_model *m, cxm_sampler *s, uint32_t *token_out);
 
 /* Modelo::generar (src/forward.rs:533-559): forward the prompt, then

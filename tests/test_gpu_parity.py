@@ -239,3 +239,46 @@ def test_qwen3b_prompt_logits_and_64_greedy_tokens(qwen3b_path):
     otoks = om.generate(oc2, prompt, 64, O.Sampler(0, 0.0, 1.0))
     assert toks == otoks
     assert len(c2) == len(oc2) == 16 + 64
+
+
+# ── the sampler (src/sampler.rs:61-152: top-p 0.9, T 0.7) ──
+
+@pytest.mark.parametrize("temperature,top_p", [(0.7, 0.9), (0.05, 0.9), (1.0, 1.0), (2.0, 0.5), (0.7, 0.0)])
+def test_device_sampler_matches_oracle(tiny_path, temperature, top_p):
+    # one pick at a time on the same logits: the flat case (top-1024 mass
+    # below top_p: the whole vocabulary sorted), the peaked case (the 1024
+    # candidates), no nucleus (index order), and a cut at the first token
+    m = cx.Modelo(tiny_path)
+    prompt = prompt_of(5, 12, m.cfg.vocab)
+    c = m.cache()
+    logits = m.forward(prompt, c)
+    for seed in (42, 1, 99):
+        dev = cx.Muestreador(seed, temperature, top_p)
+        ref = O.Sampler(seed, temperature, top_p)
+        for _ in range(4):
+            assert m.elegir(dev) == ref.pick(logits)
+            assert dev.estado == ref.state
+
+
+def test_sampled_generation_matches_oracle(tiny_path):
+    m = cx.Modelo(tiny_path)
+    om = O.Model(tiny_path)
+    prompt = prompt_of(11, 24, m.cfg.vocab)
+    dev, ref = cx.Muestreador(42, 0.7, 0.9), O.Sampler(42, 0.7, 0.9)
+    c, oc = m.cache(), om.cache()
+    got = m.generar(prompt, 64, dev, c)
+    want = om.generate(oc, prompt, 64, ref)
+    assert got == want
+    assert dev.estado == ref.state
+    assert len(c) == len(oc)
+
+
+def test_qwen3b_vocab_sampler_matches_oracle(qwen3b_path):
+    # the 151,936-entry vocabulary at the benchmark's sampling settings
+    m = cx.Modelo(qwen3b_path)
+    prompt = prompt_of(3, 8, m.cfg.vocab)
+    logits = m.forward(prompt, m.cache(64))
+    dev, ref = cx.Muestreador(42, 0.7, 0.9), O.Sampler(42, 0.7, 0.9)
+    for _ in range(3):
+        assert m.elegir(dev) == ref.pick(logits)
+    assert dev.estado == ref.state
