@@ -2,11 +2,14 @@
 
     python -m cosxamix_b200.kernel_bench [--config qwen3b] [--reps 108]
                                          [--layers N] [--vocab V]
+                                         [--decode STEPS --prompt P]
 
 Times the gate|up matvec phase of the decode kernel: `reps` such phases in
 one launch, behind grid barriers as in the step, cycling over the model's
 layers so every phase streams its own weights (36 layers x 25 MB > L2).
 Prints the per-phase time and the algorithmic weight bytes per second.
+With --decode: prefills a seeded P-token prompt (one decode-kernel launch
+per token), then times STEPS greedy decode steps (one launch each).
 `--layers` / `--vocab` shrink the synthetic model (same matrix shapes) so an
 ncu capture holds little device memory; keep layers x 25 MB above the 126 MB
 L2 for DRAM figures to mean something.
@@ -31,6 +34,8 @@ def main() -> None:
     ap.add_argument("--reps", type=int, default=108)
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--vocab", type=int, default=0)
+    ap.add_argument("--decode", type=int, default=0)
+    ap.add_argument("--prompt", type=int, default=16)
     args = ap.parse_args()
     import bench
     import cosxamix_b200 as cx
@@ -50,6 +55,14 @@ def main() -> None:
     else:
         path = bench.ensure_model(args.config, args.seed)
     m = cx.Modelo(path)
+    if args.decode:
+        c = m.cache(min(m.cfg.ctx, args.prompt + args.decode + 8))
+        m.forward(bench.seeded_prompt(args.seed, args.prompt, m.cfg.vocab), c)
+        ms = m.bench_decode(c, args.decode) / args.decode
+        print(json.dumps({"kernel": "k_decode step", "config": args.config, "layers": args.layers or None,
+                          "prompt": args.prompt, "step_ms": round(ms, 4),
+                          "weight_gbs": round(m.weight_bytes / (ms / 1000) / 1e9, 1)}))
+        return
     ms, nbytes = m.bench_matvec(args.reps)
     print(json.dumps({"kernel": "k_decode gate|up phase", "config": args.config, "layers": args.layers or None,
                       "phase_us": round(ms * 1000, 3), "bytes_per_phase": nbytes,
