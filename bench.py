@@ -164,6 +164,62 @@ def run_reference(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_shared_prefix(args, rank: int, world: int, local: int) -> None:
+    """`--workload shared-prefix`: 64 conversations
+    sharing a 1024-token seeded system prefix, each with its own 64-token
+    suffix and 128 greedy tokens, sharded over the ranks (replicated weights,
+    no collective). Each rank prefills the prefix once (untimed setup), then
+    serves its conversations through the public API (copy the prefix,
+    cxm_generate). value = all ranks' generated tokens / the slowest rank's
+    time."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import cosxamix_b200 as cx
+    from cosxamix_b200 import serving
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=torch.device("cuda", local))
+    if rank == 0:
+        ensure_model(args.config, args.seed)
+    if world > 1:
+        dist.barrier()
+    m = cx.Modelo(model_path(args.config, args.seed), device=local)
+    work = serving.Workload(conversations=args.conversations, seed=args.seed)
+    mine = serving.shard(work.conversations, rank, world)
+    # warm-up: one conversation's worth, outside the timed region
+    serving.serve(m, serving.Workload(conversations=1, prefix=16, suffix=4, new_tokens=4, seed=args.seed + 7), [0],
+                  cx.Muestreador.voraz)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    _, secs, n = serving.serve(m, work, mine, cx.Muestreador.voraz)
+    torch.cuda.synchronize()
+    secs, n = serving.reduce_job(secs, n)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    v = n / secs
+    line = {
+        "metric": "shared-prefix serving tok/s (generated), 3B-shape Q4_K_M", "value": round(v, 3), "unit": "tok/s",
+        "n_gpus": world, "steps": work.conversations, "warmup": 1, "ms_per_step": round(secs * 1000 / max(1, len(mine)), 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8-dot/f32",
+        "data": "synthetic",
+        "config": {"workload": f"configs[3]: {work.conversations} conversations, shared {work.prefix}-token seeded "
+                               f"prefix (prefilled once per GPU), {work.suffix}-token suffix each, "
+                               f"{work.new_tokens} greedy tokens each",
+                   "parallelism": f"dp{world} (conversations sharded, replicated weights, no collective)"},
+        "generated_tokens": n,
+        "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * work.suffix,
+                "d2h_bytes_per_step": 4 * work.new_tokens, "api": "cxm_cache_copy_prefix + cxm_generate per conversation"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -175,6 +231,8 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "shared-prefix"])
+    ap.add_argument("--conversations", type=int, default=64)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -184,6 +242,9 @@ def main() -> None:
 
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.workload == "shared-prefix":
+        run_shared_prefix(args, rank, world, local)
         return
 
     import torch

@@ -194,6 +194,11 @@ class Cache:
         _check(lib().cxm_cache_copy_prefix(self.h, n, other.h))
         return other
 
+    def copiar_prefijo(self, src: "Cache", n: int) -> None:
+        """Become a copy of the first n tokens of `src` (Cache::prefijo into
+        this cache's own buffers, which keeps its captured decode graphs)."""
+        _check(lib().cxm_cache_copy_prefix(src.h, n, self.h))
+
     def capa(self, layer: int, v: bool = False) -> np.ndarray:
         cfg = self.modelo.cfg
         out = np.zeros(len(self) * cfg.n_head_kv * cfg.head_dim, np.float32)
