@@ -590,9 +590,13 @@ __host__ __device__ inline size_t attn_region(int max_pos) {
 // score[h][p] = (sequential dot of q_h and k_p over the head dim) · scale; an
 // item is one kv head and P positions, shared by the G query heads on it
 __device__ void phase_scores(const AtPhase &at, int n, float *region) {
-    const int tid = threadIdx.x, hd = at.hd, G = at.H / at.KV, P = at.P, kvd = at.KV * hd, c4 = hd / 4;
+    const int tid = threadIdx.x, hd = at.hd, G = at.H / at.KV, kvd = at.KV * hd, c4 = hd / 4;
+    // positions per item: enough items for every CTA, at most at.P (the
+    // region's capacity)
+    const int want = (at.KV * n + gridDim.x - 1) / gridDim.x;
+    const int P = want < 1 ? 1 : (want > at.P ? at.P : want);
     const int nchunk = (n + P - 1) / P, items = at.KV * nchunk;
-    float *ks = region, *qs = region + (size_t)P * (hd + 4);
+    float *ks = region, *qs = region + (size_t)at.P * (hd + 4);
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int g = item / nchunk, p0 = (item % nchunk) * P, cnt = min(P, n - p0);
         for (int i = tid; i < G * c4; i += kDW * 32) {
