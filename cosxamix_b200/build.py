@@ -26,7 +26,7 @@ CUDA_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-ffp
 
 CXX_SOURCES = ["gguf.cpp", "synth.cpp"]
 CU_SOURCES = ["model.cu"]
-HEADERS = ["cxm_internal.h", "kernels.cuh", "step_kernels.cuh"]
+HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith((".h", ".cuh")))
 
 
 def _newer(target: str, deps: list[str]) -> bool:

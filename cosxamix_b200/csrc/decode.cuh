@@ -175,9 +175,25 @@ struct __align__(16) Phase {
 };
 static_assert(sizeof(Phase) % 16 == 0, "phase descriptors are staged in 16-byte copies");
 
+// What a warp's tile walk needs of one matvec phase. The host writes one per
+// matvec phase, in program order, after the program's phases; each CTA
+// stages the table in shared memory, so crossing into the next phase costs
+// the walk no global-memory round trip.
+struct __align__(16) FeedPhase {
+    const uint8_t *b[3];  // segment bases
+    uint32_t g[3];        // group strides
+    int n0, n1;           // groups of segments 0 and 1 (segment 2 takes the rest)
+    int ngroup;
+    uint16_t p[3];        // bytes per super-block
+    uint16_t ntile, nblk, lpr, rpt, pad;
+};
+static_assert(sizeof(FeedPhase) == 64, "FeedPhase is four 16-byte chunks");
+
 struct DecodeArgs {
     const Phase *prog;
     int nphase;
+    const FeedPhase *feed;    // the matvec phases' walk table
+    int nfeed;
     unsigned *bar;            // grid-barrier counter, zeroed before each launch
     int *err;
     int *d_len;               // position of the token; NULL: position 0, no token checks
@@ -235,114 +251,216 @@ __device__ inline Act carve_act(unsigned char *region, int K, int need16, int ne
     return a;
 }
 
-// Activation quantization by the consumer warps, redundantly in every CTA,
-// from the activation `xin` (and the RMSNorm weights `wn`, NULL without the
-// norm) already staged in shared memory: optional RMSNorm
-// (src/kernels/scalar.rs:36-54, f64 sum of squares), then i8 per sub-block of
-// 16 and/or 32 (src/ops.rs:178-198).
-__device__ void quantize_act(const float *xin, const float *wn, int K, float eps, bool need16, bool need32,
-                             const Act &a, double *red, double *scale_s) {
+// The prologue of a matvec phase, redundantly in every CTA: its activation x
+// (written by other CTAs before the barrier, read through L2; or the token's
+// embedding row), RMSNorm when the phase has norm weights
+// (src/kernels/scalar.rs:36-54), then i8 per sub-block of 16 and/or 32
+// (src/ops.rs:178-198). The values live in registers: thread t takes, in
+// round i, the 8 values of half-chunk hc = i*256 + t (a chunk is 16 values;
+// a sub-block of 32 is the 4 half-chunks of 4 consecutive lanes).
+// RMSNorm: scale = 1 / sqrt(Σx²/K + eps) in f64, each op correctly rounded,
+// then f32(x·scale)·w. The f64 sum of f32 squares is taken per thread, then
+// across lanes and warps. A normed activation has at most two rounds, and
+// its norm weights are loaded before the grid barrier (they depend on
+// nothing). A plain one (the attention output, the FFN's hidden vector) is
+// first staged whole in shared memory by one bulk copy: a copy engine pulls
+// data that every CTA reads at once far faster than 256 threads' loads.
+constexpr int kMaxActivation = 16384;         // values of a quantized activation
+constexpr int kMaxNormed = 2 * kDW * 32 * 8;  // 4096: values of a normed one
+
+__device__ __forceinline__ void load8(const float *src, int hc, float (&x)[8], bool cg) {
+    const float4 *p = (const float4 *)src + 2 * hc;
+    const float4 u = cg ? __ldcg(p) : __ldg(p), w = cg ? __ldcg(p + 1) : __ldg(p + 1);
+    x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
+    x[4] = w.x; x[5] = w.y; x[6] = w.z; x[7] = w.w;
+}
+
+// round hc of x from the previous phase (zeros past the end)
+__device__ __forceinline__ void load_x(const MvPhase &P, int hc, float (&x)[8]) {
+    if (hc < (P.K >> 3)) {
+        load8(P.in, hc, x, true);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++) x[k] = 0.0f;
+    }
+}
+
+// one value of a k-quant embedding row (a call: the dequantizer stays out of
+// the inlined prologue)
+__device__ __noinline__ float embed_value(const QMat &E, int tok, int i) { return qm_dequant(E, tok, i); }
+
+// round hc of the token's embedding row; CTA 0 also starts the residual
+// stream with it
+__device__ __forceinline__ void load_embed(const MvPhase &P, uint32_t tok, int hc, float (&x)[8]) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) x[k] = 0.0f;
+    if (hc >= (P.K >> 3)) return;
+    if (P.e32) {
+        load8(P.e32 + (size_t)tok * P.K, hc, x, false);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++) x[k] = embed_value(P.E, (int)tok, 8 * hc + k);
+    }
+    if (blockIdx.x == 0) {
+        ((float4 *)P.x_out)[2 * hc] = make_float4(x[0], x[1], x[2], x[3]);
+        ((float4 *)P.x_out)[2 * hc + 1] = make_float4(x[4], x[5], x[6], x[7]);
+    }
+}
+
+// the norm weights of this thread's two rounds, loaded before the barrier
+struct NormW {
+    float w[2][8];
+};
+__device__ __forceinline__ void load_norm_w(const MvPhase &P, NormW &nw) {
+    const int tid = threadIdx.x, nh = P.K >> 3;
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int hc = r * kDW * 32 + tid;
+        if (hc < nh) {
+            load8(P.norm_w, hc, nw.w[r], false);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; k++) nw.w[r][k] = 0.0f;
+        }
+    }
+}
+
+__device__ __forceinline__ void norm8(float (&x)[8], double scale, const float (&w)[8]) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) x[k] = __fmul_rn(__double2float_rn(__dmul_rn((double)x[k], scale)), w[k]);
+}
+
+// i8 values of 8 elements against the sub-block's amax, packed, and their sum
+__device__ __forceinline__ int quant8(const float (&x)[8], float am, uint32_t &w0, uint32_t &w1) {
+    const float inv = am > 0.0f ? __fdiv_rn(127.0f, am) : 0.0f;
+    int sm = 0;
+    w0 = w1 = 0u;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int qv = (int)roundf(__fmul_rn(x[k], inv));
+        sm += qv;
+        if (k < 4) w0 |= ((uint32_t)qv & 0xFFu) << (8 * k);
+        else w1 |= ((uint32_t)qv & 0xFFu) << (8 * (k - 4));
+    }
+    return sm;
+}
+
+// R rounds (first half-chunk hc0, then hc0 + 256, ...) quantized stage by
+// stage in lockstep, so their latency chains (shuffles, divisions) overlap.
+// nh (= K/8) is a multiple of 32: a warp's lanes are all in range or all
+// out, and the shuffles see full warps; rounds past the end store nothing.
+template <int R>
+__device__ __forceinline__ void quant_rounds(const MvPhase &P, const Act &a, int hc0, const float (&x)[R][8]) {
+    const int nh = P.K >> 3;
+    float amax[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        amax[r] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) amax[r] = fmaxf(amax[r], fabsf(x[r][k]));
+    }
+    if (P.need16) {
+        float am[R];
+        int sm[R];
+        uint32_t w0[R], w1[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) am[r] = fmaxf(amax[r], __shfl_xor_sync(0xffffffffu, amax[r], 1));
+#pragma unroll
+        for (int r = 0; r < R; r++) sm[r] = quant8(x[r], am[r], w0[r], w1[r]);
+#pragma unroll
+        for (int r = 0; r < R; r++) sm[r] += __shfl_xor_sync(0xffffffffu, sm[r], 1);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const int hc = hc0 + r * kDW * 32, c = hc >> 1;
+            if (hc < nh) {
+                *(uint2 *)(a.q16 + ((16 * c) >> 8) * kXqStride + ((16 * c) & 255) + 8 * (hc & 1)) = make_uint2(w0[r], w1[r]);
+                if (!(hc & 1)) {
+                    a.e16[c] = am[r] > 0.0f ? __fdiv_rn(am[r], 127.0f) : 0.0f;
+                    a.s16[c] = (float)sm[r];
+                }
+            }
+        }
+    }
+    if (P.need32) {
+        float am[R];
+        int sm[R];
+        uint32_t w0[R], w1[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) am[r] = fmaxf(amax[r], __shfl_xor_sync(0xffffffffu, amax[r], 1));
+#pragma unroll
+        for (int r = 0; r < R; r++) am[r] = fmaxf(am[r], __shfl_xor_sync(0xffffffffu, am[r], 2));
+#pragma unroll
+        for (int r = 0; r < R; r++) sm[r] = quant8(x[r], am[r], w0[r], w1[r]);
+#pragma unroll
+        for (int r = 0; r < R; r++) sm[r] += __shfl_xor_sync(0xffffffffu, sm[r], 1);
+#pragma unroll
+        for (int r = 0; r < R; r++) sm[r] += __shfl_xor_sync(0xffffffffu, sm[r], 2);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const int hc = hc0 + r * kDW * 32, c = hc >> 1;
+            if (hc < nh) {
+                *(uint2 *)(a.q32 + ((16 * c) >> 8) * kXqStride + ((16 * c) & 255) + 8 * (hc & 1)) = make_uint2(w0[r], w1[r]);
+                if (!(hc & 3)) {
+                    a.e32[hc >> 2] = am[r] > 0.0f ? __fdiv_rn(am[r], 127.0f) : 0.0f;
+                    a.s32[hc >> 2] = (float)sm[r];
+                }
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void quantize_act(const MvPhase &P, uint32_t tok, const NormW &nw, const float *stage,
+                                             const Act &a, double *red) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = kDW * 32;
-    const bool norm = wn != nullptr;
-    double scale = 0.0;
-    if (norm) {
+    const int nr = ((P.K >> 3) + nt - 1) / nt;  // rounds
+    if (P.prologue != PRO_QUANT) {  // at most two rounds
+        float x[2][8];
+        if (P.prologue == PRO_EMBED) {
+            load_embed(P, tok, tid, x[0]);
+            load_embed(P, tok, nt + tid, x[1]);
+        } else {
+            load_x(P, tid, x[0]);
+            load_x(P, nt + tid, x[1]);
+        }
         double acc = 0.0;
-        for (int i = tid; i < (K >> 2); i += nt) {
-            const float4 v = ((const float4 *)xin)[i];
-            const double x0 = v.x, x1 = v.y, x2 = v.z, x3 = v.w;
-            acc = __dadd_rn(acc, __dmul_rn(x0, x0));
-            acc = __dadd_rn(acc, __dmul_rn(x1, x1));
-            acc = __dadd_rn(acc, __dmul_rn(x2, x2));
-            acc = __dadd_rn(acc, __dmul_rn(x3, x3));
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+#pragma unroll
+            for (int k = 0; k < 8; k++) acc = __dadd_rn(acc, __dmul_rn((double)x[r][k], (double)x[r][k]));
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
         if (lane == 0) red[warp] = acc;
         dsync();
-        if (tid == 0) {
-            double s = 0.0;
-            for (int w = 0; w < kDW; w++) s = __dadd_rn(s, red[w]);
-            *scale_s = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s, (double)K), (double)eps)));
-        }
-        dsync();
-        scale = *scale_s;
-    }
-    // a thread per 16 values: the sub-block of 16, or one half of a sub-block
-    // of 32 (its partner is the neighbouring lane); amax and the i8 sum are
-    // exact in any order
-    const int n16 = K >> 4;
-    for (int base = 0; base < n16; base += nt) {  // trip count uniform across the warp
-        const int c = base + tid;
-        const bool valid = c < n16;
-        float v[16];
-        float amax = 0.0f;
-        if (valid) {
+        // every thread finishes the reduction itself (same order, same result)
+        double sum = 0.0;
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const float4 x = ((const float4 *)xin)[4 * c + u];
-                v[4 * u] = x.x;
-                v[4 * u + 1] = x.y;
-                v[4 * u + 2] = x.z;
-                v[4 * u + 3] = x.w;
+        for (int w = 0; w < kDW; w++) sum = __dadd_rn(sum, red[w]);
+        const int K = P.K;
+        // Σ/K: a product by 1/K (exact) when K is a power of two
+        const double ms = (K & (K - 1)) == 0 ? __dmul_rn(sum, 1.0 / (double)K) : __ddiv_rn(sum, (double)K);
+        const double scale = __drcp_rn(__dsqrt_rn(__dadd_rn(ms, (double)P.eps)));
+        norm8(x[0], scale, nw.w[0]);
+        norm8(x[1], scale, nw.w[1]);
+        if (nr == 1) quant_rounds<1>(P, a, tid, *(const float(*)[1][8])x);
+        else quant_rounds<2>(P, a, tid, x);
+    } else {  // from the staged copy, two rounds at a time
+        const int nh = P.K >> 3;
+        for (int i = 0; i < nr; i += 2) {
+            float x[2][8];
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const int hc = (i + r) * nt + tid;
+                const float4 u = hc < nh ? ((const float4 *)stage)[2 * hc] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                const float4 w = hc < nh ? ((const float4 *)stage)[2 * hc + 1] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                x[r][0] = u.x; x[r][1] = u.y; x[r][2] = u.z; x[r][3] = u.w;
+                x[r][4] = w.x; x[r][5] = w.y; x[r][6] = w.z; x[r][7] = w.w;
             }
-            if (norm) {
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const float4 w = ((const float4 *)wn)[4 * c + u];
-                    v[4 * u] = __fmul_rn(__double2float_rn(__dmul_rn((double)v[4 * u], scale)), w.x);
-                    v[4 * u + 1] = __fmul_rn(__double2float_rn(__dmul_rn((double)v[4 * u + 1], scale)), w.y);
-                    v[4 * u + 2] = __fmul_rn(__double2float_rn(__dmul_rn((double)v[4 * u + 2], scale)), w.z);
-                    v[4 * u + 3] = __fmul_rn(__double2float_rn(__dmul_rn((double)v[4 * u + 3], scale)), w.w);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 16; u++) amax = fmaxf(amax, fabsf(v[u]));
-        } else {
-#pragma unroll
-            for (int u = 0; u < 16; u++) v[u] = 0.0f;
-        }
-        const int off = ((16 * c) >> 8) * kXqStride + ((16 * c) & 255);
-        if (need16 && valid) {
-            const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-            uint32_t w[4] = {0u, 0u, 0u, 0u};
-            int sm = 0;
-#pragma unroll
-            for (int u = 0; u < 16; u++) {
-                const int qv = (int)roundf(__fmul_rn(v[u], inv));
-                sm += qv;
-                w[u >> 2] |= ((uint32_t)qv & 0xFFu) << (8 * (u & 3));
-            }
-            *(uint4 *)(a.q16 + off) = make_uint4(w[0], w[1], w[2], w[3]);
-            a.e16[c] = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f;
-            a.s16[c] = (float)sm;
-        }
-        if (need32) {
-            const float am = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-            const float inv = am > 0.0f ? __fdiv_rn(127.0f, am) : 0.0f;
-            uint32_t w[4] = {0u, 0u, 0u, 0u};
-            int sm = 0;
-#pragma unroll
-            for (int u = 0; u < 16; u++) {
-                const int qv = (int)roundf(__fmul_rn(v[u], inv));
-                sm += qv;
-                w[u >> 2] |= ((uint32_t)qv & 0xFFu) << (8 * (u & 3));
-            }
-            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-            if (valid) {
-                *(uint4 *)(a.q32 + off) = make_uint4(w[0], w[1], w[2], w[3]);
-                if (!(c & 1)) {
-                    a.e32[c >> 1] = am > 0.0f ? __fdiv_rn(am, 127.0f) : 0.0f;
-                    a.s32[c >> 1] = (float)sm;
-                }
-            }
+            if (i + 1 < nr) quant_rounds<2>(P, a, i * nt + tid, x);
+            else quant_rounds<1>(P, a, i * nt + tid, *(const float(*)[1][8])x);
         }
     }
     dsync();
-}
-
-// stage n floats (n % 4 == 0) from global memory into shared memory
-__device__ __forceinline__ void stage_floats(float *dst, const float *src, int n) {
-    for (int i = threadIdx.x; i < (n >> 2); i += kDW * 32) cp_async16(dst + 4 * i, src + 4 * i);
 }
 
 // rows (r0, r1) of output unit u of a segment: the pair an epilogue combines
@@ -452,43 +570,36 @@ __device__ __forceinline__ void cta_groups(int ngroup, int &qb, int &qe) {
 // on the activations, so the copies overlap barriers, prologues and
 // attention.
 struct Feed {
-    int ph, q, qe, t;  // next tile: phase, phase-global group, tile
+    int m, q, qe, t;  // next tile: matvec phase (index into the walk table), phase-global group, tile
     int ntile, nblk, lpr, rpt;
-    int n0, n1;        // groups of segments 0 and 1 (segment 2 takes the rest)
-    int p0, p1, p2;    // bytes per super-block
+    int n0, n1;       // groups of segments 0 and 1 (segment 2 takes the rest)
+    int p0, p1, p2;   // bytes per super-block
     uint32_t g0, g1, g2;  // group strides
     const uint8_t *b0, *b1, *b2;
 };
 
-// position the walk at the first group of this warp in phase >= f.ph
-__device__ inline void feed_phase(const DecodeArgs &A, Feed &f, int warp) {
-    for (; f.ph < A.nphase; f.ph++) {
-        if (__ldg(&A.prog[f.ph].kind) != PH_MATVEC) continue;
-        const MvPhase &P = A.prog[f.ph].mv;
+// position the walk at the first group of this warp in matvec phase >= f.m
+__device__ inline void feed_phase(const FeedPhase *tab, int ntab, Feed &f, int warp) {
+    for (; f.m < ntab; f.m++) {
+        const FeedPhase &F = tab[f.m];
         int qb, qe;
-        cta_groups(__ldg(&P.ngroup), qb, qe);
+        cta_groups(F.ngroup, qb, qe);
         if (qb + warp >= qe) continue;
-        const int nseg = __ldg(&P.nseg);
-        f.ntile = __ldg(&P.ntile);
-        f.n0 = __ldg(&P.seg[0].M.ngroup);
-        f.p0 = __ldg(&P.seg[0].M.bpb);
-        f.g0 = __ldg(&P.seg[0].M.group_stride);
-        f.b0 = (const uint8_t *)__ldg((const unsigned long long *)&P.seg[0].M.base);
-        f.n1 = nseg > 1 ? __ldg(&P.seg[1].M.ngroup) : 0x7fffffff;
-        if (nseg > 1) {
-            f.p1 = __ldg(&P.seg[1].M.bpb);
-            f.g1 = __ldg(&P.seg[1].M.group_stride);
-            f.b1 = (const uint8_t *)__ldg((const unsigned long long *)&P.seg[1].M.base);
-        }
-        if (nseg > 2) {
-            f.p2 = __ldg(&P.seg[2].M.bpb);
-            f.g2 = __ldg(&P.seg[2].M.group_stride);
-            f.b2 = (const uint8_t *)__ldg((const unsigned long long *)&P.seg[2].M.base);
-        }
-        if (nseg == 1) f.n0 = 0x7fffffff;
-        f.nblk = __ldg(&P.seg[0].M.nblk);
-        f.lpr = __ldg(&P.seg[0].M.lpr);
-        f.rpt = __ldg(&P.seg[0].M.rpt);
+        f.ntile = F.ntile;
+        f.nblk = F.nblk;
+        f.lpr = F.lpr;
+        f.rpt = F.rpt;
+        f.n0 = F.n0;
+        f.n1 = F.n1;
+        f.p0 = F.p[0];
+        f.p1 = F.p[1];
+        f.p2 = F.p[2];
+        f.g0 = F.g[0];
+        f.g1 = F.g[1];
+        f.g2 = F.g[2];
+        f.b0 = F.b[0];
+        f.b1 = F.b[1];
+        f.b2 = F.b[2];
         f.q = qb + warp;
         f.qe = qe;
         f.t = 0;
@@ -496,8 +607,9 @@ __device__ inline void feed_phase(const DecodeArgs &A, Feed &f, int warp) {
     }
 }
 
-__device__ __forceinline__ bool feed_next(const DecodeArgs &A, Feed &f, int warp, const uint8_t *&src, uint32_t &bytes) {
-    if (f.ph >= A.nphase) return false;
+__device__ __forceinline__ bool feed_next(const FeedPhase *tab, int ntab, Feed &f, int warp, const uint8_t *&src,
+                                          uint32_t &bytes) {
+    if (f.m >= ntab) return false;
     int lq = f.q;
     const uint8_t *b;
     uint32_t gs;
@@ -517,8 +629,8 @@ __device__ __forceinline__ bool feed_next(const DecodeArgs &A, Feed &f, int warp
         f.t = 0;
         f.q += kDW;
         if (f.q >= f.qe) {
-            f.ph++;
-            feed_phase(A, f, warp);
+            f.m++;
+            feed_phase(tab, ntab, f, warp);
         }
     }
     return true;
@@ -722,6 +834,8 @@ struct Ring {
     int ns;
     uint32_t issued, consumed;
     int islot, cslot;  // slots of the next copy and of the next compute
+    const FeedPhase *tab;  // the walk table, in shared memory
+    int ntab;
     Feed feed;
 };
 
@@ -730,7 +844,7 @@ struct Ring {
 __device__ __forceinline__ const unsigned char *ring_next(const DecodeArgs &A, Ring &R, int warp, int lane) {
     const uint8_t *src;
     uint32_t bytes;
-    if (R.issued < R.consumed + (uint32_t)R.ns && feed_next(A, R.feed, warp, src, bytes)) {
+    if (R.issued < R.consumed + (uint32_t)R.ns && feed_next(R.tab, R.ntab, R.feed, warp, src, bytes)) {
         issue_tile(R.base + (size_t)R.islot * R.slot_bytes, src, bytes, lane);
         R.issued++;
         if (++R.islot == R.ns) R.islot = 0;
@@ -758,9 +872,9 @@ __device__ __forceinline__ void tile_terms(const unsigned char *tile, int lane, 
 }
 
 // One row group (rpt = 32/lpr rows x nblk super-blocks) of type T: returns,
-// in lanes 0..rpt-1, the rows' totals, each added term by term in sub-block
-// order (the lane of block j holds its terms until the row's running total
-// reaches it).
+// in every lane, the total of row (lane mod rpt), each added term by term in
+// block and sub-block order (the lane of block j holds its terms until the
+// row's running total reaches it).
 struct Lanes {  // a lane's place in this phase's tiles: lane = rpt*bl + sl
     int lpr, rpt, bl, sl, ntile;
 };
@@ -782,16 +896,20 @@ __device__ __forceinline__ float group_dot(const DecodeArgs &A, Ring &R, int war
             const int b = lpr * t + bl;
             const XB xb{xq + b * kXqStride, xe + b * NSUB, xs + b * NSUB};
             tile_terms<T>(tile, lane, rpt * nb, xb, tv);
+        } else {
+#pragma unroll
+            for (int k = 0; k < NSUB; k++) tv[k] = 0.0f;  // a lane past the tile's last block: its sums are dropped
         }
         __syncwarp();  // the slot may be refilled from here on
-        // each row's running total visits the tile's blocks in order
+        // each row's running total visits the tile's blocks in order: at hop
+        // jb every lane adds its own terms to the total it was handed, and
+        // the lane of block jb passes its result on (the others' results are
+        // dropped), so no lane waits on a divergent branch
         float run = acc;
         for (int jb = 0; jb < nb; jb++) {
             float v = run;
-            if (bl == jb) {
 #pragma unroll
-                for (int k = 0; k < NSUB; k++) v = fa(v, tv[k]);
-            }
+            for (int k = 0; k < NSUB; k++) v = fa(v, tv[k]);
             run = __shfl_sync(0xffffffffu, v, jb * rpt + sl);
         }
         acc = run;
@@ -806,11 +924,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
     const int ns = A.ring_slots;
     unsigned char *region = smem + (size_t)kDW * ns * A.slot_bytes;
     Phase *phbuf = (Phase *)(region + A.region_bytes);  // two staged phase descriptors
-    __shared__ __align__(8) uint64_t act_bar;           // bulk copies of a prologue's inputs
+    FeedPhase *ftab = (FeedPhase *)(phbuf + 2);         // the walk table
+    __shared__ __align__(8) uint64_t act_bar;  // the bulk copy of a quantize-only prologue's input
     __shared__ volatile int abort_flag;
     __shared__ int sync_ok;
     __shared__ double red[kDW];
-    __shared__ double scale_s;
     __shared__ unsigned long long best_s[kDW];
     __shared__ float fred[kDW];
     __shared__ float fbc;
@@ -842,6 +960,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         bad_s = bad;
     }
     if (tid < kDescWords) ((uint4 *)&phbuf[0])[tid] = __ldg((const uint4 *)&A.prog[0] + tid);
+    for (int i = tid; i < A.nfeed * 4; i += kDecodeThreads) ((uint4 *)ftab)[i] = __ldg((const uint4 *)A.feed + i);
     __syncthreads();
 
     // an invalid position or token stops every CTA before any work
@@ -859,62 +978,52 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
     R.ns = ns;
     R.issued = R.consumed = 0;
     R.islot = R.cslot = 0;
-    R.feed.ph = 0;
-    feed_phase(A, R.feed, warp);
+    R.tab = ftab;
+    R.ntab = A.nfeed;
+    R.feed.m = 0;
+    feed_phase(R.tab, R.ntab, R.feed, warp);
     {
         const uint8_t *src;
         uint32_t bytes;
-        while (R.issued < (uint32_t)ns - 1 && feed_next(A, R.feed, warp, src, bytes)) {
+        while (R.issued < (uint32_t)ns - 1 && feed_next(R.tab, R.ntab, R.feed, warp, src, bytes)) {
             issue_tile(R.base + (size_t)R.islot * R.slot_bytes, src, bytes, lane);
             R.issued++;
             if (++R.islot == ns) R.islot = 0;
         }
     }
-    uint32_t act_phase = 0;
     unsigned nbar = 0;
+    uint32_t act_phase = 0;
     bool stop = false;
     for (int pi = 0; pi < A.nphase && !stop; pi++) {
         const Phase &ph = phbuf[pi & 1];
         uint4 nextd = make_uint4(0, 0, 0, 0);  // the next descriptor, stored at the end of this phase
         if (pi + 1 < A.nphase && tid < kDescWords) nextd = __ldg((const uint4 *)&A.prog[pi + 1] + tid);
-        // A matvec's norm weights depend on nothing: their copy starts before
-        // the barrier (the region is free: every warp left the last phase).
-        const bool mv = ph.kind == PH_MATVEC;
-        const bool has_norm = mv && ph.mv.prologue != PRO_QUANT;
-        const uint32_t kbytes = mv ? (uint32_t)ph.mv.K * 4u : 0u;
-        float *xin = mv ? (float *)(region + act_bytes(ph.mv.K, ph.mv.need16, ph.mv.need32)) : nullptr;
-        float *wn = has_norm ? xin + ph.mv.K : nullptr;
-        if (mv && tid == 0) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive_expect_tx(&act_bar, (ph.mv.prologue != PRO_EMBED ? kbytes : 0u) + (has_norm ? kbytes : 0u));
-            if (has_norm) bulk_g2s(wn, ph.mv.norm_w, kbytes, &act_bar);
-        }
+        // a normed matvec's weights depend on nothing: loaded before the barrier
+        NormW nw;
+        if (ph.kind == PH_MATVEC && ph.mv.prologue != PRO_QUANT) load_norm_w(ph.mv, nw);
         if (ph.barrier) {
             nbar++;
-            if (!grid_sync(A, nbar * gridDim.x, &abort_flag, &sync_ok)) {  // uniform
-                if (mv) mbar_wait_bounded(&act_bar, act_phase, &abort_flag, 1u << 14);  // no copy left in flight
-                break;
-            }
+            if (!grid_sync(A, nbar * gridDim.x, &abort_flag, &sync_ok)) break;  // uniform
         }
         const int n = pos + 1;
         if (ph.kind == PH_MATVEC) {
             const MvPhase &P = ph.mv;
             const Act act = carve_act(region, P.K, P.need16, P.need32);
-            // the activation (written by other CTAs before the barrier)
-            if (tid == 0 && P.prologue != PRO_EMBED) bulk_g2s(xin, P.in, kbytes, &act_bar);
-            if (P.prologue == PRO_EMBED) {
-                for (int i = tid; i < P.K; i += kDW * 32) {
-                    const float v = P.e32 ? __ldg(P.e32 + (size_t)tok * P.K + i) : qm_dequant(P.E, (int)tok, i);
-                    xin[i] = v;
-                    if (blockIdx.x == 0) P.x_out[i] = v;
+            if (P.prologue == PRO_EMBED && blockIdx.x == 0 && tid == 0 && A.argmax_key) *A.argmax_key = 0ull;
+            float *stage = (float *)(region + act_bytes(P.K, P.need16, P.need32));
+            if (P.prologue == PRO_QUANT) {
+                const uint32_t kbytes = (uint32_t)P.K * 4u;
+                if (tid == 0) {
+                    // the staging area was last read through the generic proxy
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive_expect_tx(&act_bar, kbytes);
+                    bulk_g2s(stage, P.in, kbytes, &act_bar);
                 }
-                if (blockIdx.x == 0 && tid == 0 && A.argmax_key) *A.argmax_key = 0ull;
+                const bool landed = mbar_wait_bounded(&act_bar, act_phase, &abort_flag);
+                act_phase ^= 1u;
+                if (!landed) abort_flag = 1;
             }
-            const bool landed = mbar_wait_bounded(&act_bar, act_phase, &abort_flag);
-            act_phase ^= 1u;
-            if (!landed) abort_flag = 1;
-            dsync();
-            quantize_act(xin, wn, P.K, P.eps, P.need16, P.need32, act, red, &scale_s);
+            quantize_act(P, tok, nw, stage, act, red);
             unsigned long long best = 0ull;
             int qb, qe;
             cta_groups(P.ngroup, qb, qe);
@@ -943,10 +1052,28 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
                 __syncwarp();
                 nepi = 0;
             };
+            // the segments' fields, in registers: the descriptor lives in shared
+            // memory, which every asm memory clobber in the tile loop would
+            // otherwise make the group loop load again
+            const int nseg = P.nseg;
+            const int sn0 = P.seg[0].M.ngroup, sn1 = nseg > 1 ? P.seg[1].M.ngroup : 0;
+            const int sT0 = P.seg[0].M.type, sT1 = nseg > 1 ? P.seg[1].M.type : 0, sT2 = nseg > 2 ? P.seg[2].M.type : 0;
+            const int sb0 = P.seg[0].M.nblk, sb1 = nseg > 1 ? P.seg[1].M.nblk : 0, sb2 = nseg > 2 ? P.seg[2].M.nblk : 0;
+            const int su0 = P.seg[0].units, su1 = nseg > 1 ? P.seg[1].units : 0, su2 = nseg > 2 ? P.seg[2].units : 0;
             for (int q0 = qb + warp; q0 < qe; q0 += kDW) {
-                int j = 0, lq = q0;  // phase-global group index -> segment, local group
-                while (j < P.nseg - 1 && lq >= P.seg[j].M.ngroup) lq -= P.seg[j++].M.ngroup;
-                const int T = P.seg[j].M.type, nblk = P.seg[j].M.nblk;
+                // phase-global group index -> segment j, local group lq
+                int j = 0, lq = q0;
+                if (nseg > 1 && lq >= sn0) {
+                    lq -= sn0;
+                    j = 1;
+                    if (nseg > 2 && lq >= sn1) {
+                        lq -= sn1;
+                        j = 2;
+                    }
+                }
+                const int T = j == 0 ? sT0 : (j == 1 ? sT1 : sT2);
+                const int nblk = j == 0 ? sb0 : (j == 1 ? sb1 : sb2);
+                const int units = j == 0 ? su0 : (j == 1 ? su1 : su2);
                 float acc;
                 switch (T) {
                 case 12: acc = group_dot<12>(A, R, warp, lane, nblk, g, act); break;
@@ -960,13 +1087,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
                 const float other = __shfl_down_sync(0xffffffffu, acc, 1);
                 if (nepi + upg > 32) flush();
                 const int u = (lq * g.rpt + g.sl) >> 1;
-                if (lane < g.rpt && !(g.sl & 1) && u < P.seg[j].units) {
+                if (lane < g.rpt && !(g.sl & 1) && u < units) {
                     epi_su[warp][nepi + (g.sl >> 1)] = make_int2(j, u);
                     epi_y[warp][nepi + (g.sl >> 1)] = make_float2(acc, other);
                 }
                 // units past the segment's end (zero rows of a padded group)
                 // are left in place with their unit index and skipped below
-                if (lane < g.rpt && !(g.sl & 1) && u >= P.seg[j].units) epi_su[warp][nepi + (g.sl >> 1)] = make_int2(j, -1);
+                if (lane < g.rpt && !(g.sl & 1) && u >= units) epi_su[warp][nepi + (g.sl >> 1)] = make_int2(j, -1);
                 nepi += upg;
             }
             if (nepi) flush();

@@ -86,8 +86,10 @@ struct cxm_model {
 
 // a decode program on the device and the launch geometry it needs
 struct Program {
-    Phase *d = nullptr;
+    Phase *d = nullptr;  // the phases, then the walk table (one allocation)
     int n = 0;
+    const FeedPhase *feed = nullptr;
+    int nfeed = 0;
     size_t region = 0;
 };
 
@@ -244,6 +246,11 @@ int check_matrix(const TensorInfo &t) {
                   (unsigned long long)t.dims[0]);
         return -1;
     }
+    if (t.dims[0] > (uint64_t)kMaxActivation) {
+        set_error("%s: rows of %llu values: the decode kernel quantizes activations of at most %d", t.name.c_str(),
+                  (unsigned long long)t.dims[0], kMaxActivation);
+        return -1;
+    }
     return 0;
 }
 
@@ -393,9 +400,9 @@ Phase mv_phase(const std::vector<MvSeg> &segs, int K, int prologue, const float 
 }
 
 size_t phase_region(const Phase &ph, int max_pos) {
-    if (ph.kind == PH_MATVEC)  // quantized activation + staged activation (+ norm weights)
+    if (ph.kind == PH_MATVEC)  // the quantized activation (+ the staged input of a quantize-only prologue)
         return act_bytes(ph.mv.K, ph.mv.need16, ph.mv.need32) +
-               (size_t)ph.mv.K * sizeof(float) * (ph.mv.prologue == PRO_QUANT ? 1 : 2);
+               (ph.mv.prologue == PRO_QUANT ? (size_t)ph.mv.K * sizeof(float) : 0);
     if (ph.kind == PH_SCORES) return scores_region(ph.at.P, ph.at.H / ph.at.KV, ph.at.hd);
     if (ph.kind == PH_ATTN) return attn_region(max_pos);
     return 0;
@@ -473,22 +480,51 @@ std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode) {
     return prog;
 }
 
+// one walk-table entry per matvec phase, in program order
+std::vector<FeedPhase> feed_table(const std::vector<Phase> &ph) {
+    std::vector<FeedPhase> t;
+    for (const Phase &x : ph) {
+        if (x.kind != PH_MATVEC) continue;
+        const MvPhase &P = x.mv;
+        FeedPhase f{};
+        for (int i = 0; i < P.nseg; i++) {
+            f.b[i] = P.seg[i].M.base;
+            f.g[i] = P.seg[i].M.group_stride;
+            f.p[i] = (uint16_t)P.seg[i].M.bpb;
+        }
+        f.n0 = P.nseg > 1 ? P.seg[0].M.ngroup : 0x7fffffff;
+        f.n1 = P.nseg > 2 ? P.seg[1].M.ngroup : 0x7fffffff;
+        f.ngroup = P.ngroup;
+        f.ntile = (uint16_t)P.ntile;
+        f.nblk = (uint16_t)P.seg[0].M.nblk;
+        f.lpr = (uint16_t)P.seg[0].M.lpr;
+        f.rpt = (uint16_t)P.seg[0].M.rpt;
+        t.push_back(f);
+    }
+    return t;
+}
+
 int upload_program(const std::vector<Phase> &ph, int max_pos, Program *out) {
     Program p;
     p.n = (int)ph.size();
     for (const Phase &x : ph) p.region = std::max(p.region, phase_region(x, max_pos));
     p.region = (p.region + 127) & ~(size_t)127;
-    CU(cudaMalloc(&p.d, ph.size() * sizeof(Phase)));
-    CU(cudaMemcpy(p.d, ph.data(), ph.size() * sizeof(Phase), cudaMemcpyHostToDevice));
+    const std::vector<FeedPhase> ft = feed_table(ph);
+    p.nfeed = (int)ft.size();
+    const size_t pb = ph.size() * sizeof(Phase), fb = ft.size() * sizeof(FeedPhase);
+    CU(cudaMalloc(&p.d, pb + fb));
+    CU(cudaMemcpy(p.d, ph.data(), pb, cudaMemcpyHostToDevice));
+    p.feed = (const FeedPhase *)((const char *)p.d + pb);
+    if (fb) CU(cudaMemcpy((void *)p.feed, ft.data(), fb, cudaMemcpyHostToDevice));
     *out = p;
     return 0;
 }
 
 // Shared memory of a decode launch: per-warp tile rings (as many slots as
 // fit, at most kMaxSlots), the activation/attention region, two staged
-// phase descriptors.
+// phase descriptors, the walk table.
 int decode_geometry(uint32_t slot_bytes, const Program &p, DecodeArgs &a, size_t *smem) {
-    const size_t fixed = p.region + 2 * sizeof(Phase) + 128;
+    const size_t fixed = p.region + 2 * sizeof(Phase) + (size_t)p.nfeed * sizeof(FeedPhase) + 128;
     const uint32_t slot = (std::max<uint32_t>(slot_bytes, 16) + 127) & ~127u;
     const long long room = (long long)g_decode_smem_max - (long long)fixed;
     const int ns = (int)std::min<long long>(kMaxSlots, room > 0 ? room / ((long long)kDW * slot) : 0);
@@ -500,6 +536,10 @@ int decode_geometry(uint32_t slot_bytes, const Program &p, DecodeArgs &a, size_t
     a.ring_slots = ns;
     a.slot_bytes = slot;
     a.region_bytes = (uint32_t)p.region;
+    a.prog = p.d;
+    a.nphase = p.n;
+    a.feed = p.feed;
+    a.nfeed = p.nfeed;
     *smem = (size_t)kDW * ns * slot + fixed;
     return 0;
 }
@@ -757,6 +797,10 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
         m->layers.push_back(L);
     }
     cfg.ffn = m->layers.empty() ? 0 : m->layers[0].gu.rows / 2;
+    if (cfg.dim > kMaxNormed) {
+        set_error("hidden size %d: the decode kernel's RMSNorm prologue takes at most %d", cfg.dim, kMaxNormed);
+        return -1;
+    }
     // RoPE tables exactly as src/ops.rs:1108-1129 (f32 frequency, f64 angle)
     {
         const int half = cfg.head_dim / 2;
@@ -1142,8 +1186,8 @@ extern "C" int cxm_debug_subblock_sums(int type, const uint8_t *row, const int8_
 
 extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint32_t k, const float *x, float *y) {
     if (need_device()) return -1;
-    if (!w || !x || !y || rows % 2 || rows == 0 || !is_kquant(type) || k == 0 || k % 256) {
-        set_error("bad arguments (k-quant type, k a multiple of 256, rows even)");
+    if (!w || !x || !y || rows % 2 || rows == 0 || !is_kquant(type) || k == 0 || k % 256 || k > kMaxActivation) {
+        set_error("bad arguments (k-quant type, k a multiple of 256 up to %d, rows even)", kMaxActivation);
         return -1;
     }
     // the decode kernel on a one-phase program: quantize x, W·x, store
@@ -1167,11 +1211,8 @@ extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint3
     Phase ph = mv_phase({mv_seg(M, (int)rows / 2, PAIR_ADJ, EPI_STORE, (float *)dy.p)}, (int)k, PRO_QUANT,
                         (const float *)dx.p, nullptr, 0.0f, 0);
     Program prog;
-    prog.n = 1;
-    prog.region = (phase_region(ph, 0) + 127) & ~(size_t)127;
-    CU(cudaMalloc(&dprog.p, sizeof(Phase)));
-    CU(cudaMemcpy(dprog.p, &ph, sizeof(Phase), cudaMemcpyHostToDevice));
-    prog.d = (Phase *)dprog.p;
+    if (upload_program({ph}, 0, &prog)) return -1;
+    dprog.p = prog.d;
     int dev = 0, sms = 148;
     CU(cudaGetDevice(&dev));
     CU(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));

@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
     extern __shared__ __align__(16) float stage[];  // 2 x kScanChunk
     __shared__ float red[kSampWarps];
     __shared__ uint32_t hist[256 * kSampWarps];
-    __shared__ float u_s, total_s, sum_s;
+    __shared__ float u_s, sum_s;
     __shared__ int flag_s;
     const int tid = threadIdx.x, n = a.n;
     const float inv_t = a.params[0], top_p = a.params[1];
