@@ -220,6 +220,74 @@ def run_shared_prefix(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_formats(args, rank: int, world: int, local: int) -> None:
+    """`--workload formats`: the Qwen2.5-3B shape
+    re-quantized uniformly to Q5_K, Q3_K and Q2_K, one model after the other:
+    128-token seeded prompt (untimed prefill), then sampled decode at
+    temperature 0.7, top-p 0.9 (seed 42), every step the decode kernel plus
+    the device sampler. Per format: device-timed tok/s and weight-stream GB/s.
+    Each rank runs its own conversation (replicated weights, no collective)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import cosxamix_b200 as cx
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=torch.device("cuda", local))
+    peak, peak_kind = peaks()
+    out = {}
+    total_ms = 0.0
+    for fmt in ("q5k", "q3k", "q2k"):
+        name = f"qwen3b_{fmt}"
+        if rank == 0:
+            ensure_model(name, args.seed)
+        if world > 1:
+            dist.barrier()
+        m = cx.Modelo(model_path(name, args.seed), device=local)
+        cache = m.cache(args.prompt + args.warmup + args.steps + 8)
+        m.forward(seeded_prompt(args.seed + rank, args.prompt, m.cfg.vocab), cache)
+        samp = cx.Muestreador(42, 0.7, 0.9)
+        m.bench_decode(cache, args.warmup, samp)
+        clocks = Clocks(local)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ms = m.bench_decode(cache, args.steps, samp)
+        clk = clocks.stop()
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        tok_s = world * args.steps / (ms / 1000.0)
+        gbs = m.weight_bytes / (ms / args.steps / 1000.0) / 1e9
+        out[fmt] = {"tok_s": round(tok_s, 3), "ms_per_step": round(ms / args.steps, 4),
+                    "weight_bytes": m.weight_bytes, "weight_gbs_per_gpu": round(gbs, 1),
+                    "frac": round(gbs / peak, 4), "clocks": clk}
+        total_ms += ms
+        del cache, m
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = world * 3 * args.steps / (total_ms / 1000.0)
+    line = {
+        "metric": "decode tok/s bs=1, 3B-shape uniform Q5_K/Q3_K/Q2_K, top-p 0.9 T 0.7; weight-stream GB/s per format",
+        "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_ms / (3 * args.steps), 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
+        "config": {"workload": f"configs[2]: qwen2.5-3B shape, uniform Q5_K, Q3_K, Q2_K (three models), "
+                               f"{args.prompt}-token seeded prompt, sampled decode (seed 42, T 0.7, top-p 0.9)",
+                   "parallelism": f"dp{world} (independent conversations, replicated weights)",
+                   "l2": "inputs larger than L2: 1.0-2.1 GB of weights streamed per step vs 126 MB L2"},
+        "formats": out, "peak_gbs": peak, "peak_kind": peak_kind,
+        "gpu_launches": 3 * args.steps * 2,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -231,7 +299,7 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "shared-prefix"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "shared-prefix", "formats"])
     ap.add_argument("--conversations", type=int, default=64)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -245,6 +313,11 @@ def main() -> None:
         return
     if args.workload == "shared-prefix":
         run_shared_prefix(args, rank, world, local)
+        return
+    if args.workload == "formats":
+        if args.prompt == 512:  # the default of the main workload; configs[2] prompts with 128
+            args.prompt = 128
+        run_formats(args, rank, world, local)
         return
 
     import torch

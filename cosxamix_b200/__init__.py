@@ -24,6 +24,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libcxm.so")
 
 Q2_K, Q3_K, Q4_K, Q5_K, Q6_K = 10, 11, 12, 13, 14
+TP_HANDLE_BYTES = 64  # CXM_TP_HANDLE_BYTES
 MIX_UNIFORM, MIX_Q4_K_M = 0, 1
 
 _lib = None
@@ -51,6 +52,11 @@ def lib() -> C.CDLL:
         sig = {
             "cxm_last_error": (C.c_char_p, []),
             "cxm_model_open": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(P)]),
+            "cxm_model_open_tp": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_int, C.POINTER(P)]),
+            "cxm_tp_handle": (C.c_int, [P, P]),
+            "cxm_tp_connect": (C.c_int, [P, P]),
+            "cxm_model_tp_info": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                            C.POINTER(C.c_int)]),
             "cxm_model_config": (C.c_int, [P, C.POINTER(Config)]),
             "cxm_model_weight_bytes": (C.c_uint64, [P]),
             "cxm_model_close": (None, [P]),
@@ -73,6 +79,7 @@ def lib() -> C.CDLL:
             "cxm_debug_expf": (C.c_int, [P, P, C.c_uint64]),
             "cxm_attention_noalloc": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P, P]),
             "cxm_bench_decode": (C.c_int, [P, P, C.c_uint32, C.POINTER(C.c_float)]),
+            "cxm_bench_decode_sampled": (C.c_int, [P, P, P, C.c_uint32, C.POINTER(C.c_float)]),
             "cxm_bench_matvec": (C.c_int, [P, C.c_uint32, C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
             "cxm_step_launches": (C.c_int, [P]),
             "cxm_synth_write": (C.c_int, [C.POINTER(SynthSpec), C.c_char_p]),
@@ -109,6 +116,17 @@ CONFIGS = {
     # Qwen2.5-3B shape, Q4_K_M-style, tied embeddings
     "qwen3b": dict(vocab=151936, dim=2048, n_layer=36, n_head=16, n_head_kv=2, ffn=11008, ctx=4096, eps=1e-6,
                    rope_base=1e6, tied=1, mix=MIX_Q4_K_M, type=Q4_K),
+    # the Qwen2.5-3B shape re-quantized uniformly (output included)
+    "qwen3b_q5k": dict(vocab=151936, dim=2048, n_layer=36, n_head=16, n_head_kv=2, ffn=11008, ctx=4096, eps=1e-6,
+                       rope_base=1e6, tied=1, mix=MIX_UNIFORM, type=Q5_K),
+    "qwen3b_q3k": dict(vocab=151936, dim=2048, n_layer=36, n_head=16, n_head_kv=2, ffn=11008, ctx=4096, eps=1e-6,
+                       rope_base=1e6, tied=1, mix=MIX_UNIFORM, type=Q3_K),
+    "qwen3b_q2k": dict(vocab=151936, dim=2048, n_layer=36, n_head=16, n_head_kv=2, ffn=11008, ctx=4096, eps=1e-6,
+                       rope_base=1e6, tied=1, mix=MIX_UNIFORM, type=Q2_K),
+    # a small Llama-style shape that splits over 2 or 4 tensor-parallel ranks
+    # (whole heads, o/down K slices of whole super-blocks): the TP tests' model
+    "tp_small": dict(vocab=8192, dim=1024, n_layer=4, n_head=8, n_head_kv=4, ffn=2048, ctx=512, eps=1e-5,
+                     rope_base=5e5, tied=0, mix=MIX_Q4_K_M, type=Q4_K),
     # Llama-3-8B shape, Q4_K_M-style, untied
     "llama8b": dict(vocab=128256, dim=4096, n_layer=32, n_head=32, n_head_kv=8, ffn=14336, ctx=8192, eps=1e-5,
                     rope_base=5e5, tied=0, mix=MIX_Q4_K_M, type=Q4_K),
@@ -216,13 +234,35 @@ class Cache:
 class Modelo:
     """Modelo::abrir(ruta) on a CUDA device (src/forward.rs:187-266)."""
 
-    def __init__(self, ruta: str, device: int = 0):
+    def __init__(self, ruta: str, device: int = 0, tp: tuple[int, int] | None = None):
+        """`tp=(rank, size)`: this process's share of a tensor-parallel model
+        (one process per GPU); it runs after `tp_connect`."""
         h = P()
-        _check(lib().cxm_model_open(ruta.encode(), device, C.byref(h)))
+        if tp is None:
+            _check(lib().cxm_model_open(ruta.encode(), device, C.byref(h)))
+        else:
+            _check(lib().cxm_model_open_tp(ruta.encode(), device, int(tp[0]), int(tp[1]), C.byref(h)))
         self.h = h
         self.cfg = Config()
         _check(lib().cxm_model_config(h, C.byref(self.cfg)))
         self.ruta = ruta
+        r, n, lo, vn = (C.c_int() for _ in range(4))
+        _check(lib().cxm_model_tp_info(h, C.byref(r), C.byref(n), C.byref(lo), C.byref(vn)))
+        self.tp_rank, self.tp_size, self.vocab_lo, self.vocab_n = r.value, n.value, lo.value, vn.value
+
+    # ── tensor parallelism ──
+    def tp_handle(self) -> bytes:
+        """The CUDA IPC handle of this rank's exchange area."""
+        buf = (C.c_uint8 * TP_HANDLE_BYTES)()
+        _check(lib().cxm_tp_handle(self.h, buf))
+        return bytes(buf)
+
+    def tp_connect(self, handles: list[bytes]) -> None:
+        """Map every rank's exchange area (handles in rank order)."""
+        if len(handles) != self.tp_size or any(len(x) != TP_HANDLE_BYTES for x in handles):
+            raise ValueError(f"need {self.tp_size} handles of {TP_HANDLE_BYTES} bytes")
+        buf = (C.c_uint8 * (TP_HANDLE_BYTES * self.tp_size)).from_buffer_copy(b"".join(handles))
+        _check(lib().cxm_tp_connect(self.h, buf))
 
     abrir = classmethod(lambda cls, ruta, device=0: cls(ruta, device))
     open = abrir
@@ -235,9 +275,11 @@ class Modelo:
         return Cache(self, max_tokens)
 
     def forward(self, tokens, cache: Cache) -> np.ndarray:
-        """Logits of the last token; extends `cache` (src/forward.rs:375-505)."""
+        """Logits of the last token; extends `cache` (src/forward.rs:375-505).
+        A tensor-parallel rank returns its vocabulary rows
+        [vocab_lo, vocab_lo + vocab_n)."""
         t = np.ascontiguousarray(tokens, np.uint32)
-        out = np.zeros(self.cfg.vocab, np.float32)
+        out = np.zeros(self.vocab_n, np.float32)
         _check(lib().cxm_forward(self.h, cache.h, _ptr(t) if t.size else None, t.size, _ptr(out)))
         return out
 
@@ -259,9 +301,14 @@ class Modelo:
     generate = generar
 
     # measurement hooks (device-timed; include/cxm.h)
-    def bench_decode(self, cache: Cache, steps: int) -> float:
+    def bench_decode(self, cache: Cache, steps: int, sampler: "Muestreador | None" = None) -> float:
+        """Device time (ms) of `steps` decode steps replayed from the cache's
+        end: greedy, or sampled with `sampler` (temperature > 0)."""
         ms = C.c_float(0)
-        _check(lib().cxm_bench_decode(self.h, cache.h, steps, C.byref(ms)))
+        if sampler is None:
+            _check(lib().cxm_bench_decode(self.h, cache.h, steps, C.byref(ms)))
+        else:
+            _check(lib().cxm_bench_decode_sampled(self.h, cache.h, sampler.h, steps, C.byref(ms)))
         return ms.value
 
     def bench_matvec(self, reps: int):

@@ -139,13 +139,16 @@ __device__ inline float qm_dequant(const QMat &M, int r, int idx) {
 }
 
 // ── the program ──
-enum PhaseKind : int { PH_MATVEC = 0, PH_SCORES = 1, PH_ATTN = 2, PH_COMMIT = 3 };
+// PH_XREDUCE / PH_XARGMAX: the tensor-parallel exchanges with the other ranks
+// (GPUs) of the model, over their exchange areas mapped into this process
+enum PhaseKind : int { PH_MATVEC = 0, PH_SCORES = 1, PH_ATTN = 2, PH_COMMIT = 3, PH_XREDUCE = 4, PH_XARGMAX = 5 };
 
 struct MvSeg {
     QMat M;
     int units;                // output units (row pairs); padded groups hold more
     int pairing, epi, half;   // Pairing, Epilogue; half = head_dim/2 for PAIR_ROPE
     int at_pos, pos_stride;   // out += pos*pos_stride (K/V cache rows)
+    int idx_off;              // EPI_LOGITS: vocabulary index of row 0 (this rank's slice)
     const float *bias;
     float *out;
 };
@@ -168,10 +171,19 @@ struct AtPhase {
     float scale;
 };
 
+// an exchange: PH_XREDUCE adds Σ over ranks (in rank order) of partial
+// vector `parity` to dst[0..n); PH_XARGMAX takes the largest argmax key.
+// `seq`: the exchange's number in the program (from 1), its flag epoch.
+struct XPhase {
+    float *dst;
+    int n, parity, seq;
+};
+
 struct __align__(16) Phase {
     int kind, barrier;  // barrier: a grid barrier comes first
     MvPhase mv;
     AtPhase at;
+    XPhase xp;
 };
 static_assert(sizeof(Phase) % 16 == 0, "phase descriptors are staged in 16-byte copies");
 
@@ -189,9 +201,21 @@ struct __align__(16) FeedPhase {
 };
 static_assert(sizeof(FeedPhase) == 64, "FeedPhase is four 16-byte chunks");
 
+// A rank's exchange area, mapped by its peers through CUDA IPC: the two
+// partial vectors [2][xdim] f32 (o_proj's and ffn_down's, alternating), the
+// argmax keys [kTpMax] (slot p written by rank p), the flags [kTpMax] (slot p
+// written by rank p: the epoch of its last exchange).
+constexpr int kTpMax = 8;
+__host__ __device__ inline size_t xch_keys_off(int xdim) { return (size_t)2 * xdim * sizeof(float); }
+__host__ __device__ inline size_t xch_flags_off(int xdim) { return xch_keys_off(xdim) + kTpMax * sizeof(uint64_t); }
+__host__ __device__ inline size_t xch_bytes(int xdim) { return xch_flags_off(xdim) + kTpMax * sizeof(unsigned); }
+
 struct DecodeArgs {
     const Phase *prog;
     int nphase;
+    int tp, tp_rank, xdim, nx;      // ranks; this one; partial length; exchanges in the program
+    unsigned char *xch[kTpMax];     // every rank's exchange area (this rank's own at tp_rank)
+    unsigned *epoch;                // exchanges completed by earlier launches (this rank)
     const FeedPhase *feed;    // the matvec phases' walk table
     int nfeed;
     unsigned *bar;            // grid-barrier counter, zeroed before each launch
@@ -546,8 +570,8 @@ __device__ void unit_epilogue(const DecodeArgs &A, const MvSeg &g, int r0, int r
     case EPI_LOGITS: {
         out[r0] = y0;
         out[r1] = y1;
-        const unsigned long long ka = (y0 == y0) ? argmax_key(y0, (uint32_t)r0) : 0ull;
-        const unsigned long long kb = (y1 == y1) ? argmax_key(y1, (uint32_t)r1) : 0ull;
+        const unsigned long long ka = (y0 == y0) ? argmax_key(y0, (uint32_t)(r0 + g.idx_off)) : 0ull;
+        const unsigned long long kb = (y1 == y1) ? argmax_key(y1, (uint32_t)(r1 + g.idx_off)) : 0ull;
         const unsigned long long kk = ka > kb ? ka : kb;
         best = kk > best ? kk : best;
         break;
@@ -687,6 +711,128 @@ __device__ bool grid_sync(const DecodeArgs &A, unsigned target, volatile int *ab
     }
     dsync();
     return *ok_s != 0;
+}
+
+// ── tensor-parallel exchanges over the peers' exchange areas ──
+// A flag store is a release at system scope after a system-scope fence, so a
+// peer that acquires the flag sees this rank's partial vector (or key). Every
+// wait is bounded like the grid barrier's; a timeout raises ERR_TIMEOUT here
+// and stops the kernel, so a lost peer never hangs this GPU.
+__device__ __forceinline__ unsigned *xch_flags(unsigned char *area, int xdim) {
+    return (unsigned *)(area + xch_flags_off(xdim));
+}
+__device__ __forceinline__ void flag_store(unsigned *f, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned flag_load(const unsigned *f) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    return v;
+}
+__device__ __forceinline__ float4 ld_sys4(const float4 *p) {
+    float4 v;
+    asm volatile("ld.relaxed.sys.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
+// Every other rank's flag in this rank's area reaches `ep` (thread 0). The
+// ranks are separate processes whose launches can drift apart by host-side
+// delays (a graph capture), so this wait is bounded by time, 10 s on the
+// global timer (and, as a backstop, by a count of polls), not by the grid
+// barrier's poll count.
+constexpr unsigned long long kXchWaitNs = 10ull * 1000 * 1000 * 1000;
+constexpr uint32_t kXchSpins = 1u << 26;
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ bool wait_peers(const DecodeArgs &A, unsigned ep) {
+    const unsigned *mine = xch_flags(A.xch[A.tp_rank], A.xdim);
+    const unsigned long long t0 = global_ns();
+    for (int p = 0; p < A.tp; p++) {
+        if (p == A.tp_rank) continue;
+        for (uint32_t i = 0;; i++) {
+            if ((int)(flag_load(mine + p) - ep) >= 0) break;
+            if ((i & 255) == 255) {
+                if (*(volatile int *)A.err & ERR_TIMEOUT) return false;
+                if (global_ns() - t0 > kXchWaitNs || i >= kXchSpins) {
+                    atomicOr(A.err, ERR_TIMEOUT);
+                    return false;
+                }
+                __nanosleep(128);
+            }
+        }
+    }
+    return true;
+}
+
+// this rank's flag `ep` into every peer's area (after its data)
+__device__ void signal_peers(const DecodeArgs &A, unsigned ep) {
+    __threadfence_system();
+    for (int p = 0; p < A.tp; p++)
+        if (p != A.tp_rank) flag_store(xch_flags(A.xch[p], A.xdim) + A.tp_rank, ep);
+}
+
+// dst[i] = dst[i] + (((partial_0[i] + partial_1[i]) + ...) + partial_{tp-1}[i]):
+// the ranks' partial sums of o_proj / ffn_down (each over its K slice),
+// added in rank order, then the residual add of src/forward.rs:467-469 /
+// :489-491. CTA 0 publishes this rank's partial (complete: a grid barrier
+// precedes this phase); every CTA waits for the peers', then adds its slice.
+__device__ void phase_xreduce(const DecodeArgs &A, const XPhase &X, unsigned ep, volatile int *abort_flag,
+                              int *ok_s) {
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0) signal_peers(A, ep);
+        const bool ok = wait_peers(A, ep);
+        if (!ok) *abort_flag = 1;
+        *ok_s = ok;
+    }
+    dsync();
+    if (!*ok_s) return;
+    const int n4 = X.n / 4, per = (n4 + gridDim.x - 1) / gridDim.x;
+    const int i0 = blockIdx.x * per, i1 = min(n4, i0 + per);
+    const size_t off = (size_t)X.parity * A.xdim * sizeof(float);
+    for (int i = i0 + threadIdx.x; i < i1; i += kDW * 32) {
+        float4 s = ld_sys4((const float4 *)(A.xch[0] + off) + i);
+        for (int p = 1; p < A.tp; p++) {
+            const float4 v = ld_sys4((const float4 *)(A.xch[p] + off) + i);
+            s = make_float4(fa(s.x, v.x), fa(s.y, v.y), fa(s.z, v.z), fa(s.w, v.w));
+        }
+        float4 *d = (float4 *)X.dst + i;
+        const float4 x = __ldcg(d);
+        *d = make_float4(fa(x.x, s.x), fa(x.y, s.y), fa(x.z, s.z), fa(x.w, s.w));
+    }
+}
+
+// the greedy pick over the ranks' vocabulary slices: CTA 0 publishes this
+// rank's argmax key (its slice's first maximum), takes every peer's, and
+// leaves the largest (the first maximum of the whole vocabulary) in
+// *argmax_key for the commit
+__device__ void phase_xargmax(const DecodeArgs &A, unsigned ep, volatile int *abort_flag) {
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
+    const unsigned long long mine = __ldcg(A.argmax_key);
+    for (int p = 0; p < A.tp; p++)
+        if (p != A.tp_rank) {
+            unsigned long long *k = (unsigned long long *)(A.xch[p] + xch_keys_off(A.xdim)) + A.tp_rank;
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(k), "l"(mine) : "memory");
+        }
+    signal_peers(A, ep);
+    if (!wait_peers(A, ep)) {
+        *abort_flag = 1;
+        return;
+    }
+    unsigned long long best = mine;
+    const unsigned long long *keys = (const unsigned long long *)(A.xch[A.tp_rank] + xch_keys_off(A.xdim));
+    for (int p = 0; p < A.tp; p++) {
+        if (p == A.tp_rank) continue;
+        unsigned long long v;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(keys + p) : "memory");
+        best = v > best ? v : best;
+    }
+    *A.argmax_key = best;
 }
 
 // ── attention phases (src/ops.rs:1258-1325), reference order ──
@@ -933,6 +1079,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
     __shared__ float fred[kDW];
     __shared__ float fbc;
     __shared__ int pos_s, tok_s, bad_s;
+    __shared__ unsigned xbase_s;  // exchanges completed before this launch
     // deferred epilogues: (segment, unit, y0, y1) per output unit, per warp
     __shared__ int2 epi_su[kDW][32];
     __shared__ float2 epi_y[kDW][32];
@@ -958,6 +1105,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         pos_s = p;
         tok_s = (int)t;
         bad_s = bad;
+        // read before the first grid barrier, so before CTA 0's commit updates it
+        xbase_s = A.epoch ? *(volatile unsigned *)A.epoch : 0u;
     }
     if (tid < kDescWords) ((uint4 *)&phbuf[0])[tid] = __ldg((const uint4 *)&A.prog[0] + tid);
     for (int i = tid; i < A.nfeed * 4; i += kDecodeThreads) ((uint4 *)ftab)[i] = __ldg((const uint4 *)A.feed + i);
@@ -1115,11 +1264,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
             phase_scores(ph.at, n, (float *)region);
         } else if (ph.kind == PH_ATTN) {
             phase_attn(ph.at, n, A.max_pos, (float *)region, fred, &fbc);
+        } else if (ph.kind == PH_XREDUCE) {
+            phase_xreduce(A, ph.xp, xbase_s + (unsigned)ph.xp.seq, &abort_flag, &sync_ok);
+        } else if (ph.kind == PH_XARGMAX) {
+            phase_xargmax(A, xbase_s + (unsigned)ph.xp.seq, &abort_flag);
         } else if (ph.kind == PH_COMMIT) {
-            if (blockIdx.x == 0 && tid == 0 && A.d_len) {
-                if (A.write_token && A.argmax_key && pos + 1 < A.max_pos + 1)
-                    A.toks[pos + 1] = argmax_index(__ldcg(A.argmax_key));
-                if (A.commit) *(volatile int *)A.d_len = pos + 1;
+            if (blockIdx.x == 0 && tid == 0) {
+                if (A.d_len) {
+                    if (A.write_token && A.argmax_key && pos + 1 < A.max_pos + 1)
+                        A.toks[pos + 1] = argmax_index(__ldcg(A.argmax_key));
+                    if (A.commit) *(volatile int *)A.d_len = pos + 1;
+                }
+                if (A.epoch) *A.epoch = xbase_s + (unsigned)A.nx;
             }
         }
         stop = dsync_or(abort_flag != 0);  // every reader of this phase's descriptor is done

@@ -61,12 +61,24 @@ struct cxm_model {
     float *samp_probs = nullptr, *samp_prefix = nullptr;
     uint32_t *samp_k0 = nullptr, *samp_v0 = nullptr, *samp_k1 = nullptr, *samp_v1 = nullptr;
     int sms = 148;
+    // tensor parallelism: this rank's heads, KV heads, FFN rows and
+    // vocabulary rows (all of them at tp = 1); the exchange areas (own, and
+    // the peers' mapped through CUDA IPC by cxm_tp_connect)
+    int tp = 1, tp_rank = 0;
+    int h_loc = 0, kv_loc = 0, f_loc = 0, v_loc = 0, v_off = 0;
+    unsigned char *xch = nullptr;
+    unsigned char *peer[kTpMax] = {};
+    bool peer_mapped[kTpMax] = {};
+    bool connected = true;  // false from open until cxm_tp_connect when tp > 1
+    unsigned *epoch = nullptr;
     uint32_t slot_bytes = 0;  // largest quad tile of the model
     uint64_t weight_bytes = 0;
     bool logits_valid = false;
 
     ~cxm_model() {
         if (device >= 0) cudaSetDevice(device);
+        for (int p = 0; p < kTpMax; p++)
+            if (peer_mapped[p]) cudaIpcCloseMemHandle(peer[p]);
         for (void *p : allocs) cudaFree(p);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -88,6 +100,7 @@ struct cxm_model {
 struct Program {
     Phase *d = nullptr;  // the phases, then the walk table (one allocation)
     int n = 0;
+    int nx = 0;          // tensor-parallel exchanges
     const FeedPhase *feed = nullptr;
     int nfeed = 0;
     size_t region = 0;
@@ -123,7 +136,7 @@ namespace {
 // STEP_SAMPLE: the STEP_LOGITS step, then the sampler writes the next token
 enum StepMode { STEP_PREFILL = 0, STEP_GREEDY = 1, STEP_LOGITS = 2, STEP_SAMPLE = 3 };
 
-size_t kv_dim(const cxm_model *m) { return (size_t)m->cfg.n_head_kv * m->cfg.head_dim; }
+size_t kv_dim(const cxm_model *m) { return (size_t)m->kv_loc * m->cfg.head_dim; }  // this rank's KV heads
 
 int sub_of(int type) { return (type == Q4K || type == Q5K) ? 32 : 16; }
 
@@ -133,6 +146,7 @@ int sub_of(int type) { return (type == Q4K || type == Q5K) ? 32 : 16; }
 struct RowSrc {
     const uint8_t *m;
     int row;
+    int src_nblk = 0, blk0 = 0;  // a K slice: the source row's blocks, the slice's first (0: the whole row)
 };
 
 QMat tiled_desc(int type, int K, int nrows, int lpr) {
@@ -187,8 +201,9 @@ void build_tiles(const QMat &M, const std::vector<RowSrc> &rows, std::vector<uin
                     for (int sl = 0; sl < M.rpt; sl++) {
                         const size_t ri = (size_t)M.rpt * q + sl;
                         if (ri >= rows.size() || !rows[ri].m) continue;
-                        const uint8_t *blk =
-                            rows[ri].m + ((size_t)rows[ri].row * M.nblk + (size_t)M.lpr * t + bl) * M.bpb;
+                        const size_t sn = rows[ri].src_nblk ? (size_t)rows[ri].src_nblk : (size_t)M.nblk;
+                        const uint8_t *blk = rows[ri].m + ((size_t)rows[ri].row * sn + (size_t)rows[ri].blk0 +
+                                                           (size_t)M.lpr * t + bl) * M.bpb;
                         const int lane = M.rpt * bl + sl;
                         for (int c = 0; c < ach; c++) memcpy(tile + ((size_t)c * L + lane) * 16, blk + lo_a + 16 * c, 16);
                         if (ps) memcpy(tile + (size_t)ach * L * 16 + (size_t)lane * ps, blk + lo_s, ps);
@@ -209,25 +224,26 @@ void build_tiles(const QMat &M, const std::vector<RowSrc> &rows, std::vector<uin
 
 // row orders: PAIR_ADJ (rows in order), PAIR_ROPE (rows i and i + half of a
 // head side by side), PAIR_TWO (row u of A, then row u of B)
-std::vector<RowSrc> rows_adj(const uint8_t *a, int n) {
+// (rows from `row0` on: a tensor-parallel rank's share)
+std::vector<RowSrc> rows_adj(const uint8_t *a, int n, int row0 = 0) {
     std::vector<RowSrc> r(n);
-    for (int i = 0; i < n; i++) r[i] = {a, i};
+    for (int i = 0; i < n; i++) r[i] = {a, row0 + i};
     return r;
 }
-std::vector<RowSrc> rows_rope(const uint8_t *a, int n, int half) {
+std::vector<RowSrc> rows_rope(const uint8_t *a, int n, int half, int row0 = 0) {
     std::vector<RowSrc> r(n);
     for (int u = 0; u < n / 2; u++) {
         const int h = u / half, i = u % half, r0 = h * 2 * half + i;
-        r[2 * u] = {a, r0};
-        r[2 * u + 1] = {a, r0 + half};
+        r[2 * u] = {a, row0 + r0};
+        r[2 * u + 1] = {a, row0 + r0 + half};
     }
     return r;
 }
-std::vector<RowSrc> rows_two(const uint8_t *a, const uint8_t *b, int n) {
+std::vector<RowSrc> rows_two(const uint8_t *a, const uint8_t *b, int n, int row0 = 0) {
     std::vector<RowSrc> r(2 * (size_t)n);
     for (int u = 0; u < n; u++) {
-        r[2 * u] = {a, u};
-        r[2 * u + 1] = {b, u};
+        r[2 * u] = {a, row0 + u};
+        r[2 * u + 1] = {b, row0 + u};
     }
     return r;
 }
@@ -266,42 +282,71 @@ int upload_tiles(cxm_model *m, QMat &M, const std::vector<RowSrc> &rows) {
 }
 
 // one GGUF matrix, rows in order (pairing ADJ) or RoPE order, in tiles of
-// `lpr` lanes per row
-int upload_matrix(cxm_model *m, const Gguf &g, const TensorInfo &t, int pairing, int half, int lpr, QMat *out) {
+// `lpr` lanes per row; or its part rows [row0, row0 + nrows) x super-blocks
+// [blk0, blk0 + nblk) (a tensor-parallel rank's share; nrows 0: all rows,
+// nblk 0: all blocks)
+int upload_matrix(cxm_model *m, const Gguf &g, const TensorInfo &t, int pairing, int half, int lpr, QMat *out,
+                  int row0 = 0, int nrows = 0, int blk0 = 0, int nblk = 0) {
     if (check_matrix(t)) return -1;
-    const int K = (int)t.dims[0], rows = (int)t.dims[1];
-    if (rows % 2 || (pairing == PAIR_ROPE && (half % 2 || rows % (2 * half)))) {
-        set_error("%s: %d rows do not pair", t.name.c_str(), rows);
+    const int all_blk = (int)(t.dims[0] / 256), all_rows = (int)t.dims[1];
+    if (!nrows) nrows = all_rows;
+    if (!nblk) nblk = all_blk;
+    if (row0 < 0 || row0 + nrows > all_rows || blk0 < 0 || blk0 + nblk > all_blk) {
+        set_error("%s: part rows %d+%d, blocks %d+%d outside %dx%d", t.name.c_str(), row0, nrows, blk0, nblk,
+                  all_rows, all_blk);
         return -1;
     }
-    QMat M = tiled_desc(t.type, K, rows, lpr);
-    const auto order = pairing == PAIR_ROPE ? rows_rope(g.data(t), rows, half) : rows_adj(g.data(t), rows);
+    if (nrows % 2 || (pairing == PAIR_ROPE && (half % 2 || nrows % (2 * half)))) {
+        set_error("%s: %d rows do not pair", t.name.c_str(), nrows);
+        return -1;
+    }
+    QMat M = tiled_desc(t.type, nblk * 256, nrows, lpr);
+    auto order = pairing == PAIR_ROPE ? rows_rope(g.data(t), nrows, half, row0) : rows_adj(g.data(t), nrows, row0);
+    if (nblk != all_blk)
+        for (RowSrc &r : order) {
+            r.src_nblk = all_blk;
+            r.blk0 = blk0;
+        }
     if (upload_tiles(m, M, order)) return -1;
-    M.rows = rows;
+    M.rows = nrows;
     *out = M;
-    m->weight_bytes += (uint64_t)t.nbytes;
+    m->weight_bytes += (uint64_t)nrows * nblk * M.bpb;
     return 0;
 }
 
-// gate and up as one matrix of PAIR_TWO quads
-int upload_pair(cxm_model *m, const Gguf &g, const TensorInfo &a, const TensorInfo &b, int lpr, QMat *out) {
+// gate and up as one matrix of PAIR_TWO quads (rows [row0, row0 + n) of
+// each; n 0: all)
+int upload_pair(cxm_model *m, const Gguf &g, const TensorInfo &a, const TensorInfo &b, int lpr, QMat *out,
+                int row0 = 0, int n = 0) {
     if (check_matrix(a) || check_matrix(b)) return -1;
     if (a.type != b.type || a.dims[0] != b.dims[0] || a.dims[1] != b.dims[1] || a.dims[1] % 2) {
         set_error("%s and %s must have the same type and shape", a.name.c_str(), b.name.c_str());
         return -1;
     }
-    const int K = (int)a.dims[0], n = (int)a.dims[1];
+    const int K = (int)a.dims[0];
+    if (!n) n = (int)a.dims[1];
+    if (row0 < 0 || row0 + n > (int)a.dims[1]) {
+        set_error("%s: part rows %d+%d outside %d", a.name.c_str(), row0, n, (int)a.dims[1]);
+        return -1;
+    }
     QMat M = tiled_desc(a.type, K, 2 * n, lpr);
-    if (upload_tiles(m, M, rows_two(g.data(a), g.data(b), n))) return -1;
+    if (upload_tiles(m, M, rows_two(g.data(a), g.data(b), n, row0))) return -1;
     M.rows = 2 * n;
     *out = M;
-    m->weight_bytes += (uint64_t)a.nbytes + (uint64_t)b.nbytes;
+    m->weight_bytes += (uint64_t)2 * n * M.nblk * M.bpb;
     return 0;
 }
 
-int upload_vector(cxm_model *m, const Gguf &g, const TensorInfo &t, size_t n, float **out) {
+// a vector of n values (or its part [off, off + len); len 0: all)
+int upload_vector(cxm_model *m, const Gguf &g, const TensorInfo &t, size_t n, float **out, size_t off = 0,
+                  size_t len = 0) {
     if (t.elements() != n) {
         set_error("%s: %llu values, expected %zu", t.name.c_str(), (unsigned long long)t.elements(), n);
+        return -1;
+    }
+    if (!len) len = n;
+    if (off + len > n) {
+        set_error("%s: part %zu+%zu outside %zu", t.name.c_str(), off, len, n);
         return -1;
     }
     std::vector<float> h(n);
@@ -314,9 +359,9 @@ int upload_vector(cxm_model *m, const Gguf &g, const TensorInfo &t, size_t n, fl
         set_error("%s: vectors must be F32 or F16", t.name.c_str());
         return -1;
     }
-    if (m->alloc(out, n)) return -1;
-    CU(cudaMemcpy(*out, h.data(), n * 4, cudaMemcpyHostToDevice));
-    m->weight_bytes += (uint64_t)t.nbytes;
+    if (m->alloc(out, len)) return -1;
+    CU(cudaMemcpy(*out, h.data() + off, len * 4, cudaMemcpyHostToDevice));
+    m->weight_bytes += (uint64_t)t.nbytes * len / n;
     return 0;
 }
 
@@ -415,16 +460,36 @@ int score_positions(int G) { return std::max(1, std::min(64, 256 / std::max(1, G
 // embedding (fused into layer 0's first prologue), then per layer q|k|v,
 // scores, softmax+output, o, gate|up, down; the output projection unless the
 // step only prefills; the commit.
+// an exchange phase of a tensor-parallel program
+Phase x_phase(int kind, float *dst, int n, int parity, int seq) {
+    Phase ph{};
+    ph.kind = kind;
+    ph.barrier = 1;
+    ph.xp.dst = dst;
+    ph.xp.n = n;
+    ph.xp.parity = parity;
+    ph.xp.seq = seq;
+    return ph;
+}
+
+// One token through the model (src/forward.rs:375-505) as decode-kernel
+// phases. With tensor parallelism the sizes are this rank's (heads, KV heads,
+// FFN rows, vocabulary rows), o_proj and ffn_down leave partial sums in the
+// exchange area, and exchange phases add the ranks' partials to the residual
+// and pick the argmax over the ranks' vocabulary slices.
 std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode) {
     const cxm_config &cfg = m->cfg;
-    const int D = cfg.dim, hd = cfg.head_dim, F = cfg.ffn, H = cfg.n_head, KV = cfg.n_head_kv;
+    const int D = cfg.dim, hd = cfg.head_dim, F = m->f_loc, H = m->h_loc, KV = m->kv_loc, dl = H * hd;
     const size_t kvd = kv_dim(m);
+    const bool tp = m->tp > 1;
+    float *partial = (float *)m->xch;  // [2][D]: o_proj's, ffn_down's
+    int nx = 0;
     std::vector<Phase> prog;
     for (int l = 0; l < cfg.n_layer; l++) {
         const Layer &L = m->layers[l];
         float *kl = c->k + (size_t)l * c->max_tokens * kvd, *vl = c->v + (size_t)l * c->max_tokens * kvd;
         {  // RMSNorm + quantize, q/k/v with bias, RoPE, KV append
-            MvSeg sq = mv_seg(L.q, D / 2, PAIR_ROPE, EPI_ROPE, m->q);
+            MvSeg sq = mv_seg(L.q, dl / 2, PAIR_ROPE, EPI_ROPE, m->q);
             sq.half = hd / 2;
             sq.bias = L.bq;
             MvSeg sk = mv_seg(L.k, (int)kvd / 2, PAIR_ROPE, EPI_ROPE, kl);
@@ -466,13 +531,26 @@ std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode) {
             prog.push_back(ph);
         }
         // o_proj + residual; RMSNorm + gate/up + SwiGLU; down + residual
-        prog.push_back(mv_phase({mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->x)}, D, PRO_QUANT, m->att, nullptr, 0.0f, 1));
+        if (!tp) {
+            prog.push_back(mv_phase({mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->x)}, dl, PRO_QUANT, m->att, nullptr, 0.0f, 1));
+        } else {
+            prog.push_back(mv_phase({mv_seg(L.o, D / 2, PAIR_ADJ, EPI_STORE, partial)}, dl, PRO_QUANT, m->att, nullptr, 0.0f, 1));
+            prog.push_back(x_phase(PH_XREDUCE, m->x, D, 0, ++nx));
+        }
         prog.push_back(mv_phase({mv_seg(L.gu, F, PAIR_TWO, EPI_SWIGLU, m->h)}, D, PRO_NORM, m->x, L.ffn_norm, cfg.eps, 1));
-        prog.push_back(mv_phase({mv_seg(L.down, D / 2, PAIR_ADJ, EPI_RESID, m->x)}, F, PRO_QUANT, m->h, nullptr, 0.0f, 1));
+        if (!tp) {
+            prog.push_back(mv_phase({mv_seg(L.down, D / 2, PAIR_ADJ, EPI_RESID, m->x)}, F, PRO_QUANT, m->h, nullptr, 0.0f, 1));
+        } else {
+            prog.push_back(mv_phase({mv_seg(L.down, D / 2, PAIR_ADJ, EPI_STORE, partial + D)}, F, PRO_QUANT, m->h, nullptr, 0.0f, 1));
+            prog.push_back(x_phase(PH_XREDUCE, m->x, D, 1, ++nx));
+        }
     }
-    if (mode != STEP_PREFILL)  // final RMSNorm, output projection, argmax
-        prog.push_back(mv_phase({mv_seg(m->out, cfg.vocab / 2, PAIR_ADJ, EPI_LOGITS, m->logits)}, D, PRO_NORM, m->x,
-                                m->out_norm, cfg.eps, 1));
+    if (mode != STEP_PREFILL) {  // final RMSNorm, output projection, argmax
+        MvSeg so = mv_seg(m->out, m->v_loc / 2, PAIR_ADJ, EPI_LOGITS, m->logits);
+        so.idx_off = m->v_off;
+        prog.push_back(mv_phase({so}, D, PRO_NORM, m->x, m->out_norm, cfg.eps, 1));
+        if (tp) prog.push_back(x_phase(PH_XARGMAX, nullptr, 0, 0, ++nx));
+    }
     Phase cm{};
     cm.kind = PH_COMMIT;
     cm.barrier = 1;
@@ -511,6 +589,7 @@ int upload_program(const std::vector<Phase> &ph, int max_pos, Program *out) {
     p.region = (p.region + 127) & ~(size_t)127;
     const std::vector<FeedPhase> ft = feed_table(ph);
     p.nfeed = (int)ft.size();
+    for (const Phase &x : ph) p.nx += x.kind == PH_XREDUCE || x.kind == PH_XARGMAX;
     const size_t pb = ph.size() * sizeof(Phase), fb = ft.size() * sizeof(FeedPhase);
     CU(cudaMalloc(&p.d, pb + fb));
     CU(cudaMemcpy(p.d, ph.data(), pb, cudaMemcpyHostToDevice));
@@ -540,6 +619,7 @@ int decode_geometry(uint32_t slot_bytes, const Program &p, DecodeArgs &a, size_t
     a.nphase = p.n;
     a.feed = p.feed;
     a.nfeed = p.nfeed;
+    a.nx = p.nx;
     *smem = (size_t)kDW * ns * slot + fixed;
     return 0;
 }
@@ -564,6 +644,11 @@ int launch_decode(int sms, cudaStream_t st, const DecodeArgs &a, size_t smem) {
 
 DecodeArgs base_args(cxm_model *m) {
     DecodeArgs a{};
+    a.tp = m->tp;
+    a.tp_rank = m->tp_rank;
+    a.xdim = m->cfg.dim;
+    for (int p = 0; p < m->tp; p++) a.xch[p] = m->peer[p];
+    a.epoch = m->epoch;
     a.bar = m->bar;
     a.err = m->err;
     a.vocab = m->cfg.vocab;
@@ -576,6 +661,14 @@ DecodeArgs base_args(cxm_model *m) {
 int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out);
 
 int enqueue_step(cxm_model *m, cxm_cache *c, int mode) {
+    if (!m->connected) {
+        set_error("tensor-parallel rank %d of %d: cxm_tp_connect first", m->tp_rank, m->tp);
+        return -1;
+    }
+    if (m->tp > 1 && mode == STEP_SAMPLE) {
+        set_error("sampling needs the whole vocabulary on one rank: tensor-parallel models decode greedily");
+        return -1;
+    }
     if (mode == STEP_SAMPLE)
         return enqueue_step(m, c, STEP_LOGITS) || launch_sample(m, c->d_len, c->toks, nullptr) ? -1 : 0;
     Program &p = c->prog[mode];
@@ -680,11 +773,19 @@ int check_err(cxm_model *m) {
 extern "C" const char *cxm_last_error(void) { return last_error(); }
 
 extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
+    return cxm_model_open_tp(path, device, 0, 1, out);
+}
+
+extern "C" int cxm_model_open_tp(const char *path, int device, int tp_rank, int tp_size, cxm_model **out) {
     if (!path || !out) {
         set_error("null argument");
         return -1;
     }
     *out = nullptr;
+    if (tp_size < 1 || tp_size > kTpMax || tp_rank < 0 || tp_rank >= tp_size) {
+        set_error("tensor-parallel rank %d of %d (1..%d ranks)", tp_rank, tp_size, kTpMax);
+        return -1;
+    }
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
         set_error("no CUDA device: this library has no CPU path");
@@ -706,6 +807,9 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
     std::unique_ptr<cxm_model> m(new cxm_model);
     m->device = device;
     m->sms = prop.multiProcessorCount;
+    m->tp = tp_size;
+    m->tp_rank = tp_rank;
+    m->connected = tp_size == 1;
     cxm_config &cfg = m->cfg;
     uint64_t v;
     const char *ik[] = {"qwen2.block_count", "qwen2.embedding_length", "qwen2.attention.head_count",
@@ -730,6 +834,17 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
         return -1;
     }
     cfg.head_dim = cfg.dim / cfg.n_head;
+    // this rank's share (src/forward.rs has one rank): whole heads, whole
+    // KV heads, FFN rows and o/down K slices of whole super-blocks
+    const int tp = tp_size, r = tp_rank;
+    if (cfg.n_head % tp || cfg.n_head_kv % tp || (tp > 1 && (cfg.n_head / tp * cfg.head_dim) % 256)) {
+        set_error("%d heads / %d KV heads of %d do not split over %d ranks in whole super-blocks", cfg.n_head,
+                  cfg.n_head_kv, cfg.head_dim, tp);
+        return -1;
+    }
+    m->h_loc = cfg.n_head / tp;
+    m->kv_loc = cfg.n_head_kv / tp;
+    const int dl = m->h_loc * cfg.head_dim;  // this rank's attention output: o's K slice
     const TensorInfo *embd = g.tensor("token_embd.weight");
     const TensorInfo *outw = g.tensor("output.weight");
     const TensorInfo *onorm = g.tensor("output_norm.weight");
@@ -739,6 +854,10 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
     }
     cfg.vocab = (int32_t)embd->dims[1];
     cfg.tied = outw == nullptr;
+    // output rows: an even share per rank, the last takes the rest
+    m->v_loc = tp == 1 ? cfg.vocab : (cfg.vocab / tp) & ~1;
+    m->v_off = r * m->v_loc;
+    if (r == tp - 1) m->v_loc = cfg.vocab - m->v_off;
     CU(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     if (embd->type == F32) {
         if (upload_vector(m.get(), g, *embd, (size_t)cfg.vocab * cfg.dim, &m->embd_f32)) return -1;
@@ -749,15 +868,23 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
     }
     if (outw) {
         if (check_matrix(*outw) ||
-            upload_matrix(m.get(), g, *outw, PAIR_ADJ, 0, choose_lpr(cfg.vocab, (int)(outw->dims[0] / 256), m->sms),
-                          &m->out))
+            upload_matrix(m.get(), g, *outw, PAIR_ADJ, 0, choose_lpr(m->v_loc, (int)(outw->dims[0] / 256), m->sms),
+                          &m->out, m->v_off, m->v_loc))
             return -1;
     } else {
         if (embd->type == F32) {
             set_error("a tied F32 embedding table has no device output kernel");
             return -1;
         }
-        m->out = m->embd;
+        if (tp == 1) {
+            m->out = m->embd;
+        } else {  // this rank's rows of the tied table, as its own output matrix
+            const uint64_t wb = m->weight_bytes;
+            if (upload_matrix(m.get(), g, *embd, PAIR_ADJ, 0, choose_lpr(m->v_loc, (int)(embd->dims[0] / 256), m->sms),
+                              &m->out, m->v_off, m->v_loc))
+                return -1;
+            m->weight_bytes = wb;  // the bytes of the table are counted once
+        }
     }
     if (upload_vector(m.get(), g, *onorm, (size_t)cfg.dim, &m->out_norm)) return -1;
     const size_t hd = (size_t)cfg.head_dim, kvd = (size_t)cfg.n_head_kv * hd;
@@ -771,32 +898,46 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
         };
         const TensorInfo *t, *t2;
         const int half = (int)hd / 2, nbd = cfg.dim / 256;
-        // tile shapes by phase: q|k|v share one; o, gate|up and down their own
-        const int lpr_qkv = choose_lpr(cfg.dim + 2 * (int)kvd, nbd, m->sms), lpr_o = choose_lpr(cfg.dim, nbd, m->sms);
         const TensorInfo *tg = T("ffn_gate.weight"), *td = T("ffn_down.weight");
         if (!tg || !td || check_matrix(*tg) || check_matrix(*td)) return -1;
-        const int lpr_gu = choose_lpr(2 * (int)tg->dims[1], nbd, m->sms);
-        const int lpr_down = choose_lpr(cfg.dim, (int)(td->dims[0] / 256), m->sms);
+        const int F = (int)tg->dims[1];
+        if (F % (256 * tp)) {
+            set_error("FFN of %d rows does not split over %d ranks in whole super-blocks", F, tp);
+            return -1;
+        }
+        const int fl = F / tp, ql = dl, kl = m->kv_loc * (int)hd;  // this rank's rows
+        // tile shapes by phase: q|k|v share one; o, gate|up and down their own
+        const int lpr_qkv = choose_lpr(ql + 2 * kl, nbd, m->sms), lpr_o = choose_lpr(cfg.dim, dl / 256, m->sms);
+        const int lpr_gu = choose_lpr(2 * fl, nbd, m->sms);
+        const int lpr_down = choose_lpr(cfg.dim, fl / 256, m->sms);
         if (!(t = T("attn_norm.weight")) || upload_vector(m.get(), g, *t, cfg.dim, &L.attn_norm)) return -1;
-        if (!(t = T("attn_q.weight")) || upload_matrix(m.get(), g, *t, PAIR_ROPE, half, lpr_qkv, &L.q)) return -1;
-        if (!(t = T("attn_q.bias")) || upload_vector(m.get(), g, *t, cfg.dim, &L.bq)) return -1;
-        if (!(t = T("attn_k.weight")) || upload_matrix(m.get(), g, *t, PAIR_ROPE, half, lpr_qkv, &L.k)) return -1;
-        if (!(t = T("attn_k.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bk)) return -1;
-        if (!(t = T("attn_v.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, lpr_qkv, &L.v)) return -1;
-        if (!(t = T("attn_v.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bv)) return -1;
-        if (!(t = T("attn_output.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, lpr_o, &L.o)) return -1;
+        if (!(t = T("attn_q.weight")) ||
+            upload_matrix(m.get(), g, *t, PAIR_ROPE, half, lpr_qkv, &L.q, r * ql, ql))
+            return -1;
+        if (!(t = T("attn_q.bias")) || upload_vector(m.get(), g, *t, cfg.dim, &L.bq, (size_t)r * ql, ql)) return -1;
+        if (!(t = T("attn_k.weight")) ||
+            upload_matrix(m.get(), g, *t, PAIR_ROPE, half, lpr_qkv, &L.k, r * kl, kl))
+            return -1;
+        if (!(t = T("attn_k.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bk, (size_t)r * kl, kl)) return -1;
+        if (!(t = T("attn_v.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, lpr_qkv, &L.v, r * kl, kl))
+            return -1;
+        if (!(t = T("attn_v.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bv, (size_t)r * kl, kl)) return -1;
+        if (!(t = T("attn_output.weight")) ||
+            upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, lpr_o, &L.o, 0, 0, r * (dl / 256), dl / 256))
+            return -1;
         if (!(t = T("ffn_norm.weight")) || upload_vector(m.get(), g, *t, cfg.dim, &L.ffn_norm)) return -1;
-        if (!(t2 = T("ffn_up.weight")) || upload_pair(m.get(), g, *tg, *t2, lpr_gu, &L.gu)) return -1;
-        if (upload_matrix(m.get(), g, *td, PAIR_ADJ, 0, lpr_down, &L.down)) return -1;
-        if (L.q.rows != cfg.dim || L.k.rows != (int)kvd || L.v.rows != (int)kvd || L.o.rows != cfg.dim ||
-            L.q.K != cfg.dim || L.k.K != cfg.dim || L.v.K != cfg.dim || L.o.K != cfg.dim || L.gu.K != cfg.dim ||
-            L.down.K != L.gu.rows / 2 || L.down.rows != cfg.dim) {
+        if (!(t2 = T("ffn_up.weight")) || upload_pair(m.get(), g, *tg, *t2, lpr_gu, &L.gu, r * fl, fl)) return -1;
+        if (upload_matrix(m.get(), g, *td, PAIR_ADJ, 0, lpr_down, &L.down, 0, 0, r * (fl / 256), fl / 256)) return -1;
+        if (L.q.rows != ql || L.k.rows != kl || L.v.rows != kl || L.o.rows != cfg.dim || L.q.K != cfg.dim ||
+            L.k.K != cfg.dim || L.v.K != cfg.dim || L.o.K != dl || L.gu.K != cfg.dim || L.gu.rows != 2 * fl ||
+            L.down.K != fl || L.down.rows != cfg.dim || (int)td->dims[0] != F) {
             set_error("layer %d: matrix shapes do not match the config", i);
             return -1;
         }
         m->layers.push_back(L);
+        cfg.ffn = F;
+        m->f_loc = fl;
     }
-    cfg.ffn = m->layers.empty() ? 0 : m->layers[0].gu.rows / 2;
     if (cfg.dim > kMaxNormed) {
         set_error("hidden size %d: the decode kernel's RMSNorm prologue takes at most %d", cfg.dim, kMaxNormed);
         return -1;
@@ -828,6 +969,11 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
         m->alloc(&m->scores, (size_t)cfg.n_head * ((cfg.ctx + 3) & ~3)))
         return -1;
     CU(cudaMemset(m->err, 0, sizeof(int)));
+    // the tensor-parallel exchange area and the exchange count
+    if (m->alloc(&m->xch, xch_bytes(cfg.dim)) || m->alloc(&m->epoch, 1)) return -1;
+    CU(cudaMemset(m->xch, 0, xch_bytes(cfg.dim)));
+    CU(cudaMemset(m->epoch, 0, sizeof(unsigned)));
+    m->peer[tp_rank] = m->xch;
     if (set_kernel_smem_limits()) return -1;
     if (out_smem((uint32_t)cfg.ctx) > 200 * 1024 || cfg.head_dim % 16 || cfg.head_dim > kKRow - 4 ||
         cfg.vocab % 2 || cfg.dim % 4) {
@@ -843,6 +989,58 @@ extern "C" int cxm_model_open(const char *path, int device, cxm_model **out) {
     }
     CU(cudaDeviceSynchronize());
     *out = m.release();
+    return 0;
+}
+
+extern "C" int cxm_tp_handle(cxm_model *m, uint8_t *handle_out) {
+    if (!m || !handle_out) {
+        set_error("null argument");
+        return -1;
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == CXM_TP_HANDLE_BYTES, "IPC handle size");
+    CU(cudaSetDevice(m->device));
+    cudaIpcMemHandle_t h;
+    CU(cudaIpcGetMemHandle(&h, m->xch));
+    memcpy(handle_out, &h, sizeof(h));
+    return 0;
+}
+
+extern "C" int cxm_tp_connect(cxm_model *m, const uint8_t *handles) {
+    if (!m || !handles) {
+        set_error("null argument");
+        return -1;
+    }
+    if (m->connected) {
+        set_error("already connected");
+        return -1;
+    }
+    CU(cudaSetDevice(m->device));
+    for (int p = 0; p < m->tp; p++) {
+        if (p == m->tp_rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles + (size_t)p * CXM_TP_HANDLE_BYTES, sizeof(h));
+        void *ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            set_error("rank %d: mapping rank %d's exchange area failed: %s", m->tp_rank, p, cudaGetErrorString(e));
+            return -1;
+        }
+        m->peer[p] = (unsigned char *)ptr;
+        m->peer_mapped[p] = true;
+    }
+    m->connected = true;
+    return 0;
+}
+
+extern "C" int cxm_model_tp_info(const cxm_model *m, int *tp_rank, int *tp_size, int *vocab_lo, int *vocab_n) {
+    if (!m) {
+        set_error("null argument");
+        return -1;
+    }
+    if (tp_rank) *tp_rank = m->tp_rank;
+    if (tp_size) *tp_size = m->tp;
+    if (vocab_lo) *vocab_lo = m->v_off;
+    if (vocab_n) *vocab_n = m->v_loc;
     return 0;
 }
 
@@ -976,8 +1174,8 @@ extern "C" int cxm_forward(cxm_model *m, cxm_cache *c, const uint32_t *tokens, u
     CU(cudaSetDevice(m->device));
     CU(cudaMemcpyAsync(c->toks + c->len, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, m->stream));
     if (run_steps(m, c, STEP_PREFILL, n - 1) || run_steps(m, c, STEP_LOGITS, 1)) return -1;
-    if (logits_out)
-        CU(cudaMemcpyAsync(logits_out, m->logits, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    if (logits_out)  // this rank's vocabulary rows (all of them without tensor parallelism)
+        CU(cudaMemcpyAsync(logits_out, m->logits, (size_t)m->v_loc * 4, cudaMemcpyDeviceToHost, m->stream));
     if (check_err(m)) return -1;
     c->len += n;
     m->logits_valid = true;
@@ -1009,6 +1207,10 @@ extern "C" int cxm_sample(cxm_model *m, cxm_sampler *s, uint32_t *token_out) {
         return -1;
     }
     CU(cudaSetDevice(m->device));
+    if (s->temperature > 0.0f && m->tp > 1) {
+        set_error("sampling needs the whole vocabulary on one rank: tensor-parallel models decode greedily");
+        return -1;
+    }
     if (s->temperature > 0.0f) {  // the device Muestreador::elegir
         if (set_sampler(m, s) || launch_sample(m, nullptr, nullptr, m->samp_tok)) return -1;
         uint32_t tok = 0;
@@ -1309,10 +1511,15 @@ extern "C" int cxm_debug_expf(const float *x, float *y, uint64_t n) {
 extern "C" int cxm_step_launches(const cxm_model *m) { return m ? 1 : 0; }
 
 extern "C" int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, float *ms_total) {
+    return cxm_bench_decode_sampled(m, c, nullptr, steps, ms_total);
+}
+
+extern "C" int cxm_bench_decode_sampled(cxm_model *m, cxm_cache *c, cxm_sampler *s, uint32_t steps, float *ms_total) {
     if (!m || !c || !ms_total || c->m != m) {
         set_error("bad arguments");
         return -1;
     }
+    const bool sampled = s && s->temperature > 0.0f;
     if (c->len == 0 || (uint64_t)c->len + steps + 1 > std::min<uint64_t>(c->max_tokens, (uint64_t)m->cfg.ctx)) {
         set_error("cache needs a token to start from and room for %u more", steps);
         return -1;
@@ -1320,8 +1527,9 @@ extern "C" int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, floa
     CU(cudaSetDevice(m->device));
     // the step reads the token at toks[len]; start from the last cached one
     if (set_len(c, c->len - 1)) return -1;
+    if (sampled && set_sampler(m, s)) return -1;
     cudaGraphExec_t g;
-    if (get_graph(m, c, STEP_GREEDY, &g)) return -1;
+    if (get_graph(m, c, sampled ? STEP_SAMPLE : STEP_GREEDY, &g)) return -1;
     cudaEvent_t e0, e1;
     CU(cudaEventCreate(&e0));
     CU(cudaEventCreate(&e1));
@@ -1333,6 +1541,17 @@ extern "C" int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, floa
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     if (check_err(m)) return -1;
+    if (sampled) {  // one draw per step
+        uint64_t st = s->state;
+        for (uint32_t i = 0; i < steps; i++) {
+            uint64_t x = st;
+            x ^= x >> 12;
+            x ^= x << 25;
+            x ^= x >> 27;
+            st = x;
+        }
+        s->state = st;
+    }
     return set_len(c, c->len + steps);
 }
 

@@ -51,6 +51,30 @@ int  cxm_model_config(const cxm_model *m, cxm_config *out);
 uint64_t cxm_model_weight_bytes(const cxm_model *m);
 void cxm_model_close(cxm_model *m);
 
+/* ── tensor parallelism (one process per GPU; no counterpart in the
+ * reference, whose engine runs one model on one machine) ──────────────── */
+
+/* Rank `tp_rank` of `tp_size` (1..8): this process's GPU holds q/k/v and
+ * gate/up rows of its heads / FFN rows, the K slice of o_proj and ffn_down
+ * for them (whole super-blocks), its share of the output rows, and the full
+ * embedding and norms. Every decode step then exchanges the o_proj and
+ * ffn_down partial sums with the other ranks (added in rank order, then the
+ * residual) and the argmax of each vocabulary slice, over peer memory inside
+ * the decode kernel; each wait is bounded (a lost rank ends the step with an
+ * error, never a hang). Greedy decode only. cxm_model_config reports the
+ * whole model. The model runs after cxm_tp_connect. */
+int cxm_model_open_tp(const char *gguf_path, int device, int tp_rank, int tp_size, cxm_model **out);
+#define CXM_TP_HANDLE_BYTES 64
+/* The CUDA IPC handle of this rank's exchange area (CXM_TP_HANDLE_BYTES). */
+int cxm_tp_handle(cxm_model *m, uint8_t *handle_out);
+/* Map every rank's exchange area: `handles` holds tp_size handles in rank
+ * order (this rank's own included), as cxm_tp_handle returned them. */
+int cxm_tp_connect(cxm_model *m, const uint8_t *handles);
+/* this rank, the number of ranks, and this rank's vocabulary rows
+ * [vocab_lo, vocab_lo + vocab_n): the logits cxm_forward returns when
+ * tp_size > 1 (vocab_n floats) */
+int cxm_model_tp_info(const cxm_model *m, int *tp_rank, int *tp_size, int *vocab_lo, int *vocab_n);
+
 /* ── KV cache (src/forward.rs:62-137) ─────────────────────────────────── */
 
 /* Cache::nuevo: f32 K and V per layer, [max_tokens x n_head_kv*head_dim],
@@ -146,6 +170,11 @@ int cxm_debug_expf(const float *x, float *y, uint64_t n);
  * current end, timing on the device (CUDA events on the model's stream).
  * Inputs stay resident; the cache grows by `steps`. */
 int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, float *ms_total);
+
+/* The same with the sampled step (decode kernel, then the device sampler,
+ * Muestreador::elegir) for a sampler with temperature > 0; the sampler's
+ * state advances one draw per step. NULL or temperature 0: greedy. */
+int cxm_bench_decode_sampled(cxm_model *m, cxm_cache *c, cxm_sampler *s, uint32_t steps, float *ms_total);
 
 /* Average device time of one gate|up matvec phase (the largest of a layer)
  * of the decode kernel: `reps` such phases, cycling over the layers so every

@@ -44,6 +44,14 @@ const char *orc_last_error(void) { return g_err; }
 
 static int g_threads = 0;
 void orc_set_threads(int n) { g_threads = n; }
+
+/* Tensor-parallel emulation (test infrastructure for the GPU's TP path, not
+ * a reference behaviour): with n ranks, o_proj and ffn_down are computed as
+ * n partial sums, each over its K slice of whole super-blocks (the K/n
+ * values of rank r's heads / FFN rows), added in rank order before the
+ * residual. Every other projection splits by rows, which changes no value. */
+static int g_tp = 1;
+void orc_set_tp(int n) { g_tp = n > 0 ? n : 1; }
 int orc_get_threads(void) {
     if (g_threads > 0) return g_threads;
     long n = sysconf(_SC_NPROCESSORS_ONLN);
@@ -1384,6 +1392,37 @@ static int project(orc_model *m, const float *x, int t, const orc_tensor *w, con
     return 0;
 }
 
+/* project() without bias, as the sum over `tp` K slices of the row, slice
+ * by slice in order (orc_set_tp); tp = 1 is project() itself */
+static int project_split(orc_model *m, const float *x, int t, const orc_tensor *w, float *dst, int tp) {
+    int k = (int)w->dims[0], n = (int)w->dims[1];
+    if (tp <= 1) return project(m, x, t, w, NULL, dst);
+    int sub = orc_sub_block(w->type);
+    if (k % (256 * tp) || sub == 0) { set_err("%d values do not split over %d ranks", k, tp); return -1; }
+    size_t ks = (size_t)k / tp, nsub = (size_t)k / sub, rb = (size_t)k / 256 * orc_bytes_per_block(w->type);
+    int8_t *xq = (int8_t *)malloc((size_t)t * k);
+    float *xe = (float *)malloc(sizeof(float) * (size_t)t * nsub), *xs = (float *)malloc(sizeof(float) * (size_t)t * nsub);
+    for (int f = 0; f < t; f++)
+        orc_quantize_i8(x + (size_t)f * k, (size_t)k, sub, xq + (size_t)f * k, xe + f * nsub, xs + f * nsub);
+    const uint8_t *base = gguf_data(&m->g, w);
+    for (int f = 0; f < t; f++)
+        for (int j = 0; j < n; j++) {
+            float s = 0.0f;
+            for (int r = 0; r < tp; r++) {
+                const size_t o = (size_t)r * ks;
+                const float part = orc_dot_row(w->type, base + (size_t)j * rb + o / 256 * orc_bytes_per_block(w->type),
+                                               xq + (size_t)f * k + o, xe + f * nsub + o / sub, xs + f * nsub + o / sub,
+                                               ks / 256);
+                s = r == 0 ? part : s + part;
+            }
+            dst[(size_t)f * n + j] = s;
+        }
+    free(xq);
+    free(xe);
+    free(xs);
+    return 0;
+}
+
 static int read_vec(orc_model *m, const orc_tensor *t, float *dst, size_t n) {
     return orc_dequantize(t->type, gguf_data(&m->g, t), t->nbytes, n, dst);
 }
@@ -1428,14 +1467,14 @@ int orc_forward(orc_model *m, orc_cache *c, const uint32_t *tokens, int t, float
         memcpy(c->k[l] + (size_t)c->len * kvd, kk, sizeof(float) * T * kvd);
         memcpy(c->v[l] + (size_t)c->len * kvd, vv, sizeof(float) * T * kvd);
         if (orc_attention(q, c->k[l], c->v[l], t, total, H, KV, hd, att)) goto done;
-        if (project(m, att, t, L->o, NULL, proj)) goto done;
+        if (project_split(m, att, t, L->o, proj, g_tp)) goto done;
         for (size_t i = 0; i < T * D; i++) x[i] += proj[i];
         read_vec(m, L->ffn_norm, w, (size_t)D);
         for (int i = 0; i < t; i++) orc_rmsnorm(xn + (size_t)i * D, x + (size_t)i * D, w, (size_t)D, cfg->eps);
         if (project(m, xn, t, L->gate, NULL, gate) || project(m, xn, t, L->up, NULL, up)) goto done;
         orc_silu(act, gate, T * F);
         for (size_t i = 0; i < T * F; i++) act[i] *= up[i];
-        if (project(m, act, t, L->down, NULL, proj)) goto done;
+        if (project_split(m, act, t, L->down, proj, g_tp)) goto done;
         for (size_t i = 0; i < T * D; i++) x[i] += proj[i];
     }
     read_vec(m, m->out_norm, w, (size_t)D);

@@ -123,6 +123,9 @@ void orc_expf(const float *x, float *y, size_t n);
 
 void orc_set_threads(int n);
 int  orc_get_threads(void);
+/* test infrastructure: emulate n tensor-parallel ranks (o_proj and ffn_down
+ * as n K-slice partial sums added in rank order); 1 = the reference */
+void orc_set_tp(int n);
 
 #ifdef __cplusplus
 }

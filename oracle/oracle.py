@@ -83,6 +83,7 @@ def _declare(L: C.CDLL) -> None:
         "orc_cache_fill": (None, [P, C.c_int, C.c_uint64]),
         "orc_expf": (None, [P, P, C.c_size_t]),
         "orc_set_threads": (None, [C.c_int]),
+        "orc_set_tp": (None, [C.c_int]),
         "orc_get_threads": (C.c_int, []),
     }
     for name, (res, args) in sig.items():
@@ -313,6 +314,11 @@ class Model:
 
 def set_threads(n: int) -> None:
     lib().orc_set_threads(n)
+
+
+def set_tp(n: int) -> None:
+    """Emulate n tensor-parallel ranks in o_proj / ffn_down (1: the reference)."""
+    lib().orc_set_tp(n)
 
 
 def threads() -> int:
