@@ -288,6 +288,69 @@ def run_formats(args, rank: int, world: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_tp(args, rank: int, world: int, local: int) -> None:
+    """`--workload tp`: one Llama-3-8B-shaped Q4_K_M
+    conversation, tensor-parallel over the ranks (torchrun, one process per
+    GPU): each rank holds its heads / FFN rows / vocabulary rows, and every
+    step exchanges the o_proj and ffn_down partial sums and the argmax over
+    peer memory inside the decode kernel. Untimed prefill of a seeded prompt,
+    then K greedy steps timed with CUDA events; value = tokens of the one
+    conversation / the slowest rank's time (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import cosxamix_b200 as cx
+    from cosxamix_b200 import tensor_parallel as tpm
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=timedelta(seconds=1200))
+    if rank == 0:
+        ensure_model(args.config, args.seed)
+    if world > 1:
+        dist.barrier()
+    m = cx.Modelo(model_path(args.config, args.seed), device=local, tp=(rank, world))
+    if world > 1:
+        tpm.connect(m)
+    cache = m.cache(min(args.prompt + args.warmup + args.steps + 8, m.cfg.ctx))
+    m.forward(seeded_prompt(args.seed, args.prompt, m.cfg.vocab), cache)  # prefill (untimed)
+    m.bench_decode(cache, args.warmup)
+    clocks = Clocks(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = m.bench_decode(cache, args.steps)
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    peak, peak_kind = peaks()
+    wbytes = m.weight_bytes  # this rank's share
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = args.steps / (ms / 1000.0)
+    line = {
+        "metric": "decode tok/s bs=1, 8B-shape Q4_K_M, tensor-parallel", "value": round(value, 3), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8-dot/f32",
+        "data": "synthetic",
+        "config": {"workload": f"configs[4]: {args.config} shape Q4_K_M, {args.prompt}-token seeded prompt, "
+                               f"greedy decode bs=1", "parallelism": f"tp{world} (o_proj/ffn_down partials and "
+                               f"the argmax exchanged over peer memory inside the decode kernel)",
+                   "l2": "inputs larger than L2: the weight shares stream from HBM every step"},
+        "weight_stream": {"bytes_per_token_rank0": wbytes,
+                          "gbs_per_gpu_rank0": round(wbytes / (ms / args.steps / 1000.0) / 1e9, 1),
+                          "peak_gbs": peak, "peak_kind": peak_kind},
+        "gpu_launches": args.steps * m.step_launches, "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -299,7 +362,7 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "shared-prefix", "formats"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "shared-prefix", "formats", "tp"])
     ap.add_argument("--conversations", type=int, default=64)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -313,6 +376,13 @@ def main() -> None:
         return
     if args.workload == "shared-prefix":
         run_shared_prefix(args, rank, world, local)
+        return
+    if args.workload == "tp":
+        if args.config == "qwen3b":  # configs[4] is the 8B shape with a 4096-token prompt
+            args.config = "llama8b"
+            if args.prompt == 512:
+                args.prompt = 4096
+        run_tp(args, rank, world, local)
         return
     if args.workload == "formats":
         if args.prompt == 512:  # the default of the main workload; configs[2] prompts with 128
