@@ -226,7 +226,11 @@ def run_formats(args, rank: int, world: int, local: int) -> None:
     128-token seeded prompt (untimed prefill), then sampled decode at
     temperature 0.7, top-p 0.9 (seed 42), every step the decode kernel plus
     the device sampler. Per format: device-timed tok/s and weight-stream GB/s.
-    Each rank runs its own conversation (replicated weights, no collective)."""
+    Each rank runs its own conversation (replicated weights, no collective).
+    The greedy decode step is timed as well, K more steps on the same cache:
+    its weight-stream GB/s is the format's figure, the sampled step's extra
+    time is the device sampler's (sequential sums over the whole vocabulary
+    in the reference's order)."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -246,7 +250,7 @@ def run_formats(args, rank: int, world: int, local: int) -> None:
         if world > 1:
             dist.barrier()
         m = cx.Modelo(model_path(name, args.seed), device=local)
-        cache = m.cache(args.prompt + args.warmup + args.steps + 8)
+        cache = m.cache(args.prompt + args.warmup + 2 * args.steps + 8)
         m.forward(seeded_prompt(args.seed + rank, args.prompt, m.cfg.vocab), cache)
         samp = cx.Muestreador(42, 0.7, 0.9)
         m.bench_decode(cache, args.warmup, samp)
@@ -255,14 +259,18 @@ def run_formats(args, rank: int, world: int, local: int) -> None:
             dist.barrier()
         torch.cuda.synchronize()
         ms = m.bench_decode(cache, args.steps, samp)
+        # the decode kernel alone (greedy steps), for the format's weight stream
+        ms_k = m.bench_decode(cache, args.steps)
         clk = clocks.stop()
         if world > 1:
-            t = torch.tensor([ms], device="cuda")
+            t = torch.tensor([ms, ms_k], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+            ms, ms_k = (float(v) for v in t.tolist())
         tok_s = world * args.steps / (ms / 1000.0)
-        gbs = m.weight_bytes / (ms / args.steps / 1000.0) / 1e9
+        gbs = m.weight_bytes / (ms_k / args.steps / 1000.0) / 1e9
         out[fmt] = {"tok_s": round(tok_s, 3), "ms_per_step": round(ms / args.steps, 4),
+                    "decode_kernel_ms_per_step": round(ms_k / args.steps, 4),
+                    "sampler_ms_per_step": round((ms - ms_k) / args.steps, 4),
                     "weight_bytes": m.weight_bytes, "weight_gbs_per_gpu": round(gbs, 1),
                     "frac": round(gbs / peak, 4), "clocks": clk}
         total_ms += ms
