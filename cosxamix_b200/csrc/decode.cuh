@@ -168,6 +168,7 @@ struct AtPhase {
     const float *q, *k, *v;  // k/v: this layer's cache, [max_pos][KV*hd]
     float *out, *scores;
     int H, KV, hd, score_stride, P;  // P: positions per score item
+    int dims;                        // output dims per attention item
     float scale;
 };
 
@@ -836,13 +837,14 @@ __device__ void phase_xargmax(const DecodeArgs &A, unsigned ep, volatile int *ab
 }
 
 // ── attention phases (src/ops.rs:1258-1325), reference order ──
-constexpr int kAttnVChunk = 64, kAttnVRing = 8, kAttnDims = 16;
+constexpr int kAttnVChunk = 64, kAttnVRing = 8;
 
 __host__ __device__ inline size_t scores_region(int P, int G, int hd) {
     return ((size_t)P * (hd + 4) + (size_t)G * hd) * sizeof(float);
 }
-__host__ __device__ inline size_t attn_region(int max_pos) {
-    return ((size_t)((max_pos + 3) & ~3) + (size_t)kAttnVRing * kAttnVChunk * kAttnDims) * sizeof(float);
+// dims: output dims per work item (a multiple of 16 dividing head_dim, at most 256)
+__host__ __device__ inline size_t attn_region(int max_pos, int dims) {
+    return ((size_t)((max_pos + 3) & ~3) + (size_t)kAttnVRing * kAttnVChunk * dims) * sizeof(float);
 }
 
 // score[h][p] = (sequential dot of q_h and k_p over the head dim) · scale; an
@@ -894,21 +896,22 @@ __device__ void phase_scores(const AtPhase &at, int n, float *region) {
 // and kAttnDims dims
 __device__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region, float *fred, float *fbc) {
     const int tid = threadIdx.x, nt = kDW * 32, hd = at.hd, G = at.H / at.KV, kvd = at.KV * hd;
-    const int nslice = hd / kAttnDims, items = at.H * nslice;
+    const int dims = at.dims, nslice = hd / dims, items = at.H * nslice;
     float *pr = region;
     float *vs = region + ((max_pos + 3) & ~3);
     const int nchunks = (n + kAttnVChunk - 1) / kAttnVChunk;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
-        const int h = item / nslice, d0 = (item % nslice) * kAttnDims, g = h / G;
+        const int h = item / nslice, d0 = (item % nslice) * dims, g = h / G;
         const float *sc = at.scores + (size_t)h * at.score_stride;
         const float *vb = at.v + (size_t)g * hd + d0;
         auto stage = [&](int c) {
             if (c >= nchunks) return;
             const int base = c * kAttnVChunk, cnt = min(kAttnVChunk, n - base);
-            float *dst = vs + (c % kAttnVRing) * kAttnVChunk * kAttnDims;
-            for (int i = tid; i < cnt * (kAttnDims / 4); i += nt) {
-                const int r = i / (kAttnDims / 4), q = i - r * (kAttnDims / 4);
-                cp_async16(dst + r * kAttnDims + 4 * q, vb + (size_t)(base + r) * kvd + 4 * q);
+            float *dst = vs + (c % kAttnVRing) * kAttnVChunk * dims;
+            const int d4 = dims / 4;
+            for (int i = tid; i < cnt * d4; i += nt) {
+                const int r = i / d4, q = i - r * d4;
+                cp_async16(dst + r * dims + 4 * q, vb + (size_t)(base + r) * kvd + 4 * q);
             }
         };
         for (int i = tid; i < (n + 3) / 4; i += nt) cp_async16(pr + 4 * i, sc + 4 * i);
@@ -960,14 +963,15 @@ __device__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region,
             cp_async_commit();
             cp_async_wait<kAttnVRing - 1>();
             dsync();
-            if (tid < kAttnDims) {
-                const float *src = vs + (c % kAttnVRing) * kAttnVChunk * kAttnDims + tid;
+            if (tid < dims) {
+                const float *src = vs + (c % kAttnVRing) * kAttnVChunk * dims + tid;
                 const int base = c * kAttnVChunk, cnt = min(kAttnVChunk, n - base);
-                for (int r = 0; r < cnt; r++) acc = fa(acc, fm(pr[base + r], src[r * kAttnDims]));
+#pragma unroll 8
+                for (int r = 0; r < cnt; r++) acc = fa(acc, fm(pr[base + r], src[r * dims]));
             }
             dsync();
         }
-        if (tid < kAttnDims) at.out[(size_t)h * hd + d0 + tid] = acc;
+        if (tid < dims) at.out[(size_t)h * hd + d0 + tid] = acc;
         cp_async_wait<0>();
         dsync();
     }

@@ -449,12 +449,21 @@ size_t phase_region(const Phase &ph, int max_pos) {
         return act_bytes(ph.mv.K, ph.mv.need16, ph.mv.need32) +
                (ph.mv.prologue == PRO_QUANT ? (size_t)ph.mv.K * sizeof(float) : 0);
     if (ph.kind == PH_SCORES) return scores_region(ph.at.P, ph.at.H / ph.at.KV, ph.at.hd);
-    if (ph.kind == PH_ATTN) return attn_region(max_pos);
+    if (ph.kind == PH_ATTN) return attn_region(max_pos, ph.at.dims);
     return 0;
 }
 
 // positions per score item: the G query heads of a kv head share its K rows
 int score_positions(int G) { return std::max(1, std::min(64, 256 / std::max(1, G))); }
+
+// Output dims per attention item: the fewest (a multiple of 16 dividing the
+// head) that give at most one item per SM, so every head's softmax and its
+// position-by-position sums run in one round; at least 16.
+int attn_dims(int H, int hd, int sms) {
+    int d = 16;
+    while (d < hd && (long long)H * (hd / d) > sms && hd % (2 * d) == 0 && 2 * d <= 256) d *= 2;
+    return d;
+}
 
 // The step for the token at *d_len of cache c (src/forward.rs:375-505):
 // embedding (fused into layer 0's first prologue), then per layer q|k|v,
@@ -520,6 +529,7 @@ std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode) {
         at.hd = hd;
         at.score_stride = (cfg.ctx + 3) & ~3;
         at.P = score_positions(H / KV);
+        at.dims = attn_dims(H, hd, m->sms);
         at.scale = 1.0f / sqrtf((float)hd);  // src/ops.rs:1287
         {
             Phase ph{};

@@ -159,13 +159,56 @@ __device__ int seq_scan(const float *src, int len, float *dst, bool use_stop, fl
         float *nxt = stage + ((c + 1) & 1) * kScanChunk;
         const int base = c * kScanChunk, cnt = min(kScanChunk, len - base);
         if (tid == 0) {
-            for (int i = 0; i < cnt; i++) {
-                acc = __fadd_rn(acc, cur[i]);
-                if (dst) dst[base + i] = acc;
-                if (use_stop && acc >= stop) {
-                    done = base + i + 1;
+            // 16 values per step: four vector loads in flight, then the adds
+            // in order; the running sums never decrease (probabilities are
+            // >= 0), so the step's last one tells whether the stop is inside
+            int i = 0;
+            for (; i + 16 <= cnt; i += 16) {
+                const float4 *c4 = (const float4 *)(cur + i);
+                const float4 q0 = c4[0], q1 = c4[1], q2 = c4[2], q3 = c4[3];
+                float r[16];
+                r[0] = __fadd_rn(acc, q0.x);
+                r[1] = __fadd_rn(r[0], q0.y);
+                r[2] = __fadd_rn(r[1], q0.z);
+                r[3] = __fadd_rn(r[2], q0.w);
+                r[4] = __fadd_rn(r[3], q1.x);
+                r[5] = __fadd_rn(r[4], q1.y);
+                r[6] = __fadd_rn(r[5], q1.z);
+                r[7] = __fadd_rn(r[6], q1.w);
+                r[8] = __fadd_rn(r[7], q2.x);
+                r[9] = __fadd_rn(r[8], q2.y);
+                r[10] = __fadd_rn(r[9], q2.z);
+                r[11] = __fadd_rn(r[10], q2.w);
+                r[12] = __fadd_rn(r[11], q3.x);
+                r[13] = __fadd_rn(r[12], q3.y);
+                r[14] = __fadd_rn(r[13], q3.z);
+                r[15] = __fadd_rn(r[14], q3.w);
+                if (dst) {
+                    float4 *d4 = (float4 *)(dst + base + i);
+                    d4[0] = make_float4(r[0], r[1], r[2], r[3]);
+                    d4[1] = make_float4(r[4], r[5], r[6], r[7]);
+                    d4[2] = make_float4(r[8], r[9], r[10], r[11]);
+                    d4[3] = make_float4(r[12], r[13], r[14], r[15]);
+                }
+                if (use_stop && r[15] >= stop) {
+                    int j = 0;
+                    while (r[j] < stop) j++;
+                    acc = r[j];
+                    done = base + i + j + 1;
                     *flag = 1;
                     break;
+                }
+                acc = r[15];
+            }
+            if (!(use_stop && done < len)) {
+                for (; i < cnt; i++) {
+                    acc = __fadd_rn(acc, cur[i]);
+                    if (dst) dst[base + i] = acc;
+                    if (use_stop && acc >= stop) {
+                        done = base + i + 1;
+                        *flag = 1;
+                        break;
+                    }
                 }
             }
         } else if (c + 1 < nchunk) {
