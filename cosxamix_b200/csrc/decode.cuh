@@ -262,7 +262,7 @@ __host__ __device__ inline size_t act_bytes(int K, int need16, int need32) {
 
 struct Act {
     int8_t *q16, *q32;
-    float *e16, *s16, *e32, *s32;
+    float2 *es16, *es32;  // (scale, sum) per sub-block of 16 / 32
 };
 
 __device__ inline Act carve_act(unsigned char *region, int K, int need16, int need32) {
@@ -271,8 +271,8 @@ __device__ inline Act carve_act(unsigned char *region, int K, int need16, int ne
     const int nblk = K / 256;
     if (need16) { a.q16 = (int8_t *)p; p += nblk * kXqStride; }
     if (need32) { a.q32 = (int8_t *)p; p += nblk * kXqStride; }
-    if (need16) { a.e16 = (float *)p; p += K / 16 * 4; a.s16 = (float *)p; p += K / 16 * 4; }
-    if (need32) { a.e32 = (float *)p; p += K / 32 * 4; a.s32 = (float *)p; p += K / 32 * 4; }
+    if (need16) { a.es16 = (float2 *)p; p += K / 16 * 8; }
+    if (need32) { a.es32 = (float2 *)p; p += K / 32 * 8; }
     return a;
 }
 
@@ -287,11 +287,14 @@ __device__ inline Act carve_act(unsigned char *region, int K, int need16, int ne
 // then f32(x·scale)·w. The f64 sum of f32 squares is taken per thread, then
 // across lanes and warps. A normed activation has at most two rounds, and
 // its norm weights are loaded before the grid barrier (they depend on
-// nothing). A plain one (the attention output, the FFN's hidden vector) is
-// first staged whole in shared memory by one bulk copy: a copy engine pulls
-// data that every CTA reads at once far faster than 256 threads' loads.
+// nothing). A plain one of at most kMaxStaged values (the attention output)
+// is first staged whole in shared memory by one bulk copy: a copy engine
+// pulls data that every CTA reads at once faster than the threads' loads. A
+// longer one (the FFN's hidden vector) is loaded straight into registers,
+// four rounds at a time (staging it would take the ring's shared memory).
 constexpr int kMaxActivation = 16384;         // values of a quantized activation
-constexpr int kMaxNormed = 2 * kDW * 32 * 8;  // 4096: values of a normed one
+constexpr int kMaxNormed = 2 * kDW * 32 * 8;  // values of a normed one (4096 at 8 warps)
+constexpr int kMaxStaged = 4096;              // values of a quantize-only activation staged by a bulk copy
 
 __device__ __forceinline__ void load8(const float *src, int hc, float (&x)[8], bool cg) {
     const float4 *p = (const float4 *)src + 2 * hc;
@@ -400,8 +403,7 @@ __device__ __forceinline__ void quant_rounds(const MvPhase &P, const Act &a, int
             if (hc < nh) {
                 *(uint2 *)(a.q16 + ((16 * c) >> 8) * kXqStride + ((16 * c) & 255) + 8 * (hc & 1)) = make_uint2(w0[r], w1[r]);
                 if (!(hc & 1)) {
-                    a.e16[c] = am[r] > 0.0f ? __fdiv_rn(am[r], 127.0f) : 0.0f;
-                    a.s16[c] = (float)sm[r];
+                    a.es16[c] = make_float2(am[r] > 0.0f ? __fdiv_rn(am[r], 127.0f) : 0.0f, (float)sm[r]);
                 }
             }
         }
@@ -426,8 +428,7 @@ __device__ __forceinline__ void quant_rounds(const MvPhase &P, const Act &a, int
             if (hc < nh) {
                 *(uint2 *)(a.q32 + ((16 * c) >> 8) * kXqStride + ((16 * c) & 255) + 8 * (hc & 1)) = make_uint2(w0[r], w1[r]);
                 if (!(hc & 3)) {
-                    a.e32[hc >> 2] = am[r] > 0.0f ? __fdiv_rn(am[r], 127.0f) : 0.0f;
-                    a.s32[hc >> 2] = (float)sm[r];
+                    a.es32[hc >> 2] = make_float2(am[r] > 0.0f ? __fdiv_rn(am[r], 127.0f) : 0.0f, (float)sm[r]);
                 }
             }
         }
@@ -469,6 +470,13 @@ __device__ __forceinline__ void quantize_act(const MvPhase &P, uint32_t tok, con
         norm8(x[1], scale, nw.w[1]);
         if (nr == 1) quant_rounds<1>(P, a, tid, *(const float(*)[1][8])x);
         else quant_rounds<2>(P, a, tid, x);
+    } else if (!stage) {  // straight from L2, four rounds at a time, each batch's loads issued first
+        for (int i = 0; i < nr; i += 4) {
+            float x[4][8];
+#pragma unroll
+            for (int r = 0; r < 4; r++) load_x(P, (i + r) * nt + tid, x[r]);
+            quant_rounds<4>(P, a, i * nt + tid, x);
+        }
     } else {  // from the staged copy, two rounds at a time
         const int nh = P.K >> 3;
         for (int i = 0; i < nr; i += 2) {
@@ -1036,7 +1044,7 @@ __device__ __forceinline__ float group_dot(const DecodeArgs &A, Ring &R, int war
     constexpr int NSUB = S32 ? 8 : 16;
     const int lpr = g.lpr, rpt = g.rpt, bl = g.bl, sl = g.sl;
     const int8_t *xq = S32 ? act.q32 : act.q16;
-    const float *xe = S32 ? act.e32 : act.e16, *xs = S32 ? act.s32 : act.s16;
+    const float2 *xes = S32 ? act.es32 : act.es16;
     float acc = 0.0f;
     for (int t = 0; t < g.ntile; t++) {
         const unsigned char *tile = ring_next(A, R, warp, lane);
@@ -1044,7 +1052,7 @@ __device__ __forceinline__ float group_dot(const DecodeArgs &A, Ring &R, int war
         float tv[NSUB];
         if (bl < nb) {
             const int b = lpr * t + bl;
-            const XB xb{xq + b * kXqStride, xe + b * NSUB, xs + b * NSUB};
+            const XB xb{xq + b * kXqStride, xes + b * NSUB};
             tile_terms<T>(tile, lane, rpt * nb, xb, tv);
         } else {
 #pragma unroll
@@ -1163,8 +1171,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
             const MvPhase &P = ph.mv;
             const Act act = carve_act(region, P.K, P.need16, P.need32);
             if (P.prologue == PRO_EMBED && blockIdx.x == 0 && tid == 0 && A.argmax_key) *A.argmax_key = 0ull;
-            float *stage = (float *)(region + act_bytes(P.K, P.need16, P.need32));
-            if (P.prologue == PRO_QUANT) {
+            float *stage = P.prologue == PRO_QUANT && P.K <= kMaxStaged
+                               ? (float *)(region + act_bytes(P.K, P.need16, P.need32))
+                               : nullptr;
+            if (stage) {
                 const uint32_t kbytes = (uint32_t)P.K * 4u;
                 if (tid == 0) {
                     // the staging area was last read through the generic proxy

@@ -303,7 +303,7 @@ constexpr int kXqStride = 272;
 
 struct XB {  // one block of the quantized activation
     const int8_t *q;      // 256 values
-    const float *e, *s;   // its scales and sums, nsub each
+    const float2 *es;     // (scale, sum) of each of its nsub sub-blocks: one 8-byte load per sub-block
 };
 
 __device__ __forceinline__ int dot16(uint4 w, int4 a) {
@@ -311,6 +311,21 @@ __device__ __forceinline__ int dot16(uint4 w, int4 a) {
     s = __dp4a((int)w.y, a.y, s);
     s = __dp4a((int)w.z, a.z, s);
     return __dp4a((int)w.w, a.w, s);
+}
+
+// unsigned bytes of w times signed bytes of a, accumulated (dp4a.u32.s32)
+__device__ __forceinline__ int dp4a_us(uint32_t w, int a, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(w), "r"(a), "r"(c));
+    return d;
+}
+// the same over 16 bytes: w's bytes are high nibbles left in place (n·16),
+// so the sum is 16 times the nibbles' sum, exactly
+__device__ __forceinline__ int dot16_hi(uint4 w, int4 a, int c) {
+    int s = dp4a_us(w.x, a.x, c);
+    s = dp4a_us(w.y, a.y, s);
+    s = dp4a_us(w.z, a.z, s);
+    return dp4a_us(w.w, a.w, s);
 }
 __device__ __forceinline__ uint4 and4(uint4 v, uint32_t m) { return make_uint4(v.x & m, v.y & m, v.z & m, v.w & m); }
 __device__ __forceinline__ uint4 shr4(uint4 v, int n) { return make_uint4(v.x >> n, v.y >> n, v.z >> n, v.w >> n); }
@@ -333,21 +348,29 @@ __device__ __forceinline__ void block_k4(const uint8_t *pa, int cs, const XB &x,
     for (int p = 0; p < 4; p++) {
         const uint4 wa = *(const uint4 *)(pa + (c0 + 2 * p) * cs), wb = *(const uint4 *)(pa + (c0 + 2 * p + 1) * cs);
         uint4 la = and4(wa, 0x0F0F0F0Fu), lb = and4(wb, 0x0F0F0F0Fu);
-        uint4 ha = and4(shr4(wa, 4), 0x0F0F0F0Fu), hb = and4(shr4(wb, 4), 0x0F0F0F0Fu);
+        uint4 ha = make_uint4(0, 0, 0, 0), hb = ha;
         if (Q5) {
+            ha = and4(shr4(wa, 4), 0x0F0F0F0Fu);
+            hb = and4(shr4(wb, 4), 0x0F0F0F0Fu);
             la = or4(la, shl4(and4(shr4(qh0, 2 * p), 0x01010101u), 4));
             lb = or4(lb, shl4(and4(shr4(qh1, 2 * p), 0x01010101u), 4));
             ha = or4(ha, shl4(and4(shr4(qh0, 2 * p + 1), 0x01010101u), 4));
             hb = or4(hb, shl4(and4(shr4(qh1, 2 * p + 1), 0x01010101u), 4));
         }
         const int s0 = dot16(la, xp[4 * p]) + dot16(lb, xp[4 * p + 1]);
-        const int s1 = dot16(ha, xp[4 * p + 2]) + dot16(hb, xp[4 * p + 3]);
+        int s1;
+        if (Q5) {
+            s1 = dot16(ha, xp[4 * p + 2]) + dot16(hb, xp[4 * p + 3]);
+        } else {  // the high nibbles in place: one mask per word instead of a shift and a mask
+            s1 = dot16_hi(and4(wb, 0xF0F0F0F0u), xp[4 * p + 3], dot16_hi(and4(wa, 0xF0F0F0F0u), xp[4 * p + 2], 0)) >> 4;
+        }
         int sc0, m0, sc1, m1;
         scale_min_k4(2 * p, hdr.y, hdr.z, hdr.w, sc0, m0);
         scale_min_k4(2 * p + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
         const int j0 = 2 * p;
-        t[j0] = fm(x.e[j0], fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), x.s[j0])));
-        t[j0 + 1] = fm(x.e[j0 + 1], fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), x.s[j0 + 1])));
+        const float2 es0 = x.es[j0], es1 = x.es[j0 + 1];
+        t[j0] = fm(es0.x, fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), es0.y)));
+        t[j0 + 1] = fm(es1.x, fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), es1.y)));
     }
 }
 
@@ -373,7 +396,8 @@ __device__ __forceinline__ void block_q6k(const uint8_t *pa, int cs, const uint8
                 const int g = 4 * h + gi, si = 2 * g + md;
                 const int s = dot16(v, xp[si]);
                 const int sc = (int)(int8_t)((scw[si >> 2] >> (8 * (si & 3))) & 0xFF);
-                t[si] = fm(fm(x.e[si], fm(d, (float)sc)), fs((float)s, fm(32.0f, x.s[si])));
+                const float2 es = x.es[si];
+                t[si] = fm(fm(es.x, fm(d, (float)sc)), fs((float)s, fm(32.0f, es.y)));
             }
         }
     }
@@ -399,7 +423,8 @@ __device__ __forceinline__ void block_q3k(const uint8_t *pa, int cs, const uint8
                 const uint32_t aa = (wi & 1) ? a1 : a0;
                 const uint32_t wq = ((aa >> ((wi >> 1) * 4)) & 0x0F0F0F0Fu) | (((tt >> (2 * wi)) & 0x03030303u) << 4);
                 const int sc = (int)((wq >> (8 * (si & 3))) & 0xFF);
-                t[si] = fm(fm(x.e[si], fm(d, fs((float)sc, 32.0f))), fs((float)s, fm(4.0f, x.s[si])));
+                const float2 es = x.es[si];
+                t[si] = fm(fm(es.x, fm(d, fs((float)sc, 32.0f))), fs((float)s, fm(4.0f, es.y)));
             }
         }
     }
@@ -425,7 +450,8 @@ __device__ __forceinline__ void block_q2k(const uint8_t *pa, int cs, const uint8
                 const int s = dot16(v, xp[si]);
                 const int sc = (int)((scw[si >> 2] >> (8 * (si & 3))) & 0xFF);
                 const float ev = fm(d, (float)(sc & 0xF)), mv = fm(dm, (float)(sc >> 4));
-                t[si] = fm(x.e[si], fs(fm(ev, (float)s), fm(mv, x.s[si])));
+                const float2 es = x.es[si];
+                t[si] = fm(es.x, fs(fm(ev, (float)s), fm(mv, es.y)));
             }
         }
     }

@@ -445,9 +445,9 @@ Phase mv_phase(const std::vector<MvSeg> &segs, int K, int prologue, const float 
 }
 
 size_t phase_region(const Phase &ph, int max_pos) {
-    if (ph.kind == PH_MATVEC)  // the quantized activation (+ the staged input of a quantize-only prologue)
+    if (ph.kind == PH_MATVEC)  // the quantized activation (+ the staged input of a short quantize-only prologue)
         return act_bytes(ph.mv.K, ph.mv.need16, ph.mv.need32) +
-               (ph.mv.prologue == PRO_QUANT ? (size_t)ph.mv.K * sizeof(float) : 0);
+               (ph.mv.prologue == PRO_QUANT && ph.mv.K <= kMaxStaged ? (size_t)ph.mv.K * sizeof(float) : 0);
     if (ph.kind == PH_SCORES) return scores_region(ph.at.P, ph.at.H / ph.at.KV, ph.at.hd);
     if (ph.kind == PH_ATTN) return attn_region(max_pos, ph.at.dims);
     return 0;
