@@ -218,8 +218,9 @@ class Cache:
         _check(lib().cxm_cache_copy_prefix(src.h, n, self.h))
 
     def capa(self, layer: int, v: bool = False) -> np.ndarray:
+        """Layer `layer`'s K (or V) rows [0, len): this rank's KV heads."""
         cfg = self.modelo.cfg
-        out = np.zeros(len(self) * cfg.n_head_kv * cfg.head_dim, np.float32)
+        out = np.zeros(len(self) * (cfg.n_head_kv // self.modelo.tp_size) * cfg.head_dim, np.float32)
         _check(lib().cxm_cache_read(self.h, layer, int(v), _ptr(out)))
         return out
 

@@ -67,18 +67,31 @@ __device__ __forceinline__ float block_max(float v, float *red) {
     return r;
 }
 
+// the count of digit d in warp w's chunk: warp-major with a padded row, so
+// a warp's lanes with different digits hit different banks
+constexpr int kHistRow = 257;
+__device__ __forceinline__ int hidx(int d, int w) { return w * kHistRow + d; }
+
 // one stable counting pass of an LSD radix sort on 8 key bits; a warp owns a
 // contiguous chunk and keeps its elements' order
 __device__ void radix_pass(const uint32_t *kin, const uint32_t *vin, uint32_t *kout, uint32_t *vout, int n, int shift,
-                           uint32_t *hist /* [256][kSampWarps] */) {
+                           uint32_t *hist /* [kSampWarps][kHistRow] */) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int chunk = (n + kSampWarps - 1) / kSampWarps;
     const int lo = warp * chunk, hi = min(n, lo + chunk);
-    for (int i = tid; i < 256 * kSampWarps; i += kSampThreads) hist[i] = 0;
+    for (int i = tid; i < kHistRow * kSampWarps; i += kSampThreads) hist[i] = 0;
     __syncthreads();
-    for (int b = lo; b < hi; b += 32) {
-        const int i = b + lane;
-        if (i < hi) atomicAdd(&hist[((kin[i] >> shift) & 255) * kSampWarps + warp], 1u);
+    // four keys per lane in flight before their counts
+    for (int b = lo; b < hi; b += 128) {
+        uint32_t k[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = b + 32 * u + lane;
+            k[u] = i < hi ? __ldcg(kin + i) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            if (b + 32 * u + lane < hi) atomicAdd(&hist[hidx((k[u] >> shift) & 255, warp)], 1u);
     }
     __syncthreads();
     // exclusive scan over (digit, warp): digit-major, so equal digits keep
@@ -87,8 +100,9 @@ __device__ void radix_pass(const uint32_t *kin, const uint32_t *vin, uint32_t *k
         constexpr int kPer = 256 * kSampWarps / kSampThreads;
         uint32_t c[kPer], loc = 0;
 #pragma unroll
-        for (int j = 0; j < kPer; j++) {
-            c[j] = hist[tid * kPer + j];
+        for (int j = 0; j < kPer; j++) {  // entry e = digit * kSampWarps + warp
+            const int e = tid * kPer + j;
+            c[j] = hist[hidx(e / kSampWarps, e % kSampWarps)];
             loc += c[j];
         }
         uint32_t inc = loc;
@@ -113,27 +127,36 @@ __device__ void radix_pass(const uint32_t *kin, const uint32_t *vin, uint32_t *k
         uint32_t run = wsum[warp] + inc - loc;
 #pragma unroll
         for (int j = 0; j < kPer; j++) {
-            hist[tid * kPer + j] = run;
+            const int e = tid * kPer + j;
+            hist[hidx(e / kSampWarps, e % kSampWarps)] = run;
             run += c[j];
         }
     }
     __syncthreads();
+    // the scatter keeps the chunk's order, 32 keys at a time; the next 32
+    // keys and values are loaded while this 32 is placed
+    uint32_t kn = lo + lane < hi ? __ldcg(kin + lo + lane) : 0u;
+    uint32_t vn = lo + lane < hi ? __ldcg(vin + lo + lane) : 0u;
     for (int b = lo; b < hi; b += 32) {
         const int i = b + lane;
         const bool ok = i < hi;
-        const uint32_t k = ok ? kin[i] : 0u, d = (k >> shift) & 255;
+        const uint32_t k = kn, vv = vn, d = (k >> shift) & 255;
+        if (b + 32 + lane < hi) {
+            kn = __ldcg(kin + b + 32 + lane);
+            vn = __ldcg(vin + b + 32 + lane);
+        }
         const unsigned same = __match_any_sync(0xffffffffu, ok ? d : 0x100u + lane);
         const int rank = __popc(same & ((1u << lane) - 1));
         const int leader = __ffs(same) - 1;
         uint32_t base = 0;
-        if (ok && lane == leader) base = hist[d * kSampWarps + warp];
+        if (ok && lane == leader) base = hist[hidx(d, warp)];
         base = __shfl_sync(0xffffffffu, base, leader);
         if (ok) {
             kout[base + rank] = k;
-            vout[base + rank] = vin[i];
+            vout[base + rank] = vv;
         }
         __syncwarp();
-        if (ok && lane == leader) hist[d * kSampWarps + warp] = base + __popc(same);
+        if (ok && lane == leader) hist[hidx(d, warp)] = base + __popc(same);
         __syncwarp();
     }
     __syncthreads();
@@ -163,9 +186,24 @@ __device__ int seq_scan(const float *src, int len, float *dst, bool use_stop, fl
             // in order; the running sums never decrease (probabilities are
             // >= 0), so the step's last one tells whether the stop is inside
             int i = 0;
+            // the next step's four loads are issued before this step's adds
+            float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0, n2 = n0, n3 = n0;
+            if (16 <= cnt) {
+                const float4 *c4 = (const float4 *)cur;
+                n0 = c4[0];
+                n1 = c4[1];
+                n2 = c4[2];
+                n3 = c4[3];
+            }
             for (; i + 16 <= cnt; i += 16) {
-                const float4 *c4 = (const float4 *)(cur + i);
-                const float4 q0 = c4[0], q1 = c4[1], q2 = c4[2], q3 = c4[3];
+                const float4 q0 = n0, q1 = n1, q2 = n2, q3 = n3;
+                if (i + 32 <= cnt) {
+                    const float4 *c4 = (const float4 *)(cur + i + 16);
+                    n0 = c4[0];
+                    n1 = c4[1];
+                    n2 = c4[2];
+                    n3 = c4[3];
+                }
                 float r[16];
                 r[0] = __fadd_rn(acc, q0.x);
                 r[1] = __fadd_rn(r[0], q0.y);
@@ -242,7 +280,7 @@ __device__ __forceinline__ int first_above(const float *prefix, int len, float t
 __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constant__ SampleArgs a) {
     extern __shared__ __align__(16) float stage[];  // 2 x kScanChunk
     __shared__ float red[kSampWarps];
-    __shared__ uint32_t hist[256 * kSampWarps];
+    __shared__ uint32_t hist[kHistRow * kSampWarps];
     __shared__ float u_s, sum_s;
     __shared__ int flag_s;
     const int tid = threadIdx.x, n = a.n;
@@ -252,23 +290,47 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
         u_s = (float)(azar_next(st) >> 40) / 16777216.0f;
         *a.rng = st;
     }
-    // temperature, then softmax (src/ops.rs:1206-1230)
+    // temperature, then softmax (src/ops.rs:1206-1230). The element-wise
+    // loops take four elements per thread per step, loads first, so their
+    // L2 round trips overlap.
+    constexpr int kU = 4, kStep = kU * kSampThreads;
     float m = -INFINITY;
-    for (int i = tid; i < n; i += kSampThreads) {
-        const float v = __fmul_rn(a.logits[i], inv_t);
-        a.probs[i] = v;
-        m = fmaxf(m, v);
+    for (int i0 = tid; i0 < n; i0 += kStep) {
+        float v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; u++) v[u] = i0 + u * kSampThreads < n ? __ldcg(a.logits + i0 + u * kSampThreads) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < kU; u++)
+            if (i0 + u * kSampThreads < n) {
+                const float t = __fmul_rn(v[u], inv_t);
+                a.probs[i0 + u * kSampThreads] = t;
+                m = fmaxf(m, t);
+            }
     }
     m = block_max(m, red);
     if (!isfinite(m)) {
         const float p = __fdiv_rn(1.0f, (float)n);
         for (int i = tid; i < n; i += kSampThreads) a.probs[i] = p;
     } else {
-        for (int i = tid; i < n; i += kSampThreads) a.probs[i] = expf_glibc(__fsub_rn(a.probs[i], m));
+        for (int i0 = tid; i0 < n; i0 += kStep) {
+            float v[kU];
+#pragma unroll
+            for (int u = 0; u < kU; u++) v[u] = i0 + u * kSampThreads < n ? a.probs[i0 + u * kSampThreads] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < kU; u++)
+                if (i0 + u * kSampThreads < n) a.probs[i0 + u * kSampThreads] = expf_glibc(__fsub_rn(v[u], m));
+        }
         __syncthreads();
         seq_scan(a.probs, n, nullptr, false, 0.0f, stage, &sum_s, &flag_s);  // the total, in index order
         const float inv = __fdiv_rn(1.0f, sum_s);
-        for (int i = tid; i < n; i += kSampThreads) a.probs[i] = __fmul_rn(a.probs[i], inv);
+        for (int i0 = tid; i0 < n; i0 += kStep) {
+            float v[kU];
+#pragma unroll
+            for (int u = 0; u < kU; u++) v[u] = i0 + u * kSampThreads < n ? a.probs[i0 + u * kSampThreads] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < kU; u++)
+                if (i0 + u * kSampThreads < n) a.probs[i0 + u * kSampThreads] = __fmul_rn(v[u], inv);
+        }
     }
     __syncthreads();
     const float u = u_s;
@@ -281,9 +343,16 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
     } else {
         // descending probability, ties by ascending index: ascending key
         // 0x7fffffff - bits (probabilities are >= 0) on an index-ordered start
-        for (int i = tid; i < n; i += kSampThreads) {
-            a.key0[i] = 0x7fffffffu - __float_as_uint(a.probs[i]);
-            a.val0[i] = (uint32_t)i;
+        for (int i0 = tid; i0 < n; i0 += kStep) {
+            float v[kU];
+#pragma unroll
+            for (int u = 0; u < kU; u++) v[u] = i0 + u * kSampThreads < n ? a.probs[i0 + u * kSampThreads] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < kU; u++)
+                if (i0 + u * kSampThreads < n) {
+                    a.key0[i0 + u * kSampThreads] = 0x7fffffffu - __float_as_uint(v[u]);
+                    a.val0[i0 + u * kSampThreads] = (uint32_t)(i0 + u * kSampThreads);
+                }
         }
         __syncthreads();
         radix_pass(a.key0, a.val0, a.key1, a.val1, n, 0, hist);
@@ -292,7 +361,17 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
         radix_pass(a.key1, a.val1, a.key0, a.val0, n, 24, hist);
         const uint32_t *order = a.val0;
         float *sorted = a.key1 ? (float *)a.key1 : nullptr;  // probabilities in sorted order
-        for (int i = tid; i < n; i += kSampThreads) sorted[i] = a.probs[order[i]];
+        for (int i0 = tid; i0 < n; i0 += kStep) {
+            uint32_t o[kU];
+            float v[kU];
+#pragma unroll
+            for (int u = 0; u < kU; u++) o[u] = i0 + u * kSampThreads < n ? __ldcg(order + i0 + u * kSampThreads) : 0u;
+#pragma unroll
+            for (int u = 0; u < kU; u++) v[u] = i0 + u * kSampThreads < n ? a.probs[o[u]] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < kU; u++)
+                if (i0 + u * kSampThreads < n) sorted[i0 + u * kSampThreads] = v[u];
+        }
         __syncthreads();
         const int k = n < kCandidates ? n : kCandidates;
         seq_scan(sorted, k, nullptr, false, 0.0f, stage, &sum_s, &flag_s);  // the candidates' mass

@@ -9,7 +9,8 @@ one launch, behind grid barriers as in the step, cycling over the model's
 layers so every phase streams its own weights (36 layers x 25 MB > L2).
 Prints the per-phase time and the algorithmic weight bytes per second.
 With --decode: prefills a seeded P-token prompt (one decode-kernel launch
-per token), then times STEPS greedy decode steps (one launch each).
+per token), then times STEPS greedy decode steps (one launch each), or with
+--sample STEPS sampled steps (the decode kernel, then k_sample).
 `--layers` / `--vocab` shrink the synthetic model (same matrix shapes) so an
 ncu capture holds little device memory; keep layers x 25 MB above the 126 MB
 L2 for DRAM figures to mean something.
@@ -36,6 +37,7 @@ def main() -> None:
     ap.add_argument("--vocab", type=int, default=0)
     ap.add_argument("--decode", type=int, default=0)
     ap.add_argument("--prompt", type=int, default=16)
+    ap.add_argument("--sample", action="store_true", help="--decode with the device top-p sampler (T 0.7, top-p 0.9)")
     args = ap.parse_args()
     import bench
     import cosxamix_b200 as cx
@@ -58,9 +60,11 @@ def main() -> None:
     if args.decode:
         c = m.cache(min(m.cfg.ctx, args.prompt + args.decode + 8))
         m.forward(bench.seeded_prompt(args.seed, args.prompt, m.cfg.vocab), c)
-        ms = m.bench_decode(c, args.decode) / args.decode
-        print(json.dumps({"kernel": "k_decode step", "config": args.config, "layers": args.layers or None,
-                          "prompt": args.prompt, "step_ms": round(ms, 4),
+        samp = cx.Muestreador(42, 0.7, 0.9) if args.sample else None
+        ms = m.bench_decode(c, args.decode, samp) / args.decode
+        print(json.dumps({"kernel": "k_decode step" + (" + k_sample" if args.sample else ""), "config": args.config,
+                          "layers": args.layers or None,
+                          "vocab": m.cfg.vocab, "prompt": args.prompt, "step_ms": round(ms, 4),
                           "weight_gbs": round(m.weight_bytes / (ms / 1000) / 1e9, 1)}))
         return
     ms, nbytes = m.bench_matvec(args.reps)

@@ -273,6 +273,27 @@ def test_sampled_generation_matches_oracle(tiny_path):
     assert len(c) == len(oc)
 
 
+def test_sampled_bench_steps_replay_sampled_generation(tiny_path):
+    # cxm_bench_decode_sampled replays the sampled step graph from the
+    # cache's end: its KV rows and sampler state equal cxm_generate's
+    m = cx.Modelo(tiny_path)
+    prompt = prompt_of(13, 20, m.cfg.vocab)
+    n = 12
+    a, b = cx.Muestreador(7, 0.7, 0.9), cx.Muestreador(7, 0.7, 0.9)
+    c1 = m.cache()
+    m.generar(prompt, n, a, c1)
+    c2 = m.cache()
+    m.forward(prompt, c2)
+    m.bench_decode(c2, n, b)
+    assert b.estado == a.estado
+    rows = len(prompt) - 1 + n  # positions both caches hold after the same picks
+    assert len(c2) == rows
+    kvd = m.cfg.n_head_kv * m.cfg.head_dim
+    for layer in (0, m.cfg.n_layer - 1):
+        for v in (False, True):
+            np.testing.assert_array_equal(c1.capa(layer, v)[:rows * kvd], c2.capa(layer, v)[:rows * kvd])
+
+
 def test_qwen3b_vocab_sampler_matches_oracle(qwen3b_path):
     # the 151,936-entry vocabulary at the benchmark's sampling settings
     m = cx.Modelo(qwen3b_path)
