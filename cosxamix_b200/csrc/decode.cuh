@@ -294,7 +294,7 @@ __device__ inline Act carve_act(unsigned char *region, int K, int need16, int ne
 // four rounds at a time (staging it would take the ring's shared memory).
 constexpr int kMaxActivation = 16384;         // values of a quantized activation
 constexpr int kMaxNormed = 2 * kDW * 32 * 8;  // values of a normed one (4096 at 8 warps)
-constexpr int kMaxStaged = 4096;              // values of a quantize-only activation staged by a bulk copy
+constexpr int kMaxStaged = kMaxActivation;    // values of a quantize-only activation staged by a bulk copy
 
 __device__ __forceinline__ void load8(const float *src, int hc, float (&x)[8], bool cg) {
     const float4 *p = (const float4 *)src + 2 * hc;
@@ -850,7 +850,7 @@ constexpr int kAttnVChunk = 64, kAttnVRing = 8;
 __host__ __device__ inline size_t scores_region(int P, int G, int hd) {
     return ((size_t)P * (hd + 4) + (size_t)G * hd) * sizeof(float);
 }
-// dims: output dims per work item (a multiple of 16 dividing head_dim, at most 256)
+// dims: output dims per work item (16 or 32, dividing head_dim)
 __host__ __device__ inline size_t attn_region(int max_pos, int dims) {
     return ((size_t)((max_pos + 3) & ~3) + (size_t)kAttnVRing * kAttnVChunk * dims) * sizeof(float);
 }
@@ -896,6 +896,36 @@ __device__ void phase_scores(const AtPhase &at, int n, float *region) {
         }
         dsync();
     }
+}
+
+// the sum of p[0..n) added one value after another from 0.0f (one thread):
+// 16 values per step, the next step's loads in flight during this step's adds
+__device__ __forceinline__ float seq_sum(const float *p, int n) {
+    float acc = 0.0f;
+    int i = 0;
+    float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0, n2 = n0, n3 = n0;
+    if (16 <= n) {
+        n0 = ((const float4 *)p)[0];
+        n1 = ((const float4 *)p)[1];
+        n2 = ((const float4 *)p)[2];
+        n3 = ((const float4 *)p)[3];
+    }
+    for (; i + 16 <= n; i += 16) {
+        const float4 q0 = n0, q1 = n1, q2 = n2, q3 = n3;
+        if (i + 32 <= n) {
+            const float4 *c4 = (const float4 *)(p + i + 16);
+            n0 = c4[0];
+            n1 = c4[1];
+            n2 = c4[2];
+            n3 = c4[3];
+        }
+        acc = fa(fa(fa(fa(acc, q0.x), q0.y), q0.z), q0.w);
+        acc = fa(fa(fa(fa(acc, q1.x), q1.y), q1.z), q1.w);
+        acc = fa(fa(fa(fa(acc, q2.x), q2.y), q2.z), q2.w);
+        acc = fa(fa(fa(fa(acc, q3.x), q3.y), q3.z), q3.w);
+    }
+    for (; i < n; i++) acc = fa(acc, p[i]);
+    return acc;
 }
 
 // softmax over a head's scores (subtract the max, exp, sum position by
@@ -950,16 +980,7 @@ __device__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region,
         } else {
             for (int i = tid; i < n; i += nt) pr[i] = expf_glibc(fs(pr[i], mx));
             dsync();
-            if (tid == 0) {
-                float total = 0.0f;
-                int i = 0;
-                for (; i + 4 <= n; i += 4) {
-                    const float4 v = *(const float4 *)(pr + i);
-                    total = fa(fa(fa(fa(total, v.x), v.y), v.z), v.w);
-                }
-                for (; i < n; i++) total = fa(total, pr[i]);
-                *fbc = __fdiv_rn(1.0f, total);
-            }
+            if (tid == 0) *fbc = __fdiv_rn(1.0f, seq_sum(pr, n));
             dsync();
             const float inv = *fbc;
             for (int i = tid; i < n; i += nt) pr[i] = fm(pr[i], inv);

@@ -456,12 +456,12 @@ size_t phase_region(const Phase &ph, int max_pos) {
 // positions per score item: the G query heads of a kv head share its K rows
 int score_positions(int G) { return std::max(1, std::min(64, 256 / std::max(1, G))); }
 
-// Output dims per attention item: the fewest (a multiple of 16 dividing the
-// head) that give at most one item per SM, so every head's softmax and its
-// position-by-position sums run in one round; at least 16.
+// Output dims per attention item: 16, or 32 when that keeps the items at
+// one per SM where 16 would not (every head's softmax and its
+// position-by-position sums in one round). One lane per dim, all in warp 0.
 int attn_dims(int H, int hd, int sms) {
     int d = 16;
-    while (d < hd && (long long)H * (hd / d) > sms && hd % (2 * d) == 0 && 2 * d <= 256) d *= 2;
+    if ((long long)H * (hd / 16) > sms && hd % 32 == 0) d = 32;
     return d;
 }
 
