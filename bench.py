@@ -52,6 +52,13 @@ def ensure_model(config: str, seed: int) -> str:
     return p
 
 
+def workload_of(args) -> str:
+    """The workload label: configs[1]'s, or the named synthetic shape."""
+    if args.config == "qwen3b":
+        return WORKLOAD
+    return f"{args.config}-shape synthetic model, {args.prompt}-token seeded prompt, greedy decode bs=1"
+
+
 def seeded_prompt(seed: int, n: int, vocab: int):
     # uniform token ids from the reference's xorshift64* (src/daiss.rs:317-337)
     st = seed if seed else 0x9E3779B97F4A7C15
@@ -154,7 +161,7 @@ def run_reference(args, rank: int, world: int) -> None:
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1000 / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "prompt": args.prompt, "decode_steps": args.steps},
+        "config": {"workload": workload_of(args), "prompt": args.prompt, "decode_steps": args.steps},
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": O.threads(), "kind": "port",
                          "sample": f"{args.steps} greedy decode tokens per step-set at context {args.prompt} (KV "
                                    f"prefix seeded instead of a CPU prefill); C restatement of the reference's "
@@ -493,7 +500,7 @@ def main() -> None:
         "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "prompt": args.prompt, "decode_steps": args.steps,
+        "config": {"workload": workload_of(args), "prompt": args.prompt, "decode_steps": args.steps,
                    "parallelism": f"dp{world} (independent conversations, replicated weights)",
                    "l2": "inputs larger than L2: 1.92 GB of weights streamed per step vs 126 MB L2"},
         "weight_stream": {"bytes_per_token": wbytes, "gbs_per_gpu": round(value / world * wbytes / 1e9, 1),
