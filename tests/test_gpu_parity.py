@@ -176,6 +176,22 @@ def test_tiny_greedy_64_tokens_identical(tiny_path):
         assert len(c) == len(oc) == 96
 
 
+@pytest.mark.parametrize("t", [cx.Q5_K, cx.Q3_K, cx.Q2_K, cx.Q6_K])
+def test_uniform_format_model_matches_oracle(tmp_path, t):
+    # BASELINE configs[2] re-quantizes the whole model to one format: the
+    # tiny shape so, logits bit-exact and greedy and top-p picks identical
+    p = str(tmp_path / f"tiny_t{t}.gguf")
+    cx.synth_write(p, cx.synth_spec("tiny", seed=5, type=t, tied=1))
+    m, om = cx.Modelo(p), O.Model(p)
+    prompt = prompt_of(3, 24, m.cfg.vocab)
+    np.testing.assert_array_equal(m.forward(prompt, m.cache()), om.forward(om.cache(), prompt))
+    assert m.generar(prompt, 24, cx.Muestreador.voraz(), m.cache()) == \
+        om.generate(om.cache(), prompt, 24, O.Sampler(0, 0.0, 1.0))
+    dev, ref = cx.Muestreador(42, 0.7, 0.9), O.Sampler(42, 0.7, 0.9)
+    assert m.generar(prompt, 24, dev, m.cache()) == om.generate(om.cache(), prompt, 24, ref)
+    assert dev.estado == ref.state
+
+
 def test_cache_prefix_truncate_clear(tiny_path):
     # src/forward.rs:587-603 and src/engine_own.rs:207-245 semantics
     m = cx.Modelo(tiny_path)
