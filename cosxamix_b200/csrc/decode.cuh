@@ -857,7 +857,7 @@ __host__ __device__ inline size_t attn_region(int max_pos, int dims) {
 
 // score[h][p] = (sequential dot of q_h and k_p over the head dim) · scale; an
 // item is one kv head and P positions, shared by the G query heads on it
-__device__ void phase_scores(const AtPhase &at, int n, float *region) {
+__device__ __forceinline__ void phase_scores(const AtPhase &at, int n, float *region) {
     const int tid = threadIdx.x, hd = at.hd, G = at.H / at.KV, kvd = at.KV * hd, c4 = hd / 4;
     // positions per item: enough items for every CTA, at most at.P (the
     // region's capacity)
@@ -932,7 +932,7 @@ __device__ __forceinline__ float seq_sum(const float *p, int n) {
 // position, multiply by 1/total; src/ops.rs:1206-1230), then
 // out[d] = Σ_p prob_p·v_p[d] added position by position; an item is one head
 // and kAttnDims dims
-__device__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region, float *fred, float *fbc) {
+__device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region, float *fred, float *fbc) {
     const int tid = threadIdx.x, nt = kDW * 32, hd = at.hd, G = at.H / at.KV, kvd = at.KV * hd;
     const int dims = at.dims, nslice = hd / dims, items = at.H * nslice;
     float *pr = region;
@@ -1099,7 +1099,10 @@ __device__ __forceinline__ float group_dot(const DecodeArgs &A, Ring &R, int war
 // ── the kernel ──
 __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_constant__ DecodeArgs A) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    unsigned char *smem = (unsigned char *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+    // aligned by an offset from the shared array itself (not a round trip
+    // through an integer), so every pointer derived from it stays a
+    // shared-memory pointer to the compiler
+    unsigned char *smem = smem_raw + ((128u - ((uint32_t)(uintptr_t)smem_raw & 127u)) & 127u);
     const int ns = A.ring_slots;
     unsigned char *region = smem + (size_t)kDW * ns * A.slot_bytes;
     Phase *phbuf = (Phase *)(region + A.region_bytes);  // two staged phase descriptors

@@ -74,7 +74,7 @@ __device__ __forceinline__ int hidx(int d, int w) { return w * kHistRow + d; }
 
 // one stable counting pass of an LSD radix sort on 8 key bits; a warp owns a
 // contiguous chunk and keeps its elements' order
-__device__ void radix_pass(const uint32_t *kin, const uint32_t *vin, uint32_t *kout, uint32_t *vout, int n, int shift,
+__device__ __forceinline__ void radix_pass(const uint32_t *kin, const uint32_t *vin, uint32_t *kout, uint32_t *vout, int n, int shift,
                            uint32_t *hist /* [kSampWarps][kHistRow] */) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int chunk = (n + kSampWarps - 1) / kSampWarps;
@@ -168,7 +168,7 @@ constexpr int kScanChunk = 8192;  // floats per shared-memory stage of a sequent
 // dst[i] when dst is set and stopping after the first i with sum >= stop when
 // use_stop. The other threads stage the next chunk of src into shared memory
 // meanwhile. Returns the number of terms added (uniform).
-__device__ int seq_scan(const float *src, int len, float *dst, bool use_stop, float stop, float *stage,
+__device__ __forceinline__ int seq_scan(const float *src, int len, float *dst, bool use_stop, float stop, float *stage,
                         float *sum_out, int *flag) {
     const int tid = threadIdx.x;
     float acc = 0.0f;
