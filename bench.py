@@ -2,11 +2,18 @@
 synthetic model through the C ABI.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+                    [--config tiny|qwen3b|...] [--workload decode|formats|shared-prefix|tp]
 
 One process per GPU (torchrun for N > 1). Every rank decodes its own
 conversation with replicated weights — independent conversations, no
 collective on the data path — so `value` is the sum over ranks (weak scaling).
 A step is one decode token: the forward of one token plus the greedy pick.
+
+The other workloads (each prints its own one-line JSON): `formats`
+(configs[2]: the 3B shape uniform in Q5_K, Q3_K, Q2_K, sampled decode),
+`shared-prefix` (configs[3]: 64 conversations sharded over the ranks, one
+shared 1024-token prefix prefilled once per GPU), `tp` (configs[4]: one
+Llama-3-8B-shaped conversation, tensor-parallel over the ranks).
 """
 from __future__ import annotations
 

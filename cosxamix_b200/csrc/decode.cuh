@@ -13,15 +13,20 @@
 // copies into a private shared-memory ring that runs ahead across phase
 // boundaries — while the warps sit in barriers, prologues or attention. (Many
 // small 1-D bulk copies from one thread per SM top out near 4.3 TB/s on B200;
-// warp-wide 16-byte copies stream at over 7.) A prologue's inputs (the
-// activation and the norm weights) come in as two 1-D bulk copies.
+// warp-wide 16-byte copies stream at over 7.) A normed prologue loads its
+// activation through L2 into registers, its norm weights before the barrier;
+// a quantize-only prologue stages its activation with one 1-D bulk copy.
+// With tensor parallelism, exchange phases add the ranks' partial sums of
+// o_proj / ffn_down and pick the argmax over the ranks' vocabulary slices,
+// over peer memory.
 //
 // Weights are stored as tiles of R rows x LPR super-blocks (R*LPR = 32: one
 // warp's lanes, lane = R*block + row), lane-interleaved in 16-byte chunks so
 // the 32 lanes read consecutive 16-byte words. LPR ("lanes per row") is
-// chosen per matrix: 1 for the tall matrices (a lane owns a row and adds its
-// terms as it forms them), up to 32 for the short ones, whose rows would
-// otherwise leave most warps idle. A warp owns a group of R rows at a time:
+// chosen per matrix: the fewest lanes for which the phase's row groups split
+// evenly over the warps, more for the short matrices, whose rows would
+// otherwise leave most warps idle (at most 16, so a tile holds both rows of
+// an output pair). A warp owns a group of R rows at a time:
 // lane (block, row) forms that super-block's sub-block terms, and each row's
 // running total visits the blocks in order, handed from lane to lane (the
 // reference's sequential sum, src/ops.rs:435-522 with
@@ -931,7 +936,7 @@ __device__ __forceinline__ float seq_sum(const float *p, int n) {
 // softmax over a head's scores (subtract the max, exp, sum position by
 // position, multiply by 1/total; src/ops.rs:1206-1230), then
 // out[d] = Σ_p prob_p·v_p[d] added position by position; an item is one head
-// and kAttnDims dims
+// and `dims` of its output dims (16 or 32)
 __device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region, float *fred, float *fbc) {
     const int tid = threadIdx.x, nt = kDW * 32, hd = at.hd, G = at.H / at.KV, kvd = at.KV * hd;
     const int dims = at.dims, nslice = hd / dims, items = at.H * nslice;
