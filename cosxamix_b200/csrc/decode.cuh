@@ -850,14 +850,18 @@ __device__ void phase_xargmax(const DecodeArgs &A, unsigned ep, volatile int *ab
 }
 
 // ── attention phases (src/ops.rs:1258-1325), reference order ──
-constexpr int kAttnVChunk = 64, kAttnVRing = 8;
+// the attention phase's V ring: 8 chunks of 2048 floats (128 positions at
+// 16 dims per item, 64 at 32)
+constexpr int kAttnVRing = 8, kAttnVChunkFloats = 2048;
+__host__ __device__ inline int attn_chunk(int dims) { return kAttnVChunkFloats / dims; }
 
 __host__ __device__ inline size_t scores_region(int P, int G, int hd) {
     return ((size_t)P * (hd + 4) + (size_t)G * hd) * sizeof(float);
 }
 // dims: output dims per work item (16 or 32, dividing head_dim)
 __host__ __device__ inline size_t attn_region(int max_pos, int dims) {
-    return ((size_t)((max_pos + 3) & ~3) + (size_t)kAttnVRing * kAttnVChunk * dims) * sizeof(float);
+    (void)dims;
+    return ((size_t)((max_pos + 3) & ~3) + (size_t)kAttnVRing * kAttnVChunkFloats) * sizeof(float);
 }
 
 // score[h][p] = (sequential dot of q_h and k_p over the head dim) · scale; an
@@ -939,18 +943,18 @@ __device__ __forceinline__ float seq_sum(const float *p, int n) {
 // and `dims` of its output dims (16 or 32)
 __device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region, float *fred, float *fbc) {
     const int tid = threadIdx.x, nt = kDW * 32, hd = at.hd, G = at.H / at.KV, kvd = at.KV * hd;
-    const int dims = at.dims, nslice = hd / dims, items = at.H * nslice;
+    const int dims = at.dims, nslice = hd / dims, items = at.H * nslice, cpos = attn_chunk(dims);
     float *pr = region;
     float *vs = region + ((max_pos + 3) & ~3);
-    const int nchunks = (n + kAttnVChunk - 1) / kAttnVChunk;
+    const int nchunks = (n + cpos - 1) / cpos;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int h = item / nslice, d0 = (item % nslice) * dims, g = h / G;
         const float *sc = at.scores + (size_t)h * at.score_stride;
         const float *vb = at.v + (size_t)g * hd + d0;
         auto stage = [&](int c) {
             if (c >= nchunks) return;
-            const int base = c * kAttnVChunk, cnt = min(kAttnVChunk, n - base);
-            float *dst = vs + (c % kAttnVRing) * kAttnVChunk * dims;
+            const int base = c * cpos, cnt = min(cpos, n - base);
+            float *dst = vs + (c % kAttnVRing) * cpos * dims;
             const int d4 = dims / 4;
             for (int i = tid; i < cnt * d4; i += nt) {
                 const int r = i / d4, q = i - r * d4;
@@ -998,10 +1002,42 @@ __device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos
             cp_async_wait<kAttnVRing - 1>();
             dsync();
             if (tid < dims) {
-                const float *src = vs + (c % kAttnVRing) * kAttnVChunk * dims + tid;
-                const int base = c * kAttnVChunk, cnt = min(kAttnVChunk, n - base);
-#pragma unroll 8
-                for (int r = 0; r < cnt; r++) acc = fa(acc, fm(pr[base + r], src[r * dims]));
+                // 16 positions per step, the next step's probabilities and V
+                // values loaded while this step's products are added in order
+                const float *src = vs + (c % kAttnVRing) * cpos * dims + tid;
+                const int base = c * cpos, cnt = min(cpos, n - base);
+                const float *pp = pr + base;
+                float np[16], nv[16];
+                if (16 <= cnt) {
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const float4 q = ((const float4 *)pp)[k];
+                        np[4 * k] = q.x; np[4 * k + 1] = q.y; np[4 * k + 2] = q.z; np[4 * k + 3] = q.w;
+                    }
+#pragma unroll
+                    for (int k = 0; k < 16; k++) nv[k] = src[k * dims];
+                }
+                int r = 0;
+                for (; r + 16 <= cnt; r += 16) {
+                    float cp[16], cv[16];
+#pragma unroll
+                    for (int k = 0; k < 16; k++) {
+                        cp[k] = np[k];
+                        cv[k] = nv[k];
+                    }
+                    if (r + 32 <= cnt) {
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            const float4 q = ((const float4 *)(pp + r + 16))[k];
+                            np[4 * k] = q.x; np[4 * k + 1] = q.y; np[4 * k + 2] = q.z; np[4 * k + 3] = q.w;
+                        }
+#pragma unroll
+                        for (int k = 0; k < 16; k++) nv[k] = src[(r + 16 + k) * dims];
+                    }
+#pragma unroll
+                    for (int k = 0; k < 16; k++) acc = fa(acc, fm(cp[k], cv[k]));
+                }
+                for (; r < cnt; r++) acc = fa(acc, fm(pp[r], src[r * dims]));
             }
             dsync();
         }
