@@ -100,3 +100,32 @@ def test_two_gloo_ranks_exchange_handles_and_gather_logits():
     for rank, handles, full in res:
         assert handles == [bytes([1]) * 64, bytes([2]) * 64]  # rank order, own included
         assert full == [0.5 * i for i in range(10)]
+
+
+def test_oracle_tp_emulation_is_deterministic_and_bounded(tmp_path):
+    # the oracle's emulation of N ranks (o_proj / ffn_down as N K-slice
+    # partial sums added in rank order), which the GPU's tensor-parallel
+    # path matches bit for bit: repeatable, 1 rank = the reference exactly,
+    # and within the bound the GPU test uses against the single-rank order
+    import cosxamix_b200 as cx
+    from cosxamix_b200 import serving
+    from oracle import oracle as O
+    p = str(tmp_path / "tp_small.gguf")
+    cx.synth_write(p, cx.synth_spec("tp_small", seed=11, n_layer=2))
+    m = O.Model(p)
+    prompt = serving.seeded_tokens(5, 16, 8192)
+    try:
+        ref = m.forward(O.Cache(m), prompt)
+        out = {}
+        for n in (2, 4):
+            O.set_tp(n)
+            a, b = m.forward(O.Cache(m), prompt), m.forward(O.Cache(m), prompt)
+            np.testing.assert_array_equal(a, b)
+            out[n] = a
+        O.set_tp(1)
+        np.testing.assert_array_equal(m.forward(O.Cache(m), prompt), ref)
+        for n, a in out.items():
+            assert not np.array_equal(a, ref)  # the split rounds differently
+            assert float(np.max(np.abs(a - ref)) / (ref.max() - ref.min())) <= 2e-2
+    finally:
+        O.set_tp(1)
