@@ -118,12 +118,31 @@ class Clocks:
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax, "reasons": reasons, "samples": len(rows)}
 
 
+def reference_cpu_path() -> tuple:
+    """Put the oracle on the kernels the reference runs on an AVX2 host and
+    describe them: (kind, text). The Q4_K/Q5_K/Q3_K/Q2_K rows go through the
+    reference's own compiled kernels when oracle/_ref was built (the kernel
+    whose speed decides the baseline is then the reference's code), Q6_K,
+    RMSNorm and attention's dot products through AVX2 restatements of
+    src/kernels/x86.rs; the loop around them is the C restatement of
+    src/forward.rs:375-505 on a persistent thread pool (32-row tasks, as
+    src/ops.rs:486-506)."""
+    from oracle import oracle as O
+    used = O.set_backend("x86")
+    names = {O.Q4K: "Q4_K", O.Q6K: "Q6_K", O.Q5K: "Q5_K", O.Q3K: "Q3_K", O.Q2K: "Q2_K"}
+    kernels = ", ".join(f"{names[t]}: {used[t]}" for t in (O.Q4K, O.Q6K))
+    return "port", (f"C restatement of the reference's engine_own decode on its x86 AVX2 path ({kernels}; "
+                    f"RMSNorm and attention dots: AVX2 restatements of x86.rs), reference Rust not buildable here")
+
+
 def cpu_baseline(path: str, prompt_len: int, budget_s: float, threads: int = 0) -> dict:
-    """The oracle (C restatement of the reference's engine_own decode) on the
-    host cores: decode tokens at context `prompt_len` for about `budget_s`."""
+    """The reference's decode on the host cores (its C restatement on the
+    reference's x86 kernels, reference_cpu_path): decode tokens at context
+    `prompt_len` for about `budget_s`."""
     from oracle import oracle as O
     if threads:
         O.set_threads(threads)
+    kind, text = reference_cpu_path()
     m = O.Model(path)
     c = m.cache()
     c.fill(prompt_len, seed=1)
@@ -137,19 +156,21 @@ def cpu_baseline(path: str, prompt_len: int, budget_s: float, threads: int = 0) 
         tok = int(O.lib().orc_argmax(O.ptr(logits), logits.size))
         logits = m.forward(c, [tok])
     dt = time.perf_counter() - t0
-    return {"value": n / dt, "unit": "tok/s", "cores": O.threads(), "kind": "port",
+    O.set_backend("scalar")
+    return {"value": n / dt, "unit": "tok/s", "cores": O.threads(), "kind": kind,
             "sample": f"{n} greedy decode tokens at context {prompt_len}..{prompt_len + n} "
-                      f"(KV prefix filled with seeded values instead of a CPU prefill), C restatement of the "
-                      f"reference's engine_own path (reference Rust not buildable here)"}
+                      f"(KV prefix filled with seeded values instead of a CPU prefill); {text}"}
 
 
 def run_reference(args, rank: int, world: int) -> None:
     """`--impl reference`: the reference's CPU implementation of the path
-    (its C restatement, oracle/), timed on this box's host cores."""
+    (its C restatement on the reference's x86 kernels, reference_cpu_path),
+    timed on this box's host cores."""
     if rank != 0:
         return
     path = ensure_model(args.config, args.seed)
     from oracle import oracle as O
+    kind, text = reference_cpu_path()
     m = O.Model(path)
     c = m.cache()
     c.fill(args.prompt, seed=1)
@@ -169,10 +190,9 @@ def run_reference(args, rank: int, world: int) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1000 / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
         "config": {"workload": workload_of(args), "prompt": args.prompt, "decode_steps": args.steps},
-        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": O.threads(), "kind": "port",
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": O.threads(), "kind": kind,
                          "sample": f"{args.steps} greedy decode tokens per step-set at context {args.prompt} (KV "
-                                   f"prefix seeded instead of a CPU prefill); C restatement of the reference's "
-                                   f"engine_own decode, all host threads (reference Rust not buildable here)"},
+                                   f"prefix seeded instead of a CPU prefill), all host threads; {text}"},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -27,7 +27,9 @@
 #include <string.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
+#include <time.h>
 #include <unistd.h>
+#include <immintrin.h>
 
 /* ───────────────────────── errors ───────────────────────── */
 
@@ -52,6 +54,19 @@ void orc_set_threads(int n) { g_threads = n; }
  * residual. Every other projection splits by rows, which changes no value. */
 static int g_tp = 1;
 void orc_set_tp(int n) { g_tp = n > 0 ? n : 1; }
+
+/* Kernel backend of orc_forward (cxm_oracle.h). */
+static int g_backend = ORC_BACKEND_SCALAR;
+static orc_dot_fn g_dot_kernel[16];
+static orc_q4k_acc_fn g_q4k_acc;
+void orc_set_backend(int b) { g_backend = b == ORC_BACKEND_X86 ? ORC_BACKEND_X86 : ORC_BACKEND_SCALAR; }
+int orc_get_backend(void) { return g_backend; }
+int orc_set_dot_kernel(int type, orc_dot_fn f) {
+    if (type < 0 || type >= 16) return -1;
+    g_dot_kernel[type] = f;
+    return 0;
+}
+void orc_set_q4k_acc_kernel(orc_q4k_acc_fn f) { g_q4k_acc = f; }
 int orc_get_threads(void) {
     if (g_threads > 0) return g_threads;
     long n = sysconf(_SC_NPROCESSORS_ONLN);
@@ -59,26 +74,99 @@ int orc_get_threads(void) {
 }
 
 typedef void (*task_fn)(void *ctx, size_t begin, size_t end);
-typedef struct {
+
+/* A persistent pool, as rayon's: the workers outlive each call, spin for a
+ * short while after a job (back-to-back matmuls find them awake) and then
+ * sleep on a condition variable. One job at a time; callers on other threads
+ * queue on `call_mu`. Chunks are claimed with an atomic counter. */
+#define POOL_MAX 256
+#define POOL_SPIN_NS 200000L
+static struct {
+    pthread_mutex_t call_mu, mu;
+    pthread_cond_t go, done;
+    pthread_t th[POOL_MAX];
+    int nworkers, quit;
+    unsigned long gen;      /* bumped once per job */
+    int pending;            /* workers that have not yet finished the current job */
     task_fn fn;
     void *ctx;
-    size_t n, chunk;
-    size_t next;
-    pthread_mutex_t mu;
-} par_state;
+    size_t n, chunk, next;
+} g_pool = {PTHREAD_MUTEX_INITIALIZER, PTHREAD_MUTEX_INITIALIZER, PTHREAD_COND_INITIALIZER,
+            PTHREAD_COND_INITIALIZER};
 
-static void *par_worker(void *arg) {
-    par_state *st = (par_state *)arg;
+static long now_ns(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1000000000L + ts.tv_nsec;
+}
+
+static void pool_run_chunks(void) {
     for (;;) {
-        pthread_mutex_lock(&st->mu);
-        size_t b = st->next;
-        st->next += st->chunk;
-        pthread_mutex_unlock(&st->mu);
-        if (b >= st->n) break;
-        size_t e = b + st->chunk < st->n ? b + st->chunk : st->n;
-        st->fn(st->ctx, b, e);
+        size_t b = __atomic_fetch_add(&g_pool.next, g_pool.chunk, __ATOMIC_RELAXED);
+        if (b >= g_pool.n) break;
+        size_t e = b + g_pool.chunk < g_pool.n ? b + g_pool.chunk : g_pool.n;
+        g_pool.fn(g_pool.ctx, b, e);
     }
-    return NULL;
+}
+
+static void *pool_worker(void *arg) {
+    unsigned long seen = (unsigned long)(uintptr_t)arg;
+    for (;;) {
+        long t0 = now_ns();
+        while (__atomic_load_n(&g_pool.gen, __ATOMIC_ACQUIRE) == seen && !__atomic_load_n(&g_pool.quit, __ATOMIC_ACQUIRE) &&
+               now_ns() - t0 < POOL_SPIN_NS)
+            __builtin_ia32_pause();
+        pthread_mutex_lock(&g_pool.mu);
+        while (g_pool.gen == seen && !g_pool.quit) pthread_cond_wait(&g_pool.go, &g_pool.mu);
+        if (g_pool.quit) {
+            pthread_mutex_unlock(&g_pool.mu);
+            return NULL;
+        }
+        seen = g_pool.gen;
+        pthread_mutex_unlock(&g_pool.mu);
+        pool_run_chunks();
+        if (__atomic_sub_fetch(&g_pool.pending, 1, __ATOMIC_ACQ_REL) == 0) {
+            pthread_mutex_lock(&g_pool.mu);
+            pthread_cond_signal(&g_pool.done);
+            pthread_mutex_unlock(&g_pool.mu);
+        }
+    }
+}
+
+static void pool_stop(void) {
+    if (g_pool.nworkers == 0) return;
+    pthread_mutex_lock(&g_pool.mu);
+    __atomic_store_n(&g_pool.quit, 1, __ATOMIC_RELEASE);
+    pthread_cond_broadcast(&g_pool.go);
+    pthread_mutex_unlock(&g_pool.mu);
+    for (int i = 0; i < g_pool.nworkers; i++) pthread_join(g_pool.th[i], NULL);
+    g_pool.nworkers = 0;
+    g_pool.quit = 0;
+}
+
+/* A forked child has only the calling thread: forget the parent's workers. */
+static void pool_after_fork(void) {
+    pthread_mutex_init(&g_pool.call_mu, NULL);
+    pthread_mutex_init(&g_pool.mu, NULL);
+    pthread_cond_init(&g_pool.go, NULL);
+    pthread_cond_init(&g_pool.done, NULL);
+    g_pool.nworkers = 0;
+    g_pool.quit = 0;
+}
+
+static void pool_register_fork(void) { pthread_atfork(NULL, NULL, pool_after_fork); }
+
+/* (Re)start the pool with `workers` threads besides the caller's. Called with
+ * call_mu held. */
+static void pool_resize(int workers) {
+    static pthread_once_t once = PTHREAD_ONCE_INIT;
+    pthread_once(&once, pool_register_fork);
+    if (workers == g_pool.nworkers) return;
+    pool_stop();
+    for (int i = 0; i < workers; i++) {
+        if (pthread_create(&g_pool.th[i], NULL, pool_worker, (void *)(uintptr_t)g_pool.gen) != 0) break;
+        g_pool.nworkers = i + 1;
+    }
 }
 
 /* Work split in chunks of `chunk` items, like rayon's par_chunks_mut over
@@ -89,14 +177,32 @@ static void par_for(size_t n, size_t chunk, task_fn fn, void *ctx) {
         fn(ctx, 0, n);
         return;
     }
-    size_t tasks = (n + chunk - 1) / chunk;
-    if ((size_t)t > tasks) t = (int)tasks;
-    par_state st = {fn, ctx, n, chunk, 0, PTHREAD_MUTEX_INITIALIZER};
-    pthread_t th[256];
-    if (t > 256) t = 256;
-    for (int i = 1; i < t; i++) pthread_create(&th[i], NULL, par_worker, &st);
-    par_worker(&st);
-    for (int i = 1; i < t; i++) pthread_join(th[i], NULL);
+    if (t > POOL_MAX) t = POOL_MAX;
+    pthread_mutex_lock(&g_pool.call_mu);
+    pool_resize(t - 1);
+    if (g_pool.nworkers == 0) {
+        pthread_mutex_unlock(&g_pool.call_mu);
+        fn(ctx, 0, n);
+        return;
+    }
+    pthread_mutex_lock(&g_pool.mu);
+    g_pool.fn = fn;
+    g_pool.ctx = ctx;
+    g_pool.n = n;
+    g_pool.chunk = chunk;
+    g_pool.next = 0;
+    g_pool.pending = g_pool.nworkers;
+    __atomic_store_n(&g_pool.gen, g_pool.gen + 1, __ATOMIC_RELEASE);
+    pthread_cond_broadcast(&g_pool.go);
+    pthread_mutex_unlock(&g_pool.mu);
+    pool_run_chunks();
+    long t0 = now_ns();
+    while (__atomic_load_n(&g_pool.pending, __ATOMIC_ACQUIRE) != 0 && now_ns() - t0 < POOL_SPIN_NS)
+        __builtin_ia32_pause();
+    pthread_mutex_lock(&g_pool.mu);
+    while (__atomic_load_n(&g_pool.pending, __ATOMIC_ACQUIRE) != 0) pthread_cond_wait(&g_pool.done, &g_pool.mu);
+    pthread_mutex_unlock(&g_pool.mu);
+    pthread_mutex_unlock(&g_pool.call_mu);
 }
 
 /* ───────────────────────── formats ───────────────────────── */
@@ -817,6 +923,25 @@ float orc_dot_row(int type, const uint8_t *row, const int8_t *xq, const float *x
     }
 }
 
+/* What the reference's dispatch (src/kernels/mod.rs:347-509) runs on an AVX2
+ * host: a registered kernel of the reference's own where one was given, else
+ * the AVX2 restatement (Q4_K, Q6_K), else the scalar restatement. */
+float orc_x86_dot_row(int type, const uint8_t *row, const int8_t *xq, const float *xe, const float *xs, size_t nblk) {
+    if (type >= 0 && type < 16 && g_dot_kernel[type]) return g_dot_kernel[type](row, xq, xe, xs, nblk);
+    switch (type) {
+    case ORC_Q4K:
+        if (g_q4k_acc) {
+            /* the kernel adds into the accumulators; its caller zeroes them */
+            float acc[16] = {0};
+            g_q4k_acc(row, xq, xe, xs, nblk, acc);
+            return orc_x86_reduce_q4k_acc(acc);
+        }
+        return orc_x86_dot_q4k(row, xq, xe, xs, nblk);
+    case ORC_Q6K: return orc_x86_dot_q6k(row, xq, xe, xs, nblk);
+    default: return orc_dot_row(type, row, xq, xe, xs, nblk);
+    }
+}
+
 /* ───────────────────────── elementwise ops ───────────────────────── */
 
 /* src/kernels/scalar.rs:36-54 — the sum of squares in f64 */
@@ -897,12 +1022,14 @@ int orc_attention(const float *q, const float *k, const float *v, int tokens, in
     float scale = 1.0f / sqrtf((float)hd);
     int offset = total - tokens;
     float *pts = (float *)malloc(sizeof(float) * (size_t)(total > 0 ? total : 1));
+    /* kernels::dot is the AVX2 one on an AVX2 host (src/kernels/mod.rs:240-262) */
+    float (*dotf)(const float *, const float *, size_t) = g_backend == ORC_BACKEND_X86 ? orc_x86_dot_f32 : orc_dot_f32;
     for (int t = 0; t < tokens; t++) {
         int vis = offset + t + 1;
         for (int h = 0; h < heads; h++) {
             const float *qh = q + (size_t)t * wq + (size_t)h * hd;
             int base = (h / per) * hd;
-            for (int p = 0; p < vis; p++) pts[p] = orc_dot_f32(qh, k + (size_t)p * wkv + base, (size_t)hd) * scale;
+            for (int p = 0; p < vis; p++) pts[p] = dotf(qh, k + (size_t)p * wkv + base, (size_t)hd) * scale;
             orc_softmax(pts, (size_t)vis, (size_t)vis);
             float *dst = out + (size_t)t * wq + (size_t)h * hd;
             for (int d = 0; d < hd; d++) dst[d] = 0.0f;
@@ -930,6 +1057,19 @@ typedef struct {
 static void mm_task(void *c_, size_t b, size_t e) {
     mm_ctx *c = (mm_ctx *)c_;
     size_t nsub = (size_t)c->k / (size_t)c->sub;
+    if (g_backend == ORC_BACKEND_X86) {
+        /* src/ops.rs:486-506: the row two ahead is prefetched line by line
+         * (:45-80) while this one is computed */
+        for (size_t col = b; col < e; col++) {
+            const uint8_t *row = c->w + col * c->row_bytes;
+            if (col + 2 < e)
+                for (size_t o = 0; o < c->row_bytes; o += 64) _mm_prefetch((const char *)(row + 2 * c->row_bytes + o), _MM_HINT_T0);
+            for (int f = 0; f < c->m; f++)
+                c->dst[(size_t)f * c->n + col] = orc_x86_dot_row(c->type, row, c->xq + (size_t)f * c->k,
+                                                                 c->xe + f * nsub, c->xs + f * nsub, c->nblk);
+        }
+        return;
+    }
     for (size_t col = b; col < e; col++) {
         const uint8_t *row = c->w + col * c->row_bytes;
         for (int f = 0; f < c->m; f++)
@@ -1431,6 +1571,9 @@ static int read_vec(orc_model *m, const orc_tensor *t, float *dst, size_t n) {
 int orc_forward(orc_model *m, orc_cache *c, const uint32_t *tokens, int t, float *logits) {
     const orc_config *cfg = &m->cfg;
     if (t <= 0) { set_err("no tokens to process"); return -1; }
+    /* kernels::rmsnorm is the f32 AVX2 one on an AVX2 host (src/kernels/mod.rs:511) */
+    void (*norm)(float *, const float *, const float *, size_t, float) =
+        g_backend == ORC_BACKEND_X86 ? orc_x86_rmsnorm : orc_rmsnorm;
     int total = c->len + t;
     if (total > cfg->ctx) { set_err("%d tokens exceed the context of %d", total, cfg->ctx); return -1; }
     int D = cfg->dim, hd = cfg->head_dim, H = cfg->n_head, KV = cfg->n_head_kv, F = cfg->ffn;
@@ -1460,7 +1603,7 @@ int orc_forward(orc_model *m, orc_cache *c, const uint32_t *tokens, int t, float
     for (int l = 0; l < cfg->n_layer; l++) {
         const orc_layer *L = &m->layers[l];
         read_vec(m, L->attn_norm, w, (size_t)D);
-        for (int i = 0; i < t; i++) orc_rmsnorm(xn + (size_t)i * D, x + (size_t)i * D, w, (size_t)D, cfg->eps);
+        for (int i = 0; i < t; i++) norm(xn + (size_t)i * D, x + (size_t)i * D, w, (size_t)D, cfg->eps);
         if (project(m, xn, t, L->q, L->qb, q) || project(m, xn, t, L->k, L->kb, kk) || project(m, xn, t, L->v, L->vb, vv)) goto done;
         orc_rope(q, t, H, hd, m->cos_t, m->sin_t, cfg->ctx, c->len);
         orc_rope(kk, t, KV, hd, m->cos_t, m->sin_t, cfg->ctx, c->len);
@@ -1470,7 +1613,7 @@ int orc_forward(orc_model *m, orc_cache *c, const uint32_t *tokens, int t, float
         if (project_split(m, att, t, L->o, proj, g_tp)) goto done;
         for (size_t i = 0; i < T * D; i++) x[i] += proj[i];
         read_vec(m, L->ffn_norm, w, (size_t)D);
-        for (int i = 0; i < t; i++) orc_rmsnorm(xn + (size_t)i * D, x + (size_t)i * D, w, (size_t)D, cfg->eps);
+        for (int i = 0; i < t; i++) norm(xn + (size_t)i * D, x + (size_t)i * D, w, (size_t)D, cfg->eps);
         if (project(m, xn, t, L->gate, NULL, gate) || project(m, xn, t, L->up, NULL, up)) goto done;
         orc_silu(act, gate, T * F);
         for (size_t i = 0; i < T * F; i++) act[i] *= up[i];
@@ -1478,7 +1621,7 @@ int orc_forward(orc_model *m, orc_cache *c, const uint32_t *tokens, int t, float
         for (size_t i = 0; i < T * D; i++) x[i] += proj[i];
     }
     read_vec(m, m->out_norm, w, (size_t)D);
-    orc_rmsnorm(xn, x + (size_t)(t - 1) * D, w, (size_t)D, cfg->eps);
+    norm(xn, x + (size_t)(t - 1) * D, w, (size_t)D, cfg->eps);
     if (project(m, xn, 1, m->out, NULL, logits)) goto done;
     c->len = total;
     rc = 0;

@@ -121,8 +121,41 @@ int orc_generate(orc_model *m, orc_cache *c, const uint32_t *prompt, int n_promp
 void orc_cache_fill(orc_cache *c, int n, uint64_t seed);
 void orc_expf(const float *x, float *y, size_t n);
 
+/* worker threads of the row-parallel matmul (0 = one per online CPU); the
+ * workers persist between calls, like the reference's rayon pool */
 void orc_set_threads(int n);
 int  orc_get_threads(void);
+
+/* Backend of orc_forward's kernels. SCALAR (the default) is the parity
+ * restatement above. X86 runs what the reference runs on an AVX2/FMA/F16C
+ * host (src/kernels/mod.rs:136-163): the AVX2 kernels below for Q4_K, Q6_K,
+ * RMSNorm and attention's dot products, a registered reference kernel where
+ * one is given, and a prefetch of the row two ahead (src/ops.rs:45-80). It
+ * exists to time the CPU baseline at the reference's speed; its logits differ
+ * from SCALAR's in float summation order only. */
+enum { ORC_BACKEND_SCALAR = 0, ORC_BACKEND_X86 = 1 };
+void orc_set_backend(int backend);
+int  orc_get_backend(void);
+
+/* the reference's kernel ABI (src/kernels/c.rs:18-30) */
+typedef float (*orc_dot_fn)(const uint8_t *blocks, const int8_t *xq, const float *xe, const float *xs,
+                            size_t n_superblocks);
+/* the reference's Q4_K assembly with the "complete" contract: two 8-float
+ * accumulators out (src/kernels/q4k_asm.rs:214-235) */
+typedef void (*orc_q4k_acc_fn)(const uint8_t *blocks, const int8_t *xq, const float *xe, const float *xs,
+                               size_t n_superblocks, float *acc16);
+/* use `f` for `type` under the X86 backend (NULL: the built-in choice) */
+int  orc_set_dot_kernel(int type, orc_dot_fn f);
+void orc_set_q4k_acc_kernel(orc_q4k_acc_fn f);
+
+/* AVX2 restatements, src/kernels/x86.rs (cxm_x86.c) */
+float orc_x86_dot_f32(const float *a, const float *b, size_t n);                              /* x86.rs:25-128 */
+void  orc_x86_rmsnorm(float *out, const float *in, const float *w, size_t n, float eps);      /* x86.rs:152-213 */
+float orc_x86_dot_q4k(const uint8_t *row, const int8_t *xq, const float *xe, const float *xs, size_t nblk); /* :394-558 */
+float orc_x86_dot_q6k(const uint8_t *row, const int8_t *xq, const float *xe, const float *xs, size_t nblk); /* :760-846 */
+float orc_x86_reduce_q4k_acc(const float *acc16);                                             /* q4k_asm.rs:214-235 */
+/* one row through the X86 backend's choice for `type` */
+float orc_x86_dot_row(int type, const uint8_t *row, const int8_t *xq, const float *xe, const float *xs, size_t nblk);
 /* test infrastructure: emulate n tensor-parallel ranks (o_proj and ffn_down
  * as n K-slice partial sums added in rank order); 1 = the reference */
 void orc_set_tp(int n);

@@ -85,6 +85,15 @@ def _declare(L: C.CDLL) -> None:
         "orc_set_threads": (None, [C.c_int]),
         "orc_set_tp": (None, [C.c_int]),
         "orc_get_threads": (C.c_int, []),
+        "orc_set_backend": (None, [C.c_int]),
+        "orc_get_backend": (C.c_int, []),
+        "orc_set_dot_kernel": (C.c_int, [C.c_int, P]),
+        "orc_set_q4k_acc_kernel": (None, [P]),
+        "orc_x86_dot_f32": (C.c_float, [P, P, C.c_size_t]),
+        "orc_x86_rmsnorm": (None, [P, P, P, C.c_size_t, C.c_float]),
+        "orc_x86_dot_q4k": (C.c_float, [P, P, P, P, C.c_size_t]),
+        "orc_x86_dot_q6k": (C.c_float, [P, P, P, P, C.c_size_t]),
+        "orc_x86_dot_row": (C.c_float, [C.c_int, P, P, P, P, C.c_size_t]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -323,6 +332,47 @@ def set_tp(n: int) -> None:
 
 def threads() -> int:
     return lib().orc_get_threads()
+
+
+SCALAR, X86 = 0, 1
+# the reference's own compiled kernels (oracle/_ref) the X86 backend takes when
+# they were built: GGML type -> (symbol, "dot" = kernel ABI | "acc" = 16 floats out)
+REF_KERNELS = {Q4K: ("cosxamix_q4k_completo", "acc"), Q5K: ("cosxamix_q5k_asm", "dot"),
+               Q3K: ("cosxamix_q3k_completo", "dot"), Q2K: ("cosxamix_q2k_asm", "dot")}
+
+
+def set_backend(name: str, reference_kernels: bool = True) -> dict:
+    """Kernel backend of Model.forward: "scalar" (the parity restatement, the
+    default) or "x86" (what the reference runs on an AVX2/FMA/F16C host; for
+    timing only). With `reference_kernels`, "x86" runs the reference's own
+    compiled kernels of oracle/_ref where they were built. Returns, per GGML
+    type, the kernel in use."""
+    L = lib()
+    for t in range(16):
+        L.orc_set_dot_kernel(t, None)
+    L.orc_set_q4k_acc_kernel(None)
+    if name == "scalar":
+        L.orc_set_backend(SCALAR)
+        return {t: "scalar restatement" for t in (Q2K, Q3K, Q4K, Q5K, Q6K)}
+    if name != "x86":
+        raise ValueError(f"unknown backend {name!r}")
+    L.orc_set_backend(X86)
+    used = {Q4K: "AVX2 restatement (x86.rs)", Q6K: "AVX2 restatement (x86.rs)",
+            Q5K: "scalar restatement", Q3K: "scalar restatement", Q2K: "scalar restatement"}
+    R = ref_lib() if reference_kernels else None
+    if R is not None:
+        for t, (sym, abi) in REF_KERNELS.items():
+            addr = C.cast(getattr(R, sym), C.c_void_p).value
+            if abi == "acc":
+                L.orc_set_q4k_acc_kernel(addr)
+            else:
+                L.orc_set_dot_kernel(t, addr)
+            used[t] = f"reference {sym}"
+    return used
+
+
+def backend() -> str:
+    return "x86" if lib().orc_get_backend() == X86 else "scalar"
 
 
 # ───────────── the reference's own kernels (oracle/_ref) ─────────────
