@@ -108,6 +108,7 @@ struct Program {
 
 struct cxm_cache {
     cxm_model *m = nullptr;
+    int device = -1;                   // the model's, kept so freeing never reads the model
     uint32_t max_tokens = 0, len = 0;
     float *k = nullptr, *v = nullptr;  // [n_layer][max_tokens][kvd]
     uint32_t *toks = nullptr;          // [max_tokens + 2]
@@ -115,7 +116,7 @@ struct cxm_cache {
     Program prog[4];
     cudaGraphExec_t graph[4] = {nullptr, nullptr, nullptr, nullptr};
     ~cxm_cache() {
-        if (m) cudaSetDevice(m->device);
+        if (device >= 0) cudaSetDevice(device);
         for (auto &g : graph)
             if (g) cudaGraphExecDestroy(g);
         for (auto &p : prog) cudaFree(p.d);
@@ -1080,6 +1081,7 @@ extern "C" int cxm_cache_new(cxm_model *m, uint32_t max_tokens, cxm_cache **out)
     CU(cudaSetDevice(m->device));
     std::unique_ptr<cxm_cache> c(new cxm_cache);
     c->m = m;
+    c->device = m->device;
     c->max_tokens = max_tokens;
     size_t n = (size_t)m->cfg.n_layer * max_tokens * kv_dim(m);
     CU(cudaMalloc(&c->k, n * 4));

@@ -43,12 +43,14 @@ typedef struct {
 
 /* Modelo::abrir (src/forward.rs:187-266): parse the GGUF, upload every tensor
  * to HBM once (k-quant blocks regrouped, bytes unchanged, into the decode
- * kernel's tiles of 4 rows x 8 super-blocks) and build the RoPE tables
- * (src/ops.rs:1108-1129). */
+ * kernel's tiles of R rows x L super-blocks, R*L = 32, L chosen per matrix)
+ * and build the RoPE tables (src/ops.rs:1108-1129). */
 int  cxm_model_open(const char *gguf_path, int device, cxm_model **out);
 int  cxm_model_config(const cxm_model *m, cxm_config *out);
 /* bytes of weights resident on the device (the per-token weight stream) */
 uint64_t cxm_model_weight_bytes(const cxm_model *m);
+/* Caches belong to their model: use a cache only while its model is open
+ * (freeing it afterwards is allowed). */
 void cxm_model_close(cxm_model *m);
 
 /* ── tensor parallelism (one process per GPU; no counterpart in the

@@ -21,6 +21,7 @@
 #include <fcntl.h>
 #include <math.h>
 #include <pthread.h>
+#include <sched.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -67,8 +68,12 @@ int orc_set_dot_kernel(int type, orc_dot_fn f) {
     return 0;
 }
 void orc_set_q4k_acc_kernel(orc_q4k_acc_fn f) { g_q4k_acc = f; }
+/* default: one thread per CPU this process may run on (its affinity mask,
+ * which a container's cpuset narrows), as rayon's default pool */
 int orc_get_threads(void) {
     if (g_threads > 0) return g_threads;
+    cpu_set_t set;
+    if (sched_getaffinity(0, sizeof set, &set) == 0 && CPU_COUNT(&set) > 0) return CPU_COUNT(&set);
     long n = sysconf(_SC_NPROCESSORS_ONLN);
     return n > 0 ? (int)n : 1;
 }

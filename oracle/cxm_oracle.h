@@ -121,7 +121,8 @@ int orc_generate(orc_model *m, orc_cache *c, const uint32_t *prompt, int n_promp
 void orc_cache_fill(orc_cache *c, int n, uint64_t seed);
 void orc_expf(const float *x, float *y, size_t n);
 
-/* worker threads of the row-parallel matmul (0 = one per online CPU); the
+/* worker threads of the row-parallel matmul (0 = one per CPU of the process's
+ * affinity mask); the
  * workers persist between calls, like the reference's rayon pool */
 void orc_set_threads(int n);
 int  orc_get_threads(void);
