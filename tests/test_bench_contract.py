@@ -32,4 +32,6 @@ def test_reference_arm_prints_one_contract_line(tmp_path):
     assert d["config"]["workload"].startswith("tiny")
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    # timed on the reference's x86 kernels, each format's kernel named
+    assert "x86 AVX2 path" in cb["sample"] and "Q4_K: " in cb["sample"] and "Q6_K: " in cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
