@@ -1537,6 +1537,74 @@ static int project(orc_model *m, const float *x, int t, const orc_tensor *w, con
     return 0;
 }
 
+/* Several projections of one token's x (q, k, v; gate, up) as ONE parallel
+ * region over all their 32-row tasks, x quantized once per sub-block size
+ * (src/forward.rs:333-368, src/ops.rs:895-1009). The values are those of
+ * separate project() calls, bit for bit (the reference's own check,
+ * src/ops.rs:1613-1670); only the fork/join count changes. */
+#define MANY_MAX 3
+typedef struct {
+    int nw;
+    mm_ctx mm[MANY_MAX];
+    size_t first_task[MANY_MAX + 1];
+} many_ctx;
+
+static void many_task(void *c_, size_t b, size_t e) {
+    many_ctx *c = (many_ctx *)c_;
+    for (size_t task = b; task < e; task++) {
+        int i = 0;
+        while (task >= c->first_task[i + 1]) i++;
+        const size_t r0 = (task - c->first_task[i]) * 32, n = (size_t)c->mm[i].n;
+        mm_task(&c->mm[i], r0, r0 + 32 < n ? r0 + 32 : n);
+    }
+}
+
+/* 0: one call per matrix, as the reference's COSXAMIX_SIN_VARIAS (src/forward.rs:340-342) */
+static int g_varias = 1;
+void orc_set_varias(int on) { g_varias = on != 0; }
+
+static int project_many(orc_model *m, const float *x, int t, const orc_tensor *const *ws,
+                        const orc_tensor *const *bs, float *const *dsts, int nw) {
+    int k = (int)ws[0]->dims[0], fused = g_varias && t == 1 && nw <= MANY_MAX;
+    for (int i = 0; i < nw && fused; i++) {
+        const int ty = ws[i]->type;
+        fused = (int)ws[i]->dims[0] == k && k % 256 == 0 &&
+                (ty == ORC_Q2K || ty == ORC_Q3K || ty == ORC_Q4K || ty == ORC_Q5K || ty == ORC_Q6K) &&
+                ws[i]->nbytes >= (size_t)ws[i]->dims[1] * (size_t)(k / 256) * (size_t)orc_bytes_per_block(ty);
+    }
+    if (!fused) {
+        for (int i = 0; i < nw; i++)
+            if (project(m, x, t, ws[i], bs[i], dsts[i])) return -1;
+        return 0;
+    }
+    int8_t q16[k], q32[k];
+    float e16[k / 16], s16[k / 16], e32[k / 32], s32[k / 32];
+    int need16 = 0, need32 = 0;
+    for (int i = 0; i < nw; i++) {
+        if (orc_sub_block(ws[i]->type) == 16) need16 = 1;
+        else need32 = 1;
+    }
+    if (need16) orc_quantize_i8(x, (size_t)k, 16, q16, e16, s16);
+    if (need32) orc_quantize_i8(x, (size_t)k, 32, q32, e32, s32);
+    many_ctx c;
+    c.nw = nw;
+    c.first_task[0] = 0;
+    for (int i = 0; i < nw; i++) {
+        const int ty = ws[i]->type, sub = orc_sub_block(ty), n = (int)ws[i]->dims[1];
+        const int s16b = sub == 16;
+        c.mm[i] = (mm_ctx){1, k, n, sub, ty, (size_t)(k / 256) * (size_t)orc_bytes_per_block(ty), (size_t)(k / 256),
+                           gguf_data(&m->g, ws[i]), s16b ? q16 : q32, s16b ? e16 : e32, s16b ? s16 : s32, dsts[i]};
+        c.first_task[i + 1] = c.first_task[i] + ((size_t)n + 31) / 32;
+    }
+    par_for(c.first_task[nw], 1, many_task, &c);
+    for (int i = 0; i < nw; i++)
+        if (bs[i]) {
+            const float *b = (const float *)gguf_data(&m->g, bs[i]);
+            for (int j = 0; j < (int)ws[i]->dims[1]; j++) dsts[i][j] += b[j];
+        }
+    return 0;
+}
+
 /* project() without bias, as the sum over `tp` K slices of the row, slice
  * by slice in order (orc_set_tp); tp = 1 is project() itself */
 static int project_split(orc_model *m, const float *x, int t, const orc_tensor *w, float *dst, int tp) {
@@ -1609,7 +1677,11 @@ int orc_forward(orc_model *m, orc_cache *c, const uint32_t *tokens, int t, float
         const orc_layer *L = &m->layers[l];
         read_vec(m, L->attn_norm, w, (size_t)D);
         for (int i = 0; i < t; i++) norm(xn + (size_t)i * D, x + (size_t)i * D, w, (size_t)D, cfg->eps);
-        if (project(m, xn, t, L->q, L->qb, q) || project(m, xn, t, L->k, L->kb, kk) || project(m, xn, t, L->v, L->vb, vv)) goto done;
+        {
+            const orc_tensor *ws[3] = {L->q, L->k, L->v}, *bs[3] = {L->qb, L->kb, L->vb};
+            float *ds[3] = {q, kk, vv};
+            if (project_many(m, xn, t, ws, bs, ds, 3)) goto done;
+        }
         orc_rope(q, t, H, hd, m->cos_t, m->sin_t, cfg->ctx, c->len);
         orc_rope(kk, t, KV, hd, m->cos_t, m->sin_t, cfg->ctx, c->len);
         memcpy(c->k[l] + (size_t)c->len * kvd, kk, sizeof(float) * T * kvd);
@@ -1619,7 +1691,11 @@ int orc_forward(orc_model *m, orc_cache *c, const uint32_t *tokens, int t, float
         for (size_t i = 0; i < T * D; i++) x[i] += proj[i];
         read_vec(m, L->ffn_norm, w, (size_t)D);
         for (int i = 0; i < t; i++) norm(xn + (size_t)i * D, x + (size_t)i * D, w, (size_t)D, cfg->eps);
-        if (project(m, xn, t, L->gate, NULL, gate) || project(m, xn, t, L->up, NULL, up)) goto done;
+        {
+            const orc_tensor *ws[2] = {L->gate, L->up}, *bs[2] = {NULL, NULL};
+            float *ds[2] = {gate, up};
+            if (project_many(m, xn, t, ws, bs, ds, 2)) goto done;
+        }
         orc_silu(act, gate, T * F);
         for (size_t i = 0; i < T * F; i++) act[i] *= up[i];
         if (project_split(m, act, t, L->down, proj, g_tp)) goto done;

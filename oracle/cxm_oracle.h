@@ -160,6 +160,11 @@ float orc_x86_dot_row(int type, const uint8_t *row, const int8_t *xq, const floa
 /* test infrastructure: emulate n tensor-parallel ranks (o_proj and ffn_down
  * as n K-slice partial sums added in rank order); 1 = the reference */
 void orc_set_tp(int n);
+/* 1 (default): with one token, q/k/v and gate/up run as one parallel region
+ * with x quantized once per sub-block size (src/forward.rs:333-368,
+ * src/ops.rs:895-1009); 0: one call per matrix, the reference's
+ * COSXAMIX_SIN_VARIAS. Same values either way. */
+void orc_set_varias(int on);
 
 #ifdef __cplusplus
 }

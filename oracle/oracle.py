@@ -85,6 +85,7 @@ def _declare(L: C.CDLL) -> None:
         "orc_set_threads": (None, [C.c_int]),
         "orc_set_tp": (None, [C.c_int]),
         "orc_get_threads": (C.c_int, []),
+        "orc_set_varias": (None, [C.c_int]),
         "orc_set_backend": (None, [C.c_int]),
         "orc_get_backend": (C.c_int, []),
         "orc_set_dot_kernel": (C.c_int, [C.c_int, P]),

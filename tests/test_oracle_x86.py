@@ -189,3 +189,31 @@ def test_pool_serialises_callers_on_several_threads():
         t.join()
     O.set_threads(0)
     assert not errors, errors
+
+
+@pytest.mark.parametrize("backend", ["scalar", "x86"])
+def test_projections_in_one_region_equal_separate_calls(tmp_path, backend):
+    # src/ops.rs:1613-1670: q/k/v (and gate/up) in one parallel region with the
+    # input quantized once give the separate calls' values bit for bit; the
+    # Q6_K model mixes sub-blocks of 16 and 32 in one region
+    import cosxamix_b200 as cx
+    paths = [_tiny(tmp_path)]
+    p6 = str(tmp_path / "q6.gguf")
+    cx.synth_write(p6, cx.synth_spec("tiny", seed=5, n_layer=2, mix=cx.MIX_Q4_K_M))  # Q6_K attn_v in layer 0
+    paths.append(p6)
+    O.set_backend(backend)
+    try:
+        for p in paths:
+            m = O.Model(p)
+            out = {}
+            for varias in (1, 0):
+                O.lib().orc_set_varias(varias)
+                c = O.Cache(m)
+                lg = [m.forward(c, [3, 1, 4, 1, 5])]
+                for _ in range(4):
+                    lg.append(m.forward(c, [int(np.argmax(lg[-1]))]))
+                out[varias] = np.stack(lg)
+            np.testing.assert_array_equal(out[1].view(np.uint32), out[0].view(np.uint32))
+    finally:
+        O.lib().orc_set_varias(1)
+        O.set_backend("scalar")
