@@ -155,6 +155,8 @@ void  orc_x86_rmsnorm(float *out, const float *in, const float *w, size_t n, flo
 float orc_x86_dot_q4k(const uint8_t *row, const int8_t *xq, const float *xe, const float *xs, size_t nblk); /* :394-558 */
 float orc_x86_dot_q6k(const uint8_t *row, const int8_t *xq, const float *xe, const float *xs, size_t nblk); /* :760-846 */
 float orc_x86_reduce_q4k_acc(const float *acc16);                                             /* q4k_asm.rs:214-235 */
+void  orc_x86_q4k_scales(const uint8_t *block, const float *xe, const float *xs, float *scales8,
+                         float *mins8);                                                       /* x86.rs:394-471 */
 /* one row through the X86 backend's choice for `type` */
 float orc_x86_dot_row(int type, const uint8_t *row, const int8_t *xq, const float *xe, const float *xs, size_t nblk);
 /* test infrastructure: emulate n tensor-parallel ranks (o_proj and ffn_down

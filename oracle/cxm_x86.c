@@ -90,24 +90,35 @@ static inline uint32_t rd32(const uint8_t *p) {
  * vpmaddwd widens the pairs to i32, and one FMA per 32 values adds the
  * sub-block's products times its scale. The row total is one reduction of
  * each accumulator. */
+static inline void q4k_block_scales(const uint8_t *b, const float *xe, const float *xs, float s[8], __m256 *mins) {
+    const __m128 h = _mm_cvtph_ps(_mm_cvtsi32_si128((int)rd32(b)));
+    const float d = _mm_cvtss_f32(h), dmin = _mm_cvtss_f32(_mm_movehdup_ps(h));
+    const uint32_t w0 = rd32(b + 4), w1 = rd32(b + 8), w2 = rd32(b + 12);
+    const uint64_t sc = (uint64_t)(w0 & 0x3F3F3F3Fu) |
+                        (uint64_t)((w2 & 0x0F0F0F0Fu) | (((w0 >> 6) & 0x03030303u) << 4)) << 32;
+    const uint64_t mn = (uint64_t)(w1 & 0x3F3F3F3Fu) |
+                        (uint64_t)(((w2 >> 4) & 0x0F0F0F0Fu) | (((w1 >> 6) & 0x03030303u) << 4)) << 32;
+    const __m256 xe8 = _mm256_loadu_ps(xe);
+    _mm256_storeu_ps(s, _mm256_mul_ps(_mm256_mul_ps(_mm256_set1_ps(d), bytes8_to_ps(sc)), xe8));
+    *mins = _mm256_fmadd_ps(_mm256_mul_ps(_mm256_mul_ps(_mm256_set1_ps(dmin), bytes8_to_ps(mn)), xe8),
+                            _mm256_loadu_ps(xs), *mins);
+}
+
+/* One block's scale step alone (test access): xe*d*scale of its 8
+ * sub-blocks, and the 8 lanes of dmin*min*xe*xs from a zero accumulator. */
+void orc_x86_q4k_scales(const uint8_t *block, const float *xe, const float *xs, float *scales8, float *mins8) {
+    __m256 mins = _mm256_setzero_ps();
+    q4k_block_scales(block, xe, xs, scales8, &mins);
+    _mm256_storeu_ps(mins8, mins);
+}
+
 float orc_x86_dot_q4k(const uint8_t *row, const int8_t *xq, const float *xe, const float *xs, size_t nblk) {
     const __m256i ones = _mm256_set1_epi16(1), low4 = _mm256_set1_epi8(0x0F);
     __m256 acc = _mm256_setzero_ps(), mins = _mm256_setzero_ps();
     for (size_t bl = 0; bl < nblk; bl++) {
         const uint8_t *b = row + bl * 144;
-        const __m128 h = _mm_cvtph_ps(_mm_cvtsi32_si128((int)rd32(b)));
-        const float d = _mm_cvtss_f32(h), dmin = _mm_cvtss_f32(_mm_movehdup_ps(h));
-        const uint32_t w0 = rd32(b + 4), w1 = rd32(b + 8), w2 = rd32(b + 12);
-        const uint64_t sc = (uint64_t)(w0 & 0x3F3F3F3Fu) |
-                            (uint64_t)((w2 & 0x0F0F0F0Fu) | (((w0 >> 6) & 0x03030303u) << 4)) << 32;
-        const uint64_t mn = (uint64_t)(w1 & 0x3F3F3F3Fu) |
-                            (uint64_t)(((w2 >> 4) & 0x0F0F0F0Fu) | (((w1 >> 6) & 0x03030303u) << 4)) << 32;
-        const __m256 xe8 = _mm256_loadu_ps(xe + bl * 8);
-        const __m256 scl = _mm256_mul_ps(_mm256_mul_ps(_mm256_set1_ps(d), bytes8_to_ps(sc)), xe8);
-        mins = _mm256_fmadd_ps(_mm256_mul_ps(_mm256_mul_ps(_mm256_set1_ps(dmin), bytes8_to_ps(mn)), xe8),
-                               _mm256_loadu_ps(xs + bl * 8), mins);
         float s[8];
-        _mm256_storeu_ps(s, scl);
+        q4k_block_scales(b, xe + bl * 8, xs + bl * 8, s, &mins);
         const uint8_t *qs = b + 16;
         const int8_t *x = xq + bl * 256;
         for (int p = 0; p < 4; p++) {

@@ -95,6 +95,7 @@ def _declare(L: C.CDLL) -> None:
         "orc_x86_dot_q4k": (C.c_float, [P, P, P, P, C.c_size_t]),
         "orc_x86_dot_q6k": (C.c_float, [P, P, P, P, C.c_size_t]),
         "orc_x86_dot_row": (C.c_float, [C.c_int, P, P, P, P, C.c_size_t]),
+        "orc_x86_q4k_scales": (None, [P, P, P, P, P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

@@ -76,6 +76,42 @@ def test_avx2_q4k_matches_reference_golden():
     assert seen >= 3
 
 
+def test_avx2_q4k_scales_equal_the_readable_unpack():
+    # src/kernels/mod.rs:913-970: the word-mask unpack of the eight 6-bit
+    # scales gives d*scale*xe bit for bit over 5000 xorshift blocks; the mins
+    # (through one FMA) within 1e-5
+    state = 0x9E3779B97F4A7C15
+    mask = (1 << 64) - 1
+
+    def azar():
+        nonlocal state
+        state ^= (state << 13) & mask
+        state ^= state >> 7
+        state ^= (state << 17) & mask
+        return state
+
+    L = O.lib()
+    sc, mn = np.zeros(8, np.float32), np.zeros(8, np.float32)
+    for _ in range(5000):
+        block = np.array([azar() & 0xFF for _ in range(144)], np.uint8)
+        d = np.float32(0.001) + np.float32(azar() % 1000) * np.float32(1e-5)
+        dmin = np.float32(0.0005) + np.float32(azar() % 1000) * np.float32(1e-5)
+        block[0:2] = np.frombuffer(np.uint16(O.f32_to_f16(float(d))).tobytes(), np.uint8)
+        block[2:4] = np.frombuffer(np.uint16(O.f32_to_f16(float(dmin))).tobytes(), np.uint8)
+        xe = np.array([np.float32(azar() % 1000) * np.float32(1e-3) for _ in range(8)], np.float32)
+        xs = np.array([np.float32(azar() % 4000) - np.float32(2000) for _ in range(8)], np.float32)
+        L.orc_x86_q4k_scales(O.ptr(block), O.ptr(xe), O.ptr(xs), O.ptr(sc), O.ptr(mn))
+        _, e, off = O.unpack_i8(O.Q4K, block, 256)  # e = d*scale, off = -(dmin*min)
+        np.testing.assert_array_equal(sc.view(np.uint32), (e * xe).astype(np.float32).view(np.uint32))
+        want = np.float32(0)
+        for j in range(8):
+            want = np.float32(want + np.float32(np.float32(-off[j] * xe[j]) * xs[j]))
+        got = np.float32(0)
+        for v in mn:  # the lanes summed in order, in f32, as the reference's check does
+            got = np.float32(got + v)
+        assert abs(float(got) - float(want)) <= abs(float(want)) * 1e-5 + 1e-6
+
+
 def test_x86_backend_takes_reference_kernels_when_built():
     used = O.set_backend("x86")
     try:
