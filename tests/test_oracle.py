@@ -352,3 +352,33 @@ def test_azar_known_first_outputs():
         out.append((x * 0x2545F4914F6CDD1D) & 0xFFFFFFFFFFFFFFFF)
     a = O.Azar(7)
     assert [a.next() for _ in range(3)] == out
+
+
+# ── KV cache (src/forward.rs:62-127; the reference's test :587-603) ──
+
+def test_cache_prefix_copies_first_tokens_and_equals_truncate(tmp_path):
+    import cosxamix_b200 as cx
+    p = str(tmp_path / "tiny.gguf")
+    cx.synth_write(p, cx.synth_spec("tiny", seed=42, n_layer=2))
+    m = O.Model(p)
+    cfg = m.config
+    w = cfg.n_head_kv * cfg.head_dim
+    c = O.Cache(m)
+    m.forward(c, [7, 3, 9, 1])
+    k_all, v_all = c.layer(1, False), c.layer(0, True)
+    pre = c.prefix(2)
+    assert len(pre) == 2
+    np.testing.assert_array_equal(pre.layer(1, False), k_all[: 2 * w])
+    np.testing.assert_array_equal(pre.layer(0, True), v_all[: 2 * w])
+    assert len(c) == 4, "the original is untouched"
+    assert len(c.prefix(10)) == 4, "asking for more than there is keeps it all"
+    c.truncate(2)
+    for layer in range(cfg.n_layer):
+        for v in (False, True):
+            np.testing.assert_array_equal(c.layer(layer, v), pre.layer(layer, v))
+    c.truncate(5)  # longer than the cache: nothing changes
+    assert len(c) == 2
+    # continuing from the prefix equals computing the whole prompt afresh
+    np.testing.assert_array_equal(m.forward(pre, [9, 1, 4]), m.forward(O.Cache(m), [7, 3, 9, 1, 4]))
+    c.clear()
+    assert len(c) == 0
