@@ -354,6 +354,38 @@ def test_azar_known_first_outputs():
     assert [a.next() for _ in range(3)] == out
 
 
+# ── dispatch (src/ops.rs:1706-1758) ──
+
+@pytest.mark.parametrize("t", [O.Q4K, O.Q3K, O.Q2K, O.F32, O.F16])
+def test_quantized_matmul_within_3pct_of_f32(t):
+    # the integer path quantizes the input and the f32 path does not: within
+    # 3 % of the f32 result's range, for each row count either side of the
+    # reference's blocked-path threshold (24)
+    k, n = 256, 64
+    if t == O.F32:
+        w = np.sin(np.arange(n * k, dtype=np.float32) * np.float32(0.019)).astype(np.float32).view(np.uint8)
+    elif t == O.F16:
+        vals = np.sin(np.arange(n * k, dtype=np.float32) * np.float32(0.019)).astype(np.float32)
+        w = np.array([O.f32_to_f16(float(v)) for v in vals], np.uint16).view(np.uint8)
+    else:
+        w = np.array([(i * 97 + 29) % 251 for i in range(n * O.BLOCK_BYTES[t])], np.uint8)
+    dense = np.stack([O.dequantize(t, w[r * (w.size // n):(r + 1) * (w.size // n)], k) for r in range(n)])
+    lib = O.lib()
+    for m in (1, 2, 4, 8, 23, 24, 37):
+        x = np.cos(np.arange(m * k, dtype=np.float32) * np.float32(0.021)).astype(np.float32)
+        ref = (x.reshape(m, k).astype(np.float64) @ dense.T.astype(np.float64)).astype(np.float32)
+        got = np.zeros(m * n, np.float32)
+        assert lib.orc_matmul_fused(m, k, n, O.ptr(x), O.ptr(w), w.size, t, O.ptr(got)) == 0
+        # the byte pattern gives some blocks NaN/Inf scales; the reference's
+        # folds with f32::max skip NaN, and so do these
+        with np.errstate(invalid="ignore"):
+            rng = float(np.nanmax(ref) - np.nanmin(ref))
+            worst = float(np.nanmax(np.abs(got.reshape(m, n) - ref)))
+        assert worst < 0.03 * rng, (t, m, worst, rng)
+        # non-finite exactly where the f32 path is (the blocks with NaN/Inf scales)
+        np.testing.assert_array_equal(np.isfinite(got.reshape(m, n)), np.isfinite(ref))
+
+
 # ── KV cache (src/forward.rs:62-127; the reference's test :587-603) ──
 
 def test_cache_prefix_copies_first_tokens_and_equals_truncate(tmp_path):
