@@ -354,6 +354,22 @@ def test_azar_known_first_outputs():
     assert [a.next() for _ in range(3)] == out
 
 
+@pytest.mark.parametrize("t", [O.Q2K, O.Q3K, O.Q4K, O.Q5K, O.Q6K])
+def test_fused_dot_equals_dequantize_then_multiply(t):
+    # src/kernels/q2k.rs:325-340, src/kernels/q5k.rs:195-250: the fused dot
+    # against the definition, sum of dequant(w)_i * xq_i * xe[i / sub] in f64
+    from tests.golden.make_golden import finite_row
+    rng = np.random.default_rng(30 + t)
+    sub = O.SUB[t]
+    for nb in (1, 2, 8):
+        row = finite_row(rng, t, nb)
+        xq, xe, xs = O.quantize_i8(rng.standard_normal(nb * 256).astype(np.float32), sub)
+        w = O.dequantize(t, row, nb * 256).astype(np.float64)
+        want = float((w * xq.astype(np.float64) * np.repeat(xe.astype(np.float64), sub)).sum())
+        got = O.dot_row(t, row, xq, xe, xs)
+        assert abs(got - want) / max(abs(want), 1.0) < 1e-3, (nb, got, want)
+
+
 # ── dispatch (src/ops.rs:1706-1758) ──
 
 @pytest.mark.parametrize("t", [O.Q4K, O.Q3K, O.Q2K, O.F32, O.F16])
