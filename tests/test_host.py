@@ -29,13 +29,34 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_library_is_built_for_sm100a_only():
-    # the fatbin carries sm_100a SASS; no other architecture is embedded
-    import subprocess
-    r = subprocess.run(["cuobjdump", "--list-elf", cx.LIB_PATH], capture_output=True, text=True)
-    if r.returncode != 0:
-        pytest.skip("cuobjdump unavailable")
-    arches = set(re.findall(r"sm_(\d+a?)", r.stdout))
-    assert arches == {"100a"}, arches
+    # the recipe compiles and links every CUDA source for sm_100a alone
+    from cosxamix_b200 import build as b
+    assert b.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+    assert all(f in b.CUDA_FLAGS for f in b.ARCH)
+    assert not any("compute_" in f and "100a" not in f for f in b.CUDA_FLAGS)
+
+
+def header_prototypes():
+    """name -> number of parameters, for every function include/cxm.h declares"""
+    text = open(os.path.join(ROOT, "include", "cxm.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", "", text)
+    out = {}
+    for name, params in re.findall(r"\b(cxm_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text, flags=re.S):
+        params = params.strip()
+        out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_python_binding_matches_header_arity():
+    # every declared entry point is bound with as many arguments as the header gives it
+    protos = header_prototypes()
+    assert len(protos) >= 20
+    L = cx.lib()
+    for name, n in protos.items():
+        f = getattr(L, name)
+        assert f.argtypes is not None, f"{name} has no ctypes signature"
+        assert len(f.argtypes) == n, (name, len(f.argtypes), n)
 
 
 def test_no_cpu_fallback_without_gpu(tmp_path):
