@@ -1,5 +1,6 @@
 """Decode benchmark: batch-1 greedy decode of the Qwen2.5-3B-shaped Q4_K_M
-synthetic model through the C ABI.
+synthetic model (the headline configuration: 512-token prompt) through the
+C ABI.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
                     [--config tiny|qwen3b|...] [--workload decode|formats|shared-prefix|tp]
@@ -10,10 +11,10 @@ collective on the data path — so `value` is the sum over ranks (weak scaling).
 A step is one decode token: the forward of one token plus the greedy pick.
 
 The other workloads (each prints its own one-line JSON): `formats`
-(configs[2]: the 3B shape uniform in Q5_K, Q3_K, Q2_K, sampled decode),
-`shared-prefix` (configs[3]: 64 conversations sharded over the ranks, one
-shared 1024-token prefix prefilled once per GPU), `tp` (configs[4]: one
-Llama-3-8B-shaped conversation, tensor-parallel over the ranks).
+(the 3B shape uniform in Q5_K, Q3_K, Q2_K, sampled decode),
+`shared-prefix` (64 conversations sharded over the ranks, one shared
+1024-token prefix prefilled once per GPU), `tp` (one Llama-3-8B-shaped
+conversation, tensor-parallel over the ranks).
 """
 from __future__ import annotations
 
@@ -60,7 +61,7 @@ def ensure_model(config: str, seed: int) -> str:
 
 
 def workload_of(args) -> str:
-    """The workload label: configs[1]'s, or the named synthetic shape."""
+    """The workload label: the headline configuration's, or the named synthetic shape."""
     if args.config == "qwen3b":
         return WORKLOAD
     return f"{args.config}-shape synthetic model, {args.prompt}-token seeded prompt, greedy decode bs=1"
@@ -199,7 +200,7 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 def run_shared_prefix(args, rank: int, world: int, local: int) -> None:
-    """`--workload shared-prefix`: 64 conversations
+    """`--workload shared-prefix` (the data-parallel configuration): 64 conversations
     sharing a 1024-token seeded system prefix, each with its own 64-token
     suffix and 128 greedy tokens, sharded over the ranks (replicated weights,
     no collective). Each rank prefills the prefix once (untimed setup), then
@@ -255,7 +256,7 @@ def run_shared_prefix(args, rank: int, world: int, local: int) -> None:
 
 
 def run_formats(args, rank: int, world: int, local: int) -> None:
-    """`--workload formats`: the Qwen2.5-3B shape
+    """`--workload formats` (the uniform-format configuration): the Qwen2.5-3B shape
     re-quantized uniformly to Q5_K, Q3_K and Q2_K, one model after the other:
     128-token seeded prompt (untimed prefill), then sampled decode at
     temperature 0.7, top-p 0.9 (seed 42), every step the decode kernel plus
@@ -331,7 +332,7 @@ def run_formats(args, rank: int, world: int, local: int) -> None:
 
 
 def run_tp(args, rank: int, world: int, local: int) -> None:
-    """`--workload tp`: one Llama-3-8B-shaped Q4_K_M
+    """`--workload tp` (the tensor-parallel configuration): one Llama-3-8B-shaped Q4_K_M
     conversation, tensor-parallel over the ranks (torchrun, one process per
     GPU): each rank holds its heads / FFN rows / vocabulary rows, and every
     step exchanges the o_proj and ffn_down partial sums and the argmax over
@@ -420,14 +421,14 @@ def main() -> None:
         run_shared_prefix(args, rank, world, local)
         return
     if args.workload == "tp":
-        if args.config == "qwen3b":  # configs[4] is the 8B shape with a 4096-token prompt
+        if args.config == "qwen3b":  # the tensor-parallel configuration is the 8B shape with a 4096-token prompt
             args.config = "llama8b"
             if args.prompt == 512:
                 args.prompt = 4096
         run_tp(args, rank, world, local)
         return
     if args.workload == "formats":
-        if args.prompt == 512:  # the default of the main workload; configs[2] prompts with 128
+        if args.prompt == 512:  # the default of the main workload; the uniform-format configuration prompts with 128
             args.prompt = 128
         run_formats(args, rank, world, local)
         return

@@ -110,13 +110,13 @@ def _ptr(a: np.ndarray) -> int:
 # ───────────── synthetic models (src/daiss.rs) ─────────────
 
 CONFIGS = {
-    # tiny Llama-style decoder, untied, all Q4_K
+    # the tiny parity configuration: Llama-style decoder, untied, all Q4_K
     "tiny": dict(vocab=8192, dim=256, n_layer=6, n_head=8, n_head_kv=8, ffn=768, ctx=256, eps=1e-6,
                  rope_base=10000.0, tied=0, mix=MIX_UNIFORM, type=Q4_K),
-    # Qwen2.5-3B shape, Q4_K_M-style, tied embeddings
+    # the headline configuration: Qwen2.5-3B shape, Q4_K_M-style, tied embeddings
     "qwen3b": dict(vocab=151936, dim=2048, n_layer=36, n_head=16, n_head_kv=2, ffn=11008, ctx=4096, eps=1e-6,
                    rope_base=1e6, tied=1, mix=MIX_Q4_K_M, type=Q4_K),
-    # the Qwen2.5-3B shape re-quantized uniformly (output included)
+    # the uniform-format configurations: the Qwen2.5-3B shape re-quantized uniformly (output included)
     "qwen3b_q5k": dict(vocab=151936, dim=2048, n_layer=36, n_head=16, n_head_kv=2, ffn=11008, ctx=4096, eps=1e-6,
                        rope_base=1e6, tied=1, mix=MIX_UNIFORM, type=Q5_K),
     "qwen3b_q3k": dict(vocab=151936, dim=2048, n_layer=36, n_head=16, n_head_kv=2, ffn=11008, ctx=4096, eps=1e-6,
@@ -127,7 +127,7 @@ CONFIGS = {
     # (whole heads, o/down K slices of whole super-blocks): the TP tests' model
     "tp_small": dict(vocab=8192, dim=1024, n_layer=4, n_head=8, n_head_kv=4, ffn=2048, ctx=512, eps=1e-5,
                      rope_base=5e5, tied=0, mix=MIX_Q4_K_M, type=Q4_K),
-    # Llama-3-8B shape, Q4_K_M-style, untied
+    # the tensor-parallel configuration: Llama-3-8B shape, Q4_K_M-style, untied
     "llama8b": dict(vocab=128256, dim=4096, n_layer=32, n_head=32, n_head_kv=8, ffn=14336, ctx=8192, eps=1e-5,
                     rope_base=5e5, tied=0, mix=MIX_Q4_K_M, type=Q4_K),
 }

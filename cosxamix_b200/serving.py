@@ -1,4 +1,4 @@
-"""Shared-prefix serving across GPUs.
+"""Shared-prefix serving across GPUs (the data-parallel configuration).
 
 Independent conversations, replicated weights, no collective on the data
 path: rank r of N serves conversations r, r + N, r + 2N, ... Each rank
@@ -41,7 +41,7 @@ def seeded_tokens(seed: int, n: int, vocab: int) -> list[int]:
 
 @dataclass
 class Workload:
-    """one shared prefix, a suffix per conversation, greedy decode."""
+    """One shared prefix, a suffix per conversation, greedy decode."""
     conversations: int = 64
     prefix: int = 1024
     suffix: int = 64

@@ -1,4 +1,4 @@
-"""Tensor parallelism across the GPUs of one box.
+"""Tensor parallelism across the GPUs of one box (the 8B-shape configuration).
 
 One process per GPU. Rank r of N opens its share of the model
 (`Modelo(path, device, tp=(r, N))`): the q/k/v rows of its heads, the

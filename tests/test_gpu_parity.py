@@ -136,7 +136,7 @@ def test_attention_matches_oracle(heads, kvh, hd, total):
     np.testing.assert_array_equal(got, want)
 
 
-# ── model level (tiny config) ──
+# ── model level (the tiny parity configuration) ──
 
 def rel_range(a, b):
     return float(np.abs(a - b).max() / (b.max() - b.min()))
@@ -178,7 +178,7 @@ def test_tiny_greedy_64_tokens_identical(tiny_path):
 
 @pytest.mark.parametrize("t", [cx.Q5_K, cx.Q3_K, cx.Q2_K, cx.Q6_K])
 def test_uniform_format_model_matches_oracle(tmp_path, t):
-    # BASELINE configs[2] re-quantizes the whole model to one format: the
+    # the uniform-format configuration re-quantizes the whole model to one format: the
     # tiny shape so, logits bit-exact and greedy and top-p picks identical
     p = str(tmp_path / f"tiny_t{t}.gguf")
     cx.synth_write(p, cx.synth_spec("tiny", seed=5, type=t, tied=1))
@@ -230,7 +230,7 @@ def test_errors_are_reported_not_faulted(tiny_path):
     assert len(c) == 3
 
 
-# ── model level (Qwen2.5-3B shape) ──
+# ── model level (Qwen2.5-3B shape, the headline configuration) ──
 
 @pytest.fixture(scope="module")
 def qwen3b_path():
@@ -257,7 +257,7 @@ def test_qwen3b_prompt_logits_and_64_greedy_tokens(qwen3b_path):
     assert len(c2) == len(oc2) == 16 + 64
 
 
-# ── the sampler (src/sampler.rs:61-152: top-p 0.9, T 0.7) ──
+# ── the sampler (src/sampler.rs:61-152; the sampled configuration: top-p 0.9, T 0.7) ──
 
 @pytest.mark.parametrize("temperature,top_p", [(0.7, 0.9), (0.05, 0.9), (1.0, 1.0), (2.0, 0.5), (0.7, 0.0)])
 def test_device_sampler_matches_oracle(tiny_path, temperature, top_p):

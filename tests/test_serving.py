@@ -1,4 +1,4 @@
-"""Host logic of data-parallel serving on CPU: the
+"""Host logic of data-parallel serving (the shared-prefix configuration) on CPU: the
 conversation shards, the shared-prefix reuse and the job reduction, run as
 world_size-2 gloo process groups (no GPU)."""
 import os

@@ -1,4 +1,4 @@
-"""Host logic of tensor parallelism on CPU: the row
+"""Host logic of tensor parallelism (the 8B-shape configuration) on CPU: the row
 shares, the exchange of the ranks' IPC handles and the gather of the logits
 slices, run as world_size-2 gloo process groups (no GPU)."""
 import os
