@@ -50,14 +50,29 @@ def model_path(config: str, seed: int) -> str:
     return os.path.join(d, f"cxm_{config}_s{seed}.gguf")
 
 
-def ensure_model(config: str, seed: int) -> str:
-    import cosxamix_b200 as cx
+def ensure_model(config: str, seed: int, separate_process: bool = False) -> str:
+    """The seeded synthetic GGUF of `config` (written once per box). The
+    writer is this library's; `separate_process` writes it from a child
+    process, so a process that times the reference never loads the library."""
     p = model_path(config, seed)
     if not os.path.exists(p):
         t = time.time()
-        cx.synth_write(p, cx.synth_spec(config, seed=seed))
+        if separate_process:
+            code = ("import sys; sys.path.insert(0, %r); import cosxamix_b200 as cx; "
+                    "cx.synth_write(%r, cx.synth_spec(%r, seed=%d))" % (ROOT, p, config, seed))
+            subprocess.run([sys.executable, "-c", code], check=True)
+        else:
+            import cosxamix_b200 as cx
+            cx.synth_write(p, cx.synth_spec(config, seed=seed))
         print(f"[bench] wrote {p} in {time.time() - t:.1f}s", file=sys.stderr)
     return p
+
+
+def decode_config(args, world: int) -> dict:
+    """The `config` of the decode workload's line, the same in both arms."""
+    return {"workload": workload_of(args), "prompt": args.prompt, "decode_steps": args.steps,
+            "parallelism": f"dp{world} (independent conversations, replicated weights)",
+            "l2": "inputs larger than L2: 1.92 GB of weights streamed per step vs 126 MB L2"}
 
 
 def workload_of(args) -> str:
@@ -169,7 +184,7 @@ def run_reference(args, rank: int, world: int) -> None:
     timed on this box's host cores."""
     if rank != 0:
         return
-    path = ensure_model(args.config, args.seed)
+    path = ensure_model(args.config, args.seed, separate_process=True)
     from oracle import oracle as O
     kind, text = reference_cpu_path()
     m = O.Model(path)
@@ -190,7 +205,7 @@ def run_reference(args, rank: int, world: int) -> None:
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1000 / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
-        "config": {"workload": workload_of(args), "prompt": args.prompt, "decode_steps": args.steps},
+        "config": decode_config(args, world),
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": O.threads(), "kind": kind,
                          "sample": f"{args.steps} greedy decode tokens per step-set at context {args.prompt} (KV "
                                    f"prefix seeded instead of a CPU prefill), all host threads; {text}"},
@@ -508,8 +523,8 @@ def main() -> None:
     try:
         with open(os.path.join(ROOT, "profiles", "decode_step_qwen3b.md")) as f:
             for line in f:
-                if line.startswith("traffic_bytes_per_launch:"):
-                    traffic = int(line.split(":")[1].strip())
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    traffic = int(line.split(":")[1].strip().split()[0])
     except OSError:
         pass
     # the largest matvec phase alone: gate|up, cycled over the layers
@@ -528,9 +543,7 @@ def main() -> None:
         "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8-dot/f32", "data": "synthetic",
-        "config": {"workload": workload_of(args), "prompt": args.prompt, "decode_steps": args.steps,
-                   "parallelism": f"dp{world} (independent conversations, replicated weights)",
-                   "l2": "inputs larger than L2: 1.92 GB of weights streamed per step vs 126 MB L2"},
+        "config": decode_config(args, world),
         "weight_stream": {"bytes_per_token": wbytes, "gbs_per_gpu": round(value / world * wbytes / 1e9, 1),
                           "frac": round(value / world * wbytes / 1e9 / peak, 4), "peak_gbs": peak,
                           "peak_kind": peak_kind},

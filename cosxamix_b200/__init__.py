@@ -75,6 +75,7 @@ def lib() -> C.CDLL:
             "cxm_generate": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32, P, P, C.POINTER(C.c_uint32)]),
             "cxm_debug_subblock_sums": (C.c_int, [C.c_int, P, P, C.c_uint32, P]),
             "cxm_debug_matvec": (C.c_int, [C.c_int, P, C.c_uint32, C.c_uint32, P, P]),
+            "cxm_debug_matmul": (C.c_int, [C.c_int, P, C.c_uint32, C.c_uint32, P, C.c_uint32, P]),
             "cxm_debug_attention": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P]),
             "cxm_debug_expf": (C.c_int, [P, P, C.c_uint64]),
             "cxm_attention_noalloc": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P, P]),
@@ -348,6 +349,17 @@ def matvec(ggml_type: int, w: np.ndarray, rows: int, k: int, x: np.ndarray) -> n
     y = np.zeros(rows, np.float32)
     _check(lib().cxm_debug_matvec(ggml_type, _ptr(w), rows, k, _ptr(x), _ptr(y)))
     return y
+
+
+def matmul(ggml_type: int, w: np.ndarray, rows: int, k: int, x: np.ndarray) -> np.ndarray:
+    """ops::matmul_auto on the device: x (m x k) times W (rows x k), each
+    output in the order the reference's path for m rows gives it."""
+    w = np.ascontiguousarray(w, np.uint8)
+    x = np.ascontiguousarray(x, np.float32)
+    m = x.size // k
+    y = np.zeros(m * rows, np.float32)
+    _check(lib().cxm_debug_matmul(ggml_type, _ptr(w), rows, k, _ptr(x), m, _ptr(y)))
+    return y.reshape(m, rows)
 
 
 def expf(x: np.ndarray) -> np.ndarray:

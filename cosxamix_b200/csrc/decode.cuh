@@ -16,9 +16,10 @@
 // warp-wide 16-byte copies stream at over 7.) A normed prologue loads its
 // activation through L2 into registers, its norm weights before the barrier;
 // a quantize-only prologue stages its activation with one 1-D bulk copy.
-// With tensor parallelism, exchange phases add the ranks' partial sums of
-// o_proj / ffn_down and pick the argmax over the ranks' vocabulary slices,
-// over peer memory.
+// With tensor parallelism the FFN is split by output rows over the ranks,
+// and exchange phases gather the ranks' slices of the FFN's hidden vector and
+// of the residual stream, and pick the argmax over the ranks' vocabulary
+// slices, over peer memory.
 //
 // Weights are stored as tiles of R rows x LPR super-blocks (R*LPR = 32: one
 // warp's lanes, lane = R*block + row), lane-interleaved in 16-byte chunks so
@@ -144,24 +145,37 @@ __device__ inline float qm_dequant(const QMat &M, int r, int idx) {
 }
 
 // ── the program ──
-// PH_XREDUCE / PH_XARGMAX: the tensor-parallel exchanges with the other ranks
-// (GPUs) of the model, over their exchange areas mapped into this process
-enum PhaseKind : int { PH_MATVEC = 0, PH_SCORES = 1, PH_ATTN = 2, PH_COMMIT = 3, PH_XREDUCE = 4, PH_XARGMAX = 5 };
+// PH_XGATHER / PH_XARGMAX: the tensor-parallel exchanges with the other
+// ranks (GPUs) of the model, over their exchange areas mapped into this
+// process
+enum PhaseKind : int { PH_MATVEC = 0, PH_SCORES = 1, PH_ATTN = 2, PH_COMMIT = 3, PH_XGATHER = 4, PH_XARGMAX = 5 };
+
+// Float order of a segment's row totals, as the reference's matmul_auto
+// picks it for the number of activation rows (src/ops.rs:1056-1093):
+// ORD_FUSED, the per-row fused kernel (src/ops.rs:435-522); ORD_BUFFERED,
+// matmul_i8_directo (src/ops.rs:310-414): dot_i8_escalado over the row, then
+// the offset terms as a second chain. The two differ only for the formats
+// with a minimum (Q4_K, Q5_K, Q2_K).
+enum Order : int { ORD_FUSED = 0, ORD_BUFFERED = 1 };
 
 struct MvSeg {
     QMat M;
     int units;                // output units (row pairs); padded groups hold more
     int pairing, epi, half;   // Pairing, Epilogue; half = head_dim/2 for PAIR_ROPE
+    int ord;                  // Order
     int at_pos, pos_stride;   // out += pos*pos_stride (K/V cache rows)
     int idx_off;              // EPI_LOGITS: vocabulary index of row 0 (this rank's slice)
     const float *bias;
     float *out;
+    float *out2;              // EPI_RESID: a second copy of the result (a tensor-parallel rank's exported slice)
 };
 
 struct MvPhase {
     MvSeg seg[3];
     int nseg, ngroup, K, ntile;  // segments share K and the tile shape (lpr)
     int prologue, need16, need32;
+    uint32_t sv_off;             // region offset of the warps' offset-term spill (ORD_BUFFERED with a minimum)
+    int sv_warp;                 // floats of it per warp: rows per tile x sub-blocks per row
     const float *in, *norm_w;
     float eps;
     QMat E;          // PRO_EMBED: token_embd (tiled); or e32 when it is F32
@@ -177,12 +191,14 @@ struct AtPhase {
     float scale;
 };
 
-// an exchange: PH_XREDUCE adds Σ over ranks (in rank order) of partial
-// vector `parity` to dst[0..n); PH_XARGMAX takes the largest argmax key.
+// an exchange: PH_XGATHER copies every other rank's slice of an n-float
+// vector (rank p's slice: [p·n/tp, (p+1)·n/tp), at byte offset src_off of
+// its exchange area) into dst; PH_XARGMAX takes the largest argmax key.
 // `seq`: the exchange's number in the program (from 1), its flag epoch.
 struct XPhase {
     float *dst;
-    int n, parity, seq;
+    int n, seq;
+    uint32_t src_off;
 };
 
 struct __align__(16) Phase {
@@ -207,19 +223,28 @@ struct __align__(16) FeedPhase {
 };
 static_assert(sizeof(FeedPhase) == 64, "FeedPhase is four 16-byte chunks");
 
-// A rank's exchange area, mapped by its peers through CUDA IPC: the two
-// partial vectors [2][xdim] f32 (o_proj's and ffn_down's, alternating), the
-// argmax keys [kTpMax] (slot p written by rank p), the flags [kTpMax] (slot p
-// written by rank p: the epoch of its last exchange).
+// A rank's exchange area, mapped by its peers through CUDA IPC: the FFN's
+// hidden vector [hdim] f32 (the model's own; the rank writes its slice, the
+// peers read it), the exported residual slices [2][xdim] f32 (alternating by
+// layer, so a peer still reading one layer's never sees the next layer's
+// writes), the argmax keys [kTpMax] (slot p written by rank p), the flags
+// [kTpMax] (slot p written by rank p: the epoch of its last exchange).
 constexpr int kTpMax = 8;
-__host__ __device__ inline size_t xch_keys_off(int xdim) { return (size_t)2 * xdim * sizeof(float); }
-__host__ __device__ inline size_t xch_flags_off(int xdim) { return xch_keys_off(xdim) + kTpMax * sizeof(uint64_t); }
-__host__ __device__ inline size_t xch_bytes(int xdim) { return xch_flags_off(xdim) + kTpMax * sizeof(unsigned); }
+__host__ __device__ inline size_t xch_xo_off(int hdim) { return (size_t)hdim * sizeof(float); }
+__host__ __device__ inline size_t xch_keys_off(int hdim, int xdim) {
+    return xch_xo_off(hdim) + (size_t)2 * xdim * sizeof(float);
+}
+__host__ __device__ inline size_t xch_flags_off(int hdim, int xdim) {
+    return xch_keys_off(hdim, xdim) + kTpMax * sizeof(uint64_t);
+}
+__host__ __device__ inline size_t xch_bytes(int hdim, int xdim) {
+    return xch_flags_off(hdim, xdim) + kTpMax * sizeof(unsigned);
+}
 
 struct DecodeArgs {
     const Phase *prog;
     int nphase;
-    int tp, tp_rank, xdim, nx;      // ranks; this one; partial length; exchanges in the program
+    int tp, tp_rank, xdim, hdim, nx;  // ranks; this one; residual and FFN lengths; exchanges in the program
     unsigned char *xch[kTpMax];     // every rank's exchange area (this rank's own at tp_rank)
     unsigned *epoch;                // exchanges completed by earlier launches (this rank)
     const FeedPhase *feed;    // the matvec phases' walk table
@@ -574,6 +599,10 @@ __device__ void unit_epilogue(const DecodeArgs &A, const MvSeg &g, int r0, int r
     case EPI_RESID:  // src/forward.rs:467-469, :489-491
         out[r0] = fa(e.a, y0);
         out[r1] = fa(e.b, y1);
+        if (g.out2) {
+            g.out2[r0] = out[r0];
+            g.out2[r1] = out[r1];
+        }
         break;
     case EPI_SWIGLU: {
         // src/kernels/scalar.rs:63-67 then `*a *= u` (src/forward.rs:485-487)
@@ -732,8 +761,8 @@ __device__ bool grid_sync(const DecodeArgs &A, unsigned target, volatile int *ab
 // peer that acquires the flag sees this rank's partial vector (or key). Every
 // wait is bounded like the grid barrier's; a timeout raises ERR_TIMEOUT here
 // and stops the kernel, so a lost peer never hangs this GPU.
-__device__ __forceinline__ unsigned *xch_flags(unsigned char *area, int xdim) {
-    return (unsigned *)(area + xch_flags_off(xdim));
+__device__ __forceinline__ unsigned *xch_flags(unsigned char *area, int hdim, int xdim) {
+    return (unsigned *)(area + xch_flags_off(hdim, xdim));
 }
 __device__ __forceinline__ void flag_store(unsigned *f, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
@@ -765,7 +794,7 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 __device__ bool wait_peers(const DecodeArgs &A, unsigned ep) {
-    const unsigned *mine = xch_flags(A.xch[A.tp_rank], A.xdim);
+    const unsigned *mine = xch_flags(A.xch[A.tp_rank], A.hdim, A.xdim);
     const unsigned long long t0 = global_ns();
     for (int p = 0; p < A.tp; p++) {
         if (p == A.tp_rank) continue;
@@ -788,15 +817,15 @@ __device__ bool wait_peers(const DecodeArgs &A, unsigned ep) {
 __device__ void signal_peers(const DecodeArgs &A, unsigned ep) {
     __threadfence_system();
     for (int p = 0; p < A.tp; p++)
-        if (p != A.tp_rank) flag_store(xch_flags(A.xch[p], A.xdim) + A.tp_rank, ep);
+        if (p != A.tp_rank) flag_store(xch_flags(A.xch[p], A.hdim, A.xdim) + A.tp_rank, ep);
 }
 
-// dst[i] = dst[i] + (((partial_0[i] + partial_1[i]) + ...) + partial_{tp-1}[i]):
-// the ranks' partial sums of o_proj / ffn_down (each over its K slice),
-// added in rank order, then the residual add of src/forward.rs:467-469 /
-// :489-491. CTA 0 publishes this rank's partial (complete: a grid barrier
-// precedes this phase); every CTA waits for the peers', then adds its slice.
-__device__ void phase_xreduce(const DecodeArgs &A, const XPhase &X, unsigned ep, volatile int *abort_flag,
+// The other ranks' slices of an n-float vector into this rank's copy: CTA
+// 0 publishes this rank's slice (complete: a grid barrier precedes this
+// phase), every CTA waits for the peers', then copies its share of their
+// slices out of their exchange areas. Each value is the one the rank that
+// owns it computed, so the gathered vector is exactly the single-GPU one.
+__device__ void phase_xgather(const DecodeArgs &A, const XPhase &X, unsigned ep, volatile int *abort_flag,
                               int *ok_s) {
     if (threadIdx.x == 0) {
         if (blockIdx.x == 0) signal_peers(A, ep);
@@ -806,18 +835,15 @@ __device__ void phase_xreduce(const DecodeArgs &A, const XPhase &X, unsigned ep,
     }
     dsync();
     if (!*ok_s) return;
-    const int n4 = X.n / 4, per = (n4 + gridDim.x - 1) / gridDim.x;
+    const int s4 = X.n / A.tp / 4;      // float4s per slice
+    const int n4 = s4 * (A.tp - 1);     // the other ranks' float4s
+    const int per = (n4 + gridDim.x - 1) / gridDim.x;
     const int i0 = blockIdx.x * per, i1 = min(n4, i0 + per);
-    const size_t off = (size_t)X.parity * A.xdim * sizeof(float);
     for (int i = i0 + threadIdx.x; i < i1; i += kDW * 32) {
-        float4 s = ld_sys4((const float4 *)(A.xch[0] + off) + i);
-        for (int p = 1; p < A.tp; p++) {
-            const float4 v = ld_sys4((const float4 *)(A.xch[p] + off) + i);
-            s = make_float4(fa(s.x, v.x), fa(s.y, v.y), fa(s.z, v.z), fa(s.w, v.w));
-        }
-        float4 *d = (float4 *)X.dst + i;
-        const float4 x = __ldcg(d);
-        *d = make_float4(fa(x.x, s.x), fa(x.y, s.y), fa(x.z, s.z), fa(x.w, s.w));
+        int p = i / s4;
+        p += p >= A.tp_rank;            // skip this rank's own slice
+        const int j = p * s4 + i % s4;  // float4 index in the vector
+        ((float4 *)X.dst)[j] = ld_sys4((const float4 *)(A.xch[p] + X.src_off) + j);
     }
 }
 
@@ -830,7 +856,7 @@ __device__ void phase_xargmax(const DecodeArgs &A, unsigned ep, volatile int *ab
     const unsigned long long mine = __ldcg(A.argmax_key);
     for (int p = 0; p < A.tp; p++)
         if (p != A.tp_rank) {
-            unsigned long long *k = (unsigned long long *)(A.xch[p] + xch_keys_off(A.xdim)) + A.tp_rank;
+            unsigned long long *k = (unsigned long long *)(A.xch[p] + xch_keys_off(A.hdim, A.xdim)) + A.tp_rank;
             asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(k), "l"(mine) : "memory");
         }
     signal_peers(A, ep);
@@ -839,7 +865,7 @@ __device__ void phase_xargmax(const DecodeArgs &A, unsigned ep, volatile int *ab
         return;
     }
     unsigned long long best = mine;
-    const unsigned long long *keys = (const unsigned long long *)(A.xch[A.tp_rank] + xch_keys_off(A.xdim));
+    const unsigned long long *keys = (const unsigned long long *)(A.xch[A.tp_rank] + xch_keys_off(A.hdim, A.xdim));
     for (int p = 0; p < A.tp; p++) {
         if (p == A.tp_rank) continue;
         unsigned long long v;
@@ -1077,19 +1103,23 @@ __device__ __forceinline__ const unsigned char *ring_next(const DecodeArgs &A, R
     return tile;
 }
 
-// the sub-block terms of this lane's super-block in a tile of L lanes
-template <int T>
-__device__ __forceinline__ void tile_terms(const unsigned char *tile, int lane, int L, const XB &xb, float *tv) {
+// the sub-block terms of this lane's super-block in a tile of L lanes (BUF:
+// the buffered path's dot terms in tv and offset terms in sv)
+template <int T, bool BUF>
+__device__ __forceinline__ void tile_terms(const unsigned char *tile, int lane, int L, const XB &xb, float *tv,
+                                           float *sv, bool *anyd) {
     const int cs = L * 16;
     const uint8_t *pa = tile + lane * 16;
     const uint8_t *pss = tile + a_chunks(T) * cs + lane * plane_s_bytes(T);
     const uint8_t *pd = tile + a_chunks(T) * cs + L * plane_s_bytes(T) + lane * plane_d_bytes(T);
-    if (T == 12) block_k4<false>(pa, cs, xb, tv);
-    else if (T == 13) block_k4<true>(pa, cs, xb, tv);
+    if (T == 12) block_k4<false, BUF>(pa, cs, xb, tv, sv, anyd);
+    else if (T == 13) block_k4<true, BUF>(pa, cs, xb, tv, sv, anyd);
     else if (T == 14) block_q6k(pa, cs, pss, pd, xb, tv);
     else if (T == 11) block_q3k(pa, cs, pss, pd, xb, tv);
-    else block_q2k(pa, cs, pss, pd, xb, tv);
+    else block_q2k<BUF>(pa, cs, pss, pd, xb, tv, sv, anyd);
 }
+
+__host__ __device__ constexpr bool has_minimum(int T) { return T == 12 || T == 13 || T == 10; }
 
 // One row group (rpt = 32/lpr rows x nblk super-blocks) of type T: returns,
 // in every lane, the total of row (lane mod rpt), each added term by term in
@@ -1099,15 +1129,21 @@ struct Lanes {  // a lane's place in this phase's tiles: lane = rpt*bl + sl
     int lpr, rpt, bl, sl, ntile;
 };
 
-template <int T>
+// BUF (ORD_BUFFERED on a format with a minimum): the lanes also form each
+// block's offset terms and spill them to `sv` (this warp's area:
+// [row of the group][sub-block of the row]); after the row's dot chain, the
+// row's lane adds them in sub-block order when any of the row's offsets is
+// nonzero (src/ops.rs:395-401).
+template <int T, bool BUF>
 __device__ __forceinline__ float group_dot(const DecodeArgs &A, Ring &R, int warp, int lane, int nblk, const Lanes &g,
-                                           const Act &act) {
+                                           const Act &act, float *sv) {
     constexpr bool S32 = (T == 12 || T == 13);
     constexpr int NSUB = S32 ? 8 : 16;
     const int lpr = g.lpr, rpt = g.rpt, bl = g.bl, sl = g.sl;
     const int8_t *xq = S32 ? act.q32 : act.q16;
     const float2 *xes = S32 ? act.es32 : act.es16;
     float acc = 0.0f;
+    bool anyd = false;
     for (int t = 0; t < g.ntile; t++) {
         const unsigned char *tile = ring_next(A, R, warp, lane);
         const int nb = nblk - lpr * t < lpr ? nblk - lpr * t : lpr;
@@ -1115,7 +1151,15 @@ __device__ __forceinline__ float group_dot(const DecodeArgs &A, Ring &R, int war
         if (bl < nb) {
             const int b = lpr * t + bl;
             const XB xb{xq + b * kXqStride, xes + b * NSUB};
-            tile_terms<T>(tile, lane, rpt * nb, xb, tv);
+            if (BUF) {
+                float svt[NSUB];
+                tile_terms<T, true>(tile, lane, rpt * nb, xb, tv, svt, &anyd);
+                float *dst = sv + (sl * nblk + b) * NSUB;
+#pragma unroll
+                for (int k = 0; k < NSUB; k++) dst[k] = svt[k];
+            } else {
+                tile_terms<T, false>(tile, lane, rpt * nb, xb, tv, nullptr, nullptr);
+            }
         } else {
 #pragma unroll
             for (int k = 0; k < NSUB; k++) tv[k] = 0.0f;  // a lane past the tile's last block: its sums are dropped
@@ -1133,6 +1177,17 @@ __device__ __forceinline__ float group_dot(const DecodeArgs &A, Ring &R, int war
             run = __shfl_sync(0xffffffffu, v, jb * rpt + sl);
         }
         acc = run;
+    }
+    if (BUF) {
+        // lanes of row sl: sl, sl + rpt, sl + 2 rpt, ...
+        const uint32_t rows_of = rpt == 32 ? 1u : 0xFFFFFFFFu / ((1u << rpt) - 1u);
+        const uint32_t any = __ballot_sync(0xffffffffu, anyd);
+        __syncwarp();  // the spilled offset terms are visible to the row's lane
+        if (lane < rpt && (any & (rows_of << sl))) {
+            const float *src = sv + sl * nblk * NSUB;
+            for (int i = 0; i < nblk * NSUB; i++) acc = fa(acc, src[i]);
+        }
+        __syncwarp();  // the next group may overwrite the spill
     }
     return acc;
 }
@@ -1288,6 +1343,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
             const int sT0 = P.seg[0].M.type, sT1 = nseg > 1 ? P.seg[1].M.type : 0, sT2 = nseg > 2 ? P.seg[2].M.type : 0;
             const int sb0 = P.seg[0].M.nblk, sb1 = nseg > 1 ? P.seg[1].M.nblk : 0, sb2 = nseg > 2 ? P.seg[2].M.nblk : 0;
             const int su0 = P.seg[0].units, su1 = nseg > 1 ? P.seg[1].units : 0, su2 = nseg > 2 ? P.seg[2].units : 0;
+            const int so0 = P.seg[0].ord, so1 = nseg > 1 ? P.seg[1].ord : 0, so2 = nseg > 2 ? P.seg[2].ord : 0;
+            float *svw = (float *)(region + P.sv_off) + (size_t)warp * P.sv_warp;
             for (int q0 = qb + warp; q0 < qe; q0 += kDW) {
                 // phase-global group index -> segment j, local group lq
                 int j = 0, lq = q0;
@@ -1302,13 +1359,19 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
                 const int T = j == 0 ? sT0 : (j == 1 ? sT1 : sT2);
                 const int nblk = j == 0 ? sb0 : (j == 1 ? sb1 : sb2);
                 const int units = j == 0 ? su0 : (j == 1 ? su1 : su2);
+                const int ord = j == 0 ? so0 : (j == 1 ? so1 : so2);
                 float acc;
+                // Q6_K and Q3_K have one order; Q5_K and Q2_K are buffered
+                // whenever the reference's portable backend multiplies them
                 switch (T) {
-                case 12: acc = group_dot<12>(A, R, warp, lane, nblk, g, act); break;
-                case 13: acc = group_dot<13>(A, R, warp, lane, nblk, g, act); break;
-                case 14: acc = group_dot<14>(A, R, warp, lane, nblk, g, act); break;
-                case 11: acc = group_dot<11>(A, R, warp, lane, nblk, g, act); break;
-                default: acc = group_dot<10>(A, R, warp, lane, nblk, g, act); break;
+                case 12:
+                    acc = ord == ORD_BUFFERED ? group_dot<12, true>(A, R, warp, lane, nblk, g, act, svw)
+                                              : group_dot<12, false>(A, R, warp, lane, nblk, g, act, nullptr);
+                    break;
+                case 13: acc = group_dot<13, true>(A, R, warp, lane, nblk, g, act, svw); break;
+                case 14: acc = group_dot<14, false>(A, R, warp, lane, nblk, g, act, nullptr); break;
+                case 11: acc = group_dot<11, false>(A, R, warp, lane, nblk, g, act, nullptr); break;
+                default: acc = group_dot<10, true>(A, R, warp, lane, nblk, g, act, svw); break;
                 }
                 // lanes 0..rpt-1 hold the group's row totals; an even one owns
                 // the unit of rows (sl, sl+1)
@@ -1343,8 +1406,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
             phase_scores(ph.at, n, (float *)region);
         } else if (ph.kind == PH_ATTN) {
             phase_attn(ph.at, n, A.max_pos, (float *)region, fred, &fbc);
-        } else if (ph.kind == PH_XREDUCE) {
-            phase_xreduce(A, ph.xp, xbase_s + (unsigned)ph.xp.seq, &abort_flag, &sync_ok);
+        } else if (ph.kind == PH_XGATHER) {
+            phase_xgather(A, ph.xp, xbase_s + (unsigned)ph.xp.seq, &abort_flag, &sync_ok);
         } else if (ph.kind == PH_XARGMAX) {
             phase_xargmax(A, xbase_s + (unsigned)ph.xp.seq, &abort_flag);
         } else if (ph.kind == PH_COMMIT) {

@@ -12,8 +12,17 @@
 // 2^(k/N) from a 32-entry table, 2^(r/N) from a cubic — evaluated in double
 // with the fused multiply-adds an FMA build of that method performs.
 //
-// Verified exhaustively against the host libm on every finite float input
-// (tests/test_expf.py, tests/test_gpu_expf.py).
+// Checked against the host libm: the host compilation of this file over
+// every 13th float bit pattern in two phases, about 660 million inputs
+// (tests/test_expf.py with tests/expf_exhaustive.cpp), and the device
+// compilation on 8 million sampled and special inputs
+// (test_expf_matches_host_libm in tests/test_gpu_parity.py).
+//
+// The 32-entry table and the polynomial coefficients below are those of
+// Arm's optimized-routines expf/exp2f (math/exp2f_data.c), which glibc
+// ships: Copyright (c) 2017-2018, Arm Limited; SPDX-License-Identifier:
+// MIT OR Apache-2.0 WITH LLVM-exception. The code around them is this
+// library's own.
 #pragma once
 
 #include <stdint.h>

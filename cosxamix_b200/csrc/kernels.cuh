@@ -332,9 +332,16 @@ __device__ __forceinline__ uint4 shr4(uint4 v, int n) { return make_uint4(v.x >>
 __device__ __forceinline__ uint4 or4(uint4 a, uint4 b) { return make_uint4(a.x | b.x, a.y | b.y, a.z | b.z, a.w | b.w); }
 __device__ __forceinline__ uint4 shl4(uint4 v, int n) { return make_uint4(v.x << n, v.y << n, v.z << n, v.w << n); }
 
-// Q4_K / Q5_K: 8 terms (src/kernels/scalar.rs:132-217)
-template <bool Q5>
-__device__ __forceinline__ void block_k4(const uint8_t *pa, int cs, const XB &x, float *t) {
+// Q4_K / Q5_K: 8 terms.
+// BUF = false: the fused kernel's term per sub-block,
+//   xe·(d·sc·Σxq·q − dmin·m·xs)            (src/kernels/scalar.rs:132-217)
+// BUF = true: the buffered path's two terms per sub-block (src/ops.rs:383-405
+// over src/quant.rs:276-300): t = (d·sc)·xe·Σxq·q for dot_i8_escalado
+// (src/kernels/scalar.rs:95-109) and sv = (−dmin·m)·xe·xs for the offset
+// chain that follows it; `anyd` gets whether any −dmin·m is nonzero.
+template <bool Q5, bool BUF = false>
+__device__ __forceinline__ void block_k4(const uint8_t *pa, int cs, const XB &x, float *t, float *sv = nullptr,
+                                         bool *anyd = nullptr) {
     const uint4 hdr = *(const uint4 *)pa;
     const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
     const int4 *xp = (const int4 *)x.q;
@@ -369,12 +376,25 @@ __device__ __forceinline__ void block_k4(const uint8_t *pa, int cs, const XB &x,
         scale_min_k4(2 * p + 1, hdr.y, hdr.z, hdr.w, sc1, m1);
         const int j0 = 2 * p;
         const float2 es0 = x.es[j0], es1 = x.es[j0 + 1];
-        t[j0] = fm(es0.x, fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), es0.y)));
-        t[j0 + 1] = fm(es1.x, fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), es1.y)));
+        if (BUF) {
+            const float mn0 = fm(dmin, (float)m0), mn1 = fm(dmin, (float)m1);
+            t[j0] = fm(fm(fm(d, (float)sc0), es0.x), (float)s0);
+            t[j0 + 1] = fm(fm(fm(d, (float)sc1), es1.x), (float)s1);
+            sv[j0] = fm(fm(-mn0, es0.x), es0.y);
+            sv[j0 + 1] = fm(fm(-mn1, es1.x), es1.y);
+            *anyd = *anyd || mn0 != 0.0f || mn1 != 0.0f;
+        } else {
+            t[j0] = fm(es0.x, fs(fm(fm(d, (float)sc0), (float)s0), fm(fm(dmin, (float)m0), es0.y)));
+            t[j0 + 1] = fm(es1.x, fs(fm(fm(d, (float)sc1), (float)s1), fm(fm(dmin, (float)m1), es1.y)));
+        }
     }
 }
 
-// Q6_K: 16 terms (src/kernels/scalar.rs:294-324)
+// Q6_K: 16 terms (src/kernels/scalar.rs:294-324). The buffered path's term
+// (d·sc)·xe·Σxq·(q−32) (src/ops.rs:383-405, src/quant.rs:432-463) is the
+// same value bit for bit: the product of two factors does not depend on
+// their order, Σxq·q − 32·xs is an exact integer in f32, and the format has
+// no offset term. Q3_K likewise.
 __device__ __forceinline__ void block_q6k(const uint8_t *pa, int cs, const uint8_t *ps, const uint8_t *pd,
                                           const XB &x, float *t) {
     const float d = h2f(*(const unsigned short *)pd);
@@ -430,9 +450,13 @@ __device__ __forceinline__ void block_q3k(const uint8_t *pa, int cs, const uint8
     }
 }
 
-// Q2_K: 16 terms (src/kernels/q2k.rs:41-69)
+// Q2_K: 16 terms. BUF = false: the fused kernel's xe·(d·sc·Σxq·q − dmin·m·xs)
+// (src/kernels/q2k.rs:41-69); BUF = true: the buffered path's two terms, as
+// in block_k4 (src/quant.rs:367-399 unpacks scale d·(sc&15), offset
+// −dmin·(sc>>4)).
+template <bool BUF = false>
 __device__ __forceinline__ void block_q2k(const uint8_t *pa, int cs, const uint8_t *ps, const uint8_t *pd,
-                                          const XB &x, float *t) {
+                                          const XB &x, float *t, float *sv = nullptr, bool *anyd = nullptr) {
     const uint32_t dd = *(const uint32_t *)pd;
     const float d = h2f(dd), dm = h2f(dd >> 16);
     const uint4 scv = *(const uint4 *)ps;
@@ -451,7 +475,13 @@ __device__ __forceinline__ void block_q2k(const uint8_t *pa, int cs, const uint8
                 const int sc = (int)((scw[si >> 2] >> (8 * (si & 3))) & 0xFF);
                 const float ev = fm(d, (float)(sc & 0xF)), mv = fm(dm, (float)(sc >> 4));
                 const float2 es = x.es[si];
-                t[si] = fm(es.x, fs(fm(ev, (float)s), fm(mv, es.y)));
+                if (BUF) {
+                    t[si] = fm(fm(ev, es.x), (float)s);
+                    sv[si] = fm(fm(-mv, es.x), es.y);
+                    *anyd = *anyd || mv != 0.0f;
+                } else {
+                    t[si] = fm(es.x, fs(fm(ev, (float)s), fm(mv, es.y)));
+                }
             }
         }
     }

@@ -113,13 +113,16 @@ struct cxm_cache {
     float *k = nullptr, *v = nullptr;  // [n_layer][max_tokens][kvd]
     uint32_t *toks = nullptr;          // [max_tokens + 2]
     int *d_len = nullptr;
-    Program prog[4];
-    cudaGraphExec_t graph[4] = {nullptr, nullptr, nullptr, nullptr};
+    // one program and one graph per step mode and row class (RowClass)
+    Program prog[4][3];
+    cudaGraphExec_t graph[4][3] = {};
     ~cxm_cache() {
         if (device >= 0) cudaSetDevice(device);
-        for (auto &g : graph)
-            if (g) cudaGraphExecDestroy(g);
-        for (auto &p : prog) cudaFree(p.d);
+        for (auto &gm : graph)
+            for (auto &g : gm)
+                if (g) cudaGraphExecDestroy(g);
+        for (auto &pm : prog)
+            for (auto &p : pm) cudaFree(p.d);
         cudaFree(k);
         cudaFree(v);
         cudaFree(toks);
@@ -136,6 +139,26 @@ namespace {
 
 // STEP_SAMPLE: the STEP_LOGITS step, then the sampler writes the next token
 enum StepMode { STEP_PREFILL = 0, STEP_GREEDY = 1, STEP_LOGITS = 2, STEP_SAMPLE = 3 };
+
+// The reference multiplies all the tokens of one forward call at once, and
+// matmul_auto picks each matrix's path by their number m
+// (src/ops.rs:1056-1093). This library's parity target is the reference's
+// portable backend (COSXAMIX_KERNEL=escalar), where hay_fusionado holds for
+// Q4_K and Q3_K only (src/ops.rs:837-858: Q6_K and Q5_K need AVX2, Q2_K a
+// non-scalar copy) and the blocked path falls back to the buffered one
+// (src/ops.rs:599-606). So three classes of m give every matrix its order:
+//   ROWS_FEW (1..4):  Q4_K, Q3_K fused; Q6_K, Q5_K, Q2_K buffered
+//   ROWS_MID (5..23): Q4_K fused; the others buffered (Q3_K's cap is 4)
+//   ROWS_MANY (24+):  all buffered (BLOQUES_DESDE = 24, src/ops.rs:1013)
+// A step replays one token of such a call with its class's orders; the
+// output projection always multiplies one row (src/forward.rs:495-501).
+enum RowClass { ROWS_FEW = 0, ROWS_MID = 1, ROWS_MANY = 2 };
+int row_class(uint64_t m) { return m >= 24 ? ROWS_MANY : (m >= 5 ? ROWS_MID : ROWS_FEW); }
+int order_for(int type, int cls) {
+    if (type == Q4K) return cls == ROWS_MANY ? ORD_BUFFERED : ORD_FUSED;
+    if (type == Q3K) return cls == ROWS_FEW ? ORD_FUSED : ORD_BUFFERED;  // the same values either way
+    return ORD_BUFFERED;  // Q6_K (the same values either way), Q5_K, Q2_K
+}
 
 size_t kv_dim(const cxm_model *m) { return (size_t)m->kv_loc * m->cfg.head_dim; }  // this rank's KV heads
 
@@ -414,13 +437,14 @@ int launch_attention_on(cudaStream_t st, AttnParams &a) {
 }
 
 // ── decode programs ──
-MvSeg mv_seg(const QMat &M, int units, int pairing, int epi, float *out) {
+MvSeg mv_seg(const QMat &M, int units, int pairing, int epi, float *out, int cls = ROWS_FEW) {
     MvSeg s{};
     s.M = M;
     s.units = units;
     s.pairing = pairing;
     s.epi = epi;
     s.out = out;
+    s.ord = order_for(M.type, cls);
     return s;
 }
 
@@ -438,6 +462,11 @@ Phase mv_phase(const std::vector<MvSeg> &segs, int K, int prologue, const float 
     }
     P.K = K;
     P.ntile = (K / 256 + segs[0].M.lpr - 1) / segs[0].M.lpr;
+    for (int i = 0; i < P.nseg; i++) {  // the offset-term spill of a buffered segment with a minimum
+        const QMat &M = segs[i].M;
+        if (segs[i].ord == ORD_BUFFERED && has_minimum(M.type))
+            P.sv_warp = std::max(P.sv_warp, M.rpt * M.nblk * (sub_of(M.type) == 32 ? 8 : 16));
+    }
     P.prologue = prologue;
     P.in = in;
     P.norm_w = norm_w;
@@ -445,10 +474,16 @@ Phase mv_phase(const std::vector<MvSeg> &segs, int K, int prologue, const float 
     return ph;
 }
 
+// bytes of the region before a matvec phase's offset-term spill
+size_t mv_spill_offset(const MvPhase &P) {
+    return act_bytes(P.K, P.need16, P.need32) +
+           (P.prologue == PRO_QUANT && P.K <= kMaxStaged ? (size_t)P.K * sizeof(float) : 0);
+}
+
 size_t phase_region(const Phase &ph, int max_pos) {
-    if (ph.kind == PH_MATVEC)  // the quantized activation (+ the staged input of a short quantize-only prologue)
-        return act_bytes(ph.mv.K, ph.mv.need16, ph.mv.need32) +
-               (ph.mv.prologue == PRO_QUANT && ph.mv.K <= kMaxStaged ? (size_t)ph.mv.K * sizeof(float) : 0);
+    if (ph.kind == PH_MATVEC)  // the quantized activation (+ the staged input of a short quantize-only
+                               // prologue, + the warps' offset-term spill)
+        return mv_spill_offset(ph.mv) + (size_t)kDW * ph.mv.sv_warp * sizeof(float);
     if (ph.kind == PH_SCORES) return scores_region(ph.at.P, ph.at.H / ph.at.KV, ph.at.hd);
     if (ph.kind == PH_ATTN) return attn_region(max_pos, ph.at.dims);
     return 0;
@@ -471,43 +506,46 @@ int attn_dims(int H, int hd, int sms) {
 // scores, softmax+output, o, gate|up, down; the output projection unless the
 // step only prefills; the commit.
 // an exchange phase of a tensor-parallel program
-Phase x_phase(int kind, float *dst, int n, int parity, int seq) {
+Phase x_phase(int kind, float *dst, int n, size_t src_off, int seq) {
     Phase ph{};
     ph.kind = kind;
     ph.barrier = 1;
     ph.xp.dst = dst;
     ph.xp.n = n;
-    ph.xp.parity = parity;
+    ph.xp.src_off = (uint32_t)src_off;
     ph.xp.seq = seq;
     return ph;
 }
 
 // One token through the model (src/forward.rs:375-505) as decode-kernel
-// phases. With tensor parallelism the sizes are this rank's (heads, KV heads,
-// FFN rows, vocabulary rows), o_proj and ffn_down leave partial sums in the
-// exchange area, and exchange phases add the ranks' partials to the residual
-// and pick the argmax over the ranks' vocabulary slices.
-std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode) {
+// phases. With tensor parallelism every rank runs the attention block whole
+// (q/k/v, attention, o_proj: replicated) and its rows of the FFN: gate|up
+// rows [r·F/N, (r+1)·F/N) and ffn_down rows [r·D/N, (r+1)·D/N) over the whole
+// hidden vector; exchange phases gather the hidden vector and the residual
+// stream from the ranks' slices, and pick the argmax over their vocabulary
+// slices. Every value is computed as on one GPU, in the same order.
+std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode, int cls) {
     const cxm_config &cfg = m->cfg;
     const int D = cfg.dim, hd = cfg.head_dim, F = m->f_loc, H = m->h_loc, KV = m->kv_loc, dl = H * hd;
     const size_t kvd = kv_dim(m);
     const bool tp = m->tp > 1;
-    float *partial = (float *)m->xch;  // [2][D]: o_proj's, ffn_down's
+    const int FF = cfg.ffn, dloc = D / m->tp, r = m->tp_rank;
+    float *xo = (float *)(m->xch + xch_xo_off(FF));  // [2][D]: the exported residual slices
     int nx = 0;
     std::vector<Phase> prog;
     for (int l = 0; l < cfg.n_layer; l++) {
         const Layer &L = m->layers[l];
         float *kl = c->k + (size_t)l * c->max_tokens * kvd, *vl = c->v + (size_t)l * c->max_tokens * kvd;
         {  // RMSNorm + quantize, q/k/v with bias, RoPE, KV append
-            MvSeg sq = mv_seg(L.q, dl / 2, PAIR_ROPE, EPI_ROPE, m->q);
+            MvSeg sq = mv_seg(L.q, dl / 2, PAIR_ROPE, EPI_ROPE, m->q, cls);
             sq.half = hd / 2;
             sq.bias = L.bq;
-            MvSeg sk = mv_seg(L.k, (int)kvd / 2, PAIR_ROPE, EPI_ROPE, kl);
+            MvSeg sk = mv_seg(L.k, (int)kvd / 2, PAIR_ROPE, EPI_ROPE, kl, cls);
             sk.half = hd / 2;
             sk.bias = L.bk;
             sk.at_pos = 1;
             sk.pos_stride = (int)kvd;
-            MvSeg sv = mv_seg(L.v, (int)kvd / 2, PAIR_ADJ, EPI_STORE, vl);
+            MvSeg sv = mv_seg(L.v, (int)kvd / 2, PAIR_ADJ, EPI_STORE, vl, cls);
             sv.bias = L.bv;
             sv.at_pos = 1;
             sv.pos_stride = (int)kvd;
@@ -542,22 +580,18 @@ std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode) {
             prog.push_back(ph);
         }
         // o_proj + residual; RMSNorm + gate/up + SwiGLU; down + residual
-        if (!tp) {
-            prog.push_back(mv_phase({mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->x)}, dl, PRO_QUANT, m->att, nullptr, 0.0f, 1));
-        } else {
-            prog.push_back(mv_phase({mv_seg(L.o, D / 2, PAIR_ADJ, EPI_STORE, partial)}, dl, PRO_QUANT, m->att, nullptr, 0.0f, 1));
-            prog.push_back(x_phase(PH_XREDUCE, m->x, D, 0, ++nx));
-        }
-        prog.push_back(mv_phase({mv_seg(L.gu, F, PAIR_TWO, EPI_SWIGLU, m->h)}, D, PRO_NORM, m->x, L.ffn_norm, cfg.eps, 1));
-        if (!tp) {
-            prog.push_back(mv_phase({mv_seg(L.down, D / 2, PAIR_ADJ, EPI_RESID, m->x)}, F, PRO_QUANT, m->h, nullptr, 0.0f, 1));
-        } else {
-            prog.push_back(mv_phase({mv_seg(L.down, D / 2, PAIR_ADJ, EPI_STORE, partial + D)}, F, PRO_QUANT, m->h, nullptr, 0.0f, 1));
-            prog.push_back(x_phase(PH_XREDUCE, m->x, D, 1, ++nx));
-        }
+        prog.push_back(mv_phase({mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->x, cls)}, dl, PRO_QUANT, m->att, nullptr, 0.0f, 1));
+        prog.push_back(mv_phase({mv_seg(L.gu, F, PAIR_TWO, EPI_SWIGLU, m->h + (size_t)r * F, cls)}, D, PRO_NORM, m->x,
+                                L.ffn_norm, cfg.eps, 1));
+        if (tp) prog.push_back(x_phase(PH_XGATHER, m->h, FF, 0, ++nx));
+        MvSeg sd = mv_seg(L.down, dloc / 2, PAIR_ADJ, EPI_RESID, m->x + (size_t)r * dloc, cls);
+        const size_t xo_off = xch_xo_off(FF) + (size_t)(l & 1) * D * sizeof(float);
+        if (tp) sd.out2 = xo + (size_t)(l & 1) * D + (size_t)r * dloc;
+        prog.push_back(mv_phase({sd}, FF, PRO_QUANT, m->h, nullptr, 0.0f, 1));
+        if (tp) prog.push_back(x_phase(PH_XGATHER, m->x, D, xo_off, ++nx));
     }
     if (mode != STEP_PREFILL) {  // final RMSNorm, output projection, argmax
-        MvSeg so = mv_seg(m->out, m->v_loc / 2, PAIR_ADJ, EPI_LOGITS, m->logits);
+        MvSeg so = mv_seg(m->out, m->v_loc / 2, PAIR_ADJ, EPI_LOGITS, m->logits, ROWS_FEW);
         so.idx_off = m->v_off;
         prog.push_back(mv_phase({so}, D, PRO_NORM, m->x, m->out_norm, cfg.eps, 1));
         if (tp) prog.push_back(x_phase(PH_XARGMAX, nullptr, 0, 0, ++nx));
@@ -596,14 +630,17 @@ std::vector<FeedPhase> feed_table(const std::vector<Phase> &ph) {
 int upload_program(const std::vector<Phase> &ph, int max_pos, Program *out) {
     Program p;
     p.n = (int)ph.size();
+    std::vector<Phase> ph2 = ph;
+    for (Phase &x : ph2)
+        if (x.kind == PH_MATVEC) x.mv.sv_off = (uint32_t)mv_spill_offset(x.mv);
     for (const Phase &x : ph) p.region = std::max(p.region, phase_region(x, max_pos));
     p.region = (p.region + 127) & ~(size_t)127;
     const std::vector<FeedPhase> ft = feed_table(ph);
     p.nfeed = (int)ft.size();
-    for (const Phase &x : ph) p.nx += x.kind == PH_XREDUCE || x.kind == PH_XARGMAX;
+    for (const Phase &x : ph) p.nx += x.kind == PH_XGATHER || x.kind == PH_XARGMAX;
     const size_t pb = ph.size() * sizeof(Phase), fb = ft.size() * sizeof(FeedPhase);
     CU(cudaMalloc(&p.d, pb + fb));
-    CU(cudaMemcpy(p.d, ph.data(), pb, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(p.d, ph2.data(), pb, cudaMemcpyHostToDevice));
     p.feed = (const FeedPhase *)((const char *)p.d + pb);
     if (fb) CU(cudaMemcpy((void *)p.feed, ft.data(), fb, cudaMemcpyHostToDevice));
     *out = p;
@@ -658,6 +695,7 @@ DecodeArgs base_args(cxm_model *m) {
     a.tp = m->tp;
     a.tp_rank = m->tp_rank;
     a.xdim = m->cfg.dim;
+    a.hdim = m->cfg.ffn;
     for (int p = 0; p < m->tp; p++) a.xch[p] = m->peer[p];
     a.epoch = m->epoch;
     a.bar = m->bar;
@@ -671,7 +709,7 @@ DecodeArgs base_args(cxm_model *m) {
 
 int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out);
 
-int enqueue_step(cxm_model *m, cxm_cache *c, int mode) {
+int enqueue_step(cxm_model *m, cxm_cache *c, int mode, int cls) {
     if (!m->connected) {
         set_error("tensor-parallel rank %d of %d: cxm_tp_connect first", m->tp_rank, m->tp);
         return -1;
@@ -681,9 +719,9 @@ int enqueue_step(cxm_model *m, cxm_cache *c, int mode) {
         return -1;
     }
     if (mode == STEP_SAMPLE)
-        return enqueue_step(m, c, STEP_LOGITS) || launch_sample(m, c->d_len, c->toks, nullptr) ? -1 : 0;
-    Program &p = c->prog[mode];
-    if (!p.d && upload_program(step_program(m, c, mode), (int)c->max_tokens, &p)) return -1;
+        return enqueue_step(m, c, STEP_LOGITS, cls) || launch_sample(m, c->d_len, c->toks, nullptr) ? -1 : 0;
+    Program &p = c->prog[mode][cls];
+    if (!p.d && upload_program(step_program(m, c, mode, cls), (int)c->max_tokens, &p)) return -1;
     DecodeArgs a = base_args(m);
     a.prog = p.d;
     a.nphase = p.n;
@@ -697,16 +735,17 @@ int enqueue_step(cxm_model *m, cxm_cache *c, int mode) {
     return launch_decode(m->sms, m->stream, a, smem);
 }
 
-int get_graph(cxm_model *m, cxm_cache *c, int mode, cudaGraphExec_t *out) {
-    if (c->graph[mode]) {
-        *out = c->graph[mode];
+int get_graph(cxm_model *m, cxm_cache *c, int mode, int cls, cudaGraphExec_t *out) {
+    if (c->graph[mode][cls]) {
+        *out = c->graph[mode][cls];
         return 0;
     }
     const int pm = mode == STEP_SAMPLE ? STEP_LOGITS : mode;
-    if (!c->prog[pm].d && upload_program(step_program(m, c, pm), (int)c->max_tokens, &c->prog[pm])) return -1;
+    if (!c->prog[pm][cls].d && upload_program(step_program(m, c, pm, cls), (int)c->max_tokens, &c->prog[pm][cls]))
+        return -1;
     cudaGraph_t g = nullptr;
     CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(m, c, mode);
+    int rc = enqueue_step(m, c, mode, cls);
     cudaError_t e = cudaStreamEndCapture(m->stream, &g);
     if (rc) {
         if (g) cudaGraphDestroy(g);
@@ -716,20 +755,22 @@ int get_graph(cxm_model *m, cxm_cache *c, int mode, cudaGraphExec_t *out) {
         set_error("graph capture failed: %s", cudaGetErrorString(e));
         return -1;
     }
-    e = cudaGraphInstantiate(&c->graph[mode], g, 0);
+    e = cudaGraphInstantiate(&c->graph[mode][cls], g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) {
         set_error("graph instantiate failed: %s", cudaGetErrorString(e));
         return -1;
     }
-    *out = c->graph[mode];
+    *out = c->graph[mode][cls];
     return 0;
 }
 
-int run_steps(cxm_model *m, cxm_cache *c, int mode, uint32_t n) {
+// n steps of one mode, replaying the tokens of a forward call of `rows`
+// tokens (its row class picks every matrix's float order)
+int run_steps(cxm_model *m, cxm_cache *c, int mode, uint64_t rows, uint32_t n) {
     if (n == 0) return 0;
     cudaGraphExec_t g;
-    if (get_graph(m, c, mode, &g)) return -1;
+    if (get_graph(m, c, mode, row_class(rows), &g)) return -1;
     for (uint32_t i = 0; i < n; i++) CU(cudaGraphLaunch(g, m->stream));
     return 0;
 }
@@ -845,17 +886,18 @@ extern "C" int cxm_model_open_tp(const char *path, int device, int tp_rank, int 
         return -1;
     }
     cfg.head_dim = cfg.dim / cfg.n_head;
-    // this rank's share (src/forward.rs has one rank): whole heads, whole
-    // KV heads, FFN rows and o/down K slices of whole super-blocks
+    // this rank's share (src/forward.rs has one rank): the attention block
+    // whole (every head, every KV head, o_proj), its rows of the FFN
+    // (gate/up rows of its FFN slice, ffn_down rows of its hidden slice, each
+    // over the whole input), its vocabulary rows
     const int tp = tp_size, r = tp_rank;
-    if (cfg.n_head % tp || cfg.n_head_kv % tp || (tp > 1 && (cfg.n_head / tp * cfg.head_dim) % 256)) {
-        set_error("%d heads / %d KV heads of %d do not split over %d ranks in whole super-blocks", cfg.n_head,
-                  cfg.n_head_kv, cfg.head_dim, tp);
+    if (cfg.dim % (4 * tp)) {
+        set_error("hidden size %d does not split over %d ranks in groups of 4", cfg.dim, tp);
         return -1;
     }
-    m->h_loc = cfg.n_head / tp;
-    m->kv_loc = cfg.n_head_kv / tp;
-    const int dl = m->h_loc * cfg.head_dim;  // this rank's attention output: o's K slice
+    m->h_loc = cfg.n_head;
+    m->kv_loc = cfg.n_head_kv;
+    const int dl = m->h_loc * cfg.head_dim;  // the attention output: o's K
     const TensorInfo *embd = g.tensor("token_embd.weight");
     const TensorInfo *outw = g.tensor("output.weight");
     const TensorInfo *onorm = g.tensor("output_norm.weight");
@@ -912,36 +954,29 @@ extern "C" int cxm_model_open_tp(const char *path, int device, int tp_rank, int 
         const TensorInfo *tg = T("ffn_gate.weight"), *td = T("ffn_down.weight");
         if (!tg || !td || check_matrix(*tg) || check_matrix(*td)) return -1;
         const int F = (int)tg->dims[1];
-        if (F % (256 * tp)) {
-            set_error("FFN of %d rows does not split over %d ranks in whole super-blocks", F, tp);
+        if (F % (4 * tp)) {
+            set_error("FFN of %d rows does not split over %d ranks in groups of 4", F, tp);
             return -1;
         }
-        const int fl = F / tp, ql = dl, kl = m->kv_loc * (int)hd;  // this rank's rows
+        const int fl = F / tp, dloc = cfg.dim / tp, ql = dl, kl = m->kv_loc * (int)hd;  // this rank's rows
         // tile shapes by phase: q|k|v share one; o, gate|up and down their own
         const int lpr_qkv = choose_lpr(ql + 2 * kl, nbd, m->sms), lpr_o = choose_lpr(cfg.dim, dl / 256, m->sms);
         const int lpr_gu = choose_lpr(2 * fl, nbd, m->sms);
-        const int lpr_down = choose_lpr(cfg.dim, fl / 256, m->sms);
+        const int lpr_down = choose_lpr(dloc, F / 256, m->sms);
         if (!(t = T("attn_norm.weight")) || upload_vector(m.get(), g, *t, cfg.dim, &L.attn_norm)) return -1;
-        if (!(t = T("attn_q.weight")) ||
-            upload_matrix(m.get(), g, *t, PAIR_ROPE, half, lpr_qkv, &L.q, r * ql, ql))
-            return -1;
-        if (!(t = T("attn_q.bias")) || upload_vector(m.get(), g, *t, cfg.dim, &L.bq, (size_t)r * ql, ql)) return -1;
-        if (!(t = T("attn_k.weight")) ||
-            upload_matrix(m.get(), g, *t, PAIR_ROPE, half, lpr_qkv, &L.k, r * kl, kl))
-            return -1;
-        if (!(t = T("attn_k.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bk, (size_t)r * kl, kl)) return -1;
-        if (!(t = T("attn_v.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, lpr_qkv, &L.v, r * kl, kl))
-            return -1;
-        if (!(t = T("attn_v.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bv, (size_t)r * kl, kl)) return -1;
-        if (!(t = T("attn_output.weight")) ||
-            upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, lpr_o, &L.o, 0, 0, r * (dl / 256), dl / 256))
-            return -1;
+        if (!(t = T("attn_q.weight")) || upload_matrix(m.get(), g, *t, PAIR_ROPE, half, lpr_qkv, &L.q)) return -1;
+        if (!(t = T("attn_q.bias")) || upload_vector(m.get(), g, *t, cfg.dim, &L.bq)) return -1;
+        if (!(t = T("attn_k.weight")) || upload_matrix(m.get(), g, *t, PAIR_ROPE, half, lpr_qkv, &L.k)) return -1;
+        if (!(t = T("attn_k.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bk)) return -1;
+        if (!(t = T("attn_v.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, lpr_qkv, &L.v)) return -1;
+        if (!(t = T("attn_v.bias")) || upload_vector(m.get(), g, *t, kvd, &L.bv)) return -1;
+        if (!(t = T("attn_output.weight")) || upload_matrix(m.get(), g, *t, PAIR_ADJ, 0, lpr_o, &L.o)) return -1;
         if (!(t = T("ffn_norm.weight")) || upload_vector(m.get(), g, *t, cfg.dim, &L.ffn_norm)) return -1;
         if (!(t2 = T("ffn_up.weight")) || upload_pair(m.get(), g, *tg, *t2, lpr_gu, &L.gu, r * fl, fl)) return -1;
-        if (upload_matrix(m.get(), g, *td, PAIR_ADJ, 0, lpr_down, &L.down, 0, 0, r * (fl / 256), fl / 256)) return -1;
+        if (upload_matrix(m.get(), g, *td, PAIR_ADJ, 0, lpr_down, &L.down, r * dloc, dloc)) return -1;
         if (L.q.rows != ql || L.k.rows != kl || L.v.rows != kl || L.o.rows != cfg.dim || L.q.K != cfg.dim ||
             L.k.K != cfg.dim || L.v.K != cfg.dim || L.o.K != dl || L.gu.K != cfg.dim || L.gu.rows != 2 * fl ||
-            L.down.K != fl || L.down.rows != cfg.dim || (int)td->dims[0] != F) {
+            L.down.K != F || L.down.rows != dloc || (int)td->dims[0] != F) {
             set_error("layer %d: matrix shapes do not match the config", i);
             return -1;
         }
@@ -972,7 +1007,7 @@ extern "C" int cxm_model_open_tp(const char *path, int device, int tp_rank, int 
     }
     // activations
     if (m->alloc(&m->x, cfg.dim) || m->alloc(&m->q, cfg.dim) || m->alloc(&m->att, cfg.dim) ||
-        m->alloc(&m->h, std::max(cfg.ffn, 1)) || m->alloc(&m->logits, cfg.vocab) || m->alloc(&m->err, 1) ||
+        m->alloc(&m->logits, cfg.vocab) || m->alloc(&m->err, 1) ||
         m->alloc(&m->bar, 1) || m->alloc(&m->argmax_key, 1) || m->alloc(&m->rng, 1) ||
         m->alloc(&m->samp_params, 2) || m->alloc(&m->samp_tok, 1) || m->alloc(&m->samp_probs, cfg.vocab) ||
         m->alloc(&m->samp_prefix, cfg.vocab) || m->alloc(&m->samp_k0, cfg.vocab) ||
@@ -980,9 +1015,11 @@ extern "C" int cxm_model_open_tp(const char *path, int device, int tp_rank, int 
         m->alloc(&m->scores, (size_t)cfg.n_head * ((cfg.ctx + 3) & ~3)))
         return -1;
     CU(cudaMemset(m->err, 0, sizeof(int)));
-    // the tensor-parallel exchange area and the exchange count
-    if (m->alloc(&m->xch, xch_bytes(cfg.dim)) || m->alloc(&m->epoch, 1)) return -1;
-    CU(cudaMemset(m->xch, 0, xch_bytes(cfg.dim)));
+    // the exchange area (it holds the FFN's hidden vector, which peers read
+    // under tensor parallelism) and the exchange count
+    if (m->alloc(&m->xch, xch_bytes(cfg.ffn, cfg.dim)) || m->alloc(&m->epoch, 1)) return -1;
+    CU(cudaMemset(m->xch, 0, xch_bytes(cfg.ffn, cfg.dim)));
+    m->h = (float *)m->xch;
     CU(cudaMemset(m->epoch, 0, sizeof(unsigned)));
     m->peer[tp_rank] = m->xch;
     if (set_kernel_smem_limits()) return -1;
@@ -1185,7 +1222,7 @@ extern "C" int cxm_forward(cxm_model *m, cxm_cache *c, const uint32_t *tokens, u
         }
     CU(cudaSetDevice(m->device));
     CU(cudaMemcpyAsync(c->toks + c->len, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, m->stream));
-    if (run_steps(m, c, STEP_PREFILL, n - 1) || run_steps(m, c, STEP_LOGITS, 1)) return -1;
+    if (run_steps(m, c, STEP_PREFILL, n, n - 1) || run_steps(m, c, STEP_LOGITS, n, 1)) return -1;
     if (logits_out)  // this rank's vocabulary rows (all of them without tensor parallelism)
         CU(cudaMemcpyAsync(logits_out, m->logits, (size_t)m->v_loc * 4, cudaMemcpyDeviceToHost, m->stream));
     if (check_err(m)) return -1;
@@ -1267,10 +1304,10 @@ extern "C" int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, 
     CU(cudaSetDevice(m->device));
     const uint32_t len0 = c->len;
     CU(cudaMemcpyAsync(c->toks + len0, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, m->stream));
-    if (run_steps(m, c, STEP_PREFILL, n_prompt - 1)) return -1;
+    if (run_steps(m, c, STEP_PREFILL, n_prompt, n_prompt - 1)) return -1;
     if (max_new == 0) {
         // the prompt is still forwarded (logits of the last token)
-        if (run_steps(m, c, STEP_LOGITS, 1) || check_err(m)) return -1;
+        if (run_steps(m, c, STEP_LOGITS, n_prompt, 1) || check_err(m)) return -1;
         c->len = (uint32_t)after;
         m->logits_valid = true;
         return 0;
@@ -1283,8 +1320,11 @@ extern "C" int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, 
     // step i (0..gen) forwards toks[after-1+i] and writes token i at toks[after+i]
     const uint64_t state0 = s->state;
     if (sampled && set_sampler(m, s)) return -1;
-    if (run_steps(m, c, sampled ? STEP_SAMPLE : STEP_GREEDY, (uint32_t)gen)) return -1;
-    if (fwd == gen && run_steps(m, c, STEP_PREFILL, 1)) return -1;
+    // the first pick ends the prompt's forward call (its row class); every
+    // later token is a forward call of one row
+    const int pick = sampled ? STEP_SAMPLE : STEP_GREEDY;
+    if (run_steps(m, c, pick, n_prompt, 1) || run_steps(m, c, pick, 1, (uint32_t)(gen - 1))) return -1;
+    if (fwd == gen && run_steps(m, c, STEP_PREFILL, 1, 1)) return -1;
     if (check_err(m)) return -1;
     std::vector<uint32_t> toks(gen);
     CU(cudaMemcpy(toks.data(), c->toks + after, gen * 4, cudaMemcpyDeviceToHost));
@@ -1398,17 +1438,20 @@ extern "C" int cxm_debug_subblock_sums(int type, const uint8_t *row, const int8_
     return 0;
 }
 
-extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint32_t k, const float *x, float *y) {
+extern "C" int cxm_debug_matmul(int type, const uint8_t *w, uint32_t rows, uint32_t k, const float *x, uint32_t m,
+                                float *y) {
     if (need_device()) return -1;
-    if (!w || !x || !y || rows % 2 || rows == 0 || !is_kquant(type) || k == 0 || k % 256 || k > kMaxActivation) {
-        set_error("bad arguments (k-quant type, k a multiple of 256 up to %d, rows even)", kMaxActivation);
+    if (!w || !x || !y || rows % 2 || rows == 0 || !is_kquant(type) || k == 0 || k % 256 || k > kMaxActivation ||
+        m == 0) {
+        set_error("bad arguments (k-quant type, k a multiple of 256 up to %d, rows even, m >= 1)", kMaxActivation);
         return -1;
     }
-    // the decode kernel on a one-phase program: quantize x, W·x, store
-    int dev0 = 0, sms0 = 148;
-    CU(cudaGetDevice(&dev0));
-    CU(cudaDeviceGetAttribute(&sms0, cudaDevAttrMultiProcessorCount, dev0));
-    QMat M = tiled_desc(type, (int)k, (int)rows, choose_lpr((int)rows, (int)(k / 256), sms0));
+    // the decode kernel on a one-phase program: quantize x, W·x, store; once
+    // per activation row, every row in the order matmul_auto takes for m rows
+    int dev = 0, sms = 148;
+    CU(cudaGetDevice(&dev));
+    CU(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    QMat M = tiled_desc(type, (int)k, (int)rows, choose_lpr((int)rows, (int)(k / 256), sms));
     std::vector<uint8_t> tiles;
     build_tiles(M, rows_adj(w, (int)rows), tiles);
     DevBuf dw, dx, dy, derr, dbar, dprog;
@@ -1420,16 +1463,12 @@ extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint3
     CU(cudaMalloc(&dy.p, (size_t)rows * 4));
     CU(cudaMalloc(&derr.p, 4));
     CU(cudaMalloc(&dbar.p, 4));
-    CU(cudaMemcpy(dx.p, x, (size_t)k * 4, cudaMemcpyHostToDevice));
     CU(cudaMemset(derr.p, 0, 4));
-    Phase ph = mv_phase({mv_seg(M, (int)rows / 2, PAIR_ADJ, EPI_STORE, (float *)dy.p)}, (int)k, PRO_QUANT,
-                        (const float *)dx.p, nullptr, 0.0f, 0);
+    Phase ph = mv_phase({mv_seg(M, (int)rows / 2, PAIR_ADJ, EPI_STORE, (float *)dy.p, row_class(m))}, (int)k,
+                        PRO_QUANT, (const float *)dx.p, nullptr, 0.0f, 0);
     Program prog;
     if (upload_program({ph}, 0, &prog)) return -1;
     dprog.p = prog.d;
-    int dev = 0, sms = 148;
-    CU(cudaGetDevice(&dev));
-    CU(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     if (set_kernel_smem_limits()) return -1;
     DecodeArgs a{};
     a.prog = prog.d;
@@ -1438,16 +1477,23 @@ extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint3
     a.err = (int *)derr.p;
     size_t smem = 0;
     if (decode_geometry((uint32_t)(32 * M.bpb), prog, a, &smem)) return -1;
-    if (launch_decode(sms, 0, a, smem)) return -1;
-    CU(cudaDeviceSynchronize());
-    int e = 0;
-    CU(cudaMemcpy(&e, derr.p, 4, cudaMemcpyDeviceToHost));
-    if (e) {
-        set_error("decode kernel reported error flags %d", e);
-        return -1;
+    for (uint32_t f = 0; f < m; f++) {
+        CU(cudaMemcpy(dx.p, x + (size_t)f * k, (size_t)k * 4, cudaMemcpyHostToDevice));
+        if (launch_decode(sms, 0, a, smem)) return -1;
+        CU(cudaDeviceSynchronize());
+        int e = 0;
+        CU(cudaMemcpy(&e, derr.p, 4, cudaMemcpyDeviceToHost));
+        if (e) {
+            set_error("decode kernel reported error flags %d", e);
+            return -1;
+        }
+        CU(cudaMemcpy(y + (size_t)f * rows, dy.p, (size_t)rows * 4, cudaMemcpyDeviceToHost));
     }
-    CU(cudaMemcpy(y, dy.p, (size_t)rows * 4, cudaMemcpyDeviceToHost));
     return 0;
+}
+
+extern "C" int cxm_debug_matvec(int type, const uint8_t *w, uint32_t rows, uint32_t k, const float *x, float *y) {
+    return cxm_debug_matmul(type, w, rows, k, x, 1, y);
 }
 
 extern "C" int cxm_debug_attention(const float *q, const float *k, const float *v, uint32_t total, uint32_t heads,
@@ -1541,7 +1587,7 @@ extern "C" int cxm_bench_decode_sampled(cxm_model *m, cxm_cache *c, cxm_sampler 
     if (set_len(c, c->len - 1)) return -1;
     if (sampled && set_sampler(m, s)) return -1;
     cudaGraphExec_t g;
-    if (get_graph(m, c, sampled ? STEP_SAMPLE : STEP_GREEDY, &g)) return -1;
+    if (get_graph(m, c, sampled ? STEP_SAMPLE : STEP_GREEDY, ROWS_FEW, &g)) return -1;
     cudaEvent_t e0, e1;
     CU(cudaEventCreate(&e0));
     CU(cudaEventCreate(&e1));

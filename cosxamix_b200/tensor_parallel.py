@@ -1,35 +1,36 @@
 """Tensor parallelism across the GPUs of one box (the 8B-shape configuration).
 
 One process per GPU. Rank r of N opens its share of the model
-(`Modelo(path, device, tp=(r, N))`): the q/k/v rows of its heads, the
-gate/up rows of its FFN slice, the K slice of o_proj and ffn_down, its
-vocabulary rows, and the full embedding and norms. Every decode step
-exchanges the o_proj and ffn_down partial sums and the per-slice argmax over
-peer memory inside the decode kernel (no NCCL on the data path); this module
-only wires the ranks together: the CUDA IPC handles of the exchange areas
-travel over any torch.distributed process group (gloo or NCCL).
+(`Modelo(path, device, tp=(r, N))`): the attention block whole (q/k/v of
+every head, the whole KV cache, o_proj), the gate/up rows of its FFN slice
+[r·F/N, (r+1)·F/N), the ffn_down rows of its hidden slice [r·D/N, (r+1)·D/N)
+over the whole FFN vector, its vocabulary rows, and the embedding and norms.
+Every decode step gathers the FFN's hidden vector and the residual stream
+from the ranks' slices and picks the argmax over their vocabulary slices,
+over peer memory inside the decode kernel (no NCCL on the data path). Each
+value is computed by one rank exactly as one GPU computes it, so the model's
+logits and tokens do not depend on N. This module only wires the ranks
+together: the CUDA IPC handles of the exchange areas travel over any
+torch.distributed process group (gloo or NCCL).
 """
 from __future__ import annotations
 
 
-def shares(n_head: int, n_head_kv: int, head_dim: int, ffn: int, vocab: int, rank: int, size: int) -> dict:
+def shares(dim: int, ffn: int, vocab: int, rank: int, size: int) -> dict:
     """This rank's rows, as the library splits them (model.cu's
-    cxm_model_open_tp): whole heads and KV heads, FFN rows and o/down K
-    slices in whole 256-value super-blocks, an even share of the vocabulary
-    rows (the last rank takes the rest)."""
+    cxm_model_open_tp): FFN rows and hidden rows in equal slices (multiples
+    of 4, the exchanges' 16-byte units), an even share of the vocabulary rows
+    (the last rank takes the rest); the attention block is every rank's."""
     if size < 1 or not 0 <= rank < size:
         raise ValueError(f"rank {rank} of {size}")
-    if n_head % size or n_head_kv % size or (size > 1 and (n_head // size * head_dim) % 256):
-        raise ValueError(f"{n_head} heads / {n_head_kv} KV heads do not split over {size} ranks")
-    if ffn % (256 * size):
-        raise ValueError(f"FFN of {ffn} rows does not split over {size} ranks in super-blocks")
-    hl, kl, fl = n_head // size, n_head_kv // size, ffn // size
+    if dim % (4 * size) or ffn % (4 * size):
+        raise ValueError(f"hidden {dim} / FFN {ffn} do not split over {size} ranks in groups of 4")
+    fl, dl = ffn // size, dim // size
     vn = vocab if size == 1 else (vocab // size) & ~1
     vlo = rank * vn
     if rank == size - 1:
         vn = vocab - vlo
-    return {"q_rows": (rank * hl * head_dim, hl * head_dim), "kv_rows": (rank * kl * head_dim, kl * head_dim),
-            "ffn_rows": (rank * fl, fl), "o_k": (rank * hl * head_dim, hl * head_dim), "down_k": (rank * fl, fl),
+    return {"attention": (0, dim), "ffn_rows": (rank * fl, fl), "down_rows": (rank * dl, dl),
             "vocab_rows": (vlo, vn)}
 
 

@@ -135,6 +135,14 @@ int cxm_debug_subblock_sums(int ggml_type, const uint8_t *row, const int8_t *xq,
  * y[rows] = W[rows x k] · x[k], W raw GGUF k-quant bytes. Host pointers. */
 int cxm_debug_matvec(int ggml_type, const uint8_t *w, uint32_t rows, uint32_t k, const float *x, float *y);
 
+/* ops::matmul_auto with m activation rows (src/ops.rs:1056-1093) on the
+ * reference's portable backend: y[m x rows] = x[m x k] · W[rows x k]^T, each
+ * output in the float order the reference's path for m rows gives it (the
+ * fused kernel, or matmul_i8_directo's scaled dot and offset terms, which
+ * matmul_i8_bloques also takes without AVX2). Host pointers. */
+int cxm_debug_matmul(int ggml_type, const uint8_t *w, uint32_t rows, uint32_t k, const float *x, uint32_t m,
+                     float *y);
+
 /* ops::atencion for one new token (src/ops.rs:1258-1325) on the device's
  * split-K flash-decode kernel: q[heads*hd], k/v[total x heads_kv*hd]. Host
  * pointers; allocates its device buffers per call. */

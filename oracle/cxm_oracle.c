@@ -48,13 +48,7 @@ const char *orc_last_error(void) { return g_err; }
 static int g_threads = 0;
 void orc_set_threads(int n) { g_threads = n; }
 
-/* Tensor-parallel emulation (test infrastructure for the GPU's TP path, not
- * a reference behaviour): with n ranks, o_proj and ffn_down are computed as
- * n partial sums, each over its K slice of whole super-blocks (the K/n
- * values of rank r's heads / FFN rows), added in rank order before the
- * residual. Every other projection splits by rows, which changes no value. */
-static int g_tp = 1;
-void orc_set_tp(int n) { g_tp = n > 0 ? n : 1; }
+
 
 /* Kernel backend of orc_forward (cxm_oracle.h). */
 static int g_backend = ORC_BACKEND_SCALAR;
@@ -1048,10 +1042,33 @@ int orc_attention(const float *q, const float *k, const float *v, int tokens, in
     return 0;
 }
 
-/* ───────────────────────── fused matmul ───────────────────────── */
+/* ───────────────────────── matmul dispatch ───────────────────────── */
+
+/* src/ops.rs:837-858 `hay_fusionado`: the formats whose per-row fused kernel
+ * the reference uses. Q4_K and Q3_K always; Q6_K and Q5_K only when the AVX2
+ * kernels are in use (usar_avx2(), src/kernels/mod.rs:184-190); Q2_K only when
+ * its chosen copy is not the scalar one (src/kernels/q2k.rs:210-238), which
+ * under COSXAMIX_KERNEL=escalar it is. So on the scalar backend only Q4_K and
+ * Q3_K are fused; Q6_K, Q5_K and Q2_K take the buffered path even for one
+ * activation row. */
+static int fused_available(int type, int k) {
+    if (k % 256) return 0;
+    if (type == ORC_Q4K || type == ORC_Q3K) return 1;
+    if (type == ORC_Q6K || type == ORC_Q5K || type == ORC_Q2K) return g_backend == ORC_BACKEND_X86;
+    return 0;
+}
+
+int orc_matmul_path(int m, int k, int type) {
+    if (orc_sub_block(type) == 0) return ORC_PATH_F32;              /* ops.rs:1062-1068 */
+    if (m >= ORC_BLOCKED_FROM)                                      /* ops.rs:1073-1079 */
+        return g_backend == ORC_BACKEND_X86 && k % 32 == 0 ? ORC_PATH_BLOCKED : ORC_PATH_BUFFERED;  /* :599-606 */
+    const int cap = type == ORC_Q4K ? 0x7fffffff : 4;               /* ops.rs:1081-1085 */
+    if (fused_available(type, k) && m <= cap) return ORC_PATH_FUSED;
+    return ORC_PATH_BUFFERED;                                       /* ops.rs:1090-1092 */
+}
 
 typedef struct {
-    int m, k, n, sub, type;
+    int m, k, n, sub, type, path;
     size_t row_bytes, nblk;
     const uint8_t *w;
     const int8_t *xq;
@@ -1059,9 +1076,73 @@ typedef struct {
     float *dst;
 } mm_ctx;
 
+/* kernels::dot_i8_escalado (src/kernels/mod.rs:303-339): the AVX2 kernel on
+ * the x86 backend for the sub-block sizes and lengths it accepts, else the
+ * scalar one (scalar.rs:95-109: total += ea * eb * parcial, block by block) */
+static float dot_i8_scaled_dispatch(const int8_t *a, const int8_t *b, const float *ea, const float *eb, size_t n,
+                                    int block) {
+    const size_t wide = block > 32 ? (size_t)block : 32;
+    if (g_backend == ORC_BACKEND_X86 && (block == 16 || block % 32 == 0) && n % wide == 0)
+        return orc_x86_dot_i8_scaled(a, b, ea, eb, n, block);
+    return orc_dot_i8_scaled(a, b, ea, eb, n, block);
+}
+
+/* One output of the buffered path for an unpacked column (q, esc, des of its
+ * sub-blocks): src/ops.rs:383-405 (matmul_i8_directo) and :986-1006
+ * (matmul_varias_una_fila's buffered path), which compute the same thing:
+ * dot_i8_escalado over the whole row, then, when any shift of the column is
+ * nonzero, total += des[b] * xe[b] * xs[b] sub-block by sub-block. */
+static float buffered_out(const int8_t *colq, const float *esc, const float *des, int shifted, const int8_t *xq,
+                          const float *xe, const float *xs, size_t k, int sub) {
+    float total = dot_i8_scaled_dispatch(colq, xq, esc, xe, k, sub);
+    if (shifted) {
+        const size_t nsub = k / (size_t)sub;
+        for (size_t b = 0; b < nsub; b++) total += des[b] * xe[b] * xs[b];
+    }
+    return total;
+}
+
+static int any_nonzero(const float *v, size_t n) {
+    for (size_t i = 0; i < n; i++)
+        if (v[i] != 0.0f) return 1;
+    return 0;
+}
+
+float orc_dot_row_buffered(int type, const uint8_t *row, const int8_t *xq, const float *xe, const float *xs,
+                           size_t nblk) {
+    const int sub = orc_sub_block(type);
+    const size_t k = nblk * 256, nsub = k / (size_t)sub;
+    int8_t *q = (int8_t *)malloc(k);
+    float *esc = (float *)malloc(sizeof(float) * nsub), *des = (float *)malloc(sizeof(float) * nsub);
+    float r = NAN;
+    if (orc_unpack_i8(type, row, nblk * (size_t)orc_bytes_per_block(type), k, q, esc, des) > 0)
+        r = buffered_out(q, esc, des, any_nonzero(des, nsub), xq, xe, xs, k, sub);
+    free(q);
+    free(esc);
+    free(des);
+    return r;
+}
+
 static void mm_task(void *c_, size_t b, size_t e) {
     mm_ctx *c = (mm_ctx *)c_;
     size_t nsub = (size_t)c->k / (size_t)c->sub;
+    if (c->path == ORC_PATH_BUFFERED) {
+        /* src/ops.rs:372-405: each column unpacked once (desempaquetar_i8),
+         * then one output per activation row */
+        int8_t *q = (int8_t *)malloc((size_t)c->k);
+        float *esc = (float *)malloc(sizeof(float) * nsub), *des = (float *)malloc(sizeof(float) * nsub);
+        for (size_t col = b; col < e; col++) {
+            if (orc_unpack_i8(c->type, c->w + col * c->row_bytes, c->row_bytes, (size_t)c->k, q, esc, des) < 0) continue;
+            const int shifted = any_nonzero(des, nsub);
+            for (int f = 0; f < c->m; f++)
+                c->dst[(size_t)f * c->n + col] = buffered_out(q, esc, des, shifted, c->xq + (size_t)f * c->k,
+                                                              c->xe + f * nsub, c->xs + f * nsub, (size_t)c->k, c->sub);
+        }
+        free(q);
+        free(esc);
+        free(des);
+        return;
+    }
     if (g_backend == ORC_BACKEND_X86) {
         /* src/ops.rs:486-506: the row two ahead is prefetched line by line
          * (:45-80) while this one is computed */
@@ -1083,13 +1164,125 @@ static void mm_task(void *c_, size_t b, size_t e) {
     }
 }
 
-/* The reference routes a k-quant matmul through its fused per-row kernels
- * (src/ops.rs:435-522, dispatch :1056-1093). Its buffered and blocked paths
- * (:310-414, :607-829) form the same integer sub-block sums and differ only
- * in the float order in which those are scaled and added. */
-int orc_matmul_fused(int m, int k, int n, const float *lhs, const uint8_t *w, size_t wbytes, int type, float *dst) {
-    int sub = orc_sub_block(type);
-    if (sub == 0 || (type != ORC_Q2K && type != ORC_Q3K && type != ORC_Q4K && type != ORC_Q5K && type != ORC_Q6K)) {
+/* ── the blocked prefill path of the x86 backend (src/ops.rs:633-829) ── */
+
+/* src/ops.rs:565-580 `expandir_escalas`: one scale per 32-bit lane of each
+ * 32-value chunk (lanes 0-3 / 4-7 of a chunk take sub-blocks 2t / 2t+1 when
+ * sub-blocks hold 16 values; all eight take sub-block t when they hold 32) */
+static void expand_scales(const float *esc, int sub, size_t chunks, float *out) {
+    for (size_t t = 0; t < chunks; t++)
+        for (int l = 0; l < 8; l++) out[t * 8 + l] = sub == 16 ? esc[2 * t + (l >= 4)] : esc[t];
+}
+
+typedef struct {
+    int m, k, n, sub, type;
+    size_t row_bytes, nsub, chunks;
+    const uint8_t *w;
+    const int8_t *xq;     /* [m][k] */
+    const float *xe8;     /* [m][chunks*8] expanded activation scales */
+    const float *xes;     /* [m][nsub] scale x sum (src/ops.rs:671-675) */
+    float *dst;           /* [m][n] */
+} blk_ctx;
+
+/* One task = one tramo of COLUMNAS_MINIMAS (32) columns, as the
+ * reference's par_chunks_mut over salida_t (src/ops.rs:683-687). The tile
+ * walk of :758-820 (4x2 register tiles over row strips) only changes which
+ * outputs are computed together; each output's arithmetic is the tile
+ * kernel's for one (row, column), so it is computed here one by one. */
+static void blk_task(void *c_, size_t b, size_t e) {
+    blk_ctx *c = (blk_ctx *)c_;
+    const size_t ncols = e - b, k = (size_t)c->k, nsub = c->nsub, ch8 = c->chunks * 8;
+    int8_t *q = (int8_t *)malloc(ncols * k);
+    float *e8 = (float *)malloc(sizeof(float) * ncols * ch8), *des = (float *)malloc(sizeof(float) * ncols * nsub);
+    float *esc = (float *)malloc(sizeof(float) * nsub);
+    char *ok = (char *)calloc(ncols, 1), *has = (char *)calloc(ncols, 1);
+    /* :693-710 the tramo unpacked once */
+    for (size_t j = 0; j < ncols; j++) {
+        if (orc_unpack_i8(c->type, c->w + (b + j) * c->row_bytes, c->row_bytes, k, q + j * k, esc, des + j * nsub) < 0) {
+            memset(q + j * k, 0, k);
+            memset(e8 + j * ch8, 0, sizeof(float) * ch8);
+            continue;
+        }
+        ok[j] = 1;
+        expand_scales(esc, c->sub, c->chunks, e8 + j * ch8);
+    }
+    /* :712-736 unsigned weights when the tramo's range allows: every value
+     * shifted by -min, the shift taken out of the offset term */
+    int mn = 127, mx = -128;
+    for (size_t i = 0; i < ncols * k; i++) {
+        if (q[i] < mn) mn = q[i];
+        if (q[i] > mx) mx = q[i];
+    }
+    const int corr = -mn, unsig = mx + corr <= 129;
+    if (unsig && corr != 0)
+        for (size_t i = 0; i < ncols * k; i++) q[i] = (int8_t)(uint8_t)((int)q[i] + corr);
+    for (size_t j = 0; j < ncols; j++) {
+        float *d = des + j * nsub;
+        if (unsig && corr != 0)
+            for (size_t s = 0; s < nsub; s++) d[s] -= (float)corr * e8[j * ch8 + s * (size_t)c->sub / 4];
+        has[j] = (char)any_nonzero(d, nsub);
+    }
+    /* :758-820 the tile kernel, one output at a time (same arithmetic) */
+    for (size_t j = 0; j < ncols; j++)
+        for (int f = 0; f < c->m; f++) {
+            const int8_t *x = c->xq + (size_t)f * k;
+            const float *ef = c->xe8 + (size_t)f * ch8;
+            c->dst[(size_t)f * c->n + b + j] = orc_x86_tile_out(x, ef, q + j * k, e8 + j * ch8, c->chunks, unsig);
+        }
+    /* :822-831 the offset term, in the formats that have one */
+    for (size_t j = 0; j < ncols; j++) {
+        if (!has[j]) continue;
+        for (int f = 0; f < c->m; f++)
+            c->dst[(size_t)f * c->n + b + j] += orc_x86_dot_f32(des + j * nsub, c->xes + (size_t)f * nsub, nsub);
+    }
+    (void)ok;
+    free(q);
+    free(e8);
+    free(des);
+    free(esc);
+    free(ok);
+    free(has);
+}
+
+static int matmul_blocked_x86(int m, int k, int n, const float *lhs, const uint8_t *w, int type, float *dst) {
+    const int sub = orc_sub_block(type);
+    const size_t nsub = (size_t)k / sub, chunks = (size_t)k / 32;
+    int8_t *xq = (int8_t *)malloc((size_t)m * k);
+    float *xe = (float *)malloc(sizeof(float) * (size_t)m * nsub), *xs = (float *)malloc(sizeof(float) * (size_t)m * nsub);
+    float *xe8 = (float *)malloc(sizeof(float) * (size_t)m * chunks * 8), *xes = (float *)malloc(sizeof(float) * (size_t)m * nsub);
+    /* :662-677 the input quantized row by row, scales expanded, scale x sum */
+    for (int f = 0; f < m; f++) {
+        orc_quantize_i8(lhs + (size_t)f * k, (size_t)k, sub, xq + (size_t)f * k, xe + f * nsub, xs + f * nsub);
+        expand_scales(xe + f * nsub, sub, chunks, xe8 + (size_t)f * chunks * 8);
+        for (size_t s = 0; s < nsub; s++) xes[f * nsub + s] = xe[f * nsub + s] * xs[f * nsub + s];
+    }
+    blk_ctx c = {m, k, n, sub, type, (size_t)k / orc_values_per_block(type) * (size_t)orc_bytes_per_block(type),
+                 nsub, chunks, w, xq, xe8, xes, dst};
+    par_for((size_t)n, 32, blk_task, &c);
+    free(xq);
+    free(xe);
+    free(xs);
+    free(xe8);
+    free(xes);
+    return 0;
+}
+
+/* ops::matmul_auto (src/ops.rs:1056-1093) on this oracle's backend:
+ * dst[m][n] = lhs[m][k] · W[n][k]ᵀ by the path orc_matmul_path names. */
+int orc_matmul_auto(int m, int k, int n, const float *lhs, const uint8_t *w, size_t wbytes, int type, float *dst) {
+    return orc_matmul_by_path(orc_matmul_path(m, k, type), m, k, n, lhs, w, wbytes, type, dst);
+}
+
+/* One path forced (test access: the reference's own tests call
+ * matmul_i8_directo and matmul_i8_bloques directly, src/ops.rs:1517-1561). */
+int orc_matmul_by_path(int path, int m, int k, int n, const float *lhs, const uint8_t *w, size_t wbytes, int type,
+                       float *dst) {
+    if (path == ORC_PATH_BLOCKED && (g_backend != ORC_BACKEND_X86 || k % 32)) path = ORC_PATH_BUFFERED;  /* :599-606 */
+    if (path == ORC_PATH_FUSED && !(type == ORC_Q2K || type == ORC_Q3K || type == ORC_Q4K || type == ORC_Q5K ||
+                                    type == ORC_Q6K) ) path = ORC_PATH_BUFFERED;  /* :443-452 */
+    if (path == ORC_PATH_FUSED && k % 256) path = ORC_PATH_BUFFERED;              /* :453-455 */
+    if (orc_sub_block(type) == 0) path = ORC_PATH_F32;
+    if (path == ORC_PATH_F32) {
         /* F32/F16: ops::matmul (src/ops.rs:88-156): dequantize a row, f32 dot */
         int vpb = orc_values_per_block(type);
         if (!vpb || k % vpb) { set_err("type %d unsupported for matmul", type); return -1; }
@@ -1103,16 +1296,18 @@ int orc_matmul_fused(int m, int k, int n, const float *lhs, const uint8_t *w, si
         free(col);
         return 0;
     }
-    if (k % 256) { set_err("row of %d is not a multiple of 256", k); return -1; }
-    size_t rb = (size_t)k / 256 * (size_t)orc_bytes_per_block(type);
+    const int sub = orc_sub_block(type), vpb = orc_values_per_block(type);
+    if (k % vpb || k % sub) { set_err("row of %d is not a multiple of the blocks", k); return -1; }
+    size_t rb = (size_t)k / (size_t)vpb * (size_t)orc_bytes_per_block(type);
     if (wbytes < (size_t)n * rb) { set_err("missing weight bytes"); return -1; }
+    if (path == ORC_PATH_BLOCKED) return matmul_blocked_x86(m, k, n, lhs, w, type, dst);
     size_t nsub = (size_t)k / (size_t)sub;
     int8_t *xq = (int8_t *)malloc((size_t)m * k);
     float *xe = (float *)malloc(sizeof(float) * (size_t)m * nsub);
     float *xs = (float *)malloc(sizeof(float) * (size_t)m * nsub);
     for (int f = 0; f < m; f++)
         orc_quantize_i8(lhs + (size_t)f * k, (size_t)k, sub, xq + (size_t)f * k, xe + f * nsub, xs + f * nsub);
-    mm_ctx c = {m, k, n, sub, type, rb, (size_t)k / 256, w, xq, xe, xs, dst};
+    mm_ctx c = {m, k, n, sub, type, path, rb, (size_t)k / 256, w, xq, xe, xs, dst};
     par_for((size_t)n, 32, mm_task, &c);
     free(xq);
     free(xe);
@@ -1528,7 +1723,7 @@ orc_cache *orc_cache_prefix(const orc_cache *c, int n) {
 
 static int project(orc_model *m, const float *x, int t, const orc_tensor *w, const orc_tensor *bias, float *dst) {
     int k = (int)w->dims[0], n = (int)w->dims[1];
-    if (orc_matmul_fused(t, k, n, x, gguf_data(&m->g, w), w->nbytes, w->type, dst)) return -1;
+    if (orc_matmul_auto(t, k, n, x, gguf_data(&m->g, w), w->nbytes, w->type, dst)) return -1;
     if (bias) {
         const float *b = (const float *)gguf_data(&m->g, bias); /* f32, forward.rs:316-322 */
         for (int f = 0; f < t; f++)
@@ -1539,9 +1734,10 @@ static int project(orc_model *m, const float *x, int t, const orc_tensor *w, con
 
 /* Several projections of one token's x (q, k, v; gate, up) as ONE parallel
  * region over all their 32-row tasks, x quantized once per sub-block size
- * (src/forward.rs:333-368, src/ops.rs:895-1009). The values are those of
- * separate project() calls, bit for bit (the reference's own check,
- * src/ops.rs:1613-1670); only the fork/join count changes. */
+ * (src/forward.rs:333-368, src/ops.rs:895-1009). Each matrix takes the fused
+ * kernel when hay_fusionado allows it and the buffered path otherwise
+ * (src/ops.rs:956-1006); the values are those of separate project() calls,
+ * bit for bit (the reference's own check, src/ops.rs:1613-1670). */
 #define MANY_MAX 3
 typedef struct {
     int nw;
@@ -1565,14 +1761,13 @@ void orc_set_varias(int on) { g_varias = on != 0; }
 
 static int project_many(orc_model *m, const float *x, int t, const orc_tensor *const *ws,
                         const orc_tensor *const *bs, float *const *dsts, int nw) {
-    int k = (int)ws[0]->dims[0], fused = g_varias && t == 1 && nw <= MANY_MAX;
-    for (int i = 0; i < nw && fused; i++) {
-        const int ty = ws[i]->type;
-        fused = (int)ws[i]->dims[0] == k && k % 256 == 0 &&
-                (ty == ORC_Q2K || ty == ORC_Q3K || ty == ORC_Q4K || ty == ORC_Q5K || ty == ORC_Q6K) &&
-                ws[i]->nbytes >= (size_t)ws[i]->dims[1] * (size_t)(k / 256) * (size_t)orc_bytes_per_block(ty);
+    int k = (int)ws[0]->dims[0], many = g_varias && t == 1 && nw <= MANY_MAX;
+    for (int i = 0; i < nw && many; i++) {
+        const int ty = ws[i]->type, sub = orc_sub_block(ty), vpb = orc_values_per_block(ty);
+        many = (int)ws[i]->dims[0] == k && sub != 0 && k % vpb == 0 && k % sub == 0 &&
+               ws[i]->nbytes >= (size_t)ws[i]->dims[1] * (size_t)(k / vpb) * (size_t)orc_bytes_per_block(ty);
     }
-    if (!fused) {
+    if (!many) {
         for (int i = 0; i < nw; i++)
             if (project(m, x, t, ws[i], bs[i], dsts[i])) return -1;
         return 0;
@@ -1592,8 +1787,10 @@ static int project_many(orc_model *m, const float *x, int t, const orc_tensor *c
     for (int i = 0; i < nw; i++) {
         const int ty = ws[i]->type, sub = orc_sub_block(ty), n = (int)ws[i]->dims[1];
         const int s16b = sub == 16;
-        c.mm[i] = (mm_ctx){1, k, n, sub, ty, (size_t)(k / 256) * (size_t)orc_bytes_per_block(ty), (size_t)(k / 256),
-                           gguf_data(&m->g, ws[i]), s16b ? q16 : q32, s16b ? e16 : e32, s16b ? s16 : s32, dsts[i]};
+        const size_t rb = (size_t)(k / orc_values_per_block(ty)) * (size_t)orc_bytes_per_block(ty);
+        c.mm[i] = (mm_ctx){1, k, n, sub, ty, fused_available(ty, k) ? ORC_PATH_FUSED : ORC_PATH_BUFFERED, rb,
+                           (size_t)(k / 256), gguf_data(&m->g, ws[i]), s16b ? q16 : q32, s16b ? e16 : e32,
+                           s16b ? s16 : s32, dsts[i]};
         c.first_task[i + 1] = c.first_task[i] + ((size_t)n + 31) / 32;
     }
     par_for(c.first_task[nw], 1, many_task, &c);
@@ -1602,37 +1799,6 @@ static int project_many(orc_model *m, const float *x, int t, const orc_tensor *c
             const float *b = (const float *)gguf_data(&m->g, bs[i]);
             for (int j = 0; j < (int)ws[i]->dims[1]; j++) dsts[i][j] += b[j];
         }
-    return 0;
-}
-
-/* project() without bias, as the sum over `tp` K slices of the row, slice
- * by slice in order (orc_set_tp); tp = 1 is project() itself */
-static int project_split(orc_model *m, const float *x, int t, const orc_tensor *w, float *dst, int tp) {
-    int k = (int)w->dims[0], n = (int)w->dims[1];
-    if (tp <= 1) return project(m, x, t, w, NULL, dst);
-    int sub = orc_sub_block(w->type);
-    if (k % (256 * tp) || sub == 0) { set_err("%d values do not split over %d ranks", k, tp); return -1; }
-    size_t ks = (size_t)k / tp, nsub = (size_t)k / sub, rb = (size_t)k / 256 * orc_bytes_per_block(w->type);
-    int8_t *xq = (int8_t *)malloc((size_t)t * k);
-    float *xe = (float *)malloc(sizeof(float) * (size_t)t * nsub), *xs = (float *)malloc(sizeof(float) * (size_t)t * nsub);
-    for (int f = 0; f < t; f++)
-        orc_quantize_i8(x + (size_t)f * k, (size_t)k, sub, xq + (size_t)f * k, xe + f * nsub, xs + f * nsub);
-    const uint8_t *base = gguf_data(&m->g, w);
-    for (int f = 0; f < t; f++)
-        for (int j = 0; j < n; j++) {
-            float s = 0.0f;
-            for (int r = 0; r < tp; r++) {
-                const size_t o = (size_t)r * ks;
-                const float part = orc_dot_row(w->type, base + (size_t)j * rb + o / 256 * orc_bytes_per_block(w->type),
-                                               xq + (size_t)f * k + o, xe + f * nsub + o / sub, xs + f * nsub + o / sub,
-                                               ks / 256);
-                s = r == 0 ? part : s + part;
-            }
-            dst[(size_t)f * n + j] = s;
-        }
-    free(xq);
-    free(xe);
-    free(xs);
     return 0;
 }
 
@@ -1687,7 +1853,7 @@ int orc_forward(orc_model *m, orc_cache *c, const uint32_t *tokens, int t, float
         memcpy(c->k[l] + (size_t)c->len * kvd, kk, sizeof(float) * T * kvd);
         memcpy(c->v[l] + (size_t)c->len * kvd, vv, sizeof(float) * T * kvd);
         if (orc_attention(q, c->k[l], c->v[l], t, total, H, KV, hd, att)) goto done;
-        if (project_split(m, att, t, L->o, proj, g_tp)) goto done;
+        if (project(m, att, t, L->o, NULL, proj)) goto done;
         for (size_t i = 0; i < T * D; i++) x[i] += proj[i];
         read_vec(m, L->ffn_norm, w, (size_t)D);
         for (int i = 0; i < t; i++) norm(xn + (size_t)i * D, x + (size_t)i * D, w, (size_t)D, cfg->eps);
@@ -1698,7 +1864,7 @@ int orc_forward(orc_model *m, orc_cache *c, const uint32_t *tokens, int t, float
         }
         orc_silu(act, gate, T * F);
         for (size_t i = 0; i < T * F; i++) act[i] *= up[i];
-        if (project_split(m, act, t, L->down, proj, g_tp)) goto done;
+        if (project(m, act, t, L->down, NULL, proj)) goto done;
         for (size_t i = 0; i < T * D; i++) x[i] += proj[i];
     }
     read_vec(m, m->out_norm, w, (size_t)D);

@@ -73,10 +73,28 @@ int  orc_softmax(float *x, size_t n, size_t width);                             
 int  orc_attention(const float *q, const float *k, const float *v, int tokens, int total,
                    int heads, int heads_kv, int head_dim, float *out);             /* ops.rs:1258-1325 */
 
-/* dst[m,n] = lhs[m,k] · W[n,k]^T with the fused per-row kernels
- * (ops.rs:435-522 semantics; any k-quant type). */
-int orc_matmul_fused(int m, int k, int n, const float *lhs, const uint8_t *w, size_t wbytes,
-                     int type, float *dst);
+/* ops::matmul_auto (ops.rs:1056-1093): dst[m,n] = lhs[m,k] · W[n,k]^T by
+ * the path the reference takes for (m, k, type) on this oracle's backend. */
+int orc_matmul_auto(int m, int k, int n, const float *lhs, const uint8_t *w, size_t wbytes,
+                    int type, float *dst);
+/* The path matmul_auto takes: F32 (ops::matmul, :88-156, unquantized
+ * formats), FUSED (matmul_i8_fusionado, :435-522: the per-row fused kernels),
+ * BUFFERED (matmul_i8_directo, :310-414: the row unpacked to i8, then
+ * dot_i8_escalado and the offset term), BLOCKED (matmul_i8_bloques,
+ * :607-829: the AVX2 tile kernel; without AVX2 it is BUFFERED, :599-606).
+ * m >= ORC_BLOCKED_FROM (BLOQUES_DESDE, :1013) is BLOCKED/BUFFERED;
+ * otherwise FUSED when hay_fusionado (:837-858) and (Q4_K or m <= 4). */
+enum { ORC_PATH_F32 = 0, ORC_PATH_FUSED = 1, ORC_PATH_BUFFERED = 2, ORC_PATH_BLOCKED = 3 };
+enum { ORC_BLOCKED_FROM = 24 };
+int orc_matmul_path(int m, int k, int type);
+/* one path forced (the reference's tests call each path directly) */
+int orc_matmul_by_path(int path, int m, int k, int n, const float *lhs, const uint8_t *w, size_t wbytes, int type,
+                       float *dst);
+/* One output of the buffered path (ops.rs:383-405): the row unpacked by
+ * desempaquetar_i8, dot_i8_escalado on this backend, then
+ * total += des[b]*xe[b]*xs[b] over the sub-blocks when any des is nonzero. */
+float orc_dot_row_buffered(int type, const uint8_t *row, const int8_t *xq, const float *xe, const float *xs,
+                           size_t nblk);
 
 /* xorshift64* generator, src/daiss.rs:317-357 */
 uint64_t orc_azar_next(uint64_t *state);
@@ -128,12 +146,14 @@ void orc_set_threads(int n);
 int  orc_get_threads(void);
 
 /* Backend of orc_forward's kernels. SCALAR (the default) is the parity
- * restatement above. X86 runs what the reference runs on an AVX2/FMA/F16C
- * host (src/kernels/mod.rs:136-163): the AVX2 kernels below for Q4_K, Q6_K,
- * RMSNorm and attention's dot products, a registered reference kernel where
- * one is given, and a prefetch of the row two ahead (src/ops.rs:45-80). It
- * exists to time the CPU baseline at the reference's speed; its logits differ
- * from SCALAR's in float summation order only. */
+ * target: the reference run with COSXAMIX_KERNEL=escalar (its portable
+ * backend, src/kernels/mod.rs:136-163), kernels and matmul dispatch both.
+ * X86 runs what the reference picks by default on an AVX2/FMA/F16C host:
+ * the AVX2 kernels below for Q4_K, Q6_K, RMSNorm, attention's dot products,
+ * dot_i8_escalado and the blocked prefill tiles, a registered reference
+ * kernel where one is given, the fused path for all five k-quants, and a
+ * prefetch of the row two ahead (src/ops.rs:45-80). Its logits differ from
+ * SCALAR's in float summation order only. */
 enum { ORC_BACKEND_SCALAR = 0, ORC_BACKEND_X86 = 1 };
 void orc_set_backend(int backend);
 int  orc_get_backend(void);
@@ -159,9 +179,13 @@ void  orc_x86_q4k_scales(const uint8_t *block, const float *xe, const float *xs,
                          float *mins8);                                                       /* x86.rs:394-471 */
 /* one row through the X86 backend's choice for `type` */
 float orc_x86_dot_row(int type, const uint8_t *row, const int8_t *xq, const float *xe, const float *xs, size_t nblk);
-/* test infrastructure: emulate n tensor-parallel ranks (o_proj and ffn_down
- * as n K-slice partial sums added in rank order); 1 = the reference */
-void orc_set_tp(int n);
+/* dot_i8_escalado_avx2 (x86.rs:315-380): one 8-lane f32 accumulator, an FMA
+ * per 32 values with the sub-block scale products, one lane reduction */
+float orc_x86_dot_i8_scaled(const int8_t *a, const int8_t *b, const float *ea, const float *eb, size_t n, int block);
+/* One output of tesela_{i8,u8}_avx2 (x86.rs:864-948): `chunks` 32-value
+ * chunks of activation x (expanded scales ex) against column w (expanded
+ * scales ew); `unsig`: w holds unsigned values 0..=129 */
+float orc_x86_tile_out(const int8_t *x, const float *ex, const int8_t *w, const float *ew, size_t chunks, int unsig);
 /* 1 (default): with one token, q/k/v and gate/up run as one parallel region
  * with x quantized once per sub-block size (src/forward.rs:333-368,
  * src/ops.rs:895-1009); 0: one call per matrix, the reference's

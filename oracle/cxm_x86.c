@@ -191,3 +191,57 @@ float orc_x86_dot_q6k(const uint8_t *row, const int8_t *xq, const float *xe, con
     }
     return lanes_sum(_mm256_add_ps(acc[0], acc[1])) - 32.0f * lanes_sum(corr);
 }
+
+/* dot_i8_escalado_avx2, x86.rs:315-380. The eight i32 lanes of a 32-byte
+ * chunk (lane l = bytes 4l..4l+3, from vpmaddubsw on |a| and sign(b, a), then
+ * vpmaddwd with ones) are converted to f32 and FMA'd into one accumulator with
+ * the chunk's scale product: [e0 x4, e1 x4] for sub-blocks of 16 (two per
+ * chunk), ea*eb on all lanes for sub-blocks of 32k; one lane reduction. */
+float orc_x86_dot_i8_scaled(const int8_t *a, const int8_t *b, const float *ea, const float *eb, size_t n, int block) {
+    const __m256i ones = _mm256_set1_epi16(1);
+    __m256 acc = _mm256_setzero_ps();
+    if (block == 16) {
+        const size_t pairs = n / 32;
+        for (size_t i = 0; i < pairs; i++) {
+            const float e0 = ea[2 * i] * eb[2 * i], e1 = ea[2 * i + 1] * eb[2 * i + 1];
+            const __m256 sc = _mm256_setr_ps(e0, e0, e0, e0, e1, e1, e1, e1);
+            const __m256i va = _mm256_loadu_si256((const __m256i *)(a + 32 * i));
+            const __m256i vb = _mm256_loadu_si256((const __m256i *)(b + 32 * i));
+            const __m256i p32 = _mm256_madd_epi16(_mm256_maddubs_epi16(_mm256_sign_epi8(va, va), _mm256_sign_epi8(vb, va)), ones);
+            acc = _mm256_fmadd_ps(_mm256_cvtepi32_ps(p32), sc, acc);
+        }
+        return lanes_sum(acc);
+    }
+    const size_t per = (size_t)block / 32, nb = n / (size_t)block;
+    for (size_t i = 0; i < nb; i++) {
+        const __m256 sc = _mm256_set1_ps(ea[i] * eb[i]);
+        for (size_t t = 0; t < per; t++) {
+            const size_t idx = i * per + t;
+            const __m256i va = _mm256_loadu_si256((const __m256i *)(a + 32 * idx));
+            const __m256i vb = _mm256_loadu_si256((const __m256i *)(b + 32 * idx));
+            const __m256i p32 = _mm256_madd_epi16(_mm256_maddubs_epi16(_mm256_sign_epi8(va, va), _mm256_sign_epi8(vb, va)), ones);
+            acc = _mm256_fmadd_ps(_mm256_cvtepi32_ps(p32), sc, acc);
+        }
+    }
+    return lanes_sum(acc);
+}
+
+/* One (row, column) output of the tile kernels, x86.rs:864-948: per chunk,
+ * the column's eight lane sums (vpmaddubsw of unsigned column bytes and
+ * signed row bytes when `unsig`, else the sign trick of the i8 kernel),
+ * converted, times the column's expanded scales, FMA'd with the row's
+ * expanded scales into the accumulator; one lane reduction at the end. */
+float orc_x86_tile_out(const int8_t *x, const float *ex, const int8_t *w, const float *ew, size_t chunks, int unsig) {
+    const __m256i ones = _mm256_set1_epi16(1);
+    __m256 acc = _mm256_setzero_ps();
+    for (size_t t = 0; t < chunks; t++) {
+        const __m256i col = _mm256_loadu_si256((const __m256i *)(w + 32 * t));
+        const __m256i xv = _mm256_loadu_si256((const __m256i *)(x + 32 * t));
+        const __m256 ec = _mm256_loadu_ps(ew + 8 * t), ef = _mm256_loadu_ps(ex + 8 * t);
+        const __m256i p32 = unsig ? _mm256_madd_epi16(_mm256_maddubs_epi16(col, xv), ones)
+                                  : _mm256_madd_epi16(_mm256_maddubs_epi16(_mm256_sign_epi8(col, col), _mm256_sign_epi8(xv, col)), ones);
+        const __m256 v = _mm256_mul_ps(_mm256_cvtepi32_ps(p32), ec);
+        acc = _mm256_fmadd_ps(v, ef, acc);
+    }
+    return lanes_sum(acc);
+}

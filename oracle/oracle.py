@@ -58,7 +58,12 @@ def _declare(L: C.CDLL) -> None:
         "orc_rope": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int, C.c_int]),
         "orc_softmax": (C.c_int, [P, C.c_size_t, C.c_size_t]),
         "orc_attention": (C.c_int, [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P]),
-        "orc_matmul_fused": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P, C.c_size_t, C.c_int, P]),
+        "orc_matmul_auto": (C.c_int, [C.c_int, C.c_int, C.c_int, P, P, C.c_size_t, C.c_int, P]),
+        "orc_matmul_path": (C.c_int, [C.c_int, C.c_int, C.c_int]),
+        "orc_matmul_by_path": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, P, P, C.c_size_t, C.c_int, P]),
+        "orc_dot_row_buffered": (C.c_float, [C.c_int, P, P, P, P, C.c_size_t]),
+        "orc_x86_dot_i8_scaled": (C.c_float, [P, P, P, P, C.c_size_t, C.c_int]),
+        "orc_x86_tile_out": (C.c_float, [P, P, P, P, C.c_size_t, C.c_int]),
         "orc_azar_next": (C.c_uint64, [P]),
         "orc_azar_normals": (None, [P, C.c_float, P, P]),
         "orc_azar_seed": (C.c_uint64, [C.c_uint64]),
@@ -83,7 +88,6 @@ def _declare(L: C.CDLL) -> None:
         "orc_cache_fill": (None, [P, C.c_int, C.c_uint64]),
         "orc_expf": (None, [P, P, C.c_size_t]),
         "orc_set_threads": (None, [C.c_int]),
-        "orc_set_tp": (None, [C.c_int]),
         "orc_get_threads": (C.c_int, []),
         "orc_set_varias": (None, [C.c_int]),
         "orc_set_backend": (None, [C.c_int]),
@@ -210,12 +214,33 @@ def attention(q, k, v, tokens, total, heads, heads_kv, hd) -> np.ndarray:
     return out
 
 
-def matmul(lhs: np.ndarray, w: np.ndarray, t: int, k: int, n: int) -> np.ndarray:
+PATH_F32, PATH_FUSED, PATH_BUFFERED, PATH_BLOCKED = 0, 1, 2, 3
+BLOCKED_FROM = 24
+
+
+def matmul_path(m: int, k: int, t: int) -> int:
+    """The path ops::matmul_auto takes for m activation rows on this backend."""
+    return lib().orc_matmul_path(m, k, t)
+
+
+def dot_row_buffered(t: int, row: np.ndarray, xq, xe, xs) -> float:
+    """One output of the buffered path (src/ops.rs:383-405)."""
+    row = np.ascontiguousarray(row, np.uint8)
+    return lib().orc_dot_row_buffered(t, ptr(row), ptr(xq), ptr(xe), ptr(xs), xq.size // 256)
+
+
+def matmul(lhs: np.ndarray, w: np.ndarray, t: int, k: int, n: int, path: int | None = None) -> np.ndarray:
+    """ops::matmul_auto: the rows of `lhs` (m x k) times W (n x k) by the
+    path the reference takes for m rows (or the one `path` forces)."""
     lhs = np.ascontiguousarray(lhs, np.float32)
     m = lhs.size // k
     w = np.ascontiguousarray(w, np.uint8)
     out = np.zeros(m * n, np.float32)
-    if lib().orc_matmul_fused(m, k, n, ptr(lhs), ptr(w), w.size, t, ptr(out)):
+    if path is None:
+        rc = lib().orc_matmul_auto(m, k, n, ptr(lhs), ptr(w), w.size, t, ptr(out))
+    else:
+        rc = lib().orc_matmul_by_path(path, m, k, n, ptr(lhs), ptr(w), w.size, t, ptr(out))
+    if rc:
         raise ValueError(err())
     return out.reshape(m, n)
 
@@ -325,11 +350,6 @@ class Model:
 
 def set_threads(n: int) -> None:
     lib().orc_set_threads(n)
-
-
-def set_tp(n: int) -> None:
-    """Emulate n tensor-parallel ranks in o_proj / ffn_down (1: the reference)."""
-    lib().orc_set_tp(n)
 
 
 def threads() -> int:

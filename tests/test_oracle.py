@@ -391,7 +391,7 @@ def test_quantized_matmul_within_3pct_of_f32(t):
         x = np.cos(np.arange(m * k, dtype=np.float32) * np.float32(0.021)).astype(np.float32)
         ref = (x.reshape(m, k).astype(np.float64) @ dense.T.astype(np.float64)).astype(np.float32)
         got = np.zeros(m * n, np.float32)
-        assert lib.orc_matmul_fused(m, k, n, O.ptr(x), O.ptr(w), w.size, t, O.ptr(got)) == 0
+        assert lib.orc_matmul_auto(m, k, n, O.ptr(x), O.ptr(w), w.size, t, O.ptr(got)) == 0
         # the byte pattern gives some blocks NaN/Inf scales; the reference's
         # folds with f32::max skip NaN, and so do these
         with np.errstate(invalid="ignore"):
@@ -430,3 +430,121 @@ def test_cache_prefix_copies_first_tokens_and_equals_truncate(tmp_path):
     np.testing.assert_array_equal(m.forward(pre, [9, 1, 4]), m.forward(O.Cache(m), [7, 3, 9, 1, 4]))
     c.clear()
     assert len(c) == 0
+
+
+# ── matmul_auto's dispatch (src/ops.rs:1056-1093, :837-858, :599-606) ──
+
+def test_matmul_path_follows_matmul_auto_on_each_backend():
+    F, B, BL, F32 = O.PATH_FUSED, O.PATH_BUFFERED, O.PATH_BLOCKED, O.PATH_F32
+    # COSXAMIX_KERNEL=escalar: only Q4_K and Q3_K have a fused kernel in use;
+    # Q3_K's is taken up to 4 rows, Q4_K's below the blocked threshold; the
+    # blocked path needs AVX2, so from 24 rows every format is buffered
+    scalar = {
+        O.Q4K: {1: F, 4: F, 5: F, 23: F, 24: B, 512: B},
+        O.Q3K: {1: F, 4: F, 5: B, 23: B, 24: B},
+        O.Q6K: {1: B, 4: B, 5: B, 24: B},
+        O.Q5K: {1: B, 24: B},
+        O.Q2K: {1: B, 24: B},
+        O.F32: {1: F32, 24: F32},
+        O.F16: {1: F32, 37: F32},
+    }
+    x86 = {
+        O.Q4K: {1: F, 23: F, 24: BL, 512: BL},
+        O.Q3K: {1: F, 4: F, 5: B, 24: BL},
+        O.Q6K: {1: F, 4: F, 5: B, 23: B, 24: BL},
+        O.Q5K: {1: F, 5: B, 24: BL},
+        O.Q2K: {1: F, 4: F, 5: B, 24: BL},
+    }
+    for backend, table in (("scalar", scalar), ("x86", x86)):
+        O.set_backend(backend)
+        try:
+            for t, rows in table.items():
+                for m, want in rows.items():
+                    assert O.matmul_path(m, 2048, t) == want, (backend, t, m)
+        finally:
+            O.set_backend("scalar")
+
+
+def _pattern_weights(t, n, k):
+    """The reference tests' byte pattern (i*97+29)%251 (src/ops.rs:1536-1540);
+    Q8_0 as its identity-plus-pattern helper (:1526-1534, :1336-1351)."""
+    if t == O.Q8_0:
+        b = np.zeros(n * (k // 32) * 34, np.uint8)
+        for r in range(n):
+            for bl in range(k // 32):
+                o = (r * (k // 32) + bl) * 34
+                b[o:o + 2] = np.frombuffer(np.uint16(0x3C00).tobytes(), np.uint8)
+                for j in range(32):
+                    b[o + 2 + j] = 1 if bl * 32 + j == r else 0
+        i = np.arange(b.size)
+        body = (i % 34) >= 2
+        b[body] = (((i[body] * 29) % 253) - 126).astype(np.int8).view(np.uint8)
+        return b
+    return ((np.arange(n * k // 256 * O.BLOCK_BYTES[t]) * 97 + 29) % 251).astype(np.uint8)
+
+
+@pytest.mark.parametrize("t", [O.Q3K, O.Q4K, O.Q5K, O.Q6K, O.Q2K, O.Q8_0])
+def test_blocked_matches_buffered(t):
+    # src/ops.rs:1517-1561 `por_bloques_coincide_con_el_de_buffer`: the AVX2
+    # blocked path and the buffered one agree within 1e-4 of the buffered
+    # result's largest magnitude; 37 rows leave a partial 4-row tile, 70 and
+    # 71 columns a last tramo of 6 and 7
+    k = 512
+    O.set_backend("x86")
+    try:
+        for n in (70, 71):
+            w = _pattern_weights(t, n, k)
+            for m in (4, 37):
+                x = np.cos(np.arange(m * k, dtype=np.float32) * np.float32(0.021)).astype(np.float32)
+                buf = O.matmul(x, w, t, k, n, path=O.PATH_BUFFERED)
+                blk = O.matmul(x, w, t, k, n, path=O.PATH_BLOCKED)
+                with np.errstate(invalid="ignore"):
+                    scale = float(np.nanmax(np.abs(buf)))
+                    worst = float(np.nanmax(np.abs(buf - blk)))
+                assert worst <= scale * 1e-4, (t, m, n, worst, scale)
+                np.testing.assert_array_equal(np.isnan(buf), np.isnan(blk))
+    finally:
+        O.set_backend("scalar")
+
+
+@pytest.mark.parametrize("t", [O.Q2K, O.Q3K, O.Q4K, O.Q5K, O.Q6K])
+def test_buffered_row_is_unpack_then_scaled_dot_then_offsets(t):
+    # src/ops.rs:383-405 restated from its parts: dot_i8_escalado of the
+    # unpacked row, then des*xe*xs per sub-block when any des is nonzero
+    from tests.golden.make_golden import finite_row
+    rng = np.random.default_rng(t)
+    nb = 8
+    row = finite_row(rng, t, nb)
+    x = rng.standard_normal(nb * 256).astype(np.float32)
+    sub = O.SUB[t]
+    xq, xe, xs = O.quantize_i8(x, sub)
+    q, esc, des = O.unpack_i8(t, row, nb * 256)
+    total = np.float32(0.0)
+    for b in range(nb * 256 // sub):
+        part = int(np.dot(q[b * sub:(b + 1) * sub].astype(np.int32), xq[b * sub:(b + 1) * sub].astype(np.int32)))
+        total = np.float32(total + np.float32(np.float32(esc[b] * xe[b]) * np.float32(part)))
+    if np.any(des != 0):
+        for b in range(nb * 256 // sub):
+            total = np.float32(total + np.float32(np.float32(des[b] * xe[b]) * xs[b]))
+    assert O.dot_row_buffered(t, row, xq, xe, xs) == total
+    # the fused kernel forms the same integer sums: within the reference's 1e-4
+    fused = O.dot_row(t, row, xq, xe, xs)
+    assert abs(fused - total) <= 1e-4 * max(abs(total), 1.0)
+
+
+def test_scalar_prompt_paths_agree_within_float_order(tmp_path):
+    # A prompt of 24+ tokens takes the buffered path for every matrix and a
+    # shorter one the fused path for Q4_K: the same integer sums in another
+    # float order, so the KV rows agree closely but not bit for bit
+    import cosxamix_b200 as cx
+    p = str(tmp_path / "tiny.gguf")
+    cx.synth_write(p, cx.synth_spec("tiny", seed=42, n_layer=2))
+    m = O.Model(p)
+    prompt = [(i * 37 + 11) % 8192 for i in range(24)]
+    whole = O.Cache(m)
+    a = m.forward(whole, prompt)
+    split = O.Cache(m)
+    m.forward(split, prompt[:12])
+    b = m.forward(split, prompt[12:])
+    assert float(np.max(np.abs(a - b)) / (a.max() - a.min())) <= 1e-2
+    assert not np.array_equal(whole.layer(1, False), split.layer(1, False))

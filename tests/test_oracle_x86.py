@@ -175,7 +175,7 @@ def test_x86_forward_close_to_scalar_and_scalar_untouched(tmp_path):
 
 def _matmul(x, w, t, k, n):
     out = np.zeros(n, np.float32)
-    assert O.lib().orc_matmul_fused(1, k, n, O.ptr(x), O.ptr(w), w.size, t, O.ptr(out)) == 0
+    assert O.lib().orc_matmul_auto(1, k, n, O.ptr(x), O.ptr(w), w.size, t, O.ptr(out)) == 0
     return out
 
 
