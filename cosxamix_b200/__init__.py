@@ -39,7 +39,8 @@ class Config(C.Structure):
 class SynthSpec(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("vocab", "dim", "n_layer", "n_head", "n_head_kv", "ffn", "ctx")] + [
         ("eps", C.c_float), ("rope_base", C.c_float), ("tied", C.c_int32), ("mix", C.c_int32), ("type", C.c_int32),
-        ("seed", C.c_uint64), ("sigma", C.c_float), ("threads", C.c_int32)]
+        ("seed", C.c_uint64), ("sigma", C.c_float), ("threads", C.c_int32), ("has_eos", C.c_int32),
+        ("eos", C.c_uint32)]
 
 
 def lib() -> C.CDLL:
@@ -59,6 +60,7 @@ def lib() -> C.CDLL:
                                             C.POINTER(C.c_int)]),
             "cxm_model_config": (C.c_int, [P, C.POINTER(Config)]),
             "cxm_model_weight_bytes": (C.c_uint64, [P]),
+            "cxm_model_set_prefill": (C.c_int, [P, C.c_int]),
             "cxm_model_close": (None, [P]),
             "cxm_cache_new": (C.c_int, [P, C.c_uint32, C.POINTER(P)]),
             "cxm_cache_free": (None, [P]),
@@ -134,10 +136,13 @@ CONFIGS = {
 }
 
 
-def synth_spec(name: str = "tiny", seed: int = 42, sigma: float = 0.02, threads: int = 0, **over) -> SynthSpec:
+def synth_spec(name: str = "tiny", seed: int = 42, sigma: float = 0.02, threads: int = 0, eos: int | None = None,
+               **over) -> SynthSpec:
+    """`eos`: write tokenizer.ggml.eos_token_id (the benchmark models have
+    none, so generation never stops early)."""
     cfg = dict(CONFIGS[name])
     cfg.update(over)
-    return SynthSpec(seed=seed, sigma=sigma, threads=threads, **cfg)
+    return SynthSpec(seed=seed, sigma=sigma, threads=threads, has_eos=int(eos is not None), eos=eos or 0, **cfg)
 
 
 def synth_write(path: str, spec: SynthSpec) -> str:
@@ -272,6 +277,11 @@ class Modelo:
     @property
     def weight_bytes(self) -> int:
         return lib().cxm_model_weight_bytes(self.h)
+
+    def set_prefill(self, tensor_cores: bool) -> None:
+        """Prompts of 24+ tokens on the tensor cores (default) or replayed
+        through the decode step; the same results either way."""
+        _check(lib().cxm_model_set_prefill(self.h, int(tensor_cores)))
 
     def cache(self, max_tokens: int | None = None) -> Cache:
         return Cache(self, max_tokens)

@@ -187,7 +187,7 @@ struct AtPhase {
     const float *q, *k, *v;  // k/v: this layer's cache, [max_pos][KV*hd]
     float *out, *scores;
     int H, KV, hd, score_stride, P;  // P: positions per score item
-    int dims;                        // output dims per attention item
+    int ring;                        // V chunks in the attention phase's ring
     float scale;
 };
 
@@ -257,6 +257,8 @@ struct DecodeArgs {
     unsigned long long *argmax_key;
     const float *rope_cos, *rope_sin;
     int write_token, commit;  // commit: toks[len+1] = argmax (write_token), len += 1
+    int *d_stop;              // set: the generation met its eos and the step does nothing (NULL: never)
+    int eos;                  // the token whose greedy pick sets *d_stop, or -1
     int ring_slots;           // tile slots per warp ring (2..kMaxSlots)
     uint32_t slot_bytes, region_bytes;
 };
@@ -717,7 +719,19 @@ __device__ __forceinline__ void cp_async_wait_n(int n) {
     case 0: cp_async_wait<0>(); break;
     case 1: cp_async_wait<1>(); break;
     case 2: cp_async_wait<2>(); break;
-    default: cp_async_wait<3>(); break;
+    case 3: cp_async_wait<3>(); break;
+    case 4: cp_async_wait<4>(); break;
+    case 5: cp_async_wait<5>(); break;
+    case 6: cp_async_wait<6>(); break;
+    case 7: cp_async_wait<7>(); break;
+    case 8: cp_async_wait<8>(); break;
+    case 9: cp_async_wait<9>(); break;
+    case 10: cp_async_wait<10>(); break;
+    case 11: cp_async_wait<11>(); break;
+    case 12: cp_async_wait<12>(); break;
+    case 13: cp_async_wait<13>(); break;
+    case 14: cp_async_wait<14>(); break;
+    default: cp_async_wait<15>(); break;
     }
 }
 
@@ -876,38 +890,64 @@ __device__ void phase_xargmax(const DecodeArgs &A, unsigned ep, volatile int *ab
 }
 
 // ── attention phases (src/ops.rs:1258-1325), reference order ──
-// the attention phase's V ring: 8 chunks of 2048 floats (128 positions at
-// 16 dims per item, 64 at 32)
-constexpr int kAttnVRing = 8, kAttnVChunkFloats = 2048;
-__host__ __device__ inline int attn_chunk(int dims) { return kAttnVChunkFloats / dims; }
-
+// An attention item is one head and 32 of its output dims. Its region: the
+// head's probabilities (max_pos rounded to 4 floats), then a ring of `ring`
+// V chunks, each kAttnPos positions of the item's 32 dims stored transposed
+// ([dim][position], rows of kAttnPos + 1 floats: the odd row length keeps
+// both the transposing 4-byte copies and the position-by-position reads free
+// of bank conflicts).
+constexpr int kAttnPos = 128, kAttnMinRing = 3, kAttnMaxRing = 8;
+constexpr int kAttnChunkFloats = 32 * (kAttnPos + 1);
 __host__ __device__ inline size_t scores_region(int P, int G, int hd) {
     return ((size_t)P * (hd + 4) + (size_t)G * hd) * sizeof(float);
 }
-// dims: output dims per work item (16 or 32, dividing head_dim)
-__host__ __device__ inline size_t attn_region(int max_pos, int dims) {
-    (void)dims;
-    return ((size_t)((max_pos + 3) & ~3) + (size_t)kAttnVRing * kAttnVChunkFloats) * sizeof(float);
+__host__ __device__ inline size_t attn_region(int max_pos, int ring) {
+    return ((size_t)((max_pos + 3) & ~3) + (size_t)ring * kAttnChunkFloats) * sizeof(float);
+}
+
+// positions per score item of a step over n positions: enough items for
+// every CTA, at most at.P (the region's capacity)
+__device__ __forceinline__ int score_span(const AtPhase &at, int n) {
+    const int want = (at.KV * n + gridDim.x - 1) / gridDim.x;
+    return want < 1 ? 1 : (want > at.P ? at.P : want);
+}
+
+// Before the scores phase's grid barrier: the K rows of this CTA's first
+// item that are already in the cache (every position but the step's own,
+// which the q|k|v phase is writing), as one cp.async group.
+__device__ __forceinline__ void scores_prefetch(const AtPhase &at, int n, float *region) {
+    const int tid = threadIdx.x, hd = at.hd, kvd = at.KV * hd, c4 = hd / 4;
+    const int P = score_span(at, n), nchunk = (n + P - 1) / P, items = at.KV * nchunk;
+    const int item = blockIdx.x;
+    if (item < items) {
+        const int g = item / nchunk, p0 = (item % nchunk) * P, cnt = min(P, n - 1 - p0);  // not position n-1
+        for (int i = tid; i < cnt * c4; i += kDW * 32) {
+            const int r = i / c4, c = i - r * c4;
+            cp_async16(region + r * (hd + 4) + 4 * c, at.k + (size_t)(p0 + r) * kvd + (size_t)g * hd + 4 * c);
+        }
+    }
+    cp_async_commit();
 }
 
 // score[h][p] = (sequential dot of q_h and k_p over the head dim) · scale; an
 // item is one kv head and P positions, shared by the G query heads on it
+// (the first item's cached K rows were staged by scores_prefetch)
 __device__ __forceinline__ void phase_scores(const AtPhase &at, int n, float *region) {
     const int tid = threadIdx.x, hd = at.hd, G = at.H / at.KV, kvd = at.KV * hd, c4 = hd / 4;
-    // positions per item: enough items for every CTA, at most at.P (the
-    // region's capacity)
-    const int want = (at.KV * n + gridDim.x - 1) / gridDim.x;
-    const int P = want < 1 ? 1 : (want > at.P ? at.P : want);
-    const int nchunk = (n + P - 1) / P, items = at.KV * nchunk;
+    const int P = score_span(at, n), nchunk = (n + P - 1) / P, items = at.KV * nchunk;
     float *ks = region, *qs = region + (size_t)at.P * (hd + 4);
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int g = item / nchunk, p0 = (item % nchunk) * P, cnt = min(P, n - p0);
+        const bool first = item == (int)blockIdx.x;
         for (int i = tid; i < G * c4; i += kDW * 32) {
             const int hq = i / c4, c = i - hq * c4;
             cp_async16(qs + hq * hd + 4 * c, at.q + (size_t)(g * G + hq) * hd + 4 * c);
         }
-        for (int i = tid; i < cnt * c4; i += kDW * 32) {
-            const int r = i / c4, c = i - r * c4;
+        // the rows the prefetch did not stage: the step's own position (the
+        // first item), or all (a later item)
+        const int r0 = first ? (n - 1 >= p0 && n - 1 < p0 + cnt ? n - 1 - p0 : cnt) : 0;
+        for (int i = tid; i < (cnt - r0) * c4; i += kDW * 32) {
+            const int r = r0 + i / c4, c = i % c4;
             cp_async16(ks + r * (hd + 4) + 4 * c, at.k + (size_t)(p0 + r) * kvd + (size_t)g * hd + 4 * c);
         }
         cp_async_commit();
@@ -963,114 +1003,116 @@ __device__ __forceinline__ float seq_sum(const float *p, int n) {
     return acc;
 }
 
-// softmax over a head's scores (subtract the max, exp, sum position by
-// position, multiply by 1/total; src/ops.rs:1206-1230), then
-// out[d] = Σ_p prob_p·v_p[d] added position by position; an item is one head
-// and `dims` of its output dims (16 or 32)
-__device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region, float *fred, float *fbc) {
-    const int tid = threadIdx.x, nt = kDW * 32, hd = at.hd, G = at.H / at.KV, kvd = at.KV * hd;
-    const int dims = at.dims, nslice = hd / dims, items = at.H * nslice, cpos = attn_chunk(dims);
-    float *pr = region;
-    float *vs = region + ((max_pos + 3) & ~3);
-    const int nchunks = (n + cpos - 1) / cpos;
-    for (int item = blockIdx.x; item < items; item += gridDim.x) {
-        const int h = item / nslice, d0 = (item % nslice) * dims, g = h / G;
-        const float *sc = at.scores + (size_t)h * at.score_stride;
-        const float *vb = at.v + (size_t)g * hd + d0;
-        auto stage = [&](int c) {
-            if (c >= nchunks) return;
-            const int base = c * cpos, cnt = min(cpos, n - base);
-            float *dst = vs + (c % kAttnVRing) * cpos * dims;
-            const int d4 = dims / 4;
-            for (int i = tid; i < cnt * d4; i += nt) {
-                const int r = i / d4, q = i - r * d4;
-                cp_async16(dst + r * dims + 4 * q, vb + (size_t)(base + r) * kvd + 4 * q);
-            }
-        };
-        for (int i = tid; i < (n + 3) / 4; i += nt) cp_async16(pr + 4 * i, sc + 4 * i);
+// One attention item: head h and dims [d0, d0 + 32) (src/ops.rs:1258-1325).
+// The head's scores staged in shared memory; their max, exp(s - max)
+// (src/ops.rs:1206-1230) and the products by 1/total across the CTA; the sum
+// position by position by thread 0; then warp 0 adds prob_p·v_p[d] position
+// by position, lane d for dim d0 + d, over the transposed V chunks.
+
+// V chunk c of an item into its ring slot, transposed (the caller commits
+// the cp.async group)
+__device__ __forceinline__ void attn_stage(const AtPhase &at, int n, const float *vb, float *ring, int c) {
+    const int tid = threadIdx.x, kvd = at.KV * at.hd;
+    if (c * kAttnPos >= n) return;
+    const int base = c * kAttnPos, cnt = min(kAttnPos, n - base);
+    float *dst = ring + (c % at.ring) * kAttnChunkFloats;
+    for (int i = tid; i < cnt * 32; i += kDW * 32) {
+        const int p = i >> 5, d = i & 31;
+        cp_async4(dst + d * (kAttnPos + 1) + p, vb + (size_t)(base + p) * kvd + d);
+    }
+}
+
+__device__ __forceinline__ const float *attn_vbase(const AtPhase &at, int item) {
+    const int ns = at.hd / 32, h = item / ns, G = at.H / at.KV;
+    return at.v + (size_t)(h / G) * at.hd + (item % ns) * 32;
+}
+
+// Before the attention phase's grid barrier: the first ring - 1 V chunks of
+// this CTA's first item (the V rows of every position are in the cache once
+// the scores phase began), one cp.async group each.
+__device__ __forceinline__ void attn_prefetch(const AtPhase &at, int n, int max_pos, float *region) {
+    const int items = at.H * (at.hd / 32), item = blockIdx.x;
+    float *ring = region + ((max_pos + 3) & ~3);
+    for (int c = 0; c < at.ring - 1; c++) {
+        if (item < items) attn_stage(at, n, attn_vbase(at, item), ring, c);
         cp_async_commit();
-        for (int c = 0; c < kAttnVRing - 1; c++) {
-            stage(c);
-            cp_async_commit();
-        }
-        cp_async_wait<kAttnVRing - 1>();
+    }
+}
+
+__device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region, float *red,
+                                           float *bc) {
+    const int tid = threadIdx.x, nt = kDW * 32, lane = tid & 31, warp = tid >> 5, hd = at.hd, ns = hd / 32;
+    const int items = at.H * ns, R = at.ring;
+    float *pr = region;
+    float *ring = region + ((max_pos + 3) & ~3);
+    const int nchunks = (n + kAttnPos - 1) / kAttnPos;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int h = item / ns, d0 = (item % ns) * 32;
+        const float *vb = attn_vbase(at, item);
+        if (item != (int)blockIdx.x)  // the first item's first chunks were staged before the barrier
+            for (int c = 0; c < R - 1; c++) {
+                attn_stage(at, n, vb, ring, c);
+                cp_async_commit();
+            }
+        const int n4 = (n + 3) / 4;
+        for (int i = tid; i < n4; i += nt)
+            ((float4 *)pr)[i] = __ldcg((const float4 *)(at.scores + (size_t)h * at.score_stride) + i);
         dsync();
         float m = -INFINITY;
         for (int i = tid; i < n; i += nt) m = fmaxf(m, pr[i]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if ((tid & 31) == 0) fred[tid >> 5] = m;
+        if (lane == 0) red[warp] = m;
         dsync();
-        if (tid == 0) {
-            float mm = -INFINITY;
-            for (int w = 0; w < kDW; w++) mm = fmaxf(mm, fred[w]);
-            *fbc = mm;
-        }
-        dsync();
-        const float mx = *fbc;
-        dsync();
-        if (!isfinite(mx)) {
+        float mx = red[0];
+        for (int w = 1; w < kDW; w++) mx = fmaxf(mx, red[w]);
+        if (!isfinite(mx)) {  // every score -inf (or NaN): uniform (src/ops.rs:1213-1218)
             const float u = __fdiv_rn(1.0f, (float)n);
             for (int i = tid; i < n; i += nt) pr[i] = u;
         } else {
             for (int i = tid; i < n; i += nt) pr[i] = expf_glibc(fs(pr[i], mx));
             dsync();
-            if (tid == 0) *fbc = __fdiv_rn(1.0f, seq_sum(pr, n));
+            if (tid == 0) *bc = __fdiv_rn(1.0f, seq_sum(pr, n));
             dsync();
-            const float inv = *fbc;
+            const float inv = *bc;
             for (int i = tid; i < n; i += nt) pr[i] = fm(pr[i], inv);
         }
         dsync();
         float acc = 0.0f;
         for (int c = 0; c < nchunks; c++) {
-            stage(c + kAttnVRing - 1);
+            attn_stage(at, n, vb, ring, c + R - 1);
             cp_async_commit();
-            cp_async_wait<kAttnVRing - 1>();
+            cp_async_wait_n(R - 1);
             dsync();
-            if (tid < dims) {
-                // 16 positions per step, the next step's probabilities and V
-                // values loaded while this step's products are added in order
-                const float *src = vs + (c % kAttnVRing) * cpos * dims + tid;
-                const int base = c * cpos, cnt = min(cpos, n - base);
+            if (warp == 0) {
+                const float *vt = ring + (c % R) * kAttnChunkFloats + lane * (kAttnPos + 1);
+                const int base = c * kAttnPos, cnt = min(kAttnPos, n - base);
                 const float *pp = pr + base;
-                float np[16], nv[16];
-                if (16 <= cnt) {
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        const float4 q = ((const float4 *)pp)[k];
-                        np[4 * k] = q.x; np[4 * k + 1] = q.y; np[4 * k + 2] = q.z; np[4 * k + 3] = q.w;
-                    }
-#pragma unroll
-                    for (int k = 0; k < 16; k++) nv[k] = src[k * dims];
-                }
                 int r = 0;
                 for (; r + 16 <= cnt; r += 16) {
-                    float cp[16], cv[16];
+                    float4 q[4];
+                    float w[16];
 #pragma unroll
-                    for (int k = 0; k < 16; k++) {
-                        cp[k] = np[k];
-                        cv[k] = nv[k];
+                    for (int k = 0; k < 4; k++) q[k] = ((const float4 *)(pp + r))[k];
+#pragma unroll
+                    for (int k = 0; k < 16; k++) w[k] = vt[r + k];
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        acc = fa(acc, fm(q[k].x, w[4 * k]));
+                        acc = fa(acc, fm(q[k].y, w[4 * k + 1]));
+                        acc = fa(acc, fm(q[k].z, w[4 * k + 2]));
+                        acc = fa(acc, fm(q[k].w, w[4 * k + 3]));
                     }
-                    if (r + 32 <= cnt) {
-#pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            const float4 q = ((const float4 *)(pp + r + 16))[k];
-                            np[4 * k] = q.x; np[4 * k + 1] = q.y; np[4 * k + 2] = q.z; np[4 * k + 3] = q.w;
-                        }
-#pragma unroll
-                        for (int k = 0; k < 16; k++) nv[k] = src[(r + 16 + k) * dims];
-                    }
-#pragma unroll
-                    for (int k = 0; k < 16; k++) acc = fa(acc, fm(cp[k], cv[k]));
                 }
-                for (; r < cnt; r++) acc = fa(acc, fm(pp[r], src[r * dims]));
+                for (; r < cnt; r++) acc = fa(acc, fm(pp[r], vt[r]));
             }
             dsync();
         }
-        if (tid < dims) at.out[(size_t)h * hd + d0 + tid] = acc;
+        if (warp == 0) at.out[(size_t)h * hd + d0 + lane] = acc;
         cp_async_wait<0>();
         dsync();
     }
+    cp_async_wait<0>();  // a CTA without an item drains its (empty) prefetch groups
 }
 
 // ── a warp's tile ring ──
@@ -1210,7 +1252,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
     __shared__ unsigned long long best_s[kDW];
     __shared__ float fred[kDW];
     __shared__ float fbc;
-    __shared__ int pos_s, tok_s, bad_s;
+    __shared__ int pos_s, tok_s, bad_s, stopped_s;
     __shared__ unsigned xbase_s;  // exchanges completed before this launch
     // deferred epilogues: (segment, unit, y0, y1) per output unit, per warp
     __shared__ int2 epi_su[kDW][32];
@@ -1237,6 +1279,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         pos_s = p;
         tok_s = (int)t;
         bad_s = bad;
+        // a generation that met its eos: read before the first grid barrier,
+        // so before this launch's own commit can set it
+        stopped_s = A.d_stop ? *(volatile int *)A.d_stop : 0;
         // read before the first grid barrier, so before CTA 0's commit updates it
         xbase_s = A.epoch ? *(volatile unsigned *)A.epoch : 0u;
     }
@@ -1244,9 +1289,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
     for (int i = tid; i < A.nfeed * 4; i += kDecodeThreads) ((uint4 *)ftab)[i] = __ldg((const uint4 *)A.feed + i);
     __syncthreads();
 
-    // an invalid position or token stops every CTA before any work
+    // an invalid position or token stops every CTA before any work; so does
+    // a generation that already met its eos (src/forward.rs:544-547)
     const int pos = pos_s;
     const uint32_t tok = (uint32_t)tok_s;
+    if (stopped_s) return;
     if (bad_s) {
         if (blockIdx.x == 0 && tid == 0) atomicOr(A.err, bad_s);
         return;
@@ -1282,11 +1329,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         // a normed matvec's weights depend on nothing: loaded before the barrier
         NormW nw;
         if (ph.kind == PH_MATVEC && ph.mv.prologue != PRO_QUANT) load_norm_w(ph.mv, nw);
+        const int n = pos + 1;
+        // what an attention phase reads from before this step lands in shared
+        // memory while the CTA waits at the barrier
+        if (ph.kind == PH_SCORES) scores_prefetch(ph.at, n, (float *)region);
+        else if (ph.kind == PH_ATTN) attn_prefetch(ph.at, n, A.max_pos, (float *)region);
         if (ph.barrier) {
             nbar++;
             if (!grid_sync(A, nbar * gridDim.x, &abort_flag, &sync_ok)) break;  // uniform
         }
-        const int n = pos + 1;
         if (ph.kind == PH_MATVEC) {
             const MvPhase &P = ph.mv;
             const Act act = carve_act(region, P.K, P.need16, P.need32);
@@ -1413,8 +1464,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         } else if (ph.kind == PH_COMMIT) {
             if (blockIdx.x == 0 && tid == 0) {
                 if (A.d_len) {
-                    if (A.write_token && A.argmax_key && pos + 1 < A.max_pos + 1)
-                        A.toks[pos + 1] = argmax_index(__ldcg(A.argmax_key));
+                    if (A.write_token && A.argmax_key && pos + 1 < A.max_pos + 1) {
+                        const uint32_t pick = argmax_index(__ldcg(A.argmax_key));
+                        A.toks[pos + 1] = pick;
+                        if (A.d_stop && A.eos >= 0 && pick == (uint32_t)A.eos) *A.d_stop = 1;
+                    }
                     if (A.commit) *(volatile int *)A.d_len = pos + 1;
                 }
                 if (A.epoch) *A.epoch = xbase_s + (unsigned)A.nx;

@@ -49,7 +49,9 @@ namespace cxm {
      0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull}
 
 #ifdef __CUDACC__
-__device__ __constant__ uint64_t kExp2TabDev[32] = CXM_EXP2_TABLE;
+// global memory read through the read-only cache: the lanes of a warp index
+// it differently, which constant memory would serialize
+__device__ const uint64_t kExp2TabDev[32] = CXM_EXP2_TABLE;
 #endif
 static const uint64_t kExp2TabHost[32] = CXM_EXP2_TABLE;
 
@@ -114,7 +116,7 @@ CXM_HD float expf_glibc(float x) {
     kd = add_d(kd, -kShift);
     const double r = fma_d(kInvLn2N, (double)x, -kd);
 #ifdef __CUDA_ARCH__
-    uint64_t t = kExp2TabDev[ki % 32];
+    uint64_t t = __ldg(&kExp2TabDev[ki % 32]);
 #else
     uint64_t t = kExp2TabHost[ki % 32];
 #endif

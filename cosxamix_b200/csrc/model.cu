@@ -17,6 +17,7 @@
 #include "../../include/cxm.h"
 #include "cxm_internal.h"
 #include "decode.cuh"
+#include "prefill.cuh"
 #include "sampler.cuh"
 
 using namespace cxm;
@@ -74,12 +75,33 @@ struct cxm_model {
     uint32_t slot_bytes = 0;  // largest quad tile of the model
     uint64_t weight_bytes = 0;
     bool logits_valid = false;
+    // pinned host copies of the error word and the argmax key, read back
+    // together after each step sequence (one host synchronisation)
+    struct HostWords {
+        int err, pad;
+        unsigned long long key;
+    } *hw = nullptr;
+    bool key_valid = false;  // hw->key holds the last forward's greedy pick
+    // the prompt forward on the tensor cores (forward calls of 24+ tokens);
+    // off: those tokens replay the decode step one by one, with the same results
+    bool prefill_tc = true;
+    struct Prefill {  // its scratch, allocated at the first such call
+        int cap = 0;  // tokens per chunk
+        float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *scores = nullptr;
+        int8_t *a16 = nullptr, *a32 = nullptr;
+        float *e16 = nullptr, *s16 = nullptr, *e32 = nullptr, *s32 = nullptr;
+        size_t score_floats = 0;
+    } pf;
 
     ~cxm_model() {
         if (device >= 0) cudaSetDevice(device);
         for (int p = 0; p < kTpMax; p++)
             if (peer_mapped[p]) cudaIpcCloseMemHandle(peer[p]);
         for (void *p : allocs) cudaFree(p);
+        for (void *p : {(void *)pf.x, (void *)pf.q, (void *)pf.att, (void *)pf.h, (void *)pf.scores, (void *)pf.a16,
+                        (void *)pf.a32, (void *)pf.e16, (void *)pf.s16, (void *)pf.e32, (void *)pf.s32})
+            cudaFree(p);
+        if (hw) cudaFreeHost(hw);
         if (stream) cudaStreamDestroy(stream);
     }
     template <class T>
@@ -113,6 +135,7 @@ struct cxm_cache {
     float *k = nullptr, *v = nullptr;  // [n_layer][max_tokens][kvd]
     uint32_t *toks = nullptr;          // [max_tokens + 2]
     int *d_len = nullptr;
+    int *d_stop = nullptr;             // set by a step whose pick is the model's eos
     // one program and one graph per step mode and row class (RowClass)
     Program prog[4][3];
     cudaGraphExec_t graph[4][3] = {};
@@ -127,6 +150,7 @@ struct cxm_cache {
         cudaFree(v);
         cudaFree(toks);
         cudaFree(d_len);
+        cudaFree(d_stop);
     }
 };
 
@@ -426,18 +450,201 @@ int set_kernel_smem_limits() {
     CU(cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     CU(cudaFuncSetAttribute(k_attn_out, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     CU(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kScanChunk * (int)sizeof(float)));
+    CU(cudaFuncSetAttribute(k_pf_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     return 0;
 }
 
-// src/ops.rs:1258-1325 for the token at *d_len, over positions 0..=*d_len
-int launch_attention_on(cudaStream_t st, AttnParams &a) {
-    const dim3 gs(a.H, (a.max_pos + kScoreThreads - 1) / kScoreThreads), go(a.H, (a.hd + kOutDims - 1) / kOutDims);
+// src/ops.rs:1258-1325 for the token at *d_len (or tokens pos0.. pos0+tokens-1),
+// over positions 0..=that one
+int launch_attention_on(cudaStream_t st, AttnParams &a, int tokens = 1) {
+    const dim3 gs(a.H, (a.max_pos + kScoreThreads - 1) / kScoreThreads, tokens);
+    const dim3 go(a.H, (a.hd + kOutDims - 1) / kOutDims, tokens);
     if (launch_pdl(k_attn_scores, gs, dim3(kScoreThreads), scores_smem(a.hd), st, a)) return -1;
     return launch_pdl(k_attn_out, go, dim3(kOutThreads), out_smem((uint32_t)a.max_pos), st, a);
 }
 
+// ── the prompt forward on the tensor cores (prefill.cuh) ──
+__global__ void k_set_int(int *p, int v) { *p = v; }
+MvSeg mv_seg(const QMat &M, int units, int pairing, int epi, float *out, int cls = ROWS_FEW);
+int run_steps(cxm_model *m, cxm_cache *c, int mode, uint64_t rows, uint32_t n);
+
+// i8 quantization (RMSNorm first when norm_w is given) of `t` rows of `in`
+// into the prefill scratch's operand tiles
+int pf_rows(cxm_model *m, const float *in, int ld, const float *norm_w, float eps, int K, int t, int need16,
+            int need32) {
+    PfRows P{};
+    P.in = in;
+    P.ld_in = ld;
+    P.norm_w = norm_w;
+    P.eps = eps;
+    P.K = K;
+    P.tokens = t;
+    P.need16 = need16;
+    P.need32 = need32;
+    P.a16 = m->pf.a16;
+    P.a32 = m->pf.a32;
+    P.e16 = m->pf.e16;
+    P.s16 = m->pf.s16;
+    P.e32 = m->pf.e32;
+    P.s32 = m->pf.s32;
+    k_pf_rows<<<t, kDecodeThreads, 0, m->stream>>>(P);
+    CU(cudaGetLastError());
+    return 0;
+}
+
+// out = W·x for the t rows quantized last, each output in the buffered
+// path's order, then the segment's epilogue (tokens at positions pos0..)
+int pf_gemm(cudaStream_t st, const MvSeg &seg, int t, int pos0, int ld_out, const int8_t *a16, const int8_t *a32,
+            const float *e16, const float *s16, const float *e32, const float *s32, const float *rc, const float *rs,
+            int *err) {
+    const int sub = sub_of(seg.M.type), N = pf_rows_per_tile(sub);
+    PfGemm G{};
+    G.seg = seg;
+    G.tokens = t;
+    G.pos0 = pos0;
+    G.a = sub == 32 ? a32 : a16;
+    G.xe = sub == 32 ? e32 : e16;
+    G.xs = sub == 32 ? s32 : s16;
+    G.nsub = seg.M.K / sub;
+    G.ld_out = ld_out;
+    G.rope_cos = rc;
+    G.rope_sin = rs;
+    G.err = err;
+    const PfSmem L = pf_smem(seg.M.type, seg.M.K);
+    // at least 116 KB, so no two of these CTAs share an SM (each takes all 512 TMEM columns)
+    const size_t smem = std::max<size_t>(L.total + 128, 116 * 1024);
+    const dim3 grid((seg.M.rows + N - 1) / N, (t + kPfM - 1) / kPfM);
+    k_pf_gemm<<<grid, kPfThreads, smem, st>>>(G);
+    CU(cudaGetLastError());
+    return 0;
+}
+
+int pf_reserve(cxm_model *m, int cap) {
+    if (m->pf.cap >= cap) return 0;
+    for (void *p : {(void *)m->pf.x, (void *)m->pf.q, (void *)m->pf.att, (void *)m->pf.h, (void *)m->pf.scores,
+                    (void *)m->pf.a16, (void *)m->pf.a32, (void *)m->pf.e16, (void *)m->pf.s16, (void *)m->pf.e32,
+                    (void *)m->pf.s32})
+        cudaFree(p);
+    m->pf = cxm_model::Prefill{};
+    const cxm_config &cfg = m->cfg;
+    const int kmax = std::max(std::max(cfg.dim, cfg.ffn), m->h_loc * cfg.head_dim);
+    m->pf.score_floats = (size_t)16 << 20;  // 64 MB of attention scores per launch
+    CU(cudaMalloc(&m->pf.x, (size_t)cap * cfg.dim * 4));
+    CU(cudaMalloc(&m->pf.q, (size_t)cap * m->h_loc * cfg.head_dim * 4));
+    CU(cudaMalloc(&m->pf.att, (size_t)cap * m->h_loc * cfg.head_dim * 4));
+    CU(cudaMalloc(&m->pf.h, (size_t)cap * cfg.ffn * 4));
+    CU(cudaMalloc(&m->pf.scores, m->pf.score_floats * 4));
+    CU(cudaMalloc(&m->pf.a16, pfa_bytes(cap, kmax)));
+    CU(cudaMalloc(&m->pf.a32, pfa_bytes(cap, kmax)));
+    CU(cudaMemset(m->pf.a16, 0, pfa_bytes(cap, kmax)));
+    CU(cudaMemset(m->pf.a32, 0, pfa_bytes(cap, kmax)));
+    CU(cudaMalloc(&m->pf.e16, (size_t)cap * (kmax / 16) * 4));
+    CU(cudaMalloc(&m->pf.s16, (size_t)cap * (kmax / 16) * 4));
+    CU(cudaMalloc(&m->pf.e32, (size_t)cap * (kmax / 32) * 4));
+    CU(cudaMalloc(&m->pf.s32, (size_t)cap * (kmax / 32) * 4));
+    m->pf.cap = cap;
+    return 0;
+}
+
+int pf_seg_gemm(cxm_model *m, const MvSeg &seg, int t, int pos0, int ld_out) {
+    return pf_gemm(m->stream, seg, t, pos0, ld_out, m->pf.a16, m->pf.a32, m->pf.e16, m->pf.s16, m->pf.e32, m->pf.s32,
+                   m->rope_cos, m->rope_sin, m->err);
+}
+
+// The prompt forward (src/forward.rs:375-492 over several tokens at once)
+// of the tokens at positions p0 .. p0+n-1 of cache c (ids in c->toks): their
+// K/V rows in every layer, as the reference's forward of a call of 24+
+// tokens computes them. The logits are not formed here.
+constexpr int kPrefillChunk = 512;
+int prefill_tokens(cxm_model *m, cxm_cache *c, uint32_t p0, uint32_t n) {
+    const cxm_config &cfg = m->cfg;
+    const int D = cfg.dim, hd = cfg.head_dim, H = m->h_loc, KV = m->kv_loc, F = cfg.ffn, dq = H * hd;
+    const size_t kvd = kv_dim(m);
+    if (pf_reserve(m, kPrefillChunk)) return -1;
+    auto need = [](const QMat &M, int s) { return sub_of(M.type) == s ? 1 : 0; };
+    for (uint32_t q0 = p0; q0 < p0 + n; q0 += kPrefillChunk) {
+        const int t = (int)std::min<uint32_t>(kPrefillChunk, p0 + n - q0);
+        {  // embeddings
+            const dim3 g((D + 255) / 256, t);
+            k_pf_embed<<<g, 256, 0, m->stream>>>(m->embd, m->embd_f32, c->toks + q0, D, m->pf.x);
+            CU(cudaGetLastError());
+        }
+        for (int l = 0; l < cfg.n_layer; l++) {
+            const Layer &L = m->layers[l];
+            float *kl = c->k + (size_t)l * c->max_tokens * kvd, *vl = c->v + (size_t)l * c->max_tokens * kvd;
+            // RMSNorm + quantize; q, k (RoPE, into the cache), v (into the cache)
+            if (pf_rows(m, m->pf.x, D, L.attn_norm, cfg.eps, D, t, need(L.q, 16) | need(L.k, 16) | need(L.v, 16),
+                        need(L.q, 32) | need(L.k, 32) | need(L.v, 32)))
+                return -1;
+            MvSeg sq = mv_seg(L.q, dq / 2, PAIR_ROPE, EPI_ROPE, m->pf.q, ROWS_MANY);
+            sq.half = hd / 2;
+            sq.bias = L.bq;
+            MvSeg sk = mv_seg(L.k, (int)kvd / 2, PAIR_ROPE, EPI_ROPE, kl, ROWS_MANY);
+            sk.half = hd / 2;
+            sk.bias = L.bk;
+            sk.at_pos = 1;
+            sk.pos_stride = (int)kvd;
+            MvSeg sv = mv_seg(L.v, (int)kvd / 2, PAIR_ADJ, EPI_STORE, vl, ROWS_MANY);
+            sv.bias = L.bv;
+            sv.at_pos = 1;
+            sv.pos_stride = (int)kvd;
+            if (pf_seg_gemm(m, sq, t, (int)q0, dq) || pf_seg_gemm(m, sk, t, (int)q0, 0) ||
+                pf_seg_gemm(m, sv, t, (int)q0, 0))
+                return -1;
+            // causal attention of the chunk's tokens over the cache
+            const int stride = (int)((q0 + t + 3) & ~3u);
+            const int tz = (int)std::max<size_t>(1, std::min<size_t>(t, m->pf.score_floats / ((size_t)H * stride)));
+            for (int z0 = 0; z0 < t; z0 += tz) {
+                AttnParams a{};
+                a.q = m->pf.q + (size_t)z0 * dq;
+                a.k = kl;
+                a.v = vl;
+                a.out = m->pf.att + (size_t)z0 * dq;
+                a.scores = m->pf.scores;
+                a.d_len = nullptr;
+                a.pos0 = (int)q0 + z0;
+                a.qs = dq;
+                a.os = dq;
+                a.H = H;
+                a.KV = KV;
+                a.hd = hd;
+                a.max_pos = (int)c->max_tokens;
+                a.score_stride = stride;
+                a.scale = 1.0f / sqrtf((float)hd);  // src/ops.rs:1287
+                a.err = m->err;
+                if (launch_attention_on(m->stream, a, std::min(tz, t - z0))) return -1;
+            }
+            // o_proj + residual; RMSNorm + gate|up + SwiGLU; down + residual
+            if (pf_rows(m, m->pf.att, dq, nullptr, 0.0f, dq, t, need(L.o, 16), need(L.o, 32)) ||
+                pf_seg_gemm(m, mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->pf.x, ROWS_MANY), t, (int)q0, D))
+                return -1;
+            if (pf_rows(m, m->pf.x, D, L.ffn_norm, cfg.eps, D, t, need(L.gu, 16), need(L.gu, 32)) ||
+                pf_seg_gemm(m, mv_seg(L.gu, F, PAIR_TWO, EPI_SWIGLU, m->pf.h, ROWS_MANY), t, (int)q0, F))
+                return -1;
+            if (pf_rows(m, m->pf.h, F, nullptr, 0.0f, F, t, need(L.down, 16), need(L.down, 32)) ||
+                pf_seg_gemm(m, mv_seg(L.down, D / 2, PAIR_ADJ, EPI_RESID, m->pf.x, ROWS_MANY), t, (int)q0, D))
+                return -1;
+        }
+    }
+    return 0;
+}
+
+// the prompt tokens before the last of a forward call of n tokens from
+// position p0: on the tensor cores when the call takes the buffered path
+// (24+ tokens) on a single-GPU model, else replayed step by step
+int prompt_prefix(cxm_model *m, cxm_cache *c, uint32_t p0, uint32_t n) {
+    if (n < 2) return 0;
+    if (m->prefill_tc && m->tp == 1 && row_class(n) == ROWS_MANY) {
+        if (prefill_tokens(m, c, p0, n - 1)) return -1;
+        k_set_int<<<1, 1, 0, m->stream>>>(c->d_len, (int)(p0 + n - 1));
+        CU(cudaGetLastError());
+        return 0;
+    }
+    return run_steps(m, c, STEP_PREFILL, n, n - 1);
+}
+
 // ── decode programs ──
-MvSeg mv_seg(const QMat &M, int units, int pairing, int epi, float *out, int cls = ROWS_FEW) {
+MvSeg mv_seg(const QMat &M, int units, int pairing, int epi, float *out, int cls) {
     MvSeg s{};
     s.M = M;
     s.units = units;
@@ -485,20 +692,22 @@ size_t phase_region(const Phase &ph, int max_pos) {
                                // prologue, + the warps' offset-term spill)
         return mv_spill_offset(ph.mv) + (size_t)kDW * ph.mv.sv_warp * sizeof(float);
     if (ph.kind == PH_SCORES) return scores_region(ph.at.P, ph.at.H / ph.at.KV, ph.at.hd);
-    if (ph.kind == PH_ATTN) return attn_region(max_pos, ph.at.dims);
+    if (ph.kind == PH_ATTN) return attn_region(max_pos, ph.at.ring);
     return 0;
 }
+
+// shared memory an attention phase may take (the rest is the weight ring)
+constexpr size_t kAttnBudget = 104 * 1024;
 
 // positions per score item: the G query heads of a kv head share its K rows
 int score_positions(int G) { return std::max(1, std::min(64, 256 / std::max(1, G))); }
 
-// Output dims per attention item: 16, or 32 when that keeps the items at
-// one per SM where 16 would not (every head's softmax and its
-// position-by-position sums in one round). One lane per dim, all in warp 0.
-int attn_dims(int H, int hd, int sms) {
-    int d = 16;
-    if ((long long)H * (hd / 16) > sms && hd % 32 == 0) d = 32;
-    return d;
+// V chunks in the attention ring: as many as `budget` bytes hold beside the
+// probabilities (at least kAttnMinRing)
+int attn_ring(int max_pos, size_t budget) {
+    int r = kAttnMinRing;
+    while (r < kAttnMaxRing && attn_region(max_pos, r + 1) <= budget) r++;
+    return r;
 }
 
 // The step for the token at *d_len of cache c (src/forward.rs:375-505):
@@ -568,7 +777,7 @@ std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode, int cls) {
         at.hd = hd;
         at.score_stride = (cfg.ctx + 3) & ~3;
         at.P = score_positions(H / KV);
-        at.dims = attn_dims(H, hd, m->sms);
+        at.ring = attn_ring((int)c->max_tokens, kAttnBudget);
         at.scale = 1.0f / sqrtf((float)hd);  // src/ops.rs:1287
         {
             Phase ph{};
@@ -707,7 +916,7 @@ DecodeArgs base_args(cxm_model *m) {
     return a;
 }
 
-int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out);
+int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out, int *d_stop);
 
 int enqueue_step(cxm_model *m, cxm_cache *c, int mode, int cls) {
     if (!m->connected) {
@@ -719,7 +928,8 @@ int enqueue_step(cxm_model *m, cxm_cache *c, int mode, int cls) {
         return -1;
     }
     if (mode == STEP_SAMPLE)
-        return enqueue_step(m, c, STEP_LOGITS, cls) || launch_sample(m, c->d_len, c->toks, nullptr) ? -1 : 0;
+        return enqueue_step(m, c, STEP_LOGITS, cls) || launch_sample(m, c->d_len, c->toks, nullptr, c->d_stop) ? -1
+                                                                                                            : 0;
     Program &p = c->prog[mode][cls];
     if (!p.d && upload_program(step_program(m, c, mode, cls), (int)c->max_tokens, &p)) return -1;
     DecodeArgs a = base_args(m);
@@ -730,6 +940,8 @@ int enqueue_step(cxm_model *m, cxm_cache *c, int mode, int cls) {
     a.max_pos = (int)c->max_tokens;
     a.write_token = mode == STEP_GREEDY;
     a.commit = 1;
+    a.d_stop = c->d_stop;
+    a.eos = m->cfg.has_eos ? (int)m->cfg.eos : -1;
     size_t smem = 0;
     if (decode_geometry(m->slot_bytes, p, a, &smem)) return -1;
     return launch_decode(m->sms, m->stream, a, smem);
@@ -777,7 +989,7 @@ int run_steps(cxm_model *m, cxm_cache *c, int mode, uint64_t rows, uint32_t n) {
 
 // the device Muestreador::elegir on the model's logits, with (1/T, top_p) and
 // the RNG state from device memory; the token goes to toks[*d_len] or *out
-int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out) {
+int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out, int *d_stop) {
     SampleArgs a{};
     a.logits = m->logits;
     a.n = m->cfg.vocab;
@@ -792,6 +1004,8 @@ int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out)
     a.val0 = m->samp_v0;
     a.key1 = m->samp_k1;
     a.val1 = m->samp_v1;
+    a.d_stop = d_stop;
+    a.eos = d_stop && m->cfg.has_eos ? (int)m->cfg.eos : -1;
     k_sample<<<1, kSampThreads, 2 * kScanChunk * sizeof(float), m->stream>>>(a);
     CU(cudaGetLastError());
     return 0;
@@ -804,10 +1018,14 @@ int set_sampler(cxm_model *m, const cxm_sampler *s) {
     return 0;
 }
 
+// The error word and the argmax key back to the host in one round trip: both
+// copies queue behind the steps, then one synchronisation.
 int check_err(cxm_model *m) {
+    CU(cudaMemcpyAsync(&m->hw->err, m->err, 4, cudaMemcpyDeviceToHost, m->stream));
+    CU(cudaMemcpyAsync(&m->hw->key, m->argmax_key, 8, cudaMemcpyDeviceToHost, m->stream));
     CU(cudaStreamSynchronize(m->stream));
-    int e = 0;
-    CU(cudaMemcpy(&e, m->err, 4, cudaMemcpyDeviceToHost));
+    const int e = m->hw->err;
+    m->key_valid = e == 0;
     if (e) {
         CU(cudaMemset(m->err, 0, 4));
         set_error("device reported %s", (e & ERR_TOKEN)      ? "a token beyond the vocabulary"
@@ -912,6 +1130,8 @@ extern "C" int cxm_model_open_tp(const char *path, int device, int tp_rank, int 
     m->v_off = r * m->v_loc;
     if (r == tp - 1) m->v_loc = cfg.vocab - m->v_off;
     CU(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    CU(cudaHostAlloc((void **)&m->hw, sizeof(cxm_model::HostWords), cudaHostAllocDefault));
+    memset(m->hw, 0, sizeof(cxm_model::HostWords));
     if (embd->type == F32) {
         if (upload_vector(m.get(), g, *embd, (size_t)cfg.vocab * cfg.dim, &m->embd_f32)) return -1;
         m->embd.type = 0;
@@ -1023,7 +1243,7 @@ extern "C" int cxm_model_open_tp(const char *path, int device, int tp_rank, int 
     CU(cudaMemset(m->epoch, 0, sizeof(unsigned)));
     m->peer[tp_rank] = m->xch;
     if (set_kernel_smem_limits()) return -1;
-    if (out_smem((uint32_t)cfg.ctx) > 200 * 1024 || cfg.head_dim % 16 || cfg.head_dim > kKRow - 4 ||
+    if (out_smem((uint32_t)cfg.ctx) > 200 * 1024 || cfg.head_dim % 32 || cfg.head_dim > kKRow - 4 ||
         cfg.vocab % 2 || cfg.dim % 4) {
         set_error("context %d / head_dim %d / vocab %d are beyond the decode kernels' layouts", cfg.ctx,
                   cfg.head_dim, cfg.vocab);
@@ -1103,6 +1323,15 @@ extern "C" int cxm_model_config(const cxm_model *m, cxm_config *out) {
 
 extern "C" uint64_t cxm_model_weight_bytes(const cxm_model *m) { return m ? m->weight_bytes : 0; }
 
+extern "C" int cxm_model_set_prefill(cxm_model *m, int tensor_cores) {
+    if (!m) {
+        set_error("null model");
+        return -1;
+    }
+    m->prefill_tc = tensor_cores != 0;
+    return 0;
+}
+
 extern "C" void cxm_model_close(cxm_model *m) { delete m; }
 
 extern "C" int cxm_cache_new(cxm_model *m, uint32_t max_tokens, cxm_cache **out) {
@@ -1126,6 +1355,8 @@ extern "C" int cxm_cache_new(cxm_model *m, uint32_t max_tokens, cxm_cache **out)
     CU(cudaMalloc(&c->toks, ((size_t)max_tokens + 2) * 4));
     CU(cudaMalloc(&c->d_len, 4));
     CU(cudaMemset(c->d_len, 0, 4));
+    CU(cudaMalloc(&c->d_stop, 4));
+    CU(cudaMemset(c->d_stop, 0, 4));
     CU(cudaMemset(c->toks, 0, ((size_t)max_tokens + 2) * 4));
     *out = c.release();
     return 0;
@@ -1221,8 +1452,9 @@ extern "C" int cxm_forward(cxm_model *m, cxm_cache *c, const uint32_t *tokens, u
             return -1;
         }
     CU(cudaSetDevice(m->device));
+    CU(cudaMemsetAsync(c->d_stop, 0, 4, m->stream));
     CU(cudaMemcpyAsync(c->toks + c->len, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, m->stream));
-    if (run_steps(m, c, STEP_PREFILL, n, n - 1) || run_steps(m, c, STEP_LOGITS, n, 1)) return -1;
+    if (prompt_prefix(m, c, c->len, n) || run_steps(m, c, STEP_LOGITS, n, 1)) return -1;
     if (logits_out)  // this rank's vocabulary rows (all of them without tensor parallelism)
         CU(cudaMemcpyAsync(logits_out, m->logits, (size_t)m->v_loc * 4, cudaMemcpyDeviceToHost, m->stream));
     if (check_err(m)) return -1;
@@ -1261,7 +1493,7 @@ extern "C" int cxm_sample(cxm_model *m, cxm_sampler *s, uint32_t *token_out) {
         return -1;
     }
     if (s->temperature > 0.0f) {  // the device Muestreador::elegir
-        if (set_sampler(m, s) || launch_sample(m, nullptr, nullptr, m->samp_tok)) return -1;
+        if (set_sampler(m, s) || launch_sample(m, nullptr, nullptr, m->samp_tok, nullptr)) return -1;
         uint32_t tok = 0;
         uint64_t st = 0;
         CU(cudaMemcpyAsync(&tok, m->samp_tok, 4, cudaMemcpyDeviceToHost, m->stream));
@@ -1271,9 +1503,13 @@ extern "C" int cxm_sample(cxm_model *m, cxm_sampler *s, uint32_t *token_out) {
         s->state = st;
         return 0;
     }
-    unsigned long long key = 0;  // greedy: the first maximum (src/sampler.rs:129-137)
-    CU(cudaStreamSynchronize(m->stream));
-    CU(cudaMemcpy(&key, m->argmax_key, 8, cudaMemcpyDeviceToHost));
+    // greedy: the first maximum (src/sampler.rs:129-137), already read back
+    // with the forward's error word
+    unsigned long long key = m->hw->key;
+    if (!m->key_valid) {
+        CU(cudaStreamSynchronize(m->stream));
+        CU(cudaMemcpy(&key, m->argmax_key, 8, cudaMemcpyDeviceToHost));
+    }
     *token_out = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
     return 0;
 }
@@ -1303,8 +1539,9 @@ extern "C" int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, 
         }
     CU(cudaSetDevice(m->device));
     const uint32_t len0 = c->len;
+    CU(cudaMemsetAsync(c->d_stop, 0, 4, m->stream));
     CU(cudaMemcpyAsync(c->toks + len0, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, m->stream));
-    if (run_steps(m, c, STEP_PREFILL, n_prompt, n_prompt - 1)) return -1;
+    if (prompt_prefix(m, c, len0, n_prompt)) return -1;
     if (max_new == 0) {
         // the prompt is still forwarded (logits of the last token)
         if (run_steps(m, c, STEP_LOGITS, n_prompt, 1) || check_err(m)) return -1;
@@ -1446,8 +1683,10 @@ extern "C" int cxm_debug_matmul(int type, const uint8_t *w, uint32_t rows, uint3
         set_error("bad arguments (k-quant type, k a multiple of 256 up to %d, rows even, m >= 1)", kMaxActivation);
         return -1;
     }
-    // the decode kernel on a one-phase program: quantize x, W·x, store; once
-    // per activation row, every row in the order matmul_auto takes for m rows
+    // 24 rows and more: the prompt forward's tensor-core GEMM (the buffered
+    // path's order); fewer: the decode kernel on a one-phase program
+    // (quantize x, W·x, store) once per activation row, every row in the
+    // order matmul_auto takes for m rows
     int dev = 0, sms = 148;
     CU(cudaGetDevice(&dev));
     CU(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -1464,6 +1703,52 @@ extern "C" int cxm_debug_matmul(int type, const uint8_t *w, uint32_t rows, uint3
     CU(cudaMalloc(&derr.p, 4));
     CU(cudaMalloc(&dbar.p, 4));
     CU(cudaMemset(derr.p, 0, 4));
+    if (row_class(m) == ROWS_MANY) {
+        DevBuf xa, a16, a32, e16, s16, e32, s32, yy, derr2;
+        const size_t ab = pfa_bytes((int)m, (int)k);
+        CU(cudaMalloc(&xa.p, (size_t)m * k * 4));
+        CU(cudaMalloc(&yy.p, (size_t)m * rows * 4));
+        CU(cudaMalloc(&a16.p, ab));
+        CU(cudaMalloc(&a32.p, ab));
+        CU(cudaMemset(a16.p, 0, ab));
+        CU(cudaMemset(a32.p, 0, ab));
+        CU(cudaMalloc(&e16.p, (size_t)m * (k / 16) * 4));
+        CU(cudaMalloc(&s16.p, (size_t)m * (k / 16) * 4));
+        CU(cudaMalloc(&e32.p, (size_t)m * (k / 32) * 4));
+        CU(cudaMalloc(&s32.p, (size_t)m * (k / 32) * 4));
+        CU(cudaMalloc(&derr2.p, 4));
+        CU(cudaMemset(derr2.p, 0, 4));
+        CU(cudaMemcpy(xa.p, x, (size_t)m * k * 4, cudaMemcpyHostToDevice));
+        if (set_kernel_smem_limits()) return -1;
+        PfRows P{};
+        P.in = (const float *)xa.p;
+        P.ld_in = (int)k;
+        P.K = (int)k;
+        P.tokens = (int)m;
+        P.need16 = sub_of(type) == 16;
+        P.need32 = sub_of(type) == 32;
+        P.a16 = (int8_t *)a16.p;
+        P.a32 = (int8_t *)a32.p;
+        P.e16 = (float *)e16.p;
+        P.s16 = (float *)s16.p;
+        P.e32 = (float *)e32.p;
+        P.s32 = (float *)s32.p;
+        k_pf_rows<<<m, kDecodeThreads>>>(P);
+        CU(cudaGetLastError());
+        const MvSeg seg = mv_seg(M, (int)rows / 2, PAIR_ADJ, EPI_STORE, (float *)yy.p, ROWS_MANY);
+        if (pf_gemm(0, seg, (int)m, 0, (int)rows, P.a16, P.a32, P.e16, P.s16, P.e32, P.s32, nullptr, nullptr,
+                    (int *)derr2.p))
+            return -1;
+        CU(cudaDeviceSynchronize());
+        int e = 0;
+        CU(cudaMemcpy(&e, derr2.p, 4, cudaMemcpyDeviceToHost));
+        if (e) {
+            set_error("prefill GEMM reported error flags %d", e);
+            return -1;
+        }
+        CU(cudaMemcpy(y, yy.p, (size_t)m * rows * 4, cudaMemcpyDeviceToHost));
+        return 0;
+    }
     Phase ph = mv_phase({mv_seg(M, (int)rows / 2, PAIR_ADJ, EPI_STORE, (float *)dy.p, row_class(m))}, (int)k,
                         PRO_QUANT, (const float *)dx.p, nullptr, 0.0f, 0);
     Program prog;
@@ -1584,6 +1869,7 @@ extern "C" int cxm_bench_decode_sampled(cxm_model *m, cxm_cache *c, cxm_sampler 
     }
     CU(cudaSetDevice(m->device));
     // the step reads the token at toks[len]; start from the last cached one
+    CU(cudaMemsetAsync(c->d_stop, 0, 4, m->stream));
     if (set_len(c, c->len - 1)) return -1;
     if (sampled && set_sampler(m, s)) return -1;
     cudaGraphExec_t g;

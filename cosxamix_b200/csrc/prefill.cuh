@@ -1,0 +1,598 @@
+// The prompt forward of 24 tokens and more on the tensor cores.
+//
+// The reference multiplies all the tokens of one forward call at once, and
+// from BLOQUES_DESDE = 24 rows every matrix takes its buffered path
+// (src/ops.rs:1073-1079, :599-606 on the portable backend): per output,
+// dot_i8_escalado over the row's sub-blocks, total += (esc·xe)·Σxq·q, then,
+// when any offset of the row is nonzero, total += (des·xe)·xs sub-block by
+// sub-block (src/ops.rs:372-405, src/kernels/scalar.rs:95-109). The integer
+// sums Σxq·q are exact and do not depend on their order, so they come from
+// int8 tensor-core MMAs (tcgen05.mma kind::i8, s32 accumulators in tensor
+// memory), one accumulator per sub-block; the float chain then runs on the
+// CUDA cores in the reference's order. The results are those of the decode
+// kernel replaying the tokens one by one with ROWS_MANY orders, bit for bit.
+//
+// Kernels:
+//   k_pf_embed  the tokens' embedding rows
+//   k_pf_rows   RMSNorm (optional) + i8 quantization of each token's row, into
+//               the MMA's K-major operand tiles and per-sub-block scale/sum
+//   k_pf_gemm   one 128-token x N-row tile of out = W·x over the whole row
+//               (warp-specialized: 4 epilogue warps own the TMEM lanes = tokens,
+//               4 producer warps unpack the k-quant blocks to int8 operand
+//               tiles, one thread copies the activation tiles and issues the
+//               MMAs), then the segment's epilogue (bias, RoPE + K/V append,
+//               residual, SwiGLU)
+// Attention over the new tokens uses the standalone attention kernels with a
+// token dimension (step_kernels.cuh).
+#pragma once
+
+#include "decode.cuh"
+
+namespace cxm {
+
+// ── tcgen05 (5th-generation tensor core) primitives, sm_100a ──
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// generic-proxy shared-memory writes made visible to the tensor core's reads
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// D[tmem] (=|+=) A[smem desc] · B[smem desc]^T, int8 x int8 -> s32
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+// the mbarrier gets one arrival when every MMA this thread issued before has completed
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes (one per thread)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand without swizzle: 8-row
+// x 16-byte core matrices, rows 16 bytes apart; `lbo` bytes from a core matrix
+// to the next along K, `sbo` bytes to the next 8 rows (sm_100 format: address
+// and offsets in 16-byte units, version 1 in bits 46-47, layout type 0).
+__device__ __forceinline__ uint64_t umma_desc(const void *smem, uint32_t lbo, uint32_t sbo) {
+    const uint64_t a = (smem_u32(smem) >> 4) & 0x3FFFu;
+    return a | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor of kind::i8: s32 accumulator, signed A and B, both
+// K-major, N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+__host__ __device__ constexpr uint32_t umma_idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ── the activation operand ──
+// M-tiles of 128 token rows; each tile holds its K-steps of 32 values one
+// after another, 4 KB each, in the canonical K-major layout (LBO 128, SBO 256):
+// byte (m, k) of a step at (m/8)·256 + (k/16)·128 + (m%8)·16 + k%16.
+constexpr int kPfM = 128;
+__host__ __device__ inline size_t pfa_bytes(int tokens, int K) {
+    return (size_t)((tokens + kPfM - 1) / kPfM) * (size_t)(K / 32) * 4096;
+}
+__device__ __forceinline__ size_t pfa_offset(int m, int k, int K) {
+    const int mt = m >> 7, mm = m & 127, s = k >> 5, kk = k & 31;
+    return ((size_t)mt * (K >> 5) + s) * 4096 + (mm >> 3) * 256 + (kk >> 4) * 128 + (mm & 7) * 16 + (kk & 15);
+}
+
+struct PfRows {
+    const float *in;        // [tokens][ld_in]
+    int ld_in;
+    const float *norm_w;    // RMSNorm weights, or null (quantize only)
+    float eps;
+    int K, tokens, need16, need32;
+    int8_t *a16, *a32;      // tiled operands (sub-blocks of 16 / 32)
+    float *e16, *s16, *e32, *s32;  // [tokens][K/16], [tokens][K/32]: scale and sum per sub-block
+};
+
+// One token row per CTA of kDecodeThreads threads, with exactly the
+// arithmetic of the decode kernel's prologue (quantize_act): the f64 sum of
+// squares per thread over its two rounds of 8 values, across the warp by
+// xor-shuffles, across the warps in order; then per sub-block the i8
+// quantization of src/ops.rs:178-198.
+__global__ void __launch_bounds__(kDecodeThreads) k_pf_rows(const __grid_constant__ PfRows P) {
+    __shared__ double red[kDW];
+    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = kDecodeThreads;
+    const float *x = P.in + (size_t)row * P.ld_in;
+    const int nh = P.K >> 3;
+    double scale = 0.0;
+    if (P.norm_w) {
+        double acc = 0.0;
+        for (int r = 0; r < 2; r++) {
+            const int hc = r * nt + tid;
+            for (int k = 0; k < 8; k++) {
+                const float v = hc < nh ? x[8 * hc + k] : 0.0f;
+                acc = __dadd_rn(acc, __dmul_rn((double)v, (double)v));
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        if (lane == 0) red[warp] = acc;
+        __syncthreads();
+        double sum = 0.0;
+        for (int w = 0; w < kDW; w++) sum = __dadd_rn(sum, red[w]);
+        const int K = P.K;
+        const double ms = (K & (K - 1)) == 0 ? __dmul_rn(sum, 1.0 / (double)K) : __ddiv_rn(sum, (double)K);
+        scale = __drcp_rn(__dsqrt_rn(__dadd_rn(ms, (double)P.eps)));
+    }
+    for (int hc0 = 0; hc0 < nh; hc0 += nt) {
+        const int hc = hc0 + tid;  // nh is a multiple of 32: warps are all in range or all out
+        if (hc0 + warp * 32 >= nh) continue;
+        float v[8];
+        for (int k = 0; k < 8; k++) {
+            v[k] = x[8 * hc + k];
+            if (P.norm_w) v[k] = __fmul_rn(__double2float_rn(__dmul_rn((double)v[k], scale)), P.norm_w[8 * hc + k]);
+        }
+        float amax = 0.0f;
+        for (int k = 0; k < 8; k++) amax = fmaxf(amax, fabsf(v[k]));
+        for (int sz = 16; sz <= 32; sz += 16) {
+            if ((sz == 16 && !P.need16) || (sz == 32 && !P.need32)) continue;
+            float am = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            if (sz == 32) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+            uint32_t w0, w1;
+            int sm = quant8(v, am, w0, w1);
+            sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+            if (sz == 32) sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+            int8_t *a = sz == 16 ? P.a16 : P.a32;
+            *(uint2 *)(a + pfa_offset(row, 8 * hc, P.K)) = make_uint2(w0, w1);
+            const int per = sz / 8;  // half-chunks per sub-block
+            if (hc % per == 0) {
+                const int nsub = P.K / sz, sb = hc / per;
+                float *e = sz == 16 ? P.e16 : P.e32, *s = sz == 16 ? P.s16 : P.s32;
+                e[(size_t)row * nsub + sb] = am > 0.0f ? __fdiv_rn(am, 127.0f) : 0.0f;
+                s[(size_t)row * nsub + sb] = (float)sm;
+            }
+        }
+    }
+}
+
+// The tokens' embedding rows (src/forward.rs:389-405), dequantized as the
+// decode kernel's first prologue does.
+__global__ void k_pf_embed(QMat E, const float *e32, const uint32_t *toks, int D, float *x) {
+    const int row = blockIdx.y;
+    const uint32_t t = toks[row];
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D; i += gridDim.x * blockDim.x)
+        x[(size_t)row * D + i] = e32 ? e32[(size_t)t * D + i] : embed_value(E, (int)t, i);
+}
+
+// ── the GEMM ──
+struct PfGemm {
+    MvSeg seg;              // weights (tiled), units, pairing, epilogue, bias
+    int tokens, pos0;       // rows of the activation; position of the first token
+    const int8_t *a;        // tiled activation operand (sub-blocks of seg's format)
+    const float *xe, *xs;   // [tokens][nsub]
+    int nsub;               // K / sub
+    int ld_out;             // floats between tokens' rows of seg.out (not for cache rows: pos_stride)
+    const float *rope_cos, *rope_sin;
+    int *err;
+};
+
+constexpr int kPfThreads = 256;  // warps 0-3: epilogue (TMEM lanes); warps 4-7: producers
+constexpr int kPfStages = 2;
+constexpr uint32_t kPfTmemCols = 512;  // two accumulator buffers of 256 columns
+
+// rows per CTA tile: every sub-block of a super-block gets its own accumulator
+// of N columns, two super-blocks in flight: 2 · subs · N = 512 columns
+__host__ __device__ constexpr int pf_rows_per_tile(int sub) { return sub == 32 ? 32 : 16; }
+
+struct PfSmem {  // byte offsets in the dynamic shared memory
+    uint32_t a[kPfStages], b[kPfStages], esc[kPfStages], raw, des, anyd, total;
+};
+__host__ __device__ inline PfSmem pf_smem(int type, int K) {
+    const int sub = type == 12 || type == 13 ? 32 : 16, N = pf_rows_per_tile(sub), nsb = 256 / sub;
+    const uint32_t bbytes = sub == 32 ? (uint32_t)(8 * N * 32) : (uint32_t)(N * 16 * 18);  // + two zero blocks
+    PfSmem s{};
+    uint32_t o = 0;
+    for (int i = 0; i < kPfStages; i++) {
+        s.a[i] = o;
+        o += 32768;
+    }
+    for (int i = 0; i < kPfStages; i++) {
+        s.b[i] = o;
+        o += (bbytes + 127) & ~127u;
+    }
+    for (int i = 0; i < kPfStages; i++) {
+        s.esc[i] = o;
+        o += (uint32_t)(nsb * N * 4);
+    }
+    s.raw = o;
+    o += (uint32_t)(N * 224);  // one super-block per row, GGUF bytes (<= 210)
+    s.des = o;
+    const bool mins = type == 12 || type == 13 || type == 10;
+    o += mins ? (uint32_t)(N * (K / sub) * 4) : 0u;
+    s.anyd = o;
+    o += 128;
+    s.total = (o + 127) & ~127u;
+    return s;
+}
+
+// GGUF bytes of super-block b of tiled row r into dst (all threads of the
+// producer group cooperate: `i0`, `step`)
+__device__ __forceinline__ void pf_gather(const QMat &M, int r0, int N, int b, uint8_t *raw, int i0, int step) {
+    const int T = M.type, pa = plane_a_bytes(T), ps = plane_s_bytes(T), pd = plane_d_bytes(T), ach = pa / 16;
+    int lo_a = 0, lo_s = pa, lo_d = pa + ps;
+    if (T == 10) {
+        lo_s = 0;
+        lo_a = 16;
+        lo_d = 80;
+    }
+    const int t = b / M.lpr, bl = b % M.lpr, nb = tile_nb(M.nblk, M.lpr, t), L = M.rpt * nb;
+    const int rows = M.ngroup * M.rpt;  // rows allocated (padded groups); rows past them are skipped
+    for (int i = i0; i < N * ach; i += step) {
+        const int n = i / ach, c = i - n * ach, r = r0 + n, g = r / M.rpt, sl = r % M.rpt, lane = M.rpt * bl + sl;
+        if (r >= rows) continue;
+        const uint8_t *tile = M.base + tile_offset(M, g, t);
+        *(uint4 *)(raw + n * 224 + lo_a + 16 * c) = __ldg((const uint4 *)(tile + ((size_t)c * L + lane) * 16));
+    }
+    for (int i = i0; i < N * (ps + pd); i += step) {
+        const int n = i / (ps + pd), k = i - n * (ps + pd), r = r0 + n, g = r / M.rpt, sl = r % M.rpt,
+                  lane = M.rpt * bl + sl;
+        if (r >= rows) continue;
+        const uint8_t *tile = M.base + tile_offset(M, g, t);
+        uint8_t v;
+        if (k < ps) v = tile[ach * L * 16 + lane * ps + k];
+        else v = tile[ach * L * 16 + L * ps + lane * pd + (k - ps)];
+        raw[n * 224 + (k < ps ? lo_s + k : lo_d + (k - ps))] = v;
+    }
+}
+
+__device__ __forceinline__ float rd_h(const uint8_t *p) { return h2f((uint32_t)p[0] | ((uint32_t)p[1] << 8)); }
+
+// Quarter q (values 64q..64q+63) of one super-block as desempaquetar_i8
+// unpacks it (src/quant.rs:238-468): the int8 values, the scale of each of
+// its sub-blocks (esc[j], j = sub-block inside the block) and the offset
+// (des[j], formats with a minimum).
+__device__ void pf_unpack_quarter(int T, const uint8_t *blk, int q, int8_t (&v)[64], float *esc, float *des) {
+    switch (T) {
+    case 12: case 13: {  // Q4_K / Q5_K: sub-blocks 2q (low nibbles) and 2q+1 (high)
+        const float d = rd_h(blk), dmin = rd_h(blk + 2);
+        const uint32_t w0 = blk[4] | blk[5] << 8 | blk[6] << 16 | (uint32_t)blk[7] << 24;
+        const uint32_t w1 = blk[8] | blk[9] << 8 | blk[10] << 16 | (uint32_t)blk[11] << 24;
+        const uint32_t w2 = blk[12] | blk[13] << 8 | blk[14] << 16 | (uint32_t)blk[15] << 24;
+        for (int t = 0; t < 2; t++) {
+            int sc, mn;
+            scale_min_k4(2 * q + t, w0, w1, w2, sc, mn);
+            esc[2 * q + t] = fm(d, (float)sc);
+            des[2 * q + t] = -fm(dmin, (float)mn);
+        }
+        const uint8_t *qs = blk + (T == 12 ? 16 : 48) + 32 * q, *qh = blk + 16;
+        for (int l = 0; l < 32; l++) {
+            int lo = qs[l] & 0xF, hi = qs[l] >> 4;
+            if (T == 13) {
+                lo += (qh[l] >> (2 * q)) & 1 ? 16 : 0;
+                hi += (qh[l] >> (2 * q + 1)) & 1 ? 16 : 0;
+            }
+            v[l] = (int8_t)lo;
+            v[32 + l] = (int8_t)hi;
+        }
+        break;
+    }
+    case 14: {  // Q6_K: half h = q/2; q%2 = 0: groups primera, segunda; 1: tercera, cuarta
+        const int h = q >> 1, odd = q & 1;
+        const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h, *sc = blk + 192 + 8 * h;
+        const float d = rd_h(blk + 208);
+        for (int p = 0; p < 4; p++) esc[8 * h + 4 * odd + p] = fm(d, (float)(int8_t)sc[4 * odd + p]);
+        for (int l = 0; l < 32; l++) {
+            const int qb = qh[l];
+            if (!odd) {
+                v[l] = (int8_t)(((ql[l] & 0xF) | ((qb & 3) << 4)) - 32);
+                v[32 + l] = (int8_t)(((ql[32 + l] & 0xF) | (((qb >> 2) & 3) << 4)) - 32);
+            } else {
+                v[l] = (int8_t)(((ql[l] >> 4) | (((qb >> 4) & 3) << 4)) - 32);
+                v[32 + l] = (int8_t)(((ql[32 + l] >> 4) | (((qb >> 6) & 3) << 4)) - 32);
+            }
+        }
+        break;
+    }
+    case 11: {  // Q3_K: half m2 = q/2, shifts 2it for it = 2(q%2), 2(q%2)+1
+        const int m2 = q >> 1;
+        const uint8_t *hm = blk, *qs = blk + 32 + 32 * m2;
+        const float d = rd_h(blk + 108);
+        const uint32_t a0 = blk[96] | blk[97] << 8 | blk[98] << 16 | (uint32_t)blk[99] << 24;
+        const uint32_t a1 = blk[100] | blk[101] << 8 | blk[102] << 16 | (uint32_t)blk[103] << 24;
+        const uint32_t tt = blk[104] | blk[105] << 8 | blk[106] << 16 | (uint32_t)blk[107] << 24;
+        for (int ii = 0; ii < 2; ii++) {
+            const int it = 2 * (q & 1) + ii, g = 4 * m2 + it;
+            for (int t = 0; t < 2; t++) {
+                const int is = 2 * g + t, wi = is >> 2;
+                const uint32_t aa = (wi & 1) ? a1 : a0;
+                const uint32_t wq = ((aa >> ((wi >> 1) * 4)) & 0x0F0F0F0Fu) | (((tt >> (2 * wi)) & 0x03030303u) << 4);
+                const int s6 = (int)((wq >> (8 * (is & 3))) & 0xFF);
+                esc[is] = fm(d, fs((float)s6, 32.0f));
+            }
+            for (int l = 0; l < 32; l++) {
+                const int hi = (hm[l] >> g) & 1 ? 0 : 4;
+                v[32 * ii + l] = (int8_t)(((qs[l] >> (2 * it)) & 3) - hi);
+            }
+        }
+        break;
+    }
+    default: {  // Q2_K
+        const int m2 = q >> 1;
+        const uint8_t *sc = blk, *qs = blk + 16 + 32 * m2;
+        const float d = rd_h(blk + 80), dmin = rd_h(blk + 82);
+        for (int ii = 0; ii < 2; ii++) {
+            const int it = 2 * (q & 1) + ii, g = 4 * m2 + it;
+            for (int t = 0; t < 2; t++) {
+                const int is = 2 * g + t;
+                esc[is] = fm(d, (float)(sc[is] & 0xF));
+                des[is] = -fm(dmin, (float)(sc[is] >> 4));
+            }
+            for (int l = 0; l < 32; l++) v[32 * ii + l] = (int8_t)((qs[l] >> (2 * it)) & 3);
+        }
+        break;
+    }
+    }
+}
+
+// bounded mbarrier wait of a role: on a timeout it raises ERR_TIMEOUT and the
+// CTA's abort flag, so every other role's wait ends too
+__device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile int *abort, int *err) {
+    if (mbar_wait_bounded(bar, parity, abort)) return true;
+    *abort = 1;
+    atomicOr(err, ERR_TIMEOUT);
+    return false;
+}
+
+// AND of `ok` over the 128 producer threads (named barrier 2), so they leave
+// their loop together and none is left waiting at a barrier of the group
+__device__ __forceinline__ bool producers_all(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 2, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)ok)
+        : "memory");
+    return r != 0;
+}
+
+__global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant__ PfGemm G) {
+    extern __shared__ __align__(128) unsigned char pf_smem_raw[];
+    // 128-byte aligned by an offset from the array itself (the operand tiles
+    // need 16; the descriptors address 16-byte units)
+    unsigned char *sm = pf_smem_raw + ((128u - ((uint32_t)(uintptr_t)pf_smem_raw & 127u)) & 127u);
+    __shared__ __align__(8) uint64_t full_a[kPfStages], full_b[kPfStages], mma_done[kPfStages], tmem_empty[kPfStages];
+    __shared__ uint32_t tmem_base_s;
+    __shared__ volatile int abort_s;
+    const QMat &M = G.seg.M;
+    const int T = M.type, sub = (T == 12 || T == 13) ? 32 : 16, N = pf_rows_per_tile(sub), nsb = 256 / sub;
+    const bool mins = has_minimum(T);
+    const PfSmem L = pf_smem(T, M.K);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r0 = blockIdx.x * N, mt = blockIdx.y, nblk = M.nblk;
+    float *des_all = (float *)(sm + L.des);
+    unsigned char *anyd = sm + L.anyd;
+
+    if (tid == 0) {
+        for (int i = 0; i < kPfStages; i++) {
+            mbar_init(&full_a[i], 1);
+            mbar_init(&full_b[i], kPfThreads / 2);
+            mbar_init(&mma_done[i], 1);
+            mbar_init(&tmem_empty[i], 4);
+        }
+        abort_s = 0;
+        mbar_fence_init();
+    }
+    if (tid < N) anyd[tid] = 0;
+    if (warp == 0) {
+        tmem_alloc(&tmem_base_s, kPfTmemCols);
+        tmem_relinquish();
+    }
+    // the two zero core-matrix columns of the sub-16 operand tiles
+    if (sub == 16)
+        for (int s = 0; s < kPfStages; s++)
+            for (int i = tid; i < N; i += kPfThreads) {
+                *(uint4 *)(sm + L.b[s] + 16 * i) = make_uint4(0, 0, 0, 0);
+                *(uint4 *)(sm + L.b[s] + 17 * N * 16 + 16 * i) = make_uint4(0, 0, 0, 0);
+            }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+    const uint32_t idesc = umma_idesc_i8(kPfM, N);
+
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+    const int m = mt * kPfM + tid;  // the epilogue thread's token
+
+    if (warp >= 4) {
+        // ── producers: unpack the N rows' super-blocks; thread 128 also
+        // copies the activation tiles and issues the MMAs ──
+        const int ptid = tid - 128;
+        int last_issued = -1;
+        bool ok = true;  // the MMA thread's waits so far (the others' stay true)
+        for (int b = 0; b < nblk; b++) {
+            const int st = b & 1;
+            bool w = true;
+            if (b >= kPfStages) w = pf_wait(&tmem_empty[st], ((b - kPfStages) >> 1) & 1, &abort_s, G.err);
+            if (!producers_all(ok && w && !abort_s)) break;
+            if (ptid == 0) {
+                mbar_arrive_expect_tx(&full_a[st], 32768);
+                bulk_g2s(sm + L.a[st], G.a + ((size_t)mt * (M.K / 32) + 8 * b) * 4096, 32768, &full_a[st]);
+            }
+            pf_gather(M, r0, N, b, sm + L.raw, ptid, 128);
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            float *esc = (float *)(sm + L.esc[st]);  // [sub-block in block][row]
+            for (int i = ptid; i < N * 4; i += 128) {
+                const int n = i >> 2, q = i & 3;
+                int8_t v[64];
+                float e[16], d[16];
+                pf_unpack_quarter(T, sm + L.raw + n * 224, q, v, e, d);
+                const int j0 = q * (64 / sub);
+                for (int j = j0; j < j0 + 64 / sub; j++) {
+                    esc[j * N + n] = e[j];
+                    if (mins) {
+                        des_all[(size_t)n * G.nsub + b * nsb + j] = d[j];
+                        if (d[j] != 0.0f) anyd[n] = 1;
+                    }
+                }
+                // 16 values at a time into the operand tile of their sub-block
+                for (int c = 0; c < 4; c++) {
+                    const int k = 64 * q + 16 * c, j = k / sub, kk = k % sub;
+                    uint4 w;
+                    w.x = (uint8_t)v[16 * c] | (uint8_t)v[16 * c + 1] << 8 | (uint8_t)v[16 * c + 2] << 16 |
+                          (uint32_t)(uint8_t)v[16 * c + 3] << 24;
+                    w.y = (uint8_t)v[16 * c + 4] | (uint8_t)v[16 * c + 5] << 8 | (uint8_t)v[16 * c + 6] << 16 |
+                          (uint32_t)(uint8_t)v[16 * c + 7] << 24;
+                    w.z = (uint8_t)v[16 * c + 8] | (uint8_t)v[16 * c + 9] << 8 | (uint8_t)v[16 * c + 10] << 16 |
+                          (uint32_t)(uint8_t)v[16 * c + 11] << 24;
+                    w.w = (uint8_t)v[16 * c + 12] | (uint8_t)v[16 * c + 13] << 8 | (uint8_t)v[16 * c + 14] << 16 |
+                          (uint32_t)(uint8_t)v[16 * c + 15] << 24;
+                    uint32_t off;
+                    if (sub == 32) off = (uint32_t)(j * N * 32 + (n >> 3) * 256 + (kk >> 4) * 128 + (n & 7) * 16);
+                    else off = (uint32_t)(N * 16 + j * N * 16 + (n >> 3) * 128 + (n & 7) * 16);
+                    *(uint4 *)(sm + L.b[st] + off) = w;
+                }
+            }
+            fence_async_smem();
+            asm volatile("bar.sync 2, 128;" ::: "memory");  // every producer is done with the gathered bytes
+            mbar_arrive(&full_b[st]);
+            if (ptid == 0) {
+                // a failed wait is voted on at the next block (or ends the loop)
+                ok = pf_wait(&full_a[st], (b >> 1) & 1, &abort_s, G.err) &&
+                     pf_wait(&full_b[st], (b >> 1) & 1, &abort_s, G.err);
+                if (!ok) continue;
+                tc_fence_after();
+                const uint32_t dcol = tmem + (uint32_t)st * 256;
+                for (int j = 0; j < nsb; j++) {
+                    const int step = sub == 32 ? j : j >> 1;
+                    const uint64_t ad = umma_desc(sm + L.a[st] + step * 4096, 128, 256);
+                    uint64_t bd;
+                    if (sub == 32) {
+                        bd = umma_desc(sm + L.b[st] + j * N * 32, 128, 256);
+                    } else {
+                        const uint32_t data = L.b[st] + N * 16 + j * N * 16;
+                        if (!(j & 1)) bd = umma_desc(sm + data, (L.b[st] + 17 * N * 16) - data, 128);
+                        else bd = umma_desc(sm + L.b[st], data - L.b[st], 128);
+                    }
+                    umma_i8(dcol + (uint32_t)(j * N), ad, bd, idesc, 0);
+                }
+                umma_commit(&mma_done[st]);
+                last_issued = b;
+            }
+        }
+        // every MMA has completed before the accumulators are released
+        if (ptid == 0 && last_issued >= 0) pf_wait(&mma_done[last_issued & 1], (last_issued >> 1) & 1, &abort_s, G.err);
+    } else {
+        // ── epilogue: thread = token m (TMEM lane); the buffered path's dot
+        // chain, sub-block by sub-block in row order ──
+        const float *xe = G.xe + (size_t)(m < G.tokens ? m : 0) * G.nsub;
+        for (int b = 0; b < nblk; b++) {
+            const int st = b & 1;
+            // warp-uniform: the TMEM loads below are collective over the warp
+            if (!__all_sync(0xffffffffu, pf_wait(&mma_done[st], (b >> 1) & 1, &abort_s, G.err) && !abort_s)) break;
+            tc_fence_after();
+            const float *esc = (const float *)(sm + L.esc[st]);
+            for (int j = 0; j < nsb; j++) {
+                const float e = xe[b * nsb + j];
+                const uint32_t col = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(st * 256 + j * N);
+                uint32_t s0[16], s1[16];
+                tmem_ld16(col, s0);
+                if (N == 32) tmem_ld16(col + 16, s1);
+                tmem_ld_wait();
+#pragma unroll
+                for (int n = 0; n < 16; n++) acc[n] = fa(acc[n], fm(fm(esc[j * N + n], e), (float)(int)s0[n]));
+                if (N == 32) {
+#pragma unroll
+                    for (int n = 0; n < 16; n++)
+                        acc[16 + n] = fa(acc[16 + n], fm(fm(esc[j * N + 16 + n], e), (float)(int)s1[n]));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty[st]);
+        }
+    }
+    __syncthreads();
+    if (warp < 4 && !abort_s && m < G.tokens) {
+        // the offset chain, after the whole row (src/ops.rs:395-401)
+        if (mins) {
+            const float *xe = G.xe + (size_t)m * G.nsub, *xs = G.xs + (size_t)m * G.nsub;
+#pragma unroll
+            for (int n = 0; n < 32; n++) {
+                if (n >= N || !anyd[n]) continue;
+                const float *d = des_all + (size_t)n * G.nsub;
+                float a = acc[n];
+                for (int s = 0; s < G.nsub; s++) a = fa(a, fm(fm(d[s], xe[s]), xs[s]));
+                acc[n] = a;
+            }
+        }
+        // the segment's epilogue, one output unit (two tiled rows) at a time
+        const MvSeg &g = G.seg;
+        const int pos = G.pos0 + m;
+        for (int n = 0; n < N; n += 2) {
+            const int u = (r0 + n) >> 1;
+            if (u >= g.units) break;
+            int ra, rb;
+            unit_rows(g, u, ra, rb);
+            const float y0 = acc[n], y1 = acc[n + 1];
+            float *out = g.at_pos ? g.out + (size_t)pos * g.pos_stride : g.out + (size_t)m * G.ld_out;
+            switch (g.epi) {
+            case EPI_STORE:
+                out[ra] = g.bias ? fa(y0, g.bias[ra]) : y0;
+                out[rb] = g.bias ? fa(y1, g.bias[rb]) : y1;
+                break;
+            case EPI_ROPE: {  // src/ops.rs:1150-1193
+                const int i = ra % (2 * g.half);
+                const float c = G.rope_cos[(size_t)pos * g.half + i], s = G.rope_sin[(size_t)pos * g.half + i];
+                const float a = g.bias ? fa(y0, g.bias[ra]) : y0, bb = g.bias ? fa(y1, g.bias[rb]) : y1;
+                out[ra] = fs(fm(a, c), fm(bb, s));
+                out[rb] = fa(fm(a, s), fm(bb, c));
+                break;
+            }
+            case EPI_RESID:  // src/forward.rs:467-469, :489-491
+                out[ra] = fa(out[ra], y0);
+                out[rb] = fa(out[rb], y1);
+                break;
+            case EPI_SWIGLU: {  // src/kernels/scalar.rs:63-67, src/forward.rs:485-487
+                const float act = __fdiv_rn(y0, fa(1.0f, expf_glibc(-y0)));
+                out[ra] = fm(act, y1);
+                break;
+            }
+            default:
+                break;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kPfTmemCols);
+    }
+}
+
+}  // namespace cxm

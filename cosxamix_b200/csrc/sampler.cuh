@@ -35,6 +35,8 @@ struct SampleArgs {
     const int *d_len;         // token goes to toks[*d_len] (or `out` when toks is null)
     uint32_t *toks;
     uint32_t *out;
+    int *d_stop;              // set: a generation met its eos; the sampler then does nothing
+    int eos;                  // the model's eos token (its pick sets *d_stop), or -1
     float *probs, *prefix;    // scratch [n]
     uint32_t *key0, *val0, *key1, *val1;  // scratch [n]
 };
@@ -278,6 +280,7 @@ __device__ __forceinline__ int first_above(const float *prefix, int len, float t
 }
 
 __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constant__ SampleArgs a) {
+    if (a.d_stop && *(volatile const int *)a.d_stop) return;  // the generation already met its eos (uniform)
     extern __shared__ __align__(16) float stage[];  // 2 x kScanChunk
     __shared__ float red[kSampWarps];
     __shared__ uint32_t hist[kHistRow * kSampWarps];
@@ -385,6 +388,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
     if (tid == 0) {
         if (a.toks) a.toks[*a.d_len] = tok;
         if (a.out) *a.out = tok;
+        if (a.d_stop && a.eos >= 0 && tok == (uint32_t)a.eos) *a.d_stop = 1;
     }
 }
 

@@ -65,15 +65,21 @@ __device__ __forceinline__ uint32_t argmax_index(unsigned long long key) {
 //           src/ops.rs:1206-1230), then out[d] = Σ_p prob_p·v_p[d] added
 //           position by position.
 struct AttnParams {
-    const float *q;      // [H*hd], rotated
+    const float *q;      // [H*hd] per token, rotated
     const float *k, *v;  // layer base, [max_tokens][KV*hd]
-    float *out;          // [H*hd]
-    float *scores;       // scratch [H][max_pos]
-    const int *d_len;
+    float *out;          // [H*hd] per token
+    float *scores;       // scratch [H][score_stride] per token
+    const int *d_len;    // position of the (first) token; NULL: pos0
     int H, KV, hd, max_pos, score_stride;
     float scale;
     int *err;
+    // several consecutive tokens (grid z): token z at position pos + z reads
+    // q + z·qs, writes out + z·os and its scores at scores + z·H·score_stride
+    int pos0, qs, os;
 };
+__device__ __forceinline__ int attn_len(const AttnParams &p) {
+    return (p.d_len ? *p.d_len : p.pos0) + 1 + (int)blockIdx.z;
+}
 
 constexpr int kScoreThreads = 128;   // positions per score CTA
 constexpr int kKRow = 132;           // smem row stride (floats) of staged K rows
@@ -86,8 +92,8 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
     extern __shared__ __align__(16) float ks[];  // [kScoreThreads][kKRow] then q [hd]
     griddep_launch_dependents();
     griddep_wait();
-    const int h = blockIdx.x, split = blockIdx.y, tid = threadIdx.x;
-    const int n = *p.d_len + 1;
+    const int h = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, z = blockIdx.z;
+    const int n = attn_len(p);
     if (n > p.max_pos || n <= 0) {
         if (tid == 0 && h == 0 && split == 0) atomicOr(p.err, ERR_POSITION);
         return;
@@ -98,7 +104,7 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
     const int hd = p.hd, G = p.H / p.KV, g = h / G, kvd = p.KV * hd, c4 = hd / 4;
     float *qs = ks + kScoreThreads * kKRow;
     // stage q and the K rows of these positions: all 16-byte copies in flight
-    for (int i = tid; i < c4; i += kScoreThreads) cp_async16(qs + 4 * i, p.q + (size_t)h * hd + 4 * i);
+    for (int i = tid; i < c4; i += kScoreThreads) cp_async16(qs + 4 * i, p.q + (size_t)z * p.qs + (size_t)h * hd + 4 * i);
     for (int i = tid; i < cnt * c4; i += kScoreThreads) {
         const int r = i / c4, c = i - r * c4;
         cp_async16(ks + r * kKRow + 4 * c, p.k + (size_t)(p0 + r) * kvd + (size_t)g * hd + 4 * c);
@@ -117,7 +123,7 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
             acc = fa(acc, fm(qv.z, kv.z));
             acc = fa(acc, fm(qv.w, kv.w));
         }
-        p.scores[(size_t)h * p.score_stride + p0 + tid] = fm(acc, p.scale);
+        p.scores[((size_t)z * p.H + h) * p.score_stride + p0 + tid] = fm(acc, p.scale);
     }
 }
 
@@ -128,15 +134,15 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
     __shared__ float bcast;
     griddep_launch_dependents();
     griddep_wait();
-    const int h = blockIdx.x, dslice = blockIdx.y, tid = threadIdx.x;
-    const int n = *p.d_len + 1;
+    const int h = blockIdx.x, dslice = blockIdx.y, tid = threadIdx.x, z = blockIdx.z;
+    const int n = attn_len(p);
     if (n > p.max_pos || n <= 0) return;  // k_attn_scores reported it
     const int hd = p.hd, G = p.H / p.KV, g = h / G, kvd = p.KV * hd;
     const int d0 = dslice * kOutDims;
     if (d0 >= hd) return;
     float *pr = so;
     float *vs = so + ((p.max_pos + 3) & ~3);
-    const float *sc = p.scores + (size_t)h * p.score_stride;
+    const float *sc = p.scores + ((size_t)z * p.H + h) * p.score_stride;
     const float *vb = p.v + (size_t)g * hd + d0;
     const int nchunks = (n + kVChunk - 1) / kVChunk;
     auto stage = [&](int c) {
@@ -207,7 +213,7 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
         }
         __syncthreads();
     }
-    if (tid < kOutDims && d0 + tid < hd) p.out[(size_t)h * hd + d0 + tid] = acc;
+    if (tid < kOutDims && d0 + tid < hd) p.out[(size_t)z * p.os + (size_t)h * hd + d0 + tid] = acc;
 }
 
 // ── kernel-level parity: integer sub-block sums of one row against an xq ──

@@ -532,8 +532,8 @@ static int synth_write(const cxm_synth_spec *s, const char *path) {
     }
     setvbuf(o.f, nullptr, _IOFBF, 1 << 22);
     const uint64_t align = 32;
-    // header + metadata (src/daiss.rs:428-448; no eos key, so generation
-    // never stops early)
+    // header + metadata (src/daiss.rs:428-448; no eos key unless asked, so
+    // generation never stops early)
     struct KV_ {
         std::string k;
         int t;  // 4 u32, 6 f32, 8 str, 10 u64
@@ -556,6 +556,7 @@ static int synth_write(const cxm_synth_spec *s, const char *path) {
         {"qwen2.rope.freq_base", 6, 0, s->rope_base, ""},
         {"cosxamix.seed", 10, s->seed, 0, ""},
     };
+    if (s->has_eos) meta.push_back({"tokenizer.ggml.eos_token_id", 4, (uint64_t)s->eos, 0, ""});
     o.raw("GGUF", 4);
     o.u32(3);
     o.u64(decls.size());

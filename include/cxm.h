@@ -49,6 +49,14 @@ int  cxm_model_open(const char *gguf_path, int device, cxm_model **out);
 int  cxm_model_config(const cxm_model *m, cxm_config *out);
 /* bytes of weights resident on the device (the per-token weight stream) */
 uint64_t cxm_model_weight_bytes(const cxm_model *m);
+/* The prompt forward of a call of 24 tokens or more (the reference's
+ * matmul_i8_bloques threshold, src/ops.rs:1013, :1073-1079) runs, by default
+ * (tensor_cores = 1), as batched int8 tensor-core GEMMs with the buffered
+ * path's float order; 0 replays those tokens through the decode step one by
+ * one. Both give the same logits and KV rows bit for bit; the switch is for
+ * comparing them, as the reference's COSXAMIX_SIN_BLOQUES compares its paths.
+ * Tensor-parallel models always replay. */
+int cxm_model_set_prefill(cxm_model *m, int tensor_cores);
 /* Caches belong to their model: use a cache only while its model is open
  * (freeing it afterwards is allowed). */
 void cxm_model_close(cxm_model *m);
@@ -56,15 +64,19 @@ void cxm_model_close(cxm_model *m);
 /* ── tensor parallelism (one process per GPU; no counterpart in the
  * reference, whose engine runs one model on one machine) ──────────────── */
 
-/* Rank `tp_rank` of `tp_size` (1..8): this process's GPU holds q/k/v and
- * gate/up rows of its heads / FFN rows, the K slice of o_proj and ffn_down
- * for them (whole super-blocks), its share of the output rows, and the full
- * embedding and norms. Every decode step then exchanges the o_proj and
- * ffn_down partial sums with the other ranks (added in rank order, then the
- * residual) and the argmax of each vocabulary slice, over peer memory inside
- * the decode kernel; each wait is bounded (a lost rank ends the step with an
- * error, never a hang). Greedy decode only. cxm_model_config reports the
- * whole model. The model runs after cxm_tp_connect. */
+/* Rank `tp_rank` of `tp_size` (1..8): this process's GPU holds the attention
+ * block whole (q/k/v of every head, the whole KV cache, o_proj), the gate/up
+ * rows of its FFN slice [r*F/N, (r+1)*F/N) and the ffn_down rows of its
+ * hidden slice [r*D/N, (r+1)*D/N) (each row over its whole input), its share
+ * of the output rows, and the embedding and norms. Every decode step gathers
+ * the FFN's hidden vector and the residual stream from the ranks' slices and
+ * picks the argmax over their vocabulary slices, over peer memory inside the
+ * decode kernel; each value is computed by one rank exactly as one GPU
+ * computes it, so logits and tokens are those of the single-GPU model. Each
+ * wait is bounded (a lost rank ends the step with an error, never a hang).
+ * Greedy decode only. cxm_model_config reports the whole model. The model
+ * runs after cxm_tp_connect. Hidden size and FFN width must split over the
+ * ranks in multiples of 4. */
 int cxm_model_open_tp(const char *gguf_path, int device, int tp_rank, int tp_size, cxm_model **out);
 #define CXM_TP_HANDLE_BYTES 64
 /* The CUDA IPC handle of this rank's exchange area (CXM_TP_HANDLE_BYTES). */
@@ -106,7 +118,9 @@ void cxm_sampler_free(cxm_sampler *s);
 uint64_t cxm_sampler_state(const cxm_sampler *s);
 
 /* Muestreador::elegir (src/sampler.rs:61-126) on the logits of the model's
- * last forward, computed on the device: greedy (first maximum) or, with
+ * last forward. Greedy (first maximum) reads the pick cxm_forward already
+ * brought back with its error word (one host synchronisation per forward
+ * and pick); with
  * temperature > 0, the reference's top-p draw with its sums in its order and
  * equal probabilities ordered by index (the reference's unstable sort leaves
  * their order unspecified). Advances the sampler's state like the reference. */
@@ -116,7 +130,8 @@ int cxm_sample(cxm_model *m, cxm_sampler *s, uint32_t *token_out);
  * sample -> forward one token, up to max_new tokens, stopping at the model's
  * eos and before the context overflows. The per-token step is one launch of
  * a persistent kernel, replayed as a CUDA graph; position and token live in
- * device memory. */
+ * device memory. The eos pick sets a device flag: the steps queued after it
+ * return at once, and neither pick nor forward another token. */
 int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, uint32_t n_prompt, uint32_t max_new,
                  cxm_sampler *s, uint32_t *out, uint32_t *n_out);
 
@@ -213,6 +228,8 @@ typedef struct {
     uint64_t seed;
     float sigma;        /* N(0, sigma) for every matrix */
     int32_t threads;    /* 0 = all host threads */
+    int32_t has_eos;    /* write tokenizer.ggml.eos_token_id = eos (0: no eos key, generation never stops early) */
+    uint32_t eos;
 } cxm_synth_spec;
 
 /* Write a seeded random-init qwen2-keyed GGUF: row r of tensor `name` draws

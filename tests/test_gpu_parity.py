@@ -209,6 +209,54 @@ def test_uniform_format_model_matches_oracle(tmp_path, t):
     assert dev.estado == ref.state
 
 
+@pytest.mark.parametrize("t", [cx.Q4_K, cx.Q6_K, cx.Q5_K, cx.Q3_K, cx.Q2_K])
+def test_tensor_core_prompt_forward_equals_the_step_replay(tmp_path, t):
+    # a 24+ token forward call on the tensor cores against the same call
+    # replayed through the decode step: logits and every KV row bit for bit
+    p = str(tmp_path / f"tiny_{t}.gguf")
+    cx.synth_write(p, cx.synth_spec("tiny", seed=9, type=t, tied=1, n_layer=3))
+    m = cx.Modelo(p)
+    prompt = prompt_of(21, 150, m.cfg.vocab)  # two M-tiles of tokens, the second ragged
+    a, b = m.cache(200), m.cache(200)
+    m.set_prefill(True)
+    la = m.forward(prompt, a)
+    m.set_prefill(False)
+    lb = m.forward(prompt, b)
+    m.set_prefill(True)
+    np.testing.assert_array_equal(la, lb)
+    for layer in range(m.cfg.n_layer):
+        for v in (False, True):
+            np.testing.assert_array_equal(a.capa(layer, v), b.capa(layer, v))
+    # continuing after a tensor-core prefix: a second call of 30 tokens
+    np.testing.assert_array_equal(m.forward(prompt[:30], a), m.forward(prompt[:30], b))
+
+
+def test_generation_stops_at_eos_on_the_device(tmp_path):
+    # src/forward.rs:544-547: the eos pick ends the generation unpicked and
+    # unforwarded; the device skips every step after it
+    base = str(tmp_path / "noeos.gguf")
+    cx.synth_write(base, cx.synth_spec("tiny", seed=42, n_layer=2))
+    om = O.Model(base)
+    prompt = prompt_of(4, 30, 8192)
+    free = om.generate(om.cache(), prompt, 16, O.Sampler(0, 0.0, 1.0))
+    eos = free[6]
+    stop = free.index(eos)
+    p = str(tmp_path / "eos.gguf")
+    cx.synth_write(p, cx.synth_spec("tiny", seed=42, n_layer=2, eos=eos))
+    m, om2 = cx.Modelo(p), O.Model(p)
+    assert m.cfg.has_eos and m.cfg.eos == eos
+    c, oc = m.cache(128), om2.cache()
+    got = m.generar(prompt, 64, cx.Muestreador.voraz(), c)
+    want = om2.generate(oc, prompt, 64, O.Sampler(0, 0.0, 1.0))
+    assert got == want == free[:stop]
+    assert len(c) == len(oc) == len(prompt) + stop
+    # the cache keeps working after a stopped generation
+    np.testing.assert_array_equal(m.forward([5, 6], c), om2.forward(oc, [5, 6]))
+    dev, ref = cx.Muestreador(3, 0.7, 0.9), O.Sampler(3, 0.7, 0.9)
+    assert m.generar(prompt, 40, dev, m.cache(128)) == om2.generate(om2.cache(), prompt, 40, ref)
+    assert dev.estado == ref.state
+
+
 def test_cache_prefix_truncate_clear(tiny_path):
     # src/forward.rs:587-603 and src/engine_own.rs:207-245 semantics
     m = cx.Modelo(tiny_path)
