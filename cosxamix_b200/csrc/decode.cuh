@@ -1004,10 +1004,10 @@ __device__ __forceinline__ float seq_sum(const float *p, int n) {
 }
 
 // One attention item: head h and dims [d0, d0 + 32) (src/ops.rs:1258-1325).
-// The head's scores staged in shared memory; their max, exp(s - max)
-// (src/ops.rs:1206-1230) and the products by 1/total across the CTA; the sum
-// position by position by thread 0; then warp 0 adds prob_p·v_p[d] position
-// by position, lane d for dim d0 + d, over the transposed V chunks.
+// The head's scores staged in shared memory; their max and exp(s - max)
+// (src/ops.rs:1206-1230) across the CTA; the sum position by position by
+// thread 0; then warp 0 adds prob_p·v_p[d] position by position, lane d for
+// dim d0 + d, over the transposed V chunks.
 
 // V chunk c of an item into its ring slot, transposed (the caller commits
 // the cp.async group)
@@ -1039,6 +1039,35 @@ __device__ __forceinline__ void attn_prefetch(const AtPhase &at, int n, int max_
     }
 }
 
+// acc + Σ (e[r]·inv)·v[r] over the cnt positions of a chunk, one position
+// after another (lane d: its dim's row of the transposed chunk)
+__device__ __forceinline__ void pv_chunk(const float *vt, const float *pp, int cnt, float inv, float &acc) {
+    int r = 0;
+    for (; r + 16 <= cnt; r += 16) {
+        float4 q[4];
+        float w[16];
+#pragma unroll
+        for (int k = 0; k < 4; k++) q[k] = ((const float4 *)(pp + r))[k];
+#pragma unroll
+        for (int k = 0; k < 16; k++) w[k] = vt[r + k];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            acc = fa(acc, fm(fm(q[k].x, inv), w[4 * k]));
+            acc = fa(acc, fm(fm(q[k].y, inv), w[4 * k + 1]));
+            acc = fa(acc, fm(fm(q[k].z, inv), w[4 * k + 2]));
+            acc = fa(acc, fm(fm(q[k].w, inv), w[4 * k + 3]));
+        }
+    }
+    for (; r < cnt; r++) acc = fa(acc, fm(fm(pp[r], inv), vt[r]));
+}
+
+// The head's scores come in from L2 with each thread's running max; every
+// thread then takes exp(s - max) of the same values (no barrier between);
+// thread 0 adds them in order and forms 1/total; warp 0 adds (e·inv)·v
+// position by position — e·inv is the reference's probability, formed where
+// it is used. When the prefetch before the barrier staged every V chunk (a
+// context up to (ring - 1)·kAttnPos positions), the PV runs without a
+// barrier per chunk.
 __device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos, float *region, float *red,
                                            float *bc) {
     const int tid = threadIdx.x, nt = kDW * 32, lane = tid & 31, warp = tid >> 5, hd = at.hd, ns = hd / 32;
@@ -1046,6 +1075,7 @@ __device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos
     float *pr = region;
     float *ring = region + ((max_pos + 3) & ~3);
     const int nchunks = (n + kAttnPos - 1) / kAttnPos;
+    const bool staged = nchunks <= R - 1;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int h = item / ns, d0 = (item % ns) * 32;
         const float *vb = attn_vbase(at, item);
@@ -1055,58 +1085,61 @@ __device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos
                 cp_async_commit();
             }
         const int n4 = (n + 3) / 4;
-        for (int i = tid; i < n4; i += nt)
-            ((float4 *)pr)[i] = __ldcg((const float4 *)(at.scores + (size_t)h * at.score_stride) + i);
-        dsync();
+        const float4 *sc = (const float4 *)(at.scores + (size_t)h * at.score_stride);
         float m = -INFINITY;
-        for (int i = tid; i < n; i += nt) m = fmaxf(m, pr[i]);
+        for (int i = tid; i < n4; i += nt) {
+            const float4 v = __ldcg(sc + i);
+            ((float4 *)pr)[i] = v;
+            const int p = 4 * i;
+            m = fmaxf(m, v.x);
+            if (p + 1 < n) m = fmaxf(m, v.y);
+            if (p + 2 < n) m = fmaxf(m, v.z);
+            if (p + 3 < n) m = fmaxf(m, v.w);
+        }
+        if (staged) cp_async_wait<0>();  // the barrier below publishes every thread's V copies
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (lane == 0) red[warp] = m;
         dsync();
         float mx = red[0];
         for (int w = 1; w < kDW; w++) mx = fmaxf(mx, red[w]);
-        if (!isfinite(mx)) {  // every score -inf (or NaN): uniform (src/ops.rs:1213-1218)
+        float inv = 1.0f;
+        if (!isfinite(mx)) {  // every score -inf (or NaN): uniform (src/ops.rs:1213-1218); u·1 = u
             const float u = __fdiv_rn(1.0f, (float)n);
             for (int i = tid; i < n; i += nt) pr[i] = u;
+            dsync();
         } else {
-            for (int i = tid; i < n; i += nt) pr[i] = expf_glibc(fs(pr[i], mx));
+            for (int i = tid; i < n4; i += nt) {
+                const int p = 4 * i;
+                float4 v = ((const float4 *)pr)[i];
+                v.x = expf_glibc(fs(v.x, mx));
+                if (p + 1 < n) v.y = expf_glibc(fs(v.y, mx));
+                if (p + 2 < n) v.z = expf_glibc(fs(v.z, mx));
+                if (p + 3 < n) v.w = expf_glibc(fs(v.w, mx));
+                ((float4 *)pr)[i] = v;
+            }
             dsync();
             if (tid == 0) *bc = __fdiv_rn(1.0f, seq_sum(pr, n));
             dsync();
-            const float inv = *bc;
-            for (int i = tid; i < n; i += nt) pr[i] = fm(pr[i], inv);
+            inv = *bc;
         }
-        dsync();
         float acc = 0.0f;
-        for (int c = 0; c < nchunks; c++) {
-            attn_stage(at, n, vb, ring, c + R - 1);
-            cp_async_commit();
-            cp_async_wait_n(R - 1);
-            dsync();
-            if (warp == 0) {
-                const float *vt = ring + (c % R) * kAttnChunkFloats + lane * (kAttnPos + 1);
-                const int base = c * kAttnPos, cnt = min(kAttnPos, n - base);
-                const float *pp = pr + base;
-                int r = 0;
-                for (; r + 16 <= cnt; r += 16) {
-                    float4 q[4];
-                    float w[16];
-#pragma unroll
-                    for (int k = 0; k < 4; k++) q[k] = ((const float4 *)(pp + r))[k];
-#pragma unroll
-                    for (int k = 0; k < 16; k++) w[k] = vt[r + k];
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        acc = fa(acc, fm(q[k].x, w[4 * k]));
-                        acc = fa(acc, fm(q[k].y, w[4 * k + 1]));
-                        acc = fa(acc, fm(q[k].z, w[4 * k + 2]));
-                        acc = fa(acc, fm(q[k].w, w[4 * k + 3]));
-                    }
-                }
-                for (; r < cnt; r++) acc = fa(acc, fm(pp[r], vt[r]));
+        if (staged) {
+            if (warp == 0)
+                for (int c = 0; c < nchunks; c++)
+                    pv_chunk(ring + (c % R) * kAttnChunkFloats + lane * (kAttnPos + 1), pr + c * kAttnPos,
+                             min(kAttnPos, n - c * kAttnPos), inv, acc);
+        } else {
+            for (int c = 0; c < nchunks; c++) {
+                attn_stage(at, n, vb, ring, c + R - 1);
+                cp_async_commit();
+                cp_async_wait_n(R - 1);
+                dsync();
+                if (warp == 0)
+                    pv_chunk(ring + (c % R) * kAttnChunkFloats + lane * (kAttnPos + 1), pr + c * kAttnPos,
+                             min(kAttnPos, n - c * kAttnPos), inv, acc);
+                dsync();
             }
-            dsync();
         }
         if (warp == 0) at.out[(size_t)h * hd + d0 + lane] = acc;
         cp_async_wait<0>();
