@@ -68,6 +68,8 @@ def lib() -> C.CDLL:
             "cxm_cache_truncate": (C.c_int, [P, C.c_uint32]),
             "cxm_cache_clear": (C.c_int, [P]),
             "cxm_cache_copy_prefix": (C.c_int, [P, C.c_uint32, P]),
+            "cxm_cache_share_prefix": (C.c_int, [P, C.c_uint32, P]),
+            "cxm_generate_batch": (C.c_int, [P, P, P, P, C.c_uint32, C.c_uint32, P, P]),
             "cxm_cache_read": (C.c_int, [P, C.c_uint32, C.c_int, P]),
             "cxm_forward": (C.c_int, [P, P, P, C.c_uint32, P]),
             "cxm_sampler_new": (C.c_int, [C.c_uint64, C.c_float, C.c_float, C.POINTER(P)]),
@@ -223,6 +225,13 @@ class Cache:
         this cache's own buffers, which keeps its captured decode graphs)."""
         _check(lib().cxm_cache_copy_prefix(src.h, n, self.h))
 
+    def compartir_prefijo(self, src: "Cache", n: int) -> None:
+        """Borrow the first n tokens of `src` as a shared prefix, held once
+        (include/cxm.h: cxm_cache_share_prefix)."""
+        _check(lib().cxm_cache_share_prefix(src.h, n, self.h))
+
+    share_prefix = compartir_prefijo
+
     def capa(self, layer: int, v: bool = False) -> np.ndarray:
         """Layer `layer`'s K (or V) rows [0, len): this rank's KV heads."""
         cfg = self.modelo.cfg
@@ -311,6 +320,23 @@ class Modelo:
         return out[: n.value].tolist()
 
     generate = generar
+
+    def generar_lote(self, prompts, max_nuevos: int, caches: "list[Cache]") -> list[list[int]]:
+        """Greedy Modelo::generar for several conversations at once, one cache
+        each (include/cxm.h: cxm_generate_batch)."""
+        n = len(caches)
+        ps = [np.ascontiguousarray(p, np.uint32) for p in prompts]
+        if len(ps) != n:
+            raise ValueError("one prompt per cache")
+        hs = (P * n)(*[c.h for c in caches])
+        pp = (P * n)(*[p.ctypes.data_as(P) for p in ps])
+        lens = np.array([p.size for p in ps], np.uint32)
+        out = np.zeros((n, max(max_nuevos, 1)), np.uint32)
+        n_out = np.zeros(n, np.uint32)
+        _check(lib().cxm_generate_batch(self.h, hs, pp, _ptr(lens), n, max_nuevos, _ptr(out), _ptr(n_out)))
+        return [out[z, : n_out[z]].tolist() for z in range(n)]
+
+    generate_batch = generar_lote
 
     # measurement hooks (device-timed; include/cxm.h)
     def bench_decode(self, cache: Cache, steps: int, sampler: "Muestreador | None" = None) -> float:

@@ -185,6 +185,8 @@ struct MvPhase {
 
 struct AtPhase {
     const float *q, *k, *v;  // k/v: this layer's cache, [max_pos][KV*hd]
+    const float *kp, *vp;    // a borrowed prefix's layer K/V: positions below plen are read there
+    int plen;
     float *out, *scores;
     int H, KV, hd, score_stride, P;  // P: positions per score item
     int ring;                        // V chunks in the attention phase's ring
@@ -923,7 +925,7 @@ __device__ __forceinline__ void scores_prefetch(const AtPhase &at, int n, float 
         const int g = item / nchunk, p0 = (item % nchunk) * P, cnt = min(P, n - 1 - p0);  // not position n-1
         for (int i = tid; i < cnt * c4; i += kDW * 32) {
             const int r = i / c4, c = i - r * c4;
-            cp_async16(region + r * (hd + 4) + 4 * c, at.k + (size_t)(p0 + r) * kvd + (size_t)g * hd + 4 * c);
+            cp_async16(region + r * (hd + 4) + 4 * c, kv_row(at.k, at.kp, at.plen, p0 + r, kvd, (size_t)g * hd + 4 * c));
         }
     }
     cp_async_commit();
@@ -948,7 +950,7 @@ __device__ __forceinline__ void phase_scores(const AtPhase &at, int n, float *re
         const int r0 = first ? (n - 1 >= p0 && n - 1 < p0 + cnt ? n - 1 - p0 : cnt) : 0;
         for (int i = tid; i < (cnt - r0) * c4; i += kDW * 32) {
             const int r = r0 + i / c4, c = i % c4;
-            cp_async16(ks + r * (hd + 4) + 4 * c, at.k + (size_t)(p0 + r) * kvd + (size_t)g * hd + 4 * c);
+            cp_async16(ks + r * (hd + 4) + 4 * c, kv_row(at.k, at.kp, at.plen, p0 + r, kvd, (size_t)g * hd + 4 * c));
         }
         cp_async_commit();
         cp_async_wait<0>();
@@ -1011,20 +1013,21 @@ __device__ __forceinline__ float seq_sum(const float *p, int n) {
 
 // V chunk c of an item into its ring slot, transposed (the caller commits
 // the cp.async group)
-__device__ __forceinline__ void attn_stage(const AtPhase &at, int n, const float *vb, float *ring, int c) {
+__device__ __forceinline__ void attn_stage(const AtPhase &at, int n, size_t voff, float *ring, int c) {
     const int tid = threadIdx.x, kvd = at.KV * at.hd;
     if (c * kAttnPos >= n) return;
     const int base = c * kAttnPos, cnt = min(kAttnPos, n - base);
     float *dst = ring + (c % at.ring) * kAttnChunkFloats;
     for (int i = tid; i < cnt * 32; i += kDW * 32) {
         const int p = i >> 5, d = i & 31;
-        cp_async4(dst + d * (kAttnPos + 1) + p, vb + (size_t)(base + p) * kvd + d);
+        cp_async4(dst + d * (kAttnPos + 1) + p, kv_row(at.v, at.vp, at.plen, base + p, kvd, voff + d));
     }
 }
 
-__device__ __forceinline__ const float *attn_vbase(const AtPhase &at, int item) {
+// the item's 32 dims of a V row: their offset in the row
+__device__ __forceinline__ size_t attn_voff(const AtPhase &at, int item) {
     const int ns = at.hd / 32, h = item / ns, G = at.H / at.KV;
-    return at.v + (size_t)(h / G) * at.hd + (item % ns) * 32;
+    return (size_t)(h / G) * at.hd + (item % ns) * 32;
 }
 
 // Before the attention phase's grid barrier: the first ring - 1 V chunks of
@@ -1034,7 +1037,7 @@ __device__ __forceinline__ void attn_prefetch(const AtPhase &at, int n, int max_
     const int items = at.H * (at.hd / 32), item = blockIdx.x;
     float *ring = region + ((max_pos + 3) & ~3);
     for (int c = 0; c < at.ring - 1; c++) {
-        if (item < items) attn_stage(at, n, attn_vbase(at, item), ring, c);
+        if (item < items) attn_stage(at, n, attn_voff(at, item), ring, c);
         cp_async_commit();
     }
 }
@@ -1078,7 +1081,7 @@ __device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos
     const bool staged = nchunks <= R - 1;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int h = item / ns, d0 = (item % ns) * 32;
-        const float *vb = attn_vbase(at, item);
+        const size_t vb = attn_voff(at, item);
         if (item != (int)blockIdx.x)  // the first item's first chunks were staged before the barrier
             for (int c = 0; c < R - 1; c++) {
                 attn_stage(at, n, vb, ring, c);

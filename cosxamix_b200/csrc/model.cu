@@ -92,6 +92,20 @@ struct cxm_model {
         float *e16 = nullptr, *s16 = nullptr, *e32 = nullptr, *s32 = nullptr;
         size_t score_floats = 0;
     } pf;
+    struct Batch {  // batched decode: per-conversation views, allocated at the first such call
+        int cap = 0;
+        void *mem = nullptr;  // one allocation for all of it
+        float *logits = nullptr;           // [cap][vocab]
+        uint32_t *tok = nullptr;           // [cap] the step's tokens
+        int *pos = nullptr;                // [cap] their positions
+        float **kz = nullptr, **vz = nullptr;            // [n_layer][cap] layer bases of each cache
+        const float **kpz = nullptr, **vpz = nullptr;    // [n_layer][cap] of each borrowed prefix
+        int *plenz = nullptr;              // [cap]
+        uint32_t **toks = nullptr;         // [cap] each cache's token array
+        int **len = nullptr, **stop = nullptr;  // [cap] each cache's position and eos flag
+        cudaGraphExec_t graph = nullptr;   // one batched step over the current views
+        int graph_n = 0;
+    } bt;
 
     ~cxm_model() {
         if (device >= 0) cudaSetDevice(device);
@@ -101,6 +115,8 @@ struct cxm_model {
         for (void *p : {(void *)pf.x, (void *)pf.q, (void *)pf.att, (void *)pf.h, (void *)pf.scores, (void *)pf.a16,
                         (void *)pf.a32, (void *)pf.e16, (void *)pf.s16, (void *)pf.e32, (void *)pf.s32})
             cudaFree(p);
+        if (bt.graph) cudaGraphExecDestroy(bt.graph);
+        cudaFree(bt.mem);
         if (hw) cudaFreeHost(hw);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -136,16 +152,34 @@ struct cxm_cache {
     uint32_t *toks = nullptr;          // [max_tokens + 2]
     int *d_len = nullptr;
     int *d_stop = nullptr;             // set by a step whose pick is the model's eos
+    // A shared prefix (src/engine_own.rs:198-245 borrows a session's cache by
+    // copy; here it is held once): positions below plen are read from
+    // prefix's K/V, never copied. A cache that lends keeps the positions below
+    // `lent` as they are while `borrowers` > 0; freed while lent, it lives on
+    // (orphan) until its last borrower lets go.
+    cxm_cache *prefix = nullptr;
+    uint32_t plen = 0;
+    int borrowers = 0;
+    uint32_t lent = 0;
+    bool orphan = false;
     // one program and one graph per step mode and row class (RowClass)
     Program prog[4][3];
     cudaGraphExec_t graph[4][3] = {};
-    ~cxm_cache() {
+    void drop_programs() {  // the programs bake in the cache's prefix
         if (device >= 0) cudaSetDevice(device);
         for (auto &gm : graph)
-            for (auto &g : gm)
+            for (auto &g : gm) {
                 if (g) cudaGraphExecDestroy(g);
+                g = nullptr;
+            }
         for (auto &pm : prog)
-            for (auto &p : pm) cudaFree(p.d);
+            for (auto &p : pm) {
+                cudaFree(p.d);
+                p = Program{};
+            }
+    }
+    ~cxm_cache() {
+        drop_programs();
         cudaFree(k);
         cudaFree(v);
         cudaFree(toks);
@@ -153,6 +187,27 @@ struct cxm_cache {
         cudaFree(d_stop);
     }
 };
+
+// the layer base of a cache's borrowed prefix (nullptr without one)
+static const float *prefix_k(const cxm_cache *c, int l, size_t kvd) {
+    return c->prefix ? c->prefix->k + (size_t)l * c->prefix->max_tokens * kvd : nullptr;
+}
+static const float *prefix_v(const cxm_cache *c, int l, size_t kvd) {
+    return c->prefix ? c->prefix->v + (size_t)l * c->prefix->max_tokens * kvd : nullptr;
+}
+
+// c stops borrowing its prefix; an orphaned lender goes with its last borrower
+static void release_prefix(cxm_cache *c) {
+    cxm_cache *p = c->prefix;
+    if (!p) return;
+    c->prefix = nullptr;
+    c->plen = 0;
+    c->drop_programs();
+    if (--p->borrowers == 0) {
+        p->lent = 0;
+        if (p->orphan) delete p;
+    }
+}
 
 struct cxm_sampler {
     uint64_t state;
@@ -492,11 +547,20 @@ int pf_rows(cxm_model *m, const float *in, int ld, const float *norm_w, float ep
     return 0;
 }
 
+// rows of several conversations (batched decode): per-row positions and
+// cache bases, each row in the order of a forward call of one row (the
+// segment's own order: mv_seg with ROWS_FEW)
+struct PfRowsDest {
+    const int *pos = nullptr;
+    float *const *out = nullptr;
+    int fused = 0;
+};
+
 // out = W·x for the t rows quantized last, each output in the buffered
 // path's order, then the segment's epilogue (tokens at positions pos0..)
 int pf_gemm(cudaStream_t st, const MvSeg &seg, int t, int pos0, int ld_out, const int8_t *a16, const int8_t *a32,
             const float *e16, const float *s16, const float *e32, const float *s32, const float *rc, const float *rs,
-            int *err) {
+            int *err, const PfRowsDest &rd = PfRowsDest{}) {
     const int sub = sub_of(seg.M.type), N = pf_rows_per_tile(sub);
     PfGemm G{};
     G.seg = seg;
@@ -510,6 +574,11 @@ int pf_gemm(cudaStream_t st, const MvSeg &seg, int t, int pos0, int ld_out, cons
     G.rope_cos = rc;
     G.rope_sin = rs;
     G.err = err;
+    G.row_pos = rd.pos;
+    G.row_out = rd.out;
+    // the one-row order is the fused kernel's only where the reference has
+    // one for the format (src/ops.rs:837-858); Q5_K and Q2_K stay buffered
+    G.fused = rd.fused && seg.ord == ORD_FUSED;
     const PfSmem L = pf_smem(seg.M.type, seg.M.K);
     // at least 116 KB, so no two of these CTAs share an SM (each takes all 512 TMEM columns)
     const size_t smem = std::max<size_t>(L.total + 128, 116 * 1024);
@@ -546,9 +615,9 @@ int pf_reserve(cxm_model *m, int cap) {
     return 0;
 }
 
-int pf_seg_gemm(cxm_model *m, const MvSeg &seg, int t, int pos0, int ld_out) {
+int pf_seg_gemm(cxm_model *m, const MvSeg &seg, int t, int pos0, int ld_out, const PfRowsDest &rd = PfRowsDest{}) {
     return pf_gemm(m->stream, seg, t, pos0, ld_out, m->pf.a16, m->pf.a32, m->pf.e16, m->pf.s16, m->pf.e32, m->pf.s32,
-                   m->rope_cos, m->rope_sin, m->err);
+                   m->rope_cos, m->rope_sin, m->err, rd);
 }
 
 // The prompt forward (src/forward.rs:375-492 over several tokens at once)
@@ -599,6 +668,9 @@ int prefill_tokens(cxm_model *m, cxm_cache *c, uint32_t p0, uint32_t n) {
                 a.q = m->pf.q + (size_t)z0 * dq;
                 a.k = kl;
                 a.v = vl;
+                a.kp = prefix_k(c, l, kvd);
+                a.vp = prefix_v(c, l, kvd);
+                a.plen = c->prefix ? (int)c->plen : 0;
                 a.out = m->pf.att + (size_t)z0 * dq;
                 a.scores = m->pf.scores;
                 a.d_len = nullptr;
@@ -770,6 +842,9 @@ std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode, int cls) {
         at.q = m->q;
         at.k = kl;
         at.v = vl;
+        at.kp = prefix_k(c, l, kvd);
+        at.vp = prefix_v(c, l, kvd);
+        at.plen = c->prefix ? (int)c->plen : 0;
         at.out = m->att;
         at.scores = m->scores;
         at.H = H;
@@ -1362,7 +1437,15 @@ extern "C" int cxm_cache_new(cxm_model *m, uint32_t max_tokens, cxm_cache **out)
     return 0;
 }
 
-extern "C" void cxm_cache_free(cxm_cache *c) { delete c; }
+extern "C" void cxm_cache_free(cxm_cache *c) {
+    if (!c) return;
+    release_prefix(c);
+    if (c->borrowers > 0) {  // still lent: deleted with its last borrower
+        c->orphan = true;
+        return;
+    }
+    delete c;
+}
 extern "C" uint32_t cxm_cache_len(const cxm_cache *c) { return c ? c->len : 0; }
 
 static int set_len(cxm_cache *c, uint32_t n) {
@@ -1380,6 +1463,14 @@ extern "C" int cxm_cache_truncate(cxm_cache *c, uint32_t n) {
         return -1;
     }
     if (n >= c->len) return 0;  // Cache::truncar keeps everything when n >= len
+    if (n < c->lent) {
+        set_error("positions below %u are lent to %d cache(s) as a shared prefix", c->lent, c->borrowers);
+        return -1;
+    }
+    if (n < c->plen) {  // borrows less of its prefix
+        c->plen = n;
+        c->drop_programs();
+    }
     return set_len(c, n);
 }
 
@@ -1388,6 +1479,11 @@ extern "C" int cxm_cache_clear(cxm_cache *c) {
         set_error("null cache");
         return -1;
     }
+    if (c->lent) {
+        set_error("positions below %u are lent to %d cache(s) as a shared prefix", c->lent, c->borrowers);
+        return -1;
+    }
+    release_prefix(c);
     return set_len(c, 0);
 }
 
@@ -1402,13 +1498,72 @@ extern "C" int cxm_cache_copy_prefix(const cxm_cache *src, uint32_t n, cxm_cache
         set_error("prefix of %u tokens does not fit a cache of %u", n, dst->max_tokens);
         return -1;
     }
+    if (dst == src) {
+        set_error("a cache cannot copy its own prefix");
+        return -1;
+    }
+    if (dst->lent) {
+        set_error("positions below %u of the destination are lent as a shared prefix", dst->lent);
+        return -1;
+    }
     CU(cudaSetDevice(m->device));
     const size_t kvd = kv_dim(m);
+    release_prefix(dst);  // the copy is the destination's own
     if (n) {
-        CU(cudaMemcpy2DAsync(dst->k, dst->max_tokens * kvd * 4, src->k, src->max_tokens * kvd * 4, n * kvd * 4,
-                             m->cfg.n_layer, cudaMemcpyDeviceToDevice, m->stream));
-        CU(cudaMemcpy2DAsync(dst->v, dst->max_tokens * kvd * 4, src->v, src->max_tokens * kvd * 4, n * kvd * 4,
-                             m->cfg.n_layer, cudaMemcpyDeviceToDevice, m->stream));
+        // rows below the source's borrowed prefix come from the lender
+        const uint32_t np = std::min(n, src->plen);
+        for (int part = 0; part < 2; part++) {
+            const uint32_t r0 = part ? np : 0, r1 = part ? n : np;
+            if (r1 <= r0) continue;
+            const cxm_cache *from = part ? src : src->prefix;
+            const size_t off = (size_t)r0 * kvd;
+            CU(cudaMemcpy2DAsync(dst->k + off, dst->max_tokens * kvd * 4, from->k + off, from->max_tokens * kvd * 4,
+                                 (r1 - r0) * kvd * 4, m->cfg.n_layer, cudaMemcpyDeviceToDevice, m->stream));
+            CU(cudaMemcpy2DAsync(dst->v + off, dst->max_tokens * kvd * 4, from->v + off, from->max_tokens * kvd * 4,
+                                 (r1 - r0) * kvd * 4, m->cfg.n_layer, cudaMemcpyDeviceToDevice, m->stream));
+        }
+        CU(cudaMemcpyAsync(dst->toks, src->toks, (size_t)(n + 1 <= src->max_tokens + 1 ? n + 1 : n) * 4,
+                           cudaMemcpyDeviceToDevice, m->stream));
+    }
+    return set_len(dst, n);
+}
+
+extern "C" int cxm_cache_share_prefix(cxm_cache *src, uint32_t n, cxm_cache *dst) {
+    if (!src || !dst || src->m != dst->m || src == dst) {
+        set_error("two distinct caches of the same model are needed");
+        return -1;
+    }
+    if (src->orphan) {
+        set_error("the source cache was freed");
+        return -1;
+    }
+    n = std::min(n, src->len);
+    if (n > dst->max_tokens) {
+        set_error("prefix of %u tokens does not fit a cache of %u", n, dst->max_tokens);
+        return -1;
+    }
+    if (dst->lent) {
+        set_error("positions below %u of the destination are lent as a shared prefix", dst->lent);
+        return -1;
+    }
+    // a prefix of a borrower is a prefix of its lender (one level of lending)
+    cxm_cache *lender = src;
+    if (src->prefix) {
+        if (n > src->plen) {
+            set_error("the source borrows its first %u positions: share at most those, or copy", src->plen);
+            return -1;
+        }
+        lender = src->prefix;
+    }
+    cxm_model *m = src->m;
+    CU(cudaSetDevice(m->device));
+    release_prefix(dst);
+    dst->drop_programs();
+    if (n) {
+        dst->prefix = lender;
+        dst->plen = n;
+        lender->borrowers++;
+        lender->lent = std::max(lender->lent, n);
         CU(cudaMemcpyAsync(dst->toks, src->toks, (size_t)(n + 1 <= src->max_tokens + 1 ? n + 1 : n) * 4,
                            cudaMemcpyDeviceToDevice, m->stream));
     }
@@ -1425,7 +1580,13 @@ extern "C" int cxm_cache_read(const cxm_cache *c, uint32_t layer, int is_v, floa
     const size_t kvd = kv_dim(m);
     const float *base = (is_v ? c->v : c->k) + (size_t)layer * c->max_tokens * kvd;
     CU(cudaStreamSynchronize(m->stream));
-    CU(cudaMemcpy(host_out, base, (size_t)c->len * kvd * 4, cudaMemcpyDeviceToHost));
+    const uint32_t np = std::min(c->plen, c->len);
+    if (np) {  // the borrowed rows from the lender
+        const float *pb = is_v ? prefix_v(c, (int)layer, kvd) : prefix_k(c, (int)layer, kvd);
+        CU(cudaMemcpy(host_out, pb, (size_t)np * kvd * 4, cudaMemcpyDeviceToHost));
+    }
+    CU(cudaMemcpy(host_out + (size_t)np * kvd, base + (size_t)np * kvd, (size_t)(c->len - np) * kvd * 4,
+                  cudaMemcpyDeviceToHost));
     return 0;
 }
 
@@ -1590,6 +1751,321 @@ extern "C" int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, 
     }
     uint32_t final_len = (uint32_t)(after + forwarded);
     if (set_len(c, final_len)) return -1;
+    m->logits_valid = false;
+    return 0;
+}
+
+// ── batched decode of several conversations ──
+// One greedy step for B conversations at once: their rows go through the
+// tensor-core GEMMs together (one read of every weight for all of them),
+// each row in the order of a forward call of one row (src/ops.rs:1081-1092
+// with m = 1: the fused per-row kernel), each conversation attending over its
+// own cache and its borrowed prefix. A conversation is, row for row, what
+// src/forward.rs:544-557 computes for it alone.
+
+// the step's token and position of each conversation
+__global__ void k_batch_gather(uint32_t *const *toks, int *const *len, int n, uint32_t *tok, int *pos) {
+    const int z = blockIdx.x * blockDim.x + threadIdx.x;
+    if (z < n) {
+        const int p = *len[z];
+        pos[z] = p;
+        tok[z] = toks[z][p];
+    }
+}
+
+// argmax of each conversation's logits (the first maximum, NaNs skipped;
+// src/sampler.rs:129-137), the token appended and the position advanced —
+// unless the conversation met its eos in an earlier step
+constexpr int kPickThreads = 512;
+__global__ void __launch_bounds__(kPickThreads) k_batch_pick(const float *logits, int V, uint32_t *const *toks,
+                                                             int *const *len, int *const *stop, int eos, int pick) {
+    __shared__ unsigned long long best_s[kPickThreads / 32];
+    const int z = blockIdx.x, tid = threadIdx.x;
+    if (*(volatile int *)stop[z]) return;  // the whole block
+    unsigned long long best = 0ull;
+    if (pick) {
+        const float *l = logits + (size_t)z * V;
+        for (int i = tid; i < V; i += kPickThreads) {
+            const float v = l[i];
+            const unsigned long long k = v == v ? argmax_key(v, (uint32_t)i) : 0ull;
+            best = k > best ? k : best;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+            best = v > best ? v : best;
+        }
+        if ((tid & 31) == 0) best_s[tid >> 5] = best;
+        __syncthreads();
+    }
+    if (tid == 0) {
+        const int p = *len[z];
+        if (pick) {
+            for (int w = 0; w < kPickThreads / 32; w++) best = best_s[w] > best ? best_s[w] : best;
+            const uint32_t t = argmax_index(best);
+            toks[z][p + 1] = t;
+            if (eos >= 0 && t == (uint32_t)eos) *stop[z] = 1;
+        }
+        *len[z] = p + 1;
+    }
+}
+
+// the per-conversation views of n caches, on the device
+static int batch_views(cxm_model *m, cxm_cache *const *cs, int n) {
+    cxm_model::Batch &B = m->bt;
+    const int L = m->cfg.n_layer;
+    const size_t kvd = kv_dim(m);
+    if (B.cap < n) {
+        if (B.graph) cudaGraphExecDestroy(B.graph);
+        B.graph = nullptr;
+        cudaFree(B.mem);
+        B = cxm_model::Batch{};
+        const int cap = std::max(n, 8);
+        const size_t bytes = (size_t)cap * m->cfg.vocab * 4 + (size_t)cap * 4 * 3 + (size_t)L * cap * 8 * 4 +
+                             (size_t)cap * 8 * 3 + 256;
+        CU(cudaMalloc(&B.mem, bytes));
+        char *p = (char *)B.mem;
+        auto take = [&](size_t nb) {
+            char *r = p;
+            p += (nb + 15) & ~(size_t)15;
+            return (void *)r;
+        };
+        B.logits = (float *)take((size_t)cap * m->cfg.vocab * 4);
+        B.tok = (uint32_t *)take((size_t)cap * 4);
+        B.pos = (int *)take((size_t)cap * 4);
+        B.plenz = (int *)take((size_t)cap * 4);
+        B.kz = (float **)take((size_t)L * cap * 8);
+        B.vz = (float **)take((size_t)L * cap * 8);
+        B.kpz = (const float **)take((size_t)L * cap * 8);
+        B.vpz = (const float **)take((size_t)L * cap * 8);
+        B.toks = (uint32_t **)take((size_t)cap * 8);
+        B.len = (int **)take((size_t)cap * 8);
+        B.stop = (int **)take((size_t)cap * 8);
+        B.cap = cap;
+    }
+    std::vector<const void *> kz((size_t)L * n), vz((size_t)L * n), kpz((size_t)L * n), vpz((size_t)L * n);
+    std::vector<const void *> tk(n), ln(n), st(n);
+    std::vector<int> plen(n);
+    for (int z = 0; z < n; z++) {
+        const cxm_cache *c = cs[z];
+        for (int l = 0; l < L; l++) {
+            kz[(size_t)l * n + z] = c->k + (size_t)l * c->max_tokens * kvd;
+            vz[(size_t)l * n + z] = c->v + (size_t)l * c->max_tokens * kvd;
+            kpz[(size_t)l * n + z] = prefix_k(c, l, kvd);
+            vpz[(size_t)l * n + z] = prefix_v(c, l, kvd);
+        }
+        tk[z] = c->toks;
+        ln[z] = c->d_len;
+        st[z] = c->d_stop;
+        plen[z] = c->prefix ? (int)c->plen : 0;
+    }
+    // the layer arrays are [n_layer][n]: row stride n for this call
+    CU(cudaMemcpy(B.kz, kz.data(), kz.size() * 8, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(B.vz, vz.data(), vz.size() * 8, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(B.kpz, kpz.data(), kpz.size() * 8, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(B.vpz, vpz.data(), vpz.size() * 8, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(B.toks, tk.data(), (size_t)n * 8, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(B.len, ln.data(), (size_t)n * 8, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(B.stop, st.data(), (size_t)n * 8, cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(B.plenz, plen.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+// One step of n conversations (views from batch_views): each forwards the
+// token at its position; with `pick`, the output projection and the greedy
+// pick follow (else only the position advances: the last token's forward).
+static int batch_step(cxm_model *m, int n, int max_pos, bool pick) {
+    const cxm_config &cfg = m->cfg;
+    const cxm_model::Batch &B = m->bt;
+    const int D = cfg.dim, hd = cfg.head_dim, H = m->h_loc, F = cfg.ffn, dq = H * hd;
+    const size_t kvd = kv_dim(m);
+    auto need = [](const QMat &M, int sz) { return sub_of(M.type) == sz ? 1 : 0; };
+    k_batch_gather<<<(n + 127) / 128, 128, 0, m->stream>>>(B.toks, B.len, n, B.tok, B.pos);
+    CU(cudaGetLastError());
+    {
+        const dim3 g((D + 255) / 256, n);
+        k_pf_embed<<<g, 256, 0, m->stream>>>(m->embd, m->embd_f32, B.tok, D, m->pf.x);
+        CU(cudaGetLastError());
+    }
+    PfRowsDest rd;
+    rd.pos = B.pos;
+    rd.fused = 1;
+    for (int l = 0; l < cfg.n_layer; l++) {
+        const Layer &L = m->layers[l];
+        if (pf_rows(m, m->pf.x, D, L.attn_norm, cfg.eps, D, n, need(L.q, 16) | need(L.k, 16) | need(L.v, 16),
+                    need(L.q, 32) | need(L.k, 32) | need(L.v, 32)))
+            return -1;
+        MvSeg sq = mv_seg(L.q, dq / 2, PAIR_ROPE, EPI_ROPE, m->pf.q, ROWS_FEW);
+        sq.half = hd / 2;
+        sq.bias = L.bq;
+        MvSeg sk = mv_seg(L.k, (int)kvd / 2, PAIR_ROPE, EPI_ROPE, nullptr, ROWS_FEW);
+        sk.half = hd / 2;
+        sk.bias = L.bk;
+        sk.at_pos = 1;
+        sk.pos_stride = (int)kvd;
+        MvSeg sv = mv_seg(L.v, (int)kvd / 2, PAIR_ADJ, EPI_STORE, nullptr, ROWS_FEW);
+        sv.bias = L.bv;
+        sv.at_pos = 1;
+        sv.pos_stride = (int)kvd;
+        PfRowsDest rk = rd, rv = rd;
+        rk.out = B.kz + (size_t)l * n;
+        rv.out = B.vz + (size_t)l * n;
+        if (pf_seg_gemm(m, sq, n, 0, dq, rd) || pf_seg_gemm(m, sk, n, 0, 0, rk) || pf_seg_gemm(m, sv, n, 0, 0, rv))
+            return -1;
+        AttnParams a{};
+        a.scores = m->pf.scores;
+        a.qs = dq;
+        a.os = dq;
+        a.H = H;
+        a.KV = m->kv_loc;
+        a.hd = hd;
+        a.max_pos = max_pos;
+        a.score_stride = (max_pos + 3) & ~3;
+        a.scale = 1.0f / sqrtf((float)hd);  // src/ops.rs:1287
+        a.err = m->err;
+        // conversations per launch: their score rows fit the scratch
+        const int tz = (int)std::max<size_t>(
+            1, std::min<size_t>(n, m->pf.score_floats / ((size_t)H * a.score_stride)));
+        for (int z0 = 0; z0 < n; z0 += tz) {
+            AttnParams az = a;
+            az.q = m->pf.q + (size_t)z0 * dq;
+            az.out = m->pf.att + (size_t)z0 * dq;
+            az.kz = B.kz + (size_t)l * n + z0;
+            az.vz = B.vz + (size_t)l * n + z0;
+            az.kpz = B.kpz + (size_t)l * n + z0;
+            az.vpz = B.vpz + (size_t)l * n + z0;
+            az.posz = B.pos + z0;
+            az.plenz = B.plenz + z0;
+            if (launch_attention_on(m->stream, az, std::min(tz, n - z0))) return -1;
+        }
+        if (pf_rows(m, m->pf.att, dq, nullptr, 0.0f, dq, n, need(L.o, 16), need(L.o, 32)) ||
+            pf_seg_gemm(m, mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->pf.x, ROWS_FEW), n, 0, D, rd))
+            return -1;
+        if (pf_rows(m, m->pf.x, D, L.ffn_norm, cfg.eps, D, n, need(L.gu, 16), need(L.gu, 32)) ||
+            pf_seg_gemm(m, mv_seg(L.gu, F, PAIR_TWO, EPI_SWIGLU, m->pf.h, ROWS_FEW), n, 0, F, rd))
+            return -1;
+        if (pf_rows(m, m->pf.h, F, nullptr, 0.0f, F, n, need(L.down, 16), need(L.down, 32)) ||
+            pf_seg_gemm(m, mv_seg(L.down, D / 2, PAIR_ADJ, EPI_RESID, m->pf.x, ROWS_FEW), n, 0, D, rd))
+            return -1;
+    }
+    if (pick) {  // final RMSNorm, output projection (src/forward.rs:495-501)
+        if (pf_rows(m, m->pf.x, D, m->out_norm, cfg.eps, D, n, need(m->out, 16), need(m->out, 32)) ||
+            pf_seg_gemm(m, mv_seg(m->out, cfg.vocab / 2, PAIR_ADJ, EPI_STORE, B.logits, ROWS_FEW), n, 0, cfg.vocab,
+                        rd))
+            return -1;
+    }
+    k_batch_pick<<<n, kPickThreads, 0, m->stream>>>(B.logits, cfg.vocab, B.toks, B.len, B.stop,
+                                                    cfg.has_eos ? (int)cfg.eos : -1, pick ? 1 : 0);
+    CU(cudaGetLastError());
+    return 0;
+}
+
+extern "C" int cxm_generate_batch(cxm_model *m, cxm_cache *const *caches, const uint32_t *const *prompts,
+                                  const uint32_t *n_prompt, uint32_t n, uint32_t max_new, uint32_t *out,
+                                  uint32_t *n_out) {
+    if (!m || !caches || !prompts || !n_prompt || !n_out || (max_new && !out) || n == 0) {
+        set_error("bad arguments");
+        return -1;
+    }
+    if (n > (uint32_t)kPrefillChunk) {
+        set_error("at most %d conversations per batch", kPrefillChunk);
+        return -1;
+    }
+    if (m->tp > 1) {
+        set_error("batched decode runs on a single-GPU model");
+        return -1;
+    }
+    int max_pos = 0;
+    for (uint32_t z = 0; z < n; z++) {
+        cxm_cache *c = caches[z];
+        if (!c || c->m != m || c->orphan || !prompts[z] || n_prompt[z] == 0) {
+            set_error("conversation %u: bad cache or empty prompt", z);
+            return -1;
+        }
+        for (uint32_t y = 0; y < z; y++)
+            if (caches[y] == c) {
+                set_error("conversations %u and %u share a cache", y, z);
+                return -1;
+            }
+        if (c->lent) {
+            set_error("conversation %u: its cache is lent as a shared prefix and cannot grow", z);
+            return -1;
+        }
+        const uint64_t need = (uint64_t)c->len + n_prompt[z] + max_new;
+        const uint64_t limit = std::min<uint64_t>((uint64_t)m->cfg.ctx, c->max_tokens);
+        if (need > limit) {
+            set_error("conversation %u: %llu tokens exceed its context of %llu", z, (unsigned long long)need,
+                      (unsigned long long)limit);
+            return -1;
+        }
+        for (uint32_t i = 0; i < n_prompt[z]; i++)
+            if (prompts[z][i] >= (uint32_t)m->cfg.vocab) {
+                set_error("token %u does not fit a vocabulary of %d", prompts[z][i], m->cfg.vocab);
+                return -1;
+            }
+        max_pos = std::max(max_pos, (int)c->max_tokens);
+    }
+    CU(cudaSetDevice(m->device));
+    for (uint32_t z = 0; z < n; z++) n_out[z] = 0;
+    std::vector<uint32_t> after(n);
+    // each prompt as its own forward call (its row class), and its first pick
+    for (uint32_t z = 0; z < n; z++) {
+        cxm_cache *c = caches[z];
+        const uint32_t len0 = c->len;
+        after[z] = len0 + n_prompt[z];
+        CU(cudaMemsetAsync(c->d_stop, 0, 4, m->stream));
+        CU(cudaMemcpyAsync(c->toks + len0, prompts[z], (size_t)n_prompt[z] * 4, cudaMemcpyHostToDevice, m->stream));
+        if (prompt_prefix(m, c, len0, n_prompt[z])) return -1;
+        if (run_steps(m, c, max_new ? STEP_GREEDY : STEP_PREFILL, n_prompt[z], 1)) return -1;
+    }
+    if (max_new) {
+        if (pf_reserve(m, kPrefillChunk) || batch_views(m, caches, (int)n)) return -1;
+        // steps 1 .. max_new-1 pick; the last one forwards the last pick
+        cxm_model::Batch &B = m->bt;
+        if (max_new > 1) {
+            if (B.graph) cudaGraphExecDestroy(B.graph);
+            B.graph = nullptr;
+            cudaGraph_t g = nullptr;
+            CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+            const int rc = batch_step(m, (int)n, max_pos, true);
+            const cudaError_t ec = cudaStreamEndCapture(m->stream, &g);
+            if (rc || ec != cudaSuccess) {
+                if (g) cudaGraphDestroy(g);
+                if (!rc) set_error("capturing the batched step failed: %s", cudaGetErrorString(ec));
+                return -1;
+            }
+            const cudaError_t ei = cudaGraphInstantiate(&B.graph, g, 0);
+            cudaGraphDestroy(g);
+            if (ei != cudaSuccess) {
+                B.graph = nullptr;
+                set_error("instantiating the batched step failed: %s", cudaGetErrorString(ei));
+                return -1;
+            }
+            for (uint32_t s = 1; s < max_new; s++) CU(cudaGraphLaunch(B.graph, m->stream));
+        }
+        if (batch_step(m, (int)n, max_pos, false)) return -1;
+    }
+    if (check_err(m)) return -1;
+    for (uint32_t z = 0; z < n; z++) {
+        cxm_cache *c = caches[z];
+        uint32_t gen = 0, fwd = n_prompt[z];
+        if (max_new) {
+            std::vector<uint32_t> t(max_new);
+            CU(cudaMemcpy(t.data(), c->toks + after[z], (size_t)max_new * 4, cudaMemcpyDeviceToHost));
+            gen = max_new;
+            fwd = n_prompt[z] + max_new;
+            if (m->cfg.has_eos)
+                for (uint32_t i = 0; i < max_new; i++)
+                    if (t[i] == m->cfg.eos) {  // the eos pick ends the generation, unforwarded
+                        gen = i;
+                        fwd = n_prompt[z] + i;
+                        break;
+                    }
+            for (uint32_t i = 0; i < gen; i++) out[(size_t)z * max_new + i] = t[i];
+        }
+        n_out[z] = gen;
+        if (set_len(c, c->len + fwd)) return -1;
+    }
     m->logits_valid = false;
     return 0;
 }

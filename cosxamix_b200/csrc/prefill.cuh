@@ -193,6 +193,15 @@ struct PfGemm {
     int ld_out;             // floats between tokens' rows of seg.out (not for cache rows: pos_stride)
     const float *rope_cos, *rope_sin;
     int *err;
+    // rows of several conversations (batched decode): row m's position, and
+    // the base its cache rows (seg.at_pos) go to; NULL: pos0 + m, seg.out
+    const int *row_pos;
+    float *const *row_out;
+    // each row in the order of a forward call of one row (ORD_FUSED: the
+    // fused per-row kernel's terms, src/kernels/scalar.rs:132-217) instead
+    // of the buffered path's; the same values for the formats without a
+    // minimum
+    int fused;
 };
 
 constexpr int kPfThreads = 256;  // warps 0-3: epilogue (TMEM lanes); warps 4-7: producers
@@ -510,6 +519,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         // ── epilogue: thread = token m (TMEM lane); the buffered path's dot
         // chain, sub-block by sub-block in row order ──
         const float *xe = G.xe + (size_t)(m < G.tokens ? m : 0) * G.nsub;
+        const float *xs = G.xs + (size_t)(m < G.tokens ? m : 0) * G.nsub;
+        const bool fused = G.fused && mins;
         for (int b = 0; b < nblk; b++) {
             const int st = b & 1;
             // warp-uniform: the TMEM loads below are collective over the warp
@@ -523,6 +534,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 tmem_ld16(col, s0);
                 if (N == 32) tmem_ld16(col + 16, s1);
                 tmem_ld_wait();
+                if (fused) {
+                    // xe·((d·sc)·Σ − (dmin·m)·xs), the offset's product being −des
+                    const float x = xs[b * nsb + j];
+                    const float *dj = des_all + b * nsb + j;
+#pragma unroll
+                    for (int n = 0; n < 16; n++)
+                        acc[n] = fa(acc[n], fm(e, fs(fm(esc[j * N + n], (float)(int)s0[n]), fm(-dj[(size_t)n * G.nsub], x))));
+                    if (N == 32) {
+#pragma unroll
+                        for (int n = 0; n < 16; n++)
+                            acc[16 + n] = fa(acc[16 + n], fm(e, fs(fm(esc[j * N + 16 + n], (float)(int)s1[n]),
+                                                                   fm(-dj[(size_t)(16 + n) * G.nsub], x))));
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int n = 0; n < 16; n++) acc[n] = fa(acc[n], fm(fm(esc[j * N + n], e), (float)(int)s0[n]));
                 if (N == 32) {
@@ -539,7 +565,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     __syncthreads();
     if (warp < 4 && !abort_s && m < G.tokens) {
         // the offset chain, after the whole row (src/ops.rs:395-401)
-        if (mins) {
+        if (mins && !G.fused) {
             const float *xe = G.xe + (size_t)m * G.nsub, *xs = G.xs + (size_t)m * G.nsub;
 #pragma unroll
             for (int n = 0; n < 32; n++) {
@@ -552,14 +578,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         }
         // the segment's epilogue, one output unit (two tiled rows) at a time
         const MvSeg &g = G.seg;
-        const int pos = G.pos0 + m;
+        const int pos = G.row_pos ? G.row_pos[m] : G.pos0 + m;
+        float *cache_base = G.row_out ? G.row_out[m] : g.out;
         for (int n = 0; n < N; n += 2) {
             const int u = (r0 + n) >> 1;
             if (u >= g.units) break;
             int ra, rb;
             unit_rows(g, u, ra, rb);
             const float y0 = acc[n], y1 = acc[n + 1];
-            float *out = g.at_pos ? g.out + (size_t)pos * g.pos_stride : g.out + (size_t)m * G.ld_out;
+            float *out = g.at_pos ? cache_base + (size_t)pos * g.pos_stride : g.out + (size_t)m * G.ld_out;
             switch (g.epi) {
             case EPI_STORE:
                 out[ra] = g.bias ? fa(y0, g.bias[ra]) : y0;

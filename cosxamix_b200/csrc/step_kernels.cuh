@@ -76,9 +76,29 @@ struct AttnParams {
     // several consecutive tokens (grid z): token z at position pos + z reads
     // q + z·qs, writes out + z·os and its scores at scores + z·H·score_stride
     int pos0, qs, os;
+    // a cache that borrows a shared prefix: its positions below plen are read
+    // from the prefix's K/V (kp, vp: the prefix's layer base)
+    const float *kp, *vp;
+    int plen;
+    // a batch of conversations (grid z = conversation; kz non-NULL): each
+    // with its own layer bases, token position and prefix
+    const float *const *kz, *const *vz, *const *kpz, *const *vpz;
+    const int *posz, *plenz;
 };
-__device__ __forceinline__ int attn_len(const AttnParams &p) {
-    return (p.d_len ? *p.d_len : p.pos0) + 1 + (int)blockIdx.z;
+// the grid-z slice's cache view: K/V bases, prefix, positions attended
+struct AttnView {
+    const float *k, *v, *kp, *vp;
+    int plen, n;
+};
+__device__ __forceinline__ AttnView attn_view(const AttnParams &p) {
+    const int z = (int)blockIdx.z;
+    if (p.kz) return AttnView{p.kz[z], p.vz[z], p.kpz[z], p.vpz[z], p.plenz[z], p.posz[z] + 1};
+    return AttnView{p.k, p.v, p.kp, p.vp, p.plen, (p.d_len ? *p.d_len : p.pos0) + 1 + z};
+}
+// the K (or V) row of position `pos`, `off` floats in (the head's slice)
+__device__ __forceinline__ const float *kv_row(const float *own, const float *pre, int plen, int pos, size_t kvd,
+                                               size_t off) {
+    return (pos < plen ? pre : own) + (size_t)pos * kvd + off;
 }
 
 constexpr int kScoreThreads = 128;   // positions per score CTA
@@ -93,7 +113,8 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
     griddep_launch_dependents();
     griddep_wait();
     const int h = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, z = blockIdx.z;
-    const int n = attn_len(p);
+    const AttnView w = attn_view(p);
+    const int n = w.n;
     if (n > p.max_pos || n <= 0) {
         if (tid == 0 && h == 0 && split == 0) atomicOr(p.err, ERR_POSITION);
         return;
@@ -107,7 +128,7 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
     for (int i = tid; i < c4; i += kScoreThreads) cp_async16(qs + 4 * i, p.q + (size_t)z * p.qs + (size_t)h * hd + 4 * i);
     for (int i = tid; i < cnt * c4; i += kScoreThreads) {
         const int r = i / c4, c = i - r * c4;
-        cp_async16(ks + r * kKRow + 4 * c, p.k + (size_t)(p0 + r) * kvd + (size_t)g * hd + 4 * c);
+        cp_async16(ks + r * kKRow + 4 * c, kv_row(w.k, w.kp, w.plen, p0 + r, kvd, (size_t)g * hd + 4 * c));
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -135,7 +156,8 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
     griddep_launch_dependents();
     griddep_wait();
     const int h = blockIdx.x, dslice = blockIdx.y, tid = threadIdx.x, z = blockIdx.z;
-    const int n = attn_len(p);
+    const AttnView w = attn_view(p);
+    const int n = w.n;
     if (n > p.max_pos || n <= 0) return;  // k_attn_scores reported it
     const int hd = p.hd, G = p.H / p.KV, g = h / G, kvd = p.KV * hd;
     const int d0 = dslice * kOutDims;
@@ -143,7 +165,7 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
     float *pr = so;
     float *vs = so + ((p.max_pos + 3) & ~3);
     const float *sc = p.scores + ((size_t)z * p.H + h) * p.score_stride;
-    const float *vb = p.v + (size_t)g * hd + d0;
+    const size_t voff = (size_t)g * hd + d0;
     const int nchunks = (n + kVChunk - 1) / kVChunk;
     auto stage = [&](int c) {
         if (c >= nchunks) return;
@@ -151,7 +173,7 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
         float *dst = vs + (c % kVRing) * kVChunk * kOutDims;
         for (int i = tid; i < cnt * (kOutDims / 4); i += kOutThreads) {
             const int r = i / (kOutDims / 4), q = i - r * (kOutDims / 4);
-            cp_async16(dst + r * kOutDims + 4 * q, vb + (size_t)(base + r) * kvd + 4 * q);
+            cp_async16(dst + r * kOutDims + 4 * q, kv_row(w.v, w.vp, w.plen, base + r, kvd, voff + 4 * q));
         }
     };
     // the scores and the first V chunks all in flight at once; the softmax

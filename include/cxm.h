@@ -101,6 +101,16 @@ int      cxm_cache_clear(cxm_cache *c);                              /* Cache::l
 /* Cache::prefijo (:115-127): dst becomes a copy of the first n tokens of src
  * (device-to-device; dst must belong to the same model). */
 int      cxm_cache_copy_prefix(const cxm_cache *src, uint32_t n, cxm_cache *dst);
+/* The shared-prefix form of the session reuse in src/engine_own.rs:198-245
+ * (which borrows a cached session's prefix by Cache::prefijo, a copy): dst
+ * reads the first n (<= src len) positions from src's K/V, held once, and
+ * continues with its own from position n. The lender counts its borrowers:
+ * while lent it cannot be truncated or cleared below the lent positions, and
+ * freeing it is deferred until its last borrower is freed or lets go (by
+ * cxm_cache_clear, cxm_cache_copy_prefix or another share). A borrower lends
+ * at most the positions it borrows (they come from its lender). Results are
+ * those of a dst holding a copy. */
+int      cxm_cache_share_prefix(cxm_cache *src, uint32_t n, cxm_cache *dst);
 /* Copy layer `layer`'s K (is_v = 0) or V (is_v = 1) rows [0, len) to host:
  * len * n_head_kv * head_dim floats. Test/inspection access. */
 int      cxm_cache_read(const cxm_cache *c, uint32_t layer, int is_v, float *host_out);
@@ -134,6 +144,18 @@ int cxm_sample(cxm_model *m, cxm_sampler *s, uint32_t *token_out);
  * return at once, and neither pick nor forward another token. */
 int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, uint32_t n_prompt, uint32_t max_new,
                  cxm_sampler *s, uint32_t *out, uint32_t *n_out);
+
+/* Greedy Modelo::generar for n conversations at once (n <= 512), each on its
+ * own cache (which may borrow a shared prefix): every prompt is forwarded as
+ * its own forward call; then each step takes every conversation's next token
+ * through the tensor-core GEMMs together (one read of the weights for all),
+ * each row in the order of a forward call of one row, so every conversation
+ * gets the tokens cxm_generate gives it alone. out: [n][max_new] tokens,
+ * n_out[z] of them valid (a conversation stops at the model's eos). Every
+ * cache needs room for len + prompt + max_new positions; a cache lent as a
+ * prefix cannot take part. Single-GPU models. */
+int cxm_generate_batch(cxm_model *m, cxm_cache *const *caches, const uint32_t *const *prompts,
+                       const uint32_t *n_prompt, uint32_t n, uint32_t max_new, uint32_t *out, uint32_t *n_out);
 
 const char *cxm_last_error(void);
 
