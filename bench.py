@@ -219,9 +219,10 @@ def run_shared_prefix(args, rank: int, world: int, local: int) -> None:
     sharing a 1024-token seeded system prefix, each with its own 64-token
     suffix and 128 greedy tokens, sharded over the ranks (replicated weights,
     no collective). Each rank prefills the prefix once (untimed setup), then
-    serves its conversations through the public API (copy the prefix,
-    cxm_generate). value = all ranks' generated tokens / the slowest rank's
-    time."""
+    serves its conversations through the public API: each borrows the prefix
+    (cxm_cache_share_prefix) and all of them decode together
+    (cxm_generate_batch). value = all ranks' generated tokens / the slowest
+    rank's time."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -240,12 +241,12 @@ def run_shared_prefix(args, rank: int, world: int, local: int) -> None:
     work = serving.Workload(conversations=args.conversations, seed=args.seed)
     mine = serving.shard(work.conversations, rank, world)
     # warm-up: one conversation's worth, outside the timed region
-    serving.serve(m, serving.Workload(conversations=1, prefix=16, suffix=4, new_tokens=4, seed=args.seed + 7), [0],
-                  cx.Muestreador.voraz)
+    serving.serve_batched(m, serving.Workload(conversations=2, prefix=16, suffix=4, new_tokens=4, seed=args.seed + 7),
+                          [0, 1])
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    _, secs, n = serving.serve(m, work, mine, cx.Muestreador.voraz)
+    _, secs, n = serving.serve_batched(m, work, mine)
     torch.cuda.synchronize()
     secs, n = serving.reduce_job(secs, n)
     if world > 1:
@@ -259,13 +260,14 @@ def run_shared_prefix(args, rank: int, world: int, local: int) -> None:
         "n_gpus": world, "steps": work.conversations, "warmup": 1, "ms_per_step": round(secs * 1000 / max(1, len(mine)), 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8-dot/f32",
         "data": "synthetic",
-        "config": {"workload": f"configs[3]: {work.conversations} conversations, shared {work.prefix}-token seeded "
-                               f"prefix (prefilled once per GPU), {work.suffix}-token suffix each, "
-                               f"{work.new_tokens} greedy tokens each",
+        "config": {"workload": f"{work.conversations} conversations, shared {work.prefix}-token seeded "
+                               f"prefix (prefilled once per GPU, held once), {work.suffix}-token suffix each, "
+                               f"{work.new_tokens} greedy tokens each, decoded together",
                    "parallelism": f"dp{world} (conversations sharded, replicated weights, no collective)"},
         "generated_tokens": n,
         "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * work.suffix,
-                "d2h_bytes_per_step": 4 * work.new_tokens, "api": "cxm_cache_copy_prefix + cxm_generate per conversation"},
+                "d2h_bytes_per_step": 4 * work.new_tokens,
+                "api": "cxm_cache_share_prefix per conversation + cxm_generate_batch"},
     }
     print(json.dumps(line), flush=True)
 

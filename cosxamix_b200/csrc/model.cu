@@ -92,18 +92,21 @@ struct cxm_model {
         float *e16 = nullptr, *s16 = nullptr, *e32 = nullptr, *s32 = nullptr;
         size_t score_floats = 0;
     } pf;
-    struct Batch {  // batched decode: per-conversation views, allocated at the first such call
-        int cap = 0;
+    struct Batch {  // batched forward: rows of many conversations, allocated at the first such call
+        int cap = 0, pcap = 0;  // rows; picked rows
+        int rows = 0, picks = 0;
         void *mem = nullptr;  // one allocation for all of it
-        float *logits = nullptr;           // [cap][vocab]
-        uint32_t *tok = nullptr;           // [cap] the step's tokens
+        float *logits = nullptr;           // [pcap][vocab]
+        float *xo = nullptr;               // [pcap][dim] the picked rows' hidden states, packed
+        uint32_t *tok = nullptr;           // [cap] the rows' tokens
         int *pos = nullptr;                // [cap] their positions
-        float **kz = nullptr, **vz = nullptr;            // [n_layer][cap] layer bases of each cache
-        const float **kpz = nullptr, **vpz = nullptr;    // [n_layer][cap] of each borrowed prefix
+        float **kz = nullptr, **vz = nullptr;            // [n_layer][rows] layer bases of each row's cache
+        const float **kpz = nullptr, **vpz = nullptr;    // [n_layer][rows] of its borrowed prefix
         int *plenz = nullptr;              // [cap]
-        uint32_t **toks = nullptr;         // [cap] each cache's token array
-        int **len = nullptr, **stop = nullptr;  // [cap] each cache's position and eos flag
-        cudaGraphExec_t graph = nullptr;   // one batched step over the current views
+        int *sel = nullptr, *ppos = nullptr;  // [pcap] the picked rows, their positions
+        uint32_t **toks = nullptr;         // [pcap] each picked row's cache: token array,
+        int **len = nullptr, **stop = nullptr;  // position and eos flag
+        cudaGraphExec_t graph = nullptr;   // one decode step over the current views
         int graph_n = 0;
     } bt;
 
@@ -1755,13 +1758,14 @@ extern "C" int cxm_generate(cxm_model *m, cxm_cache *c, const uint32_t *prompt, 
     return 0;
 }
 
-// ── batched decode of several conversations ──
-// One greedy step for B conversations at once: their rows go through the
-// tensor-core GEMMs together (one read of every weight for all of them),
-// each row in the order of a forward call of one row (src/ops.rs:1081-1092
-// with m = 1: the fused per-row kernel), each conversation attending over its
-// own cache and its borrowed prefix. A conversation is, row for row, what
-// src/forward.rs:544-557 computes for it alone.
+// ── batched forward of several conversations ──
+// Rows of many conversations go through the tensor-core GEMMs together (one
+// read of every weight for all of them): the prompts of a batch (every row of
+// a prompt in its forward call's order, src/ops.rs:1056-1093 with m = the
+// prompt's length), then each greedy step with one row per conversation (the
+// order of a forward call of one row). Each row attends over its own
+// conversation's cache and borrowed prefix. Every conversation gets, row for
+// row, what src/forward.rs:544-557 computes for it alone.
 
 // the step's token and position of each conversation
 __global__ void k_batch_gather(uint32_t *const *toks, int *const *len, int n, uint32_t *tok, int *pos) {
@@ -1773,18 +1777,28 @@ __global__ void k_batch_gather(uint32_t *const *toks, int *const *len, int n, ui
     }
 }
 
-// argmax of each conversation's logits (the first maximum, NaNs skipped;
-// src/sampler.rs:129-137), the token appended and the position advanced —
-// unless the conversation met its eos in an earlier step
+// rows sel[0..c) of x, packed (the rows whose logits are needed)
+__global__ void k_batch_rows(const float *x, const int *sel, int D, float *out) {
+    const int c = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < D; i += gridDim.x * blockDim.x)
+        out[(size_t)c * D + i] = x[(size_t)sel[c] * D + i];
+}
+
+// For each picked row c (conversation toks[c], len[c], stop[c], at position
+// pos[c]): the argmax of its logits (the first maximum, NaNs skipped;
+// src/sampler.rs:129-137) appended after the position, the eos flag, and the
+// position advanced — unless the conversation met its eos earlier. Without
+// `pick` only the position advances (the forward of the last pick).
 constexpr int kPickThreads = 512;
-__global__ void __launch_bounds__(kPickThreads) k_batch_pick(const float *logits, int V, uint32_t *const *toks,
-                                                             int *const *len, int *const *stop, int eos, int pick) {
+__global__ void __launch_bounds__(kPickThreads) k_batch_pick(const float *logits, int V, const int *pos,
+                                                             uint32_t *const *toks, int *const *len,
+                                                             int *const *stop, int eos, int pick) {
     __shared__ unsigned long long best_s[kPickThreads / 32];
-    const int z = blockIdx.x, tid = threadIdx.x;
-    if (*(volatile int *)stop[z]) return;  // the whole block
+    const int c = blockIdx.x, tid = threadIdx.x;
+    if (*(volatile int *)stop[c]) return;  // the whole block
     unsigned long long best = 0ull;
     if (pick) {
-        const float *l = logits + (size_t)z * V;
+        const float *l = logits + (size_t)c * V;
         for (int i = tid; i < V; i += kPickThreads) {
             const float v = l[i];
             const unsigned long long k = v == v ? argmax_key(v, (uint32_t)i) : 0ull;
@@ -1799,89 +1813,132 @@ __global__ void __launch_bounds__(kPickThreads) k_batch_pick(const float *logits
         __syncthreads();
     }
     if (tid == 0) {
-        const int p = *len[z];
+        const int p = pos[c];
         if (pick) {
             for (int w = 0; w < kPickThreads / 32; w++) best = best_s[w] > best ? best_s[w] : best;
             const uint32_t t = argmax_index(best);
-            toks[z][p + 1] = t;
-            if (eos >= 0 && t == (uint32_t)eos) *stop[z] = 1;
+            toks[c][p + 1] = t;
+            if (eos >= 0 && t == (uint32_t)eos) *stop[c] = 1;
         }
-        *len[z] = p + 1;
+        *len[c] = p + 1;
     }
 }
 
-// the per-conversation views of n caches, on the device
-static int batch_views(cxm_model *m, cxm_cache *const *cs, int n) {
+// the positions of the picked rows
+__global__ void k_batch_sel_pos(const int *pos, const int *sel, int n, int *out) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c < n) out[c] = pos[sel[c]];
+}
+
+// A set of rows on the device: row r is conversation cache[r]'s token at
+// position pos[r] (decode steps gather both from the caches themselves).
+struct BatchRow {
+    cxm_cache *c;
+    int pos;
+    uint32_t tok;
+};
+
+static int batch_reserve(cxm_model *m, int rows, int picks) {
     cxm_model::Batch &B = m->bt;
+    if (B.cap >= rows && B.pcap >= picks) return 0;
+    if (B.graph) cudaGraphExecDestroy(B.graph);
+    B.graph = nullptr;
+    B.graph_n = 0;
+    cudaFree(B.mem);
+    const int cap = std::max({rows, B.cap, 8}), pcap = std::max({picks, B.pcap, 8});
+    B = cxm_model::Batch{};
     const int L = m->cfg.n_layer;
-    const size_t kvd = kv_dim(m);
-    if (B.cap < n) {
-        if (B.graph) cudaGraphExecDestroy(B.graph);
-        B.graph = nullptr;
-        cudaFree(B.mem);
-        B = cxm_model::Batch{};
-        const int cap = std::max(n, 8);
-        const size_t bytes = (size_t)cap * m->cfg.vocab * 4 + (size_t)cap * 4 * 3 + (size_t)L * cap * 8 * 4 +
-                             (size_t)cap * 8 * 3 + 256;
-        CU(cudaMalloc(&B.mem, bytes));
-        char *p = (char *)B.mem;
-        auto take = [&](size_t nb) {
-            char *r = p;
-            p += (nb + 15) & ~(size_t)15;
-            return (void *)r;
-        };
-        B.logits = (float *)take((size_t)cap * m->cfg.vocab * 4);
-        B.tok = (uint32_t *)take((size_t)cap * 4);
-        B.pos = (int *)take((size_t)cap * 4);
-        B.plenz = (int *)take((size_t)cap * 4);
-        B.kz = (float **)take((size_t)L * cap * 8);
-        B.vz = (float **)take((size_t)L * cap * 8);
-        B.kpz = (const float **)take((size_t)L * cap * 8);
-        B.vpz = (const float **)take((size_t)L * cap * 8);
-        B.toks = (uint32_t **)take((size_t)cap * 8);
-        B.len = (int **)take((size_t)cap * 8);
-        B.stop = (int **)take((size_t)cap * 8);
-        B.cap = cap;
-    }
-    std::vector<const void *> kz((size_t)L * n), vz((size_t)L * n), kpz((size_t)L * n), vpz((size_t)L * n);
-    std::vector<const void *> tk(n), ln(n), st(n);
-    std::vector<int> plen(n);
-    for (int z = 0; z < n; z++) {
-        const cxm_cache *c = cs[z];
-        for (int l = 0; l < L; l++) {
-            kz[(size_t)l * n + z] = c->k + (size_t)l * c->max_tokens * kvd;
-            vz[(size_t)l * n + z] = c->v + (size_t)l * c->max_tokens * kvd;
-            kpz[(size_t)l * n + z] = prefix_k(c, l, kvd);
-            vpz[(size_t)l * n + z] = prefix_v(c, l, kvd);
-        }
-        tk[z] = c->toks;
-        ln[z] = c->d_len;
-        st[z] = c->d_stop;
-        plen[z] = c->prefix ? (int)c->plen : 0;
-    }
-    // the layer arrays are [n_layer][n]: row stride n for this call
-    CU(cudaMemcpy(B.kz, kz.data(), kz.size() * 8, cudaMemcpyHostToDevice));
-    CU(cudaMemcpy(B.vz, vz.data(), vz.size() * 8, cudaMemcpyHostToDevice));
-    CU(cudaMemcpy(B.kpz, kpz.data(), kpz.size() * 8, cudaMemcpyHostToDevice));
-    CU(cudaMemcpy(B.vpz, vpz.data(), vpz.size() * 8, cudaMemcpyHostToDevice));
-    CU(cudaMemcpy(B.toks, tk.data(), (size_t)n * 8, cudaMemcpyHostToDevice));
-    CU(cudaMemcpy(B.len, ln.data(), (size_t)n * 8, cudaMemcpyHostToDevice));
-    CU(cudaMemcpy(B.stop, st.data(), (size_t)n * 8, cudaMemcpyHostToDevice));
-    CU(cudaMemcpy(B.plenz, plen.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+    const size_t bytes = (size_t)pcap * m->cfg.vocab * 4 + (size_t)pcap * m->cfg.dim * 4 + (size_t)cap * 4 * 3 +
+                         (size_t)L * cap * 8 * 4 + (size_t)pcap * (4 * 2 + 8 * 3) + 2048;
+    CU(cudaMalloc(&B.mem, bytes));
+    char *p = (char *)B.mem;
+    auto take = [&](size_t nb) {
+        char *r = p;
+        p += (nb + 15) & ~(size_t)15;
+        return (void *)r;
+    };
+    B.logits = (float *)take((size_t)pcap * m->cfg.vocab * 4);
+    B.xo = (float *)take((size_t)pcap * m->cfg.dim * 4);
+    B.tok = (uint32_t *)take((size_t)cap * 4);
+    B.pos = (int *)take((size_t)cap * 4);
+    B.plenz = (int *)take((size_t)cap * 4);
+    B.kz = (float **)take((size_t)L * cap * 8);
+    B.vz = (float **)take((size_t)L * cap * 8);
+    B.kpz = (const float **)take((size_t)L * cap * 8);
+    B.vpz = (const float **)take((size_t)L * cap * 8);
+    B.sel = (int *)take((size_t)pcap * 4);
+    B.ppos = (int *)take((size_t)pcap * 4);
+    B.toks = (uint32_t **)take((size_t)pcap * 8);
+    B.len = (int **)take((size_t)pcap * 8);
+    B.stop = (int **)take((size_t)pcap * 8);
+    B.cap = cap;
+    B.pcap = pcap;
     return 0;
 }
 
-// One step of n conversations (views from batch_views): each forwards the
-// token at its position; with `pick`, the output projection and the greedy
-// pick follow (else only the position advances: the last token's forward).
-static int batch_step(cxm_model *m, int n, int max_pos, bool pick) {
+// upload the views of `rows` (cache layer bases, prefixes, positions,
+// tokens) and of the picked rows `picks` (indices into rows)
+static int batch_upload(cxm_model *m, const std::vector<BatchRow> &rows, const std::vector<int> &picks) {
+    cxm_model::Batch &B = m->bt;
+    if (batch_reserve(m, (int)rows.size(), (int)picks.size())) return -1;
+    const int L = m->cfg.n_layer, R = (int)rows.size();
+    const size_t kvd = kv_dim(m);
+    std::vector<const void *> kz((size_t)L * R), vz((size_t)L * R), kpz((size_t)L * R), vpz((size_t)L * R);
+    std::vector<int> plen(R), pos(R);
+    std::vector<uint32_t> tok(R);
+    for (int r = 0; r < R; r++) {
+        const cxm_cache *c = rows[r].c;
+        for (int l = 0; l < L; l++) {
+            kz[(size_t)l * R + r] = c->k + (size_t)l * c->max_tokens * kvd;
+            vz[(size_t)l * R + r] = c->v + (size_t)l * c->max_tokens * kvd;
+            kpz[(size_t)l * R + r] = prefix_k(c, l, kvd);
+            vpz[(size_t)l * R + r] = prefix_v(c, l, kvd);
+        }
+        plen[r] = c->prefix ? (int)c->plen : 0;
+        pos[r] = rows[r].pos;
+        tok[r] = rows[r].tok;
+    }
+    const int P = (int)picks.size();
+    std::vector<const void *> tk(P), ln(P), st(P);
+    for (int i = 0; i < P; i++) {
+        const cxm_cache *c = rows[picks[i]].c;
+        tk[i] = c->toks;
+        ln[i] = c->d_len;
+        st[i] = c->d_stop;
+    }
+    // layer arrays are [n_layer][R] for this upload
+    CU(cudaMemcpyAsync(B.kz, kz.data(), kz.size() * 8, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(B.vz, vz.data(), vz.size() * 8, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(B.kpz, kpz.data(), kpz.size() * 8, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(B.vpz, vpz.data(), vpz.size() * 8, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(B.plenz, plen.data(), (size_t)R * 4, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(B.pos, pos.data(), (size_t)R * 4, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(B.tok, tok.data(), (size_t)R * 4, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(B.sel, picks.data(), (size_t)P * 4, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(B.toks, tk.data(), (size_t)P * 8, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(B.len, ln.data(), (size_t)P * 8, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaMemcpyAsync(B.stop, st.data(), (size_t)P * 8, cudaMemcpyHostToDevice, m->stream));
+    CU(cudaStreamSynchronize(m->stream));  // the host vectors go out of scope
+    B.rows = R;
+    B.picks = P;
+    return 0;
+}
+
+// The forward of the uploaded rows, in the order of row class `cls`; with
+// `gather` the rows' tokens and positions are first read from the picked
+// conversations' caches (a decode step: row r is pick r). Then, for the
+// picked rows, the output projection and the greedy pick (`pick`), or the
+// position advance alone.
+static int batch_forward(cxm_model *m, int max_pos, int cls, bool gather, bool pick) {
     const cxm_config &cfg = m->cfg;
     const cxm_model::Batch &B = m->bt;
-    const int D = cfg.dim, hd = cfg.head_dim, H = m->h_loc, F = cfg.ffn, dq = H * hd;
+    const int n = B.rows, D = cfg.dim, hd = cfg.head_dim, H = m->h_loc, F = cfg.ffn, dq = H * hd;
     const size_t kvd = kv_dim(m);
     auto need = [](const QMat &M, int sz) { return sub_of(M.type) == sz ? 1 : 0; };
-    k_batch_gather<<<(n + 127) / 128, 128, 0, m->stream>>>(B.toks, B.len, n, B.tok, B.pos);
-    CU(cudaGetLastError());
+    if (gather) {
+        k_batch_gather<<<(n + 127) / 128, 128, 0, m->stream>>>(B.toks, B.len, n, B.tok, B.pos);
+        CU(cudaGetLastError());
+    }
     {
         const dim3 g((D + 255) / 256, n);
         k_pf_embed<<<g, 256, 0, m->stream>>>(m->embd, m->embd_f32, B.tok, D, m->pf.x);
@@ -1895,15 +1952,15 @@ static int batch_step(cxm_model *m, int n, int max_pos, bool pick) {
         if (pf_rows(m, m->pf.x, D, L.attn_norm, cfg.eps, D, n, need(L.q, 16) | need(L.k, 16) | need(L.v, 16),
                     need(L.q, 32) | need(L.k, 32) | need(L.v, 32)))
             return -1;
-        MvSeg sq = mv_seg(L.q, dq / 2, PAIR_ROPE, EPI_ROPE, m->pf.q, ROWS_FEW);
+        MvSeg sq = mv_seg(L.q, dq / 2, PAIR_ROPE, EPI_ROPE, m->pf.q, cls);
         sq.half = hd / 2;
         sq.bias = L.bq;
-        MvSeg sk = mv_seg(L.k, (int)kvd / 2, PAIR_ROPE, EPI_ROPE, nullptr, ROWS_FEW);
+        MvSeg sk = mv_seg(L.k, (int)kvd / 2, PAIR_ROPE, EPI_ROPE, nullptr, cls);
         sk.half = hd / 2;
         sk.bias = L.bk;
         sk.at_pos = 1;
         sk.pos_stride = (int)kvd;
-        MvSeg sv = mv_seg(L.v, (int)kvd / 2, PAIR_ADJ, EPI_STORE, nullptr, ROWS_FEW);
+        MvSeg sv = mv_seg(L.v, (int)kvd / 2, PAIR_ADJ, EPI_STORE, nullptr, cls);
         sv.bias = L.bv;
         sv.at_pos = 1;
         sv.pos_stride = (int)kvd;
@@ -1923,7 +1980,7 @@ static int batch_step(cxm_model *m, int n, int max_pos, bool pick) {
         a.score_stride = (max_pos + 3) & ~3;
         a.scale = 1.0f / sqrtf((float)hd);  // src/ops.rs:1287
         a.err = m->err;
-        // conversations per launch: their score rows fit the scratch
+        // rows per launch: their score rows fit the scratch
         const int tz = (int)std::max<size_t>(
             1, std::min<size_t>(n, m->pf.score_floats / ((size_t)H * a.score_stride)));
         for (int z0 = 0; z0 < n; z0 += tz) {
@@ -1939,22 +1996,39 @@ static int batch_step(cxm_model *m, int n, int max_pos, bool pick) {
             if (launch_attention_on(m->stream, az, std::min(tz, n - z0))) return -1;
         }
         if (pf_rows(m, m->pf.att, dq, nullptr, 0.0f, dq, n, need(L.o, 16), need(L.o, 32)) ||
-            pf_seg_gemm(m, mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->pf.x, ROWS_FEW), n, 0, D, rd))
+            pf_seg_gemm(m, mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->pf.x, cls), n, 0, D, rd))
             return -1;
         if (pf_rows(m, m->pf.x, D, L.ffn_norm, cfg.eps, D, n, need(L.gu, 16), need(L.gu, 32)) ||
-            pf_seg_gemm(m, mv_seg(L.gu, F, PAIR_TWO, EPI_SWIGLU, m->pf.h, ROWS_FEW), n, 0, F, rd))
+            pf_seg_gemm(m, mv_seg(L.gu, F, PAIR_TWO, EPI_SWIGLU, m->pf.h, cls), n, 0, F, rd))
             return -1;
         if (pf_rows(m, m->pf.h, F, nullptr, 0.0f, F, n, need(L.down, 16), need(L.down, 32)) ||
-            pf_seg_gemm(m, mv_seg(L.down, D / 2, PAIR_ADJ, EPI_RESID, m->pf.x, ROWS_FEW), n, 0, D, rd))
+            pf_seg_gemm(m, mv_seg(L.down, D / 2, PAIR_ADJ, EPI_RESID, m->pf.x, cls), n, 0, D, rd))
             return -1;
     }
-    if (pick) {  // final RMSNorm, output projection (src/forward.rs:495-501)
-        if (pf_rows(m, m->pf.x, D, m->out_norm, cfg.eps, D, n, need(m->out, 16), need(m->out, 32)) ||
-            pf_seg_gemm(m, mv_seg(m->out, cfg.vocab / 2, PAIR_ADJ, EPI_STORE, B.logits, ROWS_FEW), n, 0, cfg.vocab,
+    const int P = B.picks;
+    if (P == 0) return 0;
+    // the picked rows' positions: row sel[c]'s
+    const float *xp = m->pf.x;
+    if (pick) {  // final RMSNorm and output projection of the picked rows, one row each (src/forward.rs:495-501)
+        if (!gather) {  // prompt rows: the picked (last) rows packed first
+            const dim3 g((D + 255) / 256, P);
+            k_batch_rows<<<g, 256, 0, m->stream>>>(m->pf.x, B.sel, D, B.xo);
+            CU(cudaGetLastError());
+            xp = B.xo;
+        }
+        if (pf_rows(m, xp, D, m->out_norm, cfg.eps, D, P, need(m->out, 16), need(m->out, 32)) ||
+            pf_seg_gemm(m, mv_seg(m->out, cfg.vocab / 2, PAIR_ADJ, EPI_STORE, B.logits, ROWS_FEW), P, 0, cfg.vocab,
                         rd))
             return -1;
     }
-    k_batch_pick<<<n, kPickThreads, 0, m->stream>>>(B.logits, cfg.vocab, B.toks, B.len, B.stop,
+    // the picked rows' positions (a decode step: the gathered ones, row c = pick c)
+    const int *ppos = B.pos;
+    if (!gather) {
+        k_batch_sel_pos<<<(P + 127) / 128, 128, 0, m->stream>>>(B.pos, B.sel, P, B.ppos);
+        CU(cudaGetLastError());
+        ppos = B.ppos;
+    }
+    k_batch_pick<<<P, kPickThreads, 0, m->stream>>>(B.logits, cfg.vocab, ppos, B.toks, B.len, B.stop,
                                                     cfg.has_eos ? (int)cfg.eos : -1, pick ? 1 : 0);
     CU(cudaGetLastError());
     return 0;
@@ -2006,28 +2080,57 @@ extern "C" int cxm_generate_batch(cxm_model *m, cxm_cache *const *caches, const 
         max_pos = std::max(max_pos, (int)c->max_tokens);
     }
     CU(cudaSetDevice(m->device));
+    if (pf_reserve(m, kPrefillChunk)) return -1;
     for (uint32_t z = 0; z < n; z++) n_out[z] = 0;
-    std::vector<uint32_t> after(n);
-    // each prompt as its own forward call (its row class), and its first pick
+    std::vector<uint32_t> len0(n), after(n);
     for (uint32_t z = 0; z < n; z++) {
         cxm_cache *c = caches[z];
-        const uint32_t len0 = c->len;
-        after[z] = len0 + n_prompt[z];
+        len0[z] = c->len;
+        after[z] = c->len + n_prompt[z];
         CU(cudaMemsetAsync(c->d_stop, 0, 4, m->stream));
-        CU(cudaMemcpyAsync(c->toks + len0, prompts[z], (size_t)n_prompt[z] * 4, cudaMemcpyHostToDevice, m->stream));
-        if (prompt_prefix(m, c, len0, n_prompt[z])) return -1;
-        if (run_steps(m, c, max_new ? STEP_GREEDY : STEP_PREFILL, n_prompt[z], 1)) return -1;
+        CU(cudaMemcpyAsync(c->toks + len0[z], prompts[z], (size_t)n_prompt[z] * 4, cudaMemcpyHostToDevice,
+                           m->stream));
+    }
+    // The prompts: each prompt's rows in its forward call's order (its row
+    // class), all conversations of a class together, kPrefillChunk rows per
+    // pass in position order; each prompt's last row picks its first token
+    // (or, with max_new = 0, only advances the position).
+    for (int cls = 0; cls < 3; cls++) {
+        std::vector<BatchRow> rows;
+        std::vector<int> picks;
+        auto flush = [&]() -> int {
+            if (rows.empty()) return 0;
+            if (batch_upload(m, rows, picks) || batch_forward(m, max_pos, cls, false, max_new > 0)) return -1;
+            rows.clear();
+            picks.clear();
+            return 0;
+        };
+        for (uint32_t z = 0; z < n; z++) {
+            if (row_class(n_prompt[z]) != cls) continue;
+            for (uint32_t i = 0; i < n_prompt[z]; i++) {
+                if (rows.size() == (size_t)kPrefillChunk && flush()) return -1;
+                rows.push_back(BatchRow{caches[z], (int)(len0[z] + i), prompts[z][i]});
+                if (i + 1 == n_prompt[z]) picks.push_back((int)rows.size() - 1);
+            }
+        }
+        if (flush()) return -1;
     }
     if (max_new) {
-        if (pf_reserve(m, kPrefillChunk) || batch_views(m, caches, (int)n)) return -1;
         // steps 1 .. max_new-1 pick; the last one forwards the last pick
+        std::vector<BatchRow> rows(n);
+        std::vector<int> picks(n);
+        for (uint32_t z = 0; z < n; z++) {
+            rows[z] = BatchRow{caches[z], 0, 0};
+            picks[z] = (int)z;
+        }
+        if (batch_upload(m, rows, picks)) return -1;
         cxm_model::Batch &B = m->bt;
         if (max_new > 1) {
             if (B.graph) cudaGraphExecDestroy(B.graph);
             B.graph = nullptr;
             cudaGraph_t g = nullptr;
             CU(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-            const int rc = batch_step(m, (int)n, max_pos, true);
+            const int rc = batch_forward(m, max_pos, ROWS_FEW, true, true);
             const cudaError_t ec = cudaStreamEndCapture(m->stream, &g);
             if (rc || ec != cudaSuccess) {
                 if (g) cudaGraphDestroy(g);
@@ -2043,7 +2146,7 @@ extern "C" int cxm_generate_batch(cxm_model *m, cxm_cache *const *caches, const 
             }
             for (uint32_t s = 1; s < max_new; s++) CU(cudaGraphLaunch(B.graph, m->stream));
         }
-        if (batch_step(m, (int)n, max_pos, false)) return -1;
+        if (batch_forward(m, max_pos, ROWS_FEW, true, false)) return -1;
     }
     if (check_err(m)) return -1;
     for (uint32_t z = 0; z < n; z++) {
@@ -2064,7 +2167,7 @@ extern "C" int cxm_generate_batch(cxm_model *m, cxm_cache *const *caches, const 
             for (uint32_t i = 0; i < gen; i++) out[(size_t)z * max_new + i] = t[i];
         }
         n_out[z] = gen;
-        if (set_len(c, c->len + fwd)) return -1;
+        if (set_len(c, len0[z] + fwd)) return -1;
     }
     m->logits_valid = false;
     return 0;

@@ -243,64 +243,108 @@ __host__ __device__ inline PfSmem pf_smem(int type, int K) {
     return s;
 }
 
-// GGUF bytes of super-block b of tiled row r into dst (all threads of the
-// producer group cooperate: `i0`, `step`)
-__device__ __forceinline__ void pf_gather(const QMat &M, int r0, int N, int b, uint8_t *raw, int i0, int step) {
+// GGUF bytes of super-block b of the tile's N rows, in two halves so the
+// loads of the next block are in flight while this one is unpacked: pf_fetch
+// loads a producer thread's share (items i0, i0 + step, i0 + 2·step: at most
+// three 16-byte plane-A chunks and three plane-S/D bytes, which covers every
+// format at 128 producers) into registers; pf_put stores them in the row's
+// GGUF block in `raw`.
+struct PfFetch {
+    uint4 a[3];
+    uint32_t sd[3];
+};
+__device__ __forceinline__ void pf_fetch(const QMat &M, int r0, int N, int b, int i0, int step, PfFetch &f) {
     const int T = M.type, pa = plane_a_bytes(T), ps = plane_s_bytes(T), pd = plane_d_bytes(T), ach = pa / 16;
+    const int t = b / M.lpr, bl = b % M.lpr, nb = tile_nb(M.nblk, M.lpr, t), L = M.rpt * nb;
+    const int rows = M.ngroup * M.rpt;  // rows allocated (padded groups); rows past them are skipped
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const int i = i0 + k * step;
+        f.a[k] = make_uint4(0, 0, 0, 0);
+        if (i < N * ach) {
+            const int n = i / ach, c = i - n * ach, r = r0 + n, g = r / M.rpt, sl = r % M.rpt, lane = M.rpt * bl + sl;
+            if (r < rows)
+                f.a[k] = __ldg((const uint4 *)(M.base + tile_offset(M, g, t) + ((size_t)c * L + lane) * 16));
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const int i = i0 + k * step;
+        f.sd[k] = 0;
+        if (i < N * (ps + pd)) {
+            const int n = i / (ps + pd), kk = i - n * (ps + pd), r = r0 + n, g = r / M.rpt, sl = r % M.rpt,
+                      lane = M.rpt * bl + sl;
+            if (r < rows) {
+                const uint8_t *tile = M.base + tile_offset(M, g, t);
+                f.sd[k] = kk < ps ? tile[ach * L * 16 + lane * ps + kk] : tile[ach * L * 16 + L * ps + lane * pd + (kk - ps)];
+            }
+        }
+    }
+}
+__device__ __forceinline__ void pf_put(int T, int N, const PfFetch &f, uint8_t *raw, int i0, int step) {
+    const int pa = plane_a_bytes(T), ps = plane_s_bytes(T), pd = plane_d_bytes(T), ach = pa / 16;
     int lo_a = 0, lo_s = pa, lo_d = pa + ps;
     if (T == 10) {
         lo_s = 0;
         lo_a = 16;
         lo_d = 80;
     }
-    const int t = b / M.lpr, bl = b % M.lpr, nb = tile_nb(M.nblk, M.lpr, t), L = M.rpt * nb;
-    const int rows = M.ngroup * M.rpt;  // rows allocated (padded groups); rows past them are skipped
-    for (int i = i0; i < N * ach; i += step) {
-        const int n = i / ach, c = i - n * ach, r = r0 + n, g = r / M.rpt, sl = r % M.rpt, lane = M.rpt * bl + sl;
-        if (r >= rows) continue;
-        const uint8_t *tile = M.base + tile_offset(M, g, t);
-        *(uint4 *)(raw + n * 224 + lo_a + 16 * c) = __ldg((const uint4 *)(tile + ((size_t)c * L + lane) * 16));
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const int i = i0 + k * step;
+        if (i < N * ach) {
+            const int n = i / ach, c = i - n * ach;
+            *(uint4 *)(raw + n * 224 + lo_a + 16 * c) = f.a[k];
+        }
     }
-    for (int i = i0; i < N * (ps + pd); i += step) {
-        const int n = i / (ps + pd), k = i - n * (ps + pd), r = r0 + n, g = r / M.rpt, sl = r % M.rpt,
-                  lane = M.rpt * bl + sl;
-        if (r >= rows) continue;
-        const uint8_t *tile = M.base + tile_offset(M, g, t);
-        uint8_t v;
-        if (k < ps) v = tile[ach * L * 16 + lane * ps + k];
-        else v = tile[ach * L * 16 + L * ps + lane * pd + (k - ps)];
-        raw[n * 224 + (k < ps ? lo_s + k : lo_d + (k - ps))] = v;
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const int i = i0 + k * step;
+        if (i < N * (ps + pd)) {
+            const int n = i / (ps + pd), kk = i - n * (ps + pd);
+            raw[n * 224 + (kk < ps ? lo_s + kk : lo_d + (kk - ps))] = (uint8_t)f.sd[k];
+        }
     }
 }
+static_assert(32 * 11 <= 3 * 128 && 16 * 12 <= 3 * 128 && 16 * 20 <= 3 * 128,
+              "a producer's share of a block is at most three chunks and three bytes");
 
 __device__ __forceinline__ float rd_h(const uint8_t *p) { return h2f((uint32_t)p[0] | ((uint32_t)p[1] << 8)); }
 
 // Quarter q (values 64q..64q+63) of one super-block as desempaquetar_i8
-// unpacks it (src/quant.rs:238-468): the int8 values, the scale of each of
-// its sub-blocks (esc[j], j = sub-block inside the block) and the offset
-// (des[j], formats with a minimum).
-__device__ void pf_unpack_quarter(int T, const uint8_t *blk, int q, int8_t (&v)[64], float *esc, float *des) {
+// unpacks it (src/quant.rs:238-468): the int8 values four to a word, w[i]
+// holding values 4i..4i+3 (the byte order of the operand tile), and the
+// scale (e[k]) and offset (o[k], formats with a minimum) of each of the
+// quarter's sub-blocks k. Whole words at a time, as the decode kernel reads
+// the same bytes: a nibble or 2-bit field of four values per mask, the -32
+// (Q6_K) and -4 (Q3_K) bias per byte.
+__device__ __forceinline__ uint32_t ld_w(const uint8_t *p) { return *(const uint32_t *)p; }
+
+__device__ __forceinline__ void pf_unpack_quarter(int T, const uint8_t *blk, int q, uint32_t (&w)[16], float (&e)[4],
+                                                  float (&o)[4]) {
     switch (T) {
     case 12: case 13: {  // Q4_K / Q5_K: sub-blocks 2q (low nibbles) and 2q+1 (high)
         const float d = rd_h(blk), dmin = rd_h(blk + 2);
-        const uint32_t w0 = blk[4] | blk[5] << 8 | blk[6] << 16 | (uint32_t)blk[7] << 24;
-        const uint32_t w1 = blk[8] | blk[9] << 8 | blk[10] << 16 | (uint32_t)blk[11] << 24;
-        const uint32_t w2 = blk[12] | blk[13] << 8 | blk[14] << 16 | (uint32_t)blk[15] << 24;
+        const uint32_t w0 = ld_w(blk + 4), w1 = ld_w(blk + 8), w2 = ld_w(blk + 12);
+#pragma unroll
         for (int t = 0; t < 2; t++) {
             int sc, mn;
             scale_min_k4(2 * q + t, w0, w1, w2, sc, mn);
-            esc[2 * q + t] = fm(d, (float)sc);
-            des[2 * q + t] = -fm(dmin, (float)mn);
+            e[t] = fm(d, (float)sc);
+            o[t] = -fm(dmin, (float)mn);
         }
-        const uint8_t *qs = blk + (T == 12 ? 16 : 48) + 32 * q, *qh = blk + 16;
-        for (int l = 0; l < 32; l++) {
-            int lo = qs[l] & 0xF, hi = qs[l] >> 4;
+        const uint8_t *qs = blk + (T == 12 ? 16 : 48) + 32 * q;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t x = ld_w(qs + 4 * i);
+            uint32_t lo = x & 0x0F0F0F0Fu, hi = (x >> 4) & 0x0F0F0F0Fu;
             if (T == 13) {
-                lo += (qh[l] >> (2 * q)) & 1 ? 16 : 0;
-                hi += (qh[l] >> (2 * q + 1)) & 1 ? 16 : 0;
+                const uint32_t h = ld_w(blk + 16 + 4 * i);
+                lo |= ((h >> (2 * q)) & 0x01010101u) << 4;
+                hi |= ((h >> (2 * q + 1)) & 0x01010101u) << 4;
             }
-            v[l] = (int8_t)lo;
-            v[32 + l] = (int8_t)hi;
+            w[i] = lo;
+            w[8 + i] = hi;
         }
         break;
     }
@@ -308,16 +352,14 @@ __device__ void pf_unpack_quarter(int T, const uint8_t *blk, int q, int8_t (&v)[
         const int h = q >> 1, odd = q & 1;
         const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h, *sc = blk + 192 + 8 * h;
         const float d = rd_h(blk + 208);
-        for (int p = 0; p < 4; p++) esc[8 * h + 4 * odd + p] = fm(d, (float)(int8_t)sc[4 * odd + p]);
-        for (int l = 0; l < 32; l++) {
-            const int qb = qh[l];
-            if (!odd) {
-                v[l] = (int8_t)(((ql[l] & 0xF) | ((qb & 3) << 4)) - 32);
-                v[32 + l] = (int8_t)(((ql[32 + l] & 0xF) | (((qb >> 2) & 3) << 4)) - 32);
-            } else {
-                v[l] = (int8_t)(((ql[l] >> 4) | (((qb >> 4) & 3) << 4)) - 32);
-                v[32 + l] = (int8_t)(((ql[32 + l] >> 4) | (((qb >> 6) & 3) << 4)) - 32);
-            }
+#pragma unroll
+        for (int p = 0; p < 4; p++) e[p] = fm(d, (float)(int8_t)sc[4 * odd + p]);
+        const int sl = odd ? 4 : 0, sh0 = odd ? 4 : 0, sh1 = odd ? 6 : 2;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t a = ld_w(ql + 4 * i), c = ld_w(ql + 32 + 4 * i), hb = ld_w(qh + 4 * i);
+            w[i] = __vsub4(((a >> sl) & 0x0F0F0F0Fu) | (((hb >> sh0) & 0x03030303u) << 4), 0x20202020u);
+            w[8 + i] = __vsub4(((c >> sl) & 0x0F0F0F0Fu) | (((hb >> sh1) & 0x03030303u) << 4), 0x20202020u);
         }
         break;
     }
@@ -325,21 +367,22 @@ __device__ void pf_unpack_quarter(int T, const uint8_t *blk, int q, int8_t (&v)[
         const int m2 = q >> 1;
         const uint8_t *hm = blk, *qs = blk + 32 + 32 * m2;
         const float d = rd_h(blk + 108);
-        const uint32_t a0 = blk[96] | blk[97] << 8 | blk[98] << 16 | (uint32_t)blk[99] << 24;
-        const uint32_t a1 = blk[100] | blk[101] << 8 | blk[102] << 16 | (uint32_t)blk[103] << 24;
-        const uint32_t tt = blk[104] | blk[105] << 8 | blk[106] << 16 | (uint32_t)blk[107] << 24;
+        const uint32_t a0 = ld_w(blk + 96), a1 = ld_w(blk + 100), tt = ld_w(blk + 104);
+#pragma unroll
         for (int ii = 0; ii < 2; ii++) {
             const int it = 2 * (q & 1) + ii, g = 4 * m2 + it;
+#pragma unroll
             for (int t = 0; t < 2; t++) {
                 const int is = 2 * g + t, wi = is >> 2;
                 const uint32_t aa = (wi & 1) ? a1 : a0;
                 const uint32_t wq = ((aa >> ((wi >> 1) * 4)) & 0x0F0F0F0Fu) | (((tt >> (2 * wi)) & 0x03030303u) << 4);
                 const int s6 = (int)((wq >> (8 * (is & 3))) & 0xFF);
-                esc[is] = fm(d, fs((float)s6, 32.0f));
+                e[2 * ii + t] = fm(d, fs((float)s6, 32.0f));
             }
-            for (int l = 0; l < 32; l++) {
-                const int hi = (hm[l] >> g) & 1 ? 0 : 4;
-                v[32 * ii + l] = (int8_t)(((qs[l] >> (2 * it)) & 3) - hi);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint32_t x = ld_w(qs + 4 * i), hb = ld_w(hm + 4 * i);
+                w[8 * ii + i] = __vsub4(((x >> (2 * it)) & 0x03030303u) | (((hb >> g) & 0x01010101u) << 2), 0x04040404u);
             }
         }
         break;
@@ -348,14 +391,17 @@ __device__ void pf_unpack_quarter(int T, const uint8_t *blk, int q, int8_t (&v)[
         const int m2 = q >> 1;
         const uint8_t *sc = blk, *qs = blk + 16 + 32 * m2;
         const float d = rd_h(blk + 80), dmin = rd_h(blk + 82);
+#pragma unroll
         for (int ii = 0; ii < 2; ii++) {
             const int it = 2 * (q & 1) + ii, g = 4 * m2 + it;
+#pragma unroll
             for (int t = 0; t < 2; t++) {
                 const int is = 2 * g + t;
-                esc[is] = fm(d, (float)(sc[is] & 0xF));
-                des[is] = -fm(dmin, (float)(sc[is] >> 4));
+                e[2 * ii + t] = fm(d, (float)(sc[is] & 0xF));
+                o[2 * ii + t] = -fm(dmin, (float)(sc[is] >> 4));
             }
-            for (int l = 0; l < 32; l++) v[32 * ii + l] = (int8_t)((qs[l] >> (2 * it)) & 3);
+#pragma unroll
+            for (int i = 0; i < 8; i++) w[8 * ii + i] = (ld_w(qs + 4 * i) >> (2 * it)) & 0x03030303u;
         }
         break;
     }
@@ -436,6 +482,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
 #pragma unroll
     for (int i = 0; i < 32; i++) acc[i] = 0.0f;
     const int m = mt * kPfM + tid;  // the epilogue thread's token
+    const int groups = min(16, (G.tokens - mt * kPfM + 7) / 8);  // 8-token row groups of this tile
 
     if (warp >= 4) {
         // ── producers: unpack the N rows' super-blocks; thread 128 also
@@ -443,47 +490,58 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         const int ptid = tid - 128;
         int last_issued = -1;
         bool ok = true;  // the MMA thread's waits so far (the others' stay true)
+        // the activation tile of block bb into its stage: the tile's token rows
+        // in groups of 8 (256 bytes per K-step); a tile of few tokens (a decode
+        // batch) copies only its groups, and the MMA rows past them hold stale
+        // bytes whose sums no epilogue thread stores
+        auto copy_a = [&](int bb) {
+            const int sa = bb & 1;
+            const uint8_t *src = (const uint8_t *)(G.a + ((size_t)mt * (M.K / 32) + 8 * bb) * 4096);
+            if (groups == 16) {
+                mbar_arrive_expect_tx(&full_a[sa], 32768);
+                bulk_g2s(sm + L.a[sa], src, 32768, &full_a[sa]);
+            } else {
+                mbar_arrive_expect_tx(&full_a[sa], (uint32_t)(8 * groups * 256));
+                for (int k8 = 0; k8 < 8; k8++)
+                    bulk_g2s(sm + L.a[sa] + k8 * 4096, src + k8 * 4096, (uint32_t)(groups * 256), &full_a[sa]);
+            }
+        };
+        if (ptid == 0) copy_a(0);
+        PfFetch fw;
+        pf_fetch(M, r0, N, 0, ptid, 128, fw);
         for (int b = 0; b < nblk; b++) {
             const int st = b & 1;
             bool w = true;
             if (b >= kPfStages) w = pf_wait(&tmem_empty[st], ((b - kPfStages) >> 1) & 1, &abort_s, G.err);
             if (!producers_all(ok && w && !abort_s)) break;
-            if (ptid == 0) {
-                mbar_arrive_expect_tx(&full_a[st], 32768);
-                bulk_g2s(sm + L.a[st], G.a + ((size_t)mt * (M.K / 32) + 8 * b) * 4096, 32768, &full_a[st]);
-            }
-            pf_gather(M, r0, N, b, sm + L.raw, ptid, 128);
+            // this block's bytes (loaded during the last block), then the next block's loads
+            pf_put(T, N, fw, sm + L.raw, ptid, 128);
+            if (b + 1 < nblk) pf_fetch(M, r0, N, b + 1, ptid, 128, fw);
             asm volatile("bar.sync 2, 128;" ::: "memory");
             float *esc = (float *)(sm + L.esc[st]);  // [sub-block in block][row]
             for (int i = ptid; i < N * 4; i += 128) {
                 const int n = i >> 2, q = i & 3;
-                int8_t v[64];
-                float e[16], d[16];
-                pf_unpack_quarter(T, sm + L.raw + n * 224, q, v, e, d);
-                const int j0 = q * (64 / sub);
-                for (int j = j0; j < j0 + 64 / sub; j++) {
-                    esc[j * N + n] = e[j];
+                uint32_t w[16];
+                float e[4], o[4];
+                pf_unpack_quarter(T, sm + L.raw + n * 224, q, w, e, o);
+                const int per = 64 / sub, j0 = q * per;  // the quarter's sub-blocks
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    if (k >= per) break;
+                    esc[(j0 + k) * N + n] = e[k];
                     if (mins) {
-                        des_all[(size_t)n * G.nsub + b * nsb + j] = d[j];
-                        if (d[j] != 0.0f) anyd[n] = 1;
+                        des_all[(size_t)n * G.nsub + b * nsb + j0 + k] = o[k];
+                        if (o[k] != 0.0f) anyd[n] = 1;
                     }
                 }
                 // 16 values at a time into the operand tile of their sub-block
+#pragma unroll
                 for (int c = 0; c < 4; c++) {
                     const int k = 64 * q + 16 * c, j = k / sub, kk = k % sub;
-                    uint4 w;
-                    w.x = (uint8_t)v[16 * c] | (uint8_t)v[16 * c + 1] << 8 | (uint8_t)v[16 * c + 2] << 16 |
-                          (uint32_t)(uint8_t)v[16 * c + 3] << 24;
-                    w.y = (uint8_t)v[16 * c + 4] | (uint8_t)v[16 * c + 5] << 8 | (uint8_t)v[16 * c + 6] << 16 |
-                          (uint32_t)(uint8_t)v[16 * c + 7] << 24;
-                    w.z = (uint8_t)v[16 * c + 8] | (uint8_t)v[16 * c + 9] << 8 | (uint8_t)v[16 * c + 10] << 16 |
-                          (uint32_t)(uint8_t)v[16 * c + 11] << 24;
-                    w.w = (uint8_t)v[16 * c + 12] | (uint8_t)v[16 * c + 13] << 8 | (uint8_t)v[16 * c + 14] << 16 |
-                          (uint32_t)(uint8_t)v[16 * c + 15] << 24;
                     uint32_t off;
                     if (sub == 32) off = (uint32_t)(j * N * 32 + (n >> 3) * 256 + (kk >> 4) * 128 + (n & 7) * 16);
                     else off = (uint32_t)(N * 16 + j * N * 16 + (n >> 3) * 128 + (n & 7) * 16);
-                    *(uint4 *)(sm + L.b[st] + off) = w;
+                    *(uint4 *)(sm + L.b[st] + off) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
                 }
             }
             fence_async_smem();
@@ -511,6 +569,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 }
                 umma_commit(&mma_done[st]);
                 last_issued = b;
+                // the next block's activation tile, into the stage block b-1's
+                // MMAs read: once they are done
+                if (b + 1 < nblk) {
+                    if (b >= 1) ok = pf_wait(&mma_done[(b - 1) & 1], ((b - 1) >> 1) & 1, &abort_s, G.err);
+                    if (ok) copy_a(b + 1);
+                }
             }
         }
         // every MMA has completed before the accumulators are released
@@ -564,25 +628,36 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     }
     __syncthreads();
     if (warp < 4 && !abort_s && m < G.tokens) {
-        // the offset chain, after the whole row (src/ops.rs:395-401)
+        // the offset chain, after the whole row (src/ops.rs:395-401): each
+        // row with a nonzero offset adds its terms in sub-block order; the
+        // rows' chains advance side by side (sub-block outer), so the token's
+        // xe/xs are read once per sub-block and the 32 chains overlap
         if (mins && !G.fused) {
             const float *xe = G.xe + (size_t)m * G.nsub, *xs = G.xs + (size_t)m * G.nsub;
+            uint32_t live = 0;  // rows with a nonzero offset
 #pragma unroll
-            for (int n = 0; n < 32; n++) {
-                if (n >= N || !anyd[n]) continue;
-                const float *d = des_all + (size_t)n * G.nsub;
-                float a = acc[n];
-                for (int s = 0; s < G.nsub; s++) a = fa(a, fm(fm(d[s], xe[s]), xs[s]));
-                acc[n] = a;
+            for (int n = 0; n < 32; n++)
+                if (n < N && anyd[n]) live |= 1u << n;
+            if (live) {
+                for (int s = 0; s < G.nsub; s++) {
+                    const float e = __ldg(xe + s), x = __ldg(xs + s);
+#pragma unroll
+                    for (int n = 0; n < 32; n++) {
+                        if (n >= N) break;
+                        const float t = fm(fm(des_all[(size_t)n * G.nsub + s], e), x);
+                        acc[n] = (live >> n) & 1u ? fa(acc[n], t) : acc[n];
+                    }
+                }
             }
         }
         // the segment's epilogue, one output unit (two tiled rows) at a time
         const MvSeg &g = G.seg;
         const int pos = G.row_pos ? G.row_pos[m] : G.pos0 + m;
         float *cache_base = G.row_out ? G.row_out[m] : g.out;
-        for (int n = 0; n < N; n += 2) {
+#pragma unroll
+        for (int n = 0; n < 32; n += 2) {  // constant indices: acc stays in registers
             const int u = (r0 + n) >> 1;
-            if (u >= g.units) break;
+            if (n >= N || u >= g.units) break;
             int ra, rb;
             unit_rows(g, u, ra, rb);
             const float y0 = acc[n], y1 = acc[n + 1];

@@ -2,11 +2,15 @@
 
 Independent conversations, replicated weights, no collective on the data
 path: rank r of N serves conversations r, r + N, r + 2N, ... Each rank
-prefills the shared system prefix once into a cache and starts every
-conversation from a device-to-device copy of it (Cache::prefijo,
-src/forward.rs:115-127), which is what MotorPropio's reuse/borrow of a
-prefix does for a new chat (src/engine_own.rs:198-245): the prefix's KV is
-computed once per GPU instead of once per conversation.
+prefills the shared system prefix once into a cache. `serve_batched` (the
+served path) has every conversation borrow that prefix (held once,
+cxm_cache_share_prefix) and decodes all of the rank's conversations
+together, one read of the weights per step for all of them
+(cxm_generate_batch); `serve` starts each conversation from a
+device-to-device copy of the prefix (Cache::prefijo, src/forward.rs:115-127,
+which is what MotorPropio's reuse/borrow of a prefix does for a new chat,
+src/engine_own.rs:198-245) and decodes the conversations one after another.
+Both give every conversation the tokens the reference gives it alone.
 
 The only cross-rank operations are host bookkeeping: the slowest rank's time
 (max) and the total generated tokens (sum), over any torch.distributed
@@ -74,6 +78,31 @@ def serve(model, work: Workload, convs: list[int], sampler_factory, clock=time.p
         toks = model.generar(work.suffix_tokens(conv, vocab), work.new_tokens, sampler_factory(), c)
         out[conv] = toks
         generated += len(toks)
+    return out, clock() - t0, generated
+
+
+def serve_batched(model, work: Workload, convs: list[int], max_batch: int = 512, clock=time.perf_counter):
+    """This rank's conversations decoded together (up to max_batch at once),
+    each borrowing the prefix prefilled once; returns ({conv: tokens},
+    seconds, tokens)."""
+    vocab = model.cfg.vocab
+    total = work.prefix + work.suffix + work.new_tokens
+    base = model.cache(total)
+    model.forward(work.prefix_tokens(vocab), base)
+    out = {}
+    generated = 0
+    t0 = clock()
+    for i in range(0, len(convs), max_batch):
+        group = convs[i:i + max_batch]
+        caches = []
+        for _ in group:
+            c = model.cache(total)
+            c.compartir_prefijo(base, work.prefix)
+            caches.append(c)
+        toks = model.generar_lote([work.suffix_tokens(conv, vocab) for conv in group], work.new_tokens, caches)
+        for conv, t in zip(group, toks):
+            out[conv] = t
+            generated += len(t)
     return out, clock() - t0, generated
 
 

@@ -42,9 +42,17 @@ class _Cfg:
 class _Cache:
     def __init__(self):
         self.toks = []
+        self.lender = None
 
     def copiar_prefijo(self, src, n):
         self.toks = list(src.toks[:n])
+
+    def compartir_prefijo(self, src, n):  # borrowed, not copied: read through the lender
+        self.lender = (src, n)
+        self.toks = []
+
+    def all_toks(self):
+        return (list(self.lender[0].toks[: self.lender[1]]) if self.lender else []) + self.toks
 
 
 class _Model:
@@ -66,10 +74,14 @@ class _Model:
         c.toks += list(prompt)
         out = []
         for _ in range(n):
-            t = (sum(c.toks) * 31 + len(c.toks)) % self.cfg.vocab
+            t = (sum(c.all_toks()) * 31 + len(c.all_toks())) % self.cfg.vocab
             out.append(t)
             c.toks.append(t)
         return out
+
+    def generar_lote(self, prompts, n, caches):
+        self.batches = getattr(self, "batches", 0) + 1
+        return [self.generar(p, n, None, c) for p, c in zip(prompts, caches)]
 
 
 def _free_port():
@@ -114,3 +126,12 @@ def test_two_gloo_ranks_serve_the_same_conversations_as_one():
         assert job_n == n1         # every rank's tokens
         assert prefills == 1       # the shared prefix once per rank
     assert merged == single
+
+
+def test_batched_serving_borrows_the_prefix_and_matches_one_at_a_time():
+    work = serving.Workload(conversations=10, prefix=16, suffix=4, new_tokens=6)
+    single, _, n1 = serving.serve(_Model(), work, list(range(10)), lambda: None)
+    model = _Model()
+    batched, _, n2 = serving.serve_batched(model, work, list(range(10)), max_batch=4)
+    assert batched == single and n2 == n1
+    assert model.prefills == 1 and model.batches == 3  # groups of 4, 4 and 2
