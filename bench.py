@@ -387,6 +387,7 @@ def run_tp(args, rank: int, world: int, local: int) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
+    nccl = nccl_exchange_baseline(m, world, local) if world > 1 else None
     peak, peak_kind = peaks()
     wbytes = m.weight_bytes  # this rank's share
     if world > 1:
@@ -399,16 +400,63 @@ def run_tp(args, rank: int, world: int, local: int) -> None:
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8-dot/f32",
         "data": "synthetic",
-        "config": {"workload": f"configs[4]: {args.config} shape Q4_K_M, {args.prompt}-token seeded prompt, "
-                               f"greedy decode bs=1", "parallelism": f"tp{world} (o_proj/ffn_down partials and "
-                               f"the argmax exchanged over peer memory inside the decode kernel)",
+        "config": {"workload": f"{args.config} shape Q4_K_M, {args.prompt}-token seeded prompt, "
+                               f"greedy decode bs=1", "parallelism": f"tp{world} (attention replicated, FFN rows "
+                               f"split; the hidden vector, the residual and the argmax gathered from the peers' "
+                               f"memory inside the decode kernel)",
                    "l2": "inputs larger than L2: the weight shares stream from HBM every step"},
         "weight_stream": {"bytes_per_token_rank0": wbytes,
                           "gbs_per_gpu_rank0": round(wbytes / (ms / args.steps / 1000.0) / 1e9, 1),
                           "peak_gbs": peak, "peak_kind": peak_kind},
         "gpu_launches": args.steps * m.step_launches, "clocks": clk,
     }
+    if nccl:
+        line["nccl_baseline"] = nccl
     print(json.dumps(line), flush=True)
+
+
+def nccl_exchange_baseline(m, world: int, local: int, reps: int = 20) -> dict:
+    """The same exchanges as NCCL collectives: per token, per layer an
+    all-gather of the FFN hidden vector and one of the residual stream (the
+    ranks' slices), and one all-gather of the argmax keys; timed alone with
+    CUDA events over `reps` tokens' worth (max over ranks). What a step with
+    NCCL between kernel launches would spend in collectives, against the
+    in-kernel peer-memory gathers."""
+    import torch
+    import torch.distributed as dist
+    g = dist.new_group(backend="nccl")
+    dev = torch.device("cuda", local)
+    F, D, L = m.cfg.ffn, m.cfg.dim, m.cfg.n_layer
+    hs = torch.zeros(F // world, device=dev)
+    hb = torch.zeros(F, device=dev)
+    xs = torch.zeros(D // world, device=dev)
+    xb = torch.zeros(D, device=dev)
+    ks = torch.zeros(1, dtype=torch.int64, device=dev)
+    kb = torch.zeros(world, dtype=torch.int64, device=dev)
+
+    def token():
+        for _ in range(L):
+            dist.all_gather_into_tensor(hb, hs, group=g)
+            dist.all_gather_into_tensor(xb, xs, group=g)
+        dist.all_gather_into_tensor(kb, ks, group=g)
+
+    for _ in range(3):
+        token()
+    torch.cuda.synchronize()
+    dist.barrier(group=g)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        token()
+    e1.record()
+    e1.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX, group=g)
+    dist.barrier(group=g)
+    dist.destroy_process_group(g)
+    return {"collectives_per_token": 2 * L + 1, "ms_per_token": round(float(ms.item()), 4),
+            "what": "NCCL all_gather_into_tensor of the same slices (hidden vector and residual per layer, argmax "
+                    "keys), collectives only, CUDA-event timed, max over ranks"}
 
 
 def main() -> None:
