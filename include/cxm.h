@@ -199,7 +199,10 @@ int cxm_debug_attention(const float *q, const float *k, const float *v, uint32_t
  *   work overlaps (two host threads, or two streams) race on it.
  *   The first call on each device looks up the array's address and sets the
  *   kernels' shared-memory limits (with that device current); make that first
- *   call before any stream capture.
+ *   call before any stream capture. The address is kept for the life of the
+ *   process: after a cudaDeviceReset of that device (which ends the process's
+ *   context there) it is stale, so this entry point must not be called on
+ *   that device again in the same process.
  *   Work is enqueued on `stream` (a cudaStream_t; NULL = the default stream),
  *   which is synchronised before the call returns so the kernels' error word
  *   can be reported. */
