@@ -82,6 +82,7 @@ def lib() -> C.CDLL:
             "cxm_debug_matmul": (C.c_int, [C.c_int, P, C.c_uint32, C.c_uint32, P, C.c_uint32, P]),
             "cxm_debug_attention": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P]),
             "cxm_debug_expf": (C.c_int, [P, P, C.c_uint64]),
+            "cxm_debug_seq_sums": (C.c_int, [P, P, C.c_uint64]),
             "cxm_attention_noalloc": (C.c_int, [P, P, P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, P, P]),
             "cxm_bench_decode": (C.c_int, [P, P, C.c_uint32, C.POINTER(C.c_float)]),
             "cxm_bench_decode_sampled": (C.c_int, [P, P, P, C.c_uint32, C.POINTER(C.c_float)]),
@@ -403,6 +404,15 @@ def expf(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, np.float32)
     y = np.zeros_like(x)
     _check(lib().cxm_debug_expf(_ptr(x), _ptr(y), x.size))
+    return y
+
+
+def seq_sums(x: np.ndarray) -> np.ndarray:
+    """The running f32 sums of x, rounded one addition at a time as the
+    reference's loops round them, by the device sampler's summation."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.zeros_like(x)
+    _check(lib().cxm_debug_seq_sums(_ptr(x), _ptr(y), x.size))
     return y
 
 

@@ -168,6 +168,13 @@ struct MvSeg {
     const float *bias;
     float *out;
     float *out2;              // EPI_RESID: a second copy of the result (a tensor-parallel rank's exported slice)
+    // EPI_SWIGLU: the hidden vector also quantized for the next matvec
+    // (ffn_down) as its sub-blocks of qsub values complete: qcnt[s] counts the
+    // values of sub-block s written so far; the write that completes one
+    // quantizes it into qout (carve_act's layout for qK values). NULL: not done.
+    unsigned char *qout;
+    int *qcnt;
+    int qsub, qK;
 };
 
 struct MvPhase {
@@ -188,6 +195,11 @@ struct AtPhase {
     const float *kp, *vp;    // a borrowed prefix's layer K/V: positions below plen are read there
     int plen;
     float *out, *scores;
+    // the output quantized for the next matvec (o_proj): each item's 32 dims
+    // are whole sub-blocks of 16 or 32, quantized where they are formed,
+    // into the layout of a matvec activation (NULL: not done)
+    unsigned char *qout;
+    int qneed16, qneed32, qK;
     int H, KV, hd, score_stride, P;  // P: positions per score item
     int ring;                        // V chunks in the attention phase's ring
     float scale;
@@ -261,6 +273,8 @@ struct DecodeArgs {
     int write_token, commit;  // commit: toks[len+1] = argmax (write_token), len += 1
     int *d_stop;              // set: the generation met its eos and the step does nothing (NULL: never)
     int eos;                  // the token whose greedy pick sets *d_stop, or -1
+    int *qcnt;                // the hidden vector's sub-block counts (MvSeg.qcnt), nqcnt of them
+    int nqcnt;
     int ring_slots;           // tile slots per warp ring (2..kMaxSlots)
     uint32_t slot_bytes, region_bytes;
 };
@@ -626,6 +640,55 @@ __device__ void unit_epilogue(const DecodeArgs &A, const MvSeg &g, int r0, int r
     }
 }
 
+// The sub-block sb of a segment's hidden vector, complete in global memory,
+// quantized exactly as quantize_act quantizes it (src/ops.rs:178-198):
+// amax over the sub-block, 127/amax, round-half-away, the (scale, sum) pair.
+__device__ __noinline__ void hidden_quant_block(const MvSeg &g, int sb) {
+    const int sub = g.qsub;
+    const float *h = g.out + (size_t)sb * sub;
+    float x[32];
+    float am = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        x[i] = i < sub ? __ldcg(h + i) : 0.0f;
+        am = fmaxf(am, fabsf(x[i]));
+    }
+    const float inv = am > 0.0f ? __fdiv_rn(127.0f, am) : 0.0f;
+    const Act a = carve_act(g.qout, g.qK, sub == 16, sub == 32);
+    int8_t *q = (sub == 16 ? a.q16 : a.q32) + ((sb * sub) >> 8) * kXqStride + ((sb * sub) & 255);
+    int sm = 0;
+#pragma unroll
+    for (int w4 = 0; w4 < 8; w4++) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int qv = (int)roundf(__fmul_rn(x[4 * w4 + k], inv));
+            sm += qv;  // zero beyond sub
+            word |= ((uint32_t)qv & 0xFFu) << (8 * k);
+        }
+        if (4 * w4 < sub) ((uint32_t *)q)[w4] = word;
+    }
+    (sub == 16 ? a.es16 : a.es32)[sb] = make_float2(am > 0.0f ? __fdiv_rn(am, 127.0f) : 0.0f, (float)sm);
+}
+
+// After a flush's epilogues (whole warp): every lane that wrote hidden value
+// v of a segment with `qout` counts it into its sub-block, one atomic per
+// distinct sub-block of the warp; the lane whose count completes a sub-block
+// quantizes it and clears the count for the next layer.
+__device__ __forceinline__ void hidden_quant_arrive(const MvSeg &g, int v, bool wrote) {
+    const int lane = threadIdx.x & 31;
+    const int sb = wrote ? v / g.qsub : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, sb);
+    __threadfence();  // each lane's hidden value before its sub-block's count
+    __syncwarp();
+    if (!wrote || lane != __ffs(peers) - 1) return;
+    const int n = __popc(peers);
+    if (atomicAdd(&g.qcnt[sb], n) + n != g.qsub) return;
+    __threadfence();  // the other CTAs' values after their counts
+    hidden_quant_block(g, sb);
+    g.qcnt[sb] = 0;
+}
+
 // group range of this CTA in a matvec phase: contiguous and balanced
 __device__ __forceinline__ void cta_groups(int ngroup, int &qb, int &qe) {
     qb = (int)(((long long)blockIdx.x * ngroup) / gridDim.x);
@@ -894,12 +957,12 @@ __device__ void phase_xargmax(const DecodeArgs &A, unsigned ep, volatile int *ab
 // ── attention phases (src/ops.rs:1258-1325), reference order ──
 // An attention item is one head and 32 of its output dims. Its region: the
 // head's probabilities (max_pos rounded to 4 floats), then a ring of `ring`
-// V chunks, each kAttnPos positions of the item's 32 dims stored transposed
-// ([dim][position], rows of kAttnPos + 1 floats: the odd row length keeps
-// both the transposing 4-byte copies and the position-by-position reads free
-// of bank conflicts).
+// V chunks, each kAttnPos positions of the item's 32 dims ([position][dim]:
+// a position's 128 bytes arrive in eight 16-byte copies, and the 32 lanes of
+// the position-by-position sums read one position's 32 consecutive floats,
+// free of bank conflicts).
 constexpr int kAttnPos = 128, kAttnMinRing = 3, kAttnMaxRing = 8;
-constexpr int kAttnChunkFloats = 32 * (kAttnPos + 1);
+constexpr int kAttnChunkFloats = 32 * kAttnPos;
 __host__ __device__ inline size_t scores_region(int P, int G, int hd) {
     return ((size_t)P * (hd + 4) + (size_t)G * hd) * sizeof(float);
 }
@@ -1009,18 +1072,18 @@ __device__ __forceinline__ float seq_sum(const float *p, int n) {
 // The head's scores staged in shared memory; their max and exp(s - max)
 // (src/ops.rs:1206-1230) across the CTA; the sum position by position by
 // thread 0; then warp 0 adds prob_p·v_p[d] position by position, lane d for
-// dim d0 + d, over the transposed V chunks.
+// dim d0 + d, over the staged V chunks.
 
-// V chunk c of an item into its ring slot, transposed (the caller commits
-// the cp.async group)
+// V chunk c of an item into its ring slot (the caller commits the cp.async
+// group)
 __device__ __forceinline__ void attn_stage(const AtPhase &at, int n, size_t voff, float *ring, int c) {
     const int tid = threadIdx.x, kvd = at.KV * at.hd;
     if (c * kAttnPos >= n) return;
     const int base = c * kAttnPos, cnt = min(kAttnPos, n - base);
     float *dst = ring + (c % at.ring) * kAttnChunkFloats;
-    for (int i = tid; i < cnt * 32; i += kDW * 32) {
-        const int p = i >> 5, d = i & 31;
-        cp_async4(dst + d * (kAttnPos + 1) + p, kv_row(at.v, at.vp, at.plen, base + p, kvd, voff + d));
+    for (int i = tid; i < cnt * 8; i += kDW * 32) {
+        const int p = i >> 3, q = i & 7;
+        cp_async16(dst + p * 32 + 4 * q, kv_row(at.v, at.vp, at.plen, base + p, kvd, voff + 4 * q));
     }
 }
 
@@ -1043,7 +1106,8 @@ __device__ __forceinline__ void attn_prefetch(const AtPhase &at, int n, int max_
 }
 
 // acc + Σ (e[r]·inv)·v[r] over the cnt positions of a chunk, one position
-// after another (lane d: its dim's row of the transposed chunk)
+// after another (lane d: vt points at dim d of the chunk's first position,
+// positions 32 floats apart)
 __device__ __forceinline__ void pv_chunk(const float *vt, const float *pp, int cnt, float inv, float &acc) {
     int r = 0;
     for (; r + 16 <= cnt; r += 16) {
@@ -1052,7 +1116,7 @@ __device__ __forceinline__ void pv_chunk(const float *vt, const float *pp, int c
 #pragma unroll
         for (int k = 0; k < 4; k++) q[k] = ((const float4 *)(pp + r))[k];
 #pragma unroll
-        for (int k = 0; k < 16; k++) w[k] = vt[r + k];
+        for (int k = 0; k < 16; k++) w[k] = vt[(r + k) * 32];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             acc = fa(acc, fm(fm(q[k].x, inv), w[4 * k]));
@@ -1061,7 +1125,36 @@ __device__ __forceinline__ void pv_chunk(const float *vt, const float *pp, int c
             acc = fa(acc, fm(fm(q[k].w, inv), w[4 * k + 3]));
         }
     }
-    for (; r < cnt; r++) acc = fa(acc, fm(fm(pp[r], inv), vt[r]));
+    for (; r < cnt; r++) acc = fa(acc, fm(fm(pp[r], inv), vt[r * 32]));
+}
+
+// The 32 outputs of an attention item (one per lane of warp 0, dims d0..d0+31
+// of the concatenated heads) quantized as quantize_act quantizes them
+// (src/ops.rs:178-198: amax per sub-block, 127/amax, round half away, the
+// scale amax/127 and the integer sum), written into the global activation
+// buffer in carve_act's layout: the next phase copies it instead of
+// quantizing the whole vector in every CTA.
+__device__ __forceinline__ void attn_quant_out(const AtPhase &at, int d, float v) {
+    const int lane = threadIdx.x & 31;
+    const Act a = carve_act(at.qout, at.qK, at.qneed16, at.qneed32);
+    const float av = fabsf(v);
+    for (int sz = 16; sz <= 32; sz += 16) {
+        if ((sz == 16 && !at.qneed16) || (sz == 32 && !at.qneed32)) continue;
+        float am = av;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1)
+            if (o < sz) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        const float inv = am > 0.0f ? __fdiv_rn(127.0f, am) : 0.0f;
+        const int qv = (int)roundf(__fmul_rn(v, inv));
+        int sm = qv;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1)
+            if (o < sz) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+        int8_t *q = sz == 16 ? a.q16 : a.q32;
+        q[(d >> 8) * kXqStride + (d & 255)] = (int8_t)qv;
+        if ((lane & (sz - 1)) == 0)
+            (sz == 16 ? a.es16 : a.es32)[d / sz] = make_float2(am > 0.0f ? __fdiv_rn(am, 127.0f) : 0.0f, (float)sm);
+    }
 }
 
 // The head's scores come in from L2 with each thread's running max; every
@@ -1130,7 +1223,7 @@ __device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos
         if (staged) {
             if (warp == 0)
                 for (int c = 0; c < nchunks; c++)
-                    pv_chunk(ring + (c % R) * kAttnChunkFloats + lane * (kAttnPos + 1), pr + c * kAttnPos,
+                    pv_chunk(ring + (c % R) * kAttnChunkFloats + lane, pr + c * kAttnPos,
                              min(kAttnPos, n - c * kAttnPos), inv, acc);
         } else {
             for (int c = 0; c < nchunks; c++) {
@@ -1139,12 +1232,15 @@ __device__ __forceinline__ void phase_attn(const AtPhase &at, int n, int max_pos
                 cp_async_wait_n(R - 1);
                 dsync();
                 if (warp == 0)
-                    pv_chunk(ring + (c % R) * kAttnChunkFloats + lane * (kAttnPos + 1), pr + c * kAttnPos,
+                    pv_chunk(ring + (c % R) * kAttnChunkFloats + lane, pr + c * kAttnPos,
                              min(kAttnPos, n - c * kAttnPos), inv, acc);
                 dsync();
             }
         }
-        if (warp == 0) at.out[(size_t)h * hd + d0 + lane] = acc;
+        if (warp == 0) {
+            at.out[(size_t)h * hd + d0 + lane] = acc;
+            if (at.qout) attn_quant_out(at, h * hd + d0 + lane, acc);
+        }
         cp_async_wait<0>();
         dsync();
     }
@@ -1321,6 +1417,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         // read before the first grid barrier, so before CTA 0's commit updates it
         xbase_s = A.epoch ? *(volatile unsigned *)A.epoch : 0u;
     }
+    if (blockIdx.x == 0 && A.qcnt)  // the hidden-vector sub-block counts start at zero every step
+        for (int i = tid; i < A.nqcnt; i += kDecodeThreads) A.qcnt[i] = 0;
     if (tid < kDescWords) ((uint4 *)&phbuf[0])[tid] = __ldg((const uint4 *)&A.prog[0] + tid);
     for (int i = tid; i < A.nfeed * 4; i += kDecodeThreads) ((uint4 *)ftab)[i] = __ldg((const uint4 *)A.feed + i);
     __syncthreads();
@@ -1364,7 +1462,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
         if (pi + 1 < A.nphase && tid < kDescWords) nextd = __ldg((const uint4 *)&A.prog[pi + 1] + tid);
         // a normed matvec's weights depend on nothing: loaded before the barrier
         NormW nw;
-        if (ph.kind == PH_MATVEC && ph.mv.prologue != PRO_QUANT) load_norm_w(ph.mv, nw);
+        if (ph.kind == PH_MATVEC && (ph.mv.prologue == PRO_NORM || ph.mv.prologue == PRO_EMBED)) load_norm_w(ph.mv, nw);
         const int n = pos + 1;
         // what an attention phase reads from before this step lands in shared
         // memory while the CTA waits at the barrier
@@ -1378,6 +1476,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
             const MvPhase &P = ph.mv;
             const Act act = carve_act(region, P.K, P.need16, P.need32);
             if (P.prologue == PRO_EMBED && blockIdx.x == 0 && tid == 0 && A.argmax_key) *A.argmax_key = 0ull;
+            if (P.prologue == PRO_COPYQ) {  // the whole quantized activation in one bulk copy
+                const uint32_t nb = (uint32_t)act_bytes(P.K, P.need16, P.need32);
+                if (tid == 0) {
+                    // the region was last read through the generic proxy
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive_expect_tx(&act_bar, nb);
+                    bulk_g2s(region, P.in, nb, &act_bar);
+                }
+                const bool landed = mbar_wait_bounded(&act_bar, act_phase, &abort_flag);
+                act_phase ^= 1u;
+                if (!landed) abort_flag = 1;
+            }
             float *stage = P.prologue == PRO_QUANT && P.K <= kMaxStaged
                                ? (float *)(region + act_bytes(P.K, P.need16, P.need32))
                                : nullptr;
@@ -1393,7 +1503,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
                 act_phase ^= 1u;
                 if (!landed) abort_flag = 1;
             }
-            quantize_act(P, tok, nw, stage, act, red);
+            if (P.prologue != PRO_COPYQ) quantize_act(P, tok, nw, stage, act, red);
             unsigned long long best = 0ull;
             int qb, qe;
             cta_groups(P.ngroup, qb, qe);
@@ -1411,14 +1521,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(const __grid_const
             auto flush = [&]() {
                 __syncwarp();
                 const int2 su = lane < nepi ? epi_su[warp][lane] : make_int2(0, -1);
+                int r0 = 0, r1 = 0;
                 if (su.y >= 0) {
                     const float2 y = epi_y[warp][lane];
                     const MvSeg &sg = P.seg[su.x];
-                    int r0, r1;
                     unit_rows(sg, su.y, r0, r1);
                     const EpiIn ein = epi_load(A, sg, r0, r1, pos);
                     unit_epilogue(A, sg, r0, r1, y.x, y.y, pos, ein, best);
                 }
+                if (P.seg[0].qout) hidden_quant_arrive(P.seg[0], r0, su.y >= 0);  // uniform: one segment
                 __syncwarp();
                 nepi = 0;
             };

@@ -50,6 +50,9 @@ struct cxm_model {
     float *out_norm = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     std::vector<void *> allocs;
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+    unsigned char *attq = nullptr;  // the attention output quantized for o_proj (carve_act layout)
+    unsigned char *hq = nullptr;    // the FFN hidden vector quantized for ffn_down (carve_act layout)
+    int *hcnt = nullptr;            // its per-sub-block counts of written values (zero between steps)
     float *scores = nullptr;  // attention scratch [n_head][ctx]
     int *err = nullptr;
     unsigned *bar = nullptr;  // grid-barrier counter of the decode kernel
@@ -61,6 +64,9 @@ struct cxm_model {
     uint32_t *samp_tok = nullptr;
     float *samp_probs = nullptr, *samp_prefix = nullptr;
     uint32_t *samp_k0 = nullptr, *samp_v0 = nullptr, *samp_k1 = nullptr, *samp_v1 = nullptr;
+    uint32_t *samp_ghist = nullptr;  // the sampler's per-CTA digit counts [sms * 256]
+    float *samp_gred = nullptr;      // its per-CTA maxima and 1/total [sms + 1]
+    unsigned *samp_bar = nullptr;    // its grid-barrier counter
     int sms = 148;
     // tensor parallelism: this rank's heads, KV heads, FFN rows and
     // vocabulary rows (all of them at tp = 1); the exchange areas (own, and
@@ -507,7 +513,7 @@ int set_kernel_smem_limits() {
     CU(cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, g_decode_smem_max));
     CU(cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     CU(cudaFuncSetAttribute(k_attn_out, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    CU(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kScanChunk * (int)sizeof(float)));
+    CU(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, kSampSmem));
     CU(cudaFuncSetAttribute(k_pf_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     return 0;
 }
@@ -857,6 +863,10 @@ std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode, int cls) {
         at.P = score_positions(H / KV);
         at.ring = attn_ring((int)c->max_tokens, kAttnBudget);
         at.scale = 1.0f / sqrtf((float)hd);  // src/ops.rs:1287
+        at.qout = m->attq;
+        at.qneed16 = sub_of(L.o.type) == 16;
+        at.qneed32 = sub_of(L.o.type) == 32;
+        at.qK = dl;
         {
             Phase ph{};
             ph.kind = PH_SCORES;
@@ -867,14 +877,25 @@ std::vector<Phase> step_program(cxm_model *m, cxm_cache *c, int mode, int cls) {
             prog.push_back(ph);
         }
         // o_proj + residual; RMSNorm + gate/up + SwiGLU; down + residual
-        prog.push_back(mv_phase({mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->x, cls)}, dl, PRO_QUANT, m->att, nullptr, 0.0f, 1));
-        prog.push_back(mv_phase({mv_seg(L.gu, F, PAIR_TWO, EPI_SWIGLU, m->h + (size_t)r * F, cls)}, D, PRO_NORM, m->x,
-                                L.ffn_norm, cfg.eps, 1));
+        // o_proj's input arrives quantized by the attention items
+        prog.push_back(mv_phase({mv_seg(L.o, D / 2, PAIR_ADJ, EPI_RESID, m->x, cls)}, dl, PRO_COPYQ,
+                                (const float *)m->attq, nullptr, 0.0f, 1));
+        // one GPU: the gate|up epilogue also quantizes the hidden vector for
+        // ffn_down as its sub-blocks complete, and down copies it in
+        MvSeg sg = mv_seg(L.gu, F, PAIR_TWO, EPI_SWIGLU, m->h + (size_t)r * F, cls);
+        if (!tp) {
+            sg.qout = m->hq;
+            sg.qcnt = m->hcnt;
+            sg.qsub = sub_of(L.down.type);
+            sg.qK = FF;
+        }
+        prog.push_back(mv_phase({sg}, D, PRO_NORM, m->x, L.ffn_norm, cfg.eps, 1));
         if (tp) prog.push_back(x_phase(PH_XGATHER, m->h, FF, 0, ++nx));
         MvSeg sd = mv_seg(L.down, dloc / 2, PAIR_ADJ, EPI_RESID, m->x + (size_t)r * dloc, cls);
         const size_t xo_off = xch_xo_off(FF) + (size_t)(l & 1) * D * sizeof(float);
         if (tp) sd.out2 = xo + (size_t)(l & 1) * D + (size_t)r * dloc;
-        prog.push_back(mv_phase({sd}, FF, PRO_QUANT, m->h, nullptr, 0.0f, 1));
+        if (tp) prog.push_back(mv_phase({sd}, FF, PRO_QUANT, m->h, nullptr, 0.0f, 1));
+        else prog.push_back(mv_phase({sd}, FF, PRO_COPYQ, (const float *)m->hq, nullptr, 0.0f, 1));
         if (tp) prog.push_back(x_phase(PH_XGATHER, m->x, D, xo_off, ++nx));
     }
     if (mode != STEP_PREFILL) {  // final RMSNorm, output projection, argmax
@@ -991,6 +1012,8 @@ DecodeArgs base_args(cxm_model *m) {
     a.argmax_key = m->argmax_key;
     a.rope_cos = m->rope_cos;
     a.rope_sin = m->rope_sin;
+    a.qcnt = m->hcnt;
+    a.nqcnt = m->cfg.ffn / 16;
     return a;
 }
 
@@ -1084,8 +1107,24 @@ int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out,
     a.val1 = m->samp_v1;
     a.d_stop = d_stop;
     a.eos = d_stop && m->cfg.has_eos ? (int)m->cfg.eos : -1;
-    k_sample<<<1, kSampThreads, 2 * kScanChunk * sizeof(float), m->stream>>>(a);
-    CU(cudaGetLastError());
+    a.ghist = m->samp_ghist;
+    a.gred = m->samp_gred;
+    a.bar = m->samp_bar;
+    a.err = m->err;
+    // about 1024 probabilities per CTA, at most one CTA per SM (all resident)
+    const int grid = std::max(1, std::min(m->sms, (a.n + kSampThreads - 1) / kSampThreads));
+    CU(cudaMemsetAsync(a.bar, 0, sizeof(unsigned), m->stream));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kSampThreads);
+    cfg.dynamicSmemBytes = kSampSmem;
+    cfg.stream = m->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CU(cudaLaunchKernelEx(&cfg, k_sample, a));
     return 0;
 }
 
@@ -1305,11 +1344,15 @@ extern "C" int cxm_model_open_tp(const char *path, int device, int tp_rank, int 
     }
     // activations
     if (m->alloc(&m->x, cfg.dim) || m->alloc(&m->q, cfg.dim) || m->alloc(&m->att, cfg.dim) ||
+        m->alloc(&m->attq, act_bytes(cfg.n_head * cfg.head_dim, 1, 1)) ||
+        m->alloc(&m->hq, act_bytes(cfg.ffn, 1, 1)) || m->alloc(&m->hcnt, (size_t)cfg.ffn / 16) ||
         m->alloc(&m->logits, cfg.vocab) || m->alloc(&m->err, 1) ||
         m->alloc(&m->bar, 1) || m->alloc(&m->argmax_key, 1) || m->alloc(&m->rng, 1) ||
         m->alloc(&m->samp_params, 2) || m->alloc(&m->samp_tok, 1) || m->alloc(&m->samp_probs, cfg.vocab) ||
         m->alloc(&m->samp_prefix, cfg.vocab) || m->alloc(&m->samp_k0, cfg.vocab) ||
         m->alloc(&m->samp_v0, cfg.vocab) || m->alloc(&m->samp_k1, cfg.vocab) || m->alloc(&m->samp_v1, cfg.vocab) ||
+        m->alloc(&m->samp_ghist, (size_t)m->sms * 256) || m->alloc(&m->samp_gred, (size_t)m->sms + 1) ||
+        m->alloc(&m->samp_bar, 1) ||
         m->alloc(&m->scores, (size_t)cfg.n_head * ((cfg.ctx + 3) & ~3)))
         return -1;
     CU(cudaMemset(m->err, 0, sizeof(int)));
@@ -2421,6 +2464,29 @@ extern "C" int cxm_debug_expf(const float *x, float *y, uint64_t n) {
     CU(cudaMalloc(&dy.p, n * 4));
     CU(cudaMemcpy(dx.p, x, n * 4, cudaMemcpyHostToDevice));
     k_expf<<<1024, 256>>>((const float *)dx.p, (float *)dy.p, (int)n);
+    CU(cudaGetLastError());
+    CU(cudaDeviceSynchronize());
+    CU(cudaMemcpy(y, dy.p, n * 4, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+__global__ void __launch_bounds__(kSampThreads, 1) k_seq_sums(const float *x, float *y, int n) {
+    extern __shared__ __align__(16) float seq_win[];
+    __shared__ ScanShared sh;
+    exact_scan(x, n, y, SCAN_ALL, 0.0f, seq_win, sh, nullptr);
+}
+
+extern "C" int cxm_debug_seq_sums(const float *x, float *y, uint64_t n) {
+    if (need_device()) return -1;
+    if (!x || !y || n == 0 || n > (1ull << 30)) {
+        set_error("bad arguments");
+        return -1;
+    }
+    DevBuf dx, dy;
+    CU(cudaMalloc(&dx.p, n * 4));
+    CU(cudaMalloc(&dy.p, n * 4));
+    CU(cudaMemcpy(dx.p, x, n * 4, cudaMemcpyHostToDevice));
+    k_seq_sums<<<1, kSampThreads, kScanWin * sizeof(float)>>>((const float *)dx.p, (float *)dy.p, (int)n);
     CU(cudaGetLastError());
     CU(cudaDeviceSynchronize());
     CU(cudaMemcpy(y, dy.p, n * 4, cudaMemcpyDeviceToHost));

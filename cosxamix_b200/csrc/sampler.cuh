@@ -1,4 +1,5 @@
-// Muestreador::elegir (src/sampler.rs:61-126) on the device, one CTA.
+// Muestreador::elegir (src/sampler.rs:61-126) on the device: one
+// cooperative launch over up to one CTA per SM.
 //
 // The reference's arithmetic, in its order:
 //   u      = (xorshift64*(state) >> 40) / 2^24, drawn first      (:56-59, :73)
@@ -9,23 +10,36 @@
 //          their mass (a sequential sum in that order) is below top_p, the
 //          whole vocabulary sorted instead; cut at the first cumulative sum
 //          >= top_p; walk the nucleus against u * (its sequential sum).
-// Every sum is sequential in the reference's order, on one thread: in the
+// Every sum is the reference's sequential f32 sum, value for value: in the
 // flat distributions of a random-init model consecutive cumulative sums are
-// ~1/vocab apart, so any other order changes the sampled token. The rest is
-// parallel: exps, and a stable LSD radix sort whose ties (equal
-// probabilities; the reference's unstable sort leaves their order
-// unspecified) come out by ascending index. The walk over the cumulative
-// sums, which never decrease, is a binary search.
+// ~1/vocab apart, so any other rounding changes the sampled token. The sums
+// are nevertheless taken in parallel (exact_scan below): while the running
+// sum stays inside one binade, each addition rounds to a multiple of that
+// binade's ulp, so the sequence is an integer prefix sum; only the terms
+// that leave the binade or round to even (ties) are added one at a time.
+// The candidates' mass and the nucleus's sum are entries of the sorted
+// order's cumulative sums (they add the same values in the same order from
+// zero), and the walks over cumulative sums, which never decrease, are
+// searches. The sort is a stable LSD radix sort over all CTAs whose ties
+// (equal probabilities; the reference's unstable sort leaves their order
+// unspecified) come out by ascending index. CTAs meet at bounded grid
+// barriers: a wait that runs out raises ERR_TIMEOUT and the launch returns.
 #pragma once
 
 #include "expf_glibc.h"
 #include "kernels.cuh"
+#include "step_kernels.cuh"
 
 namespace cxm {
 
 constexpr int kSampThreads = 1024;
 constexpr int kSampWarps = kSampThreads / 32;
 constexpr int kCandidates = 1024;  // src/sampler.rs:25
+constexpr int kScanPer = 8;        // terms per thread in a window of exact_scan
+constexpr int kScanWin = kScanPer * kSampThreads;
+constexpr int kHistRow = 257;      // radix counts: warp-major rows, padded
+// dynamic shared memory of k_sample: the radix counts, the scan's window
+constexpr int kSampSmem = kSampWarps * kHistRow * 4 + kScanWin * 4;
 
 struct SampleArgs {
     const float *logits;
@@ -39,6 +53,10 @@ struct SampleArgs {
     int eos;                  // the model's eos token (its pick sets *d_stop), or -1
     float *probs, *prefix;    // scratch [n]
     uint32_t *key0, *val0, *key1, *val1;  // scratch [n]
+    uint32_t *ghist;          // scratch [grid * 256]: each CTA's digit counts
+    float *gred;              // scratch [grid + 1]: each CTA's max, then 1/total
+    unsigned *bar;            // grid-barrier counter, zeroed before each launch
+    int *err;                 // ERR_TIMEOUT when a grid barrier's wait runs out
 };
 
 __device__ __forceinline__ unsigned long long azar_next(unsigned long long &st) {
@@ -69,40 +87,273 @@ __device__ __forceinline__ float block_max(float v, float *red) {
     return r;
 }
 
-// the count of digit d in warp w's chunk: warp-major with a padded row, so
-// a warp's lanes with different digits hit different banks
-constexpr int kHistRow = 257;
+
+// ── grid barrier (bounded) ──
+// `target` counts the arrivals every CTA has made so far; each poll is an L2
+// round trip, and 2^21 polls bound a wait near one second.
+constexpr uint32_t kSampBarrierSpins = 1u << 21;
+
+__device__ bool samp_sync(const SampleArgs &a, unsigned &target, int *ok_s) {
+    target += gridDim.x;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+        for (uint32_t i = 0;; i++) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
+            if ((int)(v - target) >= 0) break;
+            if (i >= kSampBarrierSpins) {
+                atomicOr(a.err, ERR_TIMEOUT);
+                ok = 0;
+                break;
+            }
+            if ((i & 255) == 255) {
+                if (*(volatile int *)a.err & ERR_TIMEOUT) {  // another CTA gave up
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        *ok_s = ok;
+    }
+    __syncthreads();
+    return *ok_s != 0;
+}
+
+// ── the reference's sequential f32 sum, exactly, in parallel ──
+// A running sum s in the binade of biased exponent eb (s < 2^(eb-126); the
+// subnormals share the binade eb = 1) is M·u with u = 2^(eb-150) and M an
+// integer below 2^24. Adding x >= 0 whose exact sum stays below the binade's
+// top rounds to the nearest multiple of u: M' = M + round(x/u), ties to an
+// even M'. So, from one state, a window of terms is classified at once:
+// kf = floor(x/u) and kr = round(x/u) (a tie rounds down here); the running
+// M is an integer prefix sum of kr; the first term that is a tie, or whose
+// exact sum reaches the binade's top (M + kf >= 2^24), or that is negative,
+// infinite or NaN, is an event, added as an f32 addition to the exact sum
+// before it, and the next window starts after it. Each window therefore adds
+// its terms exactly as the sequential loop does. A sum from zero crosses a
+// few dozen binades at most; ties need the bits of x below u/2 to be zero.
+struct ScanTerm {
+    uint32_t kf, kr;
+    bool ev;
+};
+
+__device__ __forceinline__ ScanTerm scan_term(float x, int eb) {
+    const uint32_t xb = __float_as_uint(x);
+    ScanTerm t{0u, 0u, false};
+    const int xe = (int)(xb >> 23);  // sign and exponent
+    if (xe >= 255) {  // negative (sign set), infinite or NaN
+        t.ev = true;
+        return t;
+    }
+    const uint32_t xm = xe ? ((xb & 0x7fffffu) | 0x800000u) : (xb & 0x7fffffu);
+    const int sh = eb - (xe > 1 ? xe : 1);  // x/u = xm / 2^sh
+    if (sh < -1) {
+        t.kf = t.kr = 1u << 25;  // x >= 2^25 u: beyond the binade's top
+    } else if (sh == -1) {
+        t.kf = t.kr = xm << 1;
+    } else if (sh == 0) {
+        t.kf = t.kr = xm;
+    } else if (sh <= 25) {
+        const uint32_t rem = xm & ((1u << sh) - 1u), half = 1u << (sh - 1);
+        t.kf = xm >> sh;
+        t.kr = t.kf + (rem > half ? 1u : 0u);
+        t.ev = rem == half;
+    }  // sh > 25: x < u/2, adds nothing and never ties
+    return t;
+}
+
+// M·2^(eb-150) as an f32 (exact: M <= 2^24)
+__device__ __forceinline__ float scan_value(unsigned long long M, int eb) {
+    const float f = (float)M;
+    const int e = eb - 150;
+    if (e >= -126) return __fmul_rn(f, __int_as_float((e + 127) << 23));
+    return __fmul_rn(__fmul_rn(f, __int_as_float(1 << 23)), __int_as_float((e + 253) << 23));
+}
+
+struct ScanShared {
+    unsigned long long wtot[kSampWarps];
+    int ev[2];
+    float s;
+    int pos;
+};
+
+enum : int { SCAN_ALL = 0, SCAN_UNTIL_GE = 1, SCAN_UNTIL_GT = 2 };
+
+// One CTA: the running sums of src[0..len) from 0.0f, each written to
+// dst[i] when dst is set. With SCAN_UNTIL_GE / _GT it stops after the window
+// in which the running sum first reaches >= / > `stop` (the later entries of
+// dst are then not written). Returns the number of leading terms summed
+// (uniform); *sum is the sum of those terms. `win` holds kScanWin floats.
+__device__ int exact_scan(const float *src, int len, float *dst, int mode, float stop, float *win, ScanShared &sh,
+                          float *sum) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        sh.s = 0.0f;
+        sh.pos = 0;
+        sh.ev[0] = sh.ev[1] = INT_MAX;
+    }
+    for (int it = 0;; it++) {
+        __syncthreads();
+        const int pos = sh.pos;
+        const float s = sh.s;
+        if (pos >= len || (mode == SCAN_UNTIL_GE && s >= stop) || (mode == SCAN_UNTIL_GT && s > stop)) break;
+        if (!(s <= 3.4028235e38f)) {  // infinite or NaN: the rest in order, on one thread
+            if (tid == 0) {
+                float r = s;
+                for (int i = pos; i < len; i++) {
+                    r = __fadd_rn(r, src[i]);
+                    if (dst) dst[i] = r;
+                }
+                sh.s = r;
+                sh.pos = len;
+            }
+            continue;
+        }
+        const uint32_t sb = __float_as_uint(s);
+        const int eb = (int)(sb >> 23) > 1 ? (int)(sb >> 23) : 1;
+        const unsigned long long M0 = (sb >> 23) ? ((sb & 0x7fffffu) | 0x800000u) : (sb & 0x7fffffu);
+        // the window, coalesced into this warp's 256 floats, then 8 consecutive terms per lane
+        float *wv = win + warp * 256;
+        const int wbase = pos + warp * 256;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int i = wbase + 32 * j + lane;
+            wv[32 * j + lane] = i < len ? __ldcg(src + i) : 0.0f;
+        }
+        __syncwarp();
+        const float4 v0 = ((const float4 *)wv)[2 * lane], v1 = ((const float4 *)wv)[2 * lane + 1];
+        const float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        const int base = wbase + 8 * lane;
+        ScanTerm t[8];
+        unsigned long long loc = 0;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            t[k] = scan_term(x[k], eb);
+            loc += t[k].kr;
+        }
+        // exclusive prefix of loc over the CTA (64-bit)
+        unsigned long long inc = loc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += v;
+        }
+        if (lane == 31) sh.wtot[warp] = inc;
+        __syncthreads();
+        unsigned long long wt = sh.wtot[lane], wi = wt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long v = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += v;
+        }
+        const unsigned long long wex = __shfl_sync(0xffffffffu, wi - wt, warp);
+        const unsigned long long ex = M0 + wex + inc - loc;
+        // this lane's first event
+        {
+            unsigned long long P = ex;
+            int e = -1;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (e < 0 && base + k < len && (t[k].ev || P + t[k].kf >= (1ull << 24))) e = k;
+                P += t[k].kr;
+            }
+            if (e >= 0) atomicMin(&sh.ev[it & 1], base + e);
+        }
+        __syncthreads();
+        const int E = sh.ev[it & 1];
+        if (tid == 0) sh.ev[(it + 1) & 1] = INT_MAX;
+        unsigned long long P = ex;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int i = base + k;
+            if (i == E) {  // the event: an f32 addition to the exact sum before it
+                const float r = __fadd_rn(scan_value(P, eb), x[k]);
+                if (dst) dst[i] = r;
+                sh.s = r;
+                sh.pos = i + 1;
+            }
+            if (i >= E || i >= len) break;
+            P += t[k].kr;
+            if (dst) dst[i] = scan_value(P, eb);
+        }
+        if (E == INT_MAX && tid == kSampThreads - 1) {
+            sh.s = scan_value(ex + loc, eb);
+            sh.pos = min(len, pos + kScanWin);
+        }
+    }
+    const int r = sh.pos;
+    if (sum) *sum = sh.s;
+    __syncthreads();
+    return r;
+}
+
+// first i in [0, len) with p[i] > t (gt) or >= t, over values that never
+// decrease; len if none. One CTA, uniform result.
+__device__ int block_first(const float *p, int len, float t, bool gt) {
+    const int tid = threadIdx.x;
+    int lo = 0, hi = len;  // the answer is in [lo, hi]
+    while (hi > lo) {
+        const int span = hi - lo;
+        const int stride = span <= kSampThreads ? 1 : (span + kSampThreads - 1) / kSampThreads;
+        const int i = lo + tid * stride;
+        bool below = false;
+        if (i < hi) {
+            const float v = __ldcg(p + i);
+            below = gt ? !(v > t) : !(v >= t);
+        }
+        const int nf = __syncthreads_count(below);  // the samples below t come first
+        if (stride == 1) return lo + nf;
+        if (nf == 0) return lo;
+        const int nlo = lo + (nf - 1) * stride + 1;
+        hi = min(hi, lo + nf * stride);
+        lo = nlo;
+    }
+    return lo;
+}
+
+// ── one stable LSD radix pass over all CTAs, on 8 key bits ──
+// A CTA owns the contiguous tile [lo, hi) and its warps contiguous chunks of
+// it. Counts per (digit, warp) give each chunk's place inside the tile; the
+// CTAs' digit counts (through ghist, across a grid barrier) give the tile's
+// place among the CTAs, so equal digits keep their (CTA, warp, lane) order.
 __device__ __forceinline__ int hidx(int d, int w) { return w * kHistRow + d; }
 
-// one stable counting pass of an LSD radix sort on 8 key bits; a warp owns a
-// contiguous chunk and keeps its elements' order
-__device__ __forceinline__ void radix_pass(const uint32_t *kin, const uint32_t *vin, uint32_t *kout, uint32_t *vout, int n, int shift,
-                           uint32_t *hist /* [kSampWarps][kHistRow] */) {
+__device__ bool radix_pass(const SampleArgs &a, const uint32_t *kin, const uint32_t *vin, uint32_t *kout,
+                           uint32_t *vout, int lo, int hi, int shift, uint32_t *hist, unsigned &target, int *ok_s) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int chunk = (n + kSampWarps - 1) / kSampWarps;
-    const int lo = warp * chunk, hi = min(n, lo + chunk);
+    const int chunk = (hi - lo + kSampWarps - 1) / kSampWarps;
+    const int wlo = lo + warp * chunk, whi = min(hi, wlo + chunk);
+    __shared__ uint32_t dall[4][256], dbef[4][256], gadj[256];
+    __shared__ uint32_t wsum[kSampWarps];
     for (int i = tid; i < kHistRow * kSampWarps; i += kSampThreads) hist[i] = 0;
     __syncthreads();
-    // four keys per lane in flight before their counts
-    for (int b = lo; b < hi; b += 128) {
+    for (int b = wlo; b < whi; b += 128) {
         uint32_t k[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             const int i = b + 32 * u + lane;
-            k[u] = i < hi ? __ldcg(kin + i) : 0u;
+            k[u] = i < whi ? __ldcg(kin + i) : 0u;
         }
 #pragma unroll
         for (int u = 0; u < 4; u++)
-            if (b + 32 * u + lane < hi) atomicAdd(&hist[hidx((k[u] >> shift) & 255, warp)], 1u);
+            if (b + 32 * u + lane < whi) atomicAdd(&hist[hidx((k[u] >> shift) & 255, warp)], 1u);
     }
     __syncthreads();
-    // exclusive scan over (digit, warp): digit-major, so equal digits keep
-    // warp (= position) order; a thread per 8 entries, then the warps' sums
+    // this CTA's digit counts, published for the others
+    if (tid < 256) {
+        uint32_t c = 0;
+        for (int w = 0; w < kSampWarps; w++) c += hist[hidx(tid, w)];
+        a.ghist[blockIdx.x * 256 + tid] = c;
+    }
+    // exclusive scan over (digit, warp), digit-major: a thread per 8 entries
     {
         constexpr int kPer = 256 * kSampWarps / kSampThreads;
         uint32_t c[kPer], loc = 0;
 #pragma unroll
-        for (int j = 0; j < kPer; j++) {  // entry e = digit * kSampWarps + warp
+        for (int j = 0; j < kPer; j++) {
             const int e = tid * kPer + j;
             c[j] = hist[hidx(e / kSampWarps, e % kSampWarps)];
             loc += c[j];
@@ -113,277 +364,171 @@ __device__ __forceinline__ void radix_pass(const uint32_t *kin, const uint32_t *
             const uint32_t v = __shfl_up_sync(0xffffffffu, inc, o);
             if (lane >= o) inc += v;
         }
-        __shared__ uint32_t wsum[kSampWarps];
         if (lane == 31) wsum[warp] = inc;
         __syncthreads();
-        if (warp == 0) {
-            uint32_t w = lane < kSampWarps ? wsum[lane] : 0u, wi = w;
+        uint32_t wt = wsum[lane], wi = wt;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t v = __shfl_up_sync(0xffffffffu, wi, o);
-                if (lane >= o) wi += v;
-            }
-            if (lane < kSampWarps) wsum[lane] = wi - w;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t v = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += v;
         }
-        __syncthreads();
-        uint32_t run = wsum[warp] + inc - loc;
+        uint32_t run = __shfl_sync(0xffffffffu, wi - wt, warp) + inc - loc;
 #pragma unroll
         for (int j = 0; j < kPer; j++) {
             const int e = tid * kPer + j;
-            hist[hidx(e / kSampWarps, e % kSampWarps)] = run;
+            hist[hidx(e / kSampWarps, e % kSampWarps)] = run;  // offset inside the tile
             run += c[j];
         }
     }
-    __syncthreads();
-    // the scatter keeps the chunk's order, 32 keys at a time; the next 32
+    if (!samp_sync(a, target, ok_s)) return false;
+    // the tile's place: digit d starts after the counts of all smaller
+    // digits and of d in the CTAs before this one; four threads per digit,
+    // a quarter of the CTAs each
+    {
+        const int d = tid & 255, part = tid >> 8, G = gridDim.x;
+        const int q = (G + 3) / 4, c0 = part * q, c1 = min(G, c0 + q);
+        uint32_t all = 0, before = 0;
+        for (int c = c0; c < c1; c++) {
+            const uint32_t v = __ldcg(a.ghist + c * 256 + d);
+            all += v;
+            before += c < (int)blockIdx.x ? v : 0u;
+        }
+        dall[part][d] = all;
+        dbef[part][d] = before;
+        __syncthreads();
+        uint32_t tot = 0, inc = 0;
+        if (tid < 256) {  // warps 0-7: an exclusive scan of the 256 digit totals
+            tot = dall[0][d] + dall[1][d] + dall[2][d] + dall[3][d];
+            inc = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t v = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += v;
+            }
+            if (lane == 31) wsum[warp] = inc;
+        }
+        __syncthreads();
+        if (tid < 256) {
+            uint32_t woff = 0;
+            for (int w = 0; w < warp; w++) woff += wsum[w];
+            const uint32_t bef = dbef[0][d] + dbef[1][d] + dbef[2][d] + dbef[3][d];
+            gadj[d] = woff + inc - tot + bef - hist[hidx(d, 0)];
+        }
+        __syncthreads();
+        for (int e = tid; e < 256 * kSampWarps; e += kSampThreads) hist[hidx(e & 255, e >> 8)] += gadj[e & 255];
+        __syncthreads();
+    }
+    // the scatter keeps each chunk's order, 32 keys at a time; the next 32
     // keys and values are loaded while this 32 is placed
-    uint32_t kn = lo + lane < hi ? __ldcg(kin + lo + lane) : 0u;
-    uint32_t vn = lo + lane < hi ? __ldcg(vin + lo + lane) : 0u;
-    for (int b = lo; b < hi; b += 32) {
+    uint32_t kn = wlo + lane < whi ? __ldcg(kin + wlo + lane) : 0u;
+    uint32_t vn = wlo + lane < whi ? __ldcg(vin + wlo + lane) : 0u;
+    for (int b = wlo; b < whi; b += 32) {
         const int i = b + lane;
-        const bool ok = i < hi;
-        const uint32_t k = kn, vv = vn, d = (k >> shift) & 255;
-        if (b + 32 + lane < hi) {
+        const bool ok = i < whi;
+        const uint32_t k = kn, vv = vn, dg = (k >> shift) & 255;
+        if (b + 32 + lane < whi) {
             kn = __ldcg(kin + b + 32 + lane);
             vn = __ldcg(vin + b + 32 + lane);
         }
-        const unsigned same = __match_any_sync(0xffffffffu, ok ? d : 0x100u + lane);
+        const unsigned same = __match_any_sync(0xffffffffu, ok ? dg : 0x100u + lane);
         const int rank = __popc(same & ((1u << lane) - 1));
         const int leader = __ffs(same) - 1;
         uint32_t base = 0;
-        if (ok && lane == leader) base = hist[hidx(d, warp)];
+        if (ok && lane == leader) base = hist[hidx(dg, warp)];
         base = __shfl_sync(0xffffffffu, base, leader);
         if (ok) {
             kout[base + rank] = k;
             vout[base + rank] = vv;
         }
         __syncwarp();
-        if (ok && lane == leader) hist[hidx(d, warp)] = base + __popc(same);
+        if (ok && lane == leader) hist[hidx(dg, warp)] = base + __popc(same);
         __syncwarp();
     }
-    __syncthreads();
-}
-
-constexpr int kScanChunk = 8192;  // floats per shared-memory stage of a sequential scan
-
-// Thread 0 adds src[0..len) in order, from 0.0f, writing each running sum to
-// dst[i] when dst is set and stopping after the first i with sum >= stop when
-// use_stop. The other threads stage the next chunk of src into shared memory
-// meanwhile. Returns the number of terms added (uniform).
-__device__ __forceinline__ int seq_scan(const float *src, int len, float *dst, bool use_stop, float stop, float *stage,
-                        float *sum_out, int *flag) {
-    const int tid = threadIdx.x;
-    float acc = 0.0f;
-    int done = len;
-    const int nchunk = (len + kScanChunk - 1) / kScanChunk;
-    if (tid == 0) *flag = 0;
-    for (int i = tid; i < min(len, kScanChunk); i += kSampThreads) stage[i] = src[i];
-    __syncthreads();
-    for (int c = 0; c < nchunk; c++) {
-        const float *cur = stage + (c & 1) * kScanChunk;
-        float *nxt = stage + ((c + 1) & 1) * kScanChunk;
-        const int base = c * kScanChunk, cnt = min(kScanChunk, len - base);
-        if (tid == 0) {
-            // 16 values per step: four vector loads in flight, then the adds
-            // in order; the running sums never decrease (probabilities are
-            // >= 0), so the step's last one tells whether the stop is inside
-            int i = 0;
-            // the next step's four loads are issued before this step's adds
-            float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0, n2 = n0, n3 = n0;
-            if (16 <= cnt) {
-                const float4 *c4 = (const float4 *)cur;
-                n0 = c4[0];
-                n1 = c4[1];
-                n2 = c4[2];
-                n3 = c4[3];
-            }
-            for (; i + 16 <= cnt; i += 16) {
-                const float4 q0 = n0, q1 = n1, q2 = n2, q3 = n3;
-                if (i + 32 <= cnt) {
-                    const float4 *c4 = (const float4 *)(cur + i + 16);
-                    n0 = c4[0];
-                    n1 = c4[1];
-                    n2 = c4[2];
-                    n3 = c4[3];
-                }
-                float r[16];
-                r[0] = __fadd_rn(acc, q0.x);
-                r[1] = __fadd_rn(r[0], q0.y);
-                r[2] = __fadd_rn(r[1], q0.z);
-                r[3] = __fadd_rn(r[2], q0.w);
-                r[4] = __fadd_rn(r[3], q1.x);
-                r[5] = __fadd_rn(r[4], q1.y);
-                r[6] = __fadd_rn(r[5], q1.z);
-                r[7] = __fadd_rn(r[6], q1.w);
-                r[8] = __fadd_rn(r[7], q2.x);
-                r[9] = __fadd_rn(r[8], q2.y);
-                r[10] = __fadd_rn(r[9], q2.z);
-                r[11] = __fadd_rn(r[10], q2.w);
-                r[12] = __fadd_rn(r[11], q3.x);
-                r[13] = __fadd_rn(r[12], q3.y);
-                r[14] = __fadd_rn(r[13], q3.z);
-                r[15] = __fadd_rn(r[14], q3.w);
-                if (dst) {
-                    float4 *d4 = (float4 *)(dst + base + i);
-                    d4[0] = make_float4(r[0], r[1], r[2], r[3]);
-                    d4[1] = make_float4(r[4], r[5], r[6], r[7]);
-                    d4[2] = make_float4(r[8], r[9], r[10], r[11]);
-                    d4[3] = make_float4(r[12], r[13], r[14], r[15]);
-                }
-                if (use_stop && r[15] >= stop) {
-                    int j = 0;
-                    while (r[j] < stop) j++;
-                    acc = r[j];
-                    done = base + i + j + 1;
-                    *flag = 1;
-                    break;
-                }
-                acc = r[15];
-            }
-            if (!(use_stop && done < len)) {
-                for (; i < cnt; i++) {
-                    acc = __fadd_rn(acc, cur[i]);
-                    if (dst) dst[base + i] = acc;
-                    if (use_stop && acc >= stop) {
-                        done = base + i + 1;
-                        *flag = 1;
-                        break;
-                    }
-                }
-            }
-        } else if (c + 1 < nchunk) {
-            const int nb = base + kScanChunk, ncnt = min(kScanChunk, len - nb);
-            for (int i = tid - 1; i < ncnt; i += kSampThreads - 1) nxt[i] = src[nb + i];
-        }
-        __syncthreads();
-        if (*flag) break;
-    }
-    if (tid == 0) {
-        *sum_out = acc;
-        *flag = done;
-    }
-    __syncthreads();
-    const int r = *flag;
-    __syncthreads();
-    return r;
-}
-
-// first i in [0, len) with prefix[i] > t (prefix never decreases); len if none
-__device__ __forceinline__ int first_above(const float *prefix, int len, float t) {
-    int lo = 0, hi = len;
-    while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if (prefix[mid] > t) hi = mid;
-        else lo = mid + 1;
-    }
-    return lo;
+    return samp_sync(a, target, ok_s);
 }
 
 __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constant__ SampleArgs a) {
     if (a.d_stop && *(volatile const int *)a.d_stop) return;  // the generation already met its eos (uniform)
-    extern __shared__ __align__(16) float stage[];  // 2 x kScanChunk
+    extern __shared__ __align__(16) unsigned char samp_smem[];
+    uint32_t *hist = (uint32_t *)samp_smem;                          // [kSampWarps][kHistRow]
+    float *win = (float *)(samp_smem + kSampWarps * kHistRow * 4);  // [kScanWin]
     __shared__ float red[kSampWarps];
-    __shared__ uint32_t hist[kHistRow * kSampWarps];
+    __shared__ ScanShared sh;
     __shared__ float u_s, sum_s;
-    __shared__ int flag_s;
-    const int tid = threadIdx.x, n = a.n;
+    __shared__ int ok_s;
+    const int tid = threadIdx.x, n = a.n, G = gridDim.x, cta = blockIdx.x;
+    const int tile = (n + G - 1) / G, lo = min(n, cta * tile), hi = min(n, lo + tile);
     const float inv_t = a.params[0], top_p = a.params[1];
-    if (tid == 0) {
+    unsigned target = 0;
+    if (cta == 0 && tid == 0) {
         unsigned long long st = *a.rng;
         u_s = (float)(azar_next(st) >> 40) / 16777216.0f;
         *a.rng = st;
     }
-    // temperature, then softmax (src/ops.rs:1206-1230). The element-wise
-    // loops take four elements per thread per step, loads first, so their
-    // L2 round trips overlap.
-    constexpr int kU = 4, kStep = kU * kSampThreads;
+    // temperature, then softmax (src/ops.rs:1206-1230), each CTA on its tile
     float m = -INFINITY;
-    for (int i0 = tid; i0 < n; i0 += kStep) {
-        float v[kU];
-#pragma unroll
-        for (int u = 0; u < kU; u++) v[u] = i0 + u * kSampThreads < n ? __ldcg(a.logits + i0 + u * kSampThreads) : 0.0f;
-#pragma unroll
-        for (int u = 0; u < kU; u++)
-            if (i0 + u * kSampThreads < n) {
-                const float t = __fmul_rn(v[u], inv_t);
-                a.probs[i0 + u * kSampThreads] = t;
-                m = fmaxf(m, t);
-            }
+    for (int i = lo + tid; i < hi; i += kSampThreads) {
+        const float t = __fmul_rn(__ldcg(a.logits + i), inv_t);
+        a.probs[i] = t;
+        m = fmaxf(m, t);
     }
     m = block_max(m, red);
-    if (!isfinite(m)) {
+    if (tid == 0) a.gred[cta] = m;
+    if (!samp_sync(a, target, &ok_s)) return;
+    float gm = -INFINITY;
+    for (int c = tid; c < G; c += kSampThreads) gm = fmaxf(gm, __ldcg(a.gred + c));
+    gm = block_max(gm, red);
+    if (!isfinite(gm)) {  // all -inf, or +inf present: the uniform distribution
         const float p = __fdiv_rn(1.0f, (float)n);
-        for (int i = tid; i < n; i += kSampThreads) a.probs[i] = p;
+        for (int i = lo + tid; i < hi; i += kSampThreads) a.probs[i] = p;
     } else {
-        for (int i0 = tid; i0 < n; i0 += kStep) {
-            float v[kU];
-#pragma unroll
-            for (int u = 0; u < kU; u++) v[u] = i0 + u * kSampThreads < n ? a.probs[i0 + u * kSampThreads] : 0.0f;
-#pragma unroll
-            for (int u = 0; u < kU; u++)
-                if (i0 + u * kSampThreads < n) a.probs[i0 + u * kSampThreads] = expf_glibc(__fsub_rn(v[u], m));
+        for (int i = lo + tid; i < hi; i += kSampThreads) a.probs[i] = expf_glibc(__fsub_rn(a.probs[i], gm));
+        if (!samp_sync(a, target, &ok_s)) return;
+        if (cta == 0) {  // the total, in index order
+            exact_scan(a.probs, n, nullptr, SCAN_ALL, 0.0f, win, sh, &sum_s);
+            if (tid == 0) a.gred[G] = __fdiv_rn(1.0f, sum_s);
         }
-        __syncthreads();
-        seq_scan(a.probs, n, nullptr, false, 0.0f, stage, &sum_s, &flag_s);  // the total, in index order
-        const float inv = __fdiv_rn(1.0f, sum_s);
-        for (int i0 = tid; i0 < n; i0 += kStep) {
-            float v[kU];
-#pragma unroll
-            for (int u = 0; u < kU; u++) v[u] = i0 + u * kSampThreads < n ? a.probs[i0 + u * kSampThreads] : 0.0f;
-#pragma unroll
-            for (int u = 0; u < kU; u++)
-                if (i0 + u * kSampThreads < n) a.probs[i0 + u * kSampThreads] = __fmul_rn(v[u], inv);
-        }
+        if (!samp_sync(a, target, &ok_s)) return;
+        const float inv = __ldcg(a.gred + G);
+        for (int i = lo + tid; i < hi; i += kSampThreads) a.probs[i] = __fmul_rn(a.probs[i], inv);
     }
-    __syncthreads();
-    const float u = u_s;
     uint32_t tok;
     if (top_p >= 1.0f) {
         // the whole vocabulary in index order (src/sampler.rs:84-86)
-        seq_scan(a.probs, n, a.prefix, false, 0.0f, stage, &sum_s, &flag_s);
-        const int i = first_above(a.prefix, n, u);
-        tok = (uint32_t)(i < n ? i : n - 1);
+        if (!samp_sync(a, target, &ok_s) || cta != 0) return;
+        const float u = u_s;
+        const int len = exact_scan(a.probs, n, a.prefix, SCAN_UNTIL_GT, u, win, sh, nullptr);
+        const int i = block_first(a.prefix, len, u, true);
+        tok = (uint32_t)(i < len ? i : n - 1);
     } else {
         // descending probability, ties by ascending index: ascending key
         // 0x7fffffff - bits (probabilities are >= 0) on an index-ordered start
-        for (int i0 = tid; i0 < n; i0 += kStep) {
-            float v[kU];
-#pragma unroll
-            for (int u = 0; u < kU; u++) v[u] = i0 + u * kSampThreads < n ? a.probs[i0 + u * kSampThreads] : 0.0f;
-#pragma unroll
-            for (int u = 0; u < kU; u++)
-                if (i0 + u * kSampThreads < n) {
-                    a.key0[i0 + u * kSampThreads] = 0x7fffffffu - __float_as_uint(v[u]);
-                    a.val0[i0 + u * kSampThreads] = (uint32_t)(i0 + u * kSampThreads);
-                }
+        for (int i = lo + tid; i < hi; i += kSampThreads) {
+            a.key0[i] = 0x7fffffffu - __float_as_uint(a.probs[i]);
+            a.val0[i] = (uint32_t)i;
         }
         __syncthreads();
-        radix_pass(a.key0, a.val0, a.key1, a.val1, n, 0, hist);
-        radix_pass(a.key1, a.val1, a.key0, a.val0, n, 8, hist);
-        radix_pass(a.key0, a.val0, a.key1, a.val1, n, 16, hist);
-        radix_pass(a.key1, a.val1, a.key0, a.val0, n, 24, hist);
+        if (!radix_pass(a, a.key0, a.val0, a.key1, a.val1, lo, hi, 0, hist, target, &ok_s) ||
+            !radix_pass(a, a.key1, a.val1, a.key0, a.val0, lo, hi, 8, hist, target, &ok_s) ||
+            !radix_pass(a, a.key0, a.val0, a.key1, a.val1, lo, hi, 16, hist, target, &ok_s) ||
+            !radix_pass(a, a.key1, a.val1, a.key0, a.val0, lo, hi, 24, hist, target, &ok_s))
+            return;
         const uint32_t *order = a.val0;
-        float *sorted = a.key1 ? (float *)a.key1 : nullptr;  // probabilities in sorted order
-        for (int i0 = tid; i0 < n; i0 += kStep) {
-            uint32_t o[kU];
-            float v[kU];
-#pragma unroll
-            for (int u = 0; u < kU; u++) o[u] = i0 + u * kSampThreads < n ? __ldcg(order + i0 + u * kSampThreads) : 0u;
-#pragma unroll
-            for (int u = 0; u < kU; u++) v[u] = i0 + u * kSampThreads < n ? a.probs[o[u]] : 0.0f;
-#pragma unroll
-            for (int u = 0; u < kU; u++)
-                if (i0 + u * kSampThreads < n) sorted[i0 + u * kSampThreads] = v[u];
-        }
-        __syncthreads();
-        const int k = n < kCandidates ? n : kCandidates;
-        seq_scan(sorted, k, nullptr, false, 0.0f, stage, &sum_s, &flag_s);  // the candidates' mass
-        const int len = (sum_s < top_p && k < n) ? n : k;
-        // cut at the first cumulative sum >= top_p (the crossing token is in);
-        // the nucleus's sum is the cumulative sum there
-        const int cut = seq_scan(sorted, len, a.prefix, true, top_p, stage, &sum_s, &flag_s);
-        const int i = first_above(a.prefix, cut, __fmul_rn(u, sum_s));
-        tok = order[i < cut ? i : cut - 1];
+        float *sorted = (float *)a.key1;  // probabilities in sorted order
+        for (int i = lo + tid; i < hi; i += kSampThreads) sorted[i] = __ldcg(a.probs + __ldcg(order + i));
+        if (!samp_sync(a, target, &ok_s) || cta != 0) return;
+        const float u = u_s;
+        // The cumulative sums of the sorted probabilities. The candidates'
+        // mass is the one at k - 1; below top_p (with k < n) the whole order
+        // is the nucleus, else the candidates, whose first sum >= top_p then
+        // comes before k: either way the cut is after the first sum >= top_p,
+        // or at n (src/sampler.rs:96-117).
+        const int len = exact_scan(sorted, n, a.prefix, SCAN_UNTIL_GE, top_p, win, sh, nullptr);
+        const int first = block_first(a.prefix, len, top_p, false);
+        const int cut = first < len ? first + 1 : n;
+        const float total = __ldcg(a.prefix + cut - 1);
+        const int i = block_first(a.prefix, cut, __fmul_rn(u, total), true);
+        tok = __ldcg(order + (i < cut ? i : cut - 1));
     }
     if (tid == 0) {
         if (a.toks) a.toks[*a.d_len] = tok;

@@ -30,7 +30,8 @@ enum Pairing : int {
 enum Prologue : int {
     PRO_NORM = 0,   // RMSNorm then quantize (src/kernels/scalar.rs:36-54, src/ops.rs:178-198)
     PRO_QUANT = 1,  // quantize only
-    PRO_EMBED = 2   // embedding row of the step's token, then RMSNorm + quantize
+    PRO_EMBED = 2,  // embedding row of the step's token, then RMSNorm + quantize
+    PRO_COPYQ = 3   // the activation arrives quantized (by the phase that produced it): one bulk copy
 };
 
 enum Epilogue : int {

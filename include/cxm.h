@@ -214,6 +214,11 @@ int cxm_attention_noalloc(const float *q, const float *k, const float *v, uint32
  * reference's f32::exp calls (src/ops.rs:1221, src/kernels/scalar.rs:65). */
 int cxm_debug_expf(const float *x, float *y, uint64_t n);
 
+/* y[i] = x[0] + ... + x[i] as the reference's sequential f32 loops add them
+ * (`total += *v`, src/ops.rs:1222; `acumulada += ...`, src/sampler.rs:110,
+ * :144), each running sum rounded in turn: the device sampler's summation. */
+int cxm_debug_seq_sums(const float *x, float *y, uint64_t n);
+
 /* ── measurement hooks (no counterpart in the reference: timing only) ──── */
 
 /* Replay the greedy decode step `steps` times for the token at the cache's
