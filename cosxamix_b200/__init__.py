@@ -87,6 +87,7 @@ def lib() -> C.CDLL:
             "cxm_bench_decode": (C.c_int, [P, P, C.c_uint32, C.POINTER(C.c_float)]),
             "cxm_bench_decode_sampled": (C.c_int, [P, P, P, C.c_uint32, C.POINTER(C.c_float)]),
             "cxm_bench_matvec": (C.c_int, [P, C.c_uint32, C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
+            "cxm_bench_sample": (C.c_int, [P, P, C.c_uint32, C.POINTER(C.c_float), P, C.c_uint32]),
             "cxm_step_launches": (C.c_int, [P]),
             "cxm_synth_write": (C.c_int, [C.POINTER(SynthSpec), C.c_char_p]),
             "cxm_quantize": (C.c_int64, [C.c_int, P, C.c_uint64, P, C.c_uint64]),
@@ -349,6 +350,14 @@ class Modelo:
         else:
             _check(lib().cxm_bench_decode_sampled(self.h, cache.h, sampler.h, steps, C.byref(ms)))
         return ms.value
+
+    def bench_sample(self, sampler: "Muestreador", reps: int):
+        """Device time (ms) of `reps` runs of the device sampler on the logits
+        of the last step, and the last run's step ends (ns from its start)."""
+        ms = C.c_float(0)
+        ph = np.zeros(12, np.uint64)
+        _check(lib().cxm_bench_sample(self.h, sampler.h, reps, C.byref(ms), _ptr(ph), ph.size))
+        return ms.value, ph.tolist()
 
     def bench_matvec(self, reps: int):
         ms = C.c_float(0)

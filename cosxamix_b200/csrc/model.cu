@@ -502,6 +502,7 @@ size_t out_smem(uint32_t max_pos) {
 }
 
 int g_decode_smem_max = 0;  // dynamic shared memory the decode kernel may use
+int g_pf_smem_max = 0;      // and the prompt GEMM
 
 int set_kernel_smem_limits() {
     int dev = 0, optin = 0;
@@ -514,7 +515,9 @@ int set_kernel_smem_limits() {
     CU(cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     CU(cudaFuncSetAttribute(k_attn_out, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     CU(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, kSampSmem));
-    CU(cudaFuncSetAttribute(k_pf_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    CU(cudaFuncGetAttributes(&fa_, k_pf_gemm));
+    g_pf_smem_max = optin - (int)fa_.sharedSizeBytes;
+    CU(cudaFuncSetAttribute(k_pf_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, g_pf_smem_max));
     return 0;
 }
 
@@ -591,6 +594,11 @@ int pf_gemm(cudaStream_t st, const MvSeg &seg, int t, int pos0, int ld_out, cons
     const PfSmem L = pf_smem(seg.M.type, seg.M.K);
     // at least 116 KB, so no two of these CTAs share an SM (each takes all 512 TMEM columns)
     const size_t smem = std::max<size_t>(L.total + 128, 116 * 1024);
+    if (smem > (size_t)g_pf_smem_max) {
+        set_error("the prompt GEMM needs %zu bytes of shared memory for K = %d; the device allows %d", smem, seg.M.K,
+                  g_pf_smem_max);
+        return -1;
+    }
     const dim3 grid((seg.M.rows + N - 1) / N, (t + kPfM - 1) / kPfM);
     k_pf_gemm<<<grid, kPfThreads, smem, st>>>(G);
     CU(cudaGetLastError());
@@ -1017,7 +1025,8 @@ DecodeArgs base_args(cxm_model *m) {
     return a;
 }
 
-int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out, int *d_stop);
+int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out, int *d_stop,
+                  unsigned long long *stamps = nullptr);
 
 int enqueue_step(cxm_model *m, cxm_cache *c, int mode, int cls) {
     if (!m->connected) {
@@ -1090,8 +1099,10 @@ int run_steps(cxm_model *m, cxm_cache *c, int mode, uint64_t rows, uint32_t n) {
 
 // the device Muestreador::elegir on the model's logits, with (1/T, top_p) and
 // the RNG state from device memory; the token goes to toks[*d_len] or *out
-int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out, int *d_stop) {
+int launch_sample(cxm_model *m, const int *d_len, uint32_t *toks, uint32_t *out, int *d_stop,
+                  unsigned long long *stamps) {
     SampleArgs a{};
+    a.stamps = stamps;
     a.logits = m->logits;
     a.n = m->cfg.vocab;
     a.params = m->samp_params;
@@ -2471,9 +2482,8 @@ extern "C" int cxm_debug_expf(const float *x, float *y, uint64_t n) {
 }
 
 __global__ void __launch_bounds__(kSampThreads, 1) k_seq_sums(const float *x, float *y, int n) {
-    extern __shared__ __align__(16) float seq_win[];
     __shared__ ScanShared sh;
-    exact_scan(x, n, y, SCAN_ALL, 0.0f, seq_win, sh, nullptr);
+    exact_scan(x, n, y, SCAN_ALL, 0.0f, sh, nullptr);
 }
 
 extern "C" int cxm_debug_seq_sums(const float *x, float *y, uint64_t n) {
@@ -2486,7 +2496,7 @@ extern "C" int cxm_debug_seq_sums(const float *x, float *y, uint64_t n) {
     CU(cudaMalloc(&dx.p, n * 4));
     CU(cudaMalloc(&dy.p, n * 4));
     CU(cudaMemcpy(dx.p, x, n * 4, cudaMemcpyHostToDevice));
-    k_seq_sums<<<1, kSampThreads, kScanWin * sizeof(float)>>>((const float *)dx.p, (float *)dy.p, (int)n);
+    k_seq_sums<<<1, kSampThreads>>>((const float *)dx.p, (float *)dy.p, (int)n);
     CU(cudaGetLastError());
     CU(cudaDeviceSynchronize());
     CU(cudaMemcpy(y, dy.p, n * 4, cudaMemcpyDeviceToHost));
@@ -2542,6 +2552,45 @@ extern "C" int cxm_bench_decode_sampled(cxm_model *m, cxm_cache *c, cxm_sampler 
         s->state = st;
     }
     return set_len(c, c->len + steps);
+}
+
+extern "C" int cxm_bench_sample(cxm_model *m, cxm_sampler *s, uint32_t reps, float *ms_total, uint64_t *phase_ns,
+                                uint32_t nphase) {
+    if (!m || !s || !ms_total || reps == 0 || !(s->temperature > 0.0f) || (phase_ns && nphase > (uint32_t)kSampStamps)) {
+        set_error("bad arguments");
+        return -1;
+    }
+    CU(cudaSetDevice(m->device));
+    if (set_sampler(m, s)) return -1;
+    DevBuf st;
+    CU(cudaMalloc(&st.p, kSampStamps * sizeof(unsigned long long)));
+    CU(cudaMemsetAsync(st.p, 0, kSampStamps * sizeof(unsigned long long), m->stream));
+    cudaEvent_t e0, e1;
+    CU(cudaEventCreate(&e0));
+    CU(cudaEventCreate(&e1));
+    CU(cudaEventRecord(e0, m->stream));
+    for (uint32_t i = 0; i < reps; i++)
+        if (launch_sample(m, nullptr, nullptr, m->samp_tok, nullptr, i + 1 == reps && phase_ns ? (unsigned long long *)st.p : nullptr))
+            return -1;
+    CU(cudaEventRecord(e1, m->stream));
+    CU(cudaEventSynchronize(e1));
+    CU(cudaEventElapsedTime(ms_total, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (check_err(m)) return -1;
+    if (phase_ns) {
+        unsigned long long h[kSampStamps];
+        CU(cudaMemcpy(h, st.p, sizeof(h), cudaMemcpyDeviceToHost));
+        for (uint32_t k = 0; k < nphase; k++) phase_ns[k] = h[k] ? h[k] - h[0] : 0;
+    }
+    for (uint32_t i = 0; i < reps; i++) {  // one draw per run
+        uint64_t x = s->state;
+        x ^= x >> 12;
+        x ^= x << 25;
+        x ^= x >> 27;
+        s->state = x;
+    }
+    return 0;
 }
 
 extern "C" int cxm_bench_matvec(cxm_model *m, uint32_t reps, float *ms_per_launch, uint64_t *bytes_per_launch) {

@@ -204,8 +204,10 @@ struct PfGemm {
     int fused;
 };
 
-constexpr int kPfThreads = 256;  // warps 0-3: epilogue (TMEM lanes); warps 4-7: producers
-constexpr int kPfStages = 2;
+constexpr int kPfThreads = 288;  // warps 0-3: epilogue (TMEM lanes); 4-7: producers; 8: copies and MMAs
+constexpr int kPfStages = 2;     // operand tiles of the weights and accumulator buffers in TMEM
+constexpr int kPfAStages = 3;    // activation tiles in flight
+constexpr int kPfRaw = 4;        // weight blocks in flight (GGUF bytes)
 constexpr uint32_t kPfTmemCols = 512;  // two accumulator buffers of 256 columns
 
 // rows per CTA tile: every sub-block of a super-block gets its own accumulator
@@ -213,14 +215,14 @@ constexpr uint32_t kPfTmemCols = 512;  // two accumulator buffers of 256 columns
 __host__ __device__ constexpr int pf_rows_per_tile(int sub) { return sub == 32 ? 32 : 16; }
 
 struct PfSmem {  // byte offsets in the dynamic shared memory
-    uint32_t a[kPfStages], b[kPfStages], esc[kPfStages], raw, des, anyd, total;
+    uint32_t a[kPfAStages], b[kPfStages], esc[kPfStages], raw, des, anyd, total;
 };
 __host__ __device__ inline PfSmem pf_smem(int type, int K) {
     const int sub = type == 12 || type == 13 ? 32 : 16, N = pf_rows_per_tile(sub), nsb = 256 / sub;
     const uint32_t bbytes = sub == 32 ? (uint32_t)(8 * N * 32) : (uint32_t)(N * 16 * 18);  // + two zero blocks
     PfSmem s{};
     uint32_t o = 0;
-    for (int i = 0; i < kPfStages; i++) {
+    for (int i = 0; i < kPfAStages; i++) {
         s.a[i] = o;
         o += 32768;
     }
@@ -233,7 +235,7 @@ __host__ __device__ inline PfSmem pf_smem(int type, int K) {
         o += (uint32_t)(nsb * N * 4);
     }
     s.raw = o;
-    o += (uint32_t)(N * 224);  // one super-block per row, GGUF bytes (<= 210)
+    o += (uint32_t)(kPfRaw * N * 224);  // kPfRaw super-blocks per row, GGUF bytes (<= 210) in 224-byte slots
     s.des = o;
     const bool mins = type == 12 || type == 13 || type == 10;
     o += mins ? (uint32_t)(N * (K / sub) * 4) : 0u;
@@ -243,71 +245,53 @@ __host__ __device__ inline PfSmem pf_smem(int type, int K) {
     return s;
 }
 
-// GGUF bytes of super-block b of the tile's N rows, in two halves so the
-// loads of the next block are in flight while this one is unpacked: pf_fetch
-// loads a producer thread's share (items i0, i0 + step, i0 + 2·step: at most
-// three 16-byte plane-A chunks and three plane-S/D bytes, which covers every
-// format at 128 producers) into registers; pf_put stores them in the row's
-// GGUF block in `raw`.
-struct PfFetch {
-    uint4 a[3];
-    uint32_t sd[3];
-};
-__device__ __forceinline__ void pf_fetch(const QMat &M, int r0, int N, int b, int i0, int step, PfFetch &f) {
+// Asynchronous copies of super-block b of the tile's N rows into `raw` (one
+// 224-byte slot per row in the GGUF block layout pf_unpack_quarter reads),
+// spread over the producer threads (items i0, i0 + step, ...): plane A in
+// 16-byte chunks, plane S in one 16-byte or three 4-byte pieces, plane D as
+// the aligned 4-byte word that holds it. A 2-byte d (Q6_K, Q3_K) then sits
+// 2·(row & 1) bytes into its word: the rows of a tile group are its lanes,
+// tile groups have an even number of rows and the plane starts 4-byte
+// aligned. Rows past the matrix get zeros.
+__device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void pf_copy(const QMat &M, int r0, int N, int b, uint8_t *raw, int i0, int step) {
     const int T = M.type, pa = plane_a_bytes(T), ps = plane_s_bytes(T), pd = plane_d_bytes(T), ach = pa / 16;
     const int t = b / M.lpr, bl = b % M.lpr, nb = tile_nb(M.nblk, M.lpr, t), L = M.rpt * nb;
-    const int rows = M.ngroup * M.rpt;  // rows allocated (padded groups); rows past them are skipped
-#pragma unroll
-    for (int k = 0; k < 3; k++) {
-        const int i = i0 + k * step;
-        f.a[k] = make_uint4(0, 0, 0, 0);
-        if (i < N * ach) {
-            const int n = i / ach, c = i - n * ach, r = r0 + n, g = r / M.rpt, sl = r % M.rpt, lane = M.rpt * bl + sl;
-            if (r < rows)
-                f.a[k] = __ldg((const uint4 *)(M.base + tile_offset(M, g, t) + ((size_t)c * L + lane) * 16));
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < 3; k++) {
-        const int i = i0 + k * step;
-        f.sd[k] = 0;
-        if (i < N * (ps + pd)) {
-            const int n = i / (ps + pd), kk = i - n * (ps + pd), r = r0 + n, g = r / M.rpt, sl = r % M.rpt,
-                      lane = M.rpt * bl + sl;
-            if (r < rows) {
-                const uint8_t *tile = M.base + tile_offset(M, g, t);
-                f.sd[k] = kk < ps ? tile[ach * L * 16 + lane * ps + kk] : tile[ach * L * 16 + L * ps + lane * pd + (kk - ps)];
-            }
-        }
-    }
-}
-__device__ __forceinline__ void pf_put(int T, int N, const PfFetch &f, uint8_t *raw, int i0, int step) {
-    const int pa = plane_a_bytes(T), ps = plane_s_bytes(T), pd = plane_d_bytes(T), ach = pa / 16;
+    const int rows = M.ngroup * M.rpt;  // rows allocated (padded groups)
     int lo_a = 0, lo_s = pa, lo_d = pa + ps;
-    if (T == 10) {
+    if (T == 10) {  // Q2_K: scales, qs, d|dmin
         lo_s = 0;
         lo_a = 16;
         lo_d = 80;
     }
-#pragma unroll
-    for (int k = 0; k < 3; k++) {
-        const int i = i0 + k * step;
-        if (i < N * ach) {
-            const int n = i / ach, c = i - n * ach;
-            *(uint4 *)(raw + n * 224 + lo_a + 16 * c) = f.a[k];
+    const int sp = ps == 16 ? 1 : ps / 4, per = ach + sp + (pd ? 1 : 0);
+    for (int i = i0; i < N * per; i += step) {
+        const int n = i / per, k = i - n * per, r = r0 + n;
+        uint8_t *slot = raw + n * 224;
+        if (r >= rows) {
+            if (k < ach) cp_async16_zfill(slot + lo_a + 16 * k, M.base, 0);
+            continue;
         }
-    }
-#pragma unroll
-    for (int k = 0; k < 3; k++) {
-        const int i = i0 + k * step;
-        if (i < N * (ps + pd)) {
-            const int n = i / (ps + pd), kk = i - n * (ps + pd);
-            raw[n * 224 + (kk < ps ? lo_s + kk : lo_d + (kk - ps))] = (uint8_t)f.sd[k];
+        const int g = r / M.rpt, sl = r % M.rpt, lane = M.rpt * bl + sl;
+        const uint8_t *tile = M.base + tile_offset(M, g, t);
+        if (k < ach) {
+            cp_async16(slot + lo_a + 16 * k, tile + ((size_t)k * L + lane) * 16);
+        } else if (k < ach + sp) {
+            const uint8_t *src = tile + (size_t)ach * L * 16 + (size_t)lane * ps;
+            if (ps == 16) cp_async16(slot + lo_s, src);
+            else cp_async4(slot + lo_s + 4 * (k - ach), src + 4 * (k - ach));
+        } else {
+            const size_t off = (size_t)ach * L * 16 + (size_t)L * ps + (size_t)lane * pd;
+            cp_async4(slot + lo_d, tile + (off & ~(size_t)3));
         }
     }
 }
-static_assert(32 * 11 <= 3 * 128 && 16 * 12 <= 3 * 128 && 16 * 20 <= 3 * 128,
-              "a producer's share of a block is at most three chunks and three bytes");
 
 __device__ __forceinline__ float rd_h(const uint8_t *p) { return h2f((uint32_t)p[0] | ((uint32_t)p[1] << 8)); }
 
@@ -317,11 +301,12 @@ __device__ __forceinline__ float rd_h(const uint8_t *p) { return h2f((uint32_t)p
 // scale (e[k]) and offset (o[k], formats with a minimum) of each of the
 // quarter's sub-blocks k. Whole words at a time, as the decode kernel reads
 // the same bytes: a nibble or 2-bit field of four values per mask, the -32
-// (Q6_K) and -4 (Q3_K) bias per byte.
+// (Q6_K) and -4 (Q3_K) bias per byte. `doff`: where the 2-byte d of Q6_K
+// and Q3_K sits past its GGUF offset (pf_copy's aligned word).
 __device__ __forceinline__ uint32_t ld_w(const uint8_t *p) { return *(const uint32_t *)p; }
 
 __device__ __forceinline__ void pf_unpack_quarter(int T, const uint8_t *blk, int q, uint32_t (&w)[16], float (&e)[4],
-                                                  float (&o)[4]) {
+                                                  float (&o)[4], int doff) {
     switch (T) {
     case 12: case 13: {  // Q4_K / Q5_K: sub-blocks 2q (low nibbles) and 2q+1 (high)
         const float d = rd_h(blk), dmin = rd_h(blk + 2);
@@ -351,7 +336,7 @@ __device__ __forceinline__ void pf_unpack_quarter(int T, const uint8_t *blk, int
     case 14: {  // Q6_K: half h = q/2; q%2 = 0: groups primera, segunda; 1: tercera, cuarta
         const int h = q >> 1, odd = q & 1;
         const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h, *sc = blk + 192 + 8 * h;
-        const float d = rd_h(blk + 208);
+        const float d = rd_h(blk + 208 + doff);
 #pragma unroll
         for (int p = 0; p < 4; p++) e[p] = fm(d, (float)(int8_t)sc[4 * odd + p]);
         const int sl = odd ? 4 : 0, sh0 = odd ? 4 : 0, sh1 = odd ? 6 : 2;
@@ -366,7 +351,7 @@ __device__ __forceinline__ void pf_unpack_quarter(int T, const uint8_t *blk, int
     case 11: {  // Q3_K: half m2 = q/2, shifts 2it for it = 2(q%2), 2(q%2)+1
         const int m2 = q >> 1;
         const uint8_t *hm = blk, *qs = blk + 32 + 32 * m2;
-        const float d = rd_h(blk + 108);
+        const float d = rd_h(blk + 108 + doff);
         const uint32_t a0 = ld_w(blk + 96), a1 = ld_w(blk + 100), tt = ld_w(blk + 104);
 #pragma unroll
         for (int ii = 0; ii < 2; ii++) {
@@ -437,7 +422,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     // 128-byte aligned by an offset from the array itself (the operand tiles
     // need 16; the descriptors address 16-byte units)
     unsigned char *sm = pf_smem_raw + ((128u - ((uint32_t)(uintptr_t)pf_smem_raw & 127u)) & 127u);
-    __shared__ __align__(8) uint64_t full_a[kPfStages], full_b[kPfStages], mma_done[kPfStages], tmem_empty[kPfStages];
+    __shared__ __align__(8) uint64_t full_a[kPfAStages], full_b[kPfStages], mma_done[kPfStages], tmem_empty[kPfStages];
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_s;
     const QMat &M = G.seg.M;
@@ -450,9 +435,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     unsigned char *anyd = sm + L.anyd;
 
     if (tid == 0) {
+        for (int i = 0; i < kPfAStages; i++) mbar_init(&full_a[i], 1);
         for (int i = 0; i < kPfStages; i++) {
-            mbar_init(&full_a[i], 1);
-            mbar_init(&full_b[i], kPfThreads / 2);
+            mbar_init(&full_b[i], 128);  // the producer threads
             mbar_init(&mma_done[i], 1);
             mbar_init(&tmem_empty[i], 4);
         }
@@ -484,18 +469,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     const int m = mt * kPfM + tid;  // the epilogue thread's token
     const int groups = min(16, (G.tokens - mt * kPfM + 7) / 8);  // 8-token row groups of this tile
 
-    if (warp >= 4) {
-        // ── producers: unpack the N rows' super-blocks; thread 128 also
-        // copies the activation tiles and issues the MMAs ──
-        const int ptid = tid - 128;
-        int last_issued = -1;
-        bool ok = true;  // the MMA thread's waits so far (the others' stay true)
-        // the activation tile of block bb into its stage: the tile's token rows
-        // in groups of 8 (256 bytes per K-step); a tile of few tokens (a decode
-        // batch) copies only its groups, and the MMA rows past them hold stale
-        // bytes whose sums no epilogue thread stores
+    if (warp == 8) {
+        // ── copies of the activation tiles and the MMAs (one thread) ──
+        // the activation tile of block bb into stage bb % kPfAStages: the
+        // tile's token rows in groups of 8 (256 bytes per K-step); a tile of
+        // few tokens (a decode batch) copies only its groups, and the MMA rows
+        // past them hold stale bytes whose sums no epilogue thread stores
         auto copy_a = [&](int bb) {
-            const int sa = bb & 1;
+            const int sa = bb % kPfAStages;
             const uint8_t *src = (const uint8_t *)(G.a + ((size_t)mt * (M.K / 32) + 8 * bb) * 4096);
             if (groups == 16) {
                 mbar_arrive_expect_tx(&full_a[sa], 32768);
@@ -506,24 +487,70 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                     bulk_g2s(sm + L.a[sa] + k8 * 4096, src + k8 * 4096, (uint32_t)(groups * 256), &full_a[sa]);
             }
         };
-        if (ptid == 0) copy_a(0);
-        PfFetch fw;
-        pf_fetch(M, r0, N, 0, ptid, 128, fw);
+        if (lane == 0) {
+            int last_issued = -1;
+            for (int bb = 0; bb < kPfAStages - 1 && bb < nblk; bb++) copy_a(bb);
+            for (int b = 0; b < nblk; b++) {
+                const int st = b & 1, sa = b % kPfAStages;
+                if (!pf_wait(&full_b[st], (b >> 1) & 1, &abort_s, G.err) ||
+                    !pf_wait(&full_a[sa], (b / kPfAStages) & 1, &abort_s, G.err))
+                    break;
+                tc_fence_after();
+                const uint32_t dcol = tmem + (uint32_t)st * 256;
+                for (int j = 0; j < nsb; j++) {
+                    const int step = sub == 32 ? j : j >> 1;
+                    const uint64_t ad = umma_desc(sm + L.a[sa] + step * 4096, 128, 256);
+                    uint64_t bd;
+                    if (sub == 32) {
+                        bd = umma_desc(sm + L.b[st] + j * N * 32, 128, 256);
+                    } else {
+                        const uint32_t data = L.b[st] + N * 16 + j * N * 16;
+                        if (!(j & 1)) bd = umma_desc(sm + data, (L.b[st] + 17 * N * 16) - data, 128);
+                        else bd = umma_desc(sm + L.b[st], data - L.b[st], 128);
+                    }
+                    umma_i8(dcol + (uint32_t)(j * N), ad, bd, idesc, 0);
+                }
+                umma_commit(&mma_done[st]);
+                last_issued = b;
+                // the activation tile kPfAStages - 1 blocks ahead, into the
+                // stage block b-1's MMAs read: once they are done
+                const int nx = b + kPfAStages - 1;
+                if (nx < nblk) {
+                    if (b >= 1 && !pf_wait(&mma_done[(b - 1) & 1], ((b - 1) >> 1) & 1, &abort_s, G.err)) break;
+                    copy_a(nx);
+                }
+            }
+            // every MMA has completed before the accumulators are released
+            if (last_issued >= 0) pf_wait(&mma_done[last_issued & 1], (last_issued >> 1) & 1, &abort_s, G.err);
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        // ── producers: copy the N rows' super-blocks kPfRaw - 1 blocks ahead
+        // (cp.async), unpack each to the int8 operand tile of its stage ──
+        const int ptid = tid - 128;
+        uint8_t *raw = sm + L.raw;
+        const int slot_bytes = N * 224;
+        for (int bb = 0; bb < kPfRaw - 1; bb++) {  // one commit group per block, empty past the end
+            if (bb < nblk) pf_copy(M, r0, N, bb, raw + (bb % kPfRaw) * slot_bytes, ptid, 128);
+            cp_async_commit();
+        }
         for (int b = 0; b < nblk; b++) {
             const int st = b & 1;
+            const int nx = b + kPfRaw - 1;  // its slot was unpacked at block b-1, before that block's last barrier
+            if (nx < nblk) pf_copy(M, r0, N, nx, raw + (nx % kPfRaw) * slot_bytes, ptid, 128);
+            cp_async_commit();
+            cp_async_wait<kPfRaw - 1>();  // this thread's copies of block b
             bool w = true;
             if (b >= kPfStages) w = pf_wait(&tmem_empty[st], ((b - kPfStages) >> 1) & 1, &abort_s, G.err);
-            if (!producers_all(ok && w && !abort_s)) break;
-            // this block's bytes (loaded during the last block), then the next block's loads
-            pf_put(T, N, fw, sm + L.raw, ptid, 128);
-            if (b + 1 < nblk) pf_fetch(M, r0, N, b + 1, ptid, 128, fw);
-            asm volatile("bar.sync 2, 128;" ::: "memory");
+            // every producer's copies of block b are in; the epilogue is done with stage st
+            if (!producers_all(w && !abort_s)) break;
+            const uint8_t *blkraw = raw + (b % kPfRaw) * slot_bytes;
             float *esc = (float *)(sm + L.esc[st]);  // [sub-block in block][row]
             for (int i = ptid; i < N * 4; i += 128) {
                 const int n = i >> 2, q = i & 3;
                 uint32_t w[16];
                 float e[4], o[4];
-                pf_unpack_quarter(T, sm + L.raw + n * 224, q, w, e, o);
+                pf_unpack_quarter(T, blkraw + n * 224, q, w, e, o, 2 * (n & 1));
                 const int per = 64 / sub, j0 = q * per;  // the quarter's sub-blocks
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
@@ -545,40 +572,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 }
             }
             fence_async_smem();
-            asm volatile("bar.sync 2, 128;" ::: "memory");  // every producer is done with the gathered bytes
+            asm volatile("bar.sync 2, 128;" ::: "memory");  // every producer is done with slot b % kPfRaw
             mbar_arrive(&full_b[st]);
-            if (ptid == 0) {
-                // a failed wait is voted on at the next block (or ends the loop)
-                ok = pf_wait(&full_a[st], (b >> 1) & 1, &abort_s, G.err) &&
-                     pf_wait(&full_b[st], (b >> 1) & 1, &abort_s, G.err);
-                if (!ok) continue;
-                tc_fence_after();
-                const uint32_t dcol = tmem + (uint32_t)st * 256;
-                for (int j = 0; j < nsb; j++) {
-                    const int step = sub == 32 ? j : j >> 1;
-                    const uint64_t ad = umma_desc(sm + L.a[st] + step * 4096, 128, 256);
-                    uint64_t bd;
-                    if (sub == 32) {
-                        bd = umma_desc(sm + L.b[st] + j * N * 32, 128, 256);
-                    } else {
-                        const uint32_t data = L.b[st] + N * 16 + j * N * 16;
-                        if (!(j & 1)) bd = umma_desc(sm + data, (L.b[st] + 17 * N * 16) - data, 128);
-                        else bd = umma_desc(sm + L.b[st], data - L.b[st], 128);
-                    }
-                    umma_i8(dcol + (uint32_t)(j * N), ad, bd, idesc, 0);
-                }
-                umma_commit(&mma_done[st]);
-                last_issued = b;
-                // the next block's activation tile, into the stage block b-1's
-                // MMAs read: once they are done
-                if (b + 1 < nblk) {
-                    if (b >= 1) ok = pf_wait(&mma_done[(b - 1) & 1], ((b - 1) >> 1) & 1, &abort_s, G.err);
-                    if (ok) copy_a(b + 1);
-                }
-            }
         }
-        // every MMA has completed before the accumulators are released
-        if (ptid == 0 && last_issued >= 0) pf_wait(&mma_done[last_issued & 1], (last_issued >> 1) & 1, &abort_s, G.err);
+        cp_async_wait<0>();  // no copy outlives the loop
     } else {
         // ── epilogue: thread = token m (TMEM lane); the buffered path's dot
         // chain, sub-block by sub-block in row order ──

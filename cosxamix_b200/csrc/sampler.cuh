@@ -38,8 +38,8 @@ constexpr int kCandidates = 1024;  // src/sampler.rs:25
 constexpr int kScanPer = 8;        // terms per thread in a window of exact_scan
 constexpr int kScanWin = kScanPer * kSampThreads;
 constexpr int kHistRow = 257;      // radix counts: warp-major rows, padded
-// dynamic shared memory of k_sample: the radix counts, the scan's window
-constexpr int kSampSmem = kSampWarps * kHistRow * 4 + kScanWin * 4;
+// dynamic shared memory of k_sample: the radix counts
+constexpr int kSampSmem = kSampWarps * kHistRow * 4;
 
 struct SampleArgs {
     const float *logits;
@@ -57,7 +57,17 @@ struct SampleArgs {
     float *gred;              // scratch [grid + 1]: each CTA's max, then 1/total
     unsigned *bar;            // grid-barrier counter, zeroed before each launch
     int *err;                 // ERR_TIMEOUT when a grid barrier's wait runs out
+    unsigned long long *stamps;  // measurement only: CTA 0's %globaltimer at its steps' ends [kSampStamps], or NULL
 };
+
+constexpr int kSampStamps = 12;
+__device__ __forceinline__ void samp_stamp(const SampleArgs &a, int k) {
+    if (a.stamps && blockIdx.x == 0 && threadIdx.x == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        a.stamps[k] = t;
+    }
+}
 
 __device__ __forceinline__ unsigned long long azar_next(unsigned long long &st) {
     // src/daiss.rs:317-337
@@ -135,38 +145,36 @@ __device__ bool samp_sync(const SampleArgs &a, unsigned &target, int *ok_s) {
 // before it, and the next window starts after it. Each window therefore adds
 // its terms exactly as the sequential loop does. A sum from zero crosses a
 // few dozen binades at most; ties need the bits of x below u/2 to be zero.
+// kr = round(x/u) for the binade eb (saturated at 2^25: beyond its top),
+// rounded up or not, and whether x is an event by itself (a tie, negative,
+// infinite or NaN)
 struct ScanTerm {
-    uint32_t kf, kr;
-    bool ev;
+    uint32_t kr;
+    bool up, ev;
 };
 
 __device__ __forceinline__ ScanTerm scan_term(float x, int eb) {
     const uint32_t xb = __float_as_uint(x);
-    ScanTerm t{0u, 0u, false};
     const int xe = (int)(xb >> 23);  // sign and exponent
-    if (xe >= 255) {  // negative (sign set), infinite or NaN
-        t.ev = true;
-        return t;
-    }
-    const uint32_t xm = xe ? ((xb & 0x7fffffu) | 0x800000u) : (xb & 0x7fffffu);
+    const uint32_t xm = (xb & 0x7fffffu) | (xe ? 0x800000u : 0u);
     const int sh = eb - (xe > 1 ? xe : 1);  // x/u = xm / 2^sh
-    if (sh < -1) {
-        t.kf = t.kr = 1u << 25;  // x >= 2^25 u: beyond the binade's top
-    } else if (sh == -1) {
-        t.kf = t.kr = xm << 1;
-    } else if (sh == 0) {
-        t.kf = t.kr = xm;
-    } else if (sh <= 25) {
-        const uint32_t rem = xm & ((1u << sh) - 1u), half = 1u << (sh - 1);
-        t.kf = xm >> sh;
-        t.kr = t.kf + (rem > half ? 1u : 0u);
-        t.ev = rem == half;
-    }  // sh > 25: x < u/2, adds nothing and never ties
+    ScanTerm t;
+    if (sh <= 0) {  // x >= u: an integer multiple of u
+        t.kr = sh < -1 ? (1u << 25) : (xm << (-sh));
+        t.up = false;
+        t.ev = xe >= 255;
+    } else {  // sh > 25 leaves kr = 0 and no tie: xm < 2^24 <= half
+        const int s2 = sh < 31 ? sh : 31;
+        const uint32_t kf = xm >> s2, rem = xm - (kf << s2), half = 1u << (s2 - 1);
+        t.up = rem > half;
+        t.kr = kf + (t.up ? 1u : 0u);
+        t.ev = rem == half || xe >= 255;
+    }
     return t;
 }
 
 // M·2^(eb-150) as an f32 (exact: M <= 2^24)
-__device__ __forceinline__ float scan_value(unsigned long long M, int eb) {
+__device__ __forceinline__ float scan_value(uint32_t M, int eb) {
     const float f = (float)M;
     const int e = eb - 150;
     if (e >= -126) return __fmul_rn(f, __int_as_float((e + 127) << 23));
@@ -174,32 +182,57 @@ __device__ __forceinline__ float scan_value(unsigned long long M, int eb) {
 }
 
 struct ScanShared {
-    unsigned long long wtot[kSampWarps];
+    uint32_t wtot[kSampWarps];
     int ev[2];
     float s;
-    int pos;
+    float cand[kSampThreads];  // each thread's first event's sum
 };
 
 enum : int { SCAN_ALL = 0, SCAN_UNTIL_GE = 1, SCAN_UNTIL_GT = 2 };
 
-// One CTA: the running sums of src[0..len) from 0.0f, each written to
-// dst[i] when dst is set. With SCAN_UNTIL_GE / _GT it stops after the window
-// in which the running sum first reaches >= / > `stop` (the later entries of
-// dst are then not written). Returns the number of leading terms summed
-// (uniform); *sum is the sum of those terms. `win` holds kScanWin floats.
-__device__ int exact_scan(const float *src, int len, float *dst, int mode, float stop, float *win, ScanShared &sh,
-                          float *sum) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) {
-        sh.s = 0.0f;
-        sh.pos = 0;
-        sh.ev[0] = sh.ev[1] = INT_MAX;
+// the 8 terms [i0, i0 + 8) of a thread in a window (zeros past len); src is
+// 16-byte aligned and i0 a multiple of 8
+__device__ __forceinline__ void scan_load8(const float *src, int len, int i0, float (&x)[8]) {
+    if (i0 + 8 <= len) {
+        const float4 a = __ldcg((const float4 *)(src + i0)), b = __ldcg((const float4 *)(src + i0 + 4));
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++) x[k] = i0 + k < len ? __ldcg(src + i0 + k) : 0.0f;
     }
+}
+
+constexpr uint32_t kScanCap = 1u << 30;  // saturation of the integer prefix sums (>= 2^24 is all that matters)
+__device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) { return min(a + b, kScanCap); }
+
+// One CTA: the running sums of src[0..len) from 0.0f, each written to
+// dst[i] when dst is set. With SCAN_UNTIL_GE / _GT it stops after the pass
+// in which the running sum first reaches >= / > `stop` (entries of dst past
+// the returned count are unspecified). Returns the number of leading terms
+// summed (uniform); *sum is their sum.
+// Windows are aligned runs of kScanWin terms, thread t holding terms
+// 8t..8t+7 of each in registers, classified once per binade; the next
+// window's loads are in flight while one is summed. A pass covers `span`
+// terms from the running position: after an event it restarts there with a
+// span as long as the terms summed so far (sums from zero double between
+// binade crossings), and it doubles after a pass without one. Every thread
+// writes the sums of its terms up to its own first event; a later pass
+// rewrites those past the CTA's first event.
+__device__ int exact_scan(const float *src, int len, float *dst, int mode, float stop, ScanShared &sh, float *sum) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float x[8], xn[8];
+    uint32_t kr[8], up = 0, evm = 0;
+    int cur = 0, ceb = -1;  // the window held in x; the binade of its classification
+    scan_load8(src, len, 8 * tid, x);
+    scan_load8(src, len, kScanWin + 8 * tid, xn);
+    if (tid == 0) sh.ev[0] = sh.ev[1] = INT_MAX;
+    __syncthreads();
+    float s = 0.0f;
+    int pos = 0, span = kSampThreads;
     for (int it = 0;; it++) {
-        __syncthreads();
-        const int pos = sh.pos;
-        const float s = sh.s;
-        if (pos >= len || (mode == SCAN_UNTIL_GE && s >= stop) || (mode == SCAN_UNTIL_GT && s > stop)) break;
+        if (pos >= len || (pos > 0 && ((mode == SCAN_UNTIL_GE && s >= stop) || (mode == SCAN_UNTIL_GT && s > stop))))
+            break;  // (no term summed yet: the stop is tested after the first)
         if (!(s <= 3.4028235e38f)) {  // infinite or NaN: the rest in order, on one thread
             if (tid == 0) {
                 float r = s;
@@ -208,86 +241,97 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
                     if (dst) dst[i] = r;
                 }
                 sh.s = r;
-                sh.pos = len;
             }
-            continue;
+            __syncthreads();
+            s = sh.s;
+            pos = len;
+            break;
+        }
+        if (pos / kScanWin != cur) {  // the next window (uniform): its terms are loaded
+#pragma unroll
+            for (int k = 0; k < 8; k++) x[k] = xn[k];
+            cur++;
+            ceb = -1;
+            scan_load8(src, len, (cur + 1) * kScanWin + 8 * tid, xn);
         }
         const uint32_t sb = __float_as_uint(s);
         const int eb = (int)(sb >> 23) > 1 ? (int)(sb >> 23) : 1;
-        const unsigned long long M0 = (sb >> 23) ? ((sb & 0x7fffffu) | 0x800000u) : (sb & 0x7fffffu);
-        // the window, coalesced into this warp's 256 floats, then 8 consecutive terms per lane
-        float *wv = win + warp * 256;
-        const int wbase = pos + warp * 256;
+        const uint32_t M0 = (sb & 0x7fffffu) | ((sb >> 23) ? 0x800000u : 0u);
+        if (eb != ceb) {
+            up = evm = 0;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int i = wbase + 32 * j + lane;
-            wv[32 * j + lane] = i < len ? __ldcg(src + i) : 0.0f;
+            for (int k = 0; k < 8; k++) {
+                const ScanTerm t = scan_term(x[k], eb);
+                kr[k] = t.kr;
+                up |= (t.up ? 1u : 0u) << k;
+                evm |= (t.ev ? 1u : 0u) << k;
+            }
+            ceb = eb;
         }
-        __syncwarp();
-        const float4 v0 = ((const float4 *)wv)[2 * lane], v1 = ((const float4 *)wv)[2 * lane + 1];
-        const float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        const int base = wbase + 8 * lane;
-        ScanTerm t[8];
-        unsigned long long loc = 0;
+        const int wbase = cur * kScanWin, base = wbase + 8 * tid;
+        const int end = min(min(len, wbase + kScanWin), pos + span);  // this pass: terms [pos, end)
+        uint32_t act = 0, loc = 0;  // active terms of this thread, their sum (< 2^28)
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
-            t[k] = scan_term(x[k], eb);
-            loc += t[k].kr;
-        }
-        // exclusive prefix of loc over the CTA (64-bit)
-        unsigned long long inc = loc;
+        for (int k = 0; k < 8; k++)
+            if (base + k >= pos && base + k < end) {
+                act |= 1u << k;
+                loc += kr[k];
+            }
+        // exclusive prefix of loc over the CTA, saturating
+        uint32_t inc = loc;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += v;
+            const uint32_t v = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc = sat_add(inc, v);
         }
         if (lane == 31) sh.wtot[warp] = inc;
         __syncthreads();
-        unsigned long long wt = sh.wtot[lane], wi = wt;
+        uint32_t wi = sh.wtot[lane];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const unsigned long long v = __shfl_up_sync(0xffffffffu, wi, o);
-            if (lane >= o) wi += v;
+            const uint32_t v = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi = sat_add(wi, v);
         }
-        const unsigned long long wex = __shfl_sync(0xffffffffu, wi - wt, warp);
-        const unsigned long long ex = M0 + wex + inc - loc;
-        // this lane's first event
-        {
-            unsigned long long P = ex;
-            int e = -1;
+        const uint32_t total = __shfl_sync(0xffffffffu, wi, 31);
+        const uint32_t wex = warp ? __shfl_sync(0xffffffffu, wi, warp - 1) : 0u;
+        const uint32_t tex = __shfl_up_sync(0xffffffffu, inc, 1);
+        uint32_t P = sat_add(M0, sat_add(wex, lane ? tex : 0u));
+        // the sums of this thread's terms, up to its first event
+        if (act) {
+            bool done = false;
 #pragma unroll
             for (int k = 0; k < 8; k++) {
-                if (e < 0 && base + k < len && (t[k].ev || P + t[k].kf >= (1ull << 24))) e = k;
-                P += t[k].kr;
+                if (done || !((act >> k) & 1)) continue;
+                const uint32_t kf = kr[k] - ((up >> k) & 1);
+                float r;
+                if (((evm >> k) & 1) || P + kf >= (1u << 24)) {  // an f32 addition to the exact sum before it
+                    r = __fadd_rn(scan_value(P, eb), x[k]);
+                    sh.cand[tid] = r;
+                    atomicMin(&sh.ev[it & 1], base + k);
+                    done = true;
+                } else {
+                    P += kr[k];
+                    r = scan_value(P, eb);
+                }
+                if (dst) dst[base + k] = r;
             }
-            if (e >= 0) atomicMin(&sh.ev[it & 1], base + e);
         }
         __syncthreads();
         const int E = sh.ev[it & 1];
         if (tid == 0) sh.ev[(it + 1) & 1] = INT_MAX;
-        unsigned long long P = ex;
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const int i = base + k;
-            if (i == E) {  // the event: an f32 addition to the exact sum before it
-                const float r = __fadd_rn(scan_value(P, eb), x[k]);
-                if (dst) dst[i] = r;
-                sh.s = r;
-                sh.pos = i + 1;
-            }
-            if (i >= E || i >= len) break;
-            P += t[k].kr;
-            if (dst) dst[i] = scan_value(P, eb);
-        }
-        if (E == INT_MAX && tid == kSampThreads - 1) {
-            sh.s = scan_value(ex + loc, eb);
-            sh.pos = min(len, pos + kScanWin);
+        if (E != INT_MAX) {
+            s = sh.cand[(E - wbase) >> 3];
+            pos = E + 1;
+            span = min(kScanWin, max(kSampThreads, pos));
+        } else {
+            s = scan_value(M0 + total, eb);
+            pos = end;
+            span = min(kScanWin, 2 * span);
         }
     }
-    const int r = sh.pos;
-    if (sum) *sum = sh.s;
+    if (sum) *sum = s;
     __syncthreads();
-    return r;
+    return pos;
 }
 
 // first i in [0, len) with p[i] > t (gt) or >= t, over values that never
@@ -451,7 +495,6 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
     if (a.d_stop && *(volatile const int *)a.d_stop) return;  // the generation already met its eos (uniform)
     extern __shared__ __align__(16) unsigned char samp_smem[];
     uint32_t *hist = (uint32_t *)samp_smem;                          // [kSampWarps][kHistRow]
-    float *win = (float *)(samp_smem + kSampWarps * kHistRow * 4);  // [kScanWin]
     __shared__ float red[kSampWarps];
     __shared__ ScanShared sh;
     __shared__ float u_s, sum_s;
@@ -460,6 +503,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
     const int tile = (n + G - 1) / G, lo = min(n, cta * tile), hi = min(n, lo + tile);
     const float inv_t = a.params[0], top_p = a.params[1];
     unsigned target = 0;
+    samp_stamp(a, 0);
     if (cta == 0 && tid == 0) {
         unsigned long long st = *a.rng;
         u_s = (float)(azar_next(st) >> 40) / 16777216.0f;
@@ -475,6 +519,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
     m = block_max(m, red);
     if (tid == 0) a.gred[cta] = m;
     if (!samp_sync(a, target, &ok_s)) return;
+    samp_stamp(a, 1);
     float gm = -INFINITY;
     for (int c = tid; c < G; c += kSampThreads) gm = fmaxf(gm, __ldcg(a.gred + c));
     gm = block_max(gm, red);
@@ -484,11 +529,13 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
     } else {
         for (int i = lo + tid; i < hi; i += kSampThreads) a.probs[i] = expf_glibc(__fsub_rn(a.probs[i], gm));
         if (!samp_sync(a, target, &ok_s)) return;
+        samp_stamp(a, 2);
         if (cta == 0) {  // the total, in index order
-            exact_scan(a.probs, n, nullptr, SCAN_ALL, 0.0f, win, sh, &sum_s);
+            exact_scan(a.probs, n, nullptr, SCAN_ALL, 0.0f, sh, &sum_s);
             if (tid == 0) a.gred[G] = __fdiv_rn(1.0f, sum_s);
         }
         if (!samp_sync(a, target, &ok_s)) return;
+        samp_stamp(a, 3);
         const float inv = __ldcg(a.gred + G);
         for (int i = lo + tid; i < hi; i += kSampThreads) a.probs[i] = __fmul_rn(a.probs[i], inv);
     }
@@ -497,7 +544,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
         // the whole vocabulary in index order (src/sampler.rs:84-86)
         if (!samp_sync(a, target, &ok_s) || cta != 0) return;
         const float u = u_s;
-        const int len = exact_scan(a.probs, n, a.prefix, SCAN_UNTIL_GT, u, win, sh, nullptr);
+        const int len = exact_scan(a.probs, n, a.prefix, SCAN_UNTIL_GT, u, sh, nullptr);
         const int i = block_first(a.prefix, len, u, true);
         tok = (uint32_t)(i < len ? i : n - 1);
     } else {
@@ -508,28 +555,35 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
             a.val0[i] = (uint32_t)i;
         }
         __syncthreads();
-        if (!radix_pass(a, a.key0, a.val0, a.key1, a.val1, lo, hi, 0, hist, target, &ok_s) ||
-            !radix_pass(a, a.key1, a.val1, a.key0, a.val0, lo, hi, 8, hist, target, &ok_s) ||
-            !radix_pass(a, a.key0, a.val0, a.key1, a.val1, lo, hi, 16, hist, target, &ok_s) ||
-            !radix_pass(a, a.key1, a.val1, a.key0, a.val0, lo, hi, 24, hist, target, &ok_s))
-            return;
+        samp_stamp(a, 4);
+        if (!radix_pass(a, a.key0, a.val0, a.key1, a.val1, lo, hi, 0, hist, target, &ok_s)) return;
+        samp_stamp(a, 5);
+        if (!radix_pass(a, a.key1, a.val1, a.key0, a.val0, lo, hi, 8, hist, target, &ok_s)) return;
+        samp_stamp(a, 6);
+        if (!radix_pass(a, a.key0, a.val0, a.key1, a.val1, lo, hi, 16, hist, target, &ok_s)) return;
+        samp_stamp(a, 7);
+        if (!radix_pass(a, a.key1, a.val1, a.key0, a.val0, lo, hi, 24, hist, target, &ok_s)) return;
+        samp_stamp(a, 8);
         const uint32_t *order = a.val0;
         float *sorted = (float *)a.key1;  // probabilities in sorted order
         for (int i = lo + tid; i < hi; i += kSampThreads) sorted[i] = __ldcg(a.probs + __ldcg(order + i));
         if (!samp_sync(a, target, &ok_s) || cta != 0) return;
+        samp_stamp(a, 9);
         const float u = u_s;
         // The cumulative sums of the sorted probabilities. The candidates'
         // mass is the one at k - 1; below top_p (with k < n) the whole order
         // is the nucleus, else the candidates, whose first sum >= top_p then
         // comes before k: either way the cut is after the first sum >= top_p,
         // or at n (src/sampler.rs:96-117).
-        const int len = exact_scan(sorted, n, a.prefix, SCAN_UNTIL_GE, top_p, win, sh, nullptr);
+        const int len = exact_scan(sorted, n, a.prefix, SCAN_UNTIL_GE, top_p, sh, nullptr);
+        samp_stamp(a, 10);
         const int first = block_first(a.prefix, len, top_p, false);
         const int cut = first < len ? first + 1 : n;
         const float total = __ldcg(a.prefix + cut - 1);
         const int i = block_first(a.prefix, cut, __fmul_rn(u, total), true);
         tok = __ldcg(order + (i < cut ? i : cut - 1));
     }
+    samp_stamp(a, 11);
     if (tid == 0) {
         if (a.toks) a.toks[*a.d_len] = tok;
         if (a.out) *a.out = tok;

@@ -10,7 +10,12 @@ layers so every phase streams its own weights (36 layers x 25 MB > L2).
 Prints the per-phase time and the algorithmic weight bytes per second.
 With --decode: prefills a seeded P-token prompt (one decode-kernel launch
 per token), then times STEPS greedy decode steps (one launch each), or with
---sample STEPS sampled steps (the decode kernel, then k_sample).
+--sample STEPS sampled steps (the decode kernel, then k_sample). With
+--sampler RUNS: the device sampler alone, RUNS times on the prompt's
+logits (T 0.7, top-p 0.9), with CTA 0's step ends of the last run. With
+--prefill P: the forward of a seeded P-token prompt into an empty cache
+(wall clock around the call, which returns once the logits are on the host;
+best of 3 after a warm-up).
 `--layers` / `--vocab` shrink the synthetic model (same matrix shapes) so an
 ncu capture holds little device memory; keep layers x 25 MB above the 126 MB
 L2 for DRAM figures to mean something.
@@ -38,6 +43,8 @@ def main() -> None:
     ap.add_argument("--decode", type=int, default=0)
     ap.add_argument("--prompt", type=int, default=16)
     ap.add_argument("--sample", action="store_true", help="--decode with the device top-p sampler (T 0.7, top-p 0.9)")
+    ap.add_argument("--prefill", type=int, default=0, help="time the forward of a seeded prompt of this many tokens")
+    ap.add_argument("--sampler", type=int, default=0, help="time RUNS of the device sampler alone on the prompt's logits")
     args = ap.parse_args()
     import bench
     import cosxamix_b200 as cx
@@ -57,6 +64,29 @@ def main() -> None:
     else:
         path = bench.ensure_model(args.config, args.seed)
     m = cx.Modelo(path)
+    if args.prefill:
+        prompt = bench.seeded_prompt(args.seed, args.prefill, m.cfg.vocab)
+        c = m.cache(min(m.cfg.ctx, args.prefill + 8))
+        m.forward(prompt, c)  # warm-up: programs, graphs, workspaces
+        times = []
+        for _ in range(3):
+            c.limpiar()
+            t = time.perf_counter()
+            m.forward(prompt, c)  # returns the last token's logits: the device work is done
+            times.append((time.perf_counter() - t) * 1000)
+        print(json.dumps({"kernel": "prompt forward (tensor-core GEMMs)", "config": args.config,
+                          "layers": args.layers or None, "tokens": args.prefill,
+                          "ms": round(min(times), 2), "ms_all": [round(x, 2) for x in times]}))
+        return
+    if args.sampler:
+        c = m.cache(min(m.cfg.ctx, args.prompt + 8))
+        m.forward(bench.seeded_prompt(args.seed, args.prompt, m.cfg.vocab), c)
+        ms, ph = m.bench_sample(cx.Muestreador(42, 0.7, 0.9), args.sampler)
+        names = ["max", "exps", "total", "keys", "radix0", "radix8", "radix16", "radix24", "gather", "cumsum", "end"]
+        print(json.dumps({"kernel": "k_sample", "config": args.config, "layers": args.layers or None,
+                          "vocab": m.cfg.vocab, "us_per_run": round(ms * 1000 / args.sampler, 2),
+                          "step_end_us": {n: round(v / 1000, 2) for n, v in zip(names, ph[1:])}}))
+        return
     if args.decode:
         c = m.cache(min(m.cfg.ctx, args.prompt + args.decode + 8))
         m.forward(bench.seeded_prompt(args.seed, args.prompt, m.cfg.vocab), c)
