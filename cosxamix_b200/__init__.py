@@ -353,9 +353,10 @@ class Modelo:
 
     def bench_sample(self, sampler: "Muestreador", reps: int):
         """Device time (ms) of `reps` runs of the device sampler on the logits
-        of the last step, and the last run's step ends (ns from its start)."""
+        of the last step, the last run's step ends (ns from its start), then
+        the passes of its two sums."""
         ms = C.c_float(0)
-        ph = np.zeros(12, np.uint64)
+        ph = np.zeros(14, np.uint64)
         _check(lib().cxm_bench_sample(self.h, sampler.h, reps, C.byref(ms), _ptr(ph), ph.size))
         return ms.value, ph.tolist()
 

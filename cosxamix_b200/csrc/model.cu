@@ -496,9 +496,11 @@ int launch_pdl(void (*kernel)(Args...), dim3 grid, dim3 block, size_t smem, cuda
     return 0;
 }
 
-size_t scores_smem(int hd) { return ((size_t)kScoreThreads * kKRow + (size_t)hd) * sizeof(float); }
+size_t scores_smem(int hd, int group) {
+    return ((size_t)kScoreThreads * kKRow + (size_t)group * hd) * sizeof(float);
+}
 size_t out_smem(uint32_t max_pos) {
-    return ((size_t)((max_pos + 3) & ~3u) + kVRing * kVChunk * kOutDims) * sizeof(float);
+    return (size_t)((max_pos + 3) & ~3u) * sizeof(float);
 }
 
 int g_decode_smem_max = 0;  // dynamic shared memory the decode kernel may use
@@ -524,9 +526,9 @@ int set_kernel_smem_limits() {
 // src/ops.rs:1258-1325 for the token at *d_len (or tokens pos0.. pos0+tokens-1),
 // over positions 0..=that one
 int launch_attention_on(cudaStream_t st, AttnParams &a, int tokens = 1) {
-    const dim3 gs(a.H, (a.max_pos + kScoreThreads - 1) / kScoreThreads, tokens);
-    const dim3 go(a.H, (a.hd + kOutDims - 1) / kOutDims, tokens);
-    if (launch_pdl(k_attn_scores, gs, dim3(kScoreThreads), scores_smem(a.hd), st, a)) return -1;
+    const dim3 gs(a.KV, (a.max_pos + kScoreThreads - 1) / kScoreThreads, tokens);
+    const dim3 go(a.H, 1, tokens);
+    if (launch_pdl(k_attn_scores, gs, dim3(kScoreThreads), scores_smem(a.hd, a.H / a.KV), st, a)) return -1;
     return launch_pdl(k_attn_out, go, dim3(kOutThreads), out_smem((uint32_t)a.max_pos), st, a);
 }
 
@@ -2581,7 +2583,7 @@ extern "C" int cxm_bench_sample(cxm_model *m, cxm_sampler *s, uint32_t reps, flo
     if (phase_ns) {
         unsigned long long h[kSampStamps];
         CU(cudaMemcpy(h, st.p, sizeof(h), cudaMemcpyDeviceToHost));
-        for (uint32_t k = 0; k < nphase; k++) phase_ns[k] = h[k] ? h[k] - h[0] : 0;
+        for (uint32_t k = 0; k < nphase; k++) phase_ns[k] = k >= 12 ? h[k] : h[k] ? h[k] - h[0] : 0;
     }
     for (uint32_t i = 0; i < reps; i++) {  // one draw per run
         uint64_t x = s->state;

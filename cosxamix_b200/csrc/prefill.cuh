@@ -17,11 +17,12 @@
 //   k_pf_rows   RMSNorm (optional) + i8 quantization of each token's row, into
 //               the MMA's K-major operand tiles and per-sub-block scale/sum
 //   k_pf_gemm   one 128-token x N-row tile of out = W·x over the whole row
-//               (warp-specialized: 4 epilogue warps own the TMEM lanes = tokens,
-//               4 producer warps unpack the k-quant blocks to int8 operand
-//               tiles, one thread copies the activation tiles and issues the
-//               MMAs), then the segment's epilogue (bias, RoPE + K/V append,
-//               residual, SwiGLU)
+//               (warp-specialized: 8 epilogue warps own the TMEM lanes =
+//               tokens, two per lane quarter, each for half of the rows;
+//               4 producer warps copy the k-quant blocks a few ahead and
+//               unpack them to int8 operand tiles; one thread copies the
+//               activation tiles and issues the MMAs), then the segment's
+//               epilogue (bias, RoPE + K/V append, residual, SwiGLU)
 // Attention over the new tokens uses the standalone attention kernels with a
 // token dimension (step_kernels.cuh).
 #pragma once
@@ -69,6 +70,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
+}
+// 8 consecutive 32-bit columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -204,7 +211,7 @@ struct PfGemm {
     int fused;
 };
 
-constexpr int kPfThreads = 288;  // warps 0-3: epilogue (TMEM lanes); 4-7: producers; 8: copies and MMAs
+constexpr int kPfThreads = 416;  // warps 0-7: epilogue (TMEM lanes, two halves of the rows); 8-11: producers; 12: copies and MMAs
 constexpr int kPfStages = 2;     // operand tiles of the weights and accumulator buffers in TMEM
 constexpr int kPfAStages = 3;    // activation tiles in flight
 constexpr int kPfRaw = 4;        // weight blocks in flight (GGUF bytes)
@@ -439,7 +446,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         for (int i = 0; i < kPfStages; i++) {
             mbar_init(&full_b[i], 128);  // the producer threads
             mbar_init(&mma_done[i], 1);
-            mbar_init(&tmem_empty[i], 4);
+            mbar_init(&tmem_empty[i], 8);  // the epilogue warps
         }
         abort_s = 0;
         mbar_fence_init();
@@ -463,13 +470,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     const uint32_t tmem = tmem_base_s;
     const uint32_t idesc = umma_idesc_i8(kPfM, N);
 
-    float acc[32];
+    float acc[16];
 #pragma unroll
     for (int i = 0; i < 32; i++) acc[i] = 0.0f;
-    const int m = mt * kPfM + tid;  // the epilogue thread's token
+    const int m = mt * kPfM + (tid & 127);  // the epilogue thread's token (its TMEM lane)
+    const int HN = N / 2, c0 = (warp >> 2) * HN;  // an epilogue warp's half of the tile's rows
     const int groups = min(16, (G.tokens - mt * kPfM + 7) / 8);  // 8-token row groups of this tile
 
-    if (warp == 8) {
+    if (warp == 12) {
         // ── copies of the activation tiles and the MMAs (one thread) ──
         // the activation tile of block bb into stage bb % kPfAStages: the
         // tile's token rows in groups of 8 (256 bytes per K-step); a tile of
@@ -524,10 +532,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
             if (last_issued >= 0) pf_wait(&mma_done[last_issued & 1], (last_issued >> 1) & 1, &abort_s, G.err);
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    } else if (warp >= 8) {
         // ── producers: copy the N rows' super-blocks kPfRaw - 1 blocks ahead
         // (cp.async), unpack each to the int8 operand tile of its stage ──
-        const int ptid = tid - 128;
+        const int ptid = tid - 256;
         uint8_t *raw = sm + L.raw;
         const int slot_bytes = N * 224;
         for (int bb = 0; bb < kPfRaw - 1; bb++) {  // one commit group per block, empty past the end
@@ -577,45 +585,40 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         }
         cp_async_wait<0>();  // no copy outlives the loop
     } else {
-        // ── epilogue: thread = token m (TMEM lane); the buffered path's dot
-        // chain, sub-block by sub-block in row order ──
+        // ── epilogue: thread = token m (TMEM lane), rows c0..c0+HN-1; the
+        // buffered path's dot chain, sub-block by sub-block in row order ──
         const float *xe = G.xe + (size_t)(m < G.tokens ? m : 0) * G.nsub;
         const float *xs = G.xs + (size_t)(m < G.tokens ? m : 0) * G.nsub;
         const bool fused = G.fused && mins;
+        const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
         for (int b = 0; b < nblk; b++) {
             const int st = b & 1;
             // warp-uniform: the TMEM loads below are collective over the warp
             if (!__all_sync(0xffffffffu, pf_wait(&mma_done[st], (b >> 1) & 1, &abort_s, G.err) && !abort_s)) break;
             tc_fence_after();
-            const float *esc = (const float *)(sm + L.esc[st]);
+            const float *esc = (const float *)(sm + L.esc[st]) + c0;
             for (int j = 0; j < nsb; j++) {
                 const float e = xe[b * nsb + j];
-                const uint32_t col = tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(st * 256 + j * N);
-                uint32_t s0[16], s1[16];
-                tmem_ld16(col, s0);
-                if (N == 32) tmem_ld16(col + 16, s1);
+                const uint32_t col = tmem + lanes + (uint32_t)(st * 256 + j * N + c0);
+                uint32_t s0[16];
+                if (HN == 16) tmem_ld16(col, s0);
+                else tmem_ld8(col, s0);
                 tmem_ld_wait();
                 if (fused) {
                     // xe·((d·sc)·Σ − (dmin·m)·xs), the offset's product being −des
                     const float x = xs[b * nsb + j];
-                    const float *dj = des_all + b * nsb + j;
+                    const float *dj = des_all + (size_t)c0 * G.nsub + b * nsb + j;
 #pragma unroll
-                    for (int n = 0; n < 16; n++)
+                    for (int n = 0; n < 16; n++) {
+                        if (n >= HN) break;
                         acc[n] = fa(acc[n], fm(e, fs(fm(esc[j * N + n], (float)(int)s0[n]), fm(-dj[(size_t)n * G.nsub], x))));
-                    if (N == 32) {
-#pragma unroll
-                        for (int n = 0; n < 16; n++)
-                            acc[16 + n] = fa(acc[16 + n], fm(e, fs(fm(esc[j * N + 16 + n], (float)(int)s1[n]),
-                                                                   fm(-dj[(size_t)(16 + n) * G.nsub], x))));
                     }
                     continue;
                 }
 #pragma unroll
-                for (int n = 0; n < 16; n++) acc[n] = fa(acc[n], fm(fm(esc[j * N + n], e), (float)(int)s0[n]));
-                if (N == 32) {
-#pragma unroll
-                    for (int n = 0; n < 16; n++)
-                        acc[16 + n] = fa(acc[16 + n], fm(fm(esc[j * N + 16 + n], e), (float)(int)s1[n]));
+                for (int n = 0; n < 16; n++) {
+                    if (n >= HN) break;
+                    acc[n] = fa(acc[n], fm(fm(esc[j * N + n], e), (float)(int)s0[n]));
                 }
             }
             tc_fence_before();
@@ -624,24 +627,24 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         }
     }
     __syncthreads();
-    if (warp < 4 && !abort_s && m < G.tokens) {
+    if (warp < 8 && !abort_s && m < G.tokens) {
         // the offset chain, after the whole row (src/ops.rs:395-401): each
         // row with a nonzero offset adds its terms in sub-block order; the
         // rows' chains advance side by side (sub-block outer), so the token's
-        // xe/xs are read once per sub-block and the 32 chains overlap
+        // xe/xs are read once per sub-block and the rows' chains overlap
         if (mins && !G.fused) {
             const float *xe = G.xe + (size_t)m * G.nsub, *xs = G.xs + (size_t)m * G.nsub;
             uint32_t live = 0;  // rows with a nonzero offset
 #pragma unroll
-            for (int n = 0; n < 32; n++)
-                if (n < N && anyd[n]) live |= 1u << n;
+            for (int n = 0; n < 16; n++)
+                if (n < HN && anyd[c0 + n]) live |= 1u << n;
             if (live) {
                 for (int s = 0; s < G.nsub; s++) {
                     const float e = __ldg(xe + s), x = __ldg(xs + s);
 #pragma unroll
-                    for (int n = 0; n < 32; n++) {
-                        if (n >= N) break;
-                        const float t = fm(fm(des_all[(size_t)n * G.nsub + s], e), x);
+                    for (int n = 0; n < 16; n++) {
+                        if (n >= HN) break;
+                        const float t = fm(fm(des_all[(size_t)(c0 + n) * G.nsub + s], e), x);
                         acc[n] = (live >> n) & 1u ? fa(acc[n], t) : acc[n];
                     }
                 }
@@ -652,9 +655,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         const int pos = G.row_pos ? G.row_pos[m] : G.pos0 + m;
         float *cache_base = G.row_out ? G.row_out[m] : g.out;
 #pragma unroll
-        for (int n = 0; n < 32; n += 2) {  // constant indices: acc stays in registers
-            const int u = (r0 + n) >> 1;
-            if (n >= N || u >= g.units) break;
+        for (int n = 0; n < 16; n += 2) {  // constant indices: acc stays in registers
+            const int u = (r0 + c0 + n) >> 1;
+            if (n >= HN || u >= g.units) break;
             int ra, rb;
             unit_rows(g, u, ra, rb);
             const float y0 = acc[n], y1 = acc[n + 1];

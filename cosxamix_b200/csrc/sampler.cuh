@@ -60,7 +60,7 @@ struct SampleArgs {
     unsigned long long *stamps;  // measurement only: CTA 0's %globaltimer at its steps' ends [kSampStamps], or NULL
 };
 
-constexpr int kSampStamps = 12;
+constexpr int kSampStamps = 14;  // 12 step ends, then the two sums' pass counts
 __device__ __forceinline__ void samp_stamp(const SampleArgs &a, int k) {
     if (a.stamps && blockIdx.x == 0 && threadIdx.x == 0) {
         unsigned long long t;
@@ -186,6 +186,7 @@ struct ScanShared {
     int ev[2];
     float s;
     float cand[kSampThreads];  // each thread's first event's sum
+    int passes;                // passes of the last exact_scan (measurement)
 };
 
 enum : int { SCAN_ALL = 0, SCAN_UNTIL_GE = 1, SCAN_UNTIL_GT = 2 };
@@ -229,8 +230,8 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
     if (tid == 0) sh.ev[0] = sh.ev[1] = INT_MAX;
     __syncthreads();
     float s = 0.0f;
-    int pos = 0, span = kSampThreads;
-    for (int it = 0;; it++) {
+    int pos = 0, span = kSampThreads, it = 0;
+    for (;; it++) {
         if (pos >= len || (pos > 0 && ((mode == SCAN_UNTIL_GE && s >= stop) || (mode == SCAN_UNTIL_GT && s > stop))))
             break;  // (no term summed yet: the stop is tested after the first)
         if (!(s <= 3.4028235e38f)) {  // infinite or NaN: the rest in order, on one thread
@@ -330,6 +331,7 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
         }
     }
     if (sum) *sum = s;
+    if (tid == 0) sh.passes = it;
     __syncthreads();
     return pos;
 }
@@ -532,6 +534,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
         samp_stamp(a, 2);
         if (cta == 0) {  // the total, in index order
             exact_scan(a.probs, n, nullptr, SCAN_ALL, 0.0f, sh, &sum_s);
+            if (a.stamps && tid == 0) a.stamps[12] = (unsigned long long)sh.passes;
             if (tid == 0) a.gred[G] = __fdiv_rn(1.0f, sum_s);
         }
         if (!samp_sync(a, target, &ok_s)) return;
@@ -577,6 +580,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
         // or at n (src/sampler.rs:96-117).
         const int len = exact_scan(sorted, n, a.prefix, SCAN_UNTIL_GE, top_p, sh, nullptr);
         samp_stamp(a, 10);
+        if (a.stamps && tid == 0) a.stamps[13] = (unsigned long long)sh.passes;
         const int first = block_first(a.prefix, len, top_p, false);
         const int cut = first < len ? first + 1 : n;
         const float total = __ldcg(a.prefix + cut - 1);

@@ -104,29 +104,33 @@ __device__ __forceinline__ const float *kv_row(const float *own, const float *pr
 
 constexpr int kScoreThreads = 128;   // positions per score CTA
 constexpr int kKRow = 132;           // smem row stride (floats) of staged K rows
-constexpr int kOutThreads = 128;
-constexpr int kOutDims = 16;         // head dims per output CTA
-constexpr int kVChunk = 64;          // positions per staged V chunk
-constexpr int kVRing = 8;            // V chunks in flight
+constexpr int kOutThreads = 128;     // one thread per head dim (head_dim <= 128)
 
+// One CTA per (token, KV head, 128 positions): the K rows of the positions
+// are staged once for all the query heads of the group; thread = position,
+// each score q_h·k a sequential sum over the dims (src/ops.rs), up to eight
+// heads' chains side by side.
 __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_constant__ AttnParams p) {
-    extern __shared__ __align__(16) float ks[];  // [kScoreThreads][kKRow] then q [hd]
+    extern __shared__ __align__(16) float ks[];  // [kScoreThreads][kKRow] then q [G][hd]
     griddep_launch_dependents();
     griddep_wait();
-    const int h = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, z = blockIdx.z;
+    const int g = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, z = blockIdx.z;
     const AttnView w = attn_view(p);
     const int n = w.n;
     if (n > p.max_pos || n <= 0) {
-        if (tid == 0 && h == 0 && split == 0) atomicOr(p.err, ERR_POSITION);
+        if (tid == 0 && g == 0 && split == 0) atomicOr(p.err, ERR_POSITION);
         return;
     }
     const int p0 = split * kScoreThreads;
     if (p0 >= n) return;
     const int cnt = min(kScoreThreads, n - p0);
-    const int hd = p.hd, G = p.H / p.KV, g = h / G, kvd = p.KV * hd, c4 = hd / 4;
+    const int hd = p.hd, G = p.H / p.KV, kvd = p.KV * hd, c4 = hd / 4;
     float *qs = ks + kScoreThreads * kKRow;
-    // stage q and the K rows of these positions: all 16-byte copies in flight
-    for (int i = tid; i < c4; i += kScoreThreads) cp_async16(qs + 4 * i, p.q + (size_t)z * p.qs + (size_t)h * hd + 4 * i);
+    // stage the group's q rows and the K rows of these positions: all 16-byte copies in flight
+    for (int i = tid; i < G * c4; i += kScoreThreads) {
+        const int hq = i / c4, c = i - hq * c4;
+        cp_async16(qs + hq * hd + 4 * c, p.q + (size_t)z * p.qs + (size_t)(g * G + hq) * hd + 4 * c);
+    }
     for (int i = tid; i < cnt * c4; i += kScoreThreads) {
         const int r = i / c4, c = i - r * c4;
         cp_async16(ks + r * kKRow + 4 * c, kv_row(w.k, w.kp, w.plen, p0 + r, kvd, (size_t)g * hd + 4 * c));
@@ -134,58 +138,52 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    if (tid < cnt) {
-        const float4 *kr = (const float4 *)(ks + tid * kKRow);
-        const float4 *q4 = (const float4 *)qs;
-        float acc = 0.0f;
+    if (tid >= cnt) return;
+    const float4 *kr = (const float4 *)(ks + tid * kKRow);
+    for (int h0 = 0; h0 < G; h0 += 8) {
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[j] = 0.0f;
         for (int c = 0; c < c4; c++) {
-            const float4 kv = kr[c], qv = q4[c];
-            acc = fa(acc, fm(qv.x, kv.x));
-            acc = fa(acc, fm(qv.y, kv.y));
-            acc = fa(acc, fm(qv.z, kv.z));
-            acc = fa(acc, fm(qv.w, kv.w));
+            const float4 kv = kr[c];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                if (h0 + j >= G) break;
+                const float4 qv = ((const float4 *)(qs + (h0 + j) * hd))[c];
+                acc[j] = fa(acc[j], fm(qv.x, kv.x));
+                acc[j] = fa(acc[j], fm(qv.y, kv.y));
+                acc[j] = fa(acc[j], fm(qv.z, kv.z));
+                acc[j] = fa(acc[j], fm(qv.w, kv.w));
+            }
         }
-        p.scores[((size_t)z * p.H + h) * p.score_stride + p0 + tid] = fm(acc, p.scale);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (h0 + j >= G) break;
+            p.scores[((size_t)z * p.H + g * G + h0 + j) * p.score_stride + p0 + tid] = fm(acc[j], p.scale);
+        }
     }
 }
 
+// One CTA per (token, head): the softmax of the head's scores once, then
+// thread d adds prob_p·v_p[d] over the positions in order (one sequential
+// chain per dim, as the reference's loop). The V values come straight from
+// L2, a warp reading 32 consecutive dims of a position (128 bytes), eight
+// positions' loads in flight ahead of their additions.
 __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant__ AttnParams p) {
-    // smem: probs [max_pos rounded to 4] then a ring of kVRing V chunks [kVChunk][kOutDims]
-    extern __shared__ __align__(16) float so[];
+    extern __shared__ __align__(16) float pr[];  // the probabilities [max_pos rounded to 4]
     __shared__ float red[kOutThreads / 32];
     __shared__ float bcast;
     griddep_launch_dependents();
     griddep_wait();
-    const int h = blockIdx.x, dslice = blockIdx.y, tid = threadIdx.x, z = blockIdx.z;
+    const int h = blockIdx.x, tid = threadIdx.x, z = blockIdx.z;
     const AttnView w = attn_view(p);
     const int n = w.n;
     if (n > p.max_pos || n <= 0) return;  // k_attn_scores reported it
     const int hd = p.hd, G = p.H / p.KV, g = h / G, kvd = p.KV * hd;
-    const int d0 = dslice * kOutDims;
-    if (d0 >= hd) return;
-    float *pr = so;
-    float *vs = so + ((p.max_pos + 3) & ~3);
     const float *sc = p.scores + ((size_t)z * p.H + h) * p.score_stride;
-    const size_t voff = (size_t)g * hd + d0;
-    const int nchunks = (n + kVChunk - 1) / kVChunk;
-    auto stage = [&](int c) {
-        if (c >= nchunks) return;
-        const int base = c * kVChunk, cnt = min(kVChunk, n - base);
-        float *dst = vs + (c % kVRing) * kVChunk * kOutDims;
-        for (int i = tid; i < cnt * (kOutDims / 4); i += kOutThreads) {
-            const int r = i / (kOutDims / 4), q = i - r * (kOutDims / 4);
-            cp_async16(dst + r * kOutDims + 4 * q, kv_row(w.v, w.vp, w.plen, base + r, kvd, voff + 4 * q));
-        }
-    };
-    // the scores and the first V chunks all in flight at once; the softmax
-    // runs while V streams in
     for (int i = tid; i < (n + 3) / 4; i += kOutThreads) cp_async16(pr + 4 * i, sc + 4 * i);
     cp_async_commit();
-    for (int c = 0; c < kVRing - 1; c++) {
-        stage(c);
-        cp_async_commit();
-    }
-    cp_async_wait<kVRing - 1>();
+    cp_async_wait<0>();
     __syncthreads();
     float m = -INFINITY;
     for (int i = tid; i < n; i += kOutThreads) m = fmaxf(m, pr[i]);
@@ -195,7 +193,7 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
     __syncthreads();
     if (tid == 0) {
         float mm = -INFINITY;
-        for (int w = 0; w < kOutThreads / 32; w++) mm = fmaxf(mm, red[w]);
+        for (int i = 0; i < kOutThreads / 32; i++) mm = fmaxf(mm, red[i]);
         bcast = mm;
     }
     __syncthreads();
@@ -207,7 +205,7 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
     } else {
         for (int i = tid; i < n; i += kOutThreads) pr[i] = expf_glibc(fs(pr[i], mx));
         __syncthreads();
-        if (tid == 0) {
+        if (tid == 0) {  // the total in position order (src/ops.rs:1219-1223)
             float total = 0.0f;
             int i = 0;
             for (; i + 4 <= n; i += 4) {
@@ -222,21 +220,19 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
         for (int i = tid; i < n; i += kOutThreads) pr[i] = fm(pr[i], inv);
     }
     __syncthreads();
-    // out[d] = Σ_p prob_p·v_p[d], one sequential chain per dim
+    if (tid >= hd) return;
+    const size_t voff = (size_t)g * hd + tid;
     float acc = 0.0f;
-    for (int c = 0; c < nchunks; c++) {
-        stage(c + kVRing - 1);
-        cp_async_commit();
-        cp_async_wait<kVRing - 1>();
-        __syncthreads();
-        if (tid < kOutDims && d0 + tid < hd) {
-            const float *src = vs + (c % kVRing) * kVChunk * kOutDims + tid;
-            const int base = c * kVChunk, cnt = min(kVChunk, n - base);
-            for (int r = 0; r < cnt; r++) acc = fa(acc, fm(pr[base + r], src[r * kOutDims]));
-        }
-        __syncthreads();
+    int r = 0;
+    for (; r + 8 <= n; r += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = __ldcg(kv_row(w.v, w.vp, w.plen, r + k, kvd, voff));
+#pragma unroll
+        for (int k = 0; k < 8; k++) acc = fa(acc, fm(pr[r + k], v[k]));
     }
-    if (tid < kOutDims && d0 + tid < hd) p.out[(size_t)z * p.os + (size_t)h * hd + d0 + tid] = acc;
+    for (; r < n; r++) acc = fa(acc, fm(pr[r], __ldcg(kv_row(w.v, w.vp, w.plen, r, kvd, voff))));
+    p.out[(size_t)z * p.os + (size_t)h * hd + tid] = acc;
 }
 
 // ── kernel-level parity: integer sub-block sums of one row against an xq ──

@@ -85,7 +85,8 @@ def main() -> None:
         names = ["max", "exps", "total", "keys", "radix0", "radix8", "radix16", "radix24", "gather", "cumsum", "end"]
         print(json.dumps({"kernel": "k_sample", "config": args.config, "layers": args.layers or None,
                           "vocab": m.cfg.vocab, "us_per_run": round(ms * 1000 / args.sampler, 2),
-                          "step_end_us": {n: round(v / 1000, 2) for n, v in zip(names, ph[1:])}}))
+                          "step_end_us": {n: round(v / 1000, 2) for n, v in zip(names, ph[1:12])},
+                          "sum_passes": {"total": ph[12], "cumsum": ph[13]}}))
         return
     if args.decode:
         c = m.cache(min(m.cfg.ctx, args.prompt + args.decode + 8))

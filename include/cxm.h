@@ -232,10 +232,11 @@ int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, float *ms_total
 int cxm_bench_decode_sampled(cxm_model *m, cxm_cache *c, cxm_sampler *s, uint32_t steps, float *ms_total);
 
 /* The device sampler alone, `reps` times on the logits of the model's last
- * step (a forward first), device-timed. With phase_ns (nphase <= 12
+ * step (a forward first), device-timed. With phase_ns (nphase <= 14
  * entries), the last run's step ends on CTA 0 in ns from its start: the
  * max, the exponentials, the total, the keys, the four radix passes, the
- * gather, the cumulative sums, the end (0 where a run skips a step). */
+ * gather, the cumulative sums, the end (0 where a run skips a step); then
+ * the passes of its two sums. */
 int cxm_bench_sample(cxm_model *m, cxm_sampler *s, uint32_t reps, float *ms_total, uint64_t *phase_ns,
                      uint32_t nphase);
 
