@@ -63,7 +63,7 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
                  : "memory");
 }
 // 16 consecutive 32-bit columns of this warp's 32 TMEM lanes (one per thread)
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15}, [%16];"
@@ -71,8 +71,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
-// 8 consecutive 32-bit columns of this warp's 32 TMEM lanes
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[16]) {
+// 8 consecutive 32-bit columns of this warp's 32 TMEM lanes (into r[0..7])
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t *r) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
                  : "r"(taddr));
@@ -424,6 +424,44 @@ __device__ __forceinline__ bool producers_all(bool ok) {
     return r != 0;
 }
 
+// One group of an epilogue warp's accumulators: 64 TMEM columns (64/HN
+// sub-blocks j0.. of its HN rows) loaded behind one wait, then each row's
+// chain advanced sub-block by sub-block: acc += (esc·xe)·Σ (buffered), or
+// the fused kernel's xe·((d·sc)·Σ − (dmin·m)·xs). `cb`: the block's first
+// column of this warp's rows; `esc` and `db` start at its rows too.
+template <int HN>
+__device__ __forceinline__ void pf_epi_group(uint32_t cb, int j0, int N, const float *xeb, const float *xsb, bool fused,
+                                             const float *esc, const float *db, int nsub, float (&acc)[16]) {
+    constexpr int JB = 64 / HN;
+    uint32_t sv[64];
+    float ev[JB], xv[JB];
+#pragma unroll
+    for (int jj = 0; jj < JB; jj++) {
+        const uint32_t col = cb + (uint32_t)((j0 + jj) * N);
+        if (HN == 16) tmem_ld16(col, sv + 16 * jj);
+        else tmem_ld8(col, sv + 8 * jj);
+    }
+#pragma unroll
+    for (int jj = 0; jj < JB; jj++) {
+        ev[jj] = xeb[j0 + jj];
+        xv[jj] = fused ? xsb[j0 + jj] : 0.0f;
+    }
+    tmem_ld_wait();
+#pragma unroll
+    for (int jj = 0; jj < JB; jj++) {
+        const int j = j0 + jj;
+        if (fused) {
+#pragma unroll
+            for (int n = 0; n < HN; n++)
+                acc[n] = fa(acc[n], fm(ev[jj], fs(fm(esc[j * N + n], (float)(int)sv[HN * jj + n]),
+                                                  fm(-db[(size_t)n * nsub + j], xv[jj]))));
+        } else {
+#pragma unroll
+            for (int n = 0; n < HN; n++) acc[n] = fa(acc[n], fm(fm(esc[j * N + n], ev[jj]), (float)(int)sv[HN * jj + n]));
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant__ PfGemm G) {
     extern __shared__ __align__(128) unsigned char pf_smem_raw[];
     // 128-byte aligned by an offset from the array itself (the operand tiles
@@ -597,29 +635,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
             if (!__all_sync(0xffffffffu, pf_wait(&mma_done[st], (b >> 1) & 1, &abort_s, G.err) && !abort_s)) break;
             tc_fence_after();
             const float *esc = (const float *)(sm + L.esc[st]) + c0;
-            for (int j = 0; j < nsb; j++) {
-                const float e = xe[b * nsb + j];
-                const uint32_t col = tmem + lanes + (uint32_t)(st * 256 + j * N + c0);
-                uint32_t s0[16];
-                if (HN == 16) tmem_ld16(col, s0);
-                else tmem_ld8(col, s0);
-                tmem_ld_wait();
-                if (fused) {
-                    // xe·((d·sc)·Σ − (dmin·m)·xs), the offset's product being −des
-                    const float x = xs[b * nsb + j];
-                    const float *dj = des_all + (size_t)c0 * G.nsub + b * nsb + j;
-#pragma unroll
-                    for (int n = 0; n < 16; n++) {
-                        if (n >= HN) break;
-                        acc[n] = fa(acc[n], fm(e, fs(fm(esc[j * N + n], (float)(int)s0[n]), fm(-dj[(size_t)n * G.nsub], x))));
-                    }
-                    continue;
-                }
-#pragma unroll
-                for (int n = 0; n < 16; n++) {
-                    if (n >= HN) break;
-                    acc[n] = fa(acc[n], fm(fm(esc[j * N + n], e), (float)(int)s0[n]));
-                }
+            // 64 accumulator columns per TMEM wait: 4 sub-blocks of 16 rows
+            // (sub-blocks of 32) or 8 of 8 (sub-blocks of 16)
+            const uint32_t cb = tmem + lanes + (uint32_t)(st * 256 + c0);
+            const float *xeb = xe + b * nsb, *xsb = xs + b * nsb, *db = des_all + (size_t)c0 * G.nsub + b * nsb;
+            for (int j0 = 0; j0 < nsb; j0 += 64 / HN) {
+                if (HN == 16) pf_epi_group<16>(cb, j0, N, xeb, xsb, fused, esc, db, G.nsub, acc);
+                else pf_epi_group<8>(cb, j0, N, xeb, xsb, fused, esc, db, G.nsub, acc);
             }
             tc_fence_before();
             __syncwarp();

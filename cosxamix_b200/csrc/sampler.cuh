@@ -219,7 +219,7 @@ __device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) { return min
 // span as long as the terms summed so far (sums from zero double between
 // binade crossings), and it doubles after a pass without one. Every thread
 // writes the sums of its terms up to its own first event; a later pass
-// rewrites those past the CTA's first event.
+// rewrites those past the CTA's first event. src and dst are 16-byte aligned.
 __device__ int exact_scan(const float *src, int len, float *dst, int mode, float stop, ScanShared &sh, float *sum) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float x[8], xn[8];
@@ -297,26 +297,41 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
         const uint32_t wex = warp ? __shfl_sync(0xffffffffu, wi, warp - 1) : 0u;
         const uint32_t tex = __shfl_up_sync(0xffffffffu, inc, 1);
         uint32_t P = sat_add(M0, sat_add(wex, lane ? tex : 0u));
-        // the sums of this thread's terms, up to its first event
+        // the sums of this thread's terms, up to its first event (the sums
+        // after it are rewritten by a later pass)
+        int eloc = INT_MAX;
         if (act) {
+            float out[8];
             bool done = false;
 #pragma unroll
             for (int k = 0; k < 8; k++) {
+                out[k] = 0.0f;
                 if (done || !((act >> k) & 1)) continue;
                 const uint32_t kf = kr[k] - ((up >> k) & 1);
-                float r;
                 if (((evm >> k) & 1) || P + kf >= (1u << 24)) {  // an f32 addition to the exact sum before it
-                    r = __fadd_rn(scan_value(P, eb), x[k]);
-                    sh.cand[tid] = r;
-                    atomicMin(&sh.ev[it & 1], base + k);
+                    out[k] = __fadd_rn(scan_value(P, eb), x[k]);
+                    sh.cand[tid] = out[k];
+                    eloc = base + k;
                     done = true;
                 } else {
                     P += kr[k];
-                    r = scan_value(P, eb);
+                    out[k] = scan_value(P, eb);
                 }
-                if (dst) dst[base + k] = r;
+            }
+            if (dst) {
+                if (act == 0xFFu) {
+                    ((float4 *)(dst + base))[0] = make_float4(out[0], out[1], out[2], out[3]);
+                    ((float4 *)(dst + base))[1] = make_float4(out[4], out[5], out[6], out[7]);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        if ((act >> k) & 1) dst[base + k] = out[k];
+                }
             }
         }
+        // one shared atomic per warp: past a crossing every later thread has an event
+        const int wmin = __reduce_min_sync(0xffffffffu, eloc);
+        if (lane == 0 && wmin != INT_MAX) atomicMin(&sh.ev[it & 1], wmin);
         __syncthreads();
         const int E = sh.ev[it & 1];
         if (tid == 0) sh.ev[(it + 1) & 1] = INT_MAX;
