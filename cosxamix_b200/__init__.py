@@ -88,6 +88,8 @@ def lib() -> C.CDLL:
             "cxm_bench_decode_sampled": (C.c_int, [P, P, P, C.c_uint32, C.POINTER(C.c_float)]),
             "cxm_bench_matvec": (C.c_int, [P, C.c_uint32, C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
             "cxm_bench_sample": (C.c_int, [P, P, C.c_uint32, C.POINTER(C.c_float), P, C.c_uint32]),
+            "cxm_arm_gemm_stamps": (C.c_int, [C.c_int]),
+            "cxm_read_gemm_stamps": (C.c_int, [P, C.c_uint32]),
             "cxm_step_launches": (C.c_int, [P]),
             "cxm_synth_write": (C.c_int, [C.POINTER(SynthSpec), C.c_char_p]),
             "cxm_quantize": (C.c_int64, [C.c_int, P, C.c_uint64, P, C.c_uint64]),
@@ -356,7 +358,7 @@ class Modelo:
         of the last step, the last run's step ends (ns from its start), then
         the passes of its two sums."""
         ms = C.c_float(0)
-        ph = np.zeros(14, np.uint64)
+        ph = np.zeros(78, np.uint64)
         _check(lib().cxm_bench_sample(self.h, sampler.h, reps, C.byref(ms), _ptr(ph), ph.size))
         return ms.value, ph.tolist()
 
@@ -415,6 +417,18 @@ def expf(x: np.ndarray) -> np.ndarray:
     y = np.zeros_like(x)
     _check(lib().cxm_debug_expf(_ptr(x), _ptr(y), x.size))
     return y
+
+
+def arm_gemm_stamps(launch: int) -> None:
+    """Measurement: the launch-th prompt GEMM from now records its CTA
+    (0, 0)'s step times (include/cxm.h, cxm_arm_gemm_stamps)."""
+    _check(lib().cxm_arm_gemm_stamps(launch))
+
+
+def read_gemm_stamps() -> list:
+    out = np.zeros(98, np.uint64)
+    _check(lib().cxm_read_gemm_stamps(_ptr(out), out.size))
+    return out.tolist()
 
 
 def seq_sums(x: np.ndarray) -> np.ndarray:

@@ -570,6 +570,11 @@ struct PfRowsDest {
     int fused = 0;
 };
 
+// measurement: the launch of the prompt GEMM (counted from the arming) whose
+// CTA (0, 0) records its roles' steps (cxm_arm_gemm_stamps)
+static int g_pf_stamp_target = -1, g_pf_calls = 0;
+static unsigned long long *g_pf_stamps = nullptr;
+
 // out = W·x for the t rows quantized last, each output in the buffered
 // path's order, then the segment's epilogue (tokens at positions pos0..)
 int pf_gemm(cudaStream_t st, const MvSeg &seg, int t, int pos0, int ld_out, const int8_t *a16, const int8_t *a32,
@@ -593,6 +598,7 @@ int pf_gemm(cudaStream_t st, const MvSeg &seg, int t, int pos0, int ld_out, cons
     // the one-row order is the fused kernel's only where the reference has
     // one for the format (src/ops.rs:837-858); Q5_K and Q2_K stay buffered
     G.fused = rd.fused && seg.ord == ORD_FUSED;
+    if (g_pf_stamp_target >= 0 && g_pf_calls++ == g_pf_stamp_target) G.stamps = g_pf_stamps;
     const PfSmem L = pf_smem(seg.M.type, seg.M.K);
     // at least 116 KB, so no two of these CTAs share an SM (each takes all 512 TMEM columns)
     const size_t smem = std::max<size_t>(L.total + 128, 116 * 1024);
@@ -2583,7 +2589,7 @@ extern "C" int cxm_bench_sample(cxm_model *m, cxm_sampler *s, uint32_t reps, flo
     if (phase_ns) {
         unsigned long long h[kSampStamps];
         CU(cudaMemcpy(h, st.p, sizeof(h), cudaMemcpyDeviceToHost));
-        for (uint32_t k = 0; k < nphase; k++) phase_ns[k] = k >= 12 ? h[k] : h[k] ? h[k] - h[0] : 0;
+        for (uint32_t k = 0; k < nphase; k++) phase_ns[k] = (k == 12 || k == 13) ? h[k] : h[k] ? h[k] - h[0] : 0;
     }
     for (uint32_t i = 0; i < reps; i++) {  // one draw per run
         uint64_t x = s->state;
@@ -2592,6 +2598,31 @@ extern "C" int cxm_bench_sample(cxm_model *m, cxm_sampler *s, uint32_t reps, flo
         x ^= x >> 27;
         s->state = x;
     }
+    return 0;
+}
+
+extern "C" int cxm_arm_gemm_stamps(int launch) {
+    if (launch < 0) {
+        g_pf_stamp_target = -1;
+        return 0;
+    }
+    if (!g_pf_stamps) CU(cudaMalloc(&g_pf_stamps, kPfStampSlots * sizeof(unsigned long long)));
+    CU(cudaMemset(g_pf_stamps, 0, kPfStampSlots * sizeof(unsigned long long)));
+    g_pf_stamp_target = launch;
+    g_pf_calls = 0;
+    return 0;
+}
+
+extern "C" int cxm_read_gemm_stamps(uint64_t *out, uint32_t n) {
+    if (!out || n > (uint32_t)kPfStampSlots || !g_pf_stamps) {
+        set_error("bad arguments (arm first)");
+        return -1;
+    }
+    unsigned long long h[kPfStampSlots];
+    CU(cudaDeviceSynchronize());
+    CU(cudaMemcpy(h, g_pf_stamps, sizeof(h), cudaMemcpyDeviceToHost));
+    for (uint32_t k = 0; k < n; k++) out[k] = h[k] && h[0] ? h[k] - h[0] : 0;
+    g_pf_stamp_target = -1;
     return 0;
 }
 

@@ -19,7 +19,7 @@
 //   k_pf_gemm   one 128-token x N-row tile of out = W·x over the whole row
 //               (warp-specialized: 8 epilogue warps own the TMEM lanes =
 //               tokens, two per lane quarter, each for half of the rows;
-//               4 producer warps copy the k-quant blocks a few ahead and
+//               3 producer warps copy the k-quant blocks a few ahead and
 //               unpack them to int8 operand tiles; one thread copies the
 //               activation tiles and issues the MMAs), then the segment's
 //               epilogue (bias, RoPE + K/V append, residual, SwiGLU)
@@ -209,9 +209,12 @@ struct PfGemm {
     // of the buffered path's; the same values for the formats without a
     // minimum
     int fused;
+    // measurement only: CTA (0, 0)'s %globaltimer at its roles' steps (kPfStampSlots), or NULL
+    unsigned long long *stamps;
 };
 
-constexpr int kPfThreads = 416;  // warps 0-7: epilogue (TMEM lanes, two halves of the rows); 8-11: producers; 12: copies and MMAs
+constexpr int kPfThreads = 384;  // warps 0-7: epilogue (TMEM lanes, two halves of the rows); 8-10: producers; 11: copies and MMAs
+constexpr int kPfProducers = 96;
 constexpr int kPfStages = 2;     // operand tiles of the weights and accumulator buffers in TMEM
 constexpr int kPfAStages = 3;    // activation tiles in flight
 constexpr int kPfRaw = 4;        // weight blocks in flight (GGUF bytes)
@@ -220,6 +223,18 @@ constexpr uint32_t kPfTmemCols = 512;  // two accumulator buffers of 256 columns
 // rows per CTA tile: every sub-block of a super-block gets its own accumulator
 // of N columns, two super-blocks in flight: 2 · subs · N = 512 columns
 __host__ __device__ constexpr int pf_rows_per_tile(int sub) { return sub == 32 ? 32 : 16; }
+
+// stamp slots: [0] start; per block b < 16: [16+b] MMA inputs in, [32+b] a
+// producer's copies in, [48+b] its operands out, [64+b] epilogue warp 0's
+// accumulators in, [80+b] out; [96] offset chains done, [97] end
+constexpr int kPfStampSlots = 98;
+__device__ __forceinline__ void pf_stamp(const PfGemm &G, int slot) {
+    if (G.stamps && blockIdx.x == 0 && blockIdx.y == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        G.stamps[slot] = t;
+    }
+}
 
 struct PfSmem {  // byte offsets in the dynamic shared memory
     uint32_t a[kPfAStages], b[kPfStages], esc[kPfStages], raw, des, anyd, total;
@@ -409,14 +424,14 @@ __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile
     return false;
 }
 
-// AND of `ok` over the 128 producer threads (named barrier 2), so they leave
+// AND of `ok` over the 96 producer threads (named barrier 2), so they leave
 // their loop together and none is left waiting at a barrier of the group
 __device__ __forceinline__ bool producers_all(bool ok) {
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.and.pred q, 2, 128, p;\n\t"
+        "bar.red.and.pred q, 2, 96, p;\n\t"
         "selp.u32 %0, 1, 0, q;\n\t}"
         : "=r"(r)
         : "r"((uint32_t)ok)
@@ -424,42 +439,75 @@ __device__ __forceinline__ bool producers_all(bool ok) {
     return r != 0;
 }
 
-// One group of an epilogue warp's accumulators: 64 TMEM columns (64/HN
-// sub-blocks j0.. of its HN rows) loaded behind one wait, then each row's
-// chain advanced sub-block by sub-block: acc += (esc·xe)·Σ (buffered), or
-// the fused kernel's xe·((d·sc)·Σ − (dmin·m)·xs). `cb`: the block's first
-// column of this warp's rows; `esc` and `db` start at its rows too.
-template <int HN>
-__device__ __forceinline__ void pf_epi_group(uint32_t cb, int j0, int N, const float *xeb, const float *xsb, bool fused,
-                                             const float *esc, const float *db, int nsub, float (&acc)[16]) {
-    constexpr int JB = 64 / HN;
-    uint32_t sv[64];
-    float ev[JB], xv[JB];
+// An epilogue warp's whole main loop, for HN rows per warp (sub-blocks of
+// 32: 16 rows, 8 sub-blocks a block; of 16: 8 rows, 16 sub-blocks) and the
+// buffered or the fused order. Per block: wait for its accumulators, then
+// 64 TMEM columns behind each wait; each row's chain advances sub-block by
+// sub-block: acc += (esc·xe)·Σ (buffered), or the fused kernel's
+// xe·((d·sc)·Σ − (dmin·m)·xs). The token's xe (xs) of the next block are
+// loaded while a block is summed. `cb0`: column of this warp's rows in
+// buffer 0; `esc0`, `db0`: their scale rows (buffer 0) and offsets.
+template <int HN, bool FUSED>
+__device__ __forceinline__ bool pf_epi_loop(const PfGemm &G, const float *xe, const float *xs, int nblk, int N,
+                                            uint32_t cb0, const unsigned char *sm, const PfSmem &L, int c0,
+                                            const float *db0, uint64_t *mma_done, uint64_t *tmem_empty,
+                                            volatile int *abort_s, float (&acc)[16]) {
+    constexpr int NSB = 128 / HN, JB = 64 / HN, NX = FUSED ? NSB : 1;
+    const int lane = threadIdx.x & 31;
+    float ev[NSB], xv[NX];
 #pragma unroll
-    for (int jj = 0; jj < JB; jj++) {
-        const uint32_t col = cb + (uint32_t)((j0 + jj) * N);
-        if (HN == 16) tmem_ld16(col, sv + 16 * jj);
-        else tmem_ld8(col, sv + 8 * jj);
-    }
+    for (int k = 0; k < NSB; k++) ev[k] = __ldg(xe + k);
 #pragma unroll
-    for (int jj = 0; jj < JB; jj++) {
-        ev[jj] = xeb[j0 + jj];
-        xv[jj] = fused ? xsb[j0 + jj] : 0.0f;
-    }
-    tmem_ld_wait();
+    for (int k = 0; k < NX; k++) xv[k] = FUSED ? __ldg(xs + k) : 0.0f;
+    for (int b = 0; b < nblk; b++) {
+        const int st = b & 1, bn = b + 1 < nblk ? b + 1 : b;
+        float en[NSB], xn[NX];
 #pragma unroll
-    for (int jj = 0; jj < JB; jj++) {
-        const int j = j0 + jj;
-        if (fused) {
+        for (int k = 0; k < NSB; k++) en[k] = __ldg(xe + bn * NSB + k);
 #pragma unroll
-            for (int n = 0; n < HN; n++)
-                acc[n] = fa(acc[n], fm(ev[jj], fs(fm(esc[j * N + n], (float)(int)sv[HN * jj + n]),
-                                                  fm(-db[(size_t)n * nsub + j], xv[jj]))));
-        } else {
+        for (int k = 0; k < NX; k++) xn[k] = FUSED ? __ldg(xs + bn * NSB + k) : 0.0f;
+        // warp-uniform: the TMEM loads below are collective over the warp
+        if (!__all_sync(0xffffffffu, pf_wait(&mma_done[st], (b >> 1) & 1, abort_s, G.err) && !*abort_s)) return false;
+        tc_fence_after();
+        if (threadIdx.x == 0 && b < 16) pf_stamp(G, 64 + b);
+        const float *esc = (const float *)(sm + L.esc[st]) + c0;
+        const uint32_t cb = cb0 + (uint32_t)(st * 256);
+        const float *db = db0 + b * NSB;
 #pragma unroll
-            for (int n = 0; n < HN; n++) acc[n] = fa(acc[n], fm(fm(esc[j * N + n], ev[jj]), (float)(int)sv[HN * jj + n]));
+        for (int j0 = 0; j0 < NSB; j0 += JB) {
+            uint32_t sv[64];
+#pragma unroll
+            for (int jj = 0; jj < JB; jj++) {
+                const uint32_t col = cb + (uint32_t)((j0 + jj) * N);
+                if (HN == 16) tmem_ld16(col, sv + 16 * jj);
+                else tmem_ld8(col, sv + 8 * jj);
+            }
+            tmem_ld_wait();
+#pragma unroll
+            for (int jj = 0; jj < JB; jj++) {
+                const int j = j0 + jj;
+                if (FUSED) {
+#pragma unroll
+                    for (int n = 0; n < HN; n++)
+                        acc[n] = fa(acc[n], fm(ev[j], fs(fm(esc[j * N + n], (float)(int)sv[HN * jj + n]),
+                                                         fm(-db[(size_t)n * G.nsub + j], xv[FUSED ? j : 0]))));
+                } else {
+#pragma unroll
+                    for (int n = 0; n < HN; n++)
+                        acc[n] = fa(acc[n], fm(fm(esc[j * N + n], ev[j]), (float)(int)sv[HN * jj + n]));
+                }
+            }
         }
+#pragma unroll
+        for (int k = 0; k < NSB; k++) ev[k] = en[k];
+#pragma unroll
+        for (int k = 0; k < NX; k++) xv[k] = xn[k];
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tmem_empty[st]);
+        if (threadIdx.x == 0 && b < 16) pf_stamp(G, 80 + b);
     }
+    return true;
 }
 
 __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant__ PfGemm G) {
@@ -482,7 +530,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     if (tid == 0) {
         for (int i = 0; i < kPfAStages; i++) mbar_init(&full_a[i], 1);
         for (int i = 0; i < kPfStages; i++) {
-            mbar_init(&full_b[i], 128);  // the producer threads
+            mbar_init(&full_b[i], kPfProducers);
             mbar_init(&mma_done[i], 1);
             mbar_init(&tmem_empty[i], 8);  // the epilogue warps
         }
@@ -505,6 +553,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (tid == 0) pf_stamp(G, 0);
     const uint32_t tmem = tmem_base_s;
     const uint32_t idesc = umma_idesc_i8(kPfM, N);
 
@@ -515,7 +564,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     const int HN = N / 2, c0 = (warp >> 2) * HN;  // an epilogue warp's half of the tile's rows
     const int groups = min(16, (G.tokens - mt * kPfM + 7) / 8);  // 8-token row groups of this tile
 
-    if (warp == 12) {
+    if (warp == 11) {
         // ── copies of the activation tiles and the MMAs (one thread) ──
         // the activation tile of block bb into stage bb % kPfAStages: the
         // tile's token rows in groups of 8 (256 bytes per K-step); a tile of
@@ -541,6 +590,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 if (!pf_wait(&full_b[st], (b >> 1) & 1, &abort_s, G.err) ||
                     !pf_wait(&full_a[sa], (b / kPfAStages) & 1, &abort_s, G.err))
                     break;
+                if (b < 16) pf_stamp(G, 16 + b);
                 tc_fence_after();
                 const uint32_t dcol = tmem + (uint32_t)st * 256;
                 for (int j = 0; j < nsb; j++) {
@@ -573,26 +623,27 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     } else if (warp >= 8) {
         // ── producers: copy the N rows' super-blocks kPfRaw - 1 blocks ahead
         // (cp.async), unpack each to the int8 operand tile of its stage ──
-        const int ptid = tid - 256;
+        const int ptid = tid - 256;  // warps 8-10
         uint8_t *raw = sm + L.raw;
         const int slot_bytes = N * 224;
         for (int bb = 0; bb < kPfRaw - 1; bb++) {  // one commit group per block, empty past the end
-            if (bb < nblk) pf_copy(M, r0, N, bb, raw + (bb % kPfRaw) * slot_bytes, ptid, 128);
+            if (bb < nblk) pf_copy(M, r0, N, bb, raw + (bb % kPfRaw) * slot_bytes, ptid, kPfProducers);
             cp_async_commit();
         }
         for (int b = 0; b < nblk; b++) {
             const int st = b & 1;
             const int nx = b + kPfRaw - 1;  // its slot was unpacked at block b-1, before that block's last barrier
-            if (nx < nblk) pf_copy(M, r0, N, nx, raw + (nx % kPfRaw) * slot_bytes, ptid, 128);
+            if (nx < nblk) pf_copy(M, r0, N, nx, raw + (nx % kPfRaw) * slot_bytes, ptid, kPfProducers);
             cp_async_commit();
             cp_async_wait<kPfRaw - 1>();  // this thread's copies of block b
             bool w = true;
             if (b >= kPfStages) w = pf_wait(&tmem_empty[st], ((b - kPfStages) >> 1) & 1, &abort_s, G.err);
             // every producer's copies of block b are in; the epilogue is done with stage st
             if (!producers_all(w && !abort_s)) break;
+            if (ptid == 0 && b < 16) pf_stamp(G, 32 + b);
             const uint8_t *blkraw = raw + (b % kPfRaw) * slot_bytes;
             float *esc = (float *)(sm + L.esc[st]);  // [sub-block in block][row]
-            for (int i = ptid; i < N * 4; i += 128) {
+            for (int i = ptid; i < N * 4; i += kPfProducers) {
                 const int n = i >> 2, q = i & 3;
                 uint32_t w[16];
                 float e[4], o[4];
@@ -618,8 +669,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 }
             }
             fence_async_smem();
-            asm volatile("bar.sync 2, 128;" ::: "memory");  // every producer is done with slot b % kPfRaw
+            asm volatile("bar.sync 2, 96;" ::: "memory");  // every producer is done with slot b % kPfRaw
             mbar_arrive(&full_b[st]);
+            if (ptid == 0 && b < 16) pf_stamp(G, 48 + b);
         }
         cp_async_wait<0>();  // no copy outlives the loop
     } else {
@@ -628,24 +680,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         const float *xe = G.xe + (size_t)(m < G.tokens ? m : 0) * G.nsub;
         const float *xs = G.xs + (size_t)(m < G.tokens ? m : 0) * G.nsub;
         const bool fused = G.fused && mins;
-        const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
-        for (int b = 0; b < nblk; b++) {
-            const int st = b & 1;
-            // warp-uniform: the TMEM loads below are collective over the warp
-            if (!__all_sync(0xffffffffu, pf_wait(&mma_done[st], (b >> 1) & 1, &abort_s, G.err) && !abort_s)) break;
-            tc_fence_after();
-            const float *esc = (const float *)(sm + L.esc[st]) + c0;
-            // 64 accumulator columns per TMEM wait: 4 sub-blocks of 16 rows
-            // (sub-blocks of 32) or 8 of 8 (sub-blocks of 16)
-            const uint32_t cb = tmem + lanes + (uint32_t)(st * 256 + c0);
-            const float *xeb = xe + b * nsb, *xsb = xs + b * nsb, *db = des_all + (size_t)c0 * G.nsub + b * nsb;
-            for (int j0 = 0; j0 < nsb; j0 += 64 / HN) {
-                if (HN == 16) pf_epi_group<16>(cb, j0, N, xeb, xsb, fused, esc, db, G.nsub, acc);
-                else pf_epi_group<8>(cb, j0, N, xeb, xsb, fused, esc, db, G.nsub, acc);
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_empty[st]);
+        const uint32_t cb0 = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c0;
+        const float *db0 = des_all + (size_t)c0 * G.nsub;
+        if (HN == 16) {
+            if (fused) pf_epi_loop<16, true>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
+            else pf_epi_loop<16, false>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
+        } else {
+            if (fused) pf_epi_loop<8, true>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
+            else pf_epi_loop<8, false>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
         }
     }
     __syncthreads();
@@ -660,46 +702,77 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
 #pragma unroll
             for (int n = 0; n < 16; n++)
                 if (n < HN && anyd[c0 + n]) live |= 1u << n;
-            if (live) {
-                for (int s = 0; s < G.nsub; s++) {
-                    const float e = __ldg(xe + s), x = __ldg(xs + s);
+            if (live) {  // nsub is a multiple of 8: eight sub-blocks' xe/xs loads in flight at a time
+                for (int s0 = 0; s0 < G.nsub; s0 += 8) {
+                    float e8[8], x8[8];
 #pragma unroll
-                    for (int n = 0; n < 16; n++) {
-                        if (n >= HN) break;
-                        const float t = fm(fm(des_all[(size_t)(c0 + n) * G.nsub + s], e), x);
-                        acc[n] = (live >> n) & 1u ? fa(acc[n], t) : acc[n];
+                    for (int k = 0; k < 8; k++) {
+                        e8[k] = __ldg(xe + s0 + k);
+                        x8[k] = __ldg(xs + s0 + k);
+                    }
+#pragma unroll
+                    for (int k = 0; k < 8; k++) {
+#pragma unroll
+                        for (int n = 0; n < 16; n++) {
+                            if (n >= HN) break;
+                            const float t = fm(fm(des_all[(size_t)(c0 + n) * G.nsub + s0 + k], e8[k]), x8[k]);
+                            acc[n] = (live >> n) & 1u ? fa(acc[n], t) : acc[n];
+                        }
                     }
                 }
             }
         }
-        // the segment's epilogue, one output unit (two tiled rows) at a time
+        if (tid == 0) pf_stamp(G, 96);
+        // the segment's epilogue, one output unit (two tiled rows) at a time:
+        // every unit's inputs (bias, rotation, residual) loaded first, then
+        // the results stored
         const MvSeg &g = G.seg;
         const int pos = G.row_pos ? G.row_pos[m] : G.pos0 + m;
         float *cache_base = G.row_out ? G.row_out[m] : g.out;
+        float *out = g.at_pos ? cache_base + (size_t)pos * g.pos_stride : g.out + (size_t)m * G.ld_out;
+        int ua[8], ub[8];
+        float ia[8], ib[8], ic[8], id[8];
 #pragma unroll
-        for (int n = 0; n < 16; n += 2) {  // constant indices: acc stays in registers
-            const int u = (r0 + c0 + n) >> 1;
-            if (n >= HN || u >= g.units) break;
-            int ra, rb;
-            unit_rows(g, u, ra, rb);
-            const float y0 = acc[n], y1 = acc[n + 1];
-            float *out = g.at_pos ? cache_base + (size_t)pos * g.pos_stride : g.out + (size_t)m * G.ld_out;
+        for (int k = 0; k < 8; k++) {  // constant indices: everything stays in registers
+            const int n = 2 * k, u = (r0 + c0 + n) >> 1;
+            ua[k] = -1;
+            ub[k] = 0;
+            ia[k] = ib[k] = ic[k] = id[k] = 0.0f;
+            if (n >= HN || u >= g.units) continue;
+            unit_rows(g, u, ua[k], ub[k]);
+            const int ra = ua[k], rb = ub[k];
+            if (g.epi == EPI_RESID) {
+                ia[k] = out[ra];
+                ib[k] = out[rb];
+            } else if (g.bias && (g.epi == EPI_STORE || g.epi == EPI_ROPE)) {
+                ia[k] = __ldg(g.bias + ra);
+                ib[k] = __ldg(g.bias + rb);
+            }
+            if (g.epi == EPI_ROPE) {
+                const int i = ra % (2 * g.half);
+                ic[k] = __ldg(G.rope_cos + (size_t)pos * g.half + i);
+                id[k] = __ldg(G.rope_sin + (size_t)pos * g.half + i);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int ra = ua[k], rb = ub[k];
+            if (ra < 0) continue;
+            const float y0 = acc[2 * k], y1 = acc[2 * k + 1];
             switch (g.epi) {
             case EPI_STORE:
-                out[ra] = g.bias ? fa(y0, g.bias[ra]) : y0;
-                out[rb] = g.bias ? fa(y1, g.bias[rb]) : y1;
+                out[ra] = g.bias ? fa(y0, ia[k]) : y0;
+                out[rb] = g.bias ? fa(y1, ib[k]) : y1;
                 break;
             case EPI_ROPE: {  // src/ops.rs:1150-1193
-                const int i = ra % (2 * g.half);
-                const float c = G.rope_cos[(size_t)pos * g.half + i], s = G.rope_sin[(size_t)pos * g.half + i];
-                const float a = g.bias ? fa(y0, g.bias[ra]) : y0, bb = g.bias ? fa(y1, g.bias[rb]) : y1;
-                out[ra] = fs(fm(a, c), fm(bb, s));
-                out[rb] = fa(fm(a, s), fm(bb, c));
+                const float a = g.bias ? fa(y0, ia[k]) : y0, bb = g.bias ? fa(y1, ib[k]) : y1;
+                out[ra] = fs(fm(a, ic[k]), fm(bb, id[k]));
+                out[rb] = fa(fm(a, id[k]), fm(bb, ic[k]));
                 break;
             }
             case EPI_RESID:  // src/forward.rs:467-469, :489-491
-                out[ra] = fa(out[ra], y0);
-                out[rb] = fa(out[rb], y1);
+                out[ra] = fa(ia[k], y0);
+                out[rb] = fa(ib[k], y1);
                 break;
             case EPI_SWIGLU: {  // src/kernels/scalar.rs:63-67, src/forward.rs:485-487
                 const float act = __fdiv_rn(y0, fa(1.0f, expf_glibc(-y0)));
@@ -713,6 +786,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     }
     tc_fence_before();
     __syncthreads();
+    if (tid == 0) pf_stamp(G, 97);
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, kPfTmemCols);

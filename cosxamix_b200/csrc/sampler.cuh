@@ -60,7 +60,7 @@ struct SampleArgs {
     unsigned long long *stamps;  // measurement only: CTA 0's %globaltimer at its steps' ends [kSampStamps], or NULL
 };
 
-constexpr int kSampStamps = 14;  // 12 step ends, then the two sums' pass counts
+constexpr int kSampStamps = 14 + 64;  // 12 step ends, the two sums' pass counts, the total's first 64 passes' starts
 __device__ __forceinline__ void samp_stamp(const SampleArgs &a, int k) {
     if (a.stamps && blockIdx.x == 0 && threadIdx.x == 0) {
         unsigned long long t;
@@ -154,11 +154,25 @@ struct ScanTerm {
 };
 
 __device__ __forceinline__ ScanTerm scan_term(float x, int eb) {
+    ScanTerm t;
+    if (eb >= 24) {  // u >= 2^-126: x/u = x·2^(150-eb), exact below 2^25 (the scale is a normal power of two)
+        const float q = __fmul_rn(x, __int_as_float((277 - eb) << 23));
+        if (!(x >= 0.0f) || !(q < 33554432.0f)) {  // negative or NaN; or past the binade (infinity too)
+            t.kr = 1u << 25;
+            t.up = false;
+            t.ev = !(x >= 0.0f) || !(x <= 3.4028235e38f);
+            return t;
+        }
+        const float fl = floorf(q), fr = __fsub_rn(q, fl);  // both exact
+        t.up = fr > 0.5f;
+        t.kr = (uint32_t)fl + (t.up ? 1u : 0u);
+        t.ev = fr == 0.5f;
+        return t;
+    }
     const uint32_t xb = __float_as_uint(x);
     const int xe = (int)(xb >> 23);  // sign and exponent
     const uint32_t xm = (xb & 0x7fffffu) | (xe ? 0x800000u : 0u);
     const int sh = eb - (xe > 1 ? xe : 1);  // x/u = xm / 2^sh
-    ScanTerm t;
     if (sh <= 0) {  // x >= u: an integer multiple of u
         t.kr = sh < -1 ? (1u << 25) : (xm << (-sh));
         t.up = false;
@@ -220,7 +234,8 @@ __device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) { return min
 // binade crossings), and it doubles after a pass without one. Every thread
 // writes the sums of its terms up to its own first event; a later pass
 // rewrites those past the CTA's first event. src and dst are 16-byte aligned.
-__device__ int exact_scan(const float *src, int len, float *dst, int mode, float stop, ScanShared &sh, float *sum) {
+__device__ int exact_scan(const float *src, int len, float *dst, int mode, float stop, ScanShared &sh, float *sum,
+                          unsigned long long *pass_stamps = nullptr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float x[8], xn[8];
     uint32_t kr[8], up = 0, evm = 0;
@@ -232,6 +247,11 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
     float s = 0.0f;
     int pos = 0, span = kSampThreads, it = 0;
     for (;; it++) {
+        if (pass_stamps && tid == 0 && it < 64) {  // measurement only
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            pass_stamps[it] = t;
+        }
         if (pos >= len || (pos > 0 && ((mode == SCAN_UNTIL_GE && s >= stop) || (mode == SCAN_UNTIL_GT && s > stop))))
             break;  // (no term summed yet: the stop is tested after the first)
         if (!(s <= 3.4028235e38f)) {  // infinite or NaN: the rest in order, on one thread
@@ -548,7 +568,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) k_sample(const __grid_constan
         if (!samp_sync(a, target, &ok_s)) return;
         samp_stamp(a, 2);
         if (cta == 0) {  // the total, in index order
-            exact_scan(a.probs, n, nullptr, SCAN_ALL, 0.0f, sh, &sum_s);
+            exact_scan(a.probs, n, nullptr, SCAN_ALL, 0.0f, sh, &sum_s, a.stamps ? a.stamps + 14 : nullptr);
             if (a.stamps && tid == 0) a.stamps[12] = (unsigned long long)sh.passes;
             if (tid == 0) a.gred[G] = __fdiv_rn(1.0f, sum_s);
         }

@@ -44,6 +44,7 @@ def main() -> None:
     ap.add_argument("--prompt", type=int, default=16)
     ap.add_argument("--sample", action="store_true", help="--decode with the device top-p sampler (T 0.7, top-p 0.9)")
     ap.add_argument("--prefill", type=int, default=0, help="time the forward of a seeded prompt of this many tokens")
+    ap.add_argument("--gemm-stamps", type=int, default=-1, help="with --prefill: step times of this GEMM launch")
     ap.add_argument("--sampler", type=int, default=0, help="time RUNS of the device sampler alone on the prompt's logits")
     args = ap.parse_args()
     import bench
@@ -74,9 +75,18 @@ def main() -> None:
             t = time.perf_counter()
             m.forward(prompt, c)  # returns the last token's logits: the device work is done
             times.append((time.perf_counter() - t) * 1000)
-        print(json.dumps({"kernel": "prompt forward (tensor-core GEMMs)", "config": args.config,
-                          "layers": args.layers or None, "tokens": args.prefill,
-                          "ms": round(min(times), 2), "ms_all": [round(x, 2) for x in times]}))
+        out = {"kernel": "prompt forward (tensor-core GEMMs)", "config": args.config,
+               "layers": args.layers or None, "tokens": args.prefill,
+               "ms": round(min(times), 2), "ms_all": [round(x, 2) for x in times]}
+        if args.gemm_stamps >= 0:  # one more forward with a GEMM launch's step times
+            c.limpiar()
+            cx.arm_gemm_stamps(args.gemm_stamps)
+            m.forward(prompt, c)
+            st = [round(v / 1000, 2) for v in cx.read_gemm_stamps()]
+            out["gemm_stamps_us"] = {"launch": args.gemm_stamps, "mma_in": st[16:32], "prod_in": st[32:48],
+                                     "prod_out": st[48:64], "epi_in": st[64:80], "epi_out": st[80:96],
+                                     "offsets_done": st[96], "end": st[97]}
+        print(json.dumps(out))
         return
     if args.sampler:
         c = m.cache(min(m.cfg.ctx, args.prompt + 8))
@@ -86,7 +96,8 @@ def main() -> None:
         print(json.dumps({"kernel": "k_sample", "config": args.config, "layers": args.layers or None,
                           "vocab": m.cfg.vocab, "us_per_run": round(ms * 1000 / args.sampler, 2),
                           "step_end_us": {n: round(v / 1000, 2) for n, v in zip(names, ph[1:12])},
-                          "sum_passes": {"total": ph[12], "cumsum": ph[13]}}))
+                          "sum_passes": {"total": ph[12], "cumsum": ph[13]},
+                          "total_pass_start_us": [round(v / 1000, 2) for v in ph[14:14 + min(64, ph[12])]]}))
         return
     if args.decode:
         c = m.cache(min(m.cfg.ctx, args.prompt + args.decode + 8))

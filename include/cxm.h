@@ -232,13 +232,24 @@ int cxm_bench_decode(cxm_model *m, cxm_cache *c, uint32_t steps, float *ms_total
 int cxm_bench_decode_sampled(cxm_model *m, cxm_cache *c, cxm_sampler *s, uint32_t steps, float *ms_total);
 
 /* The device sampler alone, `reps` times on the logits of the model's last
- * step (a forward first), device-timed. With phase_ns (nphase <= 14
+ * step (a forward first), device-timed. With phase_ns (nphase <= 78
  * entries), the last run's step ends on CTA 0 in ns from its start: the
  * max, the exponentials, the total, the keys, the four radix passes, the
  * gather, the cumulative sums, the end (0 where a run skips a step); then
- * the passes of its two sums. */
+ * the passes of its two sums; then the start of each of the total's first
+ * 64 passes. */
 int cxm_bench_sample(cxm_model *m, cxm_sampler *s, uint32_t reps, float *ms_total, uint64_t *phase_ns,
                      uint32_t nphase);
+
+/* Arm the prompt GEMM's step stamps: the launch-th k_pf_gemm launch from
+ * now (0-based; < 0 disarms) records on its CTA (0, 0) the %globaltimer of
+ * its roles' steps. cxm_read_gemm_stamps then synchronizes the device and
+ * gives n <= 98 of them in ns from the CTA's start (0: not reached): [16+b]
+ * block b's MMA inputs in, [32+b] a producer's copies in, [48+b] its operands
+ * out, [64+b] epilogue warp 0's accumulators in, [80+b] out (b < 16); [96]
+ * offset chains done, [97] end. */
+int cxm_arm_gemm_stamps(int launch);
+int cxm_read_gemm_stamps(uint64_t *out, uint32_t n);
 
 /* Average device time of one gate|up matvec phase (the largest of a layer)
  * of the decode kernel: `reps` such phases, cycling over the layers so every
