@@ -426,7 +426,7 @@ def arm_gemm_stamps(launch: int) -> None:
 
 
 def read_gemm_stamps() -> list:
-    out = np.zeros(98, np.uint64)
+    out = np.zeros(100, np.uint64)
     _check(lib().cxm_read_gemm_stamps(_ptr(out), out.size))
     return out.tolist()
 

@@ -226,8 +226,9 @@ __host__ __device__ constexpr int pf_rows_per_tile(int sub) { return sub == 32 ?
 
 // stamp slots: [0] start; per block b < 16: [16+b] MMA inputs in, [32+b] a
 // producer's copies in, [48+b] its operands out, [64+b] epilogue warp 0's
-// accumulators in, [80+b] out; [96] offset chains done, [97] end
-constexpr int kPfStampSlots = 98;
+// accumulators in, [80+b] out; [96] offset chains done, [97] end; [98] the
+// epilogue past the CTA barrier, [99] the first 8 sub-blocks of its chains
+constexpr int kPfStampSlots = 100;
 __device__ __forceinline__ void pf_stamp(const PfGemm &G, int slot) {
     if (G.stamps && blockIdx.x == 0 && blockIdx.y == 0) {
         unsigned long long t;
@@ -691,6 +692,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         }
     }
     __syncthreads();
+    if (tid == 0) pf_stamp(G, 98);
     if (warp < 8 && !abort_s && m < G.tokens) {
         // the offset chain, after the whole row (src/ops.rs:395-401): each
         // row with a nonzero offset adds its terms in sub-block order; the
@@ -719,6 +721,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                             acc[n] = (live >> n) & 1u ? fa(acc[n], t) : acc[n];
                         }
                     }
+                    if (tid == 0 && s0 == 0) pf_stamp(G, 99);
                 }
             }
         }

@@ -278,7 +278,11 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
         const uint32_t sb = __float_as_uint(s);
         const int eb = (int)(sb >> 23) > 1 ? (int)(sb >> 23) : 1;
         const uint32_t M0 = (sb & 0x7fffffu) | ((sb >> 23) ? 0x800000u : 0u);
-        if (eb != ceb) {
+        const int wbase = cur * kScanWin, base = wbase + 8 * tid;
+        const int end = min(min(len, wbase + kScanWin), pos + span);  // this pass: terms [pos, end)
+        // warps whose 256 terms are all outside the pass skip to the barriers
+        const bool wact = wbase + 256 * warp + 256 > pos && wbase + 256 * warp < end;
+        if (wact && eb != ceb) {
             up = evm = 0;
 #pragma unroll
             for (int k = 0; k < 8; k++) {
@@ -289,21 +293,21 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
             }
             ceb = eb;
         }
-        const int wbase = cur * kScanWin, base = wbase + 8 * tid;
-        const int end = min(min(len, wbase + kScanWin), pos + span);  // this pass: terms [pos, end)
-        uint32_t act = 0, loc = 0;  // active terms of this thread, their sum (< 2^28)
+        uint32_t act = 0, loc = 0, inc = 0;  // active terms of this thread, their sum (< 2^28), the warp's prefix
+        if (wact) {
 #pragma unroll
-        for (int k = 0; k < 8; k++)
-            if (base + k >= pos && base + k < end) {
-                act |= 1u << k;
-                loc += kr[k];
+            for (int k = 0; k < 8; k++)
+                if (base + k >= pos && base + k < end) {
+                    act |= 1u << k;
+                    loc += kr[k];
+                }
+            // inclusive prefix of loc over the warp, saturating
+            inc = loc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t v = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc = sat_add(inc, v);
             }
-        // exclusive prefix of loc over the CTA, saturating
-        uint32_t inc = loc;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t v = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc = sat_add(inc, v);
         }
         if (lane == 31) sh.wtot[warp] = inc;
         __syncthreads();
@@ -316,7 +320,7 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
         const uint32_t total = __shfl_sync(0xffffffffu, wi, 31);
         const uint32_t wex = warp ? __shfl_sync(0xffffffffu, wi, warp - 1) : 0u;
         const uint32_t tex = __shfl_up_sync(0xffffffffu, inc, 1);
-        uint32_t P = sat_add(M0, sat_add(wex, lane ? tex : 0u));
+        uint32_t P = sat_add(M0, sat_add(wex, lane ? tex : 0u));  // (inactive warps: unused)
         // the sums of this thread's terms, up to its first event (the sums
         // after it are rewritten by a later pass)
         int eloc = INT_MAX;

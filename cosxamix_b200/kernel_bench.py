@@ -85,7 +85,8 @@ def main() -> None:
             st = [round(v / 1000, 2) for v in cx.read_gemm_stamps()]
             out["gemm_stamps_us"] = {"launch": args.gemm_stamps, "mma_in": st[16:32], "prod_in": st[32:48],
                                      "prod_out": st[48:64], "epi_in": st[64:80], "epi_out": st[80:96],
-                                     "offsets_done": st[96], "end": st[97]}
+                                     "offsets_done": st[96], "end": st[97], "barrier": st[98],
+                                     "chains_8": st[99]}
         print(json.dumps(out))
         return
     if args.sampler:

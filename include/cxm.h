@@ -244,10 +244,11 @@ int cxm_bench_sample(cxm_model *m, cxm_sampler *s, uint32_t reps, float *ms_tota
 /* Arm the prompt GEMM's step stamps: the launch-th k_pf_gemm launch from
  * now (0-based; < 0 disarms) records on its CTA (0, 0) the %globaltimer of
  * its roles' steps. cxm_read_gemm_stamps then synchronizes the device and
- * gives n <= 98 of them in ns from the CTA's start (0: not reached): [16+b]
+ * gives n <= 100 of them in ns from the CTA's start (0: not reached): [16+b]
  * block b's MMA inputs in, [32+b] a producer's copies in, [48+b] its operands
  * out, [64+b] epilogue warp 0's accumulators in, [80+b] out (b < 16); [96]
- * offset chains done, [97] end. */
+ * offset chains done, [97] end, [98] past the CTA barrier before the chains,
+ * [99] the chains' first 8 sub-blocks. */
 int cxm_arm_gemm_stamps(int launch);
 int cxm_read_gemm_stamps(uint64_t *out, uint32_t n);
 
