@@ -268,24 +268,19 @@ __host__ __device__ inline PfSmem pf_smem(int type, int K) {
     return s;
 }
 
-// Asynchronous copies of super-block b of the tile's N rows into `raw` (one
-// 224-byte slot per row in the GGUF block layout pf_unpack_quarter reads),
-// spread over the producer threads (items i0, i0 + step, ...): plane A in
-// 16-byte chunks, plane S in one 16-byte or three 4-byte pieces, plane D as
-// the aligned 4-byte word that holds it. A 2-byte d (Q6_K, Q3_K) then sits
-// 2·(row & 1) bytes into its word: the rows of a tile group are its lanes,
-// tile groups have an even number of rows and the plane starts 4-byte
-// aligned. Rows past the matrix get zeros.
-__device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void pf_copy(const QMat &M, int r0, int N, int b, uint8_t *raw, int i0, int step) {
+// A producer thread's share of a block's copies (at most 4 pieces at 96
+// producers: 32 rows x 11 chunks for Q5_K), planned once per CTA: the byte
+// offset in the row's slot, the source offset in the matrix for block 0's
+// tile position, and the piece kind (0-31: plane-A chunk k; 32: plane S
+// 16 bytes; 33-35: plane S 4 bytes; 36: plane D word; 37: zeros).
+constexpr int kPfCopyMax = 4;
+struct PfCopyPlan {
+    int cnt;
+    uint32_t dst[kPfCopyMax], src[kPfCopyMax];
+    uint8_t kind[kPfCopyMax], sl[kPfCopyMax];
+};
+__device__ __forceinline__ void pf_copy_plan(const QMat &M, int r0, int N, int i0, int step, PfCopyPlan &P) {
     const int T = M.type, pa = plane_a_bytes(T), ps = plane_s_bytes(T), pd = plane_d_bytes(T), ach = pa / 16;
-    const int t = b / M.lpr, bl = b % M.lpr, nb = tile_nb(M.nblk, M.lpr, t), L = M.rpt * nb;
     const int rows = M.ngroup * M.rpt;  // rows allocated (padded groups)
     int lo_a = 0, lo_s = pa, lo_d = pa + ps;
     if (T == 10) {  // Q2_K: scales, qs, d|dmin
@@ -294,25 +289,64 @@ __device__ __forceinline__ void pf_copy(const QMat &M, int r0, int N, int b, uin
         lo_d = 80;
     }
     const int sp = ps == 16 ? 1 : ps / 4, per = ach + sp + (pd ? 1 : 0);
-    for (int i = i0; i < N * per; i += step) {
+    P.cnt = 0;
+#pragma unroll
+    for (int c = 0; c < kPfCopyMax; c++) {
+        const int i = i0 + c * step;
+        P.kind[c] = 38;  // nothing
+        P.dst[c] = P.src[c] = 0;
+        P.sl[c] = 0;
+        if (i >= N * per) continue;
+        P.cnt = c + 1;
         const int n = i / per, k = i - n * per, r = r0 + n;
-        uint8_t *slot = raw + n * 224;
+        const int g = r / M.rpt, sl = r % M.rpt;
+        P.sl[c] = (uint8_t)sl;
+        P.src[c] = (uint32_t)g * M.group_stride;
         if (r >= rows) {
-            if (k < ach) cp_async16_zfill(slot + lo_a + 16 * k, M.base, 0);
-            continue;
-        }
-        const int g = r / M.rpt, sl = r % M.rpt, lane = M.rpt * bl + sl;
-        const uint8_t *tile = M.base + tile_offset(M, g, t);
-        if (k < ach) {
-            cp_async16(slot + lo_a + 16 * k, tile + ((size_t)k * L + lane) * 16);
+            P.kind[c] = k < ach ? 37 : 38;  // 38: nothing
+            P.dst[c] = (uint32_t)(n * 224 + lo_a + 16 * k);
+        } else if (k < ach) {
+            P.kind[c] = (uint8_t)k;
+            P.dst[c] = (uint32_t)(n * 224 + lo_a + 16 * k);
         } else if (k < ach + sp) {
-            const uint8_t *src = tile + (size_t)ach * L * 16 + (size_t)lane * ps;
-            if (ps == 16) cp_async16(slot + lo_s, src);
-            else cp_async4(slot + lo_s + 4 * (k - ach), src + 4 * (k - ach));
+            P.kind[c] = ps == 16 ? 32 : (uint8_t)(33 + (k - ach));
+            P.dst[c] = (uint32_t)(n * 224 + lo_s + (ps == 16 ? 0 : 4 * (k - ach)));
         } else {
-            const size_t off = (size_t)ach * L * 16 + (size_t)L * ps + (size_t)lane * pd;
-            cp_async4(slot + lo_d, tile + (off & ~(size_t)3));
+            P.kind[c] = 36;
+            P.dst[c] = (uint32_t)(n * 224 + lo_d);
         }
+    }
+}
+// Asynchronous copies of super-block b of the tile's rows into `raw` (one
+// 224-byte slot per row in the GGUF block layout pf_unpack_quarter reads):
+// plane A in 16-byte chunks, plane S in one 16-byte or three 4-byte pieces,
+// plane D as the aligned 4-byte word that holds it. A 2-byte d (Q6_K, Q3_K)
+// then sits 2·(row & 1) bytes into its word: the rows of a tile group are its
+// lanes, tile groups have an even number of rows and the plane starts 4-byte
+// aligned. Rows past the matrix get zeros.
+__device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void pf_copy(const QMat &M, const PfCopyPlan &P, int b, uint8_t *raw) {
+    const int T = M.type, ps = plane_s_bytes(T), pd = plane_d_bytes(T), ach = plane_a_bytes(T) / 16;
+    const int t = b / M.lpr, bl = b - t * M.lpr, nb = tile_nb(M.nblk, M.lpr, t), L = M.rpt * nb;
+    const uint8_t *tb = M.base + (size_t)t * 32 * (size_t)M.bpb;
+    const uint32_t sofs = (uint32_t)(ach * L * 16), dofs = sofs + (uint32_t)(L * ps);
+#pragma unroll
+    for (int c = 0; c < kPfCopyMax; c++) {
+        if (c >= P.cnt) break;
+        const int kind = P.kind[c], lane = M.rpt * bl + P.sl[c];
+        const uint8_t *tile = tb + P.src[c];
+        uint8_t *d = raw + P.dst[c];
+        if (kind < 32) cp_async16(d, tile + ((size_t)kind * L + lane) * 16);
+        else if (kind == 32) cp_async16(d, tile + sofs + (size_t)lane * 16);
+        else if (kind < 36) cp_async4(d, tile + sofs + (size_t)lane * ps + 4 * (kind - 33));
+        else if (kind == 36) cp_async4(d, tile + ((dofs + (uint32_t)lane * pd) & ~3u));
+        else if (kind == 37) cp_async16_zfill(d, M.base, 0);
     }
 }
 
@@ -511,6 +545,40 @@ __device__ __forceinline__ bool pf_epi_loop(const PfGemm &G, const float *xe, co
     return true;
 }
 
+// The offset chains of an epilogue thread's HN rows, after the whole rows
+// (src/ops.rs:395-401): each row with a nonzero offset adds its terms
+// (des·xe)·xs in sub-block order; the rows' chains advance side by side
+// (sub-block outer), eight sub-blocks' xe/xs loads in flight at a time
+// (nsub is a multiple of 8). `anyd`, `des`: this warp's rows.
+template <int HN>
+__device__ __forceinline__ void pf_offset_chains(const PfGemm &G, int m, const unsigned char *anyd, const float *des,
+                                                 float (&acc)[16]) {
+    const int nsub = G.nsub;
+    const float *xe = G.xe + (size_t)m * nsub, *xs = G.xs + (size_t)m * nsub;
+    uint32_t live = 0;  // rows with a nonzero offset
+#pragma unroll
+    for (int n = 0; n < HN; n++)
+        if (anyd[n]) live |= 1u << n;
+    if (!live) return;
+    for (int s0 = 0; s0 < nsub; s0 += 8) {
+        float e8[8], x8[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            e8[k] = __ldg(xe + s0 + k);
+            x8[k] = __ldg(xs + s0 + k);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+#pragma unroll
+            for (int n = 0; n < HN; n++) {
+                const float t = fm(fm(des[n * nsub + s0 + k], e8[k]), x8[k]);
+                acc[n] = (live >> n) & 1u ? fa(acc[n], t) : acc[n];
+            }
+        }
+        if (threadIdx.x == 0 && s0 == 0) pf_stamp(G, 99);
+    }
+}
+
 __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant__ PfGemm G) {
     extern __shared__ __align__(128) unsigned char pf_smem_raw[];
     // 128-byte aligned by an offset from the array itself (the operand tiles
@@ -627,14 +695,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         const int ptid = tid - 256;  // warps 8-10
         uint8_t *raw = sm + L.raw;
         const int slot_bytes = N * 224;
+        PfCopyPlan plan;
+        pf_copy_plan(M, r0, N, ptid, kPfProducers, plan);
         for (int bb = 0; bb < kPfRaw - 1; bb++) {  // one commit group per block, empty past the end
-            if (bb < nblk) pf_copy(M, r0, N, bb, raw + (bb % kPfRaw) * slot_bytes, ptid, kPfProducers);
+            if (bb < nblk) pf_copy(M, plan, bb, raw + (bb % kPfRaw) * slot_bytes);
             cp_async_commit();
         }
         for (int b = 0; b < nblk; b++) {
             const int st = b & 1;
             const int nx = b + kPfRaw - 1;  // its slot was unpacked at block b-1, before that block's last barrier
-            if (nx < nblk) pf_copy(M, r0, N, nx, raw + (nx % kPfRaw) * slot_bytes, ptid, kPfProducers);
+            if (nx < nblk) pf_copy(M, plan, nx, raw + (nx % kPfRaw) * slot_bytes);
             cp_async_commit();
             cp_async_wait<kPfRaw - 1>();  // this thread's copies of block b
             bool w = true;
@@ -699,31 +769,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         // rows' chains advance side by side (sub-block outer), so the token's
         // xe/xs are read once per sub-block and the rows' chains overlap
         if (mins && !G.fused) {
-            const float *xe = G.xe + (size_t)m * G.nsub, *xs = G.xs + (size_t)m * G.nsub;
-            uint32_t live = 0;  // rows with a nonzero offset
-#pragma unroll
-            for (int n = 0; n < 16; n++)
-                if (n < HN && anyd[c0 + n]) live |= 1u << n;
-            if (live) {  // nsub is a multiple of 8: eight sub-blocks' xe/xs loads in flight at a time
-                for (int s0 = 0; s0 < G.nsub; s0 += 8) {
-                    float e8[8], x8[8];
-#pragma unroll
-                    for (int k = 0; k < 8; k++) {
-                        e8[k] = __ldg(xe + s0 + k);
-                        x8[k] = __ldg(xs + s0 + k);
-                    }
-#pragma unroll
-                    for (int k = 0; k < 8; k++) {
-#pragma unroll
-                        for (int n = 0; n < 16; n++) {
-                            if (n >= HN) break;
-                            const float t = fm(fm(des_all[(size_t)(c0 + n) * G.nsub + s0 + k], e8[k]), x8[k]);
-                            acc[n] = (live >> n) & 1u ? fa(acc[n], t) : acc[n];
-                        }
-                    }
-                    if (tid == 0 && s0 == 0) pf_stamp(G, 99);
-                }
-            }
+            if (HN == 16) pf_offset_chains<16>(G, m, anyd + c0, des_all + (size_t)c0 * G.nsub, acc);
+            else pf_offset_chains<8>(G, m, anyd + c0, des_all + (size_t)c0 * G.nsub, acc);
         }
         if (tid == 0) pf_stamp(G, 96);
         // the segment's epilogue, one output unit (two tiled rows) at a time:
