@@ -632,10 +632,10 @@ int pf_reserve(cxm_model *m, int cap) {
     CU(cudaMalloc(&m->pf.a32, pfa_bytes(cap, kmax)));
     CU(cudaMemset(m->pf.a16, 0, pfa_bytes(cap, kmax)));
     CU(cudaMemset(m->pf.a32, 0, pfa_bytes(cap, kmax)));
-    CU(cudaMalloc(&m->pf.e16, (size_t)cap * (kmax / 16) * 4));
-    CU(cudaMalloc(&m->pf.s16, (size_t)cap * (kmax / 16) * 4));
-    CU(cudaMalloc(&m->pf.e32, (size_t)cap * (kmax / 32) * 4));
-    CU(cudaMalloc(&m->pf.s32, (size_t)cap * (kmax / 32) * 4));
+    CU(cudaMalloc(&m->pf.e16, pf_es_floats(cap, kmax / 16) * 4));
+    CU(cudaMalloc(&m->pf.s16, pf_es_floats(cap, kmax / 16) * 4));
+    CU(cudaMalloc(&m->pf.e32, pf_es_floats(cap, kmax / 32) * 4));
+    CU(cudaMalloc(&m->pf.s32, pf_es_floats(cap, kmax / 32) * 4));
     m->pf.cap = cap;
     return 0;
 }
@@ -2353,10 +2353,10 @@ extern "C" int cxm_debug_matmul(int type, const uint8_t *w, uint32_t rows, uint3
         CU(cudaMalloc(&a32.p, ab));
         CU(cudaMemset(a16.p, 0, ab));
         CU(cudaMemset(a32.p, 0, ab));
-        CU(cudaMalloc(&e16.p, (size_t)m * (k / 16) * 4));
-        CU(cudaMalloc(&s16.p, (size_t)m * (k / 16) * 4));
-        CU(cudaMalloc(&e32.p, (size_t)m * (k / 32) * 4));
-        CU(cudaMalloc(&s32.p, (size_t)m * (k / 32) * 4));
+        CU(cudaMalloc(&e16.p, pf_es_floats((int)m, (int)k / 16) * 4));
+        CU(cudaMalloc(&s16.p, pf_es_floats((int)m, (int)k / 16) * 4));
+        CU(cudaMalloc(&e32.p, pf_es_floats((int)m, (int)k / 32) * 4));
+        CU(cudaMalloc(&s32.p, pf_es_floats((int)m, (int)k / 32) * 4));
         CU(cudaMalloc(&derr2.p, 4));
         CU(cudaMemset(derr2.p, 0, 4));
         CU(cudaMemcpy(xa.p, x, (size_t)m * k * 4, cudaMemcpyHostToDevice));

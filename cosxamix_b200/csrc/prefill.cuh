@@ -110,6 +110,16 @@ __device__ __forceinline__ size_t pfa_offset(int m, int k, int K) {
     return ((size_t)mt * (K >> 5) + s) * 4096 + (mm >> 3) * 256 + (kk >> 4) * 128 + (mm & 7) * 16 + (kk & 15);
 }
 
+// Per-sub-block activation scale and sum of token m, sub-block sb: tiles of
+// the M-tiles' 128 tokens, token-minor, so a warp of consecutive tokens reads
+// one sub-block's values with one 128-byte access. Sized for whole M-tiles.
+__host__ __device__ inline size_t pf_es_index(int m, int sb, int nsub) {
+    return ((size_t)(m >> 7) * nsub + sb) * 128 + (m & 127);
+}
+__host__ __device__ inline size_t pf_es_floats(int tokens, int nsub) {
+    return (size_t)((tokens + kPfM - 1) / kPfM) * kPfM * nsub;
+}
+
 struct PfRows {
     const float *in;        // [tokens][ld_in]
     int ld_in;
@@ -117,7 +127,7 @@ struct PfRows {
     float eps;
     int K, tokens, need16, need32;
     int8_t *a16, *a32;      // tiled operands (sub-blocks of 16 / 32)
-    float *e16, *s16, *e32, *s32;  // [tokens][K/16], [tokens][K/32]: scale and sum per sub-block
+    float *e16, *s16, *e32, *s32;  // scale and sum per sub-block of 16 / 32 (pf_es_index)
 };
 
 // One token row per CTA of kDecodeThreads threads, with exactly the
@@ -174,8 +184,8 @@ __global__ void __launch_bounds__(kDecodeThreads) k_pf_rows(const __grid_constan
             if (hc % per == 0) {
                 const int nsub = P.K / sz, sb = hc / per;
                 float *e = sz == 16 ? P.e16 : P.e32, *s = sz == 16 ? P.s16 : P.s32;
-                e[(size_t)row * nsub + sb] = am > 0.0f ? __fdiv_rn(am, 127.0f) : 0.0f;
-                s[(size_t)row * nsub + sb] = (float)sm;
+                e[pf_es_index(row, sb, nsub)] = am > 0.0f ? __fdiv_rn(am, 127.0f) : 0.0f;
+                s[pf_es_index(row, sb, nsub)] = (float)sm;
             }
         }
     }
@@ -491,16 +501,16 @@ __device__ __forceinline__ bool pf_epi_loop(const PfGemm &G, const float *xe, co
     const int lane = threadIdx.x & 31;
     float ev[NSB], xv[NX];
 #pragma unroll
-    for (int k = 0; k < NSB; k++) ev[k] = __ldg(xe + k);
+    for (int k = 0; k < NSB; k++) ev[k] = __ldg(xe + (size_t)k * 128);
 #pragma unroll
-    for (int k = 0; k < NX; k++) xv[k] = FUSED ? __ldg(xs + k) : 0.0f;
+    for (int k = 0; k < NX; k++) xv[k] = FUSED ? __ldg(xs + (size_t)k * 128) : 0.0f;
     for (int b = 0; b < nblk; b++) {
         const int st = b & 1, bn = b + 1 < nblk ? b + 1 : b;
         float en[NSB], xn[NX];
 #pragma unroll
-        for (int k = 0; k < NSB; k++) en[k] = __ldg(xe + bn * NSB + k);
+        for (int k = 0; k < NSB; k++) en[k] = __ldg(xe + (size_t)(bn * NSB + k) * 128);
 #pragma unroll
-        for (int k = 0; k < NX; k++) xn[k] = FUSED ? __ldg(xs + bn * NSB + k) : 0.0f;
+        for (int k = 0; k < NX; k++) xn[k] = FUSED ? __ldg(xs + (size_t)(bn * NSB + k) * 128) : 0.0f;
         // warp-uniform: the TMEM loads below are collective over the warp
         if (!__all_sync(0xffffffffu, pf_wait(&mma_done[st], (b >> 1) & 1, abort_s, G.err) && !*abort_s)) return false;
         tc_fence_after();
@@ -554,7 +564,7 @@ template <int HN>
 __device__ __forceinline__ void pf_offset_chains(const PfGemm &G, int m, const unsigned char *anyd, const float *des,
                                                  float (&acc)[16]) {
     const int nsub = G.nsub;
-    const float *xe = G.xe + (size_t)m * nsub, *xs = G.xs + (size_t)m * nsub;
+    const float *xe = G.xe + pf_es_index(m, 0, nsub), *xs = G.xs + pf_es_index(m, 0, nsub);
     uint32_t live = 0;  // rows with a nonzero offset
 #pragma unroll
     for (int n = 0; n < HN; n++)
@@ -564,14 +574,23 @@ __device__ __forceinline__ void pf_offset_chains(const PfGemm &G, int m, const u
         float e8[8], x8[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) {
-            e8[k] = __ldg(xe + s0 + k);
-            x8[k] = __ldg(xs + s0 + k);
+            e8[k] = __ldg(xe + (size_t)(s0 + k) * 128);
+            x8[k] = __ldg(xs + (size_t)(s0 + k) * 128);
+        }
+        // each row's 8 offsets of the group: two 16-byte shared loads (des is
+        // 16-byte aligned, nsub and s0 multiples of 8)
+        float d8[HN][8];
+#pragma unroll
+        for (int n = 0; n < HN; n++) {
+            const float4 lo = *(const float4 *)(des + n * nsub + s0), hi = *(const float4 *)(des + n * nsub + s0 + 4);
+            d8[n][0] = lo.x; d8[n][1] = lo.y; d8[n][2] = lo.z; d8[n][3] = lo.w;
+            d8[n][4] = hi.x; d8[n][5] = hi.y; d8[n][6] = hi.z; d8[n][7] = hi.w;
         }
 #pragma unroll
         for (int k = 0; k < 8; k++) {
 #pragma unroll
             for (int n = 0; n < HN; n++) {
-                const float t = fm(fm(des[n * nsub + s0 + k], e8[k]), x8[k]);
+                const float t = fm(fm(d8[n][k], e8[k]), x8[k]);
                 acc[n] = (live >> n) & 1u ? fa(acc[n], t) : acc[n];
             }
         }
@@ -748,8 +767,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     } else {
         // ── epilogue: thread = token m (TMEM lane), rows c0..c0+HN-1; the
         // buffered path's dot chain, sub-block by sub-block in row order ──
-        const float *xe = G.xe + (size_t)(m < G.tokens ? m : 0) * G.nsub;
-        const float *xs = G.xs + (size_t)(m < G.tokens ? m : 0) * G.nsub;
+        // (a token past the rows reads the tile's unused entries; its sums are never stored)
+        const float *xe = G.xe + pf_es_index(m, 0, G.nsub), *xs = G.xs + pf_es_index(m, 0, G.nsub);
         const bool fused = G.fused && mins;
         const uint32_t cb0 = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c0;
         const float *db0 = des_all + (size_t)c0 * G.nsub;
