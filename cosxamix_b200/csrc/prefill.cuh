@@ -19,8 +19,8 @@
 //   k_pf_gemm   one 128-token x N-row tile of out = W·x over the whole row
 //               (warp-specialized: 8 epilogue warps own the TMEM lanes =
 //               tokens, two per lane quarter, each for half of the rows;
-//               4 producer warps copy the k-quant blocks a few ahead and
-//               unpack them to int8 operand tiles; producer 0 also copies the
+//               3 producer warps copy the k-quant blocks a few ahead and
+//               unpack them to int8 operand tiles; one thread copies the
 //               activation tiles and issues the MMAs), then the segment's
 //               epilogue (bias, RoPE + K/V append, residual, SwiGLU)
 // Attention over the new tokens uses the standalone attention kernels with a
@@ -223,8 +223,8 @@ struct PfGemm {
     unsigned long long *stamps;
 };
 
-constexpr int kPfThreads = 384;  // warps 0-7: epilogue (TMEM lanes, two halves of the rows); 8-11: producers
-constexpr int kPfProducers = 128;
+constexpr int kPfThreads = 384;  // warps 0-7: epilogue (TMEM lanes, two halves of the rows); 8-10: producers; 11: copies and MMAs
+constexpr int kPfProducers = 96;
 constexpr int kPfStages = 2;     // operand tiles of the weights and accumulator buffers in TMEM
 constexpr int kPfAStages = 3;    // activation tiles in flight
 constexpr int kPfRaw = 4;        // weight blocks in flight (GGUF bytes)
@@ -469,14 +469,14 @@ __device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity, volatile
     return false;
 }
 
-// AND of `ok` over the 128 producer threads (named barrier 2), so they leave
+// AND of `ok` over the 96 producer threads (named barrier 2), so they leave
 // their loop together and none is left waiting at a barrier of the group
 __device__ __forceinline__ bool producers_all(bool ok) {
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.and.pred q, 2, 128, p;\n\t"
+        "bar.red.and.pred q, 2, 96, p;\n\t"
         "selp.u32 %0, 1, 0, q;\n\t}"
         : "=r"(r)
         : "r"((uint32_t)ok)
@@ -603,7 +603,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     // 128-byte aligned by an offset from the array itself (the operand tiles
     // need 16; the descriptors address 16-byte units)
     unsigned char *sm = pf_smem_raw + ((128u - ((uint32_t)(uintptr_t)pf_smem_raw & 127u)) & 127u);
-    __shared__ __align__(8) uint64_t full_a[kPfAStages], mma_done[kPfStages], tmem_empty[kPfStages];
+    __shared__ __align__(8) uint64_t full_a[kPfAStages], full_b[kPfStages], mma_done[kPfStages], tmem_empty[kPfStages];
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_s;
     const QMat &M = G.seg.M;
@@ -618,6 +618,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     if (tid == 0) {
         for (int i = 0; i < kPfAStages; i++) mbar_init(&full_a[i], 1);
         for (int i = 0; i < kPfStages; i++) {
+            mbar_init(&full_b[i], kPfProducers);
             mbar_init(&mma_done[i], 1);
             mbar_init(&tmem_empty[i], 8);  // the epilogue warps
         }
@@ -651,11 +652,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     const int HN = N / 2, c0 = (warp >> 2) * HN;  // an epilogue warp's half of the tile's rows
     const int groups = min(16, (G.tokens - mt * kPfM + 7) / 8);  // 8-token row groups of this tile
 
-    if (warp >= 8) {
-        // ── producers: copy the N rows' super-blocks kPfRaw - 1 blocks ahead
-        // (cp.async), unpack each to the int8 operand tile of its stage;
-        // producer 0 also copies the activation tiles and issues the MMAs ──
-        const int ptid = tid - 256;  // warps 8-11
+    if (warp == 11) {
+        // ── copies of the activation tiles and the MMAs (one thread) ──
         // the activation tile of block bb into stage bb % kPfAStages: the
         // tile's token rows in groups of 8 (256 bytes per K-step); a tile of
         // few tokens (a decode batch) copies only its groups, and the MMA rows
@@ -672,17 +670,56 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                     bulk_g2s(sm + L.a[sa] + k8 * 4096, src + k8 * 4096, (uint32_t)(groups * 256), &full_a[sa]);
             }
         };
+        if (lane == 0) {
+            int last_issued = -1;
+            for (int bb = 0; bb < kPfAStages - 1 && bb < nblk; bb++) copy_a(bb);
+            for (int b = 0; b < nblk; b++) {
+                const int st = b & 1, sa = b % kPfAStages;
+                if (!pf_wait(&full_b[st], (b >> 1) & 1, &abort_s, G.err) ||
+                    !pf_wait(&full_a[sa], (b / kPfAStages) & 1, &abort_s, G.err))
+                    break;
+                if (b < 16) pf_stamp(G, 16 + b);
+                tc_fence_after();
+                const uint32_t dcol = tmem + (uint32_t)st * 256;
+                for (int j = 0; j < nsb; j++) {
+                    const int step = sub == 32 ? j : j >> 1;
+                    const uint64_t ad = umma_desc(sm + L.a[sa] + step * 4096, 128, 256);
+                    uint64_t bd;
+                    if (sub == 32) {
+                        bd = umma_desc(sm + L.b[st] + j * N * 32, 128, 256);
+                    } else {
+                        const uint32_t data = L.b[st] + N * 16 + j * N * 16;
+                        if (!(j & 1)) bd = umma_desc(sm + data, (L.b[st] + 17 * N * 16) - data, 128);
+                        else bd = umma_desc(sm + L.b[st], data - L.b[st], 128);
+                    }
+                    umma_i8(dcol + (uint32_t)(j * N), ad, bd, idesc, 0);
+                }
+                umma_commit(&mma_done[st]);
+                last_issued = b;
+                // the activation tile kPfAStages - 1 blocks ahead, into the
+                // stage block b-1's MMAs read: once they are done
+                const int nx = b + kPfAStages - 1;
+                if (nx < nblk) {
+                    if (b >= 1 && !pf_wait(&mma_done[(b - 1) & 1], ((b - 1) >> 1) & 1, &abort_s, G.err)) break;
+                    copy_a(nx);
+                }
+            }
+            // every MMA has completed before the accumulators are released
+            if (last_issued >= 0) pf_wait(&mma_done[last_issued & 1], (last_issued >> 1) & 1, &abort_s, G.err);
+        }
+        __syncwarp();
+    } else if (warp >= 8) {
+        // ── producers: copy the N rows' super-blocks kPfRaw - 1 blocks ahead
+        // (cp.async), unpack each to the int8 operand tile of its stage ──
+        const int ptid = tid - 256;  // warps 8-10
         uint8_t *raw = sm + L.raw;
         const int slot_bytes = N * 224;
         PfCopyPlan plan;
         pf_copy_plan(M, r0, N, ptid, kPfProducers, plan);
-        if (ptid == 0)
-            for (int bb = 0; bb < kPfAStages - 1 && bb < nblk; bb++) copy_a(bb);
         for (int bb = 0; bb < kPfRaw - 1; bb++) {  // one commit group per block, empty past the end
             if (bb < nblk) pf_copy(M, plan, bb, raw + (bb % kPfRaw) * slot_bytes);
             cp_async_commit();
         }
-        int last_issued = -1;
         for (int b = 0; b < nblk; b++) {
             const int st = b & 1;
             const int nx = b + kPfRaw - 1;  // its slot was unpacked at block b-1, before that block's last barrier
@@ -722,38 +759,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 }
             }
             fence_async_smem();
-            asm volatile("bar.sync 2, 128;" ::: "memory");  // operands complete; every producer is done with slot b % kPfRaw
+            asm volatile("bar.sync 2, 96;" ::: "memory");  // every producer is done with slot b % kPfRaw
+            mbar_arrive(&full_b[st]);
             if (ptid == 0 && b < 16) pf_stamp(G, 48 + b);
-            if (ptid == 0) {  // the block's MMAs (a failed wait is voted on at the next block)
-                const int sa = b % kPfAStages;
-                if (!pf_wait(&full_a[sa], (b / kPfAStages) & 1, &abort_s, G.err)) continue;
-                if (b < 16) pf_stamp(G, 16 + b);
-                tc_fence_after();
-                const uint32_t dcol = tmem + (uint32_t)st * 256;
-                for (int j = 0; j < nsb; j++) {
-                    const int step = sub == 32 ? j : j >> 1;
-                    const uint64_t ad = umma_desc(sm + L.a[sa] + step * 4096, 128, 256);
-                    uint64_t bd;
-                    if (sub == 32) {
-                        bd = umma_desc(sm + L.b[st] + j * N * 32, 128, 256);
-                    } else {
-                        const uint32_t data = L.b[st] + N * 16 + j * N * 16;
-                        if (!(j & 1)) bd = umma_desc(sm + data, (L.b[st] + 17 * N * 16) - data, 128);
-                        else bd = umma_desc(sm + L.b[st], data - L.b[st], 128);
-                    }
-                    umma_i8(dcol + (uint32_t)(j * N), ad, bd, idesc, 0);
-                }
-                umma_commit(&mma_done[st]);
-                last_issued = b;
-                // the activation tile kPfAStages - 1 blocks ahead, into the
-                // stage block b-1's MMAs read: once they are done
-                const int na = b + kPfAStages - 1;
-                if (na < nblk && (b == 0 || pf_wait(&mma_done[(b - 1) & 1], ((b - 1) >> 1) & 1, &abort_s, G.err)))
-                    copy_a(na);
-            }
         }
-        // every MMA has completed before the accumulators are released
-        if (ptid == 0 && last_issued >= 0) pf_wait(&mma_done[last_issued & 1], (last_issued >> 1) & 1, &abort_s, G.err);
         cp_async_wait<0>();  // no copy outlives the loop
     } else {
         // ── epilogue: thread = token m (TMEM lane), rows c0..c0+HN-1; the
