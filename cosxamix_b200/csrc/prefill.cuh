@@ -782,54 +782,66 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     }
     __syncthreads();
     if (tid == 0) pf_stamp(G, 98);
-    if (warp < 8) {
-        const bool live_tok = !abort_s && m < G.tokens;
+    if (warp < 8 && !abort_s && m < G.tokens) {
         // the offset chain, after the whole row (src/ops.rs:395-401): each
         // row with a nonzero offset adds its terms in sub-block order; the
         // rows' chains advance side by side (sub-block outer), so the token's
         // xe/xs are read once per sub-block and the rows' chains overlap
-        if (live_tok && mins && !G.fused) {
+        if (mins && !G.fused) {
             if (HN == 16) pf_offset_chains<16>(G, m, anyd + c0, des_all + (size_t)c0 * G.nsub, acc);
             else pf_offset_chains<8>(G, m, anyd + c0, des_all + (size_t)c0 * G.nsub, acc);
         }
         if (tid == 0) pf_stamp(G, 96);
-        // the rows' sums through shared memory (the activation ring is free:
-        // every MMA has completed), token-major, so that the epilogue below
-        // takes a token's units in consecutive threads and its loads and
-        // stores run along the output rows
-        float *yt = (float *)(sm + L.a[0]);  // [128 tokens][N + 1]
-#pragma unroll
-        for (int n = 0; n < 16; n++)
-            if (n < HN) yt[(tid & 127) * (N + 1) + c0 + n] = acc[n];
-        asm volatile("bar.sync 3, 256;" ::: "memory");
-        // the segment's epilogue, one output unit (two tiled rows) per thread
+        // the segment's epilogue, one output unit (two tiled rows) at a time:
+        // every unit's inputs (bias, rotation, residual) loaded first, then
+        // the results stored
         const MvSeg &g = G.seg;
-        const int upt = N / 2, tpr = 256 / upt;  // units per token; tokens per round
-        for (int t0 = 0; t0 < kPfM; t0 += tpr) {
-            const int tt = t0 + tid / upt, j = tid % upt, mm = mt * kPfM + tt, u = (r0 >> 1) + j;
-            if (abort_s || mm >= G.tokens || u >= g.units) continue;
-            int ra, rb;
-            unit_rows(g, u, ra, rb);
-            const float y0 = yt[tt * (N + 1) + 2 * j], y1 = yt[tt * (N + 1) + 2 * j + 1];
-            const int pos = G.row_pos ? G.row_pos[mm] : G.pos0 + mm;
-            float *cache_base = G.row_out ? G.row_out[mm] : g.out;
-            float *out = g.at_pos ? cache_base + (size_t)pos * g.pos_stride : g.out + (size_t)mm * G.ld_out;
+        const int pos = G.row_pos ? G.row_pos[m] : G.pos0 + m;
+        float *cache_base = G.row_out ? G.row_out[m] : g.out;
+        float *out = g.at_pos ? cache_base + (size_t)pos * g.pos_stride : g.out + (size_t)m * G.ld_out;
+        int ua[8], ub[8];
+        float ia[8], ib[8], ic[8], id[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {  // constant indices: everything stays in registers
+            const int n = 2 * k, u = (r0 + c0 + n) >> 1;
+            ua[k] = -1;
+            ub[k] = 0;
+            ia[k] = ib[k] = ic[k] = id[k] = 0.0f;
+            if (n >= HN || u >= g.units) continue;
+            unit_rows(g, u, ua[k], ub[k]);
+            const int ra = ua[k], rb = ub[k];
+            if (g.epi == EPI_RESID) {
+                ia[k] = out[ra];
+                ib[k] = out[rb];
+            } else if (g.bias && (g.epi == EPI_STORE || g.epi == EPI_ROPE)) {
+                ia[k] = __ldg(g.bias + ra);
+                ib[k] = __ldg(g.bias + rb);
+            }
+            if (g.epi == EPI_ROPE) {
+                const int i = ra % (2 * g.half);
+                ic[k] = __ldg(G.rope_cos + (size_t)pos * g.half + i);
+                id[k] = __ldg(G.rope_sin + (size_t)pos * g.half + i);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int ra = ua[k], rb = ub[k];
+            if (ra < 0) continue;
+            const float y0 = acc[2 * k], y1 = acc[2 * k + 1];
             switch (g.epi) {
             case EPI_STORE:
-                out[ra] = g.bias ? fa(y0, __ldg(g.bias + ra)) : y0;
-                out[rb] = g.bias ? fa(y1, __ldg(g.bias + rb)) : y1;
+                out[ra] = g.bias ? fa(y0, ia[k]) : y0;
+                out[rb] = g.bias ? fa(y1, ib[k]) : y1;
                 break;
             case EPI_ROPE: {  // src/ops.rs:1150-1193
-                const int i = ra % (2 * g.half);
-                const float c = __ldg(G.rope_cos + (size_t)pos * g.half + i), sn = __ldg(G.rope_sin + (size_t)pos * g.half + i);
-                const float a = g.bias ? fa(y0, __ldg(g.bias + ra)) : y0, bb = g.bias ? fa(y1, __ldg(g.bias + rb)) : y1;
-                out[ra] = fs(fm(a, c), fm(bb, sn));
-                out[rb] = fa(fm(a, sn), fm(bb, c));
+                const float a = g.bias ? fa(y0, ia[k]) : y0, bb = g.bias ? fa(y1, ib[k]) : y1;
+                out[ra] = fs(fm(a, ic[k]), fm(bb, id[k]));
+                out[rb] = fa(fm(a, id[k]), fm(bb, ic[k]));
                 break;
             }
             case EPI_RESID:  // src/forward.rs:467-469, :489-491
-                out[ra] = fa(out[ra], y0);
-                out[rb] = fa(out[rb], y1);
+                out[ra] = fa(ia[k], y0);
+                out[rb] = fa(ib[k], y1);
                 break;
             case EPI_SWIGLU: {  // src/kernels/scalar.rs:63-67, src/forward.rs:485-487
                 const float act = __fdiv_rn(y0, fa(1.0f, expf_glibc(-y0)));
