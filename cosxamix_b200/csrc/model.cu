@@ -527,9 +527,15 @@ int set_kernel_smem_limits() {
 // over positions 0..=that one
 int launch_attention_on(cudaStream_t st, AttnParams &a, int tokens = 1) {
     const dim3 gs(a.KV, (a.max_pos + kScoreThreads - 1) / kScoreThreads, tokens);
-    const dim3 go(a.H, 1, tokens);
+    // the output kernel takes up to kOutTok tokens per CTA (the tokens of one
+    // cache: not a batch of conversations), as many as 200 KB of their
+    // probabilities allow
+    const size_t per_tok = out_smem((uint32_t)a.max_pos);
+    a.ntok = tokens;
+    a.tpc = (a.kz || tokens == 1) ? 1 : (int)std::max<size_t>(1, std::min<size_t>(kOutTok, (size_t)200 * 1024 / per_tok));
+    const dim3 go(a.H, 1, (tokens + a.tpc - 1) / a.tpc);
     if (launch_pdl(k_attn_scores, gs, dim3(kScoreThreads), scores_smem(a.hd, a.H / a.KV), st, a)) return -1;
-    return launch_pdl(k_attn_out, go, dim3(kOutThreads), out_smem((uint32_t)a.max_pos), st, a);
+    return launch_pdl(k_attn_out, go, dim3(kOutThreads), per_tok * a.tpc, st, a);
 }
 
 // ── the prompt forward on the tensor cores (prefill.cuh) ──

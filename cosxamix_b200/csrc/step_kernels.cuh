@@ -85,6 +85,9 @@ struct AttnParams {
     // with its own layer bases, token position and prefix
     const float *const *kz, *const *vz, *const *kpz, *const *vpz;
     const int *posz, *plenz;
+    // the output kernel's tokens per CTA (several only without kz: they
+    // share the K/V rows) and the number of tokens
+    int tpc, ntok;
 };
 // the grid-z slice's cache view: K/V bases, prefix, positions attended
 struct AttnView {
@@ -164,75 +167,88 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
     }
 }
 
-// One CTA per (token, head): the softmax of the head's scores once, then
-// thread d adds prob_p·v_p[d] over the positions in order (one sequential
-// chain per dim, as the reference's loop). The V values come straight from
-// L2, a warp reading 32 consecutive dims of a position (128 bytes), eight
+// One CTA per (head, tpc consecutive tokens): each token's softmax of the
+// head's scores (a warp per token: max, exps, the total added position by
+// position by one lane, ×1/total), then thread d adds prob_p·v_p[d] over the
+// positions in order, one sequential chain per (token, dim), the tokens'
+// chains side by side so each V value is read once for all of them. A warp
+// reads 32 consecutive dims of a position (128 bytes) from L2, eight
 // positions' loads in flight ahead of their additions.
+constexpr int kOutTok = 8;  // tokens per CTA at most
 __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant__ AttnParams p) {
-    extern __shared__ __align__(16) float pr[];  // the probabilities [max_pos rounded to 4]
-    __shared__ float red[kOutThreads / 32];
-    __shared__ float bcast;
+    extern __shared__ __align__(16) float pr[];  // the probabilities [tpc][max_pos rounded to 4]
     griddep_launch_dependents();
     griddep_wait();
-    const int h = blockIdx.x, tid = threadIdx.x, z = blockIdx.z;
-    const AttnView w = attn_view(p);
-    const int n = w.n;
-    if (n > p.max_pos || n <= 0) return;  // k_attn_scores reported it
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int T = p.kz ? 1 : p.tpc, z0 = (int)blockIdx.z * T, nt = min(T, p.ntok - z0);
+    const AttnView w = attn_view(p);  // (z = blockIdx.z: with several tokens per CTA only its n differs)
+    const int n0 = p.kz ? w.n : (p.d_len ? *p.d_len : p.pos0) + 1 + z0;  // positions of the first token
+    const int stride = (p.max_pos + 3) & ~3;
+    if (n0 + nt - 1 > p.max_pos || n0 <= 0) return;  // k_attn_scores reported it
     const int hd = p.hd, G = p.H / p.KV, g = h / G, kvd = p.KV * hd;
-    const float *sc = p.scores + ((size_t)z * p.H + h) * p.score_stride;
-    for (int i = tid; i < (n + 3) / 4; i += kOutThreads) cp_async16(pr + 4 * i, sc + 4 * i);
+    for (int t = 0; t < nt; t++) {
+        const float *sc = p.scores + ((size_t)(z0 + t) * p.H + h) * p.score_stride;
+        for (int i = tid; i < (n0 + t + 3) / 4; i += kOutThreads) cp_async16(pr + t * stride + 4 * i, sc + 4 * i);
+    }
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    float m = -INFINITY;
-    for (int i = tid; i < n; i += kOutThreads) m = fmaxf(m, pr[i]);
+    for (int t = warp; t < nt; t += kOutThreads / 32) {  // a warp per token
+        float *q = pr + t * stride;
+        const int n = n0 + t;
+        float m = -INFINITY;
+        for (int i = lane; i < n; i += 32) m = fmaxf(m, q[i]);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((tid & 31) == 0) red[tid >> 5] = m;
-    __syncthreads();
-    if (tid == 0) {
-        float mm = -INFINITY;
-        for (int i = 0; i < kOutThreads / 32; i++) mm = fmaxf(mm, red[i]);
-        bcast = mm;
-    }
-    __syncthreads();
-    const float mx = bcast;
-    __syncthreads();
-    if (!isfinite(mx)) {
-        const float u = __fdiv_rn(1.0f, (float)n);
-        for (int i = tid; i < n; i += kOutThreads) pr[i] = u;
-    } else {
-        for (int i = tid; i < n; i += kOutThreads) pr[i] = expf_glibc(fs(pr[i], mx));
-        __syncthreads();
-        if (tid == 0) {  // the total in position order (src/ops.rs:1219-1223)
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (!isfinite(m)) {
+            const float u = __fdiv_rn(1.0f, (float)n);
+            for (int i = lane; i < n; i += 32) q[i] = u;
+            continue;
+        }
+        for (int i = lane; i < n; i += 32) q[i] = expf_glibc(fs(q[i], m));
+        __syncwarp();
+        float inv = 0.0f;
+        if (lane == 0) {  // the total in position order (src/ops.rs:1219-1223)
             float total = 0.0f;
             int i = 0;
             for (; i + 4 <= n; i += 4) {
-                const float4 v = *(const float4 *)(pr + i);
+                const float4 v = *(const float4 *)(q + i);
                 total = fa(fa(fa(fa(total, v.x), v.y), v.z), v.w);
             }
-            for (; i < n; i++) total = fa(total, pr[i]);
-            bcast = __fdiv_rn(1.0f, total);
+            for (; i < n; i++) total = fa(total, q[i]);
+            inv = __fdiv_rn(1.0f, total);
         }
-        __syncthreads();
-        const float inv = bcast;
-        for (int i = tid; i < n; i += kOutThreads) pr[i] = fm(pr[i], inv);
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+        for (int i = lane; i < n; i += 32) q[i] = fm(q[i], inv);
     }
     __syncthreads();
     if (tid >= hd) return;
     const size_t voff = (size_t)g * hd + tid;
-    float acc = 0.0f;
+    float acc[kOutTok];
+#pragma unroll
+    for (int t = 0; t < kOutTok; t++) acc[t] = 0.0f;
+    const int nmax = n0 + nt - 1;
     int r = 0;
-    for (; r + 8 <= n; r += 8) {
+    for (; r + 8 <= nmax; r += 8) {
         float v[8];
 #pragma unroll
         for (int k = 0; k < 8; k++) v[k] = __ldcg(kv_row(w.v, w.vp, w.plen, r + k, kvd, voff));
 #pragma unroll
-        for (int k = 0; k < 8; k++) acc = fa(acc, fm(pr[r + k], v[k]));
+        for (int k = 0; k < 8; k++) {
+#pragma unroll
+            for (int t = 0; t < kOutTok; t++)
+                if (t < nt && r + k < n0 + t) acc[t] = fa(acc[t], fm(pr[t * stride + r + k], v[k]));
+        }
     }
-    for (; r < n; r++) acc = fa(acc, fm(pr[r], __ldcg(kv_row(w.v, w.vp, w.plen, r, kvd, voff))));
-    p.out[(size_t)z * p.os + (size_t)h * hd + tid] = acc;
+    for (; r < nmax; r++) {
+        const float v = __ldcg(kv_row(w.v, w.vp, w.plen, r, kvd, voff));
+#pragma unroll
+        for (int t = 0; t < kOutTok; t++)
+            if (t < nt && r < n0 + t) acc[t] = fa(acc[t], fm(pr[t * stride + r], v));
+    }
+#pragma unroll
+    for (int t = 0; t < kOutTok; t++)
+        if (t < nt) p.out[(size_t)(z0 + t) * p.os + (size_t)h * hd + tid] = acc[t];
 }
 
 // ── kernel-level parity: integer sub-block sums of one row against an xq ──
