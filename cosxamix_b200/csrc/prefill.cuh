@@ -278,12 +278,12 @@ __host__ __device__ inline PfSmem pf_smem(int type, int K) {
     return s;
 }
 
-// A copier lane's share of a block's copies (at most 12 pieces over 31
-// lanes: 32 rows x 11 chunks for Q5_K), planned once per CTA: the byte
+// A producer thread's share of a block's copies (at most 4 pieces at 96
+// producers: 32 rows x 11 chunks for Q5_K), planned once per CTA: the byte
 // offset in the row's slot, the source offset in the matrix for block 0's
 // tile position, and the piece kind (0-31: plane-A chunk k; 32: plane S
 // 16 bytes; 33-35: plane S 4 bytes; 36: plane D word; 37: zeros).
-constexpr int kPfCopyMax = 12;  // pieces per copier lane: 32 rows x 11 chunks over 31 lanes
+constexpr int kPfCopyMax = 4;
 struct PfCopyPlan {
     int cnt;
     uint32_t dst[kPfCopyMax], src[kPfCopyMax];
@@ -340,11 +340,6 @@ __device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, uin
 }
 __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-// completion of this thread's earlier cp.async copies counted on `bar` (one
-// of the arrivals it expects)
-__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t *bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ void pf_copy(const QMat &M, const PfCopyPlan &P, int b, uint8_t *raw) {
     const int T = M.type, ps = plane_s_bytes(T), pd = plane_d_bytes(T), ach = plane_a_bytes(T) / 16;
@@ -609,7 +604,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     // need 16; the descriptors address 16-byte units)
     unsigned char *sm = pf_smem_raw + ((128u - ((uint32_t)(uintptr_t)pf_smem_raw & 127u)) & 127u);
     __shared__ __align__(8) uint64_t full_a[kPfAStages], full_b[kPfStages], mma_done[kPfStages], tmem_empty[kPfStages];
-    __shared__ __align__(8) uint64_t raw_full[kPfRaw], raw_empty[kPfRaw];
     __shared__ uint32_t tmem_base_s;
     __shared__ volatile int abort_s;
     const QMat &M = G.seg.M;
@@ -623,10 +617,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
 
     if (tid == 0) {
         for (int i = 0; i < kPfAStages; i++) mbar_init(&full_a[i], 1);
-        for (int i = 0; i < kPfRaw; i++) {
-            mbar_init(&raw_full[i], 31);  // the copier lanes' cp.async completions
-            mbar_init(&raw_empty[i], 1);  // producer 0, after the producers unpacked the slot
-        }
         for (int i = 0; i < kPfStages; i++) {
             mbar_init(&full_b[i], kPfProducers);
             mbar_init(&mma_done[i], 1);
@@ -680,21 +670,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                     bulk_g2s(sm + L.a[sa] + k8 * 4096, src + k8 * 4096, (uint32_t)(groups * 256), &full_a[sa]);
             }
         };
-        if (lane != 0) {
-            // ── lanes 1-31: the weight blocks' bytes into the raw ring, a
-            // slot as soon as the producers have unpacked its last block ──
-            uint8_t *raw = sm + L.raw;
-            const int slot_bytes = N * 224;
-            PfCopyPlan plan;
-            pf_copy_plan(M, r0, N, lane - 1, 31, plan);
-            for (int b = 0; b < nblk; b++) {
-                const int slot = b % kPfRaw;
-                if (b >= kPfRaw && !pf_wait(&raw_empty[slot], ((b / kPfRaw) - 1) & 1, &abort_s, G.err)) break;
-                pf_copy(M, plan, b, raw + slot * slot_bytes);
-                cp_async_mbar_arrive(&raw_full[slot]);
-            }
-            cp_async_wait<0>();  // no copy outlives the loop
-        } else {
+        if (lane == 0) {
             int last_issued = -1;
             for (int bb = 0; bb < kPfAStages - 1 && bb < nblk; bb++) copy_a(bb);
             for (int b = 0; b < nblk; b++) {
@@ -738,11 +714,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         const int ptid = tid - 256;  // warps 8-10
         uint8_t *raw = sm + L.raw;
         const int slot_bytes = N * 224;
+        PfCopyPlan plan;
+        pf_copy_plan(M, r0, N, ptid, kPfProducers, plan);
+        for (int bb = 0; bb < kPfRaw - 1; bb++) {  // one commit group per block, empty past the end
+            if (bb < nblk) pf_copy(M, plan, bb, raw + (bb % kPfRaw) * slot_bytes);
+            cp_async_commit();
+        }
         for (int b = 0; b < nblk; b++) {
             const int st = b & 1;
-            // block b's bytes are in (the copier lanes' completions); the epilogue is done with stage st
-            bool w = pf_wait(&raw_full[b % kPfRaw], (b / kPfRaw) & 1, &abort_s, G.err);
-            if (w && b >= kPfStages) w = pf_wait(&tmem_empty[st], ((b - kPfStages) >> 1) & 1, &abort_s, G.err);
+            const int nx = b + kPfRaw - 1;  // its slot was unpacked at block b-1, before that block's last barrier
+            if (nx < nblk) pf_copy(M, plan, nx, raw + (nx % kPfRaw) * slot_bytes);
+            cp_async_commit();
+            cp_async_wait<kPfRaw - 1>();  // this thread's copies of block b
+            bool w = true;
+            if (b >= kPfStages) w = pf_wait(&tmem_empty[st], ((b - kPfStages) >> 1) & 1, &abort_s, G.err);
+            // every producer's copies of block b are in; the epilogue is done with stage st
             if (!producers_all(w && !abort_s)) break;
             if (ptid == 0 && b < 16) pf_stamp(G, 32 + b);
             const uint8_t *blkraw = raw + (b % kPfRaw) * slot_bytes;
@@ -775,9 +761,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
             fence_async_smem();
             asm volatile("bar.sync 2, 96;" ::: "memory");  // every producer is done with slot b % kPfRaw
             mbar_arrive(&full_b[st]);
-            if (ptid == 0) mbar_arrive(&raw_empty[b % kPfRaw]);
             if (ptid == 0 && b < 16) pf_stamp(G, 48 + b);
         }
+        cp_async_wait<0>();  // no copy outlives the loop
     } else {
         // ── epilogue: thread = token m (TMEM lane), rows c0..c0+HN-1; the
         // buffered path's dot chain, sub-block by sub-block in row order ──
