@@ -225,16 +225,14 @@ struct PfGemm {
 
 constexpr int kPfThreads = 384;  // warps 0-7: epilogue (TMEM lanes, two halves of the rows); 8-10: producers; 11: copies and MMAs
 constexpr int kPfProducers = 96;
-constexpr int kPfStages = 4;     // at most: operand tiles of the weights and accumulator buffers in TMEM
+constexpr int kPfStages = 2;     // operand tiles of the weights and accumulator buffers in TMEM
 constexpr int kPfAStages = 3;    // activation tiles in flight
 constexpr int kPfRaw = 4;        // weight blocks in flight (GGUF bytes)
-constexpr uint32_t kPfTmemCols = 512;  // the accumulator buffers (pf_stages of them)
+constexpr uint32_t kPfTmemCols = 512;  // two accumulator buffers of 256 columns
 
 // rows per CTA tile: every sub-block of a super-block gets its own accumulator
-// of N columns; the 512 TMEM columns hold 512 / (subs · N) super-blocks in
-// flight: 4 for sub-blocks of 32 (8 · 16 columns each), 2 for 16 (16 · 16)
-__host__ __device__ constexpr int pf_rows_per_tile(int sub) { return 16; }
-__host__ __device__ constexpr int pf_stages(int sub) { return 512 / ((256 / sub) * 16); }
+// of N columns, two super-blocks in flight: 2 · subs · N = 512 columns
+__host__ __device__ constexpr int pf_rows_per_tile(int sub) { return sub == 32 ? 32 : 16; }
 
 // stamp slots: [0] start; per block b < 16: [16+b] MMA inputs in, [32+b] a
 // producer's copies in, [48+b] its operands out, [64+b] epilogue warp 0's
@@ -261,11 +259,11 @@ __host__ __device__ inline PfSmem pf_smem(int type, int K) {
         s.a[i] = o;
         o += 32768;
     }
-    for (int i = 0; i < pf_stages(sub); i++) {
+    for (int i = 0; i < kPfStages; i++) {
         s.b[i] = o;
         o += (bbytes + 127) & ~127u;
     }
-    for (int i = 0; i < pf_stages(sub); i++) {
+    for (int i = 0; i < kPfStages; i++) {
         s.esc[i] = o;
         o += (uint32_t)(nsb * N * 4);
     }
@@ -494,12 +492,12 @@ __device__ __forceinline__ bool producers_all(bool ok) {
 // xe·((d·sc)·Σ − (dmin·m)·xs). The token's xe (xs) of the next block are
 // loaded while a block is summed. `cb0`: column of this warp's rows in
 // buffer 0; `esc0`, `db0`: their scale rows (buffer 0) and offsets.
-template <int HN, int NSB, bool FUSED>
+template <int HN, bool FUSED>
 __device__ __forceinline__ bool pf_epi_loop(const PfGemm &G, const float *xe, const float *xs, int nblk, int N,
                                             uint32_t cb0, const unsigned char *sm, const PfSmem &L, int c0,
                                             const float *db0, uint64_t *mma_done, uint64_t *tmem_empty,
                                             volatile int *abort_s, float (&acc)[16]) {
-    constexpr int JB = 64 / HN < NSB ? 64 / HN : NSB, NST = 512 / (NSB * 16), NX = FUSED ? NSB : 1;
+    constexpr int NSB = 128 / HN, JB = 64 / HN, NX = FUSED ? NSB : 1;
     const int lane = threadIdx.x & 31;
     float ev[NSB], xv[NX];
 #pragma unroll
@@ -507,18 +505,18 @@ __device__ __forceinline__ bool pf_epi_loop(const PfGemm &G, const float *xe, co
 #pragma unroll
     for (int k = 0; k < NX; k++) xv[k] = FUSED ? __ldg(xs + (size_t)k * 128) : 0.0f;
     for (int b = 0; b < nblk; b++) {
-        const int st = b % NST, bn = b + 1 < nblk ? b + 1 : b;
+        const int st = b & 1, bn = b + 1 < nblk ? b + 1 : b;
         float en[NSB], xn[NX];
 #pragma unroll
         for (int k = 0; k < NSB; k++) en[k] = __ldg(xe + (size_t)(bn * NSB + k) * 128);
 #pragma unroll
         for (int k = 0; k < NX; k++) xn[k] = FUSED ? __ldg(xs + (size_t)(bn * NSB + k) * 128) : 0.0f;
         // warp-uniform: the TMEM loads below are collective over the warp
-        if (!__all_sync(0xffffffffu, pf_wait(&mma_done[st], (b / NST) & 1, abort_s, G.err) && !*abort_s)) return false;
+        if (!__all_sync(0xffffffffu, pf_wait(&mma_done[st], (b >> 1) & 1, abort_s, G.err) && !*abort_s)) return false;
         tc_fence_after();
         if (threadIdx.x == 0 && b < 16) pf_stamp(G, 64 + b);
         const float *esc = (const float *)(sm + L.esc[st]) + c0;
-        const uint32_t cb = cb0 + (uint32_t)(st * NSB * 16);
+        const uint32_t cb = cb0 + (uint32_t)(st * 256);
         const float *db = db0 + b * NSB;
 #pragma unroll
         for (int j0 = 0; j0 < NSB; j0 += JB) {
@@ -610,7 +608,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     __shared__ volatile int abort_s;
     const QMat &M = G.seg.M;
     const int T = M.type, sub = (T == 12 || T == 13) ? 32 : 16, N = pf_rows_per_tile(sub), nsb = 256 / sub;
-    const int nst = pf_stages(sub), colw = nsb * N;  // super-blocks in flight, TMEM columns of one
     const bool mins = has_minimum(T);
     const PfSmem L = pf_smem(T, M.K);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -635,7 +632,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
     }
     // the two zero core-matrix columns of the sub-16 operand tiles
     if (sub == 16)
-        for (int s = 0; s < nst; s++)
+        for (int s = 0; s < kPfStages; s++)
             for (int i = tid; i < N; i += kPfThreads) {
                 *(uint4 *)(sm + L.b[s] + 16 * i) = make_uint4(0, 0, 0, 0);
                 *(uint4 *)(sm + L.b[s] + 17 * N * 16 + 16 * i) = make_uint4(0, 0, 0, 0);
@@ -677,13 +674,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
             int last_issued = -1;
             for (int bb = 0; bb < kPfAStages - 1 && bb < nblk; bb++) copy_a(bb);
             for (int b = 0; b < nblk; b++) {
-                const int st = b % nst, sa = b % kPfAStages;
-                if (!pf_wait(&full_b[st], (b / nst) & 1, &abort_s, G.err) ||
+                const int st = b & 1, sa = b % kPfAStages;
+                if (!pf_wait(&full_b[st], (b >> 1) & 1, &abort_s, G.err) ||
                     !pf_wait(&full_a[sa], (b / kPfAStages) & 1, &abort_s, G.err))
                     break;
                 if (b < 16) pf_stamp(G, 16 + b);
                 tc_fence_after();
-                const uint32_t dcol = tmem + (uint32_t)(st * colw);
+                const uint32_t dcol = tmem + (uint32_t)st * 256;
                 for (int j = 0; j < nsb; j++) {
                     const int step = sub == 32 ? j : j >> 1;
                     const uint64_t ad = umma_desc(sm + L.a[sa] + step * 4096, 128, 256);
@@ -703,12 +700,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
                 // stage block b-1's MMAs read: once they are done
                 const int nx = b + kPfAStages - 1;
                 if (nx < nblk) {
-                    if (b >= 1 && !pf_wait(&mma_done[(b - 1) % nst], ((b - 1) / nst) & 1, &abort_s, G.err)) break;
+                    if (b >= 1 && !pf_wait(&mma_done[(b - 1) & 1], ((b - 1) >> 1) & 1, &abort_s, G.err)) break;
                     copy_a(nx);
                 }
             }
             // every MMA has completed before the accumulators are released
-            if (last_issued >= 0) pf_wait(&mma_done[last_issued % nst], (last_issued / nst) & 1, &abort_s, G.err);
+            if (last_issued >= 0) pf_wait(&mma_done[last_issued & 1], (last_issued >> 1) & 1, &abort_s, G.err);
         }
         __syncwarp();
     } else if (warp >= 8) {
@@ -724,13 +721,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
             cp_async_commit();
         }
         for (int b = 0; b < nblk; b++) {
-            const int st = b % nst;
+            const int st = b & 1;
             const int nx = b + kPfRaw - 1;  // its slot was unpacked at block b-1, before that block's last barrier
             if (nx < nblk) pf_copy(M, plan, nx, raw + (nx % kPfRaw) * slot_bytes);
             cp_async_commit();
             cp_async_wait<kPfRaw - 1>();  // this thread's copies of block b
             bool w = true;
-            if (b >= nst) w = pf_wait(&tmem_empty[st], ((b - nst) / nst) & 1, &abort_s, G.err);
+            if (b >= kPfStages) w = pf_wait(&tmem_empty[st], ((b - kPfStages) >> 1) & 1, &abort_s, G.err);
             // every producer's copies of block b are in; the epilogue is done with stage st
             if (!producers_all(w && !abort_s)) break;
             if (ptid == 0 && b < 16) pf_stamp(G, 32 + b);
@@ -775,13 +772,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant
         const bool fused = G.fused && mins;
         const uint32_t cb0 = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c0;
         const float *db0 = des_all + (size_t)c0 * G.nsub;
-        // 16-row tiles: 8 rows per epilogue warp; 8 sub-blocks a block (of 32) or 16 (of 16)
-        if (nsb == 8) {
-            if (fused) pf_epi_loop<8, 8, true>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
-            else pf_epi_loop<8, 8, false>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
+        if (HN == 16) {
+            if (fused) pf_epi_loop<16, true>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
+            else pf_epi_loop<16, false>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
         } else {
-            if (fused) pf_epi_loop<8, 16, true>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
-            else pf_epi_loop<8, 16, false>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
+            if (fused) pf_epi_loop<8, true>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
+            else pf_epi_loop<8, false>(G, xe, xs, nblk, N, cb0, sm, L, c0, db0, mma_done, tmem_empty, &abort_s, acc);
         }
     }
     __syncthreads();
