@@ -492,14 +492,6 @@ __device__ __forceinline__ bool producers_all(bool ok) {
 // xe·((d·sc)·Σ − (dmin·m)·xs). The token's xe (xs) of the next block are
 // loaded while a block is summed. `cb0`: column of this warp's rows in
 // buffer 0; `esc0`, `db0`: their scale rows (buffer 0) and offsets.
-// A sub-block's integer sum as an f32, exactly: |Σ| <= 32·127·127 < 2^22, so
-// adding 1.5·2^23 in the integer domain gives the float 1.5·2^23 + Σ, from
-// which one f32 subtraction of 1.5·2^23 leaves Σ. Integer add and f32 add
-// run at full rate; the int-to-float conversion unit at a quarter.
-__device__ __forceinline__ float pf_sum_f32(uint32_t s) {
-    return __fsub_rn(__int_as_float((int)(s + 0x4B400000u)), 12582912.0f);
-}
-
 template <int HN, bool FUSED>
 __device__ __forceinline__ bool pf_epi_loop(const PfGemm &G, const float *xe, const float *xs, int nblk, int N,
                                             uint32_t cb0, const unsigned char *sm, const PfSmem &L, int c0,
@@ -542,12 +534,12 @@ __device__ __forceinline__ bool pf_epi_loop(const PfGemm &G, const float *xe, co
                 if (FUSED) {
 #pragma unroll
                     for (int n = 0; n < HN; n++)
-                        acc[n] = fa(acc[n], fm(ev[j], fs(fm(esc[j * N + n], pf_sum_f32(sv[HN * jj + n])),
+                        acc[n] = fa(acc[n], fm(ev[j], fs(fm(esc[j * N + n], (float)(int)sv[HN * jj + n]),
                                                          fm(-db[(size_t)n * G.nsub + j], xv[FUSED ? j : 0]))));
                 } else {
 #pragma unroll
                     for (int n = 0; n < HN; n++)
-                        acc[n] = fa(acc[n], fm(fm(esc[j * N + n], ev[j]), pf_sum_f32(sv[HN * jj + n])));
+                        acc[n] = fa(acc[n], fm(fm(esc[j * N + n], ev[j]), (float)(int)sv[HN * jj + n]));
                 }
             }
         }
