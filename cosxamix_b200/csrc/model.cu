@@ -2495,9 +2495,14 @@ extern "C" int cxm_debug_expf(const float *x, float *y, uint64_t n) {
     return 0;
 }
 
-__global__ void __launch_bounds__(kSampThreads, 1) k_seq_sums(const float *x, float *y, int n) {
+// the running sums, then the total again without them (the scan's other
+// path: passes without an event skip their walk); *same = 0 when they differ
+__global__ void __launch_bounds__(kSampThreads, 1) k_seq_sums(const float *x, float *y, int n, int *same) {
     __shared__ ScanShared sh;
+    __shared__ float total;
     exact_scan(x, n, y, SCAN_ALL, 0.0f, sh, nullptr);
+    exact_scan(x, n, nullptr, SCAN_ALL, 0.0f, sh, &total);
+    if (threadIdx.x == 0) *same = __float_as_uint(total) == __float_as_uint(__ldcg(y + n - 1));
 }
 
 extern "C" int cxm_debug_seq_sums(const float *x, float *y, uint64_t n) {
@@ -2506,14 +2511,21 @@ extern "C" int cxm_debug_seq_sums(const float *x, float *y, uint64_t n) {
         set_error("bad arguments");
         return -1;
     }
-    DevBuf dx, dy;
+    DevBuf dx, dy, ds;
     CU(cudaMalloc(&dx.p, n * 4));
     CU(cudaMalloc(&dy.p, n * 4));
+    CU(cudaMalloc(&ds.p, 4));
     CU(cudaMemcpy(dx.p, x, n * 4, cudaMemcpyHostToDevice));
-    k_seq_sums<<<1, kSampThreads>>>((const float *)dx.p, (float *)dy.p, (int)n);
+    k_seq_sums<<<1, kSampThreads>>>((const float *)dx.p, (float *)dy.p, (int)n, (int *)ds.p);
     CU(cudaGetLastError());
     CU(cudaDeviceSynchronize());
     CU(cudaMemcpy(y, dy.p, n * 4, cudaMemcpyDeviceToHost));
+    int same = 0;
+    CU(cudaMemcpy(&same, ds.p, 4, cudaMemcpyDeviceToHost));
+    if (!same) {
+        set_error("the total taken without the running sums differs from the last running sum");
+        return -1;
+    }
     return 0;
 }
 

@@ -196,8 +196,8 @@ __device__ __forceinline__ float scan_value(uint32_t M, int eb) {
 }
 
 struct ScanShared {
-    uint32_t wtot[kSampWarps];
-    int ev[2];
+    uint32_t wtot[2][kSampWarps];  // by pass parity
+    int ev[3], tie[3];             // by pass mod 3: the first event; a tie among the pass's terms
     float s;
     float cand[kSampThreads];  // each thread's first event's sum
     int passes;                // passes of the last exact_scan (measurement)
@@ -242,11 +242,20 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
     int cur = 0, ceb = -1;  // the window held in x; the binade of its classification
     scan_load8(src, len, 8 * tid, x);
     scan_load8(src, len, kScanWin + 8 * tid, xn);
-    if (tid == 0) sh.ev[0] = sh.ev[1] = INT_MAX;
+    if (tid == 0)
+        for (int i = 0; i < 3; i++) {
+            sh.ev[i] = INT_MAX;
+            sh.tie[i] = 0;
+        }
     __syncthreads();
     float s = 0.0f;
     int pos = 0, span = kSampThreads, it = 0;
     for (;; it++) {
+        const int e3 = it % 3;
+        if (tid == 0) {  // the next pass's slots: their last readers (two passes back) are past this pass's first barrier
+            sh.ev[(it + 1) % 3] = INT_MAX;
+            sh.tie[(it + 1) % 3] = 0;
+        }
         if (pass_stamps && tid == 0 && it < 64) {  // measurement only
             unsigned long long t;
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -309,9 +318,10 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
                 if (lane >= o) inc = sat_add(inc, v);
             }
         }
-        if (lane == 31) sh.wtot[warp] = inc;
+        if (lane == 31) sh.wtot[it & 1][warp] = inc;
+        if (act & evm) sh.tie[e3] = 1;
         __syncthreads();
-        uint32_t wi = sh.wtot[lane];
+        uint32_t wi = sh.wtot[it & 1][lane];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const uint32_t v = __shfl_up_sync(0xffffffffu, wi, o);
@@ -321,6 +331,12 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
         const uint32_t wex = warp ? __shfl_sync(0xffffffffu, wi, warp - 1) : 0u;
         const uint32_t tex = __shfl_up_sync(0xffffffffu, inc, 1);
         uint32_t P = sat_add(M0, sat_add(wex, lane ? tex : 0u));  // (inactive warps: unused)
+        if (!dst && !sh.tie[e3] && M0 + total < (1u << 24)) {  // no event in the pass, no sums to write
+            s = scan_value(M0 + total, eb);
+            pos = end;
+            span = min(kScanWin, 2 * span);
+            continue;
+        }
         // the sums of this thread's terms, up to its first event (the sums
         // after it are rewritten by a later pass)
         int eloc = INT_MAX;
@@ -355,10 +371,9 @@ __device__ int exact_scan(const float *src, int len, float *dst, int mode, float
         }
         // one shared atomic per warp: past a crossing every later thread has an event
         const int wmin = __reduce_min_sync(0xffffffffu, eloc);
-        if (lane == 0 && wmin != INT_MAX) atomicMin(&sh.ev[it & 1], wmin);
+        if (lane == 0 && wmin != INT_MAX) atomicMin(&sh.ev[e3], wmin);
         __syncthreads();
-        const int E = sh.ev[it & 1];
-        if (tid == 0) sh.ev[(it + 1) & 1] = INT_MAX;
+        const int E = sh.ev[e3];
         if (E != INT_MAX) {
             s = sh.cand[(E - wbase) >> 3];
             pos = E + 1;

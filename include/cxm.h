@@ -216,7 +216,9 @@ int cxm_debug_expf(const float *x, float *y, uint64_t n);
 
 /* y[i] = x[0] + ... + x[i] as the reference's sequential f32 loops add them
  * (`total += *v`, src/ops.rs:1222; `acumulada += ...`, src/sampler.rs:110,
- * :144), each running sum rounded in turn: the device sampler's summation. */
+ * :144), each running sum rounded in turn: the device sampler's summation.
+ * The total is also taken a second time without the running sums (the
+ * summation's other path); the call fails if the two differ. */
 int cxm_debug_seq_sums(const float *x, float *y, uint64_t n);
 
 /* ── measurement hooks (no counterpart in the reference: timing only) ──── */
