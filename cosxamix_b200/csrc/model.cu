@@ -526,16 +526,15 @@ int set_kernel_smem_limits() {
 // src/ops.rs:1258-1325 for the token at *d_len (or tokens pos0.. pos0+tokens-1),
 // over positions 0..=that one
 int launch_attention_on(cudaStream_t st, AttnParams &a, int tokens = 1) {
-    // the kernels take several tokens per CTA (the tokens of one cache: not
-    // a batch of conversations): the scores kScoreTok, the output up to
-    // kOutTok, as many as 200 KB of their probabilities allow
+    const dim3 gs(a.KV, (a.max_pos + kScoreThreads - 1) / kScoreThreads, tokens);
+    // the output kernel takes up to kOutTok tokens per CTA (the tokens of one
+    // cache: not a batch of conversations), as many as 200 KB of their
+    // probabilities allow
     const size_t per_tok = out_smem((uint32_t)a.max_pos);
     a.ntok = tokens;
-    a.spc = (a.kz || tokens == 1) ? 1 : kScoreTok;
     a.tpc = (a.kz || tokens == 1) ? 1 : (int)std::max<size_t>(1, std::min<size_t>(kOutTok, (size_t)200 * 1024 / per_tok));
-    const dim3 gs(a.KV, (a.max_pos + kScoreThreads - 1) / kScoreThreads, (tokens + a.spc - 1) / a.spc);
     const dim3 go(a.H, 1, (tokens + a.tpc - 1) / a.tpc);
-    if (launch_pdl(k_attn_scores, gs, dim3(kScoreThreads), scores_smem(a.hd, a.spc * (a.H / a.KV)), st, a)) return -1;
+    if (launch_pdl(k_attn_scores, gs, dim3(kScoreThreads), scores_smem(a.hd, a.H / a.KV), st, a)) return -1;
     return launch_pdl(k_attn_out, go, dim3(kOutThreads), per_tok * a.tpc, st, a);
 }
 

@@ -85,9 +85,9 @@ struct AttnParams {
     // with its own layer bases, token position and prefix
     const float *const *kz, *const *vz, *const *kpz, *const *vpz;
     const int *posz, *plenz;
-    // the output and score kernels' tokens per CTA (several only without
-    // kz: they share the K/V rows) and the number of tokens
-    int tpc, spc, ntok;
+    // the output kernel's tokens per CTA (several only without kz: they
+    // share the K/V rows) and the number of tokens
+    int tpc, ntok;
 };
 // the grid-z slice's cache view: K/V bases, prefix, positions attended
 struct AttnView {
@@ -109,32 +109,30 @@ constexpr int kScoreThreads = 128;   // positions per score CTA
 constexpr int kKRow = 132;           // smem row stride (floats) of staged K rows
 constexpr int kOutThreads = 128;     // one thread per head dim (head_dim <= 128)
 
-// One CTA per (spc consecutive tokens, KV head, 128 positions): the K rows
-// of the positions are staged once for all the tokens and all the query
-// heads of the group; thread = position, each score q_h·k a sequential sum
-// over the dims (src/ops.rs), up to eight heads' chains side by side.
-constexpr int kScoreTok = 4;  // tokens per CTA at most
+// One CTA per (token, KV head, 128 positions): the K rows of the positions
+// are staged once for all the query heads of the group; thread = position,
+// each score q_h·k a sequential sum over the dims (src/ops.rs), up to eight
+// heads' chains side by side.
 __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_constant__ AttnParams p) {
-    extern __shared__ __align__(16) float ks[];  // [kScoreThreads][kKRow] then q [spc][G][hd]
+    extern __shared__ __align__(16) float ks[];  // [kScoreThreads][kKRow] then q [G][hd]
     griddep_launch_dependents();
     griddep_wait();
-    const int g = blockIdx.x, split = blockIdx.y, tid = threadIdx.x;
-    const int T = p.kz ? 1 : p.spc, z0 = (int)blockIdx.z * T, nt = min(T, p.ntok - z0);
-    const AttnView w = attn_view(p);  // (with several tokens per CTA only its n differs)
-    const int n0 = p.kz ? w.n : (p.d_len ? *p.d_len : p.pos0) + 1 + z0, nl = n0 + nt - 1;  // first, last token's positions
-    if (nl > p.max_pos || n0 <= 0) {
+    const int g = blockIdx.x, split = blockIdx.y, tid = threadIdx.x, z = blockIdx.z;
+    const AttnView w = attn_view(p);
+    const int n = w.n;
+    if (n > p.max_pos || n <= 0) {
         if (tid == 0 && g == 0 && split == 0) atomicOr(p.err, ERR_POSITION);
         return;
     }
     const int p0 = split * kScoreThreads;
-    if (p0 >= nl) return;
-    const int cnt = min(kScoreThreads, nl - p0);
+    if (p0 >= n) return;
+    const int cnt = min(kScoreThreads, n - p0);
     const int hd = p.hd, G = p.H / p.KV, kvd = p.KV * hd, c4 = hd / 4;
     float *qs = ks + kScoreThreads * kKRow;
-    // stage the tokens' q rows of the group and the K rows of these positions: all 16-byte copies in flight
-    for (int i = tid; i < nt * G * c4; i += kScoreThreads) {
-        const int th = i / c4, c = i - th * c4, t = th / G, hq = th - t * G;
-        cp_async16(qs + th * hd + 4 * c, p.q + (size_t)(z0 + t) * p.qs + (size_t)(g * G + hq) * hd + 4 * c);
+    // stage the group's q rows and the K rows of these positions: all 16-byte copies in flight
+    for (int i = tid; i < G * c4; i += kScoreThreads) {
+        const int hq = i / c4, c = i - hq * c4;
+        cp_async16(qs + hq * hd + 4 * c, p.q + (size_t)z * p.qs + (size_t)(g * G + hq) * hd + 4 * c);
     }
     for (int i = tid; i < cnt * c4; i += kScoreThreads) {
         const int r = i / c4, c = i - r * c4;
@@ -145,30 +143,26 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
     __syncthreads();
     if (tid >= cnt) return;
     const float4 *kr = (const float4 *)(ks + tid * kKRow);
-    for (int t = 0; t < nt; t++) {
-        if (p0 + tid >= n0 + t) continue;  // past this token's positions
-        const float *qt = qs + t * G * hd;
-        for (int h0 = 0; h0 < G; h0 += 8) {
-            float acc[8];
+    for (int h0 = 0; h0 < G; h0 += 8) {
+        float acc[8];
 #pragma unroll
-            for (int j = 0; j < 8; j++) acc[j] = 0.0f;
-            for (int c = 0; c < c4; c++) {
-                const float4 kv = kr[c];
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    if (h0 + j >= G) break;
-                    const float4 qv = ((const float4 *)(qt + (h0 + j) * hd))[c];
-                    acc[j] = fa(acc[j], fm(qv.x, kv.x));
-                    acc[j] = fa(acc[j], fm(qv.y, kv.y));
-                    acc[j] = fa(acc[j], fm(qv.z, kv.z));
-                    acc[j] = fa(acc[j], fm(qv.w, kv.w));
-                }
-            }
+        for (int j = 0; j < 8; j++) acc[j] = 0.0f;
+        for (int c = 0; c < c4; c++) {
+            const float4 kv = kr[c];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 if (h0 + j >= G) break;
-                p.scores[((size_t)(z0 + t) * p.H + g * G + h0 + j) * p.score_stride + p0 + tid] = fm(acc[j], p.scale);
+                const float4 qv = ((const float4 *)(qs + (h0 + j) * hd))[c];
+                acc[j] = fa(acc[j], fm(qv.x, kv.x));
+                acc[j] = fa(acc[j], fm(qv.y, kv.y));
+                acc[j] = fa(acc[j], fm(qv.z, kv.z));
+                acc[j] = fa(acc[j], fm(qv.w, kv.w));
             }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (h0 + j >= G) break;
+            p.scores[((size_t)z * p.H + g * G + h0 + j) * p.score_stride + p0 + tid] = fm(acc[j], p.scale);
         }
     }
 }
