@@ -175,6 +175,38 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const __grid_cons
 // reads 32 consecutive dims of a position (128 bytes) from L2, eight
 // positions' loads in flight ahead of their additions.
 constexpr int kOutTok = 8;  // tokens per CTA at most
+// out[t][d] = Σ_p prob_t,p·v_p[d] for TT (or nt <= TT) tokens, position by
+// position, V values loaded UB positions ahead of their additions
+template <int TT, int UB>
+__device__ __forceinline__ void attn_pv(const AttnParams &p, const AttnView &w, const float *pr, int stride, int n0, int nt,
+                                        int kvd, size_t voff, int z0, int h, int hd, int tid) {
+    float acc[TT];
+#pragma unroll
+    for (int t = 0; t < TT; t++) acc[t] = 0.0f;
+    const int nmax = n0 + nt - 1;
+    int r = 0;
+    for (; r + UB <= nmax; r += UB) {
+        float v[UB];
+#pragma unroll
+        for (int k = 0; k < UB; k++) v[k] = __ldcg(kv_row(w.v, w.vp, w.plen, r + k, kvd, voff));
+#pragma unroll
+        for (int k = 0; k < UB; k++) {
+#pragma unroll
+            for (int t = 0; t < TT; t++)
+                if (TT == 1 || (t < nt && r + k < n0 + t)) acc[t] = fa(acc[t], fm(pr[t * stride + r + k], v[k]));
+        }
+    }
+    for (; r < nmax; r++) {
+        const float v = __ldcg(kv_row(w.v, w.vp, w.plen, r, kvd, voff));
+#pragma unroll
+        for (int t = 0; t < TT; t++)
+            if (TT == 1 || (t < nt && r < n0 + t)) acc[t] = fa(acc[t], fm(pr[t * stride + r], v));
+    }
+#pragma unroll
+    for (int t = 0; t < TT; t++)
+        if (t < nt) p.out[(size_t)(z0 + t) * p.os + (size_t)h * hd + tid] = acc[t];
+}
+
 __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant__ AttnParams p) {
     extern __shared__ __align__(16) float pr[];  // the probabilities [tpc][max_pos rounded to 4]
     griddep_launch_dependents();
@@ -224,31 +256,8 @@ __global__ void __launch_bounds__(kOutThreads) k_attn_out(const __grid_constant_
     __syncthreads();
     if (tid >= hd) return;
     const size_t voff = (size_t)g * hd + tid;
-    float acc[kOutTok];
-#pragma unroll
-    for (int t = 0; t < kOutTok; t++) acc[t] = 0.0f;
-    const int nmax = n0 + nt - 1;
-    int r = 0;
-    for (; r + 8 <= nmax; r += 8) {
-        float v[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) v[k] = __ldcg(kv_row(w.v, w.vp, w.plen, r + k, kvd, voff));
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-#pragma unroll
-            for (int t = 0; t < kOutTok; t++)
-                if (t < nt && r + k < n0 + t) acc[t] = fa(acc[t], fm(pr[t * stride + r + k], v[k]));
-        }
-    }
-    for (; r < nmax; r++) {
-        const float v = __ldcg(kv_row(w.v, w.vp, w.plen, r, kvd, voff));
-#pragma unroll
-        for (int t = 0; t < kOutTok; t++)
-            if (t < nt && r < n0 + t) acc[t] = fa(acc[t], fm(pr[t * stride + r], v));
-    }
-#pragma unroll
-    for (int t = 0; t < kOutTok; t++)
-        if (t < nt) p.out[(size_t)(z0 + t) * p.os + (size_t)h * hd + tid] = acc[t];
+    if (nt == 1) attn_pv<1, 16>(p, w, pr, stride, n0, 1, kvd, voff, z0, h, hd, tid);
+    else attn_pv<kOutTok, 8>(p, w, pr, stride, n0, nt, kvd, voff, z0, h, hd, tid);
 }
 
 // ── kernel-level parity: integer sub-block sums of one row against an xq ──
