@@ -233,7 +233,11 @@ __device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) { return min
 // span as long as the terms summed so far (sums from zero double between
 // binade crossings), and it doubles after a pass without one. Every thread
 // writes the sums of its terms up to its own first event; a later pass
-// rewrites those past the CTA's first event. src and dst are 16-byte aligned.
+// rewrites those past the CTA's first event. Without dst, a pass whose block
+// sum stays inside the binade and holds no tie skips that walk. Warps whose
+// terms are all outside a pass only join its barriers. `pass_stamps`
+// (measurement only): the start time of each of the first 64 passes. src and
+// dst are 16-byte aligned.
 __device__ int exact_scan(const float *src, int len, float *dst, int mode, float stop, ScanShared &sh, float *sum,
                           unsigned long long *pass_stamps = nullptr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
