@@ -608,6 +608,10 @@ int pf_gemm(cudaStream_t st, const MvSeg &seg, int t, int pos0, int ld_out, cons
     const PfSmem L = pf_smem(seg.M.type, seg.M.K);
     // at least 116 KB, so no two of these CTAs share an SM (each takes all 512 TMEM columns)
     const size_t smem = std::max<size_t>(L.total + 128, 116 * 1024);
+    if (N * pf_copy_pieces(seg.M.type) > kPfCopyMax * kPfProducers) {  // every piece of a block has a copier
+        set_error("the prompt GEMM's copy plan cannot hold a block of format %d", seg.M.type);
+        return -1;
+    }
     if (smem > (size_t)g_pf_smem_max) {
         set_error("the prompt GEMM needs %zu bytes of shared memory for K = %d; the device allows %d", smem, seg.M.K,
                   g_pf_smem_max);
@@ -2248,6 +2252,14 @@ struct DevBuf {
     void *p = nullptr;
     ~DevBuf() { cudaFree(p); }
 };
+// a start/stop pair of CUDA events, destroyed on every return path
+struct EventPair {
+    cudaEvent_t a = nullptr, b = nullptr;
+    ~EventPair() {
+        if (a) cudaEventDestroy(a);
+        if (b) cudaEventDestroy(b);
+    }
+};
 int dev_matrix_from_host(int type, const uint8_t *w, uint32_t rows, uint32_t k, DevBuf bufs[3], DMat *out) {
     if (!is_kquant(type) || k % 256 || rows == 0) {
         set_error("type %d, k %u: not a k-quant matrix", type, k);
@@ -2555,16 +2567,14 @@ extern "C" int cxm_bench_decode_sampled(cxm_model *m, cxm_cache *c, cxm_sampler 
     if (sampled && set_sampler(m, s)) return -1;
     cudaGraphExec_t g;
     if (get_graph(m, c, sampled ? STEP_SAMPLE : STEP_GREEDY, ROWS_FEW, &g)) return -1;
-    cudaEvent_t e0, e1;
-    CU(cudaEventCreate(&e0));
-    CU(cudaEventCreate(&e1));
-    CU(cudaEventRecord(e0, m->stream));
+    EventPair ev;
+    CU(cudaEventCreate(&ev.a));
+    CU(cudaEventCreate(&ev.b));
+    CU(cudaEventRecord(ev.a, m->stream));
     for (uint32_t i = 0; i < steps; i++) CU(cudaGraphLaunch(g, m->stream));
-    CU(cudaEventRecord(e1, m->stream));
-    CU(cudaEventSynchronize(e1));
-    CU(cudaEventElapsedTime(ms_total, e0, e1));
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
+    CU(cudaEventRecord(ev.b, m->stream));
+    CU(cudaEventSynchronize(ev.b));
+    CU(cudaEventElapsedTime(ms_total, ev.a, ev.b));
     if (check_err(m)) return -1;
     if (sampled) {  // one draw per step
         uint64_t st = s->state;
@@ -2591,18 +2601,17 @@ extern "C" int cxm_bench_sample(cxm_model *m, cxm_sampler *s, uint32_t reps, flo
     DevBuf st;
     CU(cudaMalloc(&st.p, kSampStamps * sizeof(unsigned long long)));
     CU(cudaMemsetAsync(st.p, 0, kSampStamps * sizeof(unsigned long long), m->stream));
-    cudaEvent_t e0, e1;
-    CU(cudaEventCreate(&e0));
-    CU(cudaEventCreate(&e1));
-    CU(cudaEventRecord(e0, m->stream));
+    EventPair ev;
+    CU(cudaEventCreate(&ev.a));
+    CU(cudaEventCreate(&ev.b));
+    CU(cudaEventRecord(ev.a, m->stream));
     for (uint32_t i = 0; i < reps; i++)
-        if (launch_sample(m, nullptr, nullptr, m->samp_tok, nullptr, i + 1 == reps && phase_ns ? (unsigned long long *)st.p : nullptr))
+        if (launch_sample(m, nullptr, nullptr, m->samp_tok, nullptr,
+                          i + 1 == reps && phase_ns ? (unsigned long long *)st.p : nullptr))
             return -1;
-    CU(cudaEventRecord(e1, m->stream));
-    CU(cudaEventSynchronize(e1));
-    CU(cudaEventElapsedTime(ms_total, e0, e1));
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
+    CU(cudaEventRecord(ev.b, m->stream));
+    CU(cudaEventSynchronize(ev.b));
+    CU(cudaEventElapsedTime(ms_total, ev.a, ev.b));
     if (check_err(m)) return -1;
     if (phase_ns) {
         unsigned long long h[kSampStamps];

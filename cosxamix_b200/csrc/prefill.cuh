@@ -284,6 +284,11 @@ __host__ __device__ inline PfSmem pf_smem(int type, int K) {
 // tile position, and the piece kind (0-31: plane-A chunk k; 32: plane S
 // 16 bytes; 33-35: plane S 4 bytes; 36: plane D word; 37: zeros).
 constexpr int kPfCopyMax = 4;
+// pieces of one row's block: plane-A chunks, plane-S pieces, the plane-D word
+__host__ __device__ inline int pf_copy_pieces(int type) {
+    const int ps = plane_s_bytes(type), pd = plane_d_bytes(type);
+    return plane_a_bytes(type) / 16 + (ps == 16 ? 1 : ps / 4) + (pd ? 1 : 0);
+}
 struct PfCopyPlan {
     int cnt;
     uint32_t dst[kPfCopyMax], src[kPfCopyMax];
@@ -298,7 +303,7 @@ __device__ __forceinline__ void pf_copy_plan(const QMat &M, int r0, int N, int i
         lo_a = 16;
         lo_d = 80;
     }
-    const int sp = ps == 16 ? 1 : ps / 4, per = ach + sp + (pd ? 1 : 0);
+    const int sp = ps == 16 ? 1 : ps / 4, per = pf_copy_pieces(T);
     P.cnt = 0;
 #pragma unroll
     for (int c = 0; c < kPfCopyMax; c++) {
