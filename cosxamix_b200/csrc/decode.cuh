@@ -1110,39 +1110,20 @@ __device__ __forceinline__ void attn_prefetch(const AtPhase &at, int n, int max_
 // positions 32 floats apart)
 __device__ __forceinline__ void pv_chunk(const float *vt, const float *pp, int cnt, float inv, float &acc) {
     int r = 0;
-    if (cnt >= 16) {
-        // software-pipelined: the next 16 positions' loads are issued before
-        // this 16's additions, so only the chain of adds is on the path
+    for (; r + 16 <= cnt; r += 16) {
         float4 q[4];
         float w[16];
 #pragma unroll
-        for (int k = 0; k < 4; k++) q[k] = ((const float4 *)pp)[k];
+        for (int k = 0; k < 4; k++) q[k] = ((const float4 *)(pp + r))[k];
 #pragma unroll
-        for (int k = 0; k < 16; k++) w[k] = vt[k * 32];
-        for (;; r += 16) {
-            const bool more = r + 32 <= cnt;
-            float4 qn[4];
-            float wn[16];
-            if (more) {
+        for (int k = 0; k < 16; k++) w[k] = vt[(r + k) * 32];
 #pragma unroll
-                for (int k = 0; k < 4; k++) qn[k] = ((const float4 *)(pp + r + 16))[k];
-#pragma unroll
-                for (int k = 0; k < 16; k++) wn[k] = vt[(r + 16 + k) * 32];
-            }
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                acc = fa(acc, fm(fm(q[k].x, inv), w[4 * k]));
-                acc = fa(acc, fm(fm(q[k].y, inv), w[4 * k + 1]));
-                acc = fa(acc, fm(fm(q[k].z, inv), w[4 * k + 2]));
-                acc = fa(acc, fm(fm(q[k].w, inv), w[4 * k + 3]));
-            }
-            if (!more) break;
-#pragma unroll
-            for (int k = 0; k < 4; k++) q[k] = qn[k];
-#pragma unroll
-            for (int k = 0; k < 16; k++) w[k] = wn[k];
+        for (int k = 0; k < 4; k++) {
+            acc = fa(acc, fm(fm(q[k].x, inv), w[4 * k]));
+            acc = fa(acc, fm(fm(q[k].y, inv), w[4 * k + 1]));
+            acc = fa(acc, fm(fm(q[k].z, inv), w[4 * k + 2]));
+            acc = fa(acc, fm(fm(q[k].w, inv), w[4 * k + 3]));
         }
-        r += 16;
     }
     for (; r < cnt; r++) acc = fa(acc, fm(fm(pp[r], inv), vt[r * 32]));
 }
