@@ -2,7 +2,9 @@
 
     python -m cosxamix_b200.kernel_bench [--config qwen3b] [--reps 108]
                                          [--layers N] [--vocab V]
-                                         [--decode STEPS --prompt P]
+                                         [--decode STEPS --prompt P [--sample]]
+                                         [--sampler RUNS]
+                                         [--prefill P [--gemm-stamps LAUNCH]]
 
 Times the gate|up matvec phase of the decode kernel: `reps` such phases in
 one launch, behind grid barriers as in the step, cycling over the model's
@@ -15,7 +17,9 @@ per token), then times STEPS greedy decode steps (one launch each), or with
 logits (T 0.7, top-p 0.9), with CTA 0's step ends of the last run. With
 --prefill P: the forward of a seeded P-token prompt into an empty cache
 (wall clock around the call, which returns once the logits are on the host;
-best of 3 after a warm-up).
+best of 3 after a warm-up); with --gemm-stamps LAUNCH, one more forward in
+which that prompt-GEMM launch (0-based, in launch order) records CTA (0, 0)'s
+step times per role.
 `--layers` / `--vocab` shrink the synthetic model (same matrix shapes) so an
 ncu capture holds little device memory; keep layers x 25 MB above the 126 MB
 L2 for DRAM figures to mean something.
